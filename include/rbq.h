@@ -1,0 +1,181 @@
+/*
+ * rbq.h -- C ABI of the B200-native IVF-RaBitQ retrieval library (librbq.so).
+ *
+ * Drop-in boundary for Neurosamble's retrieval hot path.  The reference path is the vendored
+ * cuVS fork's C++ API (third-party/cuvs_rabitq/cpp/include/cuvs/neighbors/ivf_rabitq.hpp),
+ * driven by the rabitq_search CLI (src/rabitq_gpu/rabitq_search.cu) and consumed by
+ * src/neurosamble/overlap/map_full.py.  Every entry point below names the reference
+ * interface it replaces.
+ *
+ * Conventions
+ *   - Every function returns an int status (RBQ_OK == 0).  Nothing throws across the ABI,
+ *     nothing calls exit() or traps; rbq_last_error() returns the calling thread's message.
+ *   - Pointers named *_dev are device pointers on the index's device, owned by the caller.
+ *     The library owns the index memory.  `stream` is a cudaStream_t (0 = legacy default);
+ *     work is enqueued asynchronously on it unless the function says it synchronises.
+ *   - One handle per stream/thread at a time; distinct handles are independent.
+ *   - Distances are squared L2 (ascending); missing results have id -1 and distance +inf.
+ */
+#ifndef RBQ_H_
+#define RBQ_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RBQ_OK 0
+#define RBQ_ERR_INVALID 1 /* bad argument (size, nprobe > nlist, null pointer, ...) */
+#define RBQ_ERR_CUDA 2    /* a CUDA runtime call failed */
+#define RBQ_ERR_OOM 3     /* device allocation failed */
+#define RBQ_ERR_IO 4      /* file open/read/write failed */
+#define RBQ_ERR_STATE 5   /* wrong call order (search before add, add before train, ...) */
+#define RBQ_ERR_FORMAT 6  /* index file malformed or truncated */
+
+typedef struct rbq_index rbq_index_t;
+
+/* Build-time parameters.  Replaces cuvs::neighbors::ivf_rabitq::index_params
+ * (ivf_rabitq.hpp:50-103) for the 1-bit (bits_per_dim = 1) configuration. */
+typedef struct {
+  int32_t dim;                          /* D; padded internally to Dp = ceil(D/32)*32       */
+  int32_t n_lists;                      /* K (n_lists)                                        */
+  uint64_t seed;                        /* rotation / t4 seed (reference: RAFT seed 7)        */
+  int32_t kmeans_n_iters;               /* reference default 20                               */
+  int32_t max_train_points_per_cluster; /* reference default 256                              */
+  int32_t device;                       /* CUDA device ordinal holding the index              */
+  int32_t shard_rank;                   /* this handle stores lists l with l % count == rank  */
+  int32_t shard_count;                  /* 1 = unsharded                                      */
+} rbq_index_params_t;
+
+/* Search-time parameters.  Replaces cuvs::neighbors::ivf_rabitq::search_params
+ * (ivf_rabitq.hpp:178-228) in QUANT4 mode. */
+typedef struct {
+  int32_t n_probes;      /* P (n_probes)                                                      */
+  int32_t k;             /* neighbours returned per query                                      */
+  int32_t rerank;        /* R: exact fp32 rerank depth; 0 = return the estimator's top-k       */
+  int32_t prune;         /* 1 = RaBitQ error-bound prune (reference behaviour), 0 = off        */
+  int32_t probe_split;   /* probe slices per query (0 = auto from nq and P)                    */
+  int32_t cand_cap;      /* candidate buffer entries per slice (0 = default 1024)              */
+  int32_t coarse_margin; /* extra lists kept by the approximate coarse pass (0 = default)      */
+} rbq_search_params_t;
+
+typedef struct {
+  int32_t dim, padded_dim, n_lists, shard_rank, shard_count, trained;
+  int64_t n_total; /* vectors added (global id space)   */
+  int64_t n_local; /* vectors stored by this shard      */
+  float query_scale;
+  uint64_t seed;
+  int64_t device_bytes; /* index memory held on the device */
+} rbq_index_info_t;
+
+/* ---- errors / defaults ------------------------------------------------------------------ */
+const char* rbq_last_error(void);
+int rbq_version(void);
+void rbq_index_params_default(rbq_index_params_t* p);
+void rbq_search_params_default(rbq_search_params_t* p);
+
+/* ---- host-only index constants (no GPU needed) ------------------------------------------ */
+/* Seeded orthogonal rotation P [Dp, Dp] row-major (X_rot = X * P).  Replaces
+ * RotatorGPU::init_matmul (gpu_index/rotator_gpu.cu:52-59). */
+int rbq_make_rotation(int32_t padded_dim, uint64_t seed, float* P_host);
+/* Query scaling constant t4 for 4-bit queries (ex_bits = 3).  Replaces
+ * DataQuantizerGPU::get_const_scaling_factors (gpu_index/quantizer_gpu.cu:947-980). */
+int rbq_query_scale(int32_t padded_dim, uint64_t seed, int32_t ex_bits, float* t_out);
+
+/* ---- index lifecycle -------------------------------------------------------------------- */
+/* Create an empty index: generates the seeded rotation and the query scale t4.
+ * Replaces index(handle, n_rows, dim, n_lists, bits_per_dim) (ivf_rabitq.hpp:265-272) and the
+ * IVFGPU / RotatorGPU constructors (gpu_index/ivf_gpu.cu:37-53, rotator_gpu.cu:52-59). */
+int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out);
+int rbq_index_free(rbq_index_t* index);
+int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out);
+
+/* Train the coarse quantiser (seeded Lloyd k-means on a strided sample) on device rows.
+ * Replaces the k-means part of build (src/neighbors/ivf_rabitq.cu:117-152).  Synchronises. */
+int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream);
+
+/* Install caller-given centroids [K, D] (host memory) instead of training.  Synchronises. */
+int rbq_set_centroids(rbq_index_t* index, const float* C_host, int32_t n_lists);
+
+/* Add rows [n, D] (device) with global ids n_total .. n_total+n-1: assign lists (or take
+ * labels_dev), rotate, 1-bit quantise, compute factors, lay out per list.  Replaces
+ * build's construct_on_gpu (gpu_index/ivf_gpu.cu:623-812) + serialise/deserialise reorg
+ * (rabitq_search.cu:152-158).  Synchronises. */
+int rbq_add(rbq_index_t* index, const float* X_dev, int64_t n, const uint32_t* labels_dev, void* stream);
+
+/* Search: queries [nq, D] (device) -> dist [nq, k] f32, ids [nq, k] i64 (device).
+ * Replaces ivf_rabitq::search (ivf_rabitq.hpp:361-366; src/neighbors/ivf_rabitq.cu:197-354)
+ * and the id cast (:349-353).  Asynchronous on `stream`. */
+int rbq_search(rbq_index_t* index, const rbq_search_params_t* params, const float* Q_dev, int64_t nq,
+               float* dist_dev, int64_t* ids_dev, void* stream);
+
+/* Same as rbq_search with host buffers: copies queries in and results out on `stream`
+ * (pinned buffers are fastest) and synchronises before returning.  Replaces the CLI's
+ * H2D -> search -> D2H batch loop (rabitq_search.cu:188-204). */
+int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const float* Q_host, int64_t nq,
+                    float* dist_host, int64_t* ids_host, void* stream);
+
+/* Persist / restore.  Replaces serialize / deserialize (ivf_rabitq.hpp:395-423;
+ * gpu_index/ivf_gpu.cu:100-289, 367-461).  This library's own format ("RBQB200"). */
+int rbq_save(rbq_index_t* index, const char* path);
+int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard_count, rbq_index_t** out);
+
+/* ---- introspection (parity tests) ------------------------------------------------------- */
+/* Host copies.  rotation: [Dp*Dp]; centroids: [K*D]; rotated centroids: [K*Dp]. */
+int rbq_get_rotation(rbq_index_t* index, float* P_host);
+int rbq_get_centroids(rbq_index_t* index, float* C_host, float* C_rot_host);
+/* Host copies of the list layout: list_off [K+1], ids [n_local], codes [n_local*W],
+ * f_add / f_rescale / f_err [n_local].  Any output may be NULL. */
+int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint32_t* codes, float* fadd,
+                     float* frescale, float* ferr);
+
+/* ---- stage entry points (device pointers; parity tests and the sharded driver) ----------- */
+/* Y [n, Dp] = pad(X [n, D]) * P.  Replaces RotatorGPU::rotate (rotator_gpu.cu:162-176). */
+int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, void* stream);
+/* 4-bit query quantisation: planes [nq, 4, W], delta [nq], k1 [nq] (= -0.5 sum q).
+ * Replaces exrabitq_quantize_query (searcher_gpu_quantize_query.cu:655-793) and
+ * computeQueryFactorsWarpKernel (gpu_index/ivf_gpu.cu:1451-1490). */
+int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev,
+                   float* delta_dev, float* k1_dev, void* stream);
+/* Coarse quantiser: top-nprobe lists per rotated query, ascending exact distance g.
+ * Replaces PrepareClusterSearchInputs steps 1-4 (gpu_index/ivf_gpu.cu:1513-1628). */
+int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t nprobe, int32_t margin,
+               int32_t* probes_dev, float* g_dev, void* stream);
+/* List scan: top-R candidates (estimated distance, id) per query over its probed lists.
+ * Replaces SearchClusterQueryPairsQuantizeQuery (searcher_gpu_quantize_query.cu:1006-1596).
+ * stats_dev (optional, u64[2]) accumulates vectors scanned / admitted by the prune. */
+int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+             const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+             int32_t R, int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev,
+             float* cand_dist_dev, uint64_t* stats_dev, void* stream);
+/* Phase-1 estimator of one query against every vector of list `list`: integer popcount
+ * inner product acc, estimate est and lower bound low (slot order of the list).  Replaces the
+ * phase-1 loop of computeInnerProductsWithBitwiseBlockSort (searcher_gpu_quantize_query.cu:
+ * 233-281) for inspection; planes_dev is one query's [4, W] planes. */
+int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float delta, float k1, float g,
+                       int32_t list, int32_t* acc_dev, float* est_dev, float* low_dev, void* stream);
+/* Exact fp32 rerank of candidates [nq, R] (id -1 = empty) in the original space -> top-k.
+ * Semantics of cuvs::neighbors::refine (src/neighbors/refine/refine_device.cuh:31-150). */
+int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t* cand_ids_dev, int32_t R,
+               int32_t k, float* dist_dev, int64_t* ids_dev, void* stream);
+/* k-way merge of per-shard results [parts, nq, k] -> [nq, k] by (dist, id).  The on-device
+ * merge after the NCCL all-gather of a list-sharded search. */
+int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t parts, int64_t nq, int32_t k,
+                      float* out_dist_dev, int64_t* out_ids_dev, void* stream);
+
+/* ---- synthetic data (benchmarks and tests) ---------------------------------------------- */
+/* X [n, D]: row i = centre[h(i) % n_centres] + sigma * N(0,1) per dim, centres ~ N(0,1)
+ * (per-dim scale sqrt(1/(1+d/64)) when aniso), L2-normalised when normalize. */
+int rbq_gen_mixture(float* X_dev, int64_t n, int32_t D, int32_t n_centres, float sigma, int32_t aniso,
+                    int32_t normalize, uint64_t seed, void* stream);
+/* Q [nq, D]: row = X[src] + sigma * N(0,1), renormalised when normalize; src_rows_dev
+ * (optional) receives the source rows. */
+int rbq_gen_queries(const float* X_dev, int64_t n, int32_t D, float* Q_dev, int64_t nq, float sigma,
+                    int32_t normalize, uint64_t seed, int64_t* src_rows_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RBQ_H_ */

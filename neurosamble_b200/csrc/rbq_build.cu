@@ -1,0 +1,367 @@
+// Index-build kernels for sm_100a: rotation, 1-bit quantiser + RaBitQ factors, k-means
+// centroid update, row gathers and the synthetic-data generators used by the benchmarks.
+//
+// Compiled with -fmad=false: every float/double expression below is evaluated exactly as
+// written (no FMA contraction), which is what makes the codes and factors bit-identical to
+// the CPU oracle's.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rbq_internal.cuh"
+
+namespace rbq {
+
+// ---------------------------------------------------------------------------------------
+// Rotation: Y[n, Dp] = pad(X[n, D]) * P, P row-major [Dp, Dp] (RotatorGPU::rotate,
+// gpu_index/rotator_gpu.cu:162-176 computes the same product with cuBLAS sgemm).
+// Each output is float(sum_k double(x_k) * double(P[k][j])) accumulated for k = 0..Dp-1;
+// the float*float product is exact in double, so DFMA and DMUL+DADD give the same bits.
+// Block: RB rows x all Dp columns; thread t owns columns t, t+blockDim, ...
+// ---------------------------------------------------------------------------------------
+template <int RB, int CPT>
+__global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X, int64_t n, int D, int Dp,
+                                                     const float* __restrict__ P, float* __restrict__ Y)
+{
+  extern __shared__ float xs[];  // [RB][Dp]
+  const int64_t r0 = (int64_t)blockIdx.x * RB;
+  for (int i = threadIdx.x; i < RB * Dp; i += blockDim.x) {
+    const int r = i / Dp, k = i - r * Dp;
+    const int64_t row = r0 + r;
+    xs[i] = (row < n && k < D) ? X[row * D + k] : 0.0f;
+  }
+  __syncthreads();
+  double acc[RB][CPT];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[r][c] = 0.0;
+  for (int k = 0; k < Dp; ++k) {
+    double p[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      const int j = threadIdx.x + c * blockDim.x;
+      p[c] = (j < Dp) ? (double)P[(size_t)k * Dp + j] : 0.0;
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const double xv = (double)xs[r * Dp + k];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) acc[r][c] = __fma_rn(xv, p[c], acc[r][c]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const int64_t row = r0 + r;
+    if (row >= n) break;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      const int j = threadIdx.x + c * blockDim.x;
+      if (j < Dp) Y[row * Dp + j] = (float)acc[r][c];
+    }
+  }
+}
+
+void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, float* Y, cudaStream_t s)
+{
+  if (n <= 0) return;
+  constexpr int RB = 8;
+  const int threads = Dp < 256 ? Dp : 256;
+  const int cpt = (Dp + threads - 1) / threads;
+  const size_t smem = (size_t)RB * Dp * sizeof(float);
+  const unsigned grid = (unsigned)ceil_div(n, RB);
+  switch (cpt) {
+#define RBQ_ROT_CASE(C)                                                                               \
+  case C:                                                                                             \
+    if (smem > 48 * 1024)                                                                             \
+      RBQ_CUDA(cudaFuncSetAttribute(rotate_kernel<RB, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                    (int)smem));                                                      \
+    rotate_kernel<RB, C><<<grid, threads, smem, s>>>(X, n, D, Dp, P, Y);                              \
+    break;
+    RBQ_ROT_CASE(1)
+    RBQ_ROT_CASE(2)
+    RBQ_ROT_CASE(3)
+    RBQ_ROT_CASE(4)
+    RBQ_ROT_CASE(6)
+    RBQ_ROT_CASE(8)
+#undef RBQ_ROT_CASE
+    default: throw Error{RBQ_ERR_INVALID, "rotation: padded dim must be <= 2048 with Dp/256 in {1,2,3,4,6,8}"};
+  }
+  RBQ_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------------------
+// 1-bit quantiser + factors (subtract_normalize_binarize_Kernel and
+// pack_and_compute_factors_kernel, gpu_index/quantizer_gpu.cu:109-172 and 251-338).
+// One thread per vector; every sum is a double accumulation in dimension order, rounded to
+// float once, so the block-reduction order of the reference does not enter.
+//   r = y - c_rot[label];  bit_j = (|r| > 0 && r_j > 0);  dim 32w+j -> bit 31-j of word w
+//   xu = bit - 0.5;  l2 = |r|^2;  ip = <r, xu> (0 -> +inf);  ipc = <c_rot, xu>;  xu2 = Dp/4
+//   f_add = l2 + 2 l2 * (ipc / ip);  f_rescale = -2 l2 / ip
+//   f_err = 2 * (|r| * 1.9) * sqrt(max(0, (l2 * xu2 / ip^2 - 1) / max(Dp - 1, 1)))
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) quantize_kernel(const float* __restrict__ Y, int64_t n, int Dp,
+                                                       const float* __restrict__ C_rot,
+                                                       const uint32_t* __restrict__ labels,
+                                                       uint32_t* __restrict__ codes, float* __restrict__ fadd,
+                                                       float* __restrict__ frescale, float* __restrict__ ferr)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* y = Y + i * Dp;
+  const float* c = C_rot + (size_t)labels[i] * Dp;
+  double l2d = 0.0;
+  for (int j = 0; j < Dp; ++j) {
+    const float r = y[j] - c[j];
+    l2d += (double)r * (double)r;
+  }
+  const float l2_sqr = (float)l2d;
+  const float norm = sqrtf(l2_sqr);
+  double ipr = 0.0, ipc = 0.0;
+  const int W = Dp >> 5;
+  for (int w = 0; w < W; ++w) {
+    uint32_t word = 0u;
+    for (int b = 0; b < 32; ++b) {
+      const int j = (w << 5) + b;
+      const float r = y[j] - c[j];
+      const int bit = (norm > 0.0f && r > 0.0f) ? 1 : 0;
+      word |= (uint32_t)bit << (31 - b);
+      const double xu = bit ? 0.5 : -0.5;
+      ipr += (double)r * xu;
+      ipc += (double)c[j] * xu;
+    }
+    codes[i * W + w] = word;
+  }
+  float ip_resi = (float)ipr;
+  const float ip_cent = (float)ipc;
+  const float xu_sq = 0.25f * (float)Dp;
+  if (ip_resi == 0.0f) ip_resi = __int_as_float(0x7f800000);
+  const float l2_norm = sqrtf(fmaxf(l2_sqr, 0.0f));
+  const float denom = ip_resi;
+  fadd[i] = l2_sqr + (2.0f * l2_sqr) * (ip_cent / denom);
+  frescale[i] = (-2.0f * l2_sqr) / denom;
+  const float ratio = (l2_sqr * xu_sq) / (denom * denom);
+  float inner = (ratio - 1.0f) / fmaxf((float)(Dp - 1), 1.0f);
+  inner = fmaxf(inner, 0.0f);
+  ferr[i] = 2.0f * ((l2_norm * 1.9f) * sqrtf(inner));
+}
+
+void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, const uint32_t* labels,
+                     uint32_t* codes, float* fadd, float* frescale, float* ferr, cudaStream_t s)
+{
+  if (n <= 0) return;
+  quantize_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, s>>>(Y, n, Dp, C_rot, labels, codes, fadd, frescale,
+                                                             ferr);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+// Row squared norms (float accumulation; only used to rank candidates approximately).
+__global__ void row_norms_kernel(const float* __restrict__ A, int64_t n, int d, float* __restrict__ out)
+{
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  float s = 0.0f;
+  for (int j = lane; j < d; j += 32) {
+    const float v = A[row * d + j];
+    s = __fmaf_rn(v, v, s);
+  }
+  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) out[row] = s;
+}
+
+void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t s)
+{
+  if (n <= 0) return;
+  row_norms_kernel<<<(unsigned)ceil_div(n, 8), 256, 0, s>>>(A, n, d, out);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------------------
+// k-means centroid update: C[c] = mean of member rows, members in the order given by
+// `order` (host counting sort), double accumulation; empty lists keep their centroid.
+// ---------------------------------------------------------------------------------------
+__global__ void centroid_update_kernel(const float* __restrict__ X, int D, const int64_t* __restrict__ off,
+                                       const uint32_t* __restrict__ order, float* __restrict__ C)
+{
+  const int c = blockIdx.x;
+  const int64_t a = off[c], b = off[c + 1];
+  if (b <= a) return;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    double s = 0.0;
+    for (int64_t m = a; m < b; ++m) s += (double)X[(size_t)order[m] * D + j];
+    C[(size_t)c * D + j] = (float)(s / (double)(b - a));
+  }
+}
+
+void launch_centroid_update(const float* X, int64_t /*n*/, int D, const uint32_t* /*labels*/, const int64_t* off,
+                            const uint32_t* order, int K, float* C, cudaStream_t s)
+{
+  centroid_update_kernel<<<K, 128, 0, s>>>(X, D, off, order, C);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+__global__ void gather_rows_kernel(const float* __restrict__ src, int64_t rows, int cols,
+                                   const int64_t* __restrict__ src_row, float* __restrict__ dst)
+{
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t sr = src_row[r];
+  for (int j = threadIdx.x & 31; j < cols; j += 32) dst[r * cols + j] = src[sr * cols + j];
+}
+
+void launch_gather_rows_f32(const float* src, int64_t rows, int cols, const int64_t* src_row, float* dst,
+                            cudaStream_t s)
+{
+  if (rows <= 0) return;
+  gather_rows_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(src, rows, cols, src_row, dst);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------------------
+// Synthetic data for the benchmark configurations (2, 4, 5).
+// Philox-4x32-10 counters; normals by Box-Muller in double (CUDA's log/sincos).
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void philox_dev(uint32_t k0, uint32_t k1, uint32_t c[4])
+{
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]), lo0 = 0xD2511F53u * c[0];
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]), lo1 = 0xCD9E8D57u * c[2];
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+__device__ __forceinline__ double normal_dev(uint64_t seed, uint32_t stream, uint64_t i)
+{
+  const uint64_t blk = i >> 1;
+  uint32_t c[4] = {(uint32_t)blk, (uint32_t)(blk >> 32), stream, 0x52425142u};
+  philox_dev((uint32_t)seed, (uint32_t)(seed >> 32), c);
+  const double scale = 1.0 / 9007199254740992.0;
+  const double u1 = ((double)(((uint64_t)c[0] << 21) ^ (c[1] >> 11)) + 0.5) * scale;
+  const double u2 = ((double)(((uint64_t)c[2] << 21) ^ (c[3] >> 11)) + 0.5) * scale;
+  const double radius = sqrt(-2.0 * log(u1));
+  double sv, cv;
+  sincospi(2.0 * u2, &sv, &cv);
+  return (i & 1) ? radius * sv : radius * cv;
+}
+
+__device__ __forceinline__ uint64_t hash64_dev(uint64_t seed, uint32_t stream, uint64_t i)
+{
+  uint32_t c[4] = {(uint32_t)i, (uint32_t)(i >> 32), stream, 0x48534831u};
+  philox_dev((uint32_t)seed, (uint32_t)(seed >> 32), c);
+  return ((uint64_t)c[0] << 32) | c[1];
+}
+
+__device__ __forceinline__ float dim_scale(int d, int aniso)
+{
+  return aniso ? (float)sqrt(1.0 / (1.0 + (double)d / 64.0)) : 1.0f;
+}
+
+__global__ void gen_centres_kernel(float* __restrict__ C, int nc, int D, int aniso, uint64_t seed, uint32_t stream)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)nc * D) return;
+  const int d = (int)(i % D);
+  C[i] = (float)normal_dev(seed, stream, (uint64_t)i) * dim_scale(d, aniso);
+}
+
+// One warp per row.
+__global__ void gen_rows_kernel(float* __restrict__ X, int64_t n, int D, const float* __restrict__ C, int nc,
+                                float sigma, int aniso, int normalize, uint64_t seed, uint32_t stream)
+{
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const int cen = (int)(hash64_dev(seed, stream, (uint64_t)row) % (uint64_t)nc);
+  float ss = 0.0f;
+  for (int d = lane; d < D; d += 32) {
+    const float v = C[(size_t)cen * D + d] +
+                    sigma * dim_scale(d, aniso) * (float)normal_dev(seed, stream + 1u, (uint64_t)row * D + d);
+    X[row * D + d] = v;
+    ss = __fmaf_rn(v, v, ss);
+  }
+  if (!normalize) return;
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float inv = ss > 0.0f ? 1.0f / sqrtf(ss) : 0.0f;
+  for (int d = lane; d < D; d += 32) X[row * D + d] *= inv;
+}
+
+void launch_gen_mixture(float* X, int64_t n, int D, int n_centres, float sigma, int aniso, int normalize,
+                        uint64_t seed, uint32_t stream, float* centres, cudaStream_t s)
+{
+  const int64_t cn = (int64_t)n_centres * D;
+  gen_centres_kernel<<<(unsigned)ceil_div(cn, 256), 256, 0, s>>>(centres, n_centres, D, aniso, seed, stream);
+  RBQ_CUDA(cudaGetLastError());
+  gen_rows_kernel<<<(unsigned)ceil_div(n, 8), 256, 0, s>>>(X, n, D, centres, n_centres, sigma, aniso, normalize,
+                                                          seed, stream + 1u);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+__global__ void gen_queries_kernel(const float* __restrict__ X, int64_t n, int D, float* __restrict__ Q, int64_t nq,
+                                   float sigma, int normalize, uint64_t seed, uint32_t stream,
+                                   int64_t* __restrict__ src_rows)
+{
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= nq) return;
+  const int64_t src = (int64_t)(hash64_dev(seed, stream, (uint64_t)row) % (uint64_t)n);
+  if (src_rows && lane == 0) src_rows[row] = src;
+  float ss = 0.0f;
+  for (int d = lane; d < D; d += 32) {
+    const float v = X[src * D + d] + sigma * (float)normal_dev(seed, stream + 1u, (uint64_t)row * D + d);
+    Q[row * D + d] = v;
+    ss = __fmaf_rn(v, v, ss);
+  }
+  if (!normalize) return;
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float inv = ss > 0.0f ? 1.0f / sqrtf(ss) : 0.0f;
+  for (int d = lane; d < D; d += 32) Q[row * D + d] *= inv;
+}
+
+void launch_gen_queries(const float* X, int64_t n, int D, float* Q, int64_t nq, float sigma, int normalize,
+                        uint64_t seed, uint32_t stream, int64_t* src_rows, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  gen_queries_kernel<<<(unsigned)ceil_div(nq, 8), 256, 0, s>>>(X, n, D, Q, nq, sigma, normalize, seed, stream,
+                                                              src_rows);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+__global__ void gather_rows_u32_kernel(const uint32_t* __restrict__ src, int64_t rows, int cols,
+                                       const int64_t* __restrict__ src_row, uint32_t* __restrict__ dst)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const int64_t r = i / cols;
+  const int j = (int)(i - r * cols);
+  dst[i] = src[src_row[r] * cols + j];
+}
+
+void launch_gather_rows_u32(const uint32_t* src, int64_t rows, int cols, const int64_t* src_row, uint32_t* dst,
+                            cudaStream_t s)
+{
+  if (rows <= 0) return;
+  gather_rows_u32_kernel<<<(unsigned)ceil_div(rows * cols, 256), 256, 0, s>>>(src, rows, cols, src_row, dst);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+__global__ void scatter_id2row_kernel(const uint32_t* __restrict__ ids, int64_t n, uint32_t* __restrict__ id2row)
+{
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < n) id2row[ids[r]] = (uint32_t)r;
+}
+
+void launch_scatter_id2row(const uint32_t* ids, int64_t n, uint32_t* id2row, cudaStream_t s)
+{
+  if (n <= 0) return;
+  scatter_id2row_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(ids, n, id2row);
+  RBQ_CUDA(cudaGetLastError());
+}
+
+}  // namespace rbq

@@ -1,0 +1,1060 @@
+// C ABI of librbq.so: index lifecycle, k-means training, add (quantise + list layout),
+// the search pipeline, persistence, stage entry points and synthetic data.
+//
+// Every entry point catches everything, stores a message for rbq_last_error() and returns
+// a status code; nothing throws across the ABI and nothing exits or traps.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "rbq_internal.cuh"
+
+struct rbq_index {
+  rbq::Index ix;
+};
+
+namespace rbq {
+namespace {
+
+thread_local std::string g_last_error;
+
+// Switches to `dev` for the scope and restores the caller's device.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev)
+  {
+    RBQ_CUDA(cudaGetDevice(&prev));
+    if (prev != dev) RBQ_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard()
+  {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+template <typename F>
+int guarded(F&& f)
+{
+  try {
+    f();
+    return RBQ_OK;
+  } catch (const Error& e) {
+    g_last_error = e.msg;
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    return RBQ_ERR_OOM;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return RBQ_ERR_INVALID;
+  }
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <typename T>
+T* dev_alloc(size_t count)
+{
+  if (count == 0) count = 1;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw Error{RBQ_ERR_OOM, std::string("cudaMalloc of ") + std::to_string(count * sizeof(T)) +
+                                 " bytes failed: " + cudaGetErrorString(e)};
+  }
+  return static_cast<T*>(p);
+}
+
+template <typename T>
+void dev_free(T*& p)
+{
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+// Stream-ordered scratch from the device's default memory pool (kept cached between calls).
+struct Scratch {
+  cudaStream_t s;
+  std::vector<void*> bufs;
+  explicit Scratch(cudaStream_t st) : s(st) {}
+  template <typename T>
+  T* get(size_t count)
+  {
+    if (count == 0) count = 1;
+    void* p = nullptr;
+    cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), s);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Error{RBQ_ERR_OOM, std::string("cudaMallocAsync of ") + std::to_string(count * sizeof(T)) +
+                                   " bytes failed: " + cudaGetErrorString(e)};
+    }
+    bufs.push_back(p);
+    return static_cast<T*>(p);
+  }
+  ~Scratch()
+  {
+    for (void* p : bufs) cudaFreeAsync(p, s);
+  }
+};
+
+void keep_pool_cached(int device)
+{
+  static bool done[64] = {false};
+  if (device < 0 || device >= 64 || done[device]) return;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  done[device] = true;
+}
+
+// Grow a device array to `count` elements, keeping the first `keep` elements.
+template <typename T>
+void dev_grow(T*& p, size_t keep, size_t count)
+{
+  T* np = dev_alloc<T>(count);
+  if (p && keep) RBQ_CUDA(cudaMemcpy(np, p, keep * sizeof(T), cudaMemcpyDeviceToDevice));
+  dev_free(p);
+  p = np;
+}
+
+void install_centroids(Index& ix, cudaStream_t s)
+{
+  dev_free(ix.C);
+  dev_free(ix.C_rot);
+  dev_free(ix.C_rot_n2);
+  dev_free(ix.C_n2);
+  ix.C = dev_alloc<float>((size_t)ix.K * ix.D);
+  ix.C_rot = dev_alloc<float>((size_t)ix.K * ix.Dp);
+  ix.C_rot_n2 = dev_alloc<float>(ix.K);
+  ix.C_n2 = dev_alloc<float>(ix.K);
+  RBQ_CUDA(cudaMemcpyAsync(ix.C, ix.C_host.data(), ix.C_host.size() * 4, cudaMemcpyHostToDevice, s));
+  launch_rotate(ix.C, ix.K, ix.D, ix.Dp, ix.P, ix.C_rot, s);
+  launch_row_norms(ix.C_rot, ix.K, ix.Dp, ix.C_rot_n2, s);
+  launch_row_norms(ix.C, ix.K, ix.D, ix.C_n2, s);
+  RBQ_CUDA(cudaStreamSynchronize(s));
+  ix.trained = true;
+}
+
+// Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d]: approximate fp32
+// shortlist, then the double-accumulated distance decides.
+void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, int d,
+                   uint32_t* labels_out, cudaStream_t s)
+{
+  const int K = ix.K;
+  const int m = std::min(K, 16);
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65535 * 64, (256ll << 20) / ((int64_t)K * 4)));
+  Scratch sc(s);
+  const int64_t c0 = std::min(n, chunk);
+  float* S = sc.get<float>((size_t)c0 * K);
+  int32_t* cand = sc.get<int32_t>((size_t)c0 * m);
+  int32_t* best = sc.get<int32_t>((size_t)c0);
+  for (int64_t a = 0; a < n; a += chunk) {
+    const int64_t cn = std::min(chunk, n - a);
+    launch_coarse_scores(A + a * d, cn, C, cn2, K, d, S, s);
+    launch_topm_rows(S, cn, K, m, cand, s);
+    launch_refine_topp(A + a * d, cn, C, d, cand, m, 1, best, nullptr, s);
+    RBQ_CUDA(cudaMemcpyAsync(labels_out + a, best, cn * 4, cudaMemcpyDeviceToDevice, s));
+  }
+}
+
+// Stable counting sort of labels: off [K+1], order (row indices grouped by label, ascending).
+void counting_sort(const std::vector<uint32_t>& lab, int K, std::vector<int64_t>& off, std::vector<int64_t>& order)
+{
+  off.assign(K + 1, 0);
+  for (uint32_t l : lab) off[l + 1]++;
+  for (int k = 0; k < K; ++k) off[k + 1] += off[k];
+  std::vector<int64_t> pos(off.begin(), off.end() - 1);
+  order.resize(lab.size());
+  for (size_t i = 0; i < lab.size(); ++i) order[pos[lab[i]]++] = (int64_t)i;
+}
+
+// Rebuild slot-order arrays from the row-order storage.
+void relayout(Index& ix, cudaStream_t s)
+{
+  std::vector<uint32_t> lab(ix.n_rows);
+  if (ix.n_rows)
+    RBQ_CUDA(cudaMemcpyAsync(lab.data(), ix.labels_r, ix.n_rows * 4, cudaMemcpyDeviceToHost, s));
+  RBQ_CUDA(cudaStreamSynchronize(s));
+  std::vector<int64_t> off, order;
+  counting_sort(lab, ix.K, off, order);
+  ix.off_host = off;
+  dev_free(ix.list_off);
+  dev_free(ix.ids);
+  dev_free(ix.codes);
+  dev_free(ix.fadd);
+  dev_free(ix.frescale);
+  dev_free(ix.ferr);
+  const size_t n = (size_t)ix.n_rows;
+  ix.list_off = dev_alloc<int64_t>(ix.K + 1);
+  ix.ids = dev_alloc<uint32_t>(n);
+  ix.codes = dev_alloc<uint32_t>(n * ix.W);
+  ix.fadd = dev_alloc<float>(n);
+  ix.frescale = dev_alloc<float>(n);
+  ix.ferr = dev_alloc<float>(n);
+  RBQ_CUDA(cudaMemcpyAsync(ix.list_off, off.data(), (ix.K + 1) * 8, cudaMemcpyHostToDevice, s));
+  if (n) {
+    Scratch sc(s);
+    int64_t* ord = sc.get<int64_t>(n);
+    RBQ_CUDA(cudaMemcpyAsync(ord, order.data(), n * 8, cudaMemcpyHostToDevice, s));
+    launch_gather_rows_u32(ix.ids_r, ix.n_rows, 1, ord, ix.ids, s);
+    launch_gather_rows_u32(ix.codes_r, ix.n_rows, ix.W, ord, ix.codes, s);
+    launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.fadd_r), ix.n_rows, 1, ord,
+                           reinterpret_cast<uint32_t*>(ix.fadd), s);
+    launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.frescale_r), ix.n_rows, 1, ord,
+                           reinterpret_cast<uint32_t*>(ix.frescale), s);
+    launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.ferr_r), ix.n_rows, 1, ord,
+                           reinterpret_cast<uint32_t*>(ix.ferr), s);
+  }
+  RBQ_CUDA(cudaStreamSynchronize(s));
+}
+
+void ensure_row_capacity(Index& ix, int64_t need)
+{
+  if (need <= ix.cap_rows) return;
+  int64_t cap = std::max<int64_t>(need, ix.cap_rows + ix.cap_rows / 2);
+  const size_t keep = (size_t)ix.n_rows;
+  dev_grow(ix.X_r, keep * ix.D, (size_t)cap * ix.D);
+  dev_grow(ix.codes_r, keep * ix.W, (size_t)cap * ix.W);
+  dev_grow(ix.fadd_r, keep, cap);
+  dev_grow(ix.frescale_r, keep, cap);
+  dev_grow(ix.ferr_r, keep, cap);
+  dev_grow(ix.labels_r, keep, cap);
+  dev_grow(ix.ids_r, keep, cap);
+  ix.cap_rows = cap;
+}
+
+void ensure_id_capacity(Index& ix, int64_t need)
+{
+  if (need <= ix.cap_ids) return;
+  int64_t cap = std::max<int64_t>(need, ix.cap_ids + ix.cap_ids / 2);
+  RBQ_CHECK(cap <= 0xFFFFFFFFll, RBQ_ERR_INVALID, "index supports at most 2^32-1 vectors");
+  uint32_t* np = dev_alloc<uint32_t>(cap);
+  RBQ_CUDA(cudaMemset(np, 0xFF, cap * 4));
+  if (ix.id2row && ix.n_total) RBQ_CUDA(cudaMemcpy(np, ix.id2row, ix.n_total * 4, cudaMemcpyDeviceToDevice));
+  dev_free(ix.id2row);
+  ix.id2row = np;
+  ix.cap_ids = cap;
+}
+
+// Append already-quantised or raw rows: X_dev [n, D] with labels (device) -> this shard's rows.
+void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, cudaStream_t s)
+{
+  RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "add called before train / set_centroids");
+  RBQ_CHECK(n >= 0, RBQ_ERR_INVALID, "add: negative row count");
+  if (n == 0) return;
+  RBQ_CHECK(ix.n_total + n <= 0xFFFFFFFFll, RBQ_ERR_INVALID, "index supports at most 2^32-1 vectors");
+  Scratch sc(s);
+  uint32_t* lab = sc.get<uint32_t>(n);
+  if (labels_dev) {
+    RBQ_CUDA(cudaMemcpyAsync(lab, labels_dev, n * 4, cudaMemcpyDeviceToDevice, s));
+  } else {
+    assign_labels(ix, X, n, ix.C, ix.C_n2, ix.D, lab, s);
+  }
+  std::vector<uint32_t> hl(n);
+  RBQ_CUDA(cudaMemcpyAsync(hl.data(), lab, n * 4, cudaMemcpyDeviceToHost, s));
+  RBQ_CUDA(cudaStreamSynchronize(s));
+  std::vector<int64_t> own;
+  std::vector<uint32_t> own_lab, own_ids;
+  own.reserve(n);
+  for (int64_t i = 0; i < n; ++i) {
+    RBQ_CHECK(hl[i] < (uint32_t)ix.K, RBQ_ERR_INVALID, "add: label out of range");
+    if ((int)(hl[i] % ix.shard_count) == ix.shard_rank) {
+      own.push_back(i);
+      own_lab.push_back(hl[i]);
+      own_ids.push_back((uint32_t)(ix.n_total + i));
+    }
+  }
+  const int64_t m = (int64_t)own.size();
+  ensure_id_capacity(ix, ix.n_total + n);
+  if (m > 0) {
+    ensure_row_capacity(ix, ix.n_rows + m);
+    const int64_t r0 = ix.n_rows;
+    int64_t* src = sc.get<int64_t>(m);
+    RBQ_CUDA(cudaMemcpyAsync(src, own.data(), m * 8, cudaMemcpyHostToDevice, s));
+    launch_gather_rows_f32(X, m, ix.D, src, ix.X_r + (size_t)r0 * ix.D, s);
+    RBQ_CUDA(cudaMemcpyAsync(ix.labels_r + r0, own_lab.data(), m * 4, cudaMemcpyHostToDevice, s));
+    RBQ_CUDA(cudaMemcpyAsync(ix.ids_r + r0, own_ids.data(), m * 4, cudaMemcpyHostToDevice, s));
+    // Rotate + quantise in chunks to bound the rotated-row scratch.
+    const int64_t chunk = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.Dp * 4));
+    float* Y = sc.get<float>((size_t)std::min(chunk, m) * ix.Dp);
+    for (int64_t a = 0; a < m; a += chunk) {
+      const int64_t cn = std::min(chunk, m - a);
+      const int64_t r = r0 + a;
+      launch_rotate(ix.X_r + (size_t)r * ix.D, cn, ix.D, ix.Dp, ix.P, Y, s);
+      launch_quantize(Y, cn, ix.Dp, ix.C_rot, ix.labels_r + r, ix.codes_r + (size_t)r * ix.W, ix.fadd_r + r,
+                      ix.frescale_r + r, ix.ferr_r + r, s);
+    }
+    // id2row for this call's id range [n_total, n_total + n): ids are contiguous per call.
+    std::vector<uint32_t> id2row_new(n, 0xFFFFFFFFu);
+    for (int64_t i = 0; i < m; ++i) id2row_new[own[i]] = (uint32_t)(r0 + i);
+    RBQ_CUDA(cudaMemcpyAsync(ix.id2row + ix.n_total, id2row_new.data(), n * 4, cudaMemcpyHostToDevice, s));
+    RBQ_CUDA(cudaStreamSynchronize(s));
+    ix.n_rows += m;
+  }
+  ix.n_total += n;
+  relayout(ix, s);
+}
+
+void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
+{
+  const int K = ix.K, D = ix.D;
+  RBQ_CHECK(n >= K, RBQ_ERR_INVALID, "train: need at least n_lists rows");
+  const int64_t n_train = std::min<int64_t>(n, (int64_t)ix.max_train_per_list * K);
+  Scratch sc(s);
+  std::vector<int64_t> pick(n_train);
+  for (int64_t i = 0; i < n_train; ++i) pick[i] = (int64_t)(((__int128)i * n) / n_train);
+  int64_t* pick_d = sc.get<int64_t>(n_train);
+  RBQ_CUDA(cudaMemcpyAsync(pick_d, pick.data(), n_train * 8, cudaMemcpyHostToDevice, s));
+  float* Xs = sc.get<float>((size_t)n_train * D);
+  launch_gather_rows_f32(X, n_train, D, pick_d, Xs, s);
+  std::vector<int64_t> ipick(K);
+  for (int k = 0; k < K; ++k) ipick[k] = (int64_t)(((__int128)k * n_train) / K);
+  int64_t* ipick_d = sc.get<int64_t>(K);
+  RBQ_CUDA(cudaMemcpyAsync(ipick_d, ipick.data(), K * 8, cudaMemcpyHostToDevice, s));
+  float* C = sc.get<float>((size_t)K * D);
+  float* cn2 = sc.get<float>(K);
+  launch_gather_rows_f32(Xs, K, D, ipick_d, C, s);
+  uint32_t* lab = sc.get<uint32_t>(n_train);
+  int64_t* off_d = sc.get<int64_t>(K + 1);
+  uint32_t* order_d = sc.get<uint32_t>(n_train);
+  std::vector<uint32_t> hl(n_train), ho(n_train);
+  std::vector<int64_t> off, order;
+  for (int it = 0; it < ix.kmeans_iters; ++it) {
+    launch_row_norms(C, K, D, cn2, s);
+    assign_labels(ix, Xs, n_train, C, cn2, D, lab, s);
+    RBQ_CUDA(cudaMemcpyAsync(hl.data(), lab, n_train * 4, cudaMemcpyDeviceToHost, s));
+    RBQ_CUDA(cudaStreamSynchronize(s));
+    counting_sort(hl, K, off, order);
+    for (int64_t i = 0; i < n_train; ++i) ho[i] = (uint32_t)order[i];
+    RBQ_CUDA(cudaMemcpyAsync(off_d, off.data(), (K + 1) * 8, cudaMemcpyHostToDevice, s));
+    RBQ_CUDA(cudaMemcpyAsync(order_d, ho.data(), n_train * 4, cudaMemcpyHostToDevice, s));
+    launch_centroid_update(Xs, n_train, D, lab, off_d, order_d, K, C, s);
+  }
+  ix.C_host.resize((size_t)K * D);
+  RBQ_CUDA(cudaMemcpyAsync(ix.C_host.data(), C, (size_t)K * D * 4, cudaMemcpyDeviceToHost, s));
+  RBQ_CUDA(cudaStreamSynchronize(s));
+  install_centroids(ix, s);
+}
+
+struct SearchPlan {
+  int P, k, R, cap, slices, m;
+  int prune;
+};
+
+SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq)
+{
+  RBQ_CHECK(p.k >= 1, RBQ_ERR_INVALID, "search: k must be >= 1");
+  RBQ_CHECK(p.n_probes >= 1 && p.n_probes <= ix.K, RBQ_ERR_INVALID,
+            "search: n_probes (" + std::to_string(p.n_probes) + ") must be in [1, n_lists = " +
+                std::to_string(ix.K) + "]");
+  RBQ_CHECK(p.rerank >= 0, RBQ_ERR_INVALID, "search: rerank must be >= 0");
+  SearchPlan sp;
+  sp.P = p.n_probes;
+  sp.k = p.k;
+  sp.R = p.rerank > 0 ? std::max(p.rerank, p.k) : p.k;
+  RBQ_CHECK(sp.R <= 4096, RBQ_ERR_INVALID, "search: rerank depth / k must be <= 4096");
+  sp.cap = p.cand_cap > 0 ? p.cand_cap : 1024;
+  sp.cap = std::max(next_pow2(sp.cap), next_pow2(sp.R + kScanTile));
+  int own = std::max(1, (sp.P + ix.shard_count - 1) / ix.shard_count);
+  int sl = p.probe_split > 0 ? p.probe_split : (int)std::max<int64_t>(1, 512 / std::max<int64_t>(1, nq));
+  sl = std::min(sl, own);
+  sl = std::min(sl, std::max(1, 8192 / sp.R));
+  sp.slices = std::max(1, sl);
+  const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(16, sp.P / 2);
+  sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
+  sp.prune = p.prune ? 1 : 0;
+  return sp;
+}
+
+void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, int64_t nq, float* dist, int64_t* ids,
+                cudaStream_t s, uint64_t* stats)
+{
+  RBQ_CHECK(nq >= 0, RBQ_ERR_INVALID, "search: negative query count");
+  if (nq == 0) return;
+  RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "search called before train / set_centroids");
+  const SearchPlan sp = plan_search(ix, params, nq);
+  const int64_t by_scores = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4));
+  const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_scores, 65535ll * 64));
+  Scratch sc(s);
+  float* Qr = sc.get<float>((size_t)chunk * ix.Dp);
+  float* S = sc.get<float>((size_t)chunk * ix.K);
+  int32_t* cand = sc.get<int32_t>((size_t)chunk * sp.m);
+  int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
+  float* g = sc.get<float>((size_t)chunk * sp.P);
+  uint32_t* planes = sc.get<uint32_t>((size_t)chunk * 4 * ix.W);
+  float* delta = sc.get<float>(chunk);
+  float* k1 = sc.get<float>(chunk);
+  unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
+  unsigned long long* keys = sp.slices > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : keys_s;
+  for (int64_t a = 0; a < nq; a += chunk) {
+    const int64_t cn = std::min(chunk, nq - a);
+    const float* Qc = Q + a * ix.D;
+    launch_rotate(Qc, cn, ix.D, ix.Dp, ix.P, Qr, s);
+    launch_coarse_scores(Qr, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, s);
+    launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
+    launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
+    launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
+    ScanArgs sa;
+    sa.list_off = ix.list_off;
+    sa.ids = ix.ids;
+    sa.codes = ix.codes;
+    sa.fadd = ix.fadd;
+    sa.frescale = ix.frescale;
+    sa.ferr = ix.ferr;
+    sa.Dp = ix.Dp;
+    sa.W = ix.W;
+    sa.Qr = Qr;
+    sa.planes = planes;
+    sa.delta = delta;
+    sa.k1 = k1;
+    sa.nq = cn;
+    sa.probes = probes;
+    sa.g = g;
+    sa.nprobe = sp.P;
+    sa.R = sp.R;
+    sa.cap = sp.cap;
+    sa.prune = sp.prune;
+    sa.slices = sp.slices;
+    sa.shard_rank = ix.shard_rank;
+    sa.shard_count = ix.shard_count;
+    sa.out_keys = keys_s;
+    sa.stats = reinterpret_cast<unsigned long long*>(stats);
+    launch_scan(sa, s);
+    if (sp.slices > 1) launch_merge_keys(keys_s, cn, sp.slices, sp.R, keys, s);
+    if (params.rerank > 0)
+      launch_rerank(ix.X_r, ix.id2row, ix.D, Qc, cn, keys, sp.R, sp.k, dist + a * sp.k, ids + a * sp.k, s);
+    else
+      launch_keys_to_result(keys, cn, sp.R, sp.k, dist + a * sp.k, ids + a * sp.k, s);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Persistence: "RBQB200\0", version, dims, seed, t4, P, C, then this shard's rows.
+// ---------------------------------------------------------------------------------------
+const char kMagic[8] = {'R', 'B', 'Q', 'B', '2', '0', '0', '\0'};
+constexpr uint32_t kFormatVersion = 1;
+
+struct File {
+  FILE* f = nullptr;
+  std::string path;
+  File(const char* p, const char* mode) : path(p ? p : "")
+  {
+    RBQ_CHECK(p != nullptr, RBQ_ERR_INVALID, "null path");
+    f = std::fopen(p, mode);
+    RBQ_CHECK(f != nullptr, RBQ_ERR_IO, "cannot open " + path);
+  }
+  ~File()
+  {
+    if (f) std::fclose(f);
+  }
+  void write(const void* d, size_t n)
+  {
+    if (n) RBQ_CHECK(std::fwrite(d, 1, n, f) == n, RBQ_ERR_IO, "write failed: " + path);
+  }
+  void read(void* d, size_t n)
+  {
+    if (n) RBQ_CHECK(std::fread(d, 1, n, f) == n, RBQ_ERR_FORMAT, "truncated index file: " + path);
+  }
+};
+
+template <typename T>
+void write_dev(File& f, const T* p, size_t count)
+{
+  std::vector<T> h(count);
+  if (count) RBQ_CUDA(cudaMemcpy(h.data(), p, count * sizeof(T), cudaMemcpyDeviceToHost));
+  f.write(h.data(), count * sizeof(T));
+}
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+void free_index_memory(Index& ix)
+{
+  dev_free(ix.P);
+  dev_free(ix.C);
+  dev_free(ix.C_rot);
+  dev_free(ix.C_rot_n2);
+  dev_free(ix.C_n2);
+  dev_free(ix.X_r);
+  dev_free(ix.codes_r);
+  dev_free(ix.fadd_r);
+  dev_free(ix.frescale_r);
+  dev_free(ix.ferr_r);
+  dev_free(ix.labels_r);
+  dev_free(ix.ids_r);
+  dev_free(ix.id2row);
+  dev_free(ix.list_off);
+  dev_free(ix.ids);
+  dev_free(ix.codes);
+  dev_free(ix.fadd);
+  dev_free(ix.frescale);
+  dev_free(ix.ferr);
+}
+
+}  // namespace rbq
+
+using namespace rbq;
+
+extern "C" {
+
+const char* rbq_last_error(void) { return g_last_error.c_str(); }
+
+int rbq_version(void) { return 1; }
+
+void rbq_index_params_default(rbq_index_params_t* p)
+{
+  if (!p) return;
+  p->dim = 0;
+  p->n_lists = 1024;
+  p->seed = 7;
+  p->kmeans_n_iters = 20;
+  p->max_train_points_per_cluster = 256;
+  p->device = 0;
+  p->shard_rank = 0;
+  p->shard_count = 1;
+}
+
+void rbq_search_params_default(rbq_search_params_t* p)
+{
+  if (!p) return;
+  p->n_probes = 20;
+  p->k = 10;
+  p->rerank = 0;
+  p->prune = 1;
+  p->probe_split = 0;
+  p->cand_cap = 0;
+  p->coarse_margin = 0;
+}
+
+int rbq_make_rotation(int32_t padded_dim, uint64_t seed, float* P_host)
+{
+  return guarded([&] {
+    RBQ_CHECK(P_host && padded_dim >= 32 && padded_dim % 32 == 0 && padded_dim <= 2048, RBQ_ERR_INVALID,
+              "padded_dim must be a multiple of 32 in [32, 2048]");
+    make_rotation(padded_dim, seed, P_host);
+  });
+}
+
+int rbq_query_scale(int32_t padded_dim, uint64_t seed, int32_t ex_bits, float* t_out)
+{
+  return guarded([&] {
+    RBQ_CHECK(t_out && padded_dim >= 1 && ex_bits >= 1 && ex_bits <= 8, RBQ_ERR_INVALID, "bad arguments");
+    *t_out = query_scale(padded_dim, seed, ex_bits);
+  });
+}
+
+int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
+{
+  return guarded([&] {
+    RBQ_CHECK(params && out, RBQ_ERR_INVALID, "null argument");
+    *out = nullptr;
+    RBQ_CHECK(params->dim >= 1 && params->dim <= 2048, RBQ_ERR_INVALID, "dim must be in [1, 2048]");
+    RBQ_CHECK(params->n_lists >= 1, RBQ_ERR_INVALID, "n_lists must be >= 1");
+    RBQ_CHECK(params->shard_count >= 1 && params->shard_rank >= 0 && params->shard_rank < params->shard_count,
+              RBQ_ERR_INVALID, "bad shard rank / count");
+    RBQ_CHECK(params->kmeans_n_iters >= 0 && params->max_train_points_per_cluster >= 1, RBQ_ERR_INVALID,
+              "bad k-means parameters");
+    int ndev = 0;
+    RBQ_CUDA(cudaGetDeviceCount(&ndev));
+    RBQ_CHECK(params->device >= 0 && params->device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
+    DeviceGuard dg(params->device);
+    keep_pool_cached(params->device);
+    rbq_index* h = new rbq_index();
+    Index& ix = h->ix;
+    ix.device = params->device;
+    ix.D = params->dim;
+    ix.Dp = (params->dim + 31) / 32 * 32;
+    ix.W = ix.Dp / 32;
+    ix.K = params->n_lists;
+    ix.seed = params->seed;
+    ix.kmeans_iters = params->kmeans_n_iters;
+    ix.max_train_per_list = params->max_train_points_per_cluster;
+    ix.shard_rank = params->shard_rank;
+    ix.shard_count = params->shard_count;
+    try {
+      ix.P_host.resize((size_t)ix.Dp * ix.Dp);
+      make_rotation(ix.Dp, ix.seed, ix.P_host.data());
+      ix.t4 = query_scale(ix.Dp, ix.seed, 3);
+      ix.P = dev_alloc<float>(ix.P_host.size());
+      RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
+      ix.off_host.assign(ix.K + 1, 0);
+      ix.list_off = dev_alloc<int64_t>(ix.K + 1);
+      RBQ_CUDA(cudaMemset(ix.list_off, 0, (ix.K + 1) * 8));
+    } catch (...) {
+      free_index_memory(ix);
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int rbq_index_free(rbq_index_t* index)
+{
+  return guarded([&] {
+    if (!index) return;
+    {
+      DeviceGuard dg(index->ix.device);
+      free_index_memory(index->ix);
+    }
+    delete index;
+  });
+}
+
+int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && out, RBQ_ERR_INVALID, "null argument");
+    const Index& ix = index->ix;
+    out->dim = ix.D;
+    out->padded_dim = ix.Dp;
+    out->n_lists = ix.K;
+    out->shard_rank = ix.shard_rank;
+    out->shard_count = ix.shard_count;
+    out->trained = ix.trained ? 1 : 0;
+    out->n_total = ix.n_total;
+    out->n_local = ix.n_rows;
+    out->query_scale = ix.t4;
+    out->seed = ix.seed;
+    const int64_t per_row = (int64_t)ix.D * 4 + (int64_t)ix.W * 4 * 2 + 12 * 2 + 4 * 3;
+    out->device_bytes = ix.cap_rows * per_row + ix.cap_ids * 4 + (int64_t)ix.Dp * ix.Dp * 4 +
+                        (int64_t)ix.K * (ix.D + ix.Dp + 2) * 4 + (ix.K + 1) * 8;
+  });
+}
+
+int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && X_dev, RBQ_ERR_INVALID, "null argument");
+    DeviceGuard dg(index->ix.device);
+    train_kmeans(index->ix, X_dev, n, as_stream(stream));
+  });
+}
+
+int rbq_set_centroids(rbq_index_t* index, const float* C_host, int32_t n_lists)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && C_host, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(n_lists == ix.K, RBQ_ERR_INVALID, "set_centroids: n_lists mismatch");
+    RBQ_CHECK(ix.n_total == 0, RBQ_ERR_STATE, "set_centroids: index already holds vectors");
+    DeviceGuard dg(ix.device);
+    ix.C_host.assign(C_host, C_host + (size_t)ix.K * ix.D);
+    install_centroids(ix, 0);
+  });
+}
+
+int rbq_add(rbq_index_t* index, const float* X_dev, int64_t n, const uint32_t* labels_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && (X_dev || n == 0), RBQ_ERR_INVALID, "null argument");
+    DeviceGuard dg(index->ix.device);
+    add_rows(index->ix, X_dev, n, labels_dev, as_stream(stream));
+  });
+}
+
+int rbq_search(rbq_index_t* index, const rbq_search_params_t* params, const float* Q_dev, int64_t nq,
+               float* dist_dev, int64_t* ids_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && params, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Q_dev && dist_dev && ids_dev), RBQ_ERR_INVALID, "null buffer");
+    DeviceGuard dg(index->ix.device);
+    run_search(index->ix, *params, Q_dev, nq, dist_dev, ids_dev, as_stream(stream), nullptr);
+  });
+}
+
+int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const float* Q_host, int64_t nq,
+                    float* dist_host, int64_t* ids_host, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && params, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Q_host && dist_host && ids_host), RBQ_ERR_INVALID, "null buffer");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    Scratch sc(s);
+    float* q = sc.get<float>((size_t)nq * ix.D);
+    float* d = sc.get<float>((size_t)nq * params->k);
+    int64_t* i = sc.get<int64_t>((size_t)nq * params->k);
+    RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
+    run_search(ix, *params, q, nq, d, i, s, nullptr);
+    RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * params->k * 4, cudaMemcpyDeviceToHost, s));
+    RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * params->k * 8, cudaMemcpyDeviceToHost, s));
+    RBQ_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int rbq_save(rbq_index_t* index, const char* path)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null index");
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    RBQ_CUDA(cudaDeviceSynchronize());
+    File f(path, "wb");
+    f.write(kMagic, 8);
+    f.write(&kFormatVersion, 4);
+    int32_t hdr[8] = {ix.D, ix.Dp, ix.K, ix.kmeans_iters, ix.max_train_per_list, ix.shard_rank, ix.shard_count,
+                      ix.trained ? 1 : 0};
+    f.write(hdr, sizeof(hdr));
+    f.write(&ix.seed, 8);
+    f.write(&ix.t4, 4);
+    f.write(&ix.n_total, 8);
+    f.write(&ix.n_rows, 8);
+    f.write(ix.P_host.data(), ix.P_host.size() * 4);
+    if (ix.trained) f.write(ix.C_host.data(), ix.C_host.size() * 4);
+    const size_t n = (size_t)ix.n_rows;
+    write_dev(f, ix.labels_r, n);
+    write_dev(f, ix.ids_r, n);
+    write_dev(f, ix.codes_r, n * ix.W);
+    write_dev(f, ix.fadd_r, n);
+    write_dev(f, ix.frescale_r, n);
+    write_dev(f, ix.ferr_r, n);
+    write_dev(f, ix.X_r, n * ix.D);
+  });
+}
+
+int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard_count, rbq_index_t** out)
+{
+  return guarded([&] {
+    RBQ_CHECK(out, RBQ_ERR_INVALID, "null argument");
+    *out = nullptr;
+    File f(path, "rb");
+    char magic[8];
+    f.read(magic, 8);
+    RBQ_CHECK(std::memcmp(magic, kMagic, 8) == 0, RBQ_ERR_FORMAT, "not an RBQB200 index file: " + f.path);
+    uint32_t ver = 0;
+    f.read(&ver, 4);
+    RBQ_CHECK(ver == kFormatVersion, RBQ_ERR_FORMAT, "unsupported index file version");
+    int32_t hdr[8];
+    f.read(hdr, sizeof(hdr));
+    uint64_t seed;
+    float t4;
+    int64_t n_total, n_rows;
+    f.read(&seed, 8);
+    f.read(&t4, 4);
+    f.read(&n_total, 8);
+    f.read(&n_rows, 8);
+    const int D = hdr[0], Dp = hdr[1], K = hdr[2];
+    RBQ_CHECK(D >= 1 && D <= 2048 && Dp == (D + 31) / 32 * 32 && K >= 1 && n_rows >= 0 && n_total >= n_rows,
+              RBQ_ERR_FORMAT, "corrupt index header");
+    const int file_rank = hdr[5], file_count = hdr[6];
+    if (shard_count <= 0) {
+      shard_count = file_count;
+      shard_rank = file_rank;
+    }
+    RBQ_CHECK(file_count == 1 || (file_count == shard_count && file_rank == shard_rank), RBQ_ERR_INVALID,
+              "index file holds shard " + std::to_string(file_rank) + "/" + std::to_string(file_count));
+    rbq_index_params_t p;
+    rbq_index_params_default(&p);
+    p.dim = D;
+    p.n_lists = K;
+    p.seed = seed;
+    p.kmeans_n_iters = hdr[3];
+    p.max_train_points_per_cluster = hdr[4];
+    p.device = device;
+    p.shard_rank = shard_rank;
+    p.shard_count = shard_count;
+    RBQ_CHECK(p.shard_count >= 1 && p.shard_rank >= 0 && p.shard_rank < p.shard_count, RBQ_ERR_INVALID,
+              "bad shard rank / count");
+    int ndev = 0;
+    RBQ_CUDA(cudaGetDeviceCount(&ndev));
+    RBQ_CHECK(device >= 0 && device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
+    DeviceGuard dg(device);
+    keep_pool_cached(device);
+    rbq_index* h = new rbq_index();
+    Index& ix = h->ix;
+    try {
+      ix.device = device;
+      ix.D = D;
+      ix.Dp = Dp;
+      ix.W = Dp / 32;
+      ix.K = K;
+      ix.seed = seed;
+      ix.kmeans_iters = p.kmeans_n_iters;
+      ix.max_train_per_list = p.max_train_points_per_cluster;
+      ix.shard_rank = p.shard_rank;
+      ix.shard_count = p.shard_count;
+      ix.t4 = t4;
+      ix.P_host.resize((size_t)Dp * Dp);
+      f.read(ix.P_host.data(), ix.P_host.size() * 4);
+      ix.P = dev_alloc<float>(ix.P_host.size());
+      RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
+      ix.off_host.assign(K + 1, 0);
+      ix.list_off = dev_alloc<int64_t>(K + 1);
+      RBQ_CUDA(cudaMemset(ix.list_off, 0, (K + 1) * 8));
+      if (hdr[7]) {
+        ix.C_host.resize((size_t)K * D);
+        f.read(ix.C_host.data(), ix.C_host.size() * 4);
+        install_centroids(ix, 0);
+      }
+      const int W = ix.W;
+      std::vector<uint32_t> lab(n_rows), ids(n_rows), codes((size_t)n_rows * W);
+      std::vector<float> fa(n_rows), fr(n_rows), fe(n_rows), X((size_t)n_rows * D);
+      f.read(lab.data(), lab.size() * 4);
+      f.read(ids.data(), ids.size() * 4);
+      f.read(codes.data(), codes.size() * 4);
+      f.read(fa.data(), fa.size() * 4);
+      f.read(fr.data(), fr.size() * 4);
+      f.read(fe.data(), fe.size() * 4);
+      f.read(X.data(), X.size() * 4);
+      std::vector<int64_t> keep;
+      for (int64_t i = 0; i < n_rows; ++i) {
+        RBQ_CHECK(lab[i] < (uint32_t)K && ids[i] < (uint64_t)n_total, RBQ_ERR_FORMAT, "corrupt row data");
+        if ((int)(lab[i] % ix.shard_count) == ix.shard_rank) keep.push_back(i);
+      }
+      const int64_t m = (int64_t)keep.size();
+      auto pick_u32 = [&](const std::vector<uint32_t>& src, int w) {
+        std::vector<uint32_t> o((size_t)m * w);
+        for (int64_t i = 0; i < m; ++i)
+          std::memcpy(&o[(size_t)i * w], &src[(size_t)keep[i] * w], (size_t)w * 4);
+        return o;
+      };
+      auto pick_f32 = [&](const std::vector<float>& src, int w) {
+        std::vector<float> o((size_t)m * w);
+        for (int64_t i = 0; i < m; ++i)
+          std::memcpy(&o[(size_t)i * w], &src[(size_t)keep[i] * w], (size_t)w * 4);
+        return o;
+      };
+      ensure_id_capacity(ix, std::max<int64_t>(n_total, 1));
+      ensure_row_capacity(ix, std::max<int64_t>(m, 1));
+      auto up = [&](void* dst, const void* src, size_t bytes) {
+        if (bytes) RBQ_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+      };
+      auto l2 = pick_u32(lab, 1), i2 = pick_u32(ids, 1), c2 = pick_u32(codes, W);
+      auto fa2 = pick_f32(fa, 1), fr2 = pick_f32(fr, 1), fe2 = pick_f32(fe, 1), x2 = pick_f32(X, D);
+      up(ix.labels_r, l2.data(), m * 4);
+      up(ix.ids_r, i2.data(), m * 4);
+      up(ix.codes_r, c2.data(), (size_t)m * W * 4);
+      up(ix.fadd_r, fa2.data(), m * 4);
+      up(ix.frescale_r, fr2.data(), m * 4);
+      up(ix.ferr_r, fe2.data(), m * 4);
+      up(ix.X_r, x2.data(), (size_t)m * D * 4);
+      std::vector<uint32_t> id2row(n_total, 0xFFFFFFFFu);
+      for (int64_t i = 0; i < m; ++i) id2row[i2[i]] = (uint32_t)i;
+      up(ix.id2row, id2row.data(), (size_t)n_total * 4);
+      ix.n_rows = m;
+      ix.n_total = n_total;
+      relayout(ix, 0);
+    } catch (...) {
+      free_index_memory(ix);
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int rbq_get_rotation(rbq_index_t* index, float* P_host)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && P_host, RBQ_ERR_INVALID, "null argument");
+    std::memcpy(P_host, index->ix.P_host.data(), index->ix.P_host.size() * 4);
+  });
+}
+
+int rbq_get_centroids(rbq_index_t* index, float* C_host, float* C_rot_host)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "index is not trained");
+    if (C_host) std::memcpy(C_host, ix.C_host.data(), ix.C_host.size() * 4);
+    if (C_rot_host) {
+      DeviceGuard dg(ix.device);
+      RBQ_CUDA(cudaMemcpy(C_rot_host, ix.C_rot, (size_t)ix.K * ix.Dp * 4, cudaMemcpyDeviceToHost));
+    }
+  });
+}
+
+int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint32_t* codes, float* fadd,
+                     float* frescale, float* ferr)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    RBQ_CUDA(cudaDeviceSynchronize());
+    const size_t n = (size_t)ix.n_rows;
+    if (list_off) std::memcpy(list_off, ix.off_host.data(), (ix.K + 1) * 8);
+    if (n == 0) return;
+    if (ids) RBQ_CUDA(cudaMemcpy(ids, ix.ids, n * 4, cudaMemcpyDeviceToHost));
+    if (codes) RBQ_CUDA(cudaMemcpy(codes, ix.codes, n * ix.W * 4, cudaMemcpyDeviceToHost));
+    if (fadd) RBQ_CUDA(cudaMemcpy(fadd, ix.fadd, n * 4, cudaMemcpyDeviceToHost));
+    if (frescale) RBQ_CUDA(cudaMemcpy(frescale, ix.frescale, n * 4, cudaMemcpyDeviceToHost));
+    if (ferr) RBQ_CUDA(cudaMemcpy(ferr, ix.ferr, n * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && (n == 0 || (X_dev && Y_dev)), RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    launch_rotate(X_dev, n, ix.D, ix.Dp, ix.P, Y_dev, as_stream(stream));
+  });
+}
+
+int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev, float* delta_dev,
+                   float* k1_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && (nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev)), RBQ_ERR_INVALID,
+              "null argument");
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    launch_query_prep(Qr_dev, nq, ix.Dp, ix.t4, planes_dev, delta_dev, k1_dev, as_stream(stream));
+  });
+}
+
+int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t nprobe, int32_t margin,
+               int32_t* probes_dev, float* g_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && (nq == 0 || (Qr_dev && probes_dev && g_dev)), RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "index is not trained");
+    RBQ_CHECK(nprobe >= 1 && nprobe <= ix.K, RBQ_ERR_INVALID, "nprobe must be in [1, n_lists]");
+    if (nq == 0) return;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    const int m = std::min(ix.K, std::min(nprobe + (margin > 0 ? margin : std::max(16, nprobe / 2)), 1024));
+    const int64_t chunk = std::min<int64_t>(nq, std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4)));
+    Scratch sc(s);
+    float* S = sc.get<float>((size_t)chunk * ix.K);
+    int32_t* cand = sc.get<int32_t>((size_t)chunk * m);
+    for (int64_t a = 0; a < nq; a += chunk) {
+      const int64_t cn = std::min(chunk, nq - a);
+      launch_coarse_scores(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, s);
+      launch_topm_rows(S, cn, ix.K, m, cand, s);
+      launch_refine_topp(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.Dp, cand, m, nprobe, probes_dev + a * nprobe,
+                         g_dev + a * nprobe, s);
+    }
+  });
+}
+
+int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+             const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe, int32_t R,
+             int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
+             uint64_t* stats_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && cand_ids_dev &&
+                          cand_dist_dev),
+              RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1, RBQ_ERR_INVALID, "bad scan parameters");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
+    Scratch sc(s);
+    unsigned long long* ks = sc.get<unsigned long long>((size_t)nq * slices * R);
+    unsigned long long* k2 = slices > 1 ? sc.get<unsigned long long>((size_t)nq * R) : ks;
+    ScanArgs sa;
+    sa.list_off = ix.list_off;
+    sa.ids = ix.ids;
+    sa.codes = ix.codes;
+    sa.fadd = ix.fadd;
+    sa.frescale = ix.frescale;
+    sa.ferr = ix.ferr;
+    sa.Dp = ix.Dp;
+    sa.W = ix.W;
+    sa.Qr = Qr_dev;
+    sa.planes = planes_dev;
+    sa.delta = delta_dev;
+    sa.k1 = k1_dev;
+    sa.nq = nq;
+    sa.probes = probes_dev;
+    sa.g = g_dev;
+    sa.nprobe = nprobe;
+    sa.R = R;
+    sa.cap = cap;
+    sa.prune = prune ? 1 : 0;
+    sa.slices = slices;
+    sa.shard_rank = ix.shard_rank;
+    sa.shard_count = ix.shard_count;
+    sa.out_keys = ks;
+    sa.stats = reinterpret_cast<unsigned long long*>(stats_dev);
+    launch_scan(sa, s);
+    if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
+    launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);
+  });
+}
+
+int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float delta, float k1, float g, int32_t list,
+                       int32_t* acc_dev, float* est_dev, float* low_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && planes_dev && acc_dev && est_dev && low_dev, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(list >= 0 && list < ix.K, RBQ_ERR_INVALID, "list out of range");
+    DeviceGuard dg(ix.device);
+    launch_list_estimates(ix, planes_dev, delta, k1, g, list, acc_dev, est_dev, low_dev, as_stream(stream));
+  });
+}
+
+int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t* cand_ids_dev, int32_t R, int32_t k,
+               float* dist_dev, int64_t* ids_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Q_dev && cand_ids_dev && dist_dev && ids_dev), RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(R >= 1 && R <= 4096 && k >= 1, RBQ_ERR_INVALID, "bad rerank parameters");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    Scratch sc(s);
+    unsigned long long* keys = sc.get<unsigned long long>((size_t)nq * R);
+    launch_ids_to_keys(cand_ids_dev, nq * R, keys, s);
+    launch_rerank(ix.X_r, ix.id2row, ix.D, Q_dev, nq, keys, R, k, dist_dev, ids_dev, s);
+  });
+}
+
+int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t parts, int64_t nq, int32_t k,
+                      float* out_dist_dev, int64_t* out_ids_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(parts >= 1 && k >= 1 && nq >= 0, RBQ_ERR_INVALID, "bad merge parameters");
+    RBQ_CHECK(nq == 0 || (dist_dev && ids_dev && out_dist_dev && out_ids_dev), RBQ_ERR_INVALID, "null buffer");
+    launch_merge_results(dist_dev, ids_dev, parts, nq, k, out_dist_dev, out_ids_dev, as_stream(stream));
+  });
+}
+
+int rbq_gen_mixture(float* X_dev, int64_t n, int32_t D, int32_t n_centres, float sigma, int32_t aniso,
+                    int32_t normalize, uint64_t seed, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(X_dev && n >= 0 && D >= 1 && n_centres >= 1, RBQ_ERR_INVALID, "bad generator arguments");
+    cudaStream_t s = as_stream(stream);
+    Scratch sc(s);
+    float* cen = sc.get<float>((size_t)n_centres * D);
+    launch_gen_mixture(X_dev, n, D, n_centres, sigma, aniso, normalize, seed, 10u, cen, s);
+  });
+}
+
+int rbq_gen_queries(const float* X_dev, int64_t n, int32_t D, float* Q_dev, int64_t nq, float sigma,
+                    int32_t normalize, uint64_t seed, int64_t* src_rows_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(X_dev && Q_dev && n >= 1 && D >= 1 && nq >= 0, RBQ_ERR_INVALID, "bad generator arguments");
+    launch_gen_queries(X_dev, n, D, Q_dev, nq, sigma, normalize, seed, 20u, src_rows_dev, as_stream(stream));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,213 @@
+// Internal declarations of the B200 IVF-RaBitQ library (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/rbq.h"
+
+namespace rbq {
+
+// ---------------------------------------------------------------------------------------
+// Error plumbing: every C-ABI entry point returns an int status and never throws or exits.
+// ---------------------------------------------------------------------------------------
+void set_error(const std::string& msg);
+struct Error {
+  int code;
+  std::string msg;
+};
+
+#define RBQ_CUDA(call)                                                                     \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      throw ::rbq::Error{RBQ_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)}; \
+  } while (0)
+
+#define RBQ_CHECK(cond, code, msg)                        \
+  do {                                                    \
+    if (!(cond)) throw ::rbq::Error{(code), (msg)};       \
+  } while (0)
+
+// ---------------------------------------------------------------------------------------
+// Keys: (order-preserving float bits << 32) | id.  Ascending keys = ascending distance,
+// ties broken by the smaller id.  All-ones = empty slot.
+// ---------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint32_t ordered_bits(float f)
+{
+  uint32_t u;
+#ifdef __CUDA_ARCH__
+  u = __float_as_uint(f);
+#else
+  __builtin_memcpy(&u, &f, 4);
+#endif
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ __forceinline__ float from_ordered_bits(uint32_t o)
+{
+  uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+  float f;
+#ifdef __CUDA_ARCH__
+  f = __uint_as_float(u);
+#else
+  __builtin_memcpy(&f, &u, 4);
+#endif
+  return f;
+}
+__host__ __device__ __forceinline__ unsigned long long make_key(float d, uint32_t id)
+{
+  return ((unsigned long long)ordered_bits(d) << 32) | id;
+}
+constexpr unsigned long long kEmptyKey = ~0ull;
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int next_pow2(int v)
+{
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// ---------------------------------------------------------------------------------------
+// Device-resident index.  All per-vector arrays are in list-slot order: list l owns slots
+// [list_off[l], list_off[l+1]), members in ascending global id.
+// ---------------------------------------------------------------------------------------
+struct Index {
+  int device = 0;
+  int D = 0, Dp = 0, W = 0, K = 0;
+  uint64_t seed = 0;
+  int kmeans_iters = 20;
+  int max_train_per_list = 256;
+  int shard_rank = 0, shard_count = 1;
+  float t4 = 0.0f;
+  bool trained = false;
+
+  std::vector<float> P_host;       // [Dp*Dp] rotation (row-major)
+  std::vector<float> C_host;       // [K*D] centroids, original space
+  std::vector<int64_t> off_host;   // [K+1]
+  int64_t n_total = 0;             // vectors added across all shards (global id space)
+  int64_t n_rows = 0;              // vectors stored on this shard
+
+  float* P = nullptr;          // [Dp*Dp]
+  float* C = nullptr;          // [K*D]
+  float* C_rot = nullptr;      // [K*Dp]
+  float* C_rot_n2 = nullptr;   // [K] |c_rot|^2 (float, for the approximate coarse pass)
+  float* C_n2 = nullptr;       // [K] |c|^2 (original space, for assignment)
+
+  // Row order: append-only storage of this shard's vectors, in the order they were added.
+  int64_t cap_rows = 0;
+  float* X_r = nullptr;          // [n_rows*D] raw vectors (rerank store)
+  uint32_t* codes_r = nullptr;   // [n_rows*W]
+  float* fadd_r = nullptr;       // [n_rows]
+  float* frescale_r = nullptr;   // [n_rows]
+  float* ferr_r = nullptr;       // [n_rows]
+  uint32_t* labels_r = nullptr;  // [n_rows]
+  uint32_t* ids_r = nullptr;     // [n_rows] global ids
+  int64_t cap_ids = 0;
+  uint32_t* id2row = nullptr;    // [n_total] row of a global id, 0xFFFFFFFF if not on this shard
+
+  // Slot order (rebuilt after every add): list l owns slots [list_off[l], list_off[l+1]).
+  int64_t* list_off = nullptr;   // [K+1]
+  uint32_t* ids = nullptr;       // [n_rows] global ids
+  uint32_t* codes = nullptr;     // [n_rows*W] vector-major 1-bit codes
+  float* fadd = nullptr;         // [n_rows]
+  float* frescale = nullptr;     // [n_rows]
+  float* ferr = nullptr;         // [n_rows]
+};
+
+void free_index_memory(Index& ix);
+
+// ---------------------------------------------------------------------------------------
+// Host math (rbq_host_math.cpp): rotation and query scaling constant.
+// ---------------------------------------------------------------------------------------
+void make_rotation(int Dp, uint64_t seed, float* P_out);
+float query_scale(int Dp, uint64_t seed, int ex_bits);
+
+// ---------------------------------------------------------------------------------------
+// Kernel launchers.
+// ---------------------------------------------------------------------------------------
+// Y[n, Dp] = pad(X[n, D]) * P  (double accumulation in k order).
+void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, float* Y, cudaStream_t s);
+// 1-bit codes + factors of rotated rows Y against rotated centroids of their labels.
+void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, const uint32_t* labels,
+                     uint32_t* codes, float* fadd, float* frescale, float* ferr, cudaStream_t s);
+// Row squared norms (float, any order) of A[n, d].
+void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t s);
+// Approximate scores S[q, c] = |c|^2 - 2 <a_q, c> for ranking (fp32).
+void launch_coarse_scores(const float* A, int64_t nq, const float* C, const float* c_n2, int K, int d,
+                          float* S, cudaStream_t s);
+// Per row of S [nq, K]: top-m (score, id) keys ascending -> cand [nq, m].
+void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s);
+// Exact refine: g = sum_j double(a_j - c_j)^2 for the m candidates, then top-p by (g, id).
+void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m,
+                        int p, int32_t* probes, float* g, cudaStream_t s);
+// 4-bit query planes, delta and k1.
+void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* planes, float* delta,
+                       float* k1, cudaStream_t s);
+
+struct ScanArgs {
+  const int64_t* list_off;
+  const uint32_t* ids;
+  const uint32_t* codes;
+  const float* fadd;
+  const float* frescale;
+  const float* ferr;
+  int Dp, W;
+  const float* Qr;
+  const uint32_t* planes;
+  const float* delta;
+  const float* k1;
+  int64_t nq;
+  const int32_t* probes;
+  const float* g;
+  int nprobe;
+  int R;
+  int cap;
+  int prune;
+  int slices;
+  int shard_rank, shard_count;
+  unsigned long long* out_keys;  // [nq, slices, R]
+  unsigned long long* stats;     // optional [2]: scanned, admitted
+};
+constexpr int kScanTile = 256;
+void launch_scan(const ScanArgs& a, cudaStream_t s);
+// Phase-1 dump for one query and one list.
+void launch_list_estimates(const Index& ix, const uint32_t* planes, float delta, float k1, float g, int list,
+                           int32_t* acc, float* est, float* low, cudaStream_t s);
+// Merge [nq, parts, R] keys -> [nq, R] keys (ascending).
+void launch_merge_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,
+                       cudaStream_t s);
+// Keys [nq, R] -> dist f32 [nq, k], ids i64 [nq, k] (first k of each row).
+void launch_keys_to_result(const unsigned long long* keys, int64_t nq, int R, int k, float* dist,
+                           int64_t* ids, cudaStream_t s);
+// Exact rerank: candidate keys [nq, R] -> top-k exact L2^2 in the original space.
+void launch_rerank(const float* Xslots, const uint32_t* id2slot, int D, const float* Q, int64_t nq,
+                   const unsigned long long* cand, int R, int k, float* dist, int64_t* ids, cudaStream_t s);
+
+// k-means helpers.
+void launch_centroid_update(const float* X, int64_t n, int D, const uint32_t* labels, const int64_t* off,
+                            const uint32_t* order, int K, float* C, cudaStream_t s);
+void launch_gather_rows_f32(const float* src, int64_t rows, int cols, const int64_t* src_row, float* dst,
+                            cudaStream_t s);
+// dst[r*cols + j] = src[src_row[r]*cols + j] for 32-bit words.
+void launch_gather_rows_u32(const uint32_t* src, int64_t rows, int cols, const int64_t* src_row, uint32_t* dst,
+                            cudaStream_t s);
+// id2row[ids[r]] = r for r < n.
+void launch_scatter_id2row(const uint32_t* ids, int64_t n, uint32_t* id2row, cudaStream_t s);
+// keys[i] = ids[i] < 0 ? empty : (0 << 32 | ids[i]).
+void launch_ids_to_keys(const int64_t* ids, int64_t n, unsigned long long* keys, cudaStream_t s);
+void launch_keys_to_ids(const unsigned long long* keys, int64_t n, int64_t* ids, float* dist, cudaStream_t s);
+// k-way merge of [parts, nq, k] results.
+void launch_merge_results(const float* dist, const int64_t* ids, int parts, int64_t nq, int k, float* out_dist,
+                          int64_t* out_ids, cudaStream_t s);
+
+// Synthetic data (benchmarks): Gaussian mixture rows, optionally normalised.
+void launch_gen_mixture(float* X, int64_t n, int D, int n_centres, float sigma, int aniso, int normalize,
+                        uint64_t seed, uint32_t stream, float* centres_scratch, cudaStream_t s);
+void launch_gen_queries(const float* X, int64_t n, int D, float* Q, int64_t nq, float sigma, int normalize,
+                        uint64_t seed, uint32_t stream, int64_t* src_rows, cudaStream_t s);
+
+}  // namespace rbq

@@ -1,0 +1,297 @@
+"""ctypes wrapper of the CPU oracle (oracle/rbq_oracle.cpp).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and the
+cpu_baseline / ``--impl reference`` legs of bench.py, always as the checker or the timed CPU
+baseline, never as part of the product path.  Parity with the reference implementation
+itself is unpinned where the reference relies on RAFT/cuSOLVER (rotation generator, t4 rows,
+k-means, select_k tie order); known-answer tests pin the formulas instead.
+
+Every function takes and returns numpy arrays (C-contiguous, exact dtypes).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "librbq_oracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i64, _i32, _u64, _u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+            os.path.join(_HERE, "rbq_oracle.cpp")
+        ):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.orc_gaussian.argtypes = [_u64, _u32, _u64, _i64, _f64p]
+        L.orc_philox.argtypes = [_u32p, _u32p, _u32p]
+        L.orc_make_rotation.argtypes = [_i32, _u64, _f32p]
+        L.orc_query_scale.argtypes = [_i32, _u64, _i32]
+        L.orc_query_scale.restype = ctypes.c_float
+        L.orc_best_rescale.argtypes = [_f64p, _i32, _i32]
+        L.orc_best_rescale.restype = ctypes.c_double
+        L.orc_rotate.argtypes = [_f32p, _i64, _i32, _i32, _f32p, _f32p]
+        L.orc_quantize_one.argtypes = [_f32p, _f32p, _i32, _u32p, _f32p]
+        L.orc_build.argtypes = [_f32p, _i64, _i32, _i32, _f32p, _f32p, _i32, _u32p,
+                                _i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _f32p]
+        L.orc_query_prep.argtypes = [_f32p, _i64, _i32, ctypes.c_float, _u32p, _f32p, _f32p, _i8p]
+        L.orc_coarse.argtypes = [_f32p, _i64, _f32p, _i32, _i32, _i32, _i32p, _f32p]
+        L.orc_popcount_ip.argtypes = [_u32p, _u32p, _i32]
+        L.orc_popcount_ip.restype = ctypes.c_int32
+        L.orc_estimate.argtypes = [_f32p, ctypes.c_float, ctypes.c_int32, ctypes.c_float, ctypes.c_float, _f32p]
+        L.orc_exact_ip.argtypes = [_f32p, _u32p, _i32]
+        L.orc_exact_ip.restype = ctypes.c_float
+        L.orc_scan.argtypes = [_i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _i32, _f32p, _u32p,
+                               _f32p, _f32p, _i64, _i32p, _f32p, _i32, _i32, _i32, _i32, _i32,
+                               _i32, _i32, _i32, _i64p, _f32p, _i64p]
+        L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
+        L.orc_l2_exact.restype = ctypes.c_float
+        L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
+        L.orc_knn_exact.argtypes = [_f32p, _i64, _i32, _f32p, _i64, _i32, _f32p, _i64p]
+        L.orc_assign.argtypes = [_f32p, _i64, _i32, _f32p, _i32, _u32p]
+        L.orc_threads.restype = ctypes.c_int
+        L.orc_set_threads.argtypes = [_i32]
+        _lib = L
+    return _lib
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def pad_dim(d: int) -> int:
+    return (d + 31) // 32 * 32
+
+
+def threads() -> int:
+    return lib().orc_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def gaussian(seed: int, stream: int, start: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float64)
+    lib().orc_gaussian(seed, stream, start, n, out)
+    return out
+
+
+def philox(key, ctr) -> np.ndarray:
+    out = np.empty(4, np.uint32)
+    lib().orc_philox(_c(key, np.uint32), _c(ctr, np.uint32), out)
+    return out
+
+
+def make_rotation(dp: int, seed: int) -> np.ndarray:
+    P = np.empty((dp, dp), np.float32)
+    lib().orc_make_rotation(dp, seed, P)
+    return P
+
+
+def query_scale(dp: int, seed: int, ex_bits: int = 3) -> float:
+    return float(lib().orc_query_scale(dp, seed, ex_bits))
+
+
+def best_rescale(o, ex_bits: int) -> float:
+    o = _c(o, np.float64)
+    return float(lib().orc_best_rescale(o, o.size, ex_bits))
+
+
+def rotate(X, P) -> np.ndarray:
+    X = _c(X, np.float32)
+    n, d = X.shape
+    dp = P.shape[0]
+    Y = np.empty((n, dp), np.float32)
+    lib().orc_rotate(X, n, d, dp, _c(P, np.float32), Y)
+    return Y
+
+
+def quantize_one(y, c):
+    y, c = _c(y, np.float32), _c(c, np.float32)
+    dp = y.size
+    code = np.empty(dp // 32, np.uint32)
+    f3 = np.empty(3, np.float32)
+    lib().orc_quantize_one(y, c, dp, code, f3)
+    return code, f3
+
+
+class OracleIndex:
+    """Index arrays in list-slot order, as the CUDA library lays them out in HBM."""
+
+    def __init__(self, d, dp, k, list_off, ids, codes, fadd, frescale, ferr, c_rot, P, t4, X):
+        self.d, self.dp, self.k = d, dp, k
+        self.list_off, self.ids, self.codes = list_off, ids, codes
+        self.fadd, self.frescale, self.ferr = fadd, frescale, ferr
+        self.c_rot, self.P, self.t4, self.X = c_rot, P, t4, X
+
+
+def build(X, C, labels, P, t4) -> OracleIndex:
+    X = _c(X, np.float32)
+    C = _c(C, np.float32)
+    n, d = X.shape
+    k = C.shape[0]
+    dp = P.shape[0]
+    w = dp // 32
+    list_off = np.empty(k + 1, np.int64)
+    ids = np.empty(n, np.uint32)
+    codes = np.empty((n, w), np.uint32)
+    fadd = np.empty(n, np.float32)
+    fres = np.empty(n, np.float32)
+    ferr = np.empty(n, np.float32)
+    c_rot = np.empty((k, dp), np.float32)
+    lib().orc_build(X, n, d, dp, _c(P, np.float32), C, k, _c(labels, np.uint32), list_off, ids,
+                    codes, fadd, fres, ferr, c_rot)
+    return OracleIndex(d, dp, k, list_off, ids, codes, fadd, fres, ferr, c_rot, P, t4, X)
+
+
+def query_prep(Qr, t4: float):
+    Qr = _c(Qr, np.float32)
+    nq, dp = Qr.shape
+    w = dp // 32
+    planes = np.empty((nq, 4, w), np.uint32)
+    delta = np.empty(nq, np.float32)
+    k1 = np.empty(nq, np.float32)
+    codes = np.empty((nq, dp), np.int8)
+    lib().orc_query_prep(Qr, nq, dp, np.float32(t4), planes, delta, k1, codes)
+    return planes, delta, k1, codes
+
+
+def coarse(Qr, Cr, nprobe: int):
+    Qr, Cr = _c(Qr, np.float32), _c(Cr, np.float32)
+    nq, dp = Qr.shape
+    probes = np.empty((nq, nprobe), np.int32)
+    g = np.empty((nq, nprobe), np.float32)
+    lib().orc_coarse(Qr, nq, Cr, Cr.shape[0], dp, nprobe, probes, g)
+    return probes, g
+
+
+def popcount_ip(planes, code) -> int:
+    code = _c(code, np.uint32)
+    return int(lib().orc_popcount_ip(_c(planes, np.uint32), code, code.size))
+
+
+def estimate(f3, g, acc, delta, k1):
+    out = np.empty(2, np.float32)
+    lib().orc_estimate(_c(f3, np.float32), np.float32(g), int(acc), np.float32(delta), np.float32(k1), out)
+    return out[0], out[1]
+
+
+def exact_ip(q, code) -> float:
+    code = _c(code, np.uint32)
+    return float(lib().orc_exact_ip(_c(q, np.float32), code, code.size))
+
+
+def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=256, cap=1024, prune=1,
+         slices=1, shard_rank=0, shard_count=1, with_stats=False):
+    Qr = _c(Qr, np.float32)
+    nq = Qr.shape[0]
+    nprobe = probes.shape[1]
+    out_ids = np.empty((nq, R), np.int64)
+    out_d = np.empty((nq, R), np.float32)
+    stats = np.zeros(2, np.int64)
+    lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
+                   _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq,
+                   _c(probes, np.int32), _c(g, np.float32), nprobe, R, tile, cap, prune, slices,
+                   shard_rank, shard_count, out_ids, out_d, stats)
+    if with_stats:
+        return out_ids, out_d, stats
+    return out_ids, out_d
+
+
+def l2_exact(x, q) -> float:
+    x, q = _c(x, np.float32), _c(q, np.float32)
+    return float(lib().orc_l2_exact(x, q, x.size))
+
+
+def rerank(X, Q, cand, k):
+    X, Q = _c(X, np.float32), _c(Q, np.float32)
+    cand = _c(cand, np.int64)
+    nq, R = cand.shape
+    out_d = np.empty((nq, k), np.float32)
+    out_i = np.empty((nq, k), np.int64)
+    lib().orc_rerank(X, X.shape[1], Q, nq, cand, R, k, out_d, out_i)
+    return out_d, out_i
+
+
+def knn_exact(X, Q, k):
+    X, Q = _c(X, np.float32), _c(Q, np.float32)
+    nq = Q.shape[0]
+    out_d = np.empty((nq, k), np.float32)
+    out_i = np.empty((nq, k), np.int64)
+    lib().orc_knn_exact(X, X.shape[0], X.shape[1], Q, nq, k, out_d, out_i)
+    return out_d, out_i
+
+
+def assign(X, C) -> np.ndarray:
+    X, C = _c(X, np.float32), _c(C, np.float32)
+    labels = np.empty(X.shape[0], np.uint32)
+    lib().orc_assign(X, X.shape[0], X.shape[1], C, C.shape[0], labels)
+    return labels
+
+
+def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=256, cap=1024, prune=1, slices=1,
+           shard_rank=0, shard_count=1, with_stats=False):
+    """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
+
+    rerank_depth == 0 returns the scan's top-k estimates (the reference behaviour)."""
+    Q = _c(Q, np.float32)
+    Qr = rotate(Q, ix.P)
+    probes, g = coarse(Qr, ix.c_rot, nprobe)
+    planes, delta, k1, _ = query_prep(Qr, ix.t4)
+    R = rerank_depth if rerank_depth > 0 else k
+    res = scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
+               shard_count, with_stats=with_stats)
+    cand, cd = res[0], res[1]
+    if rerank_depth > 0:
+        dist, ids = rerank(ix.X, Q, cand, k)
+    else:
+        dist, ids = cd[:, :k].copy(), cand[:, :k].copy()
+    if with_stats:
+        return dist, ids, res[2]
+    return dist, ids
+
+
+def recall(ids, gt) -> float:
+    """Mean |ids ∩ gt| / k over queries (k = gt.shape[1])."""
+    k = gt.shape[1]
+    hit = 0
+    for a, b in zip(ids, gt):
+        hit += len(set(a[:k].tolist()) & set(b.tolist()))
+    return hit / float(gt.size)
+
+
+def kmeans(X, k, iters=10, seed=0):
+    """Small deterministic Lloyd k-means for CPU-only tests (not the product's trainer)."""
+    X = _c(X, np.float32)
+    n = X.shape[0]
+    pick = (np.arange(k, dtype=np.int64) * n) // k
+    C = X[pick].copy()
+    for _ in range(iters):
+        lab = assign(X, C)
+        sums = np.zeros((k, X.shape[1]), np.float64)
+        np.add.at(sums, lab, X.astype(np.float64))
+        cnt = np.bincount(lab, minlength=k)
+        nz = cnt > 0
+        C[nz] = (sums[nz] / cnt[nz, None]).astype(np.float32)
+    return C, assign(X, C)

@@ -1,0 +1,137 @@
+"""Properties of the oracle's search schedule (CPU): the facts the GPU parity tests rely on."""
+import numpy as np
+import pytest
+
+from conftest import mixture
+
+
+def build_small(oracle, n=6000, d=64, k=32, nq=40, seed=0, dp_seed=11):
+    X, Q = mixture(n, d, 24, 0.3, nq, seed=seed)
+    P = oracle.make_rotation(oracle.pad_dim(d), dp_seed)
+    t4 = oracle.query_scale(oracle.pad_dim(d), dp_seed)
+    C, lab = oracle.kmeans(X, k, iters=4)
+    return oracle.build(X, C, lab, P, t4), X, Q, lab
+
+
+@pytest.fixture(scope="module")
+def small(oracle):
+    return build_small(oracle)
+
+
+def prep(oracle, ix, Q, nprobe):
+    Qr = oracle.rotate(Q, ix.P)
+    probes, g = oracle.coarse(Qr, ix.c_rot, nprobe)
+    planes, delta, k1, _ = oracle.query_prep(Qr, ix.t4)
+    return Qr, probes, g, planes, delta, k1
+
+
+def test_layout_is_stable_counting_sort(oracle, small):
+    ix, X, Q, lab = small
+    assert ix.list_off[0] == 0 and ix.list_off[-1] == X.shape[0]
+    for l in range(ix.k):
+        members = ix.ids[ix.list_off[l]:ix.list_off[l + 1]]
+        assert np.all(lab[members] == l)
+        assert np.all(np.diff(members.astype(np.int64)) > 0)
+
+
+def test_exhaustive_scan_equals_estimator_sort(oracle, small):
+    """nprobe = nlist, prune off: the scan's top-R is the plain sort of every estimate."""
+    ix, X, Q, lab = small
+    Qr, probes, g, planes, delta, k1 = prep(oracle, ix, Q[:5], ix.k)
+    R = 30
+    ids, dist = oracle.scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0)
+    W = ix.dp // 32
+    for q in range(5):
+        gl = {int(l): float(gv) for l, gv in zip(probes[q], g[q])}
+        keys = []
+        for l in range(ix.k):
+            for s in range(ix.list_off[l], ix.list_off[l + 1]):
+                eip = np.float32(oracle.exact_ip(Qr[q], ix.codes[s]))
+                base = np.float32(ix.fadd[s]) + np.float32(gl[l])
+                dd = base + np.float32(ix.frescale[s]) * (eip + np.float32(k1[q]))
+                keys.append((float(np.float32(dd)), int(ix.ids[s])))
+        keys.sort()
+        assert [i for _, i in keys[:R]] == ids[q].tolist()
+        assert np.array_equal(np.array([d for d, _ in keys[:R]], np.float32).view(np.uint32),
+                              dist[q].view(np.uint32))
+
+
+def test_no_prune_result_is_schedule_independent(oracle, small):
+    ix, X, Q, lab = small
+    Qr, probes, g, planes, delta, k1 = prep(oracle, ix, Q, 8)
+    base = oracle.scan(ix, Qr, planes, delta, k1, probes, g, 20, prune=0)
+    for tile, cap, slices in ((256, 512, 1), (256, 2048, 1), (128, 1024, 3), (256, 1024, 8)):
+        other = oracle.scan(ix, Qr, planes, delta, k1, probes, g, 20, tile=tile, cap=cap, prune=0,
+                            slices=slices)
+        assert np.array_equal(base[0], other[0])
+
+
+def test_prune_keeps_recall(oracle, small):
+    ix, X, Q, lab = small
+    _, gt = oracle.knn_exact(X, Q, 10)
+    d0, i0 = oracle.search(ix, Q, 10, 8, 40, prune=0)
+    d1, i1, st = oracle.search(ix, Q, 10, 8, 40, prune=1, with_stats=True)
+    assert st[1] < st[0]  # the prune removes work
+    assert abs(oracle.recall(i0, gt) - oracle.recall(i1, gt)) <= 0.01
+
+
+def test_sharded_union_equals_unsharded_without_prune(oracle, small):
+    ix, X, Q, lab = small
+    Qr, probes, g, planes, delta, k1 = prep(oracle, ix, Q, 8)
+    R = 25
+    full = oracle.scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0)
+    parts = [oracle.scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0, shard_rank=r, shard_count=3)
+             for r in range(3)]
+    for q in range(Q.shape[0]):
+        keys = []
+        for ids, dist in parts:
+            keys += [(float(dist[q, j]), int(ids[q, j])) for j in range(R) if ids[q, j] >= 0]
+        keys.sort()
+        assert [i for _, i in keys[:R]] == full[0][q].tolist()
+
+
+def test_rerank_returns_exact_order(oracle, small):
+    ix, X, Q, lab = small
+    cand = np.tile(np.arange(50, dtype=np.int64), (3, 1))
+    cand[1, 10:] = -1
+    d, i = oracle.rerank(X, Q[:3], cand, 10)
+    for q in range(3):
+        pool = [c for c in cand[q] if c >= 0]
+        ref = sorted((oracle.l2_exact(X[c], Q[q]), c) for c in pool)[:10]
+        assert i[q].tolist() == [c for _, c in ref]
+
+
+def test_padding_when_fewer_candidates_than_k(oracle):
+    ix, X, Q, lab = build_small(oracle, n=300, d=32, k=8, nq=3)
+    d, i = oracle.search(ix, Q, 5, 1, 0, prune=1)
+    assert np.all((i >= 0).sum(axis=1) >= 1)
+    # one list only and huge k: the tail is padded
+    d, i = oracle.search(ix, Q, 400, 1, 0, prune=0)
+    assert (i == -1).any() and np.all(np.isinf(d[i == -1]))
+
+
+def test_empty_lists_and_single_vector(oracle):
+    X, Q = mixture(1, 32, 1, 0.3, 2, seed=4)
+    P = oracle.make_rotation(32, 1)
+    t4 = oracle.query_scale(32, 1)
+    C = np.concatenate([X, X + 1.0, X - 1.0]).astype(np.float32)  # lists 1, 2 stay empty
+    lab = np.zeros(1, np.uint32)
+    ix = oracle.build(X, C, lab, P, t4)
+    assert ix.list_off.tolist() == [0, 1, 1, 1]
+    d, i = oracle.search(ix, Q, 3, 3, 0, prune=1)
+    assert i[:, 0].tolist() == [0, 0] and np.all(i[:, 1:] == -1)
+
+
+def test_reference_gtest_recall_floor(oracle):
+    """cuVS gtest shape: 4096 x 64 U(0.1, 2), 1024 queries, k = 10, n_lists = clamp(N/128, 32,
+    1024) = 32; 1-bit recall floor 0.3 (ann_ivf_rabitq.cuh:82-100, 218-230)."""
+    rng = np.random.default_rng(1234)
+    X = rng.uniform(0.1, 2.0, (4096, 64)).astype(np.float32)
+    Q = rng.uniform(0.1, 2.0, (256, 64)).astype(np.float32)
+    P = oracle.make_rotation(64, 7)
+    t4 = oracle.query_scale(64, 7)
+    C, lab = oracle.kmeans(X, 32, iters=6)
+    ix = oracle.build(X, C, lab, P, t4)
+    _, gt = oracle.knn_exact(X, Q, 10)
+    _, ids = oracle.search(ix, Q, 10, 16, 0, prune=1)
+    assert oracle.recall(ids, gt) >= 0.3
