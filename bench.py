@@ -1,0 +1,518 @@
+#!/usr/bin/env python
+"""Benchmark: queries/sec of IVF-RaBitQ search on BASELINE config 2 (1M x 256, nlist 1024,
+nprobe 32, k 10, exact rerank, query batch 10,000), 1..8 B200 with lists sharded per GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one search of one query batch.  `value` times the batch with queries resident
+in HBM (CUDA events, L2 flushed before every step); `e2e` times the C-ABI call with host
+buffers (rbq_search_host: H2D of the queries, search, D2H of distances and ids).  Under
+torchrun (N > 1) every rank holds the lists l % N == rank and the per-rank results are merged
+after one NCCL all-gather; times are the max over ranks.  `--impl reference` times the CPU
+restatement of the reference search (oracle/, all host cores) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+# BASELINE config 2 (the metric's configuration).
+CFG = dict(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, nlist=1024, nprobe=32, k=10,
+           rerank=100, seed=2024)
+RERANK_LADDER = (100, 150, 200, 300, 400, 600, 800)
+RECALL_TARGET = 0.95
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_data(cfg):
+    """Seeded Gaussian mixture (centres N(0,1), sigma per dim), L2-normalised, and queries =
+    random database rows + N(0, qsigma) noise, renormalised."""
+    rng = np.random.default_rng(cfg["seed"])
+    n, d = cfg["n"], cfg["d"]
+    cent = rng.standard_normal((cfg["centres"], d), dtype=np.float32)
+    X = np.empty((n, d), np.float32)
+    step = 1 << 17
+    for a in range(0, n, step):
+        b = min(n, a + step)
+        X[a:b] = cent[rng.integers(0, cfg["centres"], b - a)]
+        X[a:b] += np.float32(cfg["sigma"]) * rng.standard_normal((b - a, d), dtype=np.float32)
+        X[a:b] /= np.linalg.norm(X[a:b], axis=1, keepdims=True)
+    src = rng.integers(0, n, cfg["nq"])
+    Q = X[src] + np.float32(cfg["qsigma"]) * rng.standard_normal((cfg["nq"], d), dtype=np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    return X, np.ascontiguousarray(Q, np.float32)
+
+
+def measured_peak():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+           0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+           0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 3:
+                try:
+                    self.samples.append((float(parts[0]), float(parts[1]), int(parts[2], 16)))
+                except ValueError:
+                    pass
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(s[0] for s in self.samples)
+        mask = 0
+        for s in self.samples:
+            mask |= s[2]
+        names = [v for k, v in REASONS.items() if mask & k and k != 0x1]
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(s[1] for s in self.samples), "reasons": names,
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------------------
+# reference arm: the CPU restatement of the reference search, all host cores
+# --------------------------------------------------------------------------------------
+def kmeans_numpy(X, k, iters, per_list, seed):
+    """Training for the CPU arm (not timed): strided sample, BLAS assignment, Lloyd updates."""
+    n = X.shape[0]
+    m = min(n, per_list * k)
+    S = X[(np.arange(m, dtype=np.int64) * n) // m]
+    C = S[(np.arange(k, dtype=np.int64) * m) // k].copy()
+
+    def assign(A):
+        out = np.empty(A.shape[0], np.int64)
+        for a in range(0, A.shape[0], 65536):
+            blk = A[a:a + 65536]
+            out[a:a + 65536] = np.argmin((C * C).sum(1)[None, :] - 2.0 * blk @ C.T, axis=1)
+        return out
+
+    for _ in range(iters):
+        lab = assign(S)
+        sums = np.zeros((k, X.shape[1]), np.float64)
+        np.add.at(sums, lab, S)
+        cnt = np.bincount(lab, minlength=k)
+        nz = cnt > 0
+        C[nz] = (sums[nz] / cnt[nz, None]).astype(np.float32)
+    return C
+
+
+def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
+    """Time the oracle search on a bounded query sample sized to ~budget_s of CPU work."""
+    probe = min(len(Q), 200)
+    t0 = time.perf_counter()
+    O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R)
+    per_q = (time.perf_counter() - t0) / probe
+    n = int(min(len(Q), max(probe, budget_s / max(per_q, 1e-9))))
+    t0 = time.perf_counter()
+    d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R)
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt, i
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    X, Q = make_data(cfg)
+    dp = O.pad_dim(cfg["d"])
+    P = O.make_rotation(dp, 7)
+    t4 = O.query_scale(dp, 7)
+    t = time.perf_counter()
+    C = kmeans_numpy(X, cfg["nlist"], 20, 256, cfg["seed"])
+    cn = (C * C).sum(1)[None, :]
+    lab = np.concatenate([np.argmin(cn - 2.0 * X[a:a + 65536] @ C.T, axis=1)
+                          for a in range(0, cfg["n"], 65536)]).astype(np.uint32)
+    oix = O.build(X, C, lab, P, t4)
+    log(f"[reference] build {time.perf_counter() - t:.1f}s, threads={O.threads()}")
+    R = args.rerank or cfg["rerank"]
+    steps = []
+    n_sample = None
+    for s in range(args.warmup + args.steps):
+        qps, n, dt, _ = cpu_search_timed(O, oix, Q, cfg, R, budget_s=max(2.0, 60.0 / (args.steps + args.warmup)))
+        if s >= args.warmup:
+            steps.append(qps)
+            n_sample = n
+    value = float(np.mean(steps))
+    line = {"impl": "reference", "metric": metric_name(), "value": round(value, 2), "unit": "queries/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
+            "config": workload(cfg, R),
+            "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
+                             "sample": f"{n_sample} of {cfg['nq']} queries per step, same index and parameters"},
+            "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name():
+    return "queries/sec @ recall@10>=0.95, 1M x 256 IVF-RaBitQ (nlist 1024, nprobe 32, k 10)"
+
+
+def workload(cfg, R):
+    return {"workload": "BASELINE config 2: 1M x 256 f32, 4096-centre mixture sigma 0.25, L2-normalised; "
+                        "10k perturbed-row queries; IVF-RaBitQ 1-bit codes, 4-bit queries",
+            "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
+            "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)"}
+
+
+# --------------------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------------------
+def run_ours(args, cfg):
+    import ctypes
+
+    import torch
+    import torch.distributed as tdist
+
+    from neurosamble_b200 import IndexIVFRaBitQ, _lib
+    from neurosamble_b200.index import _ptr, _stream_ptr
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    t = time.perf_counter()
+    X, Q = make_data(cfg)
+    log(f"[rank {rank}] data {time.perf_counter() - t:.1f}s")
+    Xd = torch.from_numpy(X).to(dev)
+    t = time.perf_counter()
+    if world > 1:
+        from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ, gather_results, merge_results
+        index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local)
+        local_ix = index.local
+    else:
+        index = IndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local)
+        local_ix = index
+    index.train(Xd)
+    index.add(Xd)
+    torch.cuda.synchronize()
+    log(f"[rank {rank}] build {time.perf_counter() - t:.1f}s, local vectors {local_ix.info().n_local}")
+    del Xd
+    Qd = torch.from_numpy(Q).to(dev)
+    index.nprobe = cfg["nprobe"]
+    index.prune = True
+
+    # ---- recall at the config's rerank depth; raise R along the ladder until recall >= target
+    gt = None
+    if rank == 0:
+        Xd = torch.from_numpy(X).to(dev)
+        xn = (Xd * Xd).sum(1)
+        gts = []
+        for a in range(0, cfg["nq"], 1000):
+            s = xn[None, :] - 2.0 * (Qd[a:a + 1000] @ Xd.T)
+            gts.append(torch.topk(s, cfg["k"], dim=1, largest=False).indices.cpu())
+        gt = torch.cat(gts).numpy()
+        del Xd, xn, s
+        torch.cuda.empty_cache()
+
+    def recall_of(ids):
+        hit = sum(len(set(a.tolist()) & set(b.tolist())) for a, b in zip(ids, gt))
+        return hit / gt.size
+
+    R = args.rerank or cfg["rerank"]
+    recalls = {}
+    ladder = [R] if args.rerank else list(RERANK_LADDER)
+    for cand in ladder:
+        index.k_rerank = cand
+        d, i = index.search(Qd, cfg["k"])
+        ok = torch.zeros(1, dtype=torch.int32, device=dev)
+        if rank == 0:
+            recalls[cand] = recall_of(i.cpu().numpy())
+            ok[0] = int(recalls[cand] >= RECALL_TARGET)
+        if world > 1:
+            tdist.broadcast(ok, src=0)
+        R = cand
+        if ok.item():
+            break
+    index.k_rerank = R
+    log(f"[rank {rank}] recall@{cfg['k']} by rerank depth: {recalls}; using R={R}")
+
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    k = cfg["k"]
+    nq = cfg["nq"]
+
+    def barrier():
+        if world > 1:
+            tdist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def step_device():
+        d, i = index.search(Qd, k)
+        return d, i
+
+    # ---- value: device-resident queries
+    for _ in range(args.warmup):
+        flush.zero_()
+        step_device()
+    barrier()
+    times = []
+    launches0 = _lib.lib().rbq_kernel_launches()
+    torch.cuda.nvtx.range_push("timed")
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step_device()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+    torch.cuda.nvtx.range_pop()
+    barrier()
+    launches = _lib.lib().rbq_kernel_launches() - launches0
+    ms = float(np.mean(times))
+    if world > 1:
+        t_max = torch.tensor([ms], device=dev)
+        tdist.all_reduce(t_max, op=tdist.ReduceOp.MAX)
+        ms = float(t_max.item())
+    value = nq / (ms / 1000.0)
+
+    # ---- e2e: host buffers through the C ABI (queries H2D, results D2H inside the timed call)
+    Qh = torch.from_numpy(Q).pin_memory()
+    dh = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    ih = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    sp = local_ix.search_params(k)
+    e2e_times = []
+
+    def step_host():
+        if world == 1:
+            _lib.call("rbq_search_host", local_ix.handle, ctypes.byref(sp), ctypes.c_void_p(Qh.data_ptr()), nq,
+                      ctypes.c_void_p(dh.data_ptr()), ctypes.c_void_p(ih.data_ptr()), _stream_ptr(local))
+        else:
+            qd = Qh.to(dev, non_blocking=True)
+            d, i = index.search(qd, k)
+            dh.copy_(d, non_blocking=True)
+            ih.copy_(i, non_blocking=True)
+            torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        step_host()
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            tdist.barrier()
+        t0 = time.perf_counter()
+        step_host()
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_s = float(np.mean(e2e_times))
+    if world > 1:
+        t_max = torch.tensor([e2e_s], device=dev)
+        tdist.all_reduce(t_max, op=tdist.ReduceOp.MAX)
+        e2e_s = float(t_max.item())
+    e2e = nq / e2e_s
+
+    # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
+    roof, roof_rr, scan_share = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(local_ix, X, Q, cfg, R)
+
+    if world > 1:
+        tdist.barrier()
+    if rank == 0:
+        line = {"metric": metric_name(), "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes x 4-bit planes (popc) + f32",
+                "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
+                "config": dict(workload(cfg, R), parallelism=f"lists sharded l % {world}" if world > 1 else "1 GPU",
+                               recall_at_10=recalls.get(R), recall_by_rerank=recalls),
+                "clocks": clk.summary(),
+                "e2e": {"value": round(e2e, 2), "unit": "queries/s", "h2d_bytes_per_step": nq * cfg["d"] * 4,
+                        "d2h_bytes_per_step": nq * k * 12},
+                "gpu_launches": int(launches),
+                "roofline": roof, "roofline_rerank": roof_rr, "scan_share_of_step": scan_share,
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        tdist.destroy_process_group()
+    return 0
+
+
+def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
+    """Time rbq_scan and rbq_rerank alone on the batch; algorithmic bytes from the actual
+    probed list sizes: sum n_l (D/8 + 12) for the scan, R (4D + 8) per query for the rerank."""
+    import ctypes
+
+    import torch
+
+    from neurosamble_b200 import _lib
+    from neurosamble_b200.index import _ptr, _stream_ptr
+
+    nq, d, P = Qd.shape[0], cfg["d"], cfg["nprobe"]
+    info = ix.info()
+    dp = info.padded_dim
+    h, st = ix.handle, _stream_ptr(dev.index)
+    qr = torch.empty((nq, dp), dtype=torch.float32, device=dev)
+    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
+    delta = torch.empty(nq, dtype=torch.float32, device=dev)
+    k1 = torch.empty(nq, dtype=torch.float32, device=dev)
+    probes = torch.empty((nq, P), dtype=torch.int32, device=dev)
+    g = torch.empty((nq, P), dtype=torch.float32, device=dev)
+    _lib.call("rbq_rotate", h, _ptr(Qd), nq, _ptr(qr), st)
+    _lib.call("rbq_coarse", h, _ptr(qr), nq, P, 0, _ptr(probes), _ptr(g), st)
+    _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), st)
+    torch.cuda.synchronize(dev)
+    off = ix.export_lists()["list_off"]
+    sizes = np.diff(off)
+    pr = probes.cpu().numpy()
+    owned = (pr % info.shard_count) == info.shard_rank
+    vec = int(sizes[pr][owned].sum())
+    scan_bytes = vec * (d // 8 + 12)
+    ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
+    dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ts = []
+    for it in range(3 + steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g), P, R, 1,
+                  1, 0, _ptr(ids), _ptr(dist), None, st)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 3:
+            ts.append(e0.elapsed_time(e1))
+    scan_ms = float(np.mean(ts))
+    od = torch.empty((nq, cfg["k"]), dtype=torch.float32, device=dev)
+    oi = torch.empty((nq, cfg["k"]), dtype=torch.int64, device=dev)
+    tr = []
+    for it in range(3 + steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _lib.call("rbq_rerank", h, _ptr(Qd), nq, _ptr(ids), R, cfg["k"], _ptr(od), _ptr(oi), st)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 3:
+            tr.append(e0.elapsed_time(e1))
+    rr_ms = float(np.mean(tr))
+    n_valid = int((ids >= 0).sum().item())
+    rr_bytes = n_valid * (4 * d + 8)
+    peak, kind = measured_peak()
+    traffic = None
+    tf = os.path.join(HERE, "profiles", "scan_traffic.json")
+    if os.path.exists(tf):
+        try:
+            with open(tf) as f:
+                traffic = json.load(f).get("bytes_per_launch_scaled_to_bench")
+        except Exception:
+            traffic = None
+    ach = scan_bytes / (scan_ms / 1000.0) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+            "traffic": traffic, "peak_kind": kind, "kernel": "rbq scan_kernel (+ key->id epilogue)",
+            "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
+            "launch_ms": round(scan_ms, 4)}
+    ach_r = rr_bytes / (rr_ms / 1000.0) / 1e9
+    roof_rr = {"bound": "hbm", "achieved": round(ach_r, 1), "peak": peak, "unit": "GB/s",
+               "frac": round(ach_r / peak, 4), "kernel": "rbq rerank_kernel (+ id->key prologue)",
+               "algorithmic_bytes_per_launch": rr_bytes, "launch_ms": round(rr_ms, 4)}
+    return roof, roof_rr, None
+
+
+def cpu_baseline(ix, X, Q, cfg, R):
+    """The oracle (the CPU restatement of the reference search), all host cores, on a bounded
+    sample of the same batch against the same index."""
+    from oracle import oracle as O
+    ex = ix.export_lists()
+    C, Cr = ix.centroids()
+    info = ix.info()
+    n = X.shape[0]
+    # the oracle's index arrays are the GPU index's own (same layout, same bytes)
+    oix = O.OracleIndex(cfg["d"], info.padded_dim, cfg["nlist"], ex["list_off"], ex["ids"], ex["codes"], ex["fadd"],
+                        ex["frescale"], ex["ferr"], Cr, ix.rotation(), ix.query_scale, X)
+    qps, n_s, dt, _ = cpu_search_timed(O, oix, Q, cfg, R, budget_s=15.0)
+    return {"value": round(qps, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
+            "sample": f"{n_s} of {cfg['nq']} queries ({dt:.1f}s), same index bytes and parameters"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rerank", type=int, default=0, help="fixed rerank depth (0 = smallest meeting recall 0.95)")
+    ap.add_argument("--n", type=int, default=0, help="database size override (smoke runs)")
+    ap.add_argument("--nq", type=int, default=0, help="query batch override")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = dict(CFG)
+    if args.n:
+        cfg["n"] = args.n
+    if args.nq:
+        cfg["nq"] = args.nq
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

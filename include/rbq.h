@@ -72,6 +72,9 @@ typedef struct {
 /* ---- errors / defaults ------------------------------------------------------------------ */
 const char* rbq_last_error(void);
 int rbq_version(void);
+/* Kernels this library has launched in this process (all devices).  No reference
+ * counterpart: lets a benchmark count the library's launches inside a timed region. */
+uint64_t rbq_kernel_launches(void);
 void rbq_index_params_default(rbq_index_params_t* p);
 void rbq_search_params_default(rbq_search_params_t* p);
 

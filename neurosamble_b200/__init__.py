@@ -1,0 +1,4 @@
+"""B200-native IVF-RaBitQ retrieval for Neurosamble (CUDA C-ABI library + FAISS-style API)."""
+from .index import IndexIVFRaBitQ, read_index, write_index
+
+__all__ = ["IndexIVFRaBitQ", "read_index", "write_index"]

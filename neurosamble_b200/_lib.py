@@ -41,6 +41,7 @@ _I32, _I64, _F32, _U64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.
 SIGNATURES = {
     "rbq_last_error": [],
     "rbq_version": [],
+    "rbq_kernel_launches": [],
     "rbq_index_params_default": [ctypes.POINTER(IndexParams)],
     "rbq_search_params_default": [ctypes.POINTER(SearchParams)],
     "rbq_make_rotation": [_I32, _U64, _P],
@@ -69,7 +70,7 @@ SIGNATURES = {
     "rbq_gen_queries": [_P, _I64, _I32, _P, _I64, _F32, _I32, _U64, _P, _P],
 }
 _RESTYPES = {"rbq_last_error": ctypes.c_char_p, "rbq_index_params_default": None,
-             "rbq_search_params_default": None}
+             "rbq_search_params_default": None, "rbq_kernel_launches": ctypes.c_uint64}
 
 _lib = None
 

@@ -86,7 +86,7 @@ void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, flo
 #undef RBQ_ROT_CASE
     default: throw Error{RBQ_ERR_INVALID, "rotation: padded dim must be <= 2048 with Dp/256 in {1,2,3,4,6,8}"};
   }
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -151,7 +151,7 @@ void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, cons
   if (n <= 0) return;
   quantize_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, s>>>(Y, n, Dp, C_rot, labels, codes, fadd, frescale,
                                                              ferr);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // Row squared norms (float accumulation; only used to rank candidates approximately).
@@ -173,7 +173,7 @@ void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t
 {
   if (n <= 0) return;
   row_norms_kernel<<<(unsigned)ceil_div(n, 8), 256, 0, s>>>(A, n, d, out);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -197,7 +197,7 @@ void launch_centroid_update(const float* X, int64_t /*n*/, int D, const uint32_t
                             const uint32_t* order, int K, float* C, cudaStream_t s)
 {
   centroid_update_kernel<<<K, 128, 0, s>>>(X, D, off, order, C);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void gather_rows_kernel(const float* __restrict__ src, int64_t rows, int cols,
@@ -214,7 +214,7 @@ void launch_gather_rows_f32(const float* src, int64_t rows, int cols, const int6
 {
   if (rows <= 0) return;
   gather_rows_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(src, rows, cols, src_row, dst);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -297,10 +297,10 @@ void launch_gen_mixture(float* X, int64_t n, int D, int n_centres, float sigma, 
 {
   const int64_t cn = (int64_t)n_centres * D;
   gen_centres_kernel<<<(unsigned)ceil_div(cn, 256), 256, 0, s>>>(centres, n_centres, D, aniso, seed, stream);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
   gen_rows_kernel<<<(unsigned)ceil_div(n, 8), 256, 0, s>>>(X, n, D, centres, n_centres, sigma, aniso, normalize,
                                                           seed, stream + 1u);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void gen_queries_kernel(const float* __restrict__ X, int64_t n, int D, float* __restrict__ Q, int64_t nq,
@@ -330,7 +330,7 @@ void launch_gen_queries(const float* X, int64_t n, int D, float* Q, int64_t nq, 
   if (nq <= 0) return;
   gen_queries_kernel<<<(unsigned)ceil_div(nq, 8), 256, 0, s>>>(X, n, D, Q, nq, sigma, normalize, seed, stream,
                                                               src_rows);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void gather_rows_u32_kernel(const uint32_t* __restrict__ src, int64_t rows, int cols,
@@ -348,7 +348,7 @@ void launch_gather_rows_u32(const uint32_t* src, int64_t rows, int cols, const i
 {
   if (rows <= 0) return;
   gather_rows_u32_kernel<<<(unsigned)ceil_div(rows * cols, 256), 256, 0, s>>>(src, rows, cols, src_row, dst);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void scatter_id2row_kernel(const uint32_t* __restrict__ ids, int64_t n, uint32_t* __restrict__ id2row)
@@ -361,7 +361,7 @@ void launch_scatter_id2row(const uint32_t* ids, int64_t n, uint32_t* id2row, cud
 {
   if (n <= 0) return;
   scatter_id2row_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(ids, n, id2row);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 }  // namespace rbq

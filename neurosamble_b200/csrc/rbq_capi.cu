@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -478,6 +479,9 @@ void write_dev(File& f, const T* p, size_t count)
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 void free_index_memory(Index& ix)
 {
   dev_free(ix.P);
@@ -510,6 +514,8 @@ extern "C" {
 const char* rbq_last_error(void) { return g_last_error.c_str(); }
 
 int rbq_version(void) { return 1; }
+
+uint64_t rbq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 void rbq_index_params_default(rbq_index_params_t* p)
 {

@@ -32,6 +32,15 @@ struct Error {
     if (!(cond)) throw ::rbq::Error{(code), (msg)};       \
   } while (0)
 
+// Process-wide count of kernels launched by this library (rbq_kernel_launches()).
+void count_launch();
+// Follows every kernel launch: counts it and surfaces launch-configuration errors.
+#define RBQ_LAUNCHED()                  \
+  do {                                  \
+    ::rbq::count_launch();              \
+    RBQ_CUDA(cudaGetLastError());       \
+  } while (0)
+
 // ---------------------------------------------------------------------------------------
 // Keys: (order-preserving float bits << 32) | id.  Ascending keys = ascending distance,
 // ties broken by the smaller id.  All-ones = empty slot.

@@ -97,7 +97,7 @@ void launch_coarse_scores(const float* A, int64_t nq, const float* C, const floa
   RBQ_CHECK(ceil_div(nq, 64) <= 65535, RBQ_ERR_INVALID, "coarse: query chunk too large");
   dim3 grid((unsigned)ceil_div(K, 64), (unsigned)ceil_div(nq, 64));
   coarse_scores_kernel<<<grid, 256, 0, s>>>(A, nq, C, cn2, K, d, S);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -131,7 +131,7 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
   if (nq <= 0) return;
   RBQ_CHECK(m >= 1 && m <= kTopmBuf / 2, RBQ_ERR_INVALID, "coarse: shortlist size out of range");
   topm_rows_kernel<<<(unsigned)nq, 256, 0, s>>>(S, K, m, cand);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -189,7 +189,7 @@ void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(refine_topp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   refine_topp_kernel<<<(unsigned)nq, 256, smem, s>>>(A, C, d, cand, m, p, mp2, probes, g);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -256,7 +256,7 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* 
 {
   if (nq <= 0) return;
   query_prep_kernel<<<(unsigned)ceil_div(nq, 128), 128, 0, s>>>(Qr, nq, Dp, t4, planes, delta, k1);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -436,7 +436,7 @@ static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
   const int64_t blocks = a.nq * a.slices;
   RBQ_CHECK(blocks <= 0x7fffffff, RBQ_ERR_INVALID, "scan: grid too large");
   scan_kernel<W><<<(unsigned)blocks, kScanTile, smem, s>>>(a);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 void launch_scan(const ScanArgs& a, cudaStream_t s)
@@ -484,7 +484,7 @@ void launch_merge_keys(const unsigned long long* in, int64_t nq, int parts, int 
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   merge_keys_kernel<<<(unsigned)nq, 256, smem, s>>>(in, parts, R, n2, out);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void keys_to_result_kernel(const unsigned long long* __restrict__ keys, int64_t nq, int R, int k,
@@ -509,7 +509,7 @@ void launch_keys_to_result(const unsigned long long* keys, int64_t nq, int R, in
 {
   if (nq <= 0) return;
   keys_to_result_kernel<<<(unsigned)ceil_div(nq * k, 256), 256, 0, s>>>(keys, nq, R, k, dist, ids);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -572,7 +572,7 @@ void launch_rerank(const float* Xrows, const uint32_t* id2row, int D, const floa
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   rerank_kernel<<<(unsigned)nq, 256, smem, s>>>(Xrows, id2row, D, Q, cand, R, k, r2, dist, ids);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void ids_to_keys_kernel(const int64_t* __restrict__ ids, int64_t n, unsigned long long* __restrict__ keys)
@@ -585,7 +585,7 @@ void launch_ids_to_keys(const int64_t* ids, int64_t n, unsigned long long* keys,
 {
   if (n <= 0) return;
   ids_to_keys_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(ids, n, keys);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int64_t n, int64_t* __restrict__ ids,
@@ -607,7 +607,7 @@ void launch_keys_to_ids(const unsigned long long* keys, int64_t n, int64_t* ids,
 {
   if (n <= 0) return;
   keys_to_ids_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(keys, n, ids, dist);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // k-way merge of per-shard results [parts, nq, k] by (distance, id): the on-device merge that
@@ -647,7 +647,7 @@ void launch_merge_results(const float* dist, const int64_t* ids, int parts, int6
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(merge_results_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   merge_results_kernel<<<(unsigned)nq, 256, smem, s>>>(dist, ids, parts, nq, k, n2, out_dist, out_ids);
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 // Phase-1 dump (inspection / parity): same arithmetic as the scan's phase 1.
@@ -705,7 +705,7 @@ void launch_list_estimates(const Index& ix, const uint32_t* planes, float delta,
     default: throw Error{RBQ_ERR_INVALID, "estimates: unsupported padded dimension"};
   }
 #undef RBQ_LE_CASE
-  RBQ_CUDA(cudaGetLastError());
+  RBQ_LAUNCHED();
 }
 
 }  // namespace rbq

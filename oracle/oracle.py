@@ -29,7 +29,7 @@ _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
 _i64, _i32, _u64, _u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32
 
 
-def build() -> str:
+def compile_lib() -> str:
     """Compile the oracle with its Makefile (idempotent)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
@@ -41,7 +41,7 @@ def lib():
         if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
             os.path.join(_HERE, "rbq_oracle.cpp")
         ):
-            build()
+            compile_lib()
         L = ctypes.CDLL(_LIB_PATH)
         L.orc_gaussian.argtypes = [_u64, _u32, _u64, _i64, _f64p]
         L.orc_philox.argtypes = [_u32p, _u32p, _u32p]

@@ -1,0 +1,346 @@
+"""GPU parity: every stage of librbq.so (called through the C ABI) against the CPU oracle on
+the same seeded inputs.  Integer and index outputs must be bit-exact; float outputs are
+compared bit for bit as well, because both sides evaluate the same operation order (the
+tolerance the path allows, 1e-4 relative on distances, is asserted in addition)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import mixture
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-4  # distance tolerance of the north star
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def dev(a):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream():
+    torch = _torch()
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def u32(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+def call(name, *args):
+    from neurosamble_b200 import _lib
+    _lib.call(name, *args)
+    _torch().cuda.synchronize()
+
+
+def make_index(oracle, X, C, lab, seed=7):
+    from neurosamble_b200 import IndexIVFRaBitQ
+    idx = IndexIVFRaBitQ(X.shape[1], C.shape[0], seed=seed)
+    idx.set_centroids(C)
+    idx.add(X, labels=lab)
+    oix = oracle.build(X, C, lab, idx.rotation(), idx.query_scale)
+    return idx, oix
+
+
+@pytest.fixture(scope="module")
+def case(oracle):
+    X, Q = mixture(20000, 128, 48, 0.3, 300, seed=1)
+    C, _ = oracle.kmeans(X[::4], 64, iters=4)
+    lab = oracle.assign(X, C)
+    idx, oix = make_index(oracle, X, C, lab)
+    return idx, oix, X, Q, C, lab
+
+
+def test_constants_match_oracle(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    assert np.array_equal(u32(idx.rotation()), u32(oracle.make_rotation(128, 7)))
+    assert np.float32(idx.query_scale).view(np.uint32) == np.float32(oracle.query_scale(128, 7)).view(np.uint32)
+    Cg, Crg = idx.centroids()
+    assert np.array_equal(u32(Crg), u32(oix.c_rot))
+
+
+def test_rotation_outputs_bit_exact(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    torch = _torch()
+    for rows in (Q, X[:1000], X[:1]):
+        x = dev(rows)
+        y = torch.empty((rows.shape[0], 128), dtype=torch.float32, device="cuda")
+        call("rbq_rotate", idx.handle, ptr(x), rows.shape[0], ptr(y), stream())
+        assert np.array_equal(u32(y.cpu().numpy()), u32(oracle.rotate(rows, oix.P)))
+
+
+def test_build_layout_codes_factors_bit_exact(case):
+    idx, oix, X, Q, C, lab = case
+    ex = idx.export_lists()
+    assert np.array_equal(ex["list_off"], oix.list_off)
+    assert np.array_equal(ex["ids"], oix.ids)
+    assert np.array_equal(ex["codes"], oix.codes)
+    for k in ("fadd", "frescale", "ferr"):
+        assert np.array_equal(u32(ex[k]), u32(getattr(oix, k))), k
+
+
+def test_gpu_assignment_matches_oracle(oracle, case):
+    from neurosamble_b200 import IndexIVFRaBitQ
+    idx, oix, X, Q, C, lab = case
+    idx2 = IndexIVFRaBitQ(128, 64, seed=7)
+    idx2.set_centroids(C)
+    idx2.add(X)  # labels assigned on the GPU
+    ex = idx2.export_lists()
+    assert np.array_equal(ex["list_off"], oix.list_off)
+    assert np.array_equal(ex["ids"], oix.ids)
+
+
+def _query_stage(idx, Qr_np):
+    torch = _torch()
+    nq, dp = Qr_np.shape
+    qr = dev(Qr_np)
+    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device="cuda")
+    delta = torch.empty(nq, dtype=torch.float32, device="cuda")
+    k1 = torch.empty(nq, dtype=torch.float32, device="cuda")
+    call("rbq_query_prep", idx.handle, ptr(qr), nq, ptr(planes), ptr(delta), ptr(k1), stream())
+    return qr, planes, delta, k1
+
+
+def test_query_quantisation_bit_exact(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    Qr = oracle.rotate(Q, oix.P)
+    _, planes, delta, k1 = _query_stage(idx, Qr)
+    p2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
+    assert np.array_equal(u32(planes.cpu().numpy()), p2)
+    assert np.array_equal(u32(delta.cpu().numpy()), u32(d2))
+    assert np.array_equal(u32(k1.cpu().numpy()), u32(k2))
+
+
+@pytest.mark.parametrize("nprobe", [1, 8, 64])
+def test_coarse_probes_bit_exact(oracle, case, nprobe):
+    idx, oix, X, Q, C, lab = case
+    torch = _torch()
+    Qr = oracle.rotate(Q, oix.P)
+    qr = dev(Qr)
+    probes = torch.empty((Q.shape[0], nprobe), dtype=torch.int32, device="cuda")
+    g = torch.empty((Q.shape[0], nprobe), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), Q.shape[0], nprobe, 0, ptr(probes), ptr(g), stream())
+    p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
+    assert np.array_equal(probes.cpu().numpy(), p2)
+    assert np.array_equal(u32(g.cpu().numpy()), u32(g2))
+
+
+def test_popcount_inner_products_and_estimates_bit_exact(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    torch = _torch()
+    Qr = oracle.rotate(Q[:4], oix.P)
+    _, planes, delta, k1 = _query_stage(idx, Qr)
+    pl_np = u32(planes.cpu().numpy())
+    dl, kk = delta.cpu().numpy(), k1.cpu().numpy()
+    for q in range(4):
+        for l in (0, 5, 63):
+            n = int(oix.list_off[l + 1] - oix.list_off[l])
+            if n == 0:
+                continue
+            acc = torch.empty(n, dtype=torch.int32, device="cuda")
+            est = torch.empty(n, dtype=torch.float32, device="cuda")
+            low = torch.empty(n, dtype=torch.float32, device="cuda")
+            g = np.float32(0.37 + 0.01 * l)
+            call("rbq_list_estimates", idx.handle, ptr(planes[q]), float(dl[q]), float(kk[q]), float(g), l, ptr(acc),
+                 ptr(est), ptr(low), stream())
+            acc_np, est_np, low_np = acc.cpu().numpy(), est.cpu().numpy(), low.cpu().numpy()
+            for v in range(n):
+                s = int(oix.list_off[l]) + v
+                a = oracle.popcount_ip(pl_np[q], oix.codes[s])
+                assert acc_np[v] == a
+                f3 = np.array([oix.fadd[s], oix.frescale[s], oix.ferr[s]], np.float32)
+                e, lo = oracle.estimate(f3, g, a, dl[q], kk[q])
+                assert u32(np.float32(e)) == u32(est_np[v]) and u32(np.float32(lo)) == u32(low_np[v])
+
+
+def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
+    torch = _torch()
+    nq = Q.shape[0]
+    Qr = oracle.rotate(Q, oix.P)
+    qr, planes, delta, k1 = _query_stage(idx, Qr)
+    probes = torch.empty((nq, nprobe), dtype=torch.int32, device="cuda")
+    g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), nq, nprobe, 0, ptr(probes), ptr(g), stream())
+    ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+    dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, R, prune,
+         slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
+    p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
+    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
+    cap_o = max(1 << ((cap if cap > 0 else 1024) - 1).bit_length(), 1 << (R + 256 - 1).bit_length())
+    oi, od, ost = oracle.scan(oix, Qr, pl2, d2, k2, p2, g2, R, 256, cap_o, prune, slices, with_stats=True)
+    return ids.cpu().numpy(), dist.cpu().numpy(), stats.cpu().numpy(), oi, od, ost
+
+
+@pytest.mark.parametrize("prune,slices,R,cap", [(1, 1, 10, 0), (1, 1, 40, 0), (0, 1, 40, 0), (1, 4, 40, 0),
+                                                 (1, 1, 40, 512), (1, 3, 100, 2048), (0, 8, 10, 0)])
+def test_scan_candidates_bit_exact(oracle, case, prune, slices, R, cap):
+    idx, oix, X, Q, C, lab = case
+    gi, gd, gst, oi, od, ost = _scan(idx, oracle, oix, Q, 8, R, prune, slices, cap)
+    assert np.array_equal(gi, oi)
+    assert np.array_equal(u32(gd), u32(od))
+    assert gst.tolist() == ost.tolist()
+
+
+def test_rerank_bit_exact(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    torch = _torch()
+    rng = np.random.default_rng(2)
+    cand = rng.integers(0, X.shape[0], (Q.shape[0], 40)).astype(np.int64)
+    cand[:, 30:] = -1
+    ci, q = dev(cand), dev(Q)
+    d = torch.empty((Q.shape[0], 10), dtype=torch.float32, device="cuda")
+    i = torch.empty((Q.shape[0], 10), dtype=torch.int64, device="cuda")
+    call("rbq_rerank", idx.handle, ptr(q), Q.shape[0], ptr(ci), 40, 10, ptr(d), ptr(i), stream())
+    d2, i2 = oracle.rerank(X, Q, cand, 10)
+    assert np.array_equal(i.cpu().numpy(), i2)
+    assert np.array_equal(u32(d.cpu().numpy()), u32(d2))
+
+
+@pytest.mark.parametrize("nprobe,R,prune", [(8, 40, 1), (8, 0, 1), (64, 40, 0), (3, 100, 1)])
+def test_search_end_to_end(oracle, case, nprobe, R, prune):
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune = nprobe, R, bool(prune)
+    d, i = idx.search(Q, 10)
+    d2, i2 = oracle.search(oix, Q, 10, nprobe, R, prune=prune)
+    assert np.array_equal(i, i2)
+    assert np.array_equal(u32(d), u32(d2))
+    fin = np.isfinite(d2)
+    assert np.allclose(d[fin], d2[fin], rtol=REL_TOL, atol=0)
+    _, gt = oracle.knn_exact(X, Q, 10)
+    assert oracle.recall(i, gt) == oracle.recall(i2, gt)
+
+
+@pytest.mark.parametrize("nq", [1, 2, 33, 64])
+def test_small_batches_use_probe_slices(oracle, case, nq):
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune = 16, 40, True
+    d, i = idx.search(Q[:nq], 10)
+    sl = max(1, min(512 // nq, 16))
+    d2, i2 = oracle.search(oix, Q[:nq], 10, 16, 40, prune=1, slices=sl)
+    assert np.array_equal(i, i2)
+    assert np.array_equal(u32(d), u32(d2))
+
+
+def test_search_host_matches_device_search(case):
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank = 8, 40
+    d, i = idx.search(Q, 10)
+    dh, ih = idx.search_host(Q, 10)
+    assert np.array_equal(i, ih) and np.array_equal(u32(d), u32(dh))
+
+
+def test_torch_inputs_stay_on_device(case):
+    torch = _torch()
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank = 8, 40
+    d, i = idx.search(torch.from_numpy(Q).cuda(), 10)
+    assert d.is_cuda and i.is_cuda and i.dtype == torch.int64
+    d2, i2 = idx.search(Q, 10)
+    assert np.array_equal(i.cpu().numpy(), i2)
+
+
+def test_save_load_round_trip(tmp_path, case):
+    from neurosamble_b200 import read_index, write_index
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank = 8, 40
+    d, i = idx.search(Q, 10)
+    path = tmp_path / "a.rbq"
+    write_index(idx, str(path))
+    idx2 = read_index(str(path))
+    idx2.nprobe, idx2.k_rerank = 8, 40
+    d2, i2 = idx2.search(Q, 10)
+    assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    assert idx2.ntotal == X.shape[0]
+
+
+def test_incremental_add_matches_single_add(oracle, case):
+    from neurosamble_b200 import IndexIVFRaBitQ
+    idx, oix, X, Q, C, lab = case
+    idx2 = IndexIVFRaBitQ(128, 64, seed=7)
+    idx2.set_centroids(C)
+    idx2.add(X[:7000], labels=lab[:7000])
+    idx2.add(X[7000:], labels=lab[7000:])
+    ex, ex2 = idx.export_lists(), idx2.export_lists()
+    for k in ex:
+        assert np.array_equal(ex[k], ex2[k]), k
+
+
+def test_errors_raise_runtime_error(case):
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe = 65
+    with pytest.raises(RuntimeError, match="n_probes"):
+        idx.search(Q[:2], 10)
+    idx.nprobe = 8
+    with pytest.raises(RuntimeError):
+        idx.search(np.zeros((2, 7), np.float32), 10)
+
+
+@pytest.mark.parametrize("d,n,k", [(100, 3000, 16), (768, 2000, 8), (32, 500, 4)])
+def test_other_dimensions(oracle, d, n, k):
+    X, Q = mixture(n, d, 6, 0.3, 40, seed=d)
+    C, _ = oracle.kmeans(X, k, iters=3)
+    lab = oracle.assign(X, C)
+    idx, oix = make_index(oracle, X, C, lab, seed=5)
+    ex = idx.export_lists()
+    assert np.array_equal(ex["codes"], oix.codes)
+    assert np.array_equal(u32(ex["ferr"]), u32(oix.ferr))
+    idx.nprobe, idx.k_rerank = min(4, k), 20
+    dd, ii = idx.search(Q, 5)
+    d2, i2 = oracle.search(oix, Q, 5, min(4, k), 20, prune=1)
+    assert np.array_equal(ii, i2) and np.array_equal(u32(dd), u32(d2))
+
+
+def test_empty_lists_and_padding(oracle):
+    X, Q = mixture(50, 64, 2, 0.3, 3, seed=9)
+    C = np.concatenate([X[:2], X[:2] + 5.0]).astype(np.float32)
+    lab = oracle.assign(X, C)
+    idx, oix = make_index(oracle, X, C, lab)
+    assert (np.diff(oix.list_off) == 0).any()
+    idx.nprobe, idx.k_rerank, idx.prune = 4, 0, False
+    d, i = idx.search(Q, 80)
+    d2, i2 = oracle.search(oix, Q, 80, 4, 0, prune=0)
+    assert np.array_equal(i, i2)
+    assert (i == -1).any() and np.all(np.isinf(d[i == -1]))
+
+
+def test_gpu_kmeans_is_deterministic():
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(30000, 64, 40, 0.3, 10, seed=3)
+    cs = []
+    for _ in range(2):
+        idx = IndexIVFRaBitQ(64, 32, seed=1, kmeans_iters=5)
+        idx.train(X)
+        cs.append(idx.centroids()[0])
+    assert np.array_equal(u32(cs[0]), u32(cs[1]))
+
+
+def test_config1_parity_and_recall(oracle):
+    """BASELINE config 1 shape at full size: 100k x 128, K = 256, P = 16, k = 10, R = 40."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(100000, 128, 256, 0.3, 1000, seed=11)
+    idx = IndexIVFRaBitQ(128, 256, seed=7, kmeans_iters=10)
+    idx.train(X)
+    idx.add(X)
+    C, _ = idx.centroids()
+    lab = oracle.assign(X, C)
+    oix = oracle.build(X, C, lab, idx.rotation(), idx.query_scale)
+    ex = idx.export_lists()
+    assert np.array_equal(ex["ids"], oix.ids) and np.array_equal(ex["codes"], oix.codes)
+    idx.nprobe, idx.k_rerank = 16, 40
+    d, i = idx.search(Q, 10)
+    d2, i2 = oracle.search(oix, Q, 10, 16, 40, prune=1)
+    assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    _, gt = oracle.knn_exact(X, Q, 10)
+    assert oracle.recall(i, gt) == oracle.recall(i2, gt)
