@@ -152,6 +152,28 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
              int32_t R, int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev,
              float* cand_dist_dev, uint64_t* stats_dev, void* stream);
+/* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
+ * search time: a host program whose device memory is handed out up front by its own pool
+ * (so a library cudaMalloc would fail or break its budget), or a latency-critical search
+ * thread that must not pay for an allocation (cudaMalloc can synchronise the whole device).
+ * The scan's only scratch, the per-slice candidate keys, lives in a fixed array of
+ * RBQ_NOALLOC_SCRATCH_BYTES compiled into librbq.so; every GPU that loads the library holds
+ * that much memory until the process exits.  Inputs, outputs and their meaning are exactly
+ * those of rbq_scan.  Limits and rules:
+ *   - needs nq*slices*R*8 bytes, plus nq*R*8 when slices > 1 (each part rounded up to 256);
+ *     anything larger is rejected with RBQ_ERR_INVALID before any work is queued;
+ *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture;
+ *   - all calls share the one array and it keeps the last call's contents (nothing in it has
+ *     to start at zero: every key read is written earlier in the same call); calls that can
+ *     overlap on the GPU (other streams, other host threads, same device) race on it and must
+ *     be serialised by the caller.
+ * It calls no cudaMalloc / cudaFree / cudaMallocAsync.  No counterpart in the reference. */
+#define RBQ_NOALLOC_SCRATCH_BYTES (32u << 20)
+int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                     const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                     int32_t R, int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev,
+                     float* cand_dist_dev, uint64_t* stats_dev, void* stream);
 /* Phase-1 estimator of one query against every vector of list `list`: integer popcount
  * inner product acc, estimate est and lower bound low (slot order of the list).  Replaces the
  * phase-1 loop of computeInnerProductsWithBitwiseBlockSort (searcher_gpu_quantize_query.cu:

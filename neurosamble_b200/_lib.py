@@ -64,6 +64,7 @@ SIGNATURES = {
     "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
     "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "rbq_merge_results": [_P, _P, _I32, _I64, _I32, _P, _P, _P],
     "rbq_gen_mixture": [_P, _I64, _I32, _I32, _F32, _I32, _I32, _U64, _P],

@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -1064,3 +1065,88 @@ int rbq_gen_queries(const float* X_dev, int64_t n, int32_t D, float* Q_dev, int6
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free scan (rbq_scan_noalloc).  Its scratch is this fixed device array; host code
+// must never pass `rbq_noalloc_scratch` itself to a kernel (on the host the name is only a
+// stand-in), so the device address is looked up once per device and cached.
+// ---------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char rbq_noalloc_scratch[RBQ_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of the scratch array on `device`, which must be the current device.
+unsigned char* noalloc_scratch_address(int device)
+{
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  RBQ_CHECK(device >= 0 && device < 64, RBQ_ERR_INVALID, "device ordinal out of range");
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    RBQ_CUDA(cudaGetSymbolAddress(&p, rbq_noalloc_scratch));
+    g_noalloc_addr[device] = p;
+  }
+  return static_cast<unsigned char*>(g_noalloc_addr[device]);
+}
+
+inline size_t round_up_256(size_t v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
+extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev,
+                                const float* delta_dev, const float* k1_dev, int64_t nq, const int32_t* probes_dev,
+                                const float* g_dev, int32_t nprobe, int32_t R, int32_t prune, int32_t slices,
+                                int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev,
+                                void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && cand_ids_dev &&
+                          cand_dist_dev),
+              RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(nq >= 0 && R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1, RBQ_ERR_INVALID,
+              "bad scan parameters");
+    const size_t keys_bytes = round_up_256((size_t)nq * slices * R * 8);
+    const size_t merged_bytes = slices > 1 ? round_up_256((size_t)nq * R * 8) : 0;
+    RBQ_CHECK(keys_bytes + merged_bytes <= (size_t)RBQ_NOALLOC_SCRATCH_BYTES, RBQ_ERR_INVALID,
+              "rbq_scan_noalloc: nq * slices * R needs " + std::to_string(keys_bytes + merged_bytes) +
+                  " bytes of scratch; the static scratch holds " + std::to_string(RBQ_NOALLOC_SCRATCH_BYTES) +
+                  " bytes (use rbq_scan, or split the batch)");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    unsigned char* base = noalloc_scratch_address(ix.device);
+    unsigned long long* ks = reinterpret_cast<unsigned long long*>(base);
+    unsigned long long* k2 = slices > 1 ? reinterpret_cast<unsigned long long*>(base + keys_bytes) : ks;
+    const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
+    ScanArgs sa;
+    sa.list_off = ix.list_off;
+    sa.ids = ix.ids;
+    sa.codes = ix.codes;
+    sa.fadd = ix.fadd;
+    sa.frescale = ix.frescale;
+    sa.ferr = ix.ferr;
+    sa.Dp = ix.Dp;
+    sa.W = ix.W;
+    sa.Qr = Qr_dev;
+    sa.planes = planes_dev;
+    sa.delta = delta_dev;
+    sa.k1 = k1_dev;
+    sa.nq = nq;
+    sa.probes = probes_dev;
+    sa.g = g_dev;
+    sa.nprobe = nprobe;
+    sa.R = R;
+    sa.cap = cap;
+    sa.prune = prune ? 1 : 0;
+    sa.slices = slices;
+    sa.shard_rank = ix.shard_rank;
+    sa.shard_count = ix.shard_count;
+    sa.out_keys = ks;
+    sa.stats = reinterpret_cast<unsigned long long*>(stats_dev);
+    launch_scan(sa, s);
+    if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
+    launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);
+  });
+}
