@@ -427,6 +427,10 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
     ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
     dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g), P, R, 1,
+              1, 0, _ptr(ids), _ptr(dist), _ptr(stats), st)
+    scanned, admitted = (int(v) for v in stats.cpu().tolist())
     ts = []
     for it in range(3 + steps):
         flush.zero_()
@@ -467,7 +471,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
             "traffic": traffic, "peak_kind": kind, "kernel": "rbq scan_kernel (+ key->id epilogue)",
             "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
-            "launch_ms": round(scan_ms, 4)}
+            "launch_ms": round(scan_ms, 4), "prune_admitted_fraction": round(admitted / max(1, scanned), 4)}
     ach_r = rr_bytes / (rr_ms / 1000.0) / 1e9
     roof_rr = {"bound": "hbm", "achieved": round(ach_r, 1), "peak": peak, "unit": "GB/s",
                "frac": round(ach_r / peak, 4), "kernel": "rbq rerank_kernel (+ id->key prologue)",

@@ -64,7 +64,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     env.pop("CC", None)
     for src in SOURCES:
         obj = os.path.join(OUT_DIR, os.path.splitext(src)[0] + ".o")
-        cmd = [nvcc, *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        extra = os.environ.get("RBQ_NVCC_EXTRA", "").split()
+        cmd = [nvcc, *NVCC_FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
         if src.endswith(".cpp"):
             cmd = [_cxx(), "-std=c++17", "-O3", "-fPIC", "-ffp-contract=off", "-fno-fast-math",
                    "-I/usr/local/cuda/include", "-c", os.path.join(CSRC, src), "-o", obj]

@@ -412,6 +412,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     sa.fadd = ix.fadd;
     sa.frescale = ix.frescale;
     sa.ferr = ix.ferr;
+    sa.n_slots = ix.n_rows;
     sa.Dp = ix.Dp;
     sa.W = ix.W;
     sa.Qr = Qr;
@@ -979,6 +980,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     sa.fadd = ix.fadd;
     sa.frescale = ix.frescale;
     sa.ferr = ix.ferr;
+    sa.n_slots = ix.n_rows;
     sa.Dp = ix.Dp;
     sa.W = ix.W;
     sa.Qr = Qr_dev;
@@ -1127,6 +1129,7 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
     sa.fadd = ix.fadd;
     sa.frescale = ix.frescale;
     sa.ferr = ix.ferr;
+    sa.n_slots = ix.n_rows;
     sa.Dp = ix.Dp;
     sa.W = ix.W;
     sa.Qr = Qr_dev;

@@ -164,6 +164,7 @@ struct ScanArgs {
   const float* fadd;
   const float* frescale;
   const float* ferr;
+  int64_t n_slots;  // vectors on the shard (the scan indexes slots with 32-bit ints)
   int Dp, W;
   const float* Qr;
   const uint32_t* planes;
@@ -181,7 +182,7 @@ struct ScanArgs {
   unsigned long long* out_keys;  // [nq, slices, R]
   unsigned long long* stats;     // optional [2]: scanned, admitted
 };
-constexpr int kScanTile = 256;
+constexpr int kScanTile = 512;  // vectors per scan tile (256 threads x 2)
 void launch_scan(const ScanArgs& a, cudaStream_t s);
 // Phase-1 dump for one query and one list.
 void launch_list_estimates(const Index& ix, const uint32_t* planes, float delta, float k1, float g, int list,

@@ -261,19 +261,26 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* 
 
 // ---------------------------------------------------------------------------------------
 // The list scan (computeInnerProductsWithBitwiseBlockSort<4, false, false>,
-// searcher_gpu_quantize_query.cu:172-626, re-designed).  One CTA per (query, probe slice):
-// the CTA walks its slice's lists in probe order in tiles of kScanTile vectors, one vector
-// per thread:
-//   phase 1  acc = sum_w [sum_{b<3} popc(P_b & c) << b  -  popc(P_3 & c) << 3]   (exact int)
+// searcher_gpu_quantize_query.cu:172-626, re-designed).  One CTA of 256 threads per
+// (query, probe slice).  The slice's lists form one flat sequence of vectors (probe order,
+// slot order inside a list) walked in tiles of kScanTile = 512 vectors that run across list
+// boundaries; thread t takes vectors t and t + 256 of each tile.
+//   phase 1 (per thread, planes in registers)
+//            acc = sum_w [sum_{b<3} popc(P_b & c) << b  -  popc(P_3 & c) << 3]   (exact int)
 //            est = (f_add + g) + f_rescale * (acc * delta + k1);  low = est - f_err * sqrt(g)
 //            admit if !prune || low < tau
-//   phase 2  exact_ip = sum over set bits of q (per byte from 0, per word ((b0+b1)+b2)+b3,
-//            words in order); dist = (f_add + g) + f_rescale * (exact_ip + k1);
-//            keep (dist, id) if dist <= tau.
-// tau (the R-th best kept distance) only changes at tile boundaries: when the buffer holds
-// more than cap - kScanTile keys it is sorted and cut to R.  The schedule is a function of
-// the data alone, so results are deterministic and equal to the oracle's.
+//   phase 2 (per warp)  right after each round of phase 1, the warp's admitted vectors are
+//            taken one at a time by all 32 lanes (warp_exact_ip: per-byte sums from a
+//            per-query table, lane sums, xor butterfly);
+//            dist = (f_add + g) + f_rescale * (exact_ip + k1); keep (dist, id) if dist <= tau.
+// tau (the R-th best kept distance) only changes between tiles: when the buffer holds more
+// than cap - kScanTile keys it is sorted and cut to R.  The schedule depends on the data
+// alone, so results are deterministic and equal to the oracle's.
 // ---------------------------------------------------------------------------------------
+constexpr int kScanThreads = 256;
+constexpr int kScanVpt = kScanTile / kScanThreads;
+static_assert(kScanTile % kScanThreads == 0, "tile must be a multiple of the block size");
+
 template <int W>
 __device__ __forceinline__ void load_code(const uint32_t* __restrict__ codes, int64_t slot, uint32_t (&c)[W])
 {
@@ -293,135 +300,462 @@ __device__ __forceinline__ void load_code(const uint32_t* __restrict__ codes, in
   }
 }
 
-template <int W>
-__device__ __forceinline__ float exact_ip_bits(const float* __restrict__ qs, const uint32_t (&c)[W])
+// Code bytes per vector up to which the scan keeps a per-query byte table in shared memory.
+constexpr int kLutMaxBytes = 32;
+
+// <bits of the vector at `slot`, q>, computed by the whole warp; every lane returns the value.
+// Lane l adds bsum(j) for the code bytes j = l, l + 32, ... (bsum(j) = sum of q over the set
+// bits of byte j of the MSB-first bit stream, dims 8j..8j+7, from 0), then an xor butterfly
+// (16, 8, 4, 2, 1) combines the lanes.  With a table, bsum(j) = lut[j * 256 + byte]; without,
+// it is summed from qsT (the query transposed by byte: qsT[jj * NB + j] = q[8 j + jj]).
+template <int W, bool kLut>
+__device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ codes, int64_t slot,
+                                               const float* __restrict__ lut, const float* __restrict__ qsT,
+                                               int lane)
 {
-  float acc = 0.0f;
+  constexpr int NB = 4 * W;
+  constexpr int M = (NB + 31) / 32;
+  const unsigned char* cb = reinterpret_cast<const unsigned char*>(codes + slot * W);
+  float v = 0.0f;
 #pragma unroll
-  for (int w = 0; w < W; ++w) {
-    const uint32_t cw = c[w];
-    float part[4];
+  for (int m = 0; m < M; ++m) {
+    const int j = lane + 32 * m;
+    if (j < NB) {
+      const uint32_t u8 = __ldg(cb + (j ^ 3));  // byte j of the MSB-first bit stream
+      float b;
+      if constexpr (kLut) {
+        b = lut[j * 256 + u8];
+      } else {
+        b = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float s = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float v = qs[32 * w + 8 * i + j];
-        s = ((cw >> (31 - (8 * i + j))) & 1u) ? __fadd_rn(s, v) : s;
+        for (int jj = 0; jj < 8; ++jj) {
+          const float q = qsT[jj * NB + j];
+          b = ((u8 >> (7 - jj)) & 1u) ? __fadd_rn(b, q) : b;
+        }
       }
-      part[i] = s;
+      v = __fadd_rn(v, b);
     }
-    const float pw = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), part[2]), part[3]);
-    acc = __fadd_rn(acc, pw);
   }
-  return acc;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
 }
 
-template <int W>
-__global__ void __launch_bounds__(kScanTile) scan_kernel(const ScanArgs a)
+// ---------------------------------------------------------------------------------------
+// Signed 4-bit x 1-bit inner product with few popcounts.  The AND-ed plane words are summed
+// bit-sliced with carry-save adders (Harley-Seal): a full adder turns three words of weight w
+// into a sum word (weight w) and a carry word (weight 2w) in two logic ops, so eight words of
+// a plane (and the carries of the plane below) collapse into one word per weight before any
+// popcount.  The integer result equals sum_w [sum_{b<3} popc(P_b & c) << b - popc(P_3 & c) << 3].
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void csa(uint32_t& h, uint32_t& l, uint32_t a, uint32_t b, uint32_t c)
 {
+  const uint32_t u = a ^ b;
+  h = (a & b) | (u & c);
+  l = u ^ c;
+}
+__device__ __forceinline__ void hadd(uint32_t& h, uint32_t& l, uint32_t a, uint32_t b)
+{
+  h = a & b;
+  l = a ^ b;
+}
+
+// Eight words: P(b, w) returns plane b word w of the chunk, c the chunk's code words.
+template <typename PF>
+__device__ __forceinline__ int32_t signed_dot8(const PF& P, const uint32_t (&c)[8])
+{
+  uint32_t a[8], b[8], d[8], e[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    a[w] = P(0, w) & c[w];
+    b[w] = P(1, w) & c[w];
+    d[w] = P(2, w) & c[w];
+    e[w] = P(3, w) & c[w];
+  }
+  uint32_t o1 = a[0], k0, k1, k2, k3;  // weight 1 (plane 0)
+  csa(k0, o1, o1, a[1], a[2]);
+  csa(k1, o1, o1, a[3], a[4]);
+  csa(k2, o1, o1, a[5], a[6]);
+  hadd(k3, o1, o1, a[7]);
+  uint32_t o2 = k0, m0, m1, m2, m3, m4, m5;  // weight 2 (carries + plane 1)
+  csa(m0, o2, o2, k1, k2);
+  csa(m1, o2, o2, k3, b[0]);
+  csa(m2, o2, o2, b[1], b[2]);
+  csa(m3, o2, o2, b[3], b[4]);
+  csa(m4, o2, o2, b[5], b[6]);
+  hadd(m5, o2, o2, b[7]);
+  uint32_t o4 = m0, n0, n1, n2, n3, n4, n5, n6;  // weight 4 (carries + plane 2)
+  csa(n0, o4, o4, m1, m2);
+  csa(n1, o4, o4, m3, m4);
+  csa(n2, o4, o4, m5, d[0]);
+  csa(n3, o4, o4, d[1], d[2]);
+  csa(n4, o4, o4, d[3], d[4]);
+  csa(n5, o4, o4, d[5], d[6]);
+  hadd(n6, o4, o4, d[7]);
+  uint32_t o8 = n0, r0, r1, r2;  // weight 8
+  csa(r0, o8, o8, n1, n2);
+  csa(r1, o8, o8, n3, n4);
+  csa(r2, o8, o8, n5, n6);
+  uint32_t o16 = r0, t0;  // weight 16, 32
+  csa(t0, o16, o16, r1, r2);
+  const int32_t pos = __popc(o1) + 2 * __popc(o2) + 4 * __popc(o4) + 8 * __popc(o8) + 16 * __popc(o16) +
+                      32 * __popc(t0);
+  // plane 3 (weight -8): one popcount per word keeps the popcount unit busy while the logic
+  // unit does the adders above
+  const int32_t neg = (__popc(e[0]) + __popc(e[1]) + __popc(e[2]) + __popc(e[3])) +
+                      (__popc(e[4]) + __popc(e[5]) + __popc(e[6]) + __popc(e[7]));
+  return pos - 8 * neg;
+}
+
+template <typename PF>
+__device__ __forceinline__ int32_t signed_dot4(const PF& P, const uint32_t (&c)[4])
+{
+  uint32_t a[4], b[4], d[4], e[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    a[w] = P(0, w) & c[w];
+    b[w] = P(1, w) & c[w];
+    d[w] = P(2, w) & c[w];
+    e[w] = P(3, w) & c[w];
+  }
+  uint32_t o1 = a[0], k0, k1;
+  csa(k0, o1, o1, a[1], a[2]);
+  hadd(k1, o1, o1, a[3]);
+  uint32_t o2 = k0, m0, m1, m2;
+  csa(m0, o2, o2, k1, b[0]);
+  csa(m1, o2, o2, b[1], b[2]);
+  hadd(m2, o2, o2, b[3]);
+  uint32_t o4 = m0, n0, n1, n2;
+  csa(n0, o4, o4, m1, m2);
+  csa(n1, o4, o4, d[0], d[1]);
+  csa(n2, o4, o4, d[2], d[3]);
+  uint32_t o8 = n0, r0;
+  csa(r0, o8, o8, n1, n2);
+  const int32_t pos = __popc(o1) + 2 * __popc(o2) + 4 * __popc(o4) + 8 * __popc(o8) + 16 * __popc(r0);
+  const int32_t neg = __popc(e[0]) + __popc(e[1]) + __popc(e[2]) + __popc(e[3]);
+  return pos - 8 * neg;
+}
+
+// Whole vector: chunks of 8 words (or one 4-word chunk), else one popcount per plane word.
+template <int W, typename PF>
+__device__ __forceinline__ int32_t signed_dot(const PF& P, const uint32_t (&c)[W])
+{
+  if constexpr (W % 8 == 0) {
+    int32_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < W / 8; ++k) {
+      uint32_t cc[8];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) cc[w] = c[8 * k + w];
+      auto Pk = [&](int b, int w) { return P(b, 8 * k + w); };
+      acc += signed_dot8(Pk, cc);
+    }
+    return acc;
+  } else if constexpr (W == 4) {
+    return signed_dot4(P, c);
+  } else {
+    int32_t s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      s0 += __popc(P(0, w) & c[w]);
+      s1 += __popc(P(1, w) & c[w]);
+      s2 += __popc(P(2, w) & c[w]);
+      s3 += __popc(P(3, w) & c[w]);
+    }
+    return s0 + 2 * s1 + 4 * s2 - 8 * s3;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Block-wide selection of the R smallest of n distinct keys src[0..n) (R <= n): a radix
+// select, 8 bits per pass from the top, finds the threshold key T with exactly R keys <= T;
+// those are copied to dst[0..R) (any order) and the largest of them (the R-th smallest key) is
+// returned.  hist: 256 shared counters; misc: 3 shared ints; kmax, cnt: shared scratch.
+// ---------------------------------------------------------------------------------------
+__device__ unsigned long long block_keep_smallest(const unsigned long long* src, int n, int R,
+                                                  unsigned long long* dst, unsigned* hist, int* misc,
+                                                  unsigned long long* kmax, int* cnt)
+{
+  const int tid = threadIdx.x, lane = tid & 31;
+  unsigned long long prefix = 0, pmask = 0;
+  int need = R;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const unsigned long long k = src[i];
+      if ((k & pmask) == prefix) atomicAdd(&hist[(unsigned)(k >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      unsigned v[8], s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = hist[lane * 8 + j];
+        s += v[j];
+      }
+      unsigned inc = s;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += t;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, inc >= (unsigned)need);
+      if (lane == __ffs(hit) - 1) {
+        unsigned cum = inc - s;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (cum + v[j] >= (unsigned)need) {
+            misc[0] = lane * 8 + j;
+            misc[1] = need - (int)cum;
+            misc[2] = (int)v[j];
+            break;
+          }
+          cum += v[j];
+        }
+      }
+    }
+    __syncthreads();
+    const int bin = misc[0], nd = misc[1], inbin = misc[2];
+    __syncthreads();
+    prefix |= (unsigned long long)bin << shift;
+    pmask |= 255ull << shift;
+    need = nd;
+    if (inbin == need) {  // the whole bin is kept: everything at or below its top
+      if (shift > 0) prefix |= (1ull << shift) - 1;
+      break;
+    }
+  }
+  if (tid == 0) {
+    *kmax = 0ull;
+    *cnt = 0;
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const unsigned long long k = src[i];
+    if (k <= prefix) {
+      dst[atomicAdd(cnt, 1)] = k;
+      atomicMax(kmax, k);
+    }
+  }
+  __syncthreads();
+  return *kmax;
+}
+
+// Resident CTAs per SM the scan is compiled for (register budget 65536 / (256 * this)).
+#ifndef RBQ_SCAN_MIN_BLOCKS
+#define RBQ_SCAN_MIN_BLOCKS 4
+#endif
+
+template <int W>
+__global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel(const ScanArgs a)
+{
+  constexpr bool kPlanesInRegs = (W <= 8);
+  constexpr int NB = 4 * W;
+  constexpr bool kLut = (NB <= kLutMaxBytes);
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);          // [cap]
-  float* qs = reinterpret_cast<float*>(keys + a.cap);                                  // [Dp]
-  uint32_t* pl = reinterpret_cast<uint32_t*>(qs + W * 32);                             // [4W]
-  int32_t* own_l = reinterpret_cast<int32_t*>(pl + 4 * W);                             // [nprobe]
-  float* own_g = reinterpret_cast<float*>(own_l + a.nprobe);                           // [nprobe]
-  __shared__ int s_count, s_m;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);  // [cap]
+  unsigned long long* keys2 = keys + a.cap;                                    // [cap]
+  int* pre = reinterpret_cast<int*>(keys2 + a.cap);                            // [nprobe + 1]
+  int* lbase = pre + (a.nprobe + 1);                                            // [nprobe]
+  float* lg = reinterpret_cast<float*>(lbase + a.nprobe);                       // [nprobe]
+  float* lsq = lg + a.nprobe;                                                   // [nprobe]
+  uint32_t* pl = reinterpret_cast<uint32_t*>(lsq + a.nprobe);                  // [4 * W]
+  float* lut = reinterpret_cast<float*>(pl + 4 * W);                            // [NB * 256] if kLut
+  float* qsT = lut + (kLut ? NB * 256 : 0);                                     // [8 * NB]
+  __shared__ int s_count, s_nl, s_misc[3], s_cnt2;
   __shared__ float s_tau;
+  __shared__ unsigned s_hist[256];
+  __shared__ unsigned long long s_kmax;
 
   const int64_t q = blockIdx.x / a.slices;
   const int slice = blockIdx.x - (int)(q * a.slices);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  for (int j = tid; j < W * 32; j += blockDim.x) qs[j] = a.Qr[q * (W * 32) + j];
-  for (int j = tid; j < 4 * W; j += blockDim.x) pl[j] = a.planes[q * 4 * W + j];
-  if (tid == 0) {
-    int m = 0;
-    for (int p = 0; p < a.nprobe; ++p) {
-      const int l = a.probes[q * a.nprobe + p];
-      if (l >= 0 && l % a.shard_count == a.shard_rank) {
-        own_l[m] = l;
-        own_g[m] = a.g[q * a.nprobe + p];
-        ++m;
-      }
+  for (int i = tid; i < 8 * NB; i += kScanThreads) {
+    const int jj = i / NB, j = i - jj * NB;
+    qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
+  }
+  for (int j = tid; j < 4 * W; j += kScanThreads) pl[j] = a.planes[q * 4 * W + j];
+  if constexpr (kLut) {
+    // lut[j * 256 + byte] = sum of q over the set bits of `byte` at code byte j (bit 7 first).
+    const float* qrow = a.Qr + q * (8 * NB);
+    for (int e = tid; e < NB * 256; e += kScanThreads) {
+      const int j = e >> 8, byte = e & 255;
+      float b = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        if ((byte >> (7 - jj)) & 1) b = __fadd_rn(b, __ldg(qrow + 8 * j + jj));
+      lut[e] = b;
     }
-    s_m = m;
-    s_count = 0;
-    s_tau = __int_as_float(0x7f800000);
+  }
+  if (warp == 0) {
+    // The slice's lists: owned probes (l % shard_count == shard_rank) with owned-rank in
+    // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
+    // sequence.
+    const int* prow = a.probes + q * a.nprobe;
+    int m = 0;
+    for (int p0 = 0; p0 < a.nprobe; p0 += 32) {
+      const int p = p0 + lane;
+      const int l = p < a.nprobe ? prow[p] : -1;
+      m += __popc(__ballot_sync(0xffffffffu, l >= 0 && l % a.shard_count == a.shard_rank));
+    }
+    const int pb = (int)(((int64_t)slice * m) / a.slices);
+    const int pe = (int)(((int64_t)(slice + 1) * m) / a.slices);
+    int o = 0;
+    for (int p0 = 0; p0 < a.nprobe && o < pe; p0 += 32) {
+      const int p = p0 + lane;
+      const int l = p < a.nprobe ? prow[p] : -1;
+      const bool own = l >= 0 && l % a.shard_count == a.shard_rank;
+      const unsigned mask = __ballot_sync(0xffffffffu, own);
+      const int rank = o + __popc(mask & ((1u << lane) - 1u));
+      if (own && rank >= pb && rank < pe) {
+        const int i = rank - pb;
+        const int64_t b0 = a.list_off[l];
+        const float g = a.g[q * a.nprobe + p];
+        lbase[i] = (int)b0;
+        pre[i + 1] = (int)(a.list_off[l + 1] - b0);  // size, turned into a prefix below
+        lg[i] = g;
+        lsq[i] = sqrtf(g);
+      }
+      o += __popc(mask);
+    }
+    const int n = pe - pb;
+    __syncwarp();
+    int carry = 0;
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      const int i = c0 + lane;
+      int v = i < n ? pre[i + 1] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += t;
+      }
+      if (i < n) pre[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) {
+      pre[0] = 0;
+      if (n == 0) {
+        lbase[0] = 0;
+        lg[0] = 0.0f;
+        lsq[0] = 0.0f;
+      }
+      s_nl = n;
+      s_count = 0;
+      s_tau = __int_as_float(0x7f800000);
+    }
   }
   __syncthreads();
-  const int m = s_m;
-  const int p_begin = (int)(((int64_t)slice * m) / a.slices);
-  const int p_end = (int)(((int64_t)(slice + 1) * m) / a.slices);
+  const int nl = s_nl;
+  const int total = pre[nl];
   const float delta = a.delta[q];
   const float k1 = a.k1[q];
-  unsigned long long n_scan = 0, n_admit = 0;
+  uint32_t plr[kPlanesInRegs ? 4 * W : 1];
+  if constexpr (kPlanesInRegs) {
+#pragma unroll
+    for (int i = 0; i < 4 * W; ++i) plr[i] = pl[i];
+  }
+  auto P = [&](int b, int w) -> uint32_t {
+    if constexpr (kPlanesInRegs) return plr[b * W + w];
+    else return pl[b * W + w];
+  };
+  unsigned n_scan = 0, n_admit = 0;
+  // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
+  int cur = 0;
+  int nxt = nl > 0 ? pre[1] : 0;
+  int sadj = lbase[0];
+  float gc = lg[0], sqc = lsq[0];
 
-  for (int pi = p_begin; pi < p_end; ++pi) {
-    const int l = own_l[pi];
-    const float g = own_g[pi];
-    const float sqrt_g = sqrtf(g);
-    const int64_t base = a.list_off[l];
-    const int64_t n = a.list_off[l + 1] - base;
-    for (int64_t t0 = 0; t0 < n; t0 += kScanTile) {
-      const float tau = s_tau;
-      const int64_t v = t0 + tid;
-      if (v < n) {
-        const int64_t slot = base + v;
+  for (int t0 = 0; t0 < total; t0 += kScanTile) {
+    const float tau = s_tau;
+#pragma unroll
+    for (int u = 0; u < kScanVpt; ++u) {
+      const int f = t0 + u * kScanThreads + tid;
+      bool surv = false;
+      int sslot = 0;
+      float sbase = 0.0f, sfr = 0.0f;
+      if (f < total) {
+        if (f >= nxt) {
+          do {
+            ++cur;
+          } while (pre[cur + 1] <= f);
+          nxt = pre[cur + 1];
+          sadj = lbase[cur] - pre[cur];
+          gc = lg[cur];
+          sqc = lsq[cur];
+        }
+        const int slot = sadj + f;
         uint32_t c[W];
         load_code<W>(a.codes, slot, c);
-        int32_t acc = 0;
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-          acc += __popc(pl[0 * W + w] & c[w]);
-          acc += __popc(pl[1 * W + w] & c[w]) << 1;
-          acc += __popc(pl[2 * W + w] & c[w]) << 2;
-          acc -= __popc(pl[3 * W + w] & c[w]) << 3;
-        }
+        const int32_t acc = signed_dot<W>(P, c);
         const float fr = __ldg(a.frescale + slot);
-        const float base_d = __fadd_rn(__ldg(a.fadd + slot), g);
+        const float base_d = __fadd_rn(__ldg(a.fadd + slot), gc);
         const float ip = __fmul_rn((float)acc, delta);
         const float est = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(ip, k1)));
-        const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqrt_g));
+        const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
         ++n_scan;
         if (!a.prune || low < tau) {
           ++n_admit;
-          const float eip = exact_ip_bits<W>(qs, c);
-          const float dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
-          if (dist <= tau) {
-            const int at = atomicAdd(&s_count, 1);
-            keys[at] = make_key(dist, __ldg(a.ids + slot));
-          }
+          surv = true;
+          sslot = slot;
+          sbase = base_d;
+          sfr = fr;
         }
       }
-      __syncthreads();
-      const int cnt = s_count;
-      if (cnt > a.cap - kScanTile) {
-        for (int i = cnt + tid; i < a.cap; i += blockDim.x) keys[i] = kEmptyKey;
-        __syncthreads();
-        block_bitonic_sort(keys, a.cap);
-        if (tid == 0) {
-          s_count = a.R;
-          s_tau = from_ordered_bits((uint32_t)(keys[a.R - 1] >> 32));
+      // phase 2: the warp's admitted vectors of this round, one at a time, all lanes.
+      unsigned mask = __ballot_sync(0xffffffffu, surv);
+      while (mask) {
+        const int src = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const int slot = __shfl_sync(0xffffffffu, sslot, src);
+        const float base_d = __shfl_sync(0xffffffffu, sbase, src);
+        const float fr = __shfl_sync(0xffffffffu, sfr, src);
+        const float eip = warp_exact_ip<W, kLut>(a.codes, slot, lut, qsT, lane);
+        const float dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
+        if (lane == 0 && dist <= tau) {
+          const int at = atomicAdd(&s_count, 1);
+          keys[at] = make_key(dist, __ldg(a.ids + slot));
         }
       }
-      __syncthreads();
     }
+    __syncthreads();
+    const int cnt = s_count;
+    if (cnt > a.cap - kScanTile) {
+      const unsigned long long kth = block_keep_smallest(keys, cnt, a.R, keys2, s_hist, s_misc, &s_kmax, &s_cnt2);
+      unsigned long long* t = keys;
+      keys = keys2;
+      keys2 = t;
+      if (tid == 0) {
+        s_count = a.R;
+        s_tau = from_ordered_bits((uint32_t)(kth >> 32));
+      }
+    }
+    __syncthreads();
   }
-  const int cnt = s_count;
-  for (int i = cnt + tid; i < a.cap; i += blockDim.x) keys[i] = kEmptyKey;
+  // Final top-R: cut to R keys if needed, then sort only the next power of two >= the count.
+  int cnt = s_count;
+  if (cnt > a.R) {
+    block_keep_smallest(keys, cnt, a.R, keys2, s_hist, s_misc, &s_kmax, &s_cnt2);
+    keys = keys2;
+    cnt = a.R;
+  }
+  int r2 = 2;
+  while (r2 < cnt) r2 <<= 1;
+  for (int i = cnt + tid; i < r2; i += kScanThreads) keys[i] = kEmptyKey;
   __syncthreads();
-  block_bitonic_sort(keys, a.cap);
+  block_bitonic_sort(keys, r2);
   unsigned long long* out = a.out_keys + ((size_t)q * a.slices + slice) * a.R;
-  for (int i = tid; i < a.R; i += blockDim.x) out[i] = keys[i];
+  for (int i = tid; i < a.R; i += kScanThreads) out[i] = i < cnt ? keys[i] : kEmptyKey;
   if (a.stats) {
+    unsigned long long s0 = n_scan, s1 = n_admit;
     for (int off = 16; off; off >>= 1) {
-      n_scan += __shfl_xor_sync(0xffffffffu, n_scan, off);
-      n_admit += __shfl_xor_sync(0xffffffffu, n_admit, off);
+      s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
     }
-    if ((tid & 31) == 0) {
-      atomicAdd(a.stats + 0, n_scan);
-      atomicAdd(a.stats + 1, n_admit);
+    if (lane == 0) {
+      atomicAdd(a.stats + 0, s0);
+      atomicAdd(a.stats + 1, s1);
     }
   }
 }
@@ -429,13 +763,15 @@ __global__ void __launch_bounds__(kScanTile) scan_kernel(const ScanArgs a)
 template <int W>
 static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
 {
-  const size_t smem = (size_t)a.cap * 8 + (size_t)W * 32 * 4 + (size_t)4 * W * 4 + (size_t)a.nprobe * 8;
+  constexpr int NB = 4 * W;
+  const size_t smem = (size_t)a.cap * 8 * 2 + (size_t)(2 * a.nprobe + 1) * 4 + (size_t)2 * a.nprobe * 4 +
+                      (size_t)4 * W * 4 + (NB <= kLutMaxBytes ? (size_t)NB * 256 * 4 : 0) + (size_t)8 * NB * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "scan: shared memory budget exceeded (cap/nprobe too large)");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t blocks = a.nq * a.slices;
   RBQ_CHECK(blocks <= 0x7fffffff, RBQ_ERR_INVALID, "scan: grid too large");
-  scan_kernel<W><<<(unsigned)blocks, kScanTile, smem, s>>>(a);
+  scan_kernel<W><<<(unsigned)blocks, kScanThreads, smem, s>>>(a);
   RBQ_LAUNCHED();
 }
 
@@ -443,7 +779,10 @@ void launch_scan(const ScanArgs& a, cudaStream_t s)
 {
   if (a.nq <= 0) return;
   RBQ_CHECK(a.cap >= a.R + kScanTile && (a.cap & (a.cap - 1)) == 0, RBQ_ERR_INVALID,
-            "scan: cap must be a power of two >= R + 256");
+            "scan: cap must be a power of two >= R + tile");
+  RBQ_CHECK(a.Dp == 32 * a.W, RBQ_ERR_INVALID, "scan: padded dim mismatch");
+  RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
+            "scan: more than 2^31 vectors on one shard");
   switch (a.W) {
     case 1: launch_scan_w<1>(a, s); break;
     case 2: launch_scan_w<2>(a, s); break;

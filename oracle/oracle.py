@@ -83,6 +83,22 @@ def pad_dim(d: int) -> int:
     return (d + 31) // 32 * 32
 
 
+# Scan schedule constants shared with the CUDA library: vectors per tile (256 threads x 2
+# vectors) and the candidate-buffer size rule cap = max(pow2(cand_cap or 1024), pow2(R + tile)).
+SCAN_TILE = 512
+
+
+def _pow2(v: int) -> int:
+    p = 1
+    while p < v:
+        p <<= 1
+    return p
+
+
+def default_cap(R: int, cand_cap: int = 0, tile: int = SCAN_TILE) -> int:
+    return max(_pow2(cand_cap if cand_cap and cand_cap > 0 else 1024), _pow2(R + tile))
+
+
 def threads() -> int:
     return lib().orc_threads()
 
@@ -202,11 +218,13 @@ def exact_ip(q, code) -> float:
     return float(lib().orc_exact_ip(_c(q, np.float32), code, code.size))
 
 
-def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=256, cap=1024, prune=1,
+def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
          slices=1, shard_rank=0, shard_count=1, with_stats=False):
     Qr = _c(Qr, np.float32)
     nq = Qr.shape[0]
     nprobe = probes.shape[1]
+    if cap is None:
+        cap = default_cap(R, 0, tile)
     out_ids = np.empty((nq, R), np.int64)
     out_d = np.empty((nq, R), np.float32)
     stats = np.zeros(2, np.int64)
@@ -250,7 +268,7 @@ def assign(X, C) -> np.ndarray:
     return labels
 
 
-def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=256, cap=1024, prune=1, slices=1,
+def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
            shard_rank=0, shard_count=1, with_stats=False):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 

@@ -440,26 +440,35 @@ void orc_estimate(const float* f3, float g, int32_t acc, float delta, float k1, 
   est_low[1] = est - f3[2] * sqrtf(g);
 }
 
-// Exact 1-bit inner product <bits, q>: per byte (8 dims, MSB first) a float sum from 0,
-// per word ((b0 + b1) + b2) + b3, words summed in order from 0.
+// Sum of q over the set bits of code byte j (byte j of the MSB-first bit stream = dims
+// 8j .. 8j+7, bit 7 first), a float sum starting from 0.
+static inline float byte_sum(const float* q, const uint32_t* code, int j)
+{
+  const uint32_t byte = (code[j >> 2] >> (24 - 8 * (j & 3))) & 0xFFu;
+  float s = 0.0f;
+  for (int jj = 0; jj < 8; ++jj)
+    if ((byte >> (7 - jj)) & 1u) s = s + q[8 * j + jj];
+  return s;
+}
+
+// Exact 1-bit inner product <bits, q> in the order of the CUDA scan's warp: lane l (0..31)
+// adds byte_sum(j) for j = l, l+32, ... (< 4W) in order from 0; the 32 lane values are
+// combined by an xor butterfly (16, 8, 4, 2, 1: v[l] = v[l] + v[l ^ off]); lane 0's value.
 float orc_exact_ip(const float* q, const uint32_t* code, int W)
 {
-  float acc = 0.0f;
-  for (int w = 0; w < W; ++w) {
-    uint32_t c = code[w];
-    float part[4];
-    for (int i = 0; i < 4; ++i) {
-      float s = 0.0f;
-      for (int j = 0; j < 8; ++j) {
-        int bitpos = 31 - (8 * i + j);
-        if ((c >> bitpos) & 1u) s = s + q[32 * w + 8 * i + j];
-      }
-      part[i] = s;
-    }
-    float pw = ((part[0] + part[1]) + part[2]) + part[3];
-    acc = acc + pw;
+  const int NB = 4 * W;
+  float v[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int j = l; j < NB; j += 32) s = s + byte_sum(q, code, j);
+    v[l] = s;
   }
-  return acc;
+  for (int off = 16; off >= 1; off >>= 1) {
+    float nv[32];
+    for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ off];
+    for (int l = 0; l < 32; ++l) v[l] = nv[l];
+  }
+  return v[0];
 }
 
 struct ScanIndex {
@@ -479,35 +488,37 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
   keys.clear();
   float tau = INFINITY;
   int64_t n_scanned = 0, n_admit = 0;
-  for (int p = 0; p < np; ++p) {
-    const int l = probe_l[p];
-    const float g = probe_g[p];
-    const float sqrt_g = sqrtf(g);
-    const int64_t base = ix.list_off[l];
-    const int64_t n = ix.list_off[l + 1] - base;
-    for (int64_t t0 = 0; t0 < n; t0 += tile) {
-      const int64_t t1 = std::min<int64_t>(n, t0 + tile);
-      for (int64_t v = t0; v < t1; ++v) {
-        const int64_t s = base + v;
-        const uint32_t* code = ix.codes + (size_t)s * W;
-        int32_t acc = orc_popcount_ip(pl, code, W);
-        float ip = (float)acc * delta;
-        float base_d = ix.fadd[s] + g;
-        float est = base_d + ix.frescale[s] * (ip + k1);
-        float low = est - ix.ferr[s] * sqrt_g;
-        ++n_scanned;
-        if (!prune || low < tau) {
-          ++n_admit;
-          float eip = orc_exact_ip(qr, code, W);
-          float dist = base_d + ix.frescale[s] * (eip + k1);
-          if (dist <= tau) keys.push_back(make_key(dist, ix.ids[s]));
-        }
+  // The slice's lists form one flat sequence of vectors (probe order, slot order inside a
+  // list); tiles of `tile` vectors run across list boundaries.
+  std::vector<int64_t> pre(np + 1, 0);
+  for (int p = 0; p < np; ++p) pre[p + 1] = pre[p] + (ix.list_off[probe_l[p] + 1] - ix.list_off[probe_l[p]]);
+  const int64_t total = pre[np];
+  int cur = 0;
+  for (int64_t t0 = 0; t0 < total; t0 += tile) {
+    const int64_t t1 = std::min<int64_t>(total, t0 + tile);
+    for (int64_t f = t0; f < t1; ++f) {
+      while (pre[cur + 1] <= f) ++cur;
+      const float g = probe_g[cur];
+      const float sqrt_g = sqrtf(g);
+      const int64_t s = ix.list_off[probe_l[cur]] + (f - pre[cur]);
+      const uint32_t* code = ix.codes + (size_t)s * W;
+      int32_t acc = orc_popcount_ip(pl, code, W);
+      float ip = (float)acc * delta;
+      float base_d = ix.fadd[s] + g;
+      float est = base_d + ix.frescale[s] * (ip + k1);
+      float low = est - ix.ferr[s] * sqrt_g;
+      ++n_scanned;
+      if (!prune || low < tau) {
+        ++n_admit;
+        float eip = orc_exact_ip(qr, code, W);
+        float dist = base_d + ix.frescale[s] * (eip + k1);
+        if (dist <= tau) keys.push_back(make_key(dist, ix.ids[s]));
       }
-      if ((int)keys.size() > cap - tile) {
-        std::sort(keys.begin(), keys.end());
-        keys.resize(R);
-        tau = from_ordered_bits((uint32_t)(keys[R - 1] >> 32));
-      }
+    }
+    if ((int)keys.size() > cap - tile) {
+      std::sort(keys.begin(), keys.end());
+      keys.resize(R);
+      tau = from_ordered_bits((uint32_t)(keys[R - 1] >> 32));
     }
   }
   std::sort(keys.begin(), keys.end());

@@ -108,19 +108,28 @@ def popcount_ip(planes, code):
     return acc
 
 
+def byte_sum(q, code, j):
+    """Sum of q over the set bits of byte j of the MSB-first bit stream (dims 8j..8j+7)."""
+    byte = (int(code[j >> 2]) >> (24 - 8 * (j & 3))) & 0xFF
+    s = F(0)
+    for jj in range(8):
+        if (byte >> (7 - jj)) & 1:
+            s = s + F(q[8 * j + jj])
+    return s
+
+
 def exact_ip(q, code):
-    acc = F(0)
-    for w in range(len(code)):
-        c = int(code[w])
-        parts = []
-        for i in range(4):
-            s = F(0)
-            for j in range(8):
-                if (c >> (31 - (8 * i + j))) & 1:
-                    s = s + F(q[32 * w + 8 * i + j])
-            parts.append(s)
-        acc = acc + (((parts[0] + parts[1]) + parts[2]) + parts[3])
-    return F(acc)
+    """32 lane sums (lane l: bytes l, l+32, ... in order), then an xor butterfly 16..1."""
+    nb = 4 * len(code)
+    v = []
+    for lane in range(32):
+        s = F(0)
+        for j in range(lane, nb, 32):
+            s = s + byte_sum(q, code, j)
+        v.append(s)
+    for off in (16, 8, 4, 2, 1):
+        v = [v[lane] + v[lane ^ off] for lane in range(32)]
+    return F(v[0])
 
 
 def estimate(f3, g, acc, delta, k1):

@@ -178,8 +178,8 @@ def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
          slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
     p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
     pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
-    cap_o = max(1 << ((cap if cap > 0 else 1024) - 1).bit_length(), 1 << (R + 256 - 1).bit_length())
-    oi, od, ost = oracle.scan(oix, Qr, pl2, d2, k2, p2, g2, R, 256, cap_o, prune, slices, with_stats=True)
+    cap_o = oracle.default_cap(R, cap)
+    oi, od, ost = oracle.scan(oix, Qr, pl2, d2, k2, p2, g2, R, oracle.SCAN_TILE, cap_o, prune, slices, with_stats=True)
     return ids.cpu().numpy(), dist.cpu().numpy(), stats.cpu().numpy(), oi, od, ost
 
 
