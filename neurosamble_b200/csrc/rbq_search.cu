@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "rbq_internal.cuh"
 
 namespace rbq {
@@ -101,42 +103,68 @@ void launch_coarse_scores(const float* A, int64_t nq, const float* C, const floa
 }
 
 // ---------------------------------------------------------------------------------------
-// Per row of S [nq, K]: the m smallest (score, column) keys, ascending.  Chunks of the row
-// are appended behind the running top-m and the buffer is re-sorted.
+// Per row of S [nq, K]: the m smallest (score, column) keys.  The row is taken in chunks of up
+// to kTopmChunk keys appended behind the running m survivors; a radix select keeps the m
+// smallest of each buffer (block_keep_smallest).  Order of the m output columns is
+// unspecified; the exact refine below ranks them.
 // ---------------------------------------------------------------------------------------
-constexpr int kTopmBuf = 2048;
+constexpr int kTopmChunk = 4096;
 
-__global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict__ S, int K, int m,
+__device__ unsigned long long block_keep_smallest(const unsigned long long* src, int n, int R,
+                                                  unsigned long long* dst, unsigned* hist, int* misc,
+                                                  unsigned long long* kmax, int* cnt);
+
+__global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict__ S, int K, int m, int buf,
                                                         int32_t* __restrict__ cand)
 {
-  __shared__ unsigned long long keys[kTopmBuf];
+  extern __shared__ unsigned long long tk[];  // [2 * buf]
+  __shared__ unsigned s_hist[256];
+  __shared__ int s_misc[3], s_cnt;
+  __shared__ unsigned long long s_kmax;
+  unsigned long long* cur = tk;
+  unsigned long long* nxt = tk + buf;
   const int64_t q = blockIdx.x;
   const float* row = S + q * K;
-  int filled = 0;  // valid running entries at the front
+  int filled = 0;  // survivors at the front of `cur`
   for (int c0 = 0; c0 < K;) {
-    const int take = min(kTopmBuf - filled, K - c0);
-    for (int i = threadIdx.x; i < kTopmBuf - filled; i += blockDim.x)
-      keys[filled + i] = (i < take) ? make_key(row[c0 + i], (uint32_t)(c0 + i)) : kEmptyKey;
+    const int take = min(buf - filled, K - c0);
+    for (int i = threadIdx.x; i < take; i += blockDim.x)
+      cur[filled + i] = make_key(__ldg(row + c0 + i), (uint32_t)(c0 + i));
     __syncthreads();
-    block_bitonic_sort(keys, kTopmBuf);
+    const int n = filled + take;
     c0 += take;
-    filled = min(m, filled + take);
+    if (n > m) {
+      block_keep_smallest(cur, n, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+      unsigned long long* t = cur;
+      cur = nxt;
+      nxt = t;
+      filled = m;
+    } else {
+      filled = n;
+    }
+    __syncthreads();
   }
   for (int i = threadIdx.x; i < m; i += blockDim.x)
-    cand[q * m + i] = (keys[i] == kEmptyKey) ? -1 : (int32_t)(keys[i] & 0xFFFFFFFFu);
+    cand[q * m + i] = i < filled ? (int32_t)(cur[i] & 0xFFFFFFFFu) : -1;
 }
 
 void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s)
 {
   if (nq <= 0) return;
-  RBQ_CHECK(m >= 1 && m <= kTopmBuf / 2, RBQ_ERR_INVALID, "coarse: shortlist size out of range");
-  topm_rows_kernel<<<(unsigned)nq, 256, 0, s>>>(S, K, m, cand);
+  RBQ_CHECK(m >= 1 && m <= kTopmChunk / 2, RBQ_ERR_INVALID, "coarse: shortlist size out of range");
+  const int buf = std::min(kTopmChunk, std::max(2 * m, K));
+  const size_t smem = (size_t)buf * 2 * 8;
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  topm_rows_kernel<<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
   RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------
-// Exact refine of the shortlist: g = float(sum_j double(a_j - c_j)^2), j ascending; keep the
-// p smallest (g, list id).  Same distance as the oracle's orc_coarse / orc_assign.
+// Exact refine of the shortlist: g = |a - c|^2 with lane l of a warp summing double(a_j - c_j)^2
+// over j = l, l+32, ... and an xor butterfly (16..1) of double adds, rounded to float (the
+// oracle's orc_coarse / orc_assign distance); keep the p smallest (g, list id), ascending.
+// One CTA per query, one warp per candidate.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restrict__ A, const float* __restrict__ C,
                                                           int d, const int32_t* __restrict__ cand, int m, int p,
@@ -147,23 +175,22 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);
   float* a = reinterpret_cast<float*>(keys + mp2);
   const int64_t q = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
+  for (int i = threadIdx.x; i < mp2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
-  for (int i = threadIdx.x; i < mp2; i += blockDim.x) {
-    unsigned long long key = kEmptyKey;
-    if (i < m) {
-      const int c = cand[q * m + i];
-      if (c >= 0) {
-        const float* cr = C + (size_t)c * d;
-        double s = 0.0;
-        for (int j = 0; j < d; ++j) {
-          const float df = a[j] - cr[j];
-          s += (double)df * (double)df;
-        }
-        key = make_key((float)s, (uint32_t)c);
-      }
+  for (int i = warp; i < m; i += nwarps) {
+    const int c = cand[q * m + i];
+    if (c < 0) continue;
+    const float* cr = C + (size_t)c * d;
+    double s = 0.0;
+    for (int j = lane; j < d; j += 32) {
+      const float df = __fsub_rn(__ldg(cr + j), a[j]);
+      s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
     }
-    keys[i] = key;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    if (lane == 0) keys[i] = make_key((float)s, (uint32_t)c);
   }
   __syncthreads();
   block_bitonic_sort(keys, mp2);

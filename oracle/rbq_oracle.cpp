@@ -385,16 +385,30 @@ void orc_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* pla
   }
 }
 
-// Exact coarse distance g = float(sum_j double(q_j - c_j)^2), j ascending, in rotated space.
-static inline float coarse_dist(const float* q, const float* c, int Dp)
+// Squared L2 in the order of a CUDA warp: lane l (0..31) sums double(x_d - q_d)^2 over
+// d = l, l+32, ... ascending; the 32 lane sums are combined by an xor butterfly (offsets
+// 16, 8, 4, 2, 1: v[l] = v[l] + v[l ^ off]); lane 0's value is rounded to float.
+static inline float l2_lanes(const float* x, const float* q, int D)
 {
-  double s = 0.0;
-  for (int j = 0; j < Dp; ++j) {
-    float d = q[j] - c[j];
-    s += (double)d * (double)d;
+  double v[32];
+  for (int l = 0; l < 32; ++l) {
+    double s = 0.0;
+    for (int d = l; d < D; d += 32) {
+      float df = x[d] - q[d];
+      s += (double)df * (double)df;
+    }
+    v[l] = s;
   }
-  return (float)s;
+  for (int off = 16; off >= 1; off >>= 1) {
+    double nv[32];
+    for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ off];
+    for (int l = 0; l < 32; ++l) v[l] = nv[l];
+  }
+  return (float)v[0];
 }
+
+// Exact coarse distance g = |q - c|^2 (rotated space) in the warp order of l2_lanes.
+static inline float coarse_dist(const float* q, const float* c, int Dp) { return l2_lanes(c, q, Dp); }
 
 // Coarse quantiser (a7): top-nprobe lists per query by (g, list id) ascending.
 void orc_coarse(const float* Qr, int64_t nq, const float* Cr, int K, int Dp, int nprobe,
@@ -596,24 +610,7 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
 // (0..31) sums double(x_d - q_d)^2 over d = l, l+32, ... ascending; the 32 lane sums are
 // combined by a butterfly (offsets 16, 8, 4, 2, 1: v[l] = v[l] + v[l ^ off]); lane 0's value
 // is rounded to float.
-float orc_l2_exact(const float* x, const float* q, int D)
-{
-  double v[32];
-  for (int l = 0; l < 32; ++l) {
-    double s = 0.0;
-    for (int d = l; d < D; d += 32) {
-      float df = x[d] - q[d];
-      s += (double)df * (double)df;
-    }
-    v[l] = s;
-  }
-  for (int off = 16; off >= 1; off >>= 1) {
-    double nv[32];
-    for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ off];
-    for (int l = 0; l < 32; ++l) v[l] = nv[l];
-  }
-  return (float)v[0];
-}
+float orc_l2_exact(const float* x, const float* q, int D) { return l2_lanes(x, q, D); }
 
 // Exact rerank (a13): candidates [nq, R] (-1 = empty) -> top-k by (exact L2^2, id).
 void orc_rerank(const float* X, int D, const float* Q, int64_t nq, const int64_t* cand, int R, int k,
