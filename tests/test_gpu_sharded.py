@@ -1,0 +1,72 @@
+"""List-sharded search on 2 GPUs (NCCL): the merged result of ShardedIndexIVFRaBitQ equals the
+oracle's sharded search merged by (distance, id), bit for bit.  Skipped with fewer than 2 GPUs."""
+import os
+import pickle
+import socket
+import tempfile
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _ngpu():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, outdir):
+    import torch
+    import torch.distributed as dist
+
+    from conftest import mixture
+    from oracle import oracle as O
+    from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device(f"cuda:{rank}"))
+    X, Q = mixture(20000, 128, 40, 0.3, 200, seed=31)
+    C, _ = O.kmeans(X[::4], 64, iters=4)
+    lab = O.assign(X, C)
+    idx = ShardedIndexIVFRaBitQ(128, 64, seed=7, device=rank)
+    idx.local.set_centroids(C)
+    idx.add(X, labels=lab)
+    idx.nprobe, idx.k_rerank, idx.probe_split = 12, 40, 1
+    d, i = idx.search(Q, 10)
+    if rank == 0:
+        with open(os.path.join(outdir, "res.pkl"), "wb") as f:
+            pickle.dump((d, i, C, lab, idx.local.rotation(), idx.local.query_scale, X, Q), f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_two_gpu_sharded_search_matches_oracle(oracle):
+    import torch.multiprocessing as mp
+    with tempfile.TemporaryDirectory() as td:
+        mp.spawn(_rank_main, args=(2, _port(), td), nprocs=2, join=True)
+        d, i, C, lab, P, t4, X, Q = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
+    oix = oracle.build(X, C, lab, P, t4)
+    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1) for r in range(2)]
+    keys = []
+    for q in range(Q.shape[0]):
+        kk = sorted((float(parts[r][0][q, j]), int(parts[r][1][q, j])) for r in range(2) for j in range(10)
+                    if parts[r][1][q, j] >= 0)[:10]
+        keys.append(kk)
+    want_i = np.array([[x[1] for x in kk] for kk in keys])
+    want_d = np.array([[x[0] for x in kk] for kk in keys], np.float32)
+    assert np.array_equal(i, want_i)
+    assert np.array_equal(d.view(np.uint32), want_d.view(np.uint32))
