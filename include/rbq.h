@@ -141,6 +141,16 @@ int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, 
  * computeQueryFactorsWarpKernel (gpu_index/ivf_gpu.cu:1451-1490). */
 int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev,
                    float* delta_dev, float* k1_dev, void* stream);
+/* Approximate coarse scores S [nq, K] = |c_rot|^2 - 2 <q_rot, c_rot> (the shortlist ranking).
+ * tensor_cores = 1: tcgen05 kind::tf32 MMA (the search path); 0: fp32 CUDA-core reference.
+ * Replaces the -2 Q C^T GEMM + add_norms of PrepareClusterSearchInputs
+ * (gpu_index/ivf_gpu.cu:1531-1596). */
+int rbq_coarse_scores(rbq_index_t* index, const float* Qr_dev, int64_t nq, float* S_dev, int32_t tensor_cores,
+                      void* stream);
+/* Synchronises the index's device and reports device-side failures recorded since the last
+ * call (a tensor-core pipeline wait that timed out): RBQ_ERR_CUDA with a message, else RBQ_OK.
+ * No reference counterpart (the reference has no bounded device waits). */
+int rbq_check_errors(rbq_index_t* index);
 /* Coarse quantiser: top-nprobe lists per rotated query, ascending exact distance g.
  * Replaces PrepareClusterSearchInputs steps 1-4 (gpu_index/ivf_gpu.cu:1513-1628). */
 int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t nprobe, int32_t margin,

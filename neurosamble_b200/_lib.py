@@ -62,6 +62,8 @@ SIGNATURES = {
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],
     "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _P],
+    "rbq_coarse_scores": [_P, _P, _I64, _P, _I32, _P],
+    "rbq_check_errors": [_P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
     "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
     "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],

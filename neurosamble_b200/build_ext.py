@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "librbq.so")
 
-SOURCES = ["rbq_host_math.cpp", "rbq_build.cu", "rbq_search.cu", "rbq_capi.cu"]
+SOURCES = ["rbq_host_math.cpp", "rbq_build.cu", "rbq_search.cu", "rbq_coarse_tc.cu", "rbq_capi.cu"]
 HEADERS = ["rbq_internal.cuh", os.path.join("..", "..", "include", "rbq.h")]
 
 # -fmad=false: no FMA contraction anywhere, so every expression is evaluated as written and

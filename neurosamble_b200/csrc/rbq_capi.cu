@@ -401,7 +401,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
     launch_rotate(Qc, cn, ix.D, ix.Dp, ix.P, Qr, s);
-    launch_coarse_scores(Qr, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, s);
+    launch_coarse_scores_tc(Qr, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
     launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
     launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
     launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
@@ -499,6 +499,7 @@ void free_index_memory(Index& ix)
   dev_free(ix.labels_r);
   dev_free(ix.ids_r);
   dev_free(ix.id2row);
+  dev_free(ix.dev_err);
   dev_free(ix.list_off);
   dev_free(ix.ids);
   dev_free(ix.codes);
@@ -594,6 +595,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
       make_rotation(ix.Dp, ix.seed, ix.P_host.data());
       ix.t4 = query_scale(ix.Dp, ix.seed, 3);
       ix.P = dev_alloc<float>(ix.P_host.size());
+      ix.dev_err = dev_alloc<int>(1);
+      RBQ_CUDA(cudaMemset(ix.dev_err, 0, sizeof(int)));
       RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
       ix.off_host.assign(ix.K + 1, 0);
       ix.list_off = dev_alloc<int64_t>(ix.K + 1);
@@ -700,7 +703,13 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
     run_search(ix, *params, q, nq, d, i, s, nullptr);
     RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * params->k * 4, cudaMemcpyDeviceToHost, s));
     RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * params->k * 8, cudaMemcpyDeviceToHost, s));
+    int code = 0;
+    RBQ_CUDA(cudaMemcpyAsync(&code, ix.dev_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RBQ_CUDA(cudaStreamSynchronize(s));
+    if (code) {
+      RBQ_CUDA(cudaMemset(ix.dev_err, 0, sizeof(int)));
+      throw Error{RBQ_ERR_CUDA, "a tensor-core pipeline wait timed out on the device (code " + std::to_string(code) + ")"};
+    }
   });
 }
 
@@ -799,6 +808,8 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.P_host.resize((size_t)Dp * Dp);
       f.read(ix.P_host.data(), ix.P_host.size() * 4);
       ix.P = dev_alloc<float>(ix.P_host.size());
+      ix.dev_err = dev_alloc<int>(1);
+      RBQ_CUDA(cudaMemset(ix.dev_err, 0, sizeof(int)));
       RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
       ix.off_host.assign(K + 1, 0);
       ix.list_off = dev_alloc<int64_t>(K + 1);
@@ -928,6 +939,39 @@ int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t
   });
 }
 
+int rbq_coarse_scores(rbq_index_t* index, const float* Qr_dev, int64_t nq, float* S_dev, int32_t tensor_cores,
+                      void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && (nq == 0 || (Qr_dev && S_dev)), RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "index is not trained");
+    if (nq == 0) return;
+    DeviceGuard dg(ix.device);
+    if (tensor_cores)
+      launch_coarse_scores_tc(Qr_dev, nq, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S_dev, ix.dev_err, as_stream(stream));
+    else
+      launch_coarse_scores(Qr_dev, nq, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S_dev, as_stream(stream));
+  });
+}
+
+int rbq_check_errors(rbq_index_t* index)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    RBQ_CUDA(cudaDeviceSynchronize());
+    int code = 0;
+    RBQ_CUDA(cudaMemcpy(&code, ix.dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) {
+      RBQ_CUDA(cudaMemset(ix.dev_err, 0, sizeof(int)));
+      throw Error{RBQ_ERR_CUDA, "a tensor-core pipeline wait timed out on the device (code " + std::to_string(code) +
+                                    "); results of the affected search are invalid"};
+    }
+  });
+}
+
 int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t nprobe, int32_t margin,
                int32_t* probes_dev, float* g_dev, void* stream)
 {
@@ -946,7 +990,7 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
     int32_t* cand = sc.get<int32_t>((size_t)chunk * m);
     for (int64_t a = 0; a < nq; a += chunk) {
       const int64_t cn = std::min(chunk, nq - a);
-      launch_coarse_scores(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, s);
+      launch_coarse_scores_tc(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
       launch_topm_rows(S, cn, ix.K, m, cand, s);
       launch_refine_topp(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.Dp, cand, m, nprobe, probes_dev + a * nprobe,
                          g_dev + a * nprobe, s);

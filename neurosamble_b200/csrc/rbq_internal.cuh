@@ -117,6 +117,7 @@ struct Index {
   uint32_t* ids_r = nullptr;     // [n_rows] global ids
   int64_t cap_ids = 0;
   uint32_t* id2row = nullptr;    // [n_total] row of a global id, 0xFFFFFFFF if not on this shard
+  int* dev_err = nullptr;        // [1] device-side error code (tensor-core waits that timed out)
 
   // Slot order (rebuilt after every add): list l owns slots [list_off[l], list_off[l+1]).
   int64_t* list_off = nullptr;   // [K+1]
@@ -146,6 +147,10 @@ void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, cons
 // Row squared norms (float, any order) of A[n, d].
 void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t s);
 // Approximate scores S[q, c] = |c|^2 - 2 <a_q, c> for ranking (fp32).
+// Same scores on the tensor cores (tcgen05 kind::tf32); err[0] is set if a wait timed out.
+bool coarse_tc_supported(int dp);
+void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const float* cn2, int K, int dp, float* S,
+                             int* err, cudaStream_t s);
 void launch_coarse_scores(const float* A, int64_t nq, const float* C, const float* c_n2, int K, int d,
                           float* S, cudaStream_t s);
 // Per row of S [nq, K]: top-m (score, id) keys ascending -> cand [nq, m].

@@ -344,3 +344,30 @@ def test_config1_parity_and_recall(oracle):
     assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
     _, gt = oracle.knn_exact(X, Q, 10)
     assert oracle.recall(i, gt) == oracle.recall(i2, gt)
+
+
+@pytest.mark.parametrize("d,K,nq", [(256, 1024, 300), (128, 300, 129), (32, 64, 1), (768, 256, 200), (100, 40, 7)])
+def test_tensor_core_scores_match_fp32(oracle, d, K, nq):
+    """tcgen05 kind::tf32 scores vs the fp32 CUDA-core scores; tf32 keeps 10 mantissa bits, so
+    |diff| <= 2e-3 * (|c|^2 + 2 |q| |c|) is asserted, and no device wait may time out."""
+    torch = _torch()
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(max(4 * K, 2000), d, 8, 0.3, nq, seed=K)
+    C, _ = oracle.kmeans(X, K, iters=2)
+    idx = IndexIVFRaBitQ(d, K, seed=3)
+    idx.set_centroids(C)
+    dp = idx.info().padded_dim
+    qr = torch.empty((nq, dp), dtype=torch.float32, device="cuda")
+    q = dev(Q)
+    call("rbq_rotate", idx.handle, ptr(q), nq, ptr(qr), stream())
+    s_tc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    s_fp = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    call("rbq_coarse_scores", idx.handle, ptr(qr), nq, ptr(s_tc), 1, stream())
+    call("rbq_coarse_scores", idx.handle, ptr(qr), nq, ptr(s_fp), 0, stream())
+    call("rbq_check_errors", idx.handle)
+    a, b = s_tc.cpu().numpy(), s_fp.cpu().numpy()
+    _, Cr = idx.centroids()
+    bound = 2e-3 * ((Cr * Cr).sum(1)[None, :] + 2.0 * np.linalg.norm(qr.cpu().numpy(), axis=1)[:, None]
+                    * np.linalg.norm(Cr, axis=1)[None, :]) + 1e-6
+    assert np.all(np.isfinite(a))
+    assert np.all(np.abs(a - b) <= bound), float(np.max(np.abs(a - b) - bound))
