@@ -292,13 +292,13 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* 
 // (query, probe slice).  The slice's lists form one flat sequence of vectors (probe order,
 // slot order inside a list) walked in tiles of kScanTile = 512 vectors that run across list
 // boundaries; thread t takes vectors t and t + 256 of each tile.
-//   phase 1 (per thread, planes in registers)
+//   phase 1 (per thread; query planes broadcast from shared memory, carry-save popcounts)
 //            acc = sum_w [sum_{b<3} popc(P_b & c) << b  -  popc(P_3 & c) << 3]   (exact int)
 //            est = (f_add + g) + f_rescale * (acc * delta + k1);  low = est - f_err * sqrt(g)
 //            admit if !prune || low < tau
 //   phase 2 (per warp)  right after each round of phase 1, the warp's admitted vectors are
-//            taken one at a time by all 32 lanes (warp_exact_ip: per-byte sums from a
-//            per-query table, lane sums, xor butterfly);
+//            taken one at a time by all 32 lanes (warp_exact_ip: per-byte sums, lane sums,
+//            xor butterfly);
 //            dist = (f_add + g) + f_rescale * (exact_ip + k1); keep (dist, id) if dist <= tau.
 // tau (the R-th best kept distance) only changes between tiles: when the buffer holds more
 // than cap - kScanTile keys it is sorted and cut to R.  The schedule depends on the data
@@ -327,18 +327,14 @@ __device__ __forceinline__ void load_code(const uint32_t* __restrict__ codes, in
   }
 }
 
-// Code bytes per vector up to which the scan keeps a per-query byte table in shared memory.
-constexpr int kLutMaxBytes = 32;
-
 // <bits of the vector at `slot`, q>, computed by the whole warp; every lane returns the value.
 // Lane l adds bsum(j) for the code bytes j = l, l + 32, ... (bsum(j) = sum of q over the set
-// bits of byte j of the MSB-first bit stream, dims 8j..8j+7, from 0), then an xor butterfly
-// (16, 8, 4, 2, 1) combines the lanes.  With a table, bsum(j) = lut[j * 256 + byte]; without,
-// it is summed from qsT (the query transposed by byte: qsT[jj * NB + j] = q[8 j + jj]).
-template <int W, bool kLut>
+// bits of byte j of the MSB-first bit stream, dims 8j..8j+7, bit 7 first, from 0), then an xor
+// butterfly (16, 8, 4, 2, 1) combines the lanes.  qsT is the query transposed by byte
+// (qsT[jj * NB + j] = q[8 j + jj]), so the 32 lanes read 32 consecutive words.
+template <int W>
 __device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ codes, int64_t slot,
-                                               const float* __restrict__ lut, const float* __restrict__ qsT,
-                                               int lane)
+                                               const float* __restrict__ qsT, int lane)
 {
   constexpr int NB = 4 * W;
   constexpr int M = (NB + 31) / 32;
@@ -349,16 +345,11 @@ __device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ code
     const int j = lane + 32 * m;
     if (j < NB) {
       const uint32_t u8 = __ldg(cb + (j ^ 3));  // byte j of the MSB-first bit stream
-      float b;
-      if constexpr (kLut) {
-        b = lut[j * 256 + u8];
-      } else {
-        b = 0.0f;
+      float b = 0.0f;
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const float q = qsT[jj * NB + j];
-          b = ((u8 >> (7 - jj)) & 1u) ? __fadd_rn(b, q) : b;
-        }
+      for (int jj = 0; jj < 8; ++jj) {
+        const float q = qsT[jj * NB + j];
+        b = ((u8 >> (7 - jj)) & 1u) ? __fadd_rn(b, q) : b;
       }
       v = __fadd_rn(v, b);
     }
@@ -569,17 +560,18 @@ __device__ unsigned long long block_keep_smallest(const unsigned long long* src,
   return *kmax;
 }
 
-// Resident CTAs per SM the scan is compiled for (register budget 65536 / (256 * this)).
-#ifndef RBQ_SCAN_MIN_BLOCKS
-#define RBQ_SCAN_MIN_BLOCKS 4
-#endif
+// Resident CTAs per SM the scan is compiled for: occupancy hides the L2 latency of the code
+// loads, so vectors up to 256 dims get 6 CTAs (40 registers, no spill); wider ones 4.
+template <int W>
+constexpr int scan_min_blocks()
+{
+  return W <= 8 ? 6 : 4;
+}
 
 template <int W>
-__global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel(const ScanArgs a)
+__global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kernel(const ScanArgs a)
 {
-  constexpr bool kPlanesInRegs = (W <= 8);
   constexpr int NB = 4 * W;
-  constexpr bool kLut = (NB <= kLutMaxBytes);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);  // [cap]
   unsigned long long* keys2 = keys + a.cap;                                    // [cap]
@@ -588,8 +580,7 @@ __global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel
   float* lg = reinterpret_cast<float*>(lbase + a.nprobe);                       // [nprobe]
   float* lsq = lg + a.nprobe;                                                   // [nprobe]
   uint32_t* pl = reinterpret_cast<uint32_t*>(lsq + a.nprobe);                  // [4 * W]
-  float* lut = reinterpret_cast<float*>(pl + 4 * W);                            // [NB * 256] if kLut
-  float* qsT = lut + (kLut ? NB * 256 : 0);                                     // [8 * NB]
+  float* qsT = reinterpret_cast<float*>(pl + 4 * W);                            // [8 * NB]
   __shared__ int s_count, s_nl, s_misc[3], s_cnt2;
   __shared__ float s_tau;
   __shared__ unsigned s_hist[256];
@@ -604,18 +595,6 @@ __global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel
     qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
   }
   for (int j = tid; j < 4 * W; j += kScanThreads) pl[j] = a.planes[q * 4 * W + j];
-  if constexpr (kLut) {
-    // lut[j * 256 + byte] = sum of q over the set bits of `byte` at code byte j (bit 7 first).
-    const float* qrow = a.Qr + q * (8 * NB);
-    for (int e = tid; e < NB * 256; e += kScanThreads) {
-      const int j = e >> 8, byte = e & 255;
-      float b = 0.0f;
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj)
-        if ((byte >> (7 - jj)) & 1) b = __fadd_rn(b, __ldg(qrow + 8 * j + jj));
-      lut[e] = b;
-    }
-  }
   if (warp == 0) {
     // The slice's lists: owned probes (l % shard_count == shard_rank) with owned-rank in
     // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
@@ -678,15 +657,7 @@ __global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel
   const int total = pre[nl];
   const float delta = a.delta[q];
   const float k1 = a.k1[q];
-  uint32_t plr[kPlanesInRegs ? 4 * W : 1];
-  if constexpr (kPlanesInRegs) {
-#pragma unroll
-    for (int i = 0; i < 4 * W; ++i) plr[i] = pl[i];
-  }
-  auto P = [&](int b, int w) -> uint32_t {
-    if constexpr (kPlanesInRegs) return plr[b * W + w];
-    else return pl[b * W + w];
-  };
+  auto P = [&](int b, int w) -> uint32_t { return pl[b * W + w]; };  // shared-memory broadcast
   unsigned n_scan = 0, n_admit = 0;
   // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
   int cur = 0;
@@ -738,7 +709,7 @@ __global__ void __launch_bounds__(kScanThreads, RBQ_SCAN_MIN_BLOCKS) scan_kernel
         const int slot = __shfl_sync(0xffffffffu, sslot, src);
         const float base_d = __shfl_sync(0xffffffffu, sbase, src);
         const float fr = __shfl_sync(0xffffffffu, sfr, src);
-        const float eip = warp_exact_ip<W, kLut>(a.codes, slot, lut, qsT, lane);
+        const float eip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
         const float dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
         if (lane == 0 && dist <= tau) {
           const int at = atomicAdd(&s_count, 1);
@@ -792,7 +763,7 @@ static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
 {
   constexpr int NB = 4 * W;
   const size_t smem = (size_t)a.cap * 8 * 2 + (size_t)(2 * a.nprobe + 1) * 4 + (size_t)2 * a.nprobe * 4 +
-                      (size_t)4 * W * 4 + (NB <= kLutMaxBytes ? (size_t)NB * 256 * 4 : 0) + (size_t)8 * NB * 4;
+                      (size_t)4 * W * 4 + (size_t)8 * NB * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "scan: shared memory budget exceeded (cap/nprobe too large)");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
