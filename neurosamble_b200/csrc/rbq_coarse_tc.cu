@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "rbq_internal.cuh"
 
 namespace rbq {
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const float* _
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * kTcM;
+  const int q0 = blockIdx.x * kTcM;  // blockIdx.y: the first centroid chunk of this CTA
   const uint32_t bar0 = smem_u32(&s_bar[0]), bar1 = smem_u32(&s_bar[1]);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const float* _
   // barrier, so every thread takes the same path.
   const int nkc = dp / kTcKc;
   int it = 0;
-  for (int n0 = 0; n0 < K; n0 += kTcN) {
+  for (int n0 = blockIdx.y * kTcN; n0 < K; n0 += gridDim.y * kTcN) {
     for (int kc = 0; kc < nkc; ++kc, ++it) {
       const int sidx = it & 1;
       const uint32_t bar = sidx ? bar1 : bar0;
@@ -238,7 +240,9 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
   RBQ_CHECK(nq <= 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "coarse (tensor cores): bad sizes");
   const size_t smem = (size_t)2 * kTcStageBytes + 1024;
   RBQ_CUDA(cudaFuncSetAttribute(coarse_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  coarse_tc_kernel<<<(unsigned)ceil_div(nq, kTcM), kTcThreads, smem, s>>>(A, (int)nq, C, cn2, K, dp, S, err);
+  // one CTA per (128 queries, 256-centroid chunk)
+  const dim3 grid((unsigned)ceil_div(nq, kTcM), (unsigned)std::min<int64_t>(ceil_div(K, kTcN), 65535));
+  coarse_tc_kernel<<<grid, kTcThreads, smem, s>>>(A, (int)nq, C, cn2, K, dp, S, err);
   RBQ_LAUNCHED();
 }
 

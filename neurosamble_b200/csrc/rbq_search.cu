@@ -853,8 +853,13 @@ void launch_keys_to_result(const unsigned long long* keys, int64_t nq, int R, in
 // Exact rerank (semantics of cuvs::neighbors::refine, refine/refine_device.cuh:31-150): for
 // each candidate, |x - q|^2 over the original D dims: lane l sums double(x_d - q_d)^2 over
 // d = l, l+32, ... ascending, then an xor butterfly (16, 8, 4, 2, 1) of double adds, rounded
-// to float.  Top-k by (distance, id).  One CTA per query, one warp per candidate.
+// to float.  Top-k by (distance, id).  One CTA per query; each warp takes kRerankInFlight
+// candidates at a time and issues all their row loads before the arithmetic (EPL = D / 32
+// values per lane; EPL = 0 is the generic loop for other D).
 // ---------------------------------------------------------------------------------------
+constexpr int kRerankInFlight = 2;
+
+template <int EPL>
 __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ Xrows,
                                                      const uint32_t* __restrict__ id2row, int D,
                                                      const float* __restrict__ Q,
@@ -869,21 +874,62 @@ __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ X
   for (int j = threadIdx.x; j < D; j += blockDim.x) qs[j] = Q[q * D + j];
   for (int i = threadIdx.x; i < r2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
-  for (int r = warp; r < R; r += nwarps) {
-    const unsigned long long ck = cand[q * R + r];
-    if (ck == kEmptyKey) continue;
-    const uint32_t id = (uint32_t)(ck & 0xFFFFFFFFu);
-    const uint32_t row = id2row[id];
-    if (row == 0xFFFFFFFFu) continue;
-    const float* x = Xrows + (size_t)row * D;
-    double s = 0.0;
-    for (int d = lane; d < D; d += 32) {
-      const float df = __fsub_rn(__ldg(x + d), qs[d]);
-      s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
-    }
+  for (int r0 = warp * kRerankInFlight; r0 < R; r0 += nwarps * kRerankInFlight) {
+    const float* xp[kRerankInFlight];
+    uint32_t idv[kRerankInFlight];
+    bool ok[kRerankInFlight];
 #pragma unroll
-    for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    if (lane == 0) keys[r] = make_key((float)s, id);
+    for (int c = 0; c < kRerankInFlight; ++c) {  // warp-uniform: every lane reads the same key
+      const int r = r0 + c;
+      ok[c] = false;
+      xp[c] = Xrows;
+      idv[c] = 0u;
+      if (r < R) {
+        const unsigned long long ck = cand[q * R + r];
+        if (ck != kEmptyKey) {
+          const uint32_t id = (uint32_t)(ck & 0xFFFFFFFFu);
+          const uint32_t row = id2row[id];
+          if (row != 0xFFFFFFFFu) {
+            ok[c] = true;
+            xp[c] = Xrows + (size_t)row * D;
+            idv[c] = id;
+          }
+        }
+      }
+    }
+    if constexpr (EPL > 0) {
+      float xv[kRerankInFlight][EPL];
+#pragma unroll
+      for (int c = 0; c < kRerankInFlight; ++c)
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) xv[c][i] = ok[c] ? __ldg(xp[c] + lane + 32 * i) : 0.0f;
+#pragma unroll
+      for (int c = 0; c < kRerankInFlight; ++c) {
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+          const float df = __fsub_rn(xv[c][i], qs[lane + 32 * i]);
+          s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+        if (lane == 0 && ok[c]) keys[r0 + c] = make_key((float)s, idv[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < kRerankInFlight; ++c) {
+        double s = 0.0;
+        if (ok[c]) {
+          for (int d = lane; d < D; d += 32) {
+            const float df = __fsub_rn(__ldg(xp[c] + d), qs[d]);
+            s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
+          }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+        if (lane == 0 && ok[c]) keys[r0 + c] = make_key((float)s, idv[c]);
+      }
+    }
   }
   __syncthreads();
   block_bitonic_sort(keys, r2);
@@ -899,6 +945,17 @@ __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ X
   }
 }
 
+template <int EPL>
+static void launch_rerank_e(const float* Xrows, const uint32_t* id2row, int D, const float* Q, int64_t nq,
+                            const unsigned long long* cand, int R, int k, int r2, size_t smem, float* dist,
+                            int64_t* ids, cudaStream_t s)
+{
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(rerank_kernel<EPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rerank_kernel<EPL><<<(unsigned)nq, 256, smem, s>>>(Xrows, id2row, D, Q, cand, R, k, r2, dist, ids);
+  RBQ_LAUNCHED();
+}
+
 void launch_rerank(const float* Xrows, const uint32_t* id2row, int D, const float* Q, int64_t nq,
                    const unsigned long long* cand, int R, int k, float* dist, int64_t* ids, cudaStream_t s)
 {
@@ -906,10 +963,16 @@ void launch_rerank(const float* Xrows, const uint32_t* id2row, int D, const floa
   const int r2 = next_pow2(R < 2 ? 2 : R);
   const size_t smem = (size_t)r2 * 8 + (size_t)D * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "rerank: depth too large");
-  if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  rerank_kernel<<<(unsigned)nq, 256, smem, s>>>(Xrows, id2row, D, Q, cand, R, k, r2, dist, ids);
-  RBQ_LAUNCHED();
+  const int epl = (D % 32 == 0) ? D / 32 : 0;
+  switch (epl) {
+    case 1: launch_rerank_e<1>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    case 2: launch_rerank_e<2>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    case 4: launch_rerank_e<4>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    case 8: launch_rerank_e<8>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    case 12: launch_rerank_e<12>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    case 24: launch_rerank_e<24>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+    default: launch_rerank_e<0>(Xrows, id2row, D, Q, nq, cand, R, k, r2, smem, dist, ids, s); break;
+  }
 }
 
 __global__ void ids_to_keys_kernel(const int64_t* __restrict__ ids, int64_t n, unsigned long long* __restrict__ keys)
