@@ -223,6 +223,7 @@ def run_ours(args, cfg):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
@@ -251,6 +252,8 @@ def run_ours(args, cfg):
     Qd = torch.from_numpy(Q).to(dev)
     index.nprobe = cfg["nprobe"]
     index.prune = True
+    if world == 1:
+        index.seeded = args.seeded
 
     # ---- recall at the config's rerank depth; raise R along the ladder until recall >= target
     gt = None
@@ -367,7 +370,8 @@ def run_ours(args, cfg):
     e2e = nq / e2e_s
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
-    roof, roof_rr, scan_share = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev)
+    seeded = world > 1 or args.seeded != 0
+    roof, roof_rr, scan_share = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -394,9 +398,11 @@ def run_ours(args, cfg):
     return 0
 
 
-def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
-    """Time rbq_scan and rbq_rerank alone on the batch; algorithmic bytes from the actual
-    probed list sizes: sum n_l (D/8 + 12) for the scan, R (4D + 8) per query for the rerank."""
+def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
+    """Time rbq_scan and rbq_rerank alone on the batch, as the search runs them (seeded: the
+    nearest probe, then the others from the threshold it gives, all-reduced across shards);
+    algorithmic bytes from the actual probed list sizes: sum n_l (D/8 + 12) for the scan,
+    (4D + 8) per candidate the rerank holds."""
     import ctypes
 
     import torch
@@ -424,38 +430,54 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
     owned = (pr % info.shard_count) == info.shard_rank
     vec = int(sizes[pr][owned].sum())
     scan_bytes = vec * (d // 8 + 12)
-    ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
-    dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     stats = torch.zeros(2, dtype=torch.int64, device=dev)
-    _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g), P, R, 1,
-              1, 0, _ptr(ids), _ptr(dist), _ptr(stats), st)
+
+    def timed(fn):
+        ts = []
+        for it in range(3 + steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            if it >= 3:
+                ts.append(e0.elapsed_time(e1))
+        return float(np.mean(ts))
+
+    def scan(pp, gg, npr, tau, init, ids_t, dist_t, stats_t):
+        _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pp), _ptr(gg), npr,
+                  _ptr(tau) if tau is not None else None, _ptr(init[0]) if init else None,
+                  _ptr(init[1]) if init else None, R, 1, 1, 0, _ptr(ids_t), _ptr(dist_t),
+                  _ptr(stats_t) if stats_t is not None else None, st)
+
+    ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
+    dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
+    if seeded:  # the search's two phases: the nearest probe, then the rest from the shared seed
+        ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
+        da = torch.empty((nq, R), dtype=torch.float32, device=dev)
+        pa, ga = probes[:, :1].contiguous(), g[:, :1].contiguous()
+        pb, gb = probes[:, 1:].contiguous(), g[:, 1:].contiguous()
+        scan(pa, ga, 1, None, None, ia, da, stats)
+        tau = da[:, R - 1].contiguous()
+        if info.shard_count > 1:
+            import torch.distributed as tdist
+            tdist.all_reduce(tau, op=tdist.ReduceOp.MIN)
+        scan(pb, gb, P - 1, tau, (ia, da), ids, dist, stats)
+
+        def run_scan():
+            scan(pa, ga, 1, None, None, ia, da, None)
+            scan(pb, gb, P - 1, tau, (ia, da), ids, dist, None)
+
+        scan_ms = timed(run_scan)
+    else:
+        scan(probes, g, P, None, None, ids, dist, stats)
+        scan_ms = timed(lambda: scan(probes, g, P, None, None, ids, dist, None))
     scanned, admitted = (int(v) for v in stats.cpu().tolist())
-    ts = []
-    for it in range(3 + steps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g), P, R, 1,
-                  1, 0, _ptr(ids), _ptr(dist), None, st)
-        e1.record(stream)
-        e1.synchronize()
-        if it >= 3:
-            ts.append(e0.elapsed_time(e1))
-    scan_ms = float(np.mean(ts))
     od = torch.empty((nq, cfg["k"]), dtype=torch.float32, device=dev)
     oi = torch.empty((nq, cfg["k"]), dtype=torch.int64, device=dev)
-    tr = []
-    for it in range(3 + steps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        _lib.call("rbq_rerank", h, _ptr(Qd), nq, _ptr(ids), R, cfg["k"], _ptr(od), _ptr(oi), st)
-        e1.record(stream)
-        e1.synchronize()
-        if it >= 3:
-            tr.append(e0.elapsed_time(e1))
-    rr_ms = float(np.mean(tr))
+    rr_ms = timed(lambda: _lib.call("rbq_rerank", h, _ptr(Qd), nq, _ptr(ids), R, cfg["k"], _ptr(od), _ptr(oi), st))
     n_valid = int((ids >= 0).sum().item())
     rr_bytes = n_valid * (4 * d + 8)
     peak, kind = measured_peak()
@@ -469,7 +491,8 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev):
             traffic = None
     ach = scan_bytes / (scan_ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-            "traffic": traffic, "peak_kind": kind, "kernel": "rbq scan_kernel (+ key->id epilogue)",
+            "traffic": traffic, "peak_kind": kind,
+            "kernel": "rbq scan_kernel (+ key->id epilogue)" + (", 2 launches: seed list + rest" if seeded else ""),
             "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
             "launch_ms": round(scan_ms, 4), "prune_admitted_fraction": round(admitted / max(1, scanned), 4)}
     ach_r = rr_bytes / (rr_ms / 1000.0) / 1e9
@@ -505,6 +528,8 @@ def main():
     ap.add_argument("--n", type=int, default=0, help="database size override (smoke runs)")
     ap.add_argument("--nq", type=int, default=0, help="query batch override")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seeded", type=int, default=1, choices=[0, 1],
+                    help="1 GPU: two-phase scan seeded by the nearest list (the library default) or one pass")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

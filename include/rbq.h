@@ -58,6 +58,9 @@ typedef struct {
   int32_t probe_split;   /* probe slices per query (0 = auto from nq and P)                    */
   int32_t cand_cap;      /* candidate buffer entries per slice (0 = default 1024)              */
   int32_t coarse_margin; /* extra lists kept by the approximate coarse pass (0 = default)      */
+  int32_t seeded;        /* two-phase scan: the nearest probed list first, its candidates and  */
+                         /* R-th estimate seed the scan of the rest; -1 = default (on),         */
+                         /* 0 = off (one pass from +inf), 1 = on                                */
 } rbq_search_params_t;
 
 typedef struct {
@@ -157,11 +160,18 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
                int32_t* probes_dev, float* g_dev, void* stream);
 /* List scan: top-R candidates (estimated distance, id) per query over its probed lists.
  * Replaces SearchClusterQueryPairsQuantizeQuery (searcher_gpu_quantize_query.cu:1006-1596).
+ * Optional seeds of a two-phase search (the query's nearest list scanned first):
+ *   tau0_dev (f32[nq]): the threshold every slice of query q starts from (default +inf), e.g.
+ *     the smallest R-th distance any shard found in its first phase;
+ *   init_ids_dev / init_dist_dev ([nq, R], id -1 = none): candidates of that earlier scan,
+ *     merged into the result (slice 0 starts from them, and from their R-th distance when
+ *     all R are present).
  * stats_dev (optional, u64[2]) accumulates vectors scanned / admitted by the prune. */
 int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-             int32_t R, int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev,
-             float* cand_dist_dev, uint64_t* stats_dev, void* stream);
+             const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
+             int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
+             uint64_t* stats_dev, void* stream);
 /* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
  * search time: a host program whose device memory is handed out up front by its own pool
  * (so a library cudaMalloc would fail or break its budget), or a latency-critical search
@@ -169,7 +179,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
  * The scan's only scratch, the per-slice candidate keys, lives in a fixed array of
  * RBQ_NOALLOC_SCRATCH_BYTES compiled into librbq.so; every GPU that loads the library holds
  * that much memory until the process exits.  Inputs, outputs and their meaning are exactly
- * those of rbq_scan.  Limits and rules:
+ * those of rbq_scan without its initial candidates (tau0_dev is accepted).  Limits and rules:
  *   - needs nq*slices*R*8 bytes, plus nq*R*8 when slices > 1 (each part rounded up to 256);
  *     anything larger is rejected with RBQ_ERR_INVALID before any work is queued;
  *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
@@ -182,8 +192,8 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
 #define RBQ_NOALLOC_SCRATCH_BYTES (32u << 20)
 int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
                      const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-                     int32_t R, int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev,
-                     float* cand_dist_dev, uint64_t* stats_dev, void* stream);
+                     const float* tau0_dev, int32_t R, int32_t prune, int32_t slices, int32_t cand_cap,
+                     int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev, void* stream);
 /* Phase-1 estimator of one query against every vector of list `list`: integer popcount
  * inner product acc, estimate est and lower bound low (slot order of the list).  Replaces the
  * phase-1 loop of computeInnerProductsWithBitwiseBlockSort (searcher_gpu_quantize_query.cu:

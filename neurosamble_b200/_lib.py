@@ -25,7 +25,7 @@ class IndexParams(ctypes.Structure):
 class SearchParams(ctypes.Structure):
     _fields_ = [("n_probes", ctypes.c_int32), ("k", ctypes.c_int32), ("rerank", ctypes.c_int32),
                 ("prune", ctypes.c_int32), ("probe_split", ctypes.c_int32), ("cand_cap", ctypes.c_int32),
-                ("coarse_margin", ctypes.c_int32)]
+                ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32)]
 
 
 class IndexInfo(ctypes.Structure):
@@ -65,8 +65,8 @@ SIGNATURES = {
     "rbq_coarse_scores": [_P, _P, _I64, _P, _I32, _P],
     "rbq_check_errors": [_P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
-    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
-    "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "rbq_merge_results": [_P, _P, _I32, _I64, _I32, _P, _P, _P],
     "rbq_gen_mixture": [_P, _I64, _I32, _I32, _F32, _I32, _I32, _U64, _P],

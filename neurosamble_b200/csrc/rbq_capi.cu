@@ -350,6 +350,7 @@ void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
 struct SearchPlan {
   int P, k, R, cap, slices, m;
   int prune;
+  bool seeded;  // two-phase scan (search_scan)
 };
 
 SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq)
@@ -374,7 +375,70 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(16, sp.P / 2);
   sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
   sp.prune = p.prune ? 1 : 0;
+  sp.seeded = p.seeded != 0;
   return sp;
+}
+
+// Scan arguments of one query batch against this shard's lists (probes: [nq, nprobe]).
+ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* planes, const float* delta,
+                         const float* k1, int64_t nq, const int32_t* probes, const float* g, int nprobe, int R,
+                         int cap, int prune, int slices, unsigned long long* out_keys, uint64_t* stats)
+{
+  ScanArgs sa;
+  sa.list_off = ix.list_off;
+  sa.ids = ix.ids;
+  sa.codes = ix.codes;
+  sa.fadd = ix.fadd;
+  sa.frescale = ix.frescale;
+  sa.ferr = ix.ferr;
+  sa.n_slots = ix.n_rows;
+  sa.Dp = ix.Dp;
+  sa.W = ix.W;
+  sa.Qr = Qr;
+  sa.planes = planes;
+  sa.delta = delta;
+  sa.k1 = k1;
+  sa.nq = nq;
+  sa.probes = probes;
+  sa.g = g;
+  sa.nprobe = nprobe;
+  sa.R = R;
+  sa.cap = cap;
+  sa.prune = prune ? 1 : 0;
+  sa.slices = slices;
+  sa.shard_rank = ix.shard_rank;
+  sa.shard_count = ix.shard_count;
+  sa.out_keys = out_keys;
+  sa.stats = reinterpret_cast<unsigned long long*>(stats);
+  return sa;
+}
+
+// The list scan of a search: one pass over all probes in sp.slices slices, or (sp.seeded) two
+// phases.  Phase A scans each query's nearest probe alone (one slice; only if this shard owns
+// it) into keys_a [nq, R]; phase B scans probes 1..P-1 in sp.slices slices, slice 0 starting
+// from phase A's candidates and every slice from their R-th distance.  Without the seed every
+// slice starts at +inf and admits its first ~R + tile vectors unpruned.
+void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const uint32_t* planes, const float* delta,
+                 const float* k1, int64_t nq, const int32_t* probes, const float* g, unsigned long long* keys_a,
+                 unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, cudaStream_t s)
+{
+  ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
+                                keys_s, stats);
+  if (sp.seeded && sp.P > 1) {
+    ScanArgs a0 = sa;
+    a0.nprobe = 1;
+    a0.pstride = sp.P;
+    a0.slices = 1;
+    a0.out_keys = keys_a;
+    launch_scan(a0, s);
+    sa.probes = probes + 1;
+    sa.g = g + 1;
+    sa.nprobe = sp.P - 1;
+    sa.pstride = sp.P;
+    sa.init_keys = keys_a;
+  }
+  launch_scan(sa, s);
+  if (sp.slices > 1) launch_merge_keys(keys_s, nq, sp.slices, sp.R, keys, s);
 }
 
 void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, int64_t nq, float* dist, int64_t* ids,
@@ -397,6 +461,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   float* k1 = sc.get<float>(chunk);
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
   unsigned long long* keys = sp.slices > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : keys_s;
+  unsigned long long* keys_a = sp.seeded && sp.P > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : nullptr;
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
@@ -405,34 +470,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
     launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
     launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
-    ScanArgs sa;
-    sa.list_off = ix.list_off;
-    sa.ids = ix.ids;
-    sa.codes = ix.codes;
-    sa.fadd = ix.fadd;
-    sa.frescale = ix.frescale;
-    sa.ferr = ix.ferr;
-    sa.n_slots = ix.n_rows;
-    sa.Dp = ix.Dp;
-    sa.W = ix.W;
-    sa.Qr = Qr;
-    sa.planes = planes;
-    sa.delta = delta;
-    sa.k1 = k1;
-    sa.nq = cn;
-    sa.probes = probes;
-    sa.g = g;
-    sa.nprobe = sp.P;
-    sa.R = sp.R;
-    sa.cap = sp.cap;
-    sa.prune = sp.prune;
-    sa.slices = sp.slices;
-    sa.shard_rank = ix.shard_rank;
-    sa.shard_count = ix.shard_count;
-    sa.out_keys = keys_s;
-    sa.stats = reinterpret_cast<unsigned long long*>(stats);
-    launch_scan(sa, s);
-    if (sp.slices > 1) launch_merge_keys(keys_s, cn, sp.slices, sp.R, keys, s);
+    search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, keys_a, keys_s, keys, stats, s);
     if (params.rerank > 0)
       launch_rerank(ix.X_r, ix.id2row, ix.D, Qc, cn, keys, sp.R, sp.k, dist + a * sp.k, ids + a * sp.k, s);
     else
@@ -543,6 +581,7 @@ void rbq_search_params_default(rbq_search_params_t* p)
   p->probe_split = 0;
   p->cand_cap = 0;
   p->coarse_margin = 0;
+  p->seeded = -1;
 }
 
 int rbq_make_rotation(int32_t padded_dim, uint64_t seed, float* P_host)
@@ -999,9 +1038,10 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
 }
 
 int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
-             const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe, int32_t R,
-             int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
-             uint64_t* stats_dev, void* stream)
+             const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+             const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R, int32_t prune,
+             int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev,
+             void* stream)
 {
   return guarded([&] {
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
@@ -1009,6 +1049,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
                           cand_dist_dev),
               RBQ_ERR_INVALID, "null buffer");
     RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1, RBQ_ERR_INVALID, "bad scan parameters");
+    RBQ_CHECK(!init_ids_dev == !init_dist_dev, RBQ_ERR_INVALID, "init_ids and init_dist go together");
     if (nq == 0) return;
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
@@ -1017,32 +1058,14 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     Scratch sc(s);
     unsigned long long* ks = sc.get<unsigned long long>((size_t)nq * slices * R);
     unsigned long long* k2 = slices > 1 ? sc.get<unsigned long long>((size_t)nq * R) : ks;
-    ScanArgs sa;
-    sa.list_off = ix.list_off;
-    sa.ids = ix.ids;
-    sa.codes = ix.codes;
-    sa.fadd = ix.fadd;
-    sa.frescale = ix.frescale;
-    sa.ferr = ix.ferr;
-    sa.n_slots = ix.n_rows;
-    sa.Dp = ix.Dp;
-    sa.W = ix.W;
-    sa.Qr = Qr_dev;
-    sa.planes = planes_dev;
-    sa.delta = delta_dev;
-    sa.k1 = k1_dev;
-    sa.nq = nq;
-    sa.probes = probes_dev;
-    sa.g = g_dev;
-    sa.nprobe = nprobe;
-    sa.R = R;
-    sa.cap = cap;
-    sa.prune = prune ? 1 : 0;
-    sa.slices = slices;
-    sa.shard_rank = ix.shard_rank;
-    sa.shard_count = ix.shard_count;
-    sa.out_keys = ks;
-    sa.stats = reinterpret_cast<unsigned long long*>(stats_dev);
+    ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
+                                  prune, slices, ks, stats_dev);
+    sa.tau0 = tau0_dev;
+    if (init_ids_dev) {
+      unsigned long long* ik = sc.get<unsigned long long>((size_t)nq * R);
+      launch_cands_to_keys(init_ids_dev, init_dist_dev, nq * R, ik, s);
+      sa.init_keys = ik;
+    }
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
     launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);
@@ -1141,9 +1164,9 @@ inline size_t round_up_256(size_t v) { return (v + 255) / 256 * 256; }
 
 extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev,
                                 const float* delta_dev, const float* k1_dev, int64_t nq, const int32_t* probes_dev,
-                                const float* g_dev, int32_t nprobe, int32_t R, int32_t prune, int32_t slices,
-                                int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev,
-                                void* stream)
+                                const float* g_dev, int32_t nprobe, const float* tau0_dev, int32_t R, int32_t prune,
+                                int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
+                                uint64_t* stats_dev, void* stream)
 {
   return guarded([&] {
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
@@ -1166,32 +1189,9 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
     unsigned long long* ks = reinterpret_cast<unsigned long long*>(base);
     unsigned long long* k2 = slices > 1 ? reinterpret_cast<unsigned long long*>(base + keys_bytes) : ks;
     const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
-    ScanArgs sa;
-    sa.list_off = ix.list_off;
-    sa.ids = ix.ids;
-    sa.codes = ix.codes;
-    sa.fadd = ix.fadd;
-    sa.frescale = ix.frescale;
-    sa.ferr = ix.ferr;
-    sa.n_slots = ix.n_rows;
-    sa.Dp = ix.Dp;
-    sa.W = ix.W;
-    sa.Qr = Qr_dev;
-    sa.planes = planes_dev;
-    sa.delta = delta_dev;
-    sa.k1 = k1_dev;
-    sa.nq = nq;
-    sa.probes = probes_dev;
-    sa.g = g_dev;
-    sa.nprobe = nprobe;
-    sa.R = R;
-    sa.cap = cap;
-    sa.prune = prune ? 1 : 0;
-    sa.slices = slices;
-    sa.shard_rank = ix.shard_rank;
-    sa.shard_count = ix.shard_count;
-    sa.out_keys = ks;
-    sa.stats = reinterpret_cast<unsigned long long*>(stats_dev);
+    ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
+                                  prune, slices, ks, stats_dev);
+    sa.tau0 = tau0_dev;
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
     launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);

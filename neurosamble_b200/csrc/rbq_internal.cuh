@@ -176,14 +176,21 @@ struct ScanArgs {
   const float* delta;
   const float* k1;
   int64_t nq;
-  const int32_t* probes;
+  const int32_t* probes;  // query q's probes: probes[q * pstride + p], p < nprobe (g alike)
   const float* g;
   int nprobe;
+  int pstride = 0;  // 0: nprobe
   int R;
   int cap;
   int prune;
   int slices;
   int shard_rank, shard_count;
+  // Optional seeds.  tau0 [nq]: every slice of query q starts from threshold tau0[q] (default
+  // +inf).  init_keys [nq, R] (kEmptyKey = none, any order): candidates of an earlier scan of
+  // the same query, loaded into slice 0's buffer; when all R are present the slice starts from
+  // min(tau0, their largest distance).
+  const float* tau0 = nullptr;
+  const unsigned long long* init_keys = nullptr;
   unsigned long long* out_keys;  // [nq, slices, R]
   unsigned long long* stats;     // optional [2]: scanned, admitted
 };
@@ -214,6 +221,8 @@ void launch_gather_rows_u32(const uint32_t* src, int64_t rows, int cols, const i
 void launch_scatter_id2row(const uint32_t* ids, int64_t n, uint32_t* id2row, cudaStream_t s);
 // keys[i] = ids[i] < 0 ? empty : (0 << 32 | ids[i]).
 void launch_ids_to_keys(const int64_t* ids, int64_t n, unsigned long long* keys, cudaStream_t s);
+// (id, distance) pairs -> keys (id < 0 -> kEmptyKey).
+void launch_cands_to_keys(const int64_t* ids, const float* dist, int64_t n, unsigned long long* keys, cudaStream_t s);
 void launch_keys_to_ids(const unsigned long long* keys, int64_t n, int64_t* ids, float* dist, cudaStream_t s);
 // k-way merge of [parts, nq, k] results.
 void launch_merge_results(const float* dist, const int64_t* ids, int parts, int64_t nq, int k, float* out_dist,

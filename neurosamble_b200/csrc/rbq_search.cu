@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     // The slice's lists: owned probes (l % shard_count == shard_rank) with owned-rank in
     // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
     // sequence.
-    const int* prow = a.probes + q * a.nprobe;
+    const int* prow = a.probes + q * a.pstride;
     int m = 0;
     for (int p0 = 0; p0 < a.nprobe; p0 += 32) {
       const int p = p0 + lane;
@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       if (own && rank >= pb && rank < pe) {
         const int i = rank - pb;
         const int64_t b0 = a.list_off[l];
-        const float g = a.g[q * a.nprobe + p];
+        const float g = a.g[q * a.pstride + p];
         lbase[i] = (int)b0;
         pre[i + 1] = (int)(a.list_off[l + 1] - b0);  // size, turned into a prefix below
         lg[i] = g;
@@ -649,10 +649,23 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       }
       s_nl = n;
       s_count = 0;
-      s_tau = __int_as_float(0x7f800000);
+      s_kmax = 0ull;
+      s_tau = a.tau0 ? a.tau0[q] : __int_as_float(0x7f800000);
     }
   }
   __syncthreads();
+  if (a.init_keys && slice == 0) {
+    for (int i = tid; i < a.R; i += kScanThreads) {
+      const unsigned long long k = a.init_keys[q * a.R + i];
+      if (k != kEmptyKey) {
+        keys[atomicAdd(&s_count, 1)] = k;
+        atomicMax(&s_kmax, k);
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && s_count == a.R) s_tau = fminf(s_tau, from_ordered_bits((uint32_t)(s_kmax >> 32)));
+    __syncthreads();
+  }
   const int nl = s_nl;
   const int total = pre[nl];
   const float delta = a.delta[q];
@@ -718,8 +731,10 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       }
     }
     __syncthreads();
+    // Tighten tau after a tile when the buffer is nearly full, when it holds 2R keys, or as soon
+    // as R keys exist while tau is still open.
     const int cnt = s_count;
-    if (cnt > a.cap - kScanTile) {
+    if (cnt > a.cap - kScanTile || cnt >= 2 * a.R || (cnt >= a.R && isinf(s_tau))) {
       const unsigned long long kth = block_keep_smallest(keys, cnt, a.R, keys2, s_hist, s_misc, &s_kmax, &s_cnt2);
       unsigned long long* t = keys;
       keys = keys2;
@@ -773,9 +788,12 @@ static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
   RBQ_LAUNCHED();
 }
 
-void launch_scan(const ScanArgs& a, cudaStream_t s)
+void launch_scan(const ScanArgs& args, cudaStream_t s)
 {
-  if (a.nq <= 0) return;
+  if (args.nq <= 0) return;
+  ScanArgs a = args;
+  if (a.pstride == 0) a.pstride = a.nprobe;
+  RBQ_CHECK(a.nprobe >= 1 && a.pstride >= a.nprobe, RBQ_ERR_INVALID, "scan: bad probe stride");
   RBQ_CHECK(a.cap >= a.R + kScanTile && (a.cap & (a.cap - 1)) == 0, RBQ_ERR_INVALID,
             "scan: cap must be a power of two >= R + tile");
   RBQ_CHECK(a.Dp == 32 * a.W, RBQ_ERR_INVALID, "scan: padded dim mismatch");
@@ -871,32 +889,35 @@ __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ X
   float* qs = reinterpret_cast<float*>(keys + r2);                           // [D]
   const int64_t q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  __shared__ int s_nv;
+  if (threadIdx.x == 0) s_nv = 0;
   for (int j = threadIdx.x; j < D; j += blockDim.x) qs[j] = Q[q * D + j];
-  for (int i = threadIdx.x; i < r2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
-  for (int r0 = warp * kRerankInFlight; r0 < R; r0 += nwarps * kRerankInFlight) {
+  // Candidates stored on this shard, compacted to keys[0, nv) as (row << 32 | id): a shard of a
+  // seeded sharded search holds only a few of the R slots, and the work follows nv, not R.
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const unsigned long long ck = cand[q * R + r];
+    if (ck != kEmptyKey) {
+      const uint32_t id = (uint32_t)(ck & 0xFFFFFFFFu);
+      const uint32_t row = id2row[id];
+      if (row != 0xFFFFFFFFu) keys[atomicAdd(&s_nv, 1)] = ((unsigned long long)row << 32) | id;
+    }
+  }
+  __syncthreads();
+  const int nv = s_nv;
+  for (int r0 = warp * kRerankInFlight; r0 < nv; r0 += nwarps * kRerankInFlight) {
     const float* xp[kRerankInFlight];
     uint32_t idv[kRerankInFlight];
     bool ok[kRerankInFlight];
 #pragma unroll
-    for (int c = 0; c < kRerankInFlight; ++c) {  // warp-uniform: every lane reads the same key
+    for (int c = 0; c < kRerankInFlight; ++c) {  // warp-uniform: every lane reads the same slot
       const int r = r0 + c;
-      ok[c] = false;
-      xp[c] = Xrows;
-      idv[c] = 0u;
-      if (r < R) {
-        const unsigned long long ck = cand[q * R + r];
-        if (ck != kEmptyKey) {
-          const uint32_t id = (uint32_t)(ck & 0xFFFFFFFFu);
-          const uint32_t row = id2row[id];
-          if (row != 0xFFFFFFFFu) {
-            ok[c] = true;
-            xp[c] = Xrows + (size_t)row * D;
-            idv[c] = id;
-          }
-        }
-      }
+      ok[c] = r < nv;
+      const unsigned long long e = ok[c] ? keys[r] : 0ull;
+      xp[c] = Xrows + (size_t)(uint32_t)(e >> 32) * D;
+      idv[c] = (uint32_t)(e & 0xFFFFFFFFu);
     }
+    __syncwarp();
     if constexpr (EPL > 0) {
       float xv[kRerankInFlight][EPL];
 #pragma unroll
@@ -932,9 +953,13 @@ __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ X
     }
   }
   __syncthreads();
-  block_bitonic_sort(keys, r2);
+  int n2 = 2;
+  while (n2 < nv) n2 <<= 1;
+  for (int i = nv + threadIdx.x; i < n2; i += blockDim.x) keys[i] = kEmptyKey;
+  __syncthreads();
+  block_bitonic_sort(keys, n2);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const unsigned long long key = (i < r2) ? keys[i] : kEmptyKey;
+    const unsigned long long key = (i < nv) ? keys[i] : kEmptyKey;
     if (key == kEmptyKey) {
       dist[q * k + i] = __int_as_float(0x7f800000);
       ids[q * k + i] = -1;
@@ -985,6 +1010,20 @@ void launch_ids_to_keys(const int64_t* ids, int64_t n, unsigned long long* keys,
 {
   if (n <= 0) return;
   ids_to_keys_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(ids, n, keys);
+  RBQ_LAUNCHED();
+}
+
+__global__ void cands_to_keys_kernel(const int64_t* __restrict__ ids, const float* __restrict__ dist, int64_t n,
+                                     unsigned long long* __restrict__ keys)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) keys[i] = ids[i] < 0 ? kEmptyKey : make_key(dist[i], (uint32_t)ids[i]);
+}
+
+void launch_cands_to_keys(const int64_t* ids, const float* dist, int64_t n, unsigned long long* keys, cudaStream_t s)
+{
+  if (n <= 0) return;
+  cands_to_keys_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(ids, dist, n, keys);
   RBQ_LAUNCHED();
 }
 

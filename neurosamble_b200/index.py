@@ -41,7 +41,8 @@ class IndexIVFRaBitQ:
     ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``.
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
-    ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto).
+    ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
+    scan seeded by the nearest list: -1 = default, on; 0 off; 1 on).
     """
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
@@ -59,6 +60,7 @@ class IndexIVFRaBitQ:
         self.probe_split = 0
         self.cand_cap = 0
         self.coarse_margin = 0
+        self.seeded = -1
         self._h = ctypes.c_void_p()
         if _handle is not None:
             self._h = _handle
@@ -149,6 +151,7 @@ class IndexIVFRaBitQ:
         sp.n_probes, sp.k, sp.rerank = int(self.nprobe), int(k), int(self.k_rerank)
         sp.prune, sp.probe_split = int(bool(self.prune)), int(self.probe_split)
         sp.cand_cap, sp.coarse_margin = int(self.cand_cap), int(self.coarse_margin)
+        sp.seeded = int(self.seeded)
         return sp
 
     def search(self, x, k: int):

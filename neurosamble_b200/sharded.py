@@ -1,11 +1,22 @@
 """List-sharded IVF-RaBitQ over the GPUs of one box: one process per GPU.
 
 List l lives on rank l % world (every rank keeps the full centroid table, rotation and t4).
-A search runs the full coarse quantiser on every rank, scans only the rank's own probed
-lists, reranks its local top-R, and returns a local top-k; the per-rank [nq, k] results
-cross NVLink in ONE all-gather (one packed buffer per rank) and are merged on the device
-by (distance, id).  The reference RaBitQ path is single-GPU (src/rabitq_gpu/rabitq_search.cu:11);
-the sharding follows FAISS's sharded GPU search that map_full.py:302-317 uses for IVF-Flat.
+A search of a batch replicated on every rank runs in four steps:
+
+1. front end, split by query: rank r rotates, coarse-quantises and 4-bit-quantises queries
+   [r*nl, (r+1)*nl) (nl = ceil(nq / world)); one all-gather hands every rank the records
+   (rotated query, planes, delta, k1, probes, g) of the whole batch;
+2. seed: each rank scans the nearest probed list of the queries whose nearest list it owns;
+   an all-reduce (min) of the per-query R-th estimate gives every rank the threshold a
+   single GPU reaches after that list, so a shard prunes its lists as tightly as one GPU
+   prunes all of them (without it a shard far from the query admits most of its vectors);
+3. scan the remaining probes from that threshold, merge with the seed keys, rerank the
+   shard's candidates (only those under the threshold survive, ~R / world per shard);
+4. the per-rank [nq, k] results cross NVLink in one all-gather (one packed buffer per rank)
+   and are merged on the device by (distance, id).
+
+The reference RaBitQ path is single-GPU (src/rabitq_gpu/rabitq_search.cu:11); the sharding
+follows FAISS's sharded GPU search that map_full.py:302-317 uses for IVF-Flat.
 """
 from __future__ import annotations
 
@@ -17,6 +28,50 @@ import torch.distributed as dist
 
 from . import _lib
 from .index import IndexIVFRaBitQ, _ptr, _stream_ptr
+
+SCAN_TILE = 512  # vectors per scan tile (kScanTile in the library)
+
+
+def _pow2(v: int) -> int:
+    p = 1
+    while p < v:
+        p <<= 1
+    return p
+
+
+def plan(nq: int, nprobe: int, k: int, k_rerank: int, probe_split: int, cand_cap: int, world: int):
+    """(R, slices, cap) of a sharded search: the library's search planning (plan_search)."""
+    R = max(k_rerank, k) if k_rerank > 0 else k
+    own = max(1, (nprobe + world - 1) // world)
+    sl = probe_split if probe_split > 0 else max(1, 512 // max(1, nq))
+    sl = max(1, min(sl, own, max(1, 8192 // R)))
+    cap = max(_pow2(cand_cap if cand_cap > 0 else 1024), _pow2(R + SCAN_TILE))
+    return R, sl, cap
+
+
+def front_layout(nl: int, dp: int, nprobe: int):
+    """Byte layout of one rank's block of front-end records for nl queries (256-B aligned
+    fields): name -> (offset, bytes per query, dtype, per-query shape); and the block size."""
+    w = dp // 32
+    fields = [("qr", 4 * dp, torch.float32, (dp,)), ("planes", 16 * w, torch.int32, (4, w)),
+              ("delta", 4, torch.float32, ()), ("k1", 4, torch.float32, ()),
+              ("probes", 4 * nprobe, torch.int32, (nprobe,)), ("g", 4 * nprobe, torch.float32, (nprobe,))]
+    out, off = {}, 0
+    for name, rb, dt, shape in fields:
+        out[name] = (off, rb, dt, shape)
+        off += (nl * rb + 255) // 256 * 256
+    return out, off
+
+
+def _field(buf: torch.Tensor, lay, name: str, n: int) -> torch.Tensor:
+    off, rb, dt, shape = lay[name]
+    return buf[off: off + n * rb].view(dt).view(n, *shape)
+
+
+def _gathered_field(per: torch.Tensor, lay, name: str, nl: int, nq: int) -> torch.Tensor:
+    """[world, block] gathered bytes -> the field for queries [0, nq), contiguous."""
+    off, rb, dt, shape = lay[name]
+    return per[:, off: off + nl * rb].contiguous().view(dt).view(-1, *shape)[:nq]
 
 
 def pack_results(dist_t: torch.Tensor, ids_t: torch.Tensor) -> torch.Tensor:
@@ -107,12 +162,107 @@ class ShardedIndexIVFRaBitQ:
         d, i = self.local.search(t, k)
         return d, i
 
-    def search(self, x, k: int):
+    def search(self, x, k: int, stats: torch.Tensor | None = None):
+        """(D [nq, k], I [nq, k]) of the whole index for a batch every rank passes.
+
+        stats (optional int64[2] on this rank's device) accumulates this rank's vectors
+        scanned / admitted by the prune."""
         t, on_dev = self.local._to_device(x)
-        d, i = self.local.search(t, k)
-        if self.world > 1:
-            dall, iall = gather_results(d, i, self.group)
-            d, i = merge_results(dall, iall)
+        if self.world == 1:
+            d, i = self.local.search(t, k)
+        else:
+            loc = self.local
+            d, i = sharded_search(LibStages(loc), t, int(k), int(loc.nprobe), int(loc.k_rerank), bool(loc.prune),
+                                  int(loc.probe_split), int(loc.cand_cap), int(loc.coarse_margin),
+                                  loc.info().padded_dim, self.rank, self.world, self.group, stats)
+            if loc.metric == "ip":
+                d = 1.0 - 0.5 * d
         if on_dev:
             return d, i
         return d.cpu().numpy(), i.cpu().numpy()
+
+
+class LibStages:
+    """The stage entry points of librbq.so on one index (CUDA tensors, the index's stream)."""
+
+    def __init__(self, index: IndexIVFRaBitQ):
+        self.h = index.handle
+        self.device = index.device
+        self.st = _stream_ptr(index.device)
+
+    def front(self, q, margin, qr, probes, g, planes, delta, k1):
+        n, nprobe = q.shape[0], probes.shape[1]
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_rotate", self.h, _ptr(q), n, _ptr(qr), self.st)
+            _lib.call("rbq_coarse", self.h, _ptr(qr), n, nprobe, margin, _ptr(probes), _ptr(g), self.st)
+            _lib.call("rbq_query_prep", self.h, _ptr(qr), n, _ptr(planes), _ptr(delta), _ptr(k1), self.st)
+
+    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_scan", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0], _ptr(probes),
+                      _ptr(g), probes.shape[1], _ptr(tau0) if tau0 is not None else None,
+                      _ptr(init[0]) if init is not None else None, _ptr(init[1]) if init is not None else None, R,
+                      prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None, self.st)
+
+    def merge(self, d, ids, out_d, out_i):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_merge_results", _ptr(d), _ptr(ids), d.shape[0], d.shape[1], d.shape[2], _ptr(out_d),
+                      _ptr(out_i), self.st)
+
+    def rerank(self, q, cand, k, out_d, out_i):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_rerank", self.h, _ptr(q), q.shape[0], _ptr(cand), cand.shape[1], k, _ptr(out_d),
+                      _ptr(out_i), self.st)
+
+
+def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, prune: bool, probe_split: int,
+                   cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None):
+    """The four steps of a sharded search (module docstring) for the batch t [nq, D] that
+    every rank passes; `stages` computes (LibStages: librbq.so), this function moves data."""
+    dev = t.device
+    nq = t.shape[0]
+    P = nprobe
+    R, slices, cap = plan(nq, P, k, k_rerank, probe_split, cand_cap, world)
+    nl = (nq + world - 1) // world
+    lo, hi = min(nq, rank * nl), min(nq, (rank + 1) * nl)
+    lay, blk = front_layout(nl, dp, P)
+    # 1. front end of this rank's queries (padded with copies of the last query), all-gathered.
+    send = torch.empty(blk, dtype=torch.uint8, device=dev)
+    qloc = t[lo:hi]
+    if hi - lo < nl:
+        qloc = torch.cat([qloc, t[nq - 1:].expand(nl - (hi - lo), t.shape[1])])
+    stages.front(qloc.contiguous(), margin, *(_field(send, lay, f, nl)
+                                              for f in ("qr", "probes", "g", "planes", "delta", "k1")))
+    recv = torch.empty(world * blk, dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    per = recv.view(world, blk)
+    qr, planes, delta, k1, probes, g = (_gathered_field(per, lay, f, nl, nq)
+                                        for f in ("qr", "planes", "delta", "k1", "probes", "g"))
+    # 2. seed: the nearest probe, scanned by the rank that owns it; min over ranks of the R-th.
+    ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
+    da = torch.empty((nq, R), dtype=torch.float32, device=dev)
+    stages.scan(qr, planes, delta, k1, probes[:, :1].contiguous(), g[:, :1].contiguous(), None, None, R, int(prune),
+                1, cap, ia, da, stats)
+    tau = da[:, R - 1].contiguous()
+    dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
+    # 3. the other probes from the shared threshold, starting from the seed candidates; rerank
+    #    this shard's candidates.
+    if P > 1:
+        mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
+        md = torch.empty((nq, R), dtype=torch.float32, device=dev)
+        stages.scan(qr, planes, delta, k1, probes[:, 1:].contiguous(), g[:, 1:].contiguous(), tau, (ia, da), R,
+                    int(prune), slices, cap, mi, md, stats)
+    else:
+        mi, md = ia, da
+    if k_rerank > 0:
+        d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        i = torch.empty((nq, k), dtype=torch.int64, device=dev)
+        stages.rerank(t, mi, k, d, i)
+    else:
+        d, i = md[:, :k].contiguous(), mi[:, :k].contiguous()
+    # 4. one all-gather of the per-rank top-k, merged by (distance, id).
+    dall, iall = gather_results(d, i, group)
+    out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    out_i = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    stages.merge(dall.contiguous(), iall.contiguous(), out_d, out_i)
+    return out_d, out_i

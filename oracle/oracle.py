@@ -62,8 +62,8 @@ def lib():
         L.orc_exact_ip.argtypes = [_f32p, _u32p, _i32]
         L.orc_exact_ip.restype = ctypes.c_float
         L.orc_scan.argtypes = [_i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _i32, _f32p, _u32p,
-                               _f32p, _f32p, _i64, _i32p, _f32p, _i32, _i32, _i32, _i32, _i32,
-                               _i32, _i32, _i32, _i64p, _f32p, _i64p]
+                               _f32p, _f32p, _i64, _i32p, _f32p, _i32, ctypes.c_void_p, ctypes.c_void_p,
+                               ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64p, _f32p, _i64p]
         L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
         L.orc_l2_exact.restype = ctypes.c_float
         L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
@@ -219,22 +219,83 @@ def exact_ip(q, code) -> float:
 
 
 def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
-         slices=1, shard_rank=0, shard_count=1, with_stats=False):
+         slices=1, shard_rank=0, shard_count=1, with_stats=False, tau0=None, init=None):
+    """rbq_scan: top-R (ids, estimated distances) per query.  tau0 [nq] seeds every slice's
+    threshold; init = (ids, dist) [nq, R] are an earlier scan's candidates slice 0 starts from."""
     Qr = _c(Qr, np.float32)
     nq = Qr.shape[0]
+    probes, g = _c(probes, np.int32), _c(g, np.float32)
     nprobe = probes.shape[1]
     if cap is None:
         cap = default_cap(R, 0, tile)
     out_ids = np.empty((nq, R), np.int64)
     out_d = np.empty((nq, R), np.float32)
     stats = np.zeros(2, np.int64)
-    lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
-                   _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq,
-                   _c(probes, np.int32), _c(g, np.float32), nprobe, R, tile, cap, prune, slices,
-                   shard_rank, shard_count, out_ids, out_d, stats)
+    t0 = i0 = d0 = None
+    if tau0 is not None:
+        tau0 = _c(tau0, np.float32)
+        t0 = tau0.ctypes.data_as(ctypes.c_void_p)
+    if init is not None:
+        init_i, init_d = _c(init[0], np.int64), _c(init[1], np.float32)
+        assert init_i.shape == (nq, R) and init_d.shape == (nq, R)
+        i0, d0 = init_i.ctypes.data_as(ctypes.c_void_p), init_d.ctypes.data_as(ctypes.c_void_p)
+    if nq and nprobe:
+        lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
+                       _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g,
+                       nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, out_ids,
+                       out_d, stats)
+    elif init is not None:
+        out_ids[:], out_d[:] = merge_candidates([(init_i, init_d)], R)
+    else:
+        out_ids.fill(-1)
+        out_d.fill(np.inf)
     if with_stats:
         return out_ids, out_d, stats
     return out_ids, out_d
+
+
+def _keys(ids, d):
+    """64-bit sort keys (ordered float bits << 32 | id), as the CUDA path builds them."""
+    b = np.ascontiguousarray(d, np.float32).view(np.uint32).astype(np.uint64)
+    ordered = np.where(b & 0x80000000, ~b & 0xFFFFFFFF, b | 0x80000000)
+    k = (ordered << np.uint64(32)) | (ids.astype(np.uint64) & np.uint64(0xFFFFFFFF))
+    return np.where(ids < 0, np.uint64(0xFFFFFFFFFFFFFFFF), k)
+
+
+def merge_candidates(parts, R):
+    """R smallest (distance, id) of several [nq, r] candidate lists (ids -1 = empty)."""
+    ids = np.concatenate([p[0] for p in parts], axis=1)
+    d = np.concatenate([p[1] for p in parts], axis=1)
+    keys = np.sort(_keys(ids, d), axis=1)[:, :R]
+    empty = keys == np.uint64(0xFFFFFFFFFFFFFFFF)
+    out_i = np.where(empty, -1, (keys & np.uint64(0xFFFFFFFF)).astype(np.int64))
+    ob = (keys >> np.uint64(32)).astype(np.uint32)
+    bits = np.where(ob & 0x80000000, ob & 0x7FFFFFFF, ~ob).astype(np.uint32)
+    out_d = np.where(empty, np.inf, bits.view(np.float32)).astype(np.float32)
+    return out_i.astype(np.int64), out_d
+
+
+def seeded_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
+                slices=1, shard_rank=0, shard_count=1, with_stats=False, exchange=False):
+    """The two-phase scan of rbq_search (seeded) and of the sharded search.
+
+    Phase A scans each query's nearest probed list alone (on the shard that owns it, one slice);
+    phase B scans the other probes in `slices` slices from phase A's R-th distance (+inf with
+    fewer than R candidates), slice 0 also starting from phase A's candidates, so phase B's
+    result is the answer.  exchange=False: the shard's own phase-A threshold (rbq_search on one
+    index).  exchange=True: the minimum of every shard's phase-A threshold, i.e. the owner's,
+    which is what the sharded search's all-reduce hands to every shard."""
+    A = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, shard_rank,
+             shard_count, with_stats=True)
+    if exchange and shard_count > 1:
+        tau = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, 0, 1)[1][:, R - 1]
+    else:
+        tau = A[1][:, R - 1]
+    B = scan(ix, Qr, planes, delta, k1, probes[:, 1:], g[:, 1:], R, tile, cap, prune, slices, shard_rank,
+             shard_count, with_stats=True, tau0=tau, init=A[:2])
+    if with_stats:
+        return B[0], B[1], A[2] + B[2]
+    return B[0], B[1]
 
 
 def l2_exact(x, q) -> float:
@@ -269,17 +330,25 @@ def assign(X, C) -> np.ndarray:
 
 
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
-           shard_rank=0, shard_count=1, with_stats=False):
+           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 
-    rerank_depth == 0 returns the scan's top-k estimates (the reference behaviour)."""
+    seeded (rbq_search_params_t.seeded): -1 (default) and 1 scan in two phases (seeded_scan),
+    0 in one pass from +inf; exchange=True is the sharded search's
+    pipeline (two phases, threshold shared by all shards).  rerank_depth == 0 returns the
+    scan's top-k estimates (the reference behaviour)."""
     Q = _c(Q, np.float32)
     Qr = rotate(Q, ix.P)
     probes, g = coarse(Qr, ix.c_rot, nprobe)
     planes, delta, k1, _ = query_prep(Qr, ix.t4)
     R = rerank_depth if rerank_depth > 0 else k
-    res = scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
-               shard_count, with_stats=with_stats)
+    two = seeded != 0
+    if exchange or (two and nprobe > 1):
+        res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
+                          shard_count, with_stats=True, exchange=exchange)
+    else:
+        res = scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
+                   shard_count, with_stats=True)
     cand, cd = res[0], res[1]
     if rerank_depth > 0:
         dist, ids = rerank(ix.X, Q, cand, k)

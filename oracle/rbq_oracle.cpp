@@ -20,8 +20,9 @@
 // follows the fixed-order schedule that the CUDA library implements too, so the two agree
 // bit for bit on codes, factors, popcount sums, estimates and ids:
 //   * every reduction is a double accumulation in index order, rounded to float once;
-//   * the prune threshold only tightens at tile boundaries (tile = TILE vectors) when the
-//     per-query candidate buffer passes CAP - TILE entries;
+//   * the prune threshold only tightens at tile boundaries (tile = TILE vectors), when the
+//     per-query candidate buffer passes CAP - TILE entries, reaches 2R, or reaches R while
+//     the threshold is still +inf;
 //   * candidates are ordered by the 64-bit key (order-preserving float bits << 32 | id).
 // Parity with the reference itself is UNPINNED at those boundaries (the reference ships no
 // golden vectors and cannot be built here); the known-answer tests in tests/ pin the
@@ -496,11 +497,18 @@ struct ScanIndex {
 
 // One slice of one query's probes.  Mirrors the CUDA scan kernel's schedule exactly.
 static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32_t* pl, float delta,
-                       float k1, const int32_t* probe_l, const float* probe_g, int np, int R, int tile,
-                       int cap, int prune, std::vector<uint64_t>& keys, int64_t* stats)
+                       float k1, const int32_t* probe_l, const float* probe_g, int np, float tau0,
+                       const std::vector<uint64_t>& init, int R, int tile, int cap, int prune,
+                       std::vector<uint64_t>& keys, int64_t* stats)
 {
-  keys.clear();
-  float tau = INFINITY;
+  // The slice starts from the candidates `init` (an earlier scan's, possibly none) and from
+  // tau0, lowered to their largest distance when all R are present.
+  keys.assign(init.begin(), init.end());
+  float tau = tau0;
+  if ((int)keys.size() == R) {
+    const uint64_t kmax = *std::max_element(keys.begin(), keys.end());
+    tau = std::fmin(tau, from_ordered_bits((uint32_t)(kmax >> 32)));
+  }
   int64_t n_scanned = 0, n_admit = 0;
   // The slice's lists form one flat sequence of vectors (probe order, slot order inside a
   // list); tiles of `tile` vectors run across list boundaries.
@@ -529,7 +537,10 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
         if (dist <= tau) keys.push_back(make_key(dist, ix.ids[s]));
       }
     }
-    if ((int)keys.size() > cap - tile) {
+    // Tighten tau after a tile when the buffer is nearly full, when it holds 2R keys, or as soon
+    // as R keys exist while tau is still open.
+    const int cnt = (int)keys.size();
+    if (cnt > cap - tile || cnt >= 2 * R || (cnt >= R && std::isinf(tau))) {
       std::sort(keys.begin(), keys.end());
       keys.resize(R);
       tau = from_ordered_bits((uint32_t)(keys[R - 1] >> 32));
@@ -544,15 +555,20 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
 }
 
 // Scan (a9-a11): for every query the top-R candidates by (estimated distance, id).
-// probes/g: [nq, nprobe] from orc_coarse.  Lists owned by this shard: l % shard_count ==
-// shard_rank, taken in probe order and split into `slices` contiguous ranges (slice s gets
-// owned[floor(s*m/S) : floor((s+1)*m/S)]), each scanned with its own threshold, then merged.
+// probes/g: [nq, nprobe] from orc_coarse.  tau0 (optional, [nq]): every slice of query q starts
+// with threshold tau0[q] instead of +inf (a threshold seeded by an earlier scan).  init_ids /
+// init_dist (optional, [nq, R], id -1 = none): candidates of an earlier scan that slice 0
+// starts from.
+// Lists owned by this shard: l % shard_count == shard_rank, taken in probe order and split into
+// `slices` contiguous ranges (slice s gets owned[floor(s*m/S) : floor((s+1)*m/S)]), each
+// scanned with its own threshold, then merged.
 // Outputs out_ids [nq, R] (int64, -1 pad) and out_dist [nq, R] (+inf pad).
 // stats (optional, int64[2]): vectors scanned, vectors admitted by the prune.
 void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* codes, const float* fadd,
               const float* frescale, const float* ferr, int Dp, const float* Qr, const uint32_t* planes,
               const float* delta, const float* k1, int64_t nq, const int32_t* probes, const float* gq,
-              int nprobe, int R, int tile, int cap, int prune, int slices, int shard_rank,
+              int nprobe, const float* tau0, const int64_t* init_ids, const float* init_dist, int R, int tile,
+              int cap, int prune, int slices, int shard_rank,
               int shard_count, int64_t* out_ids, float* out_dist, int64_t* stats)
 {
   const int W = Dp / 32;
@@ -560,7 +576,8 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
   int64_t tot[2] = {0, 0};
 #pragma omp parallel
   {
-    std::vector<uint64_t> keys, all;
+    std::vector<uint64_t> keys, all, init;
+    const std::vector<uint64_t> none;
     std::vector<int32_t> own_l;
     std::vector<float> own_g;
     int64_t loc[2] = {0, 0};
@@ -577,10 +594,16 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
       }
       const int m = (int)own_l.size();
       all.clear();
+      init.clear();
+      if (init_ids)
+        for (int r = 0; r < R; ++r)
+          if (init_ids[q * R + r] >= 0)
+            init.push_back(make_key(init_dist[q * R + r], (uint32_t)init_ids[q * R + r]));
       for (int s = 0; s < slices; ++s) {
         int a = (int)(((int64_t)s * m) / slices), b = (int)(((int64_t)(s + 1) * m) / slices);
         scan_slice(ix, W, Qr + (size_t)q * Dp, planes + (size_t)q * 4 * W, delta[q], k1[q],
-                   own_l.data() + a, own_g.data() + a, b - a, R, tile, cap, prune, keys, loc);
+                   own_l.data() + a, own_g.data() + a, b - a, tau0 ? tau0[q] : INFINITY, s == 0 ? init : none,
+                   R, tile, cap, prune, keys, loc);
         all.insert(all.end(), keys.begin(), keys.end());
       }
       std::sort(all.begin(), all.end());

@@ -174,8 +174,8 @@ def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
     ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
     dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
     stats = torch.zeros(2, dtype=torch.int64, device="cuda")
-    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, R, prune,
-         slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
+    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, None, None, None, R,
+         prune, slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
     p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
     pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
     cap_o = oracle.default_cap(R, cap)
@@ -371,3 +371,52 @@ def test_tensor_core_scores_match_fp32(oracle, d, K, nq):
                     * np.linalg.norm(Cr, axis=1)[None, :]) + 1e-6
     assert np.all(np.isfinite(a))
     assert np.all(np.abs(a - b) <= bound), float(np.max(np.abs(a - b) - bound))
+
+
+@pytest.mark.parametrize("seeded,split", [(1, 1), (1, 3), (0, 4), (-1, 2)])
+def test_search_seeded_two_phase(oracle, case, seeded, split):
+    """rbq_search_params_t.seeded: the nearest list scanned first, its candidates and R-th
+    estimate seeding the rest (the default), or one pass (0), bit-exact against the oracle."""
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune, idx.probe_split, idx.seeded = 12, 40, True, split, seeded
+    try:
+        d, i = idx.search(Q, 10)
+    finally:
+        idx.probe_split, idx.seeded = 0, -1
+    d2, i2 = oracle.search(oix, Q, 10, 12, 40, prune=1, slices=split, seeded=seeded)
+    assert np.array_equal(i, i2)
+    assert np.array_equal(u32(d), u32(d2))
+
+
+def test_scan_from_a_seeded_threshold(oracle, case):
+    """rbq_scan's seeds: every slice starts from the per-query threshold tau0; slice 0 also from
+    the initial candidates (an earlier scan's), which the result then includes."""
+    torch = _torch()
+    idx, oix, X, Q, C, lab = case
+    nq, nprobe, R = Q.shape[0], 10, 30
+    Qr = oracle.rotate(Q, oix.P)
+    qr, planes, delta, k1 = _query_stage(idx, Qr)
+    probes = torch.empty((nq, nprobe), dtype=torch.int32, device="cuda")
+    g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), nq, nprobe, 0, ptr(probes), ptr(g), stream())
+    p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
+    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
+    ai, ad = oracle.scan(oix, Qr, pl2, d2, k2, p2[:, :1], g2[:, :1], R)
+    ai[1::7, R // 2:] = -1  # some queries with fewer than R initial candidates
+    ad[1::7, R // 2:] = np.inf
+    tau = ad[:, R - 1].copy()
+    tau[::5] = np.inf  # some queries unseeded
+    t0 = torch.from_numpy(tau).cuda()
+    ti, td = torch.from_numpy(ai).cuda(), torch.from_numpy(ad).cuda()
+    pb, gb = probes[:, 1:].contiguous(), g[:, 1:].contiguous()
+    for slices in (1, 2):
+        for with_init in (False, True):
+            ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+            dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
+            init = (ptr(ti), ptr(td)) if with_init else (None, None)
+            call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(pb), ptr(gb),
+                 nprobe - 1, ptr(t0), *init, R, 1, slices, 0, ptr(ids), ptr(dist), None, stream())
+            oi, od = oracle.scan(oix, Qr, pl2, d2, k2, p2[:, 1:], g2[:, 1:], R, prune=1, slices=slices, tau0=tau,
+                                 init=(ai, ad) if with_init else None)
+            assert np.array_equal(ids.cpu().numpy(), oi)
+            assert np.array_equal(u32(dist.cpu().numpy()), u32(od))

@@ -1,5 +1,7 @@
-"""List-sharded search on 2 GPUs (NCCL): the merged result of ShardedIndexIVFRaBitQ equals the
-oracle's sharded search merged by (distance, id), bit for bit.  Skipped with fewer than 2 GPUs."""
+"""List-sharded search on 2 GPUs (NCCL): the merged result of ShardedIndexIVFRaBitQ (split
+front end, seeded threshold shared by an all-reduce, one all-gather of the results) equals the
+oracle's sharded search (exchange=True) merged by (distance, id), bit for bit.  Skipped with
+fewer than 2 GPUs."""
 import os
 import pickle
 import socket
@@ -60,13 +62,8 @@ def test_two_gpu_sharded_search_matches_oracle(oracle):
         mp.spawn(_rank_main, args=(2, _port(), td), nprocs=2, join=True)
         d, i, C, lab, P, t4, X, Q = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
     oix = oracle.build(X, C, lab, P, t4)
-    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1) for r in range(2)]
-    keys = []
-    for q in range(Q.shape[0]):
-        kk = sorted((float(parts[r][0][q, j]), int(parts[r][1][q, j])) for r in range(2) for j in range(10)
-                    if parts[r][1][q, j] >= 0)[:10]
-        keys.append(kk)
-    want_i = np.array([[x[1] for x in kk] for kk in keys])
-    want_d = np.array([[x[0] for x in kk] for kk in keys], np.float32)
+    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1, exchange=True)
+             for r in range(2)]
+    want_i, want_d = oracle.merge_candidates([(p[1], p[0]) for p in parts], 10)
     assert np.array_equal(i, want_i)
     assert np.array_equal(d.view(np.uint32), want_d.view(np.uint32))

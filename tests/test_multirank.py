@@ -108,3 +108,103 @@ def test_missing_rank_fails_the_collective_within_the_timeout():
                 p.terminate()
         err = open(os.path.join(td, "rank0.txt")).read()
     assert err, "rank 0's all-gather returned although rank 1 never joined"
+
+
+class _OracleStages:
+    """The stage interface of neurosamble_b200.sharded.LibStages, computed by the CPU oracle on
+    CPU tensors: lets the product's sharded orchestration (front-end split, record all-gather,
+    seed all-reduce, result all-gather) run over gloo without a GPU."""
+
+    def __init__(self, O, ix, rank, world):
+        self.O, self.ix, self.rank, self.world = O, ix, rank, world
+
+    def front(self, q, margin, qr, probes, g, planes, delta, k1):
+        import torch
+        O, ix = self.O, self.ix
+        Qr = O.rotate(q.numpy(), ix.P)
+        p, gg = O.coarse(Qr, ix.c_rot, probes.shape[1])
+        pl, de, kk, _ = O.query_prep(Qr, ix.t4)
+        qr.copy_(torch.from_numpy(Qr))
+        probes.copy_(torch.from_numpy(p))
+        g.copy_(torch.from_numpy(gg))
+        planes.copy_(torch.from_numpy(np.ascontiguousarray(pl).view(np.int32).reshape(planes.shape)))
+        delta.copy_(torch.from_numpy(de))
+        k1.copy_(torch.from_numpy(kk))
+
+    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
+        import torch
+        oi, od = self.O.scan(self.ix, qr.numpy(), planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(),
+                             probes.numpy(), g.numpy(), R, cap=cap, prune=prune, slices=slices,
+                             shard_rank=self.rank, shard_count=self.world,
+                             tau0=tau0.numpy() if tau0 is not None else None,
+                             init=(init[0].numpy(), init[1].numpy()) if init is not None else None)
+        ids.copy_(torch.from_numpy(oi))
+        d.copy_(torch.from_numpy(od))
+
+    def merge(self, d, ids, out_d, out_i):
+        import torch
+        mi, md = self.O.merge_candidates([(ids[p].numpy(), d[p].numpy()) for p in range(d.shape[0])], d.shape[2])
+        out_d.copy_(torch.from_numpy(md))
+        out_i.copy_(torch.from_numpy(mi))
+
+    def rerank(self, q, cand, k, out_d, out_i):
+        import torch
+        dd, ii = self.O.rerank(self.ix.X, q.numpy(), cand.numpy(), k)
+        out_d.copy_(torch.from_numpy(dd))
+        out_i.copy_(torch.from_numpy(ii))
+
+
+def _seeded_worker(rank, world, port, outdir, nq, prune):
+    import torch
+    import torch.distributed as dist
+
+    from conftest import mixture
+    from oracle import oracle as O
+    from neurosamble_b200.sharded import sharded_search
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
+    Q = Q[:nq]
+    P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
+    C, lab = O.kmeans(X, 24, iters=3)
+    ix = O.build(X, C, lab, P, t4)
+    d, i = sharded_search(_OracleStages(O, ix, rank, world), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0, 64,
+                          rank, world)
+    with open(os.path.join(outdir, f"rank{rank}.pkl"), "wb") as f:
+        pickle.dump((d.numpy(), i.numpy()), f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,nq,prune", [(2, 40, 1), (3, 7, 1), (2, 40, 0)])
+def test_seeded_sharded_search_over_gloo(world, nq, prune):
+    """The orchestration (queries split for the front end and padded, records all-gathered,
+    seeds all-reduced, results all-gathered and merged) gives, on every rank, the merge of the
+    oracle's per-shard searches with the shared seed.  With the prune off every shard keeps its
+    exact top-R by estimate, so the shards' candidates contain the single-shard top-R and the
+    reranked distances are, rank by rank, no larger than the single-shard search's."""
+    from conftest import mixture
+    from oracle import oracle as O
+    from neurosamble_b200.sharded import plan
+
+    with tempfile.TemporaryDirectory() as td:
+        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune), nprocs=world, join=True)
+        res = [pickle.load(open(os.path.join(td, f"rank{r}.pkl"), "rb")) for r in range(world)]
+    X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
+    Q = Q[:nq]
+    P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
+    C, lab = O.kmeans(X, 24, iters=3)
+    ix = O.build(X, C, lab, P, t4)
+    slices = plan(nq, 8, 10, 60, 0, 0, world)[1]
+    parts = [O.search(ix, Q, 10, 8, 60, prune=prune, slices=slices, shard_rank=r, shard_count=world, exchange=True)
+             for r in range(world)]
+    want_i, want_d = O.merge_candidates([(p[1], p[0]) for p in parts], 10)
+    for d, i in res:
+        assert np.array_equal(i, want_i)
+        assert np.array_equal(d.view(np.uint32), want_d.view(np.uint32))
+    if not prune:
+        d1, i1 = O.search(ix, Q, 10, 8, 60, prune=0)
+        assert (want_d <= d1).all()
+        assert np.mean([len(set(a) & set(b)) for a, b in zip(want_i.tolist(), i1.tolist())]) >= 9.5

@@ -135,3 +135,49 @@ def test_reference_gtest_recall_floor(oracle):
     _, gt = oracle.knn_exact(X, Q, 10)
     _, ids = oracle.search(ix, Q, 10, 16, 0, prune=1)
     assert oracle.recall(ids, gt) >= 0.3
+
+
+def test_seeded_scan_without_prune_is_the_plain_top_r(oracle, small):
+    """A seed is the R-th estimate of a subset of the probed vectors, never below the true R-th:
+    with the prune off the two-phase scan (any slicing, any shard count) keeps the exact top-R."""
+    ix, X, Q, lab = small
+    Qr, probes, g, planes, delta, k1 = prep(oracle, ix, Q, 8)
+    R = 30
+    full = oracle.scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0)
+    for slices in (1, 3):
+        ids, dist = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0, slices=slices)
+        assert np.array_equal(ids, full[0]) and np.array_equal(dist.view(np.uint32), full[1].view(np.uint32))
+    parts = [oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, prune=0, shard_rank=r, shard_count=3,
+                                exchange=True) for r in range(3)]
+    mi, md = oracle.merge_candidates(parts, R)
+    assert np.array_equal(mi, full[0])
+
+
+def test_seed_is_shared_and_keeps_shards_pruning(oracle, small):
+    """exchange=True gives every shard the owner's phase-A threshold: the shards together admit
+    about as many vectors as one shard (each shard's threshold then tightens only on its own
+    candidates), far fewer than unseeded shards, which start from +inf."""
+    ix, X, Q, lab = small
+    Qr, probes, g, planes, delta, k1 = prep(oracle, ix, Q, 12)
+    R = 40
+
+    def admitted(shards, seeded):
+        tot = np.zeros(2, np.int64)
+        for r in range(shards):
+            if seeded:
+                st = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, shard_rank=r, shard_count=shards,
+                                        with_stats=True, exchange=True)[2]
+            else:
+                st = oracle.scan(ix, Qr, planes, delta, k1, probes, g, R, shard_rank=r, shard_count=shards,
+                                 with_stats=True)[2]
+            tot += st
+        return tot
+
+    one, four = admitted(1, True), admitted(4, True)
+    assert one[0] == four[0]  # every probed vector is scanned exactly once
+    assert four[1] <= one[1] * 1.25
+    assert admitted(4, False)[1] > 1.5 * four[1]
+    # shard_count = 1: the exchanged seed is the shard's own
+    a = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, exchange=True)
+    b = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, exchange=False)
+    assert np.array_equal(a[0], b[0])

@@ -36,7 +36,8 @@ def test_size_rule_rejects_before_touching_the_index():
     dummy = ctypes.c_void_p(1)  # never dereferenced: the size rule is checked first
     buf = ctypes.c_void_p(1)
     nq, R = 9000, 512  # 9000 * 512 * 8 bytes > 32 MiB
-    st = L.rbq_scan_noalloc(dummy, buf, buf, buf, buf, nq, buf, buf, 8, R, 1, 1, 0, buf, buf, None, None)
+    st = L.rbq_scan_noalloc(dummy, buf, buf, buf, buf, nq, buf, buf, 8, None, R, 1, 1, 0, buf, buf, None,
+                            None)
     assert st == 1
     msg = L.rbq_last_error().decode()
     assert "static scratch holds 33554432 bytes" in msg
@@ -70,8 +71,9 @@ def _run(idx, name, st, nprobe, R, prune, slices):
     ids = torch.full((nq, R), -7, dtype=torch.int64, device="cuda")
     dist = torch.full((nq, R), -7.0, dtype=torch.float32, device="cuda")
     stats = torch.zeros(2, dtype=torch.int64, device="cuda")
-    _lib.call(name, idx.handle, _p(qr), _p(planes), _p(delta), _p(k1), nq, _p(probes), _p(g), nprobe, R, prune,
-              slices, 0, _p(ids), _p(dist), _p(stats), _stream_ptr(idx.device))
+    init = (None, None) if name == "rbq_scan" else ()  # rbq_scan's initial candidates: none
+    _lib.call(name, idx.handle, _p(qr), _p(planes), _p(delta), _p(k1), nq, _p(probes), _p(g), nprobe, None, *init, R,
+              prune, slices, 0, _p(ids), _p(dist), _p(stats), _stream_ptr(idx.device))
     torch.cuda.synchronize()
     return ids.cpu().numpy(), dist.cpu().numpy(), stats.cpu().numpy()
 
@@ -114,5 +116,6 @@ def test_noalloc_scan_refuses_batches_beyond_the_scratch():
     ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
     dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
     st = _lib.lib().rbq_scan_noalloc(idx.handle, _p(qr), _p(planes), _p(delta), _p(k1), nq, _p(probes), _p(g),
-                                     nprobe, R, 1, 1, 0, _p(ids), _p(dist), None, _stream_ptr(idx.device))
+                                     nprobe, None, R, 1, 1, 0, _p(ids), _p(dist), None,
+                                     _stream_ptr(idx.device))
     assert st == 1 and b"static scratch" in _lib.lib().rbq_last_error()
