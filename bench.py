@@ -370,7 +370,7 @@ def run_ours(args, cfg):
     e2e = nq / e2e_s
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
-    seeded = world > 1 or args.seeded != 0
+    seeded = world > 1 or args.seeded == 1
     roof, roof_rr, scan_share = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
 
     cpu = None
@@ -528,8 +528,8 @@ def main():
     ap.add_argument("--n", type=int, default=0, help="database size override (smoke runs)")
     ap.add_argument("--nq", type=int, default=0, help="query batch override")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--seeded", type=int, default=1, choices=[0, 1],
-                    help="1 GPU: two-phase scan seeded by the nearest list (the library default) or one pass")
+    ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
+                    help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -59,8 +59,8 @@ typedef struct {
   int32_t cand_cap;      /* candidate buffer entries per slice (0 = default 1024)              */
   int32_t coarse_margin; /* extra lists kept by the approximate coarse pass (0 = default)      */
   int32_t seeded;        /* two-phase scan: the nearest probed list first, its candidates and  */
-                         /* R-th estimate seed the scan of the rest; -1 = default (on),         */
-                         /* 0 = off (one pass from +inf), 1 = on                                */
+                         /* R-th estimate seed the scan of the rest; -1 = auto (on when the     */
+                         /* probes are split into slices), 0 = off (one pass), 1 = on           */
 } rbq_search_params_t;
 
 typedef struct {

@@ -375,7 +375,7 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(16, sp.P / 2);
   sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
   sp.prune = p.prune ? 1 : 0;
-  sp.seeded = p.seeded != 0;
+  sp.seeded = p.seeded < 0 ? sp.slices > 1 : p.seeded > 0;
   return sp;
 }
 

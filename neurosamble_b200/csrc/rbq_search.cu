@@ -671,6 +671,42 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const float delta = a.delta[q];
   const float k1 = a.k1[q];
   auto P = [&](int b, int w) -> uint32_t { return pl[b * W + w]; };  // shared-memory broadcast
+  // Bound seed: a pruning slice with no threshold and no candidates yet starts from the R-th
+  // smallest upper bound est + f_err * sqrt(g) over its leading whole lists holding at least R
+  // vectors (the RaBitQ error bound: R of them are that close), instead of admitting its first
+  // tile whole.  The bounds stream through the key buffer in tiles, cut to the R smallest
+  // whenever the buffer would overflow.
+  if (a.prune && isinf(s_tau) && s_count == 0 && total >= a.R) {
+    int nb = 0;
+    for (int i = 1; i <= nl && nb < a.R; ++i) nb = pre[i];
+    int c = 0, cnt = 0;
+    for (int c0 = 0; c0 < nb; c0 += kScanTile) {
+      const int c1 = min(nb, c0 + kScanTile);
+      for (int f = c0 + tid; f < c1; f += kScanThreads) {
+        while (pre[c + 1] <= f) ++c;
+        const int slot = lbase[c] + (f - pre[c]);
+        uint32_t cw[W];
+        load_code<W>(a.codes, slot, cw);
+        const int32_t acc = signed_dot<W>(P, cw);
+        const float base_d = __fadd_rn(__ldg(a.fadd + slot), lg[c]);
+        const float ip = __fmul_rn((float)acc, delta);
+        const float est = __fadd_rn(base_d, __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(ip, k1)));
+        const float up = __fadd_rn(est, __fmul_rn(__ldg(a.ferr + slot), lsq[c]));
+        keys[cnt + (f - c0)] = make_key(up, (uint32_t)f);
+      }
+      cnt += c1 - c0;
+      __syncthreads();
+      if (cnt > a.cap - kScanTile || c1 == nb) {
+        const unsigned long long kth = block_keep_smallest(keys, cnt, a.R, keys2, s_hist, s_misc, &s_kmax, &s_cnt2);
+        unsigned long long* t = keys;
+        keys = keys2;
+        keys2 = t;
+        cnt = a.R;
+        if (c1 == nb && tid == 0) s_tau = from_ordered_bits((uint32_t)(kth >> 32));
+      }
+      __syncthreads();
+    }
+  }
   unsigned n_scan = 0, n_admit = 0;
   // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
   int cur = 0;

@@ -333,8 +333,8 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
            shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 
-    seeded (rbq_search_params_t.seeded): -1 (default) and 1 scan in two phases (seeded_scan),
-    0 in one pass from +inf; exchange=True is the sharded search's
+    seeded (rbq_search_params_t.seeded): -1 scans in two phases (seeded_scan) when the probes
+    are split into slices > 1, 0 never, 1 always; exchange=True is the sharded search's
     pipeline (two phases, threshold shared by all shards).  rerank_depth == 0 returns the
     scan's top-k estimates (the reference behaviour)."""
     Q = _c(Q, np.float32)
@@ -342,7 +342,7 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     probes, g = coarse(Qr, ix.c_rot, nprobe)
     planes, delta, k1, _ = query_prep(Qr, ix.t4)
     R = rerank_depth if rerank_depth > 0 else k
-    two = seeded != 0
+    two = slices > 1 if seeded < 0 else seeded > 0
     if exchange or (two and nprobe > 1):
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
                           shard_count, with_stats=True, exchange=exchange)

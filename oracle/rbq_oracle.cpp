@@ -22,7 +22,9 @@
 //   * every reduction is a double accumulation in index order, rounded to float once;
 //   * the prune threshold only tightens at tile boundaries (tile = TILE vectors), when the
 //     per-query candidate buffer passes CAP - TILE entries, reaches 2R, or reaches R while
-//     the threshold is still +inf;
+//     the threshold is still +inf; a pruning slice that starts with no threshold and no
+//     candidates takes the R-th smallest upper bound est + f_err * sqrt(g) over its leading
+//     whole lists holding at least R vectors;
 //   * candidates are ordered by the 64-bit key (order-preserving float bits << 32 | id).
 // Parity with the reference itself is UNPINNED at those boundaries (the reference ships no
 // golden vectors and cannot be built here); the known-answer tests in tests/ pin the
@@ -515,6 +517,27 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
   std::vector<int64_t> pre(np + 1, 0);
   for (int p = 0; p < np; ++p) pre[p + 1] = pre[p] + (ix.list_off[probe_l[p] + 1] - ix.list_off[probe_l[p]]);
   const int64_t total = pre[np];
+  // Bound seed: a pruning slice with no threshold and no candidates yet starts from the R-th
+  // smallest upper bound est + f_err * sqrt(g) over its leading whole lists holding >= R vectors.
+  if (prune && std::isinf(tau) && keys.empty() && total >= R) {
+    int64_t nb = 0;
+    for (int i = 1; i <= np && nb < R; ++i) nb = pre[i];
+    std::vector<uint64_t> ub((size_t)nb);
+    int c = 0;
+    for (int64_t f = 0; f < nb; ++f) {
+      while (pre[c + 1] <= f) ++c;
+      const float g = probe_g[c];
+      const int64_t s = ix.list_off[probe_l[c]] + (f - pre[c]);
+      const int32_t acc = orc_popcount_ip(pl, ix.codes + (size_t)s * W, W);
+      const float ip = (float)acc * delta;
+      const float base_d = ix.fadd[s] + g;
+      const float est = base_d + ix.frescale[s] * (ip + k1);
+      const float up = est + ix.ferr[s] * sqrtf(g);
+      ub[(size_t)f] = make_key(up, (uint32_t)f);
+    }
+    std::nth_element(ub.begin(), ub.begin() + (R - 1), ub.end());
+    tau = from_ordered_bits((uint32_t)(ub[(size_t)R - 1] >> 32));
+  }
   int cur = 0;
   for (int64_t t0 = 0; t0 < total; t0 += tile) {
     const int64_t t1 = std::min<int64_t>(total, t0 + tile);

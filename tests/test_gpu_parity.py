@@ -376,7 +376,8 @@ def test_tensor_core_scores_match_fp32(oracle, d, K, nq):
 @pytest.mark.parametrize("seeded,split", [(1, 1), (1, 3), (0, 4), (-1, 2)])
 def test_search_seeded_two_phase(oracle, case, seeded, split):
     """rbq_search_params_t.seeded: the nearest list scanned first, its candidates and R-th
-    estimate seeding the rest (the default), or one pass (0), bit-exact against the oracle."""
+    estimate seeding the rest (on, or auto when the probes are split), or one pass (0),
+    bit-exact against the oracle."""
     idx, oix, X, Q, C, lab = case
     idx.nprobe, idx.k_rerank, idx.prune, idx.probe_split, idx.seeded = 12, 40, True, split, seeded
     try:
