@@ -16,7 +16,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -72,41 +71,48 @@ REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_c
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 5 ms during the timed region,
+    read through NVML (read-only queries; nothing is set)."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.samples = []
-        self.proc = None
+        self.stop = threading.Event()
+        self.t = None
+
+    def _handle(self, nv):
+        import torch
+        try:
+            return nv.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(self.gpu).uuid))
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), mx,
+                                             int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                    except Exception:
+                        pass
+                    self.stop.wait(0.005)
+
+            self.t = threading.Thread(target=run, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.t = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) == 3:
-                try:
-                    self.samples.append((float(parts[0]), float(parts[1]), int(parts[2], 16)))
-                except ValueError:
-                    pass
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.t:
+            self.t.join(timeout=2)
 
     def summary(self):
         if not self.samples:
@@ -427,7 +433,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     off = ix.export_lists()["list_off"]
     sizes = np.diff(off)
     pr = probes.cpu().numpy()
-    owned = (pr % info.shard_count) == info.shard_rank
+    owned = ix.list_owners()[pr] == info.shard_rank
     vec = int(sizes[pr][owned].sum())
     scan_bytes = vec * (d // 8 + 12)
     stream = torch.cuda.current_stream(dev)
@@ -448,7 +454,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
 
     def scan(pp, gg, npr, tau, init, ids_t, dist_t, stats_t):
         _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pp), _ptr(gg), npr,
-                  _ptr(tau) if tau is not None else None, _ptr(init[0]) if init else None,
+                  pp.stride(0), _ptr(tau) if tau is not None else None, _ptr(init[0]) if init else None,
                   _ptr(init[1]) if init else None, R, 1, 1, 0, _ptr(ids_t), _ptr(dist_t),
                   _ptr(stats_t) if stats_t is not None else None, st)
 
@@ -457,8 +463,8 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     if seeded:  # the search's two phases: the nearest probe, then the rest from the shared seed
         ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
         da = torch.empty((nq, R), dtype=torch.float32, device=dev)
-        pa, ga = probes[:, :1].contiguous(), g[:, :1].contiguous()
-        pb, gb = probes[:, 1:].contiguous(), g[:, 1:].contiguous()
+        pa, ga = probes[:, :1], g[:, :1]  # strided column views, row stride P
+        pb, gb = probes[:, 1:], g[:, 1:]
         scan(pa, ga, 1, None, None, ia, da, stats)
         tau = da[:, R - 1].contiguous()
         if info.shard_count > 1:

@@ -44,9 +44,20 @@ typedef struct {
   int32_t kmeans_n_iters;               /* reference default 20                               */
   int32_t max_train_points_per_cluster; /* reference default 256                              */
   int32_t device;                       /* CUDA device ordinal holding the index              */
-  int32_t shard_rank;                   /* this handle stores lists l with l % count == rank  */
+  int32_t shard_rank;                   /* this handle stores the lists owned by this rank    */
   int32_t shard_count;                  /* 1 = unsharded                                      */
+  int32_t shard_policy;                 /* list -> rank map: RBQ_SHARD_ROUND_ROBIN (l % count) */
+                                        /* or RBQ_SHARD_BALANCED (fixed at the first add)     */
 } rbq_index_params_t;
+
+/* List ownership across shards.  ROUND_ROBIN: list l on rank l % shard_count (the layout
+ * BASELINE's sharded configuration names).  BALANCED: the lists, taken by decreasing size^2
+ * (ties: smaller list id first), each go to the rank with the smallest sum of size^2 so far
+ * (ties: smaller rank), sizes counted over the first rbq_add batch, which every rank passes
+ * whole; a list's expected scan work grows with its size times how often it is probed, and
+ * both grow with its size. */
+#define RBQ_SHARD_ROUND_ROBIN 0
+#define RBQ_SHARD_BALANCED 1
 
 /* Search-time parameters.  Replaces cuvs::neighbors::ivf_rabitq::search_params
  * (ivf_rabitq.hpp:178-228) in QUANT4 mode. */
@@ -70,6 +81,8 @@ typedef struct {
   float query_scale;
   uint64_t seed;
   int64_t device_bytes; /* index memory held on the device */
+  int32_t shard_policy; /* RBQ_SHARD_*                      */
+  int32_t owners_fixed; /* 1 once the list -> rank map is final (ROUND_ROBIN: always) */
 } rbq_index_info_t;
 
 /* ---- errors / defaults ------------------------------------------------------------------ */
@@ -135,6 +148,8 @@ int rbq_get_centroids(rbq_index_t* index, float* C_host, float* C_rot_host);
  * f_add / f_rescale / f_err [n_local].  Any output may be NULL. */
 int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint32_t* codes, float* fadd,
                      float* frescale, float* ferr);
+/* owners [K]: the rank holding each list (-1 while a BALANCED map awaits the first add). */
+int rbq_get_list_owners(rbq_index_t* index, int32_t* owners);
 
 /* ---- stage entry points (device pointers; parity tests and the sharded driver) ----------- */
 /* Y [n, Dp] = pad(X [n, D]) * P.  Replaces RotatorGPU::rotate (rotator_gpu.cu:162-176). */
@@ -166,10 +181,12 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
  *   init_ids_dev / init_dist_dev ([nq, R], id -1 = none): candidates of that earlier scan,
  *     merged into the result (slice 0 starts from them, and from their R-th distance when
  *     all R are present).
+ * Query q's probes are probes_dev[q * probe_stride + p], p < nprobe (g alike; probe_stride
+ * 0 = nprobe), so the two phases can read columns 0 and 1.. of one [nq, P] array.
  * stats_dev (optional, u64[2]) accumulates vectors scanned / admitted by the prune. */
 int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-             const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
+             int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
              int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
              uint64_t* stats_dev, void* stream);
 /* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
@@ -192,7 +209,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
 #define RBQ_NOALLOC_SCRATCH_BYTES (32u << 20)
 int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
                      const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-                     const float* tau0_dev, int32_t R, int32_t prune, int32_t slices, int32_t cand_cap,
+                     int32_t probe_stride, const float* tau0_dev, int32_t R, int32_t prune, int32_t slices, int32_t cand_cap,
                      int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev, void* stream);
 /* Phase-1 estimator of one query against every vector of list `list`: integer popcount
  * inner product acc, estimate est and lower bound low (slot order of the list).  Replaces the

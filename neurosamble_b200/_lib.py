@@ -19,7 +19,8 @@ ERRORS = {1: "invalid argument", 2: "CUDA error", 3: "out of device memory", 4: 
 class IndexParams(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_int32), ("n_lists", ctypes.c_int32), ("seed", ctypes.c_uint64),
                 ("kmeans_n_iters", ctypes.c_int32), ("max_train_points_per_cluster", ctypes.c_int32),
-                ("device", ctypes.c_int32), ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32),
+                ("shard_policy", ctypes.c_int32)]
 
 
 class SearchParams(ctypes.Structure):
@@ -32,7 +33,10 @@ class IndexInfo(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_int32), ("padded_dim", ctypes.c_int32), ("n_lists", ctypes.c_int32),
                 ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32), ("trained", ctypes.c_int32),
                 ("n_total", ctypes.c_int64), ("n_local", ctypes.c_int64), ("query_scale", ctypes.c_float),
-                ("seed", ctypes.c_uint64), ("device_bytes", ctypes.c_int64)]
+                ("seed", ctypes.c_uint64), ("device_bytes", ctypes.c_int64), ("shard_policy", ctypes.c_int32),
+                ("owners_fixed", ctypes.c_int32)]
+
+SHARD_POLICIES = {"round_robin": 0, "balanced": 1}
 
 
 # name -> argtypes (all functions return int status unless listed in _RESTYPES)
@@ -60,13 +64,15 @@ SIGNATURES = {
     "rbq_get_rotation": [_P, _P],
     "rbq_get_centroids": [_P, _P, _P],
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
+    "rbq_get_list_owners": [_P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],
     "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _P],
     "rbq_coarse_scores": [_P, _P, _I64, _P, _I32, _P],
     "rbq_check_errors": [_P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
-    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
-    "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P,
+                         _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "rbq_merge_results": [_P, _P, _I32, _I64, _I32, _P, _P, _P],
     "rbq_gen_mixture": [_P, _I64, _I32, _I32, _F32, _I32, _I32, _U64, _P],

@@ -264,12 +264,17 @@ void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, 
   std::vector<uint32_t> hl(n);
   RBQ_CUDA(cudaMemcpyAsync(hl.data(), lab, n * 4, cudaMemcpyDeviceToHost, s));
   RBQ_CUDA(cudaStreamSynchronize(s));
+  for (int64_t i = 0; i < n; ++i) RBQ_CHECK(hl[i] < (uint32_t)ix.K, RBQ_ERR_INVALID, "add: label out of range");
+  if (!ix.owners_fixed) {  // BALANCED: the map follows the list sizes of the first batch
+    std::vector<int64_t> sizes(ix.K, 0);
+    for (int64_t i = 0; i < n; ++i) ++sizes[hl[i]];
+    install_owners(ix, list_owners(ix.shard_policy, sizes, ix.shard_count), true);
+  }
   std::vector<int64_t> own;
   std::vector<uint32_t> own_lab, own_ids;
   own.reserve(n);
   for (int64_t i = 0; i < n; ++i) {
-    RBQ_CHECK(hl[i] < (uint32_t)ix.K, RBQ_ERR_INVALID, "add: label out of range");
-    if ((int)(hl[i] % ix.shard_count) == ix.shard_rank) {
+    if (ix.owner_host[hl[i]] == ix.shard_rank) {
       own.push_back(i);
       own_lab.push_back(hl[i]);
       own_ids.push_back((uint32_t)(ix.n_total + i));
@@ -406,8 +411,8 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
   sa.cap = cap;
   sa.prune = prune ? 1 : 0;
   sa.slices = slices;
+  sa.owner = ix.owner;
   sa.shard_rank = ix.shard_rank;
-  sa.shard_count = ix.shard_count;
   sa.out_keys = out_keys;
   sa.stats = reinterpret_cast<unsigned long long*>(stats);
   return sa;
@@ -482,7 +487,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
 // Persistence: "RBQB200\0", version, dims, seed, t4, P, C, then this shard's rows.
 // ---------------------------------------------------------------------------------------
 const char kMagic[8] = {'R', 'B', 'Q', 'B', '2', '0', '0', '\0'};
-constexpr uint32_t kFormatVersion = 1;
+constexpr uint32_t kFormatVersion = 2;  // 2 adds the shard policy and list -> rank map
 
 struct File {
   FILE* f = nullptr;
@@ -522,6 +527,41 @@ void set_error(const std::string& msg) { g_last_error = msg; }
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+std::vector<int32_t> list_owners(int policy, const std::vector<int64_t>& sizes, int count)
+{
+  const int K = (int)sizes.size();
+  std::vector<int32_t> own(K, 0);
+  if (count <= 1) return own;
+  if (policy == RBQ_SHARD_ROUND_ROBIN) {
+    for (int l = 0; l < K; ++l) own[l] = l % count;
+    return own;
+  }
+  // BALANCED: lists by decreasing size^2 (ties: smaller id), each to the least-loaded rank.
+  std::vector<int> order(K);
+  for (int l = 0; l < K; ++l) order[l] = l;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return sizes[a] * sizes[a] > sizes[b] * sizes[b]; });
+  std::vector<int64_t> load(count, 0);
+  for (int l : order) {
+    int r = 0;
+    for (int j = 1; j < count; ++j)
+      if (load[j] < load[r]) r = j;
+    own[l] = r;
+    load[r] += sizes[l] * sizes[l];
+  }
+  return own;
+}
+
+void install_owners(Index& ix, const std::vector<int32_t>& owners, bool fixed)
+{
+  RBQ_CHECK((int)owners.size() == ix.K, RBQ_ERR_INVALID, "owner map size mismatch");
+  for (int32_t o : owners) RBQ_CHECK(o >= 0 && o < ix.shard_count, RBQ_ERR_INVALID, "owner out of range");
+  if (!ix.owner) ix.owner = dev_alloc<int32_t>(ix.K);
+  RBQ_CUDA(cudaMemcpy(ix.owner, owners.data(), (size_t)ix.K * 4, cudaMemcpyHostToDevice));
+  ix.owner_host = owners;
+  ix.owners_fixed = fixed;
+}
+
 void free_index_memory(Index& ix)
 {
   dev_free(ix.P);
@@ -538,6 +578,7 @@ void free_index_memory(Index& ix)
   dev_free(ix.ids_r);
   dev_free(ix.id2row);
   dev_free(ix.dev_err);
+  dev_free(ix.owner);
   dev_free(ix.list_off);
   dev_free(ix.ids);
   dev_free(ix.codes);
@@ -569,6 +610,7 @@ void rbq_index_params_default(rbq_index_params_t* p)
   p->device = 0;
   p->shard_rank = 0;
   p->shard_count = 1;
+  p->shard_policy = RBQ_SHARD_ROUND_ROBIN;
 }
 
 void rbq_search_params_default(rbq_search_params_t* p)
@@ -612,6 +654,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
               RBQ_ERR_INVALID, "bad shard rank / count");
     RBQ_CHECK(params->kmeans_n_iters >= 0 && params->max_train_points_per_cluster >= 1, RBQ_ERR_INVALID,
               "bad k-means parameters");
+    RBQ_CHECK(params->shard_policy == RBQ_SHARD_ROUND_ROBIN || params->shard_policy == RBQ_SHARD_BALANCED,
+              RBQ_ERR_INVALID, "unknown shard policy");
     int ndev = 0;
     RBQ_CUDA(cudaGetDeviceCount(&ndev));
     RBQ_CHECK(params->device >= 0 && params->device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
@@ -629,7 +673,10 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
     ix.max_train_per_list = params->max_train_points_per_cluster;
     ix.shard_rank = params->shard_rank;
     ix.shard_count = params->shard_count;
+    ix.shard_policy = params->shard_policy;
     try {
+      install_owners(ix, list_owners(RBQ_SHARD_ROUND_ROBIN, std::vector<int64_t>(ix.K, 0), ix.shard_count),
+                     ix.shard_policy == RBQ_SHARD_ROUND_ROBIN || ix.shard_count == 1);
       ix.P_host.resize((size_t)ix.Dp * ix.Dp);
       make_rotation(ix.Dp, ix.seed, ix.P_host.data());
       ix.t4 = query_scale(ix.Dp, ix.seed, 3);
@@ -678,7 +725,18 @@ int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out)
     out->seed = ix.seed;
     const int64_t per_row = (int64_t)ix.D * 4 + (int64_t)ix.W * 4 * 2 + 12 * 2 + 4 * 3;
     out->device_bytes = ix.cap_rows * per_row + ix.cap_ids * 4 + (int64_t)ix.Dp * ix.Dp * 4 +
-                        (int64_t)ix.K * (ix.D + ix.Dp + 2) * 4 + (ix.K + 1) * 8;
+                        (int64_t)ix.K * (ix.D + ix.Dp + 3) * 4 + (ix.K + 1) * 8;
+    out->shard_policy = ix.shard_policy;
+    out->owners_fixed = ix.owners_fixed ? 1 : 0;
+  });
+}
+
+int rbq_get_list_owners(rbq_index_t* index, int32_t* owners)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && owners, RBQ_ERR_INVALID, "null argument");
+    const Index& ix = index->ix;
+    for (int l = 0; l < ix.K; ++l) owners[l] = ix.owners_fixed ? ix.owner_host[l] : -1;
   });
 }
 
@@ -769,6 +827,9 @@ int rbq_save(rbq_index_t* index, const char* path)
     f.write(&ix.t4, 4);
     f.write(&ix.n_total, 8);
     f.write(&ix.n_rows, 8);
+    const int32_t pol[2] = {ix.shard_policy, ix.owners_fixed ? 1 : 0};
+    f.write(pol, sizeof(pol));
+    f.write(ix.owner_host.data(), (size_t)ix.K * 4);
     f.write(ix.P_host.data(), ix.P_host.size() * 4);
     if (ix.trained) f.write(ix.C_host.data(), ix.C_host.size() * 4);
     const size_t n = (size_t)ix.n_rows;
@@ -793,7 +854,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
     RBQ_CHECK(std::memcmp(magic, kMagic, 8) == 0, RBQ_ERR_FORMAT, "not an RBQB200 index file: " + f.path);
     uint32_t ver = 0;
     f.read(&ver, 4);
-    RBQ_CHECK(ver == kFormatVersion, RBQ_ERR_FORMAT, "unsupported index file version");
+    RBQ_CHECK(ver == 1 || ver == kFormatVersion, RBQ_ERR_FORMAT, "unsupported index file version");
     int32_t hdr[8];
     f.read(hdr, sizeof(hdr));
     uint64_t seed;
@@ -807,6 +868,16 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
     RBQ_CHECK(D >= 1 && D <= 2048 && Dp == (D + 31) / 32 * 32 && K >= 1 && n_rows >= 0 && n_total >= n_rows,
               RBQ_ERR_FORMAT, "corrupt index header");
     const int file_rank = hdr[5], file_count = hdr[6];
+    RBQ_CHECK(file_count >= 1 && file_rank >= 0 && file_rank < file_count, RBQ_ERR_FORMAT, "corrupt shard header");
+    int32_t pol[2] = {RBQ_SHARD_ROUND_ROBIN, 1};  // version 1: round robin
+    std::vector<int32_t> file_owner;
+    if (ver >= 2) {
+      f.read(pol, sizeof(pol));
+      RBQ_CHECK(pol[0] == RBQ_SHARD_ROUND_ROBIN || pol[0] == RBQ_SHARD_BALANCED, RBQ_ERR_FORMAT,
+                "corrupt shard policy");
+      file_owner.resize(K);
+      f.read(file_owner.data(), (size_t)K * 4);
+    }
     if (shard_count <= 0) {
       shard_count = file_count;
       shard_rank = file_rank;
@@ -843,6 +914,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.max_train_per_list = p.max_train_points_per_cluster;
       ix.shard_rank = p.shard_rank;
       ix.shard_count = p.shard_count;
+      ix.shard_policy = pol[0];
       ix.t4 = t4;
       ix.P_host.resize((size_t)Dp * Dp);
       f.read(ix.P_host.data(), ix.P_host.size() * 4);
@@ -868,11 +940,21 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       f.read(fr.data(), fr.size() * 4);
       f.read(fe.data(), fe.size() * 4);
       f.read(X.data(), X.size() * 4);
-      std::vector<int64_t> keep;
-      for (int64_t i = 0; i < n_rows; ++i) {
+      for (int64_t i = 0; i < n_rows; ++i)
         RBQ_CHECK(lab[i] < (uint32_t)K && ids[i] < (uint64_t)n_total, RBQ_ERR_FORMAT, "corrupt row data");
-        if ((int)(lab[i] % ix.shard_count) == ix.shard_rank) keep.push_back(i);
+      // The list -> rank map: the file's own when it is this shard's file (or unsharded);
+      // re-derived from the file's list sizes when a full index is loaded as one shard.
+      if (file_count == ix.shard_count && ver >= 2) {
+        install_owners(ix, file_owner, pol[1] != 0);
+      } else {
+        std::vector<int64_t> sizes(K, 0);
+        for (int64_t i = 0; i < n_rows; ++i) ++sizes[lab[i]];
+        install_owners(ix, list_owners(pol[0], sizes, ix.shard_count), ix.shard_policy == RBQ_SHARD_ROUND_ROBIN ||
+                                                                          n_rows > 0 || ix.shard_count == 1);
       }
+      std::vector<int64_t> keep;
+      for (int64_t i = 0; i < n_rows; ++i)
+        if (ix.owner_host[lab[i]] == ix.shard_rank) keep.push_back(i);
       const int64_t m = (int64_t)keep.size();
       auto pick_u32 = [&](const std::vector<uint32_t>& src, int w) {
         std::vector<uint32_t> o((size_t)m * w);
@@ -1039,7 +1121,7 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
 
 int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-             const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R, int32_t prune,
+             int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R, int32_t prune,
              int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev,
              void* stream)
 {
@@ -1048,7 +1130,8 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && cand_ids_dev &&
                           cand_dist_dev),
               RBQ_ERR_INVALID, "null buffer");
-    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1, RBQ_ERR_INVALID, "bad scan parameters");
+    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1 && (probe_stride == 0 || probe_stride >= nprobe),
+              RBQ_ERR_INVALID, "bad scan parameters");
     RBQ_CHECK(!init_ids_dev == !init_dist_dev, RBQ_ERR_INVALID, "init_ids and init_dist go together");
     if (nq == 0) return;
     Index& ix = index->ix;
@@ -1061,6 +1144,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
                                   prune, slices, ks, stats_dev);
     sa.tau0 = tau0_dev;
+    sa.pstride = probe_stride;
     if (init_ids_dev) {
       unsigned long long* ik = sc.get<unsigned long long>((size_t)nq * R);
       launch_cands_to_keys(init_ids_dev, init_dist_dev, nq * R, ik, s);
@@ -1164,7 +1248,8 @@ inline size_t round_up_256(size_t v) { return (v + 255) / 256 * 256; }
 
 extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev,
                                 const float* delta_dev, const float* k1_dev, int64_t nq, const int32_t* probes_dev,
-                                const float* g_dev, int32_t nprobe, const float* tau0_dev, int32_t R, int32_t prune,
+                                const float* g_dev, int32_t nprobe, int32_t probe_stride, const float* tau0_dev,
+                                int32_t R, int32_t prune,
                                 int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
                                 uint64_t* stats_dev, void* stream)
 {
@@ -1173,8 +1258,9 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
     RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && cand_ids_dev &&
                           cand_dist_dev),
               RBQ_ERR_INVALID, "null buffer");
-    RBQ_CHECK(nq >= 0 && R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1, RBQ_ERR_INVALID,
-              "bad scan parameters");
+    RBQ_CHECK(nq >= 0 && R >= 1 && R <= 4096 && nprobe >= 1 && slices >= 1 &&
+                  (probe_stride == 0 || probe_stride >= nprobe),
+              RBQ_ERR_INVALID, "bad scan parameters");
     const size_t keys_bytes = round_up_256((size_t)nq * slices * R * 8);
     const size_t merged_bytes = slices > 1 ? round_up_256((size_t)nq * R * 8) : 0;
     RBQ_CHECK(keys_bytes + merged_bytes <= (size_t)RBQ_NOALLOC_SCRATCH_BYTES, RBQ_ERR_INVALID,
@@ -1192,6 +1278,7 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
     ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
                                   prune, slices, ks, stats_dev);
     sa.tau0 = tau0_dev;
+    sa.pstride = probe_stride;
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
     launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);

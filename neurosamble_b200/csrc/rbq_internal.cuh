@@ -91,6 +91,9 @@ struct Index {
   int kmeans_iters = 20;
   int max_train_per_list = 256;
   int shard_rank = 0, shard_count = 1;
+  int shard_policy = RBQ_SHARD_ROUND_ROBIN;
+  bool owners_fixed = false;
+  std::vector<int32_t> owner_host;  // [K] rank holding list l
   float t4 = 0.0f;
   bool trained = false;
 
@@ -118,6 +121,7 @@ struct Index {
   int64_t cap_ids = 0;
   uint32_t* id2row = nullptr;    // [n_total] row of a global id, 0xFFFFFFFF if not on this shard
   int* dev_err = nullptr;        // [1] device-side error code (tensor-core waits that timed out)
+  int32_t* owner = nullptr;      // [K] device copy of owner_host
 
   // Slot order (rebuilt after every add): list l owns slots [list_off[l], list_off[l+1]).
   int64_t* list_off = nullptr;   // [K+1]
@@ -129,6 +133,10 @@ struct Index {
 };
 
 void free_index_memory(Index& ix);
+// The list -> rank map of a policy for list sizes `sizes` (ROUND_ROBIN ignores them).
+std::vector<int32_t> list_owners(int policy, const std::vector<int64_t>& sizes, int count);
+// Uploads the map (allocating the device copy on first use); fixed = final for later adds.
+void install_owners(Index& ix, const std::vector<int32_t>& owners, bool fixed);
 
 // ---------------------------------------------------------------------------------------
 // Host math (rbq_host_math.cpp): rotation and query scaling constant.
@@ -184,7 +192,8 @@ struct ScanArgs {
   int cap;
   int prune;
   int slices;
-  int shard_rank, shard_count;
+  const int32_t* owner;  // [K] rank holding list l; this shard scans lists with owner[l] == shard_rank
+  int shard_rank;
   // Optional seeds.  tau0 [nq]: every slice of query q starts from threshold tau0[q] (default
   // +inf).  init_keys [nq, R] (kEmptyKey = none, any order): candidates of an earlier scan of
   // the same query, loaded into slice 0's buffer; when all R are present the slice starts from

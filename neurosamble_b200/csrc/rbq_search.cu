@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   }
   for (int j = tid; j < 4 * W; j += kScanThreads) pl[j] = a.planes[q * 4 * W + j];
   if (warp == 0) {
-    // The slice's lists: owned probes (l % shard_count == shard_rank) with owned-rank in
+    // The slice's lists: owned probes (owner[l] == shard_rank) with owned-rank in
     // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
     // sequence.
     const int* prow = a.probes + q * a.pstride;
@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     for (int p0 = 0; p0 < a.nprobe; p0 += 32) {
       const int p = p0 + lane;
       const int l = p < a.nprobe ? prow[p] : -1;
-      m += __popc(__ballot_sync(0xffffffffu, l >= 0 && l % a.shard_count == a.shard_rank));
+      m += __popc(__ballot_sync(0xffffffffu, l >= 0 && __ldg(a.owner + l) == a.shard_rank));
     }
     const int pb = (int)(((int64_t)slice * m) / a.slices);
     const int pe = (int)(((int64_t)(slice + 1) * m) / a.slices);
@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     for (int p0 = 0; p0 < a.nprobe && o < pe; p0 += 32) {
       const int p = p0 + lane;
       const int l = p < a.nprobe ? prow[p] : -1;
-      const bool own = l >= 0 && l % a.shard_count == a.shard_rank;
+      const bool own = l >= 0 && __ldg(a.owner + l) == a.shard_rank;
       const unsigned mask = __ballot_sync(0xffffffffu, own);
       const int rank = o + __popc(mask & ((1u << lane) - 1u));
       if (own && rank >= pb && rank < pe) {

@@ -38,7 +38,9 @@ class IndexIVFRaBitQ:
     """1-bit IVF-RaBitQ index with 4-bit query quantisation and optional exact rerank.
 
     Parameters mirror cuvs::neighbors::ivf_rabitq::index_params (ivf_rabitq.hpp:50-103):
-    ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``.
+    ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``;
+    a shard of a sharded index also takes ``shard_rank`` / ``shard_count`` and ``shard_policy``
+    ("round_robin": list l on rank l % count; "balanced": lists spread by size^2 at the first add).
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
@@ -47,7 +49,7 @@ class IndexIVFRaBitQ:
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
                  max_train_points_per_cluster: int = 256, shard_rank: int = 0, shard_count: int = 1,
-                 metric: str = "l2", _handle=None):
+                 metric: str = "l2", shard_policy: str = "round_robin", _handle=None):
         if metric not in ("l2", "ip"):
             raise ValueError("metric must be 'l2' or 'ip'")
         self.d = int(d)
@@ -70,6 +72,9 @@ class IndexIVFRaBitQ:
         p.dim, p.n_lists, p.seed = self.d, self.nlist, int(seed)
         p.kmeans_n_iters, p.max_train_points_per_cluster = int(kmeans_iters), int(max_train_points_per_cluster)
         p.device, p.shard_rank, p.shard_count = self.device, int(shard_rank), int(shard_count)
+        if shard_policy not in _lib.SHARD_POLICIES:
+            raise ValueError(f"shard_policy must be one of {sorted(_lib.SHARD_POLICIES)}")
+        p.shard_policy = _lib.SHARD_POLICIES[shard_policy]
         _lib.call("rbq_index_create", ctypes.byref(p), ctypes.byref(self._h))
 
     # -- lifecycle -----------------------------------------------------------------------
@@ -210,6 +215,12 @@ class IndexIVFRaBitQ:
         fa, fr, fe = (np.empty(n, np.float32) for _ in range(3))
         _lib.call("rbq_export_lists", self._h, *(a.ctypes.data_as(ctypes.c_void_p) for a in (off, ids, codes, fa, fr, fe)))
         return {"list_off": off, "ids": ids, "codes": codes, "fadd": fa, "frescale": fr, "ferr": fe}
+
+    def list_owners(self) -> np.ndarray:
+        """[nlist] int32: the shard holding each list (-1 before a balanced map is fixed)."""
+        own = np.empty(self.nlist, np.int32)
+        _lib.call("rbq_get_list_owners", self._h, own.ctypes.data_as(ctypes.c_void_p))
+        return own
 
     @property
     def query_scale(self) -> float:

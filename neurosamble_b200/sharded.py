@@ -1,6 +1,8 @@
 """List-sharded IVF-RaBitQ over the GPUs of one box: one process per GPU.
 
-List l lives on rank l % world (every rank keeps the full centroid table, rotation and t4).
+Every list lives on one rank (every rank keeps the full centroid table, rotation and t4):
+"balanced" (the default) spreads the lists by size^2 when the first batch is added, so that
+each rank's scan work is about equal; "round_robin" puts list l on rank l % world.
 A search of a batch replicated on every rank runs in four steps:
 
 1. front end, split by query: rank r rotates, coarse-quantises and 4-bit-quantises queries
@@ -118,13 +120,14 @@ def merge_results(dist_all: torch.Tensor, ids_all: torch.Tensor):
 class ShardedIndexIVFRaBitQ:
     """The IndexIVFRaBitQ API over `world` ranks of a process group (NCCL)."""
 
-    def __init__(self, d: int, nlist: int, seed: int = 7, group=None, device: int | None = None, **kw):
+    def __init__(self, d: int, nlist: int, seed: int = 7, group=None, device: int | None = None,
+                 shard_policy: str = "balanced", **kw):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.d, self.nlist = d, nlist
         self.local = IndexIVFRaBitQ(d, nlist, seed=seed, device=device, shard_rank=self.rank,
-                                    shard_count=self.world, **kw)
+                                    shard_count=self.world, shard_policy=shard_policy, **kw)
         self.device = self.local.device
 
     def __getattr__(self, name):
@@ -198,9 +201,11 @@ class LibStages:
             _lib.call("rbq_query_prep", self.h, _ptr(qr), n, _ptr(planes), _ptr(delta), _ptr(k1), self.st)
 
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
+        """probes / g: [nq, p] views with unit column stride and one row stride."""
+        assert probes.stride(1) == 1 and g.stride() == probes.stride()
         with torch.cuda.device(self.device):
             _lib.call("rbq_scan", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0], _ptr(probes),
-                      _ptr(g), probes.shape[1], _ptr(tau0) if tau0 is not None else None,
+                      _ptr(g), probes.shape[1], probes.stride(0), _ptr(tau0) if tau0 is not None else None,
                       _ptr(init[0]) if init is not None else None, _ptr(init[1]) if init is not None else None, R,
                       prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None, self.st)
 
@@ -241,8 +246,7 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     # 2. seed: the nearest probe, scanned by the rank that owns it; min over ranks of the R-th.
     ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
     da = torch.empty((nq, R), dtype=torch.float32, device=dev)
-    stages.scan(qr, planes, delta, k1, probes[:, :1].contiguous(), g[:, :1].contiguous(), None, None, R, int(prune),
-                1, cap, ia, da, stats)
+    stages.scan(qr, planes, delta, k1, probes[:, :1], g[:, :1], None, None, R, int(prune), 1, cap, ia, da, stats)
     tau = da[:, R - 1].contiguous()
     dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
     # 3. the other probes from the shared threshold, starting from the seed candidates; rerank
@@ -250,8 +254,8 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     if P > 1:
         mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
         md = torch.empty((nq, R), dtype=torch.float32, device=dev)
-        stages.scan(qr, planes, delta, k1, probes[:, 1:].contiguous(), g[:, 1:].contiguous(), tau, (ia, da), R,
-                    int(prune), slices, cap, mi, md, stats)
+        stages.scan(qr, planes, delta, k1, probes[:, 1:], g[:, 1:], tau, (ia, da), R, int(prune), slices, cap, mi,
+                    md, stats)
     else:
         mi, md = ia, da
     if k_rerank > 0:

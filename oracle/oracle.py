@@ -63,7 +63,8 @@ def lib():
         L.orc_exact_ip.restype = ctypes.c_float
         L.orc_scan.argtypes = [_i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _i32, _f32p, _u32p,
                                _f32p, _f32p, _i64, _i32p, _f32p, _i32, ctypes.c_void_p, ctypes.c_void_p,
-                               ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64p, _f32p, _i64p]
+                               ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_void_p,
+                               _i64p, _f32p, _i64p]
         L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
         L.orc_l2_exact.restype = ctypes.c_float
         L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
@@ -219,9 +220,10 @@ def exact_ip(q, code) -> float:
 
 
 def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
-         slices=1, shard_rank=0, shard_count=1, with_stats=False, tau0=None, init=None):
+         slices=1, shard_rank=0, shard_count=1, with_stats=False, tau0=None, init=None, owner=None):
     """rbq_scan: top-R (ids, estimated distances) per query.  tau0 [nq] seeds every slice's
-    threshold; init = (ids, dist) [nq, R] are an earlier scan's candidates slice 0 starts from."""
+    threshold; init = (ids, dist) [nq, R] are an earlier scan's candidates slice 0 starts from;
+    owner [K] (default l % shard_count) is the list -> shard map."""
     Qr = _c(Qr, np.float32)
     nq = Qr.shape[0]
     probes, g = _c(probes, np.int32), _c(g, np.float32)
@@ -231,7 +233,10 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
     out_ids = np.empty((nq, R), np.int64)
     out_d = np.empty((nq, R), np.float32)
     stats = np.zeros(2, np.int64)
-    t0 = i0 = d0 = None
+    t0 = i0 = d0 = ow = None
+    if owner is not None:
+        owner = _c(owner, np.int32)
+        ow = owner.ctypes.data_as(ctypes.c_void_p)
     if tau0 is not None:
         tau0 = _c(tau0, np.float32)
         t0 = tau0.ctypes.data_as(ctypes.c_void_p)
@@ -242,8 +247,8 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
     if nq and nprobe:
         lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
                        _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g,
-                       nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, out_ids,
-                       out_d, stats)
+                       nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, ow,
+                       out_ids, out_d, stats)
     elif init is not None:
         out_ids[:], out_d[:] = merge_candidates([(init_i, init_d)], R)
     else:
@@ -276,7 +281,7 @@ def merge_candidates(parts, R):
 
 
 def seeded_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
-                slices=1, shard_rank=0, shard_count=1, with_stats=False, exchange=False):
+                slices=1, shard_rank=0, shard_count=1, with_stats=False, exchange=False, owner=None):
     """The two-phase scan of rbq_search (seeded) and of the sharded search.
 
     Phase A scans each query's nearest probed list alone (on the shard that owns it, one slice);
@@ -286,16 +291,37 @@ def seeded_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_
     index).  exchange=True: the minimum of every shard's phase-A threshold, i.e. the owner's,
     which is what the sharded search's all-reduce hands to every shard."""
     A = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, shard_rank,
-             shard_count, with_stats=True)
+             shard_count, with_stats=True, owner=owner)
     if exchange and shard_count > 1:
         tau = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, 0, 1)[1][:, R - 1]
     else:
         tau = A[1][:, R - 1]
     B = scan(ix, Qr, planes, delta, k1, probes[:, 1:], g[:, 1:], R, tile, cap, prune, slices, shard_rank,
-             shard_count, with_stats=True, tau0=tau, init=A[:2])
+             shard_count, with_stats=True, tau0=tau, init=A[:2], owner=owner)
     if with_stats:
         return B[0], B[1], A[2] + B[2]
     return B[0], B[1]
+
+
+def list_owners(policy: str, sizes, count: int) -> np.ndarray:
+    """The library's list -> shard map (include/rbq.h, RBQ_SHARD_*), restated: "round_robin"
+    puts list l on l % count; "balanced" takes the lists by decreasing size^2 (ties: smaller
+    id) and gives each to the shard with the smallest sum of size^2 so far (ties: smaller rank)."""
+    sizes = np.asarray(sizes, np.int64)
+    K = sizes.size
+    if count <= 1:
+        return np.zeros(K, np.int32)
+    if policy == "round_robin":
+        return (np.arange(K) % count).astype(np.int32)
+    sq = [int(s) * int(s) for s in sizes]
+    order = sorted(range(K), key=lambda l: (-sq[l], l))
+    load = [0] * count
+    own = np.zeros(K, np.int32)
+    for l in order:
+        r = min(range(count), key=lambda j: (load[j], j))
+        own[l] = r
+        load[r] += sq[l]
+    return own
 
 
 def l2_exact(x, q) -> float:
@@ -330,7 +356,7 @@ def assign(X, C) -> np.ndarray:
 
 
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
-           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1):
+           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 
     seeded (rbq_search_params_t.seeded): -1 scans in two phases (seeded_scan) when the probes
@@ -345,10 +371,10 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     two = slices > 1 if seeded < 0 else seeded > 0
     if exchange or (two and nprobe > 1):
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
-                          shard_count, with_stats=True, exchange=exchange)
+                          shard_count, with_stats=True, exchange=exchange, owner=owner)
     else:
         res = scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
-                   shard_count, with_stats=True)
+                   shard_count, with_stats=True, owner=owner)
     cand, cd = res[0], res[1]
     if rerank_depth > 0:
         dist, ids = rerank(ix.X, Q, cand, k)

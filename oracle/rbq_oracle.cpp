@@ -582,17 +582,17 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
 // with threshold tau0[q] instead of +inf (a threshold seeded by an earlier scan).  init_ids /
 // init_dist (optional, [nq, R], id -1 = none): candidates of an earlier scan that slice 0
 // starts from.
-// Lists owned by this shard: l % shard_count == shard_rank, taken in probe order and split into
-// `slices` contiguous ranges (slice s gets owned[floor(s*m/S) : floor((s+1)*m/S)]), each
-// scanned with its own threshold, then merged.
+// Lists owned by this shard: owner[l] == shard_rank (owner NULL: l % shard_count), taken in
+// probe order and split into `slices` contiguous ranges (slice s gets
+// owned[floor(s*m/S) : floor((s+1)*m/S)]), each scanned with its own threshold, then merged.
 // Outputs out_ids [nq, R] (int64, -1 pad) and out_dist [nq, R] (+inf pad).
 // stats (optional, int64[2]): vectors scanned, vectors admitted by the prune.
 void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* codes, const float* fadd,
               const float* frescale, const float* ferr, int Dp, const float* Qr, const uint32_t* planes,
               const float* delta, const float* k1, int64_t nq, const int32_t* probes, const float* gq,
               int nprobe, const float* tau0, const int64_t* init_ids, const float* init_dist, int R, int tile,
-              int cap, int prune, int slices, int shard_rank,
-              int shard_count, int64_t* out_ids, float* out_dist, int64_t* stats)
+              int cap, int prune, int slices, int shard_rank, int shard_count, const int32_t* owner,
+              int64_t* out_ids, float* out_dist, int64_t* stats)
 {
   const int W = Dp / 32;
   ScanIndex ix{list_off, ids, codes, fadd, frescale, ferr};
@@ -610,7 +610,7 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
       own_g.clear();
       for (int p = 0; p < nprobe; ++p) {
         int l = probes[q * nprobe + p];
-        if (l % shard_count == shard_rank) {
+        if ((owner ? owner[l] : l % shard_count) == shard_rank) {
           own_l.push_back(l);
           own_g.push_back(gq[q * nprobe + p]);
         }

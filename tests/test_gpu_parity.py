@@ -174,7 +174,7 @@ def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
     ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
     dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
     stats = torch.zeros(2, dtype=torch.int64, device="cuda")
-    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, None, None, None, R,
+    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, 0, None, None, None, R,
          prune, slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
     p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
     pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
@@ -409,15 +409,48 @@ def test_scan_from_a_seeded_threshold(oracle, case):
     tau[::5] = np.inf  # some queries unseeded
     t0 = torch.from_numpy(tau).cuda()
     ti, td = torch.from_numpy(ai).cuda(), torch.from_numpy(ad).cuda()
-    pb, gb = probes[:, 1:].contiguous(), g[:, 1:].contiguous()
+    pb, gb = probes[:, 1:], g[:, 1:]  # strided views: row stride nprobe
     for slices in (1, 2):
         for with_init in (False, True):
             ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
             dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
             init = (ptr(ti), ptr(td)) if with_init else (None, None)
             call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(pb), ptr(gb),
-                 nprobe - 1, ptr(t0), *init, R, 1, slices, 0, ptr(ids), ptr(dist), None, stream())
+                 nprobe - 1, nprobe, ptr(t0), *init, R, 1, slices, 0, ptr(ids), ptr(dist), None, stream())
             oi, od = oracle.scan(oix, Qr, pl2, d2, k2, p2[:, 1:], g2[:, 1:], R, prune=1, slices=slices, tau0=tau,
                                  init=(ai, ad) if with_init else None)
             assert np.array_equal(ids.cpu().numpy(), oi)
             assert np.array_equal(u32(dist.cpu().numpy()), u32(od))
+
+
+def test_balanced_shards_follow_the_restated_map(oracle, case, tmp_path):
+    """RBQ_SHARD_BALANCED: the map fixed at the first add equals the oracle's restatement, each
+    shard holds exactly its lists and searches them bit-exactly; the map survives save / load,
+    and a full index loaded as one shard derives the same map from its list sizes."""
+    from neurosamble_b200 import IndexIVFRaBitQ, read_index, write_index
+    idx, oix, X, Q, C, lab = case
+    sizes = np.bincount(lab, minlength=64)
+    want = oracle.list_owners("balanced", sizes, 3)
+    assert np.array_equal(oracle.list_owners("round_robin", sizes, 3), np.arange(64) % 3)
+    for r in range(3):
+        sh = IndexIVFRaBitQ(128, 64, seed=7, shard_rank=r, shard_count=3, shard_policy="balanced")
+        assert (sh.list_owners() == -1).all()
+        sh.set_centroids(C)
+        sh.add(X, labels=lab)
+        assert np.array_equal(sh.list_owners(), want)
+        sz = np.diff(sh.export_lists()["list_off"])
+        assert np.array_equal(sz[want == r], sizes[want == r]) and (sz[want != r] == 0).all()
+        sh.nprobe, sh.k_rerank = 8, 40
+        d, i = sh.search(Q, 10)
+        d2, i2 = oracle.search(oix, Q, 10, 8, 40, shard_rank=r, shard_count=3, owner=want)
+        assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+        path = tmp_path / f"s{r}.rbq"
+        write_index(sh, str(path))
+        assert np.array_equal(read_index(str(path)).list_owners(), want)
+    full = IndexIVFRaBitQ(128, 64, seed=7, shard_policy="balanced")
+    full.set_centroids(C)
+    full.add(X, labels=lab)
+    assert (full.list_owners() == 0).all()
+    path = tmp_path / "full.rbq"
+    write_index(full, str(path))
+    assert np.array_equal(read_index(str(path), shard_rank=1, shard_count=3).list_owners(), want)

@@ -115,8 +115,8 @@ class _OracleStages:
     CPU tensors: lets the product's sharded orchestration (front-end split, record all-gather,
     seed all-reduce, result all-gather) run over gloo without a GPU."""
 
-    def __init__(self, O, ix, rank, world):
-        self.O, self.ix, self.rank, self.world = O, ix, rank, world
+    def __init__(self, O, ix, rank, world, owner=None):
+        self.O, self.ix, self.rank, self.world, self.owner = O, ix, rank, world, owner
 
     def front(self, q, margin, qr, probes, g, planes, delta, k1):
         import torch
@@ -137,7 +137,8 @@ class _OracleStages:
                              probes.numpy(), g.numpy(), R, cap=cap, prune=prune, slices=slices,
                              shard_rank=self.rank, shard_count=self.world,
                              tau0=tau0.numpy() if tau0 is not None else None,
-                             init=(init[0].numpy(), init[1].numpy()) if init is not None else None)
+                             init=(init[0].numpy(), init[1].numpy()) if init is not None else None,
+                             owner=self.owner)
         ids.copy_(torch.from_numpy(oi))
         d.copy_(torch.from_numpy(od))
 
@@ -154,7 +155,7 @@ class _OracleStages:
         out_i.copy_(torch.from_numpy(ii))
 
 
-def _seeded_worker(rank, world, port, outdir, nq, prune):
+def _seeded_worker(rank, world, port, outdir, nq, prune, policy):
     import torch
     import torch.distributed as dist
 
@@ -170,16 +171,18 @@ def _seeded_worker(rank, world, port, outdir, nq, prune):
     P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
     C, lab = O.kmeans(X, 24, iters=3)
     ix = O.build(X, C, lab, P, t4)
-    d, i = sharded_search(_OracleStages(O, ix, rank, world), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0, 64,
-                          rank, world)
+    owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
+    d, i = sharded_search(_OracleStages(O, ix, rank, world, owner), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0,
+                          64, rank, world)
     with open(os.path.join(outdir, f"rank{rank}.pkl"), "wb") as f:
         pickle.dump((d.numpy(), i.numpy()), f)
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,nq,prune", [(2, 40, 1), (3, 7, 1), (2, 40, 0)])
-def test_seeded_sharded_search_over_gloo(world, nq, prune):
+@pytest.mark.parametrize("world,nq,prune,policy", [(2, 40, 1, "balanced"), (3, 7, 1, "round_robin"),
+                                                   (2, 40, 0, "balanced")])
+def test_seeded_sharded_search_over_gloo(world, nq, prune, policy):
     """The orchestration (queries split for the front end and padded, records all-gathered,
     seeds all-reduced, results all-gathered and merged) gives, on every rank, the merge of the
     oracle's per-shard searches with the shared seed.  With the prune off every shard keeps its
@@ -190,7 +193,7 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune):
     from neurosamble_b200.sharded import plan
 
     with tempfile.TemporaryDirectory() as td:
-        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune), nprocs=world, join=True)
+        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy), nprocs=world, join=True)
         res = [pickle.load(open(os.path.join(td, f"rank{r}.pkl"), "rb")) for r in range(world)]
     X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
     Q = Q[:nq]
@@ -198,8 +201,9 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune):
     C, lab = O.kmeans(X, 24, iters=3)
     ix = O.build(X, C, lab, P, t4)
     slices = plan(nq, 8, 10, 60, 0, 0, world)[1]
-    parts = [O.search(ix, Q, 10, 8, 60, prune=prune, slices=slices, shard_rank=r, shard_count=world, exchange=True)
-             for r in range(world)]
+    owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
+    parts = [O.search(ix, Q, 10, 8, 60, prune=prune, slices=slices, shard_rank=r, shard_count=world, exchange=True,
+                      owner=owner) for r in range(world)]
     want_i, want_d = O.merge_candidates([(p[1], p[0]) for p in parts], 10)
     for d, i in res:
         assert np.array_equal(i, want_i)

@@ -181,3 +181,18 @@ def test_seed_is_shared_and_keeps_shards_pruning(oracle, small):
     a = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, exchange=True)
     b = oracle.seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, exchange=False)
     assert np.array_equal(a[0], b[0])
+
+
+def test_balanced_list_owners_restated(oracle):
+    """The balanced map: every list placed, ties resolved by list id then rank, and no shard's
+    sum of size^2 exceeds another's by more than the largest single size^2."""
+    rng = np.random.default_rng(5)
+    sizes = rng.integers(0, 3000, 300)
+    sizes[:4] = [2500, 2500, 0, 0]
+    for count in (1, 2, 3, 8):
+        own = oracle.list_owners("balanced", sizes, count)
+        assert own.shape == (300,) and own.min() >= 0 and own.max() < count
+        load = np.bincount(own, weights=sizes.astype(np.float64) ** 2, minlength=count)
+        assert load.max() - load.min() <= float(sizes.max()) ** 2
+    assert oracle.list_owners("balanced", [5, 5, 3], 2).tolist() == [0, 1, 0]
+    assert oracle.list_owners("balanced", [3, 5, 5], 2).tolist() == [0, 0, 1]
