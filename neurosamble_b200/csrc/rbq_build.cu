@@ -16,18 +16,19 @@ namespace rbq {
 // gpu_index/rotator_gpu.cu:162-176 computes the same product with cuBLAS sgemm).
 // Each output is float(sum_k double(x_k) * double(P[k][j])) accumulated for k = 0..Dp-1;
 // the float*float product is exact in double, so DFMA and DMUL+DADD give the same bits.
-// Block: RB rows x all Dp columns; thread t owns columns t, t+blockDim, ...
-// ---------------------------------------------------------------------------------------
+// Block: RB rows x all Dp columns; thread t owns columns t, t+blockDim, ...  The block's rows
+// are staged in shared memory already widened to double, so the k loop issues one P load and
+// one widening per thread and RB DFMAs against broadcast shared-memory reads.
 template <int RB, int CPT>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X, int64_t n, int D, int Dp,
                                                      const float* __restrict__ P, float* __restrict__ Y)
 {
-  extern __shared__ float xs[];  // [RB][Dp]
+  extern __shared__ __align__(16) double xs[];  // [RB][Dp]
   const int64_t r0 = (int64_t)blockIdx.x * RB;
   for (int i = threadIdx.x; i < RB * Dp; i += blockDim.x) {
     const int r = i / Dp, k = i - r * Dp;
     const int64_t row = r0 + r;
-    xs[i] = (row < n && k < D) ? X[row * D + k] : 0.0f;
+    xs[i] = (row < n && k < D) ? (double)X[row * D + k] : 0.0;
   }
   __syncthreads();
   double acc[RB][CPT];
@@ -35,18 +36,22 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X
   for (int r = 0; r < RB; ++r)
 #pragma unroll
     for (int c = 0; c < CPT; ++c) acc[r][c] = 0.0;
-  for (int k = 0; k < Dp; ++k) {
-    double p[CPT];
+  for (int k = 0; k < Dp; k += 2) {  // Dp is even: rows are read two k at a time (16-byte loads)
+    double p0[CPT], p1[CPT];
 #pragma unroll
     for (int c = 0; c < CPT; ++c) {
       const int j = threadIdx.x + c * blockDim.x;
-      p[c] = (j < Dp) ? (double)P[(size_t)k * Dp + j] : 0.0;
+      p0[c] = (j < Dp) ? (double)__ldg(P + (size_t)k * Dp + j) : 0.0;
+      p1[c] = (j < Dp) ? (double)__ldg(P + (size_t)(k + 1) * Dp + j) : 0.0;
     }
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
-      const double xv = (double)xs[r * Dp + k];
+      const double2 xv = *reinterpret_cast<const double2*>(xs + r * Dp + k);
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) acc[r][c] = __fma_rn(xv, p[c], acc[r][c]);
+      for (int c = 0; c < CPT; ++c) {
+        acc[r][c] = __fma_rn(xv.x, p0[c], acc[r][c]);
+        acc[r][c] = __fma_rn(xv.y, p1[c], acc[r][c]);
+      }
     }
   }
 #pragma unroll
@@ -61,32 +66,32 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X
   }
 }
 
+template <int RB, int CPT>
+static void launch_rotate_rc(const float* X, int64_t n, int D, int Dp, const float* P, float* Y, int threads,
+                             cudaStream_t s)
+{
+  const size_t smem = (size_t)RB * Dp * sizeof(double);
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(rotate_kernel<RB, CPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rotate_kernel<RB, CPT><<<(unsigned)ceil_div(n, RB), threads, smem, s>>>(X, n, D, Dp, P, Y);
+  RBQ_LAUNCHED();
+}
+
 void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, float* Y, cudaStream_t s)
 {
   if (n <= 0) return;
-  constexpr int RB = 8;
   const int threads = Dp < 256 ? Dp : 256;
   const int cpt = (Dp + threads - 1) / threads;
-  const size_t smem = (size_t)RB * Dp * sizeof(float);
-  const unsigned grid = (unsigned)ceil_div(n, RB);
+  // Rows per block: 64 KB of staged rows at most (16 rows up to Dp = 512, 8 to 1024, then 4).
   switch (cpt) {
-#define RBQ_ROT_CASE(C)                                                                               \
-  case C:                                                                                             \
-    if (smem > 48 * 1024)                                                                             \
-      RBQ_CUDA(cudaFuncSetAttribute(rotate_kernel<RB, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                    (int)smem));                                                      \
-    rotate_kernel<RB, C><<<grid, threads, smem, s>>>(X, n, D, Dp, P, Y);                              \
-    break;
-    RBQ_ROT_CASE(1)
-    RBQ_ROT_CASE(2)
-    RBQ_ROT_CASE(3)
-    RBQ_ROT_CASE(4)
-    RBQ_ROT_CASE(6)
-    RBQ_ROT_CASE(8)
-#undef RBQ_ROT_CASE
+    case 1: launch_rotate_rc<16, 1>(X, n, D, Dp, P, Y, threads, s); break;
+    case 2: launch_rotate_rc<16, 2>(X, n, D, Dp, P, Y, threads, s); break;
+    case 3: launch_rotate_rc<8, 3>(X, n, D, Dp, P, Y, threads, s); break;
+    case 4: launch_rotate_rc<8, 4>(X, n, D, Dp, P, Y, threads, s); break;
+    case 6: launch_rotate_rc<4, 6>(X, n, D, Dp, P, Y, threads, s); break;
+    case 8: launch_rotate_rc<4, 8>(X, n, D, Dp, P, Y, threads, s); break;
     default: throw Error{RBQ_ERR_INVALID, "rotation: padded dim must be <= 2048 with Dp/256 in {1,2,3,4,6,8}"};
   }
-  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------

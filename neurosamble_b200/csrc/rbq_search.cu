@@ -222,17 +222,29 @@ void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const
 // ---------------------------------------------------------------------------------------
 // 4-bit query quantisation (exrabitq_quantize_query<256> with EX_BITS = 4,
 // searcher_gpu_quantize_query.cu:655-793) and k1 = -0.5 * sum q (ivf_gpu.cu:1451-1490).
-// One thread per query; sums are double accumulations in dimension order.
+// One thread per query; sums are double accumulations in dimension order.  A block of 32
+// queries first stages its rows in shared memory (coalesced loads; rows padded by one float so
+// that the 32 threads reading column j hit 32 banks).
 //   code_j = clamp(rint(t4 * (q_j * (1/|q|))), -8, 7)
 //   delta = (|q| / |code|) * (<q, code> / (|q| * |code|))   (0 if either norm <= 1e-6)
 //   plane b, word w, bit 31-j = bit b of (code_{32w+j} & 0xF)
 // ---------------------------------------------------------------------------------------
-__global__ void query_prep_kernel(const float* __restrict__ Qr, int64_t nq, int Dp, float t4,
-                                  uint32_t* __restrict__ planes, float* __restrict__ delta, float* __restrict__ k1)
+constexpr int kPrepQueries = 32;
+
+__global__ void __launch_bounds__(kPrepQueries) query_prep_kernel(const float* __restrict__ Qr, int64_t nq, int Dp,
+                                                                  float t4, uint32_t* __restrict__ planes,
+                                                                  float* __restrict__ delta, float* __restrict__ k1)
 {
-  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= nq) return;
-  const float* x = Qr + q * Dp;
+  extern __shared__ float rows[];  // [kPrepQueries][Dp + 1]
+  const int64_t q0 = (int64_t)blockIdx.x * kPrepQueries;
+  const int nb = (int)(nq - q0 < kPrepQueries ? nq - q0 : kPrepQueries);
+  const int ld = Dp + 1;
+  for (int r = 0; r < nb; ++r)
+    for (int j = threadIdx.x; j < Dp; j += kPrepQueries) rows[r * ld + j] = Qr[(q0 + r) * Dp + j];
+  __syncthreads();
+  if ((int)threadIdx.x >= nb) return;
+  const int64_t q = q0 + threadIdx.x;
+  const float* x = rows + threadIdx.x * ld;
   double s2 = 0.0, s1 = 0.0;
   for (int j = 0; j < Dp; ++j) {
     const double v = (double)x[j];
@@ -282,7 +294,11 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* 
                        cudaStream_t s)
 {
   if (nq <= 0) return;
-  query_prep_kernel<<<(unsigned)ceil_div(nq, 128), 128, 0, s>>>(Qr, nq, Dp, t4, planes, delta, k1);
+  const size_t smem = (size_t)kPrepQueries * (Dp + 1) * sizeof(float);
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(query_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  query_prep_kernel<<<(unsigned)ceil_div(nq, kPrepQueries), kPrepQueries, smem, s>>>(Qr, nq, Dp, t4, planes, delta,
+                                                                                       k1);
   RBQ_LAUNCHED();
 }
 
@@ -301,8 +317,10 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* 
 //            xor butterfly);
 //            dist = (f_add + g) + f_rescale * (exact_ip + k1); keep (dist, id) if dist <= tau.
 // tau (the R-th best kept distance) only changes between tiles: when the buffer holds more
-// than cap - kScanTile keys it is sorted and cut to R.  The schedule depends on the data
-// alone, so results are deterministic and equal to the oracle's.
+// than cap - kScanTile keys, 2R keys, or R keys while tau is still +inf, it is cut to the R
+// smallest.  A slice starts from tau0 (if given), slice 0 from the initial candidates (if
+// given), and a pruning slice with neither from the bound seed below.  The schedule depends on
+// the data alone, so results are deterministic and equal to the oracle's.
 // ---------------------------------------------------------------------------------------
 constexpr int kScanThreads = 256;
 constexpr int kScanVpt = kScanTile / kScanThreads;

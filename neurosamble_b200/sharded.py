@@ -5,15 +5,16 @@ Every list lives on one rank (every rank keeps the full centroid table, rotation
 each rank's scan work is about equal; "round_robin" puts list l on rank l % world.
 A search of a batch replicated on every rank runs in four steps:
 
-1. front end, split by query: rank r rotates, coarse-quantises and 4-bit-quantises queries
-   [r*nl, (r+1)*nl) (nl = ceil(nq / world)); one all-gather hands every rank the records
-   (rotated query, planes, delta, k1, probes, g) of the whole batch;
+1. front end: every rank rotates and 4-bit-quantises the whole batch (cheap, and it spares
+   moving 1 KB of rotated query per query), but coarse-quantises only queries
+   [r*nl, (r+1)*nl) (nl = ceil(nq / world)); one all-gather of [probes | g] rows hands every
+   rank the probes of the whole batch;
 2. seed: each rank scans the nearest probed list of the queries whose nearest list it owns;
    an all-reduce (min) of the per-query R-th estimate gives every rank the threshold a
    single GPU reaches after that list, so a shard prunes its lists as tightly as one GPU
    prunes all of them (without it a shard far from the query admits most of its vectors);
-3. scan the remaining probes from that threshold, merge with the seed keys, rerank the
-   shard's candidates (only those under the threshold survive, ~R / world per shard);
+3. scan the remaining probes from that threshold, starting from the seed candidates, and
+   rerank the shard's candidates (only those under the threshold survive, ~R / world each);
 4. the per-rank [nq, k] results cross NVLink in one all-gather (one packed buffer per rank)
    and are merged on the device by (distance, id).
 
@@ -49,31 +50,6 @@ def plan(nq: int, nprobe: int, k: int, k_rerank: int, probe_split: int, cand_cap
     sl = max(1, min(sl, own, max(1, 8192 // R)))
     cap = max(_pow2(cand_cap if cand_cap > 0 else 1024), _pow2(R + SCAN_TILE))
     return R, sl, cap
-
-
-def front_layout(nl: int, dp: int, nprobe: int):
-    """Byte layout of one rank's block of front-end records for nl queries (256-B aligned
-    fields): name -> (offset, bytes per query, dtype, per-query shape); and the block size."""
-    w = dp // 32
-    fields = [("qr", 4 * dp, torch.float32, (dp,)), ("planes", 16 * w, torch.int32, (4, w)),
-              ("delta", 4, torch.float32, ()), ("k1", 4, torch.float32, ()),
-              ("probes", 4 * nprobe, torch.int32, (nprobe,)), ("g", 4 * nprobe, torch.float32, (nprobe,))]
-    out, off = {}, 0
-    for name, rb, dt, shape in fields:
-        out[name] = (off, rb, dt, shape)
-        off += (nl * rb + 255) // 256 * 256
-    return out, off
-
-
-def _field(buf: torch.Tensor, lay, name: str, n: int) -> torch.Tensor:
-    off, rb, dt, shape = lay[name]
-    return buf[off: off + n * rb].view(dt).view(n, *shape)
-
-
-def _gathered_field(per: torch.Tensor, lay, name: str, nl: int, nq: int) -> torch.Tensor:
-    """[world, block] gathered bytes -> the field for queries [0, nq), contiguous."""
-    off, rb, dt, shape = lay[name]
-    return per[:, off: off + nl * rb].contiguous().view(dt).view(-1, *shape)[:nq]
 
 
 def pack_results(dist_t: torch.Tensor, ids_t: torch.Tensor) -> torch.Tensor:
@@ -193,12 +169,16 @@ class LibStages:
         self.device = index.device
         self.st = _stream_ptr(index.device)
 
-    def front(self, q, margin, qr, probes, g, planes, delta, k1):
-        n, nprobe = q.shape[0], probes.shape[1]
+    def rotate_prep(self, q, qr, planes, delta, k1):
+        n = q.shape[0]
         with torch.cuda.device(self.device):
             _lib.call("rbq_rotate", self.h, _ptr(q), n, _ptr(qr), self.st)
-            _lib.call("rbq_coarse", self.h, _ptr(qr), n, nprobe, margin, _ptr(probes), _ptr(g), self.st)
             _lib.call("rbq_query_prep", self.h, _ptr(qr), n, _ptr(planes), _ptr(delta), _ptr(k1), self.st)
+
+    def coarse(self, qr, margin, probes, g):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_coarse", self.h, _ptr(qr), qr.shape[0], probes.shape[1], margin, _ptr(probes), _ptr(g),
+                      self.st)
 
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
         """probes / g: [nq, p] views with unit column stride and one row stride."""
@@ -230,19 +210,23 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     R, slices, cap = plan(nq, P, k, k_rerank, probe_split, cand_cap, world)
     nl = (nq + world - 1) // world
     lo, hi = min(nq, rank * nl), min(nq, (rank + 1) * nl)
-    lay, blk = front_layout(nl, dp, P)
-    # 1. front end of this rank's queries (padded with copies of the last query), all-gathered.
-    send = torch.empty(blk, dtype=torch.uint8, device=dev)
-    qloc = t[lo:hi]
+    # 1. front end: rotation and query planes of the whole batch; probes of this rank's
+    #    queries (padded with copies of the last query), all-gathered as [probes | g] rows.
+    qr = torch.empty((nq, dp), dtype=torch.float32, device=dev)
+    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
+    delta = torch.empty(nq, dtype=torch.float32, device=dev)
+    k1 = torch.empty(nq, dtype=torch.float32, device=dev)
+    stages.rotate_prep(t, qr, planes, delta, k1)
+    qloc = qr[lo:hi]
     if hi - lo < nl:
-        qloc = torch.cat([qloc, t[nq - 1:].expand(nl - (hi - lo), t.shape[1])])
-    stages.front(qloc.contiguous(), margin, *(_field(send, lay, f, nl)
-                                              for f in ("qr", "probes", "g", "planes", "delta", "k1")))
-    recv = torch.empty(world * blk, dtype=torch.uint8, device=dev)
+        qloc = torch.cat([qloc, qr[nq - 1:].expand(nl - (hi - lo), dp)])
+    pl = torch.empty((nl, P), dtype=torch.int32, device=dev)
+    gl = torch.empty((nl, P), dtype=torch.float32, device=dev)
+    stages.coarse(qloc.contiguous(), margin, pl, gl)
+    send = torch.cat([pl, gl.view(torch.int32)], dim=1)
+    recv = torch.empty((world * nl, 2 * P), dtype=torch.int32, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
-    per = recv.view(world, blk)
-    qr, planes, delta, k1, probes, g = (_gathered_field(per, lay, f, nl, nq)
-                                        for f in ("qr", "planes", "delta", "k1", "probes", "g"))
+    probes, g = recv[:nq, :P], recv[:nq, P:].view(torch.float32)  # row stride 2P
     # 2. seed: the nearest probe, scanned by the rank that owns it; min over ranks of the R-th.
     ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
     da = torch.empty((nq, R), dtype=torch.float32, device=dev)

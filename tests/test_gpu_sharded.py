@@ -47,10 +47,14 @@ def _rank_main(rank, world, port, outdir):
     idx.local.set_centroids(C)
     idx.add(X, labels=lab)
     idx.nprobe, idx.k_rerank, idx.probe_split = 12, 40, 1
-    d, i = idx.search(Q, 10)
+    st = torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}")
+    d, i = idx.search(Q, 10, stats=st)
+    stats = [torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}") for _ in range(world)]
+    dist.all_gather(stats, st)
     if rank == 0:
         with open(os.path.join(outdir, "res.pkl"), "wb") as f:
-            pickle.dump((d, i, C, lab, idx.local.rotation(), idx.local.query_scale, X, Q, idx.local.list_owners()), f)
+            pickle.dump((d, i, C, lab, idx.local.rotation(), idx.local.query_scale, X, Q, idx.local.list_owners(),
+                         [s.cpu().numpy() for s in stats]), f)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -60,12 +64,14 @@ def test_two_gpu_sharded_search_matches_oracle(oracle):
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(_rank_main, args=(2, _port(), td), nprocs=2, join=True)
-        d, i, C, lab, P, t4, X, Q, owners = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
+        d, i, C, lab, P, t4, X, Q, owners, stats = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
     oix = oracle.build(X, C, lab, P, t4)
     want = oracle.list_owners("balanced", np.bincount(lab, minlength=64), 2)
     assert np.array_equal(owners, want)  # the default policy of the sharded index
-    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1, exchange=True, owner=want)
-             for r in range(2)]
+    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1, exchange=True, owner=want,
+                           with_stats=True) for r in range(2)]
+    for r in range(2):  # vectors scanned / admitted per shard: the shared threshold is the owner's
+        assert np.array_equal(stats[r], parts[r][2]), (r, stats[r], parts[r][2])
     want_i, want_d = oracle.merge_candidates([(p[1], p[0]) for p in parts], 10)
     assert np.array_equal(i, want_i)
     assert np.array_equal(d.view(np.uint32), want_d.view(np.uint32))

@@ -118,18 +118,21 @@ class _OracleStages:
     def __init__(self, O, ix, rank, world, owner=None):
         self.O, self.ix, self.rank, self.world, self.owner = O, ix, rank, world, owner
 
-    def front(self, q, margin, qr, probes, g, planes, delta, k1):
+    def rotate_prep(self, q, qr, planes, delta, k1):
         import torch
         O, ix = self.O, self.ix
         Qr = O.rotate(q.numpy(), ix.P)
-        p, gg = O.coarse(Qr, ix.c_rot, probes.shape[1])
         pl, de, kk, _ = O.query_prep(Qr, ix.t4)
         qr.copy_(torch.from_numpy(Qr))
-        probes.copy_(torch.from_numpy(p))
-        g.copy_(torch.from_numpy(gg))
         planes.copy_(torch.from_numpy(np.ascontiguousarray(pl).view(np.int32).reshape(planes.shape)))
         delta.copy_(torch.from_numpy(de))
         k1.copy_(torch.from_numpy(kk))
+
+    def coarse(self, qr, margin, probes, g):
+        import torch
+        p, gg = self.O.coarse(qr.numpy(), self.ix.c_rot, probes.shape[1])
+        probes.copy_(torch.from_numpy(p))
+        g.copy_(torch.from_numpy(gg))
 
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
         import torch
@@ -183,11 +186,11 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy):
 @pytest.mark.parametrize("world,nq,prune,policy", [(2, 40, 1, "balanced"), (3, 7, 1, "round_robin"),
                                                    (2, 40, 0, "balanced")])
 def test_seeded_sharded_search_over_gloo(world, nq, prune, policy):
-    """The orchestration (queries split for the front end and padded, records all-gathered,
-    seeds all-reduced, results all-gathered and merged) gives, on every rank, the merge of the
-    oracle's per-shard searches with the shared seed.  With the prune off every shard keeps its
-    exact top-R by estimate, so the shards' candidates contain the single-shard top-R and the
-    reranked distances are, rank by rank, no larger than the single-shard search's."""
+    """The orchestration (queries split for the coarse quantiser and padded, probe rows
+    all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
+    merge of the oracle's per-shard searches with the shared seed.  With the prune off every
+    shard keeps its exact top-R by estimate, so the shards' candidates contain the single-shard
+    top-R and the reranked distances are, rank by rank, no larger than the single-shard's."""
     from conftest import mixture
     from oracle import oracle as O
     from neurosamble_b200.sharded import plan
