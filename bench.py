@@ -315,9 +315,11 @@ def run_ours(args, cfg):
         flush.zero_()
         step_device()
     barrier()
-    times = []
     launches0 = _lib.lib().rbq_kernel_launches()
     torch.cuda.nvtx.range_push("timed")
+    # Steps are queued back to back (the host runs ahead of the GPU, as a serving loop does);
+    # each step's events bracket its search only, not the L2 flush before it.
+    evs = []
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             flush.zero_()
@@ -325,10 +327,11 @@ def run_ours(args, cfg):
             e0.record(stream)
             step_device()
             e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
+            evs.append((e0, e1))
+        torch.cuda.synchronize(dev)
     torch.cuda.nvtx.range_pop()
     barrier()
+    times = [a.elapsed_time(b) for a, b in evs]
     launches = _lib.lib().rbq_kernel_launches() - launches0
     ms = float(np.mean(times))
     if world > 1:

@@ -17,12 +17,14 @@ namespace rbq {
 // Each output is float(sum_k double(x_k) * double(P[k][j])) accumulated for k = 0..Dp-1;
 // the float*float product is exact in double, so DFMA and DMUL+DADD give the same bits.
 // Block: RB rows x all Dp columns; thread t owns columns t, t+blockDim, ...  The block's rows
-// are staged in shared memory already widened to double, so the k loop issues one P load and
-// one widening per thread and RB DFMAs against broadcast shared-memory reads.
+// are staged in shared memory already widened to double (read two k at a time, 16-byte
+// broadcasts); the thread's P values stream from L2 four k ahead of their use, so the DFMAs of
+// one step overlap the loads of the next.
 template <int RB, int CPT>
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X, int64_t n, int D, int Dp,
                                                      const float* __restrict__ P, float* __restrict__ Y)
 {
+  constexpr int KU = 4;  // k per step (Dp is a multiple of 32)
   extern __shared__ __align__(16) double xs[];  // [RB][Dp]
   const int64_t r0 = (int64_t)blockIdx.x * RB;
   for (int i = threadIdx.x; i < RB * Dp; i += blockDim.x) {
@@ -36,21 +38,34 @@ __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X
   for (int r = 0; r < RB; ++r)
 #pragma unroll
     for (int c = 0; c < CPT; ++c) acc[r][c] = 0.0;
-  for (int k = 0; k < Dp; k += 2) {  // Dp is even: rows are read two k at a time (16-byte loads)
-    double p0[CPT], p1[CPT];
+  float pn[KU][CPT];
+  auto load_p = [&](int k0) {
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) {
-      const int j = threadIdx.x + c * blockDim.x;
-      p0[c] = (j < Dp) ? (double)__ldg(P + (size_t)k * Dp + j) : 0.0;
-      p1[c] = (j < Dp) ? (double)__ldg(P + (size_t)(k + 1) * Dp + j) : 0.0;
-    }
-#pragma unroll
-    for (int r = 0; r < RB; ++r) {
-      const double2 xv = *reinterpret_cast<const double2*>(xs + r * Dp + k);
+    for (int u = 0; u < KU; ++u)
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
-        acc[r][c] = __fma_rn(xv.x, p0[c], acc[r][c]);
-        acc[r][c] = __fma_rn(xv.y, p1[c], acc[r][c]);
+        const int j = threadIdx.x + c * blockDim.x;
+        pn[u][c] = (j < Dp && k0 + u < Dp) ? __ldg(P + (size_t)(k0 + u) * Dp + j) : 0.0f;
+      }
+  };
+  load_p(0);
+  for (int k = 0; k < Dp; k += KU) {
+    double p[KU][CPT];
+#pragma unroll
+    for (int u = 0; u < KU; ++u)
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) p[u][c] = (double)pn[u][c];
+    load_p(k + KU);
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+#pragma unroll
+      for (int u = 0; u < KU; u += 2) {
+        const double2 xv = *reinterpret_cast<const double2*>(xs + r * Dp + k + u);
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          acc[r][c] = __fma_rn(xv.x, p[u][c], acc[r][c]);
+          acc[r][c] = __fma_rn(xv.y, p[u + 1][c], acc[r][c]);
+        }
       }
     }
   }

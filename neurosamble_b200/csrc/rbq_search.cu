@@ -1130,10 +1130,76 @@ __global__ void __launch_bounds__(256) merge_results_kernel(const float* __restr
   }
 }
 
+// Small merges (parts * k <= 32 * L): one warp per query holds the candidates in registers and
+// takes the k smallest keys by k rounds of a warp-wide minimum; the lowest lane holding the
+// minimum drops one copy of it, so the result equals the sort's first k.
+template <int L>
+__global__ void __launch_bounds__(256) merge_results_warp_kernel(const float* __restrict__ dist,
+                                                                 const int64_t* __restrict__ ids, int parts,
+                                                                 int64_t nq, int k, float* __restrict__ out_dist,
+                                                                 int64_t* __restrict__ out_ids)
+{
+  const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (q >= nq) return;
+  const int n = parts * k;
+  unsigned long long v[L];
+#pragma unroll
+  for (int i = 0; i < L; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = kEmptyKey;
+    if (e < n) {
+      const int p = e / k, r = e - p * k;
+      const size_t at = ((size_t)p * nq + q) * k + r;
+      if (ids[at] >= 0) v[i] = make_key(dist[at], (uint32_t)ids[at]);
+    }
+  }
+  for (int o = 0; o < k; ++o) {
+    unsigned long long m = v[0];
+#pragma unroll
+    for (int i = 1; i < L; ++i) m = v[i] < m ? v[i] : m;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, m, off);
+      m = t < m ? t : m;
+    }
+    if (m != kEmptyKey) {
+      bool has = false;
+#pragma unroll
+      for (int i = 0; i < L; ++i) has |= v[i] == m;
+      const unsigned who = __ballot_sync(0xffffffffu, has);
+      if (lane == __ffs(who) - 1) {
+        bool done = false;
+#pragma unroll
+        for (int i = 0; i < L; ++i)
+          if (!done && v[i] == m) {
+            v[i] = kEmptyKey;
+            done = true;
+          }
+      }
+    }
+    if (lane == 0) {
+      out_ids[q * k + o] = m == kEmptyKey ? -1 : (int64_t)(m & 0xFFFFFFFFu);
+      out_dist[q * k + o] = m == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(m >> 32));
+    }
+  }
+}
+
 void launch_merge_results(const float* dist, const int64_t* ids, int parts, int64_t nq, int k, float* out_dist,
                           int64_t* out_ids, cudaStream_t s)
 {
   if (nq <= 0) return;
+  if ((int64_t)parts * k <= 32 * 8) {
+    const unsigned grid = (unsigned)ceil_div(nq * 32, 256);
+    if (parts * k <= 32 * 2)
+      merge_results_warp_kernel<2><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+    else if (parts * k <= 32 * 4)
+      merge_results_warp_kernel<4><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+    else
+      merge_results_warp_kernel<8><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+    RBQ_LAUNCHED();
+    return;
+  }
   const int n2 = next_pow2(parts * k < 2 ? 2 : parts * k);
   const size_t smem = (size_t)n2 * 8;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "merge: parts * k too large");

@@ -454,3 +454,24 @@ def test_balanced_shards_follow_the_restated_map(oracle, case, tmp_path):
     path = tmp_path / "full.rbq"
     write_index(full, str(path))
     assert np.array_equal(read_index(str(path), shard_rank=1, shard_count=3).list_owners(), want)
+
+
+@pytest.mark.parametrize("parts,k", [(2, 10), (8, 10), (3, 40), (8, 30), (8, 100)])
+def test_merge_results_matches_oracle(oracle, parts, k):
+    """rbq_merge_results ([parts, nq, k] -> [nq, k] by (distance, id)): the warp path for small
+    merges and the block sort for large ones, with empty slots and a key present in two parts."""
+    torch = _torch()
+    rng = np.random.default_rng(parts * 1000 + k)
+    nq = 77
+    d = rng.standard_normal((parts, nq, k)).astype(np.float32)
+    i = rng.integers(0, 1 << 31, (parts, nq, k)).astype(np.int64)
+    i[:, ::3, k // 2:] = -1
+    d[:, ::3, k // 2:] = np.inf
+    d[0, 1, 0], i[0, 1, 0] = d[parts - 1, 1, 1], i[parts - 1, 1, 1]  # duplicate key
+    od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    oi = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    dd, ii = torch.from_numpy(d).cuda(), torch.from_numpy(i).cuda()
+    call("rbq_merge_results", ptr(dd), ptr(ii), parts, nq, k, ptr(od), ptr(oi), stream())
+    wi, wd = oracle.merge_candidates([(i[p], d[p]) for p in range(parts)], k)
+    assert np.array_equal(oi.cpu().numpy(), wi)
+    assert np.array_equal(u32(od.cpu().numpy()), u32(wd))
