@@ -21,7 +21,7 @@ namespace rbq {
 // broadcasts); the thread's P values stream from L2 four k ahead of their use, so the DFMAs of
 // one step overlap the loads of the next.
 template <int RB, int CPT>
-__global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ X, int64_t n, int D, int Dp,
+__global__ void __launch_bounds__(256, (CPT <= 2 ? 3 : 2)) rotate_kernel(const float* __restrict__ X, int64_t n, int D, int Dp,
                                                      const float* __restrict__ P, float* __restrict__ Y)
 {
   constexpr int KU = 4;  // k per step (Dp is a multiple of 32)
@@ -97,14 +97,15 @@ void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, flo
   if (n <= 0) return;
   const int threads = Dp < 256 ? Dp : 256;
   const int cpt = (Dp + threads - 1) / threads;
-  // Rows per block: 64 KB of staged rows at most (16 rows up to Dp = 512, 8 to 1024, then 4).
+  // Rows per block: at most 8 (RB * CPT double accumulators per thread), sized so that the
+  // thread's accumulators and four k of prefetched P fit three (CPT <= 2) or two blocks per SM.
   switch (cpt) {
-    case 1: launch_rotate_rc<16, 1>(X, n, D, Dp, P, Y, threads, s); break;
-    case 2: launch_rotate_rc<16, 2>(X, n, D, Dp, P, Y, threads, s); break;
-    case 3: launch_rotate_rc<8, 3>(X, n, D, Dp, P, Y, threads, s); break;
-    case 4: launch_rotate_rc<8, 4>(X, n, D, Dp, P, Y, threads, s); break;
-    case 6: launch_rotate_rc<4, 6>(X, n, D, Dp, P, Y, threads, s); break;
-    case 8: launch_rotate_rc<4, 8>(X, n, D, Dp, P, Y, threads, s); break;
+    case 1: launch_rotate_rc<8, 1>(X, n, D, Dp, P, Y, threads, s); break;
+    case 2: launch_rotate_rc<4, 2>(X, n, D, Dp, P, Y, threads, s); break;
+    case 3: launch_rotate_rc<4, 3>(X, n, D, Dp, P, Y, threads, s); break;
+    case 4: launch_rotate_rc<4, 4>(X, n, D, Dp, P, Y, threads, s); break;
+    case 6: launch_rotate_rc<2, 6>(X, n, D, Dp, P, Y, threads, s); break;
+    case 8: launch_rotate_rc<1, 8>(X, n, D, Dp, P, Y, threads, s); break;
     default: throw Error{RBQ_ERR_INVALID, "rotation: padded dim must be <= 2048 with Dp/256 in {1,2,3,4,6,8}"};
   }
 }
