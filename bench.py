@@ -380,7 +380,28 @@ def run_ours(args, cfg):
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
     seeded = world > 1 or args.seeded == 1
-    roof, roof_rr, scan_share = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
+    roof, roof_rr, _ = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
+    scan_share = round(roof["launch_ms"] / ms, 3)
+
+    # ---- config 2's batch sweep (B = 1, 64, 1024): device-resident queries, same index
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = {}
+        for B in (1, 64, 1024):
+            qb = Qd[:B]
+            reps = max(3, min(200, 20000 // B))
+            for _ in range(3):
+                index.search(qb, k)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                index.search(qb, k)
+            e1.record(stream)
+            e1.synchronize()
+            ms_b = e0.elapsed_time(e1) / reps
+            sweep[str(B)] = {"queries_per_s": round(B / (ms_b / 1000.0), 1), "ms_per_batch": round(ms_b, 4)}
+        sweep["10000"] = {"queries_per_s": round(value, 1), "ms_per_batch": round(ms, 4)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -400,6 +421,7 @@ def run_ours(args, cfg):
                         "d2h_bytes_per_step": nq * k * 12},
                 "gpu_launches": int(launches),
                 "roofline": roof, "roofline_rerank": roof_rr, "scan_share_of_step": scan_share,
+                "batch_sweep": sweep,
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -537,6 +559,7 @@ def main():
     ap.add_argument("--n", type=int, default=0, help="database size override (smoke runs)")
     ap.add_argument("--nq", type=int, default=0, help="query batch override")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the B = 1 / 64 / 1024 sweep")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
                     help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()
