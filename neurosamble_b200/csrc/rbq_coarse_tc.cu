@@ -6,18 +6,24 @@
 // tensor memory; the scores only rank a shortlist of P + margin lists per query, the exact
 // double-precision refine (refine_topp_kernel) decides the probes.
 //
-// CTA: 256 threads, 128 queries; centroids in chunks of 256 (one 128 x 256 fp32 accumulator =
+// CTA: 256 threads, 128 queries x one chunk of 256 centroids (a 128 x 256 fp32 accumulator =
 // 256 TMEM columns); the reduction dimension in chunks of 32 tf32 values (128-byte rows),
 // stored K-major with the 128-byte swizzle (16-byte unit u of row r of an 8-row atom lives at
-// u ^ r).  Two shared-memory stages: threads fill one stage while the tensor core consumes the
-// other; one elected thread issues the MMAs and commits them to a per-stage mbarrier.  The
-// epilogue reads the accumulator with tcgen05.ld (warp w: TMEM lanes 32*(w%4).., columns half
-// w/4) and writes the scores.  Every mbarrier wait is bounded: on time-out the kernel records
-// an error code in err[0] and stops issuing work, it never spins forever.
+// u ^ r).  The operand tiles arrive by TMA (cp.async.bulk.tensor, 2-D tiles of the row-major
+// query and centroid matrices, zero fill past the last row; no multicast) into a ring of four
+// shared-memory stages, so up to four k-chunks are in flight while the tensor core works.  One
+// thread issues the loads and the MMAs: a stage is refilled once the MMAs that read it have
+// committed to its "empty" mbarrier.  The epilogue reads the accumulator with tcgen05.ld
+// (warp w: TMEM lanes 32*(w%4).., columns half w/4) and writes the scores.  Every mbarrier
+// wait is bounded: on time-out the kernel records an error code in err[0], waits (bounded)
+// for its copies and MMAs in flight, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "rbq_internal.cuh"
 
@@ -29,6 +35,7 @@ constexpr int kTcN = 256;        // centroids per accumulator (TMEM columns)
 constexpr int kTcKc = 32;        // tf32 values per 128-byte smem row
 constexpr int kTcThreads = 256;
 constexpr int kTcStageBytes = (kTcM + kTcN) * 128;  // A chunk (16 KB) + B chunk (32 KB)
+constexpr int kTcStages = 4;
 constexpr uint32_t kWaitLimit = 1u << 26;           // bounded mbarrier polling
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -101,22 +108,23 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32])
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Copy `rows` rows x 32 values (columns [k0, k0+32) of a row-major [nrows_src, ld] matrix,
-// rows from r0) into a 128-byte-swizzled K-major block; rows past nrows_src are zeros.
-__device__ __forceinline__ void fill_sw128(unsigned char* blk, int rows, const float* __restrict__ src, int r0,
-                                           int nrows_src, int ld, int k0)
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
 {
-  for (int e = threadIdx.x; e < rows * 8; e += kTcThreads) {
-    const int r = e >> 3, u = e & 7;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r0 + r < nrows_src) v = __ldg(reinterpret_cast<const float4*>(src + (size_t)(r0 + r) * ld + k0) + u);
-    unsigned char* dst = blk + (r >> 3) * 1024 + (r & 7) * 128 + ((u ^ (r & 7)) << 4);
-    *reinterpret_cast<float4*>(dst) = v;
-  }
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const float* __restrict__ Qr, int nq,
-                                                                  const float* __restrict__ Cr,
+// 2-D tile load of the tensor map's box at element coordinates (x, y) into shared memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar)
+{
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                                  const __grid_constant__ CUtensorMap tmC, int nq,
                                                                   const float* __restrict__ cn2, int K, int dp,
                                                                   float* __restrict__ S, int* __restrict__ err)
 {
@@ -124,72 +132,94 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const float* _
   // 1024-byte aligned stages (the swizzle pattern is taken from the address bits).
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  unsigned char* stage[2] = {base, base + kTcStageBytes};
-  __shared__ __align__(8) unsigned long long s_bar[2];
+  __shared__ __align__(8) unsigned long long s_full[kTcStages], s_empty[kTcStages];
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * kTcM;  // blockIdx.y: the first centroid chunk of this CTA
-  const uint32_t bar0 = smem_u32(&s_bar[0]), bar1 = smem_u32(&s_bar[1]);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"((uint32_t)kTcN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar1, 1);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&s_empty[i]), 1);
+    }
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmC)) : "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
 
-  // Stage s = it & 1 of k-chunk `it` (counted over the whole kernel) is reused by chunk it + 2
-  // only after the MMAs of chunk it completed: completion number (it >> 1) of barrier s, i.e.
-  // mbarrier phase parity (it >> 1) & 1.  Only thread 0 polls; the block reads s_fail after a
-  // barrier, so every thread takes the same path.
+  // k-chunks are numbered over the CTA's whole run: chunk c = (n0 index, kc), stage c % 4.
+  // The j-th load into a stage completes phase j of its "full" barrier, the j-th MMA group
+  // that read it commits phase j of its "empty" barrier (parity j & 1).  Thread 0 alone
+  // issues loads and MMAs; the block learns of a failed wait through s_fail after a barrier.
   const int nkc = dp / kTcKc;
-  int it = 0;
-  for (int n0 = blockIdx.y * kTcN; n0 < K; n0 += gridDim.y * kTcN) {
-    for (int kc = 0; kc < nkc; ++kc, ++it) {
-      const int sidx = it & 1;
-      const uint32_t bar = sidx ? bar1 : bar0;
-      if (it >= 2 && tid == 0) {
-        if (!mbar_wait(bar, (uint32_t)((it - 2) >> 1) & 1u)) {
-          s_fail = 1;
+  int n_n0 = 0;
+  for (int n0 = blockIdx.y * kTcN; n0 < K; n0 += gridDim.y * kTcN) ++n_n0;
+  const int total = n_n0 * nkc;
+  int issued = 0, consumed = 0;
+  auto stage_of = [&](int c) { return base + (c % kTcStages) * kTcStageBytes; };
+  auto issue = [&](int c) -> bool {  // thread 0: load chunk c once its stage is free
+    const int st = c % kTcStages;
+    if (c >= kTcStages && !mbar_wait(smem_u32(&s_empty[st]), (uint32_t)((c / kTcStages - 1) & 1))) return false;
+    const int n0 = (blockIdx.y + (c / nkc) * gridDim.y) * kTcN, kc = c % nkc;
+    unsigned char* a_blk = stage_of(c);
+    const uint32_t full = smem_u32(&s_full[st]);
+    mbar_expect_tx(full, (uint32_t)kTcStageBytes);
+    tma_load_2d(smem_u32(a_blk), &tmQ, kc * kTcKc, q0, full);
+    tma_load_2d(smem_u32(a_blk + kTcM * 128), &tmC, kc * kTcKc, n0, full);
+    return true;
+  };
+  if (tid == 0)
+    for (; issued < total && issued < kTcStages; ++issued) issue(issued);
+
+  for (int t = 0; t < n_n0; ++t) {
+    const int n0 = (blockIdx.y + t * gridDim.y) * kTcN;
+    if (tid == 0) {
+      bool ok = true;
+      for (int kc = 0; kc < nkc && ok; ++kc) {
+        const int c = consumed;
+        const int st = c % kTcStages;
+        if (!mbar_wait(smem_u32(&s_full[st]), (uint32_t)((c / kTcStages) & 1))) {
+          ok = false;
           atomicExch(err, 1);
+          break;
         }
-      }
-      __syncthreads();
-      if (s_fail) break;
-      unsigned char* a_blk = stage[sidx];
-      unsigned char* b_blk = stage[sidx] + kTcM * 128;
-      fill_sw128(a_blk, kTcM, Qr, q0, nq, dp, kc * kTcKc);
-      fill_sw128(b_blk, kTcN, Cr, n0, K, dp, kc * kTcKc);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncthreads();
-      if (tid == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(a_blk), b_addr = smem_u32(b_blk);
+        const uint32_t a_addr = smem_u32(stage_of(c)), b_addr = a_addr + kTcM * 128;
 #pragma unroll
         for (int ks = 0; ks < kTcKc / 8; ++ks)  // 8 tf32 (32 bytes) per MMA
           tc_mma(tmem, sw128_desc(a_addr + ks * 32), sw128_desc(b_addr + ks * 32), kTcIdesc,
                  (kc > 0 || ks > 0) ? 1u : 0u);
-        tc_commit(bar);
+        tc_commit(smem_u32(&s_empty[st]));
+        ++consumed;
+        if (issued < total) {
+          if (!issue(issued)) {
+            ok = false;
+            atomicExch(err, 3);
+            break;
+          }
+          ++issued;
+        }
       }
-    }
-    if (s_fail) break;
-    // The last chunk's commit covers every MMA issued before it.
-    if (tid == 0) {
-      const int last = it - 1;
-      if (!mbar_wait((last & 1) ? bar1 : bar0, (uint32_t)(last >> 1) & 1u)) {
-        s_fail = 1;
-        atomicExch(err, 2);
+      // The last commit covers every MMA issued before it: the accumulator is complete.
+      if (ok) {
+        const int last = consumed - 1;
+        if (!mbar_wait(smem_u32(&s_empty[last % kTcStages]), (uint32_t)((last / kTcStages) & 1))) {
+          ok = false;
+          atomicExch(err, 2);
+        }
       }
+      if (!ok) s_fail = 1;
     }
     __syncthreads();
     if (s_fail) break;
@@ -216,16 +246,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const float* _
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
   }
-  // On failure, give the MMAs already issued a bounded chance to finish before freeing TMEM.
-  if (s_fail && tid == 0 && it > 0) {
-    const int last = it - 1;
-    mbar_wait((last & 1) ? bar1 : bar0, (uint32_t)(last >> 1) & 1u);
+  // On failure: wait (bounded) for the copies and MMAs still in flight, then free TMEM.
+  if (s_fail && tid == 0) {
+    for (int c = consumed; c < issued; ++c)
+      mbar_wait(smem_u32(&s_full[c % kTcStages]), (uint32_t)((c / kTcStages) & 1));
+    if (consumed > 0) {
+      const int last = consumed - 1;
+      mbar_wait(smem_u32(&s_empty[last % kTcStages]), (uint32_t)((last / kTcStages) & 1));
+    }
   }
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcN));
   }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  RBQ_CHECK(fn != nullptr, RBQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+
+// Row-major fp32 [rows, dp] matrix, box = [box_rows, 32 values], 128-byte swizzle, zero fill.
+CUtensorMap row_major_map(const float* ptr, int64_t rows, int dp, int box_rows)
+{
+  RBQ_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, RBQ_ERR_INVALID,
+            "coarse (tensor cores): operands must be 16-byte aligned");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)dp * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcKc, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RBQ_CHECK(r == CUDA_SUCCESS, RBQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
 }
 
 }  // namespace
@@ -238,11 +306,13 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
   if (nq <= 0) return;
   RBQ_CHECK(coarse_tc_supported(dp), RBQ_ERR_INVALID, "coarse (tensor cores): padded dim must be a multiple of 32");
   RBQ_CHECK(nq <= 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "coarse (tensor cores): bad sizes");
-  const size_t smem = (size_t)2 * kTcStageBytes + 1024;
+  const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
   RBQ_CUDA(cudaFuncSetAttribute(coarse_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const CUtensorMap tmQ = row_major_map(A, nq, dp, kTcM);
+  const CUtensorMap tmC = row_major_map(C, K, dp, kTcN);
   // one CTA per (128 queries, 256-centroid chunk)
   const dim3 grid((unsigned)ceil_div(nq, kTcM), (unsigned)std::min<int64_t>(ceil_div(K, kTcN), 65535));
-  coarse_tc_kernel<<<grid, kTcThreads, smem, s>>>(A, (int)nq, C, cn2, K, dp, S, err);
+  coarse_tc_kernel<<<grid, kTcThreads, smem, s>>>(tmQ, tmC, (int)nq, cn2, K, dp, S, err);
   RBQ_LAUNCHED();
 }
 

@@ -869,30 +869,50 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
 }
 
 // ---------------------------------------------------------------------------------------
-// Merge [nq, parts, R] ascending key lists -> first R of the union, ascending.
+// Merge [nq, parts, R] key lists -> the R smallest of their union, ascending.  The non-empty
+// keys are gathered into shared memory, cut to R by the radix select, and only those R are
+// sorted (a query split into 32 slices holds 6,400 keys; sorting all of them took 0.2 ms).
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) merge_keys_kernel(const unsigned long long* __restrict__ in, int parts, int R,
-                                                         int n2, unsigned long long* __restrict__ out)
+                                                         int r2, unsigned long long* __restrict__ out)
 {
-  extern __shared__ unsigned long long mk[];
+  extern __shared__ unsigned long long mk[];  // [parts * R] gathered keys, then [r2] result
+  unsigned long long* res = mk + (size_t)parts * R;
+  __shared__ int s_n, s_misc[3], s_cnt;
+  __shared__ unsigned s_hist[256];
+  __shared__ unsigned long long s_kmax;
   const int64_t q = blockIdx.x;
   const int tot = parts * R;
-  for (int i = threadIdx.x; i < n2; i += blockDim.x) mk[i] = (i < tot) ? in[q * tot + i] : kEmptyKey;
+  if (threadIdx.x == 0) s_n = 0;
   __syncthreads();
-  block_bitonic_sort(mk, n2);
-  for (int i = threadIdx.x; i < R; i += blockDim.x) out[q * R + i] = mk[i];
+  for (int i = threadIdx.x; i < tot; i += blockDim.x) {
+    const unsigned long long k = in[q * tot + i];
+    if (k != kEmptyKey) mk[atomicAdd(&s_n, 1)] = k;
+  }
+  __syncthreads();
+  int n = s_n;
+  if (n > R) {
+    block_keep_smallest(mk, n, R, res, s_hist, s_misc, &s_kmax, &s_cnt);
+    n = R;
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) res[i] = mk[i];
+  }
+  for (int i = n + threadIdx.x; i < r2; i += blockDim.x) res[i] = kEmptyKey;
+  __syncthreads();
+  block_bitonic_sort(res, r2);
+  for (int i = threadIdx.x; i < R; i += blockDim.x) out[q * R + i] = res[i];
 }
 
 void launch_merge_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,
                        cudaStream_t s)
 {
   if (nq <= 0) return;
-  const int n2 = next_pow2(parts * R);
-  const size_t smem = (size_t)n2 * 8;
+  const int r2 = next_pow2(R < 2 ? 2 : R);
+  const size_t smem = ((size_t)parts * R + r2) * 8;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "merge: too many candidates per query");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(merge_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  merge_keys_kernel<<<(unsigned)nq, 256, smem, s>>>(in, parts, R, n2, out);
+  merge_keys_kernel<<<(unsigned)nq, 256, smem, s>>>(in, parts, R, r2, out);
   RBQ_LAUNCHED();
 }
 

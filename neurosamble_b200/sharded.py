@@ -5,10 +5,9 @@ Every list lives on one rank (every rank keeps the full centroid table, rotation
 each rank's scan work is about equal; "round_robin" puts list l on rank l % world.
 A search of a batch replicated on every rank runs in four steps:
 
-1. front end: every rank rotates and 4-bit-quantises the whole batch (cheap, and it spares
-   moving 1 KB of rotated query per query), but coarse-quantises only queries
-   [r*nl, (r+1)*nl) (nl = ceil(nq / world)); one all-gather of [probes | g] rows hands every
-   rank the probes of the whole batch;
+1. front end: rank r rotates and coarse-quantises queries [r*nl, (r+1)*nl)
+   (nl = ceil(nq / world)); two all-gathers hand every rank the rotated queries and the
+   [probes | g] rows of the whole batch, which every rank then 4-bit-quantises (cheap);
 2. seed: each rank scans the nearest probed list of the queries whose nearest list it owns;
    an all-reduce (min) of the per-query R-th estimate gives every rank the threshold a
    single GPU reaches after that list, so a shard prunes its lists as tightly as one GPU
@@ -169,11 +168,13 @@ class LibStages:
         self.device = index.device
         self.st = _stream_ptr(index.device)
 
-    def rotate_prep(self, q, qr, planes, delta, k1):
-        n = q.shape[0]
+    def rotate(self, q, qr):
         with torch.cuda.device(self.device):
-            _lib.call("rbq_rotate", self.h, _ptr(q), n, _ptr(qr), self.st)
-            _lib.call("rbq_query_prep", self.h, _ptr(qr), n, _ptr(planes), _ptr(delta), _ptr(k1), self.st)
+            _lib.call("rbq_rotate", self.h, _ptr(q), q.shape[0], _ptr(qr), self.st)
+
+    def prep(self, qr, planes, delta, k1):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_query_prep", self.h, _ptr(qr), qr.shape[0], _ptr(planes), _ptr(delta), _ptr(k1), self.st)
 
     def coarse(self, qr, margin, probes, g):
         with torch.cuda.device(self.device):
@@ -210,23 +211,27 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     R, slices, cap = plan(nq, P, k, k_rerank, probe_split, cand_cap, world)
     nl = (nq + world - 1) // world
     lo, hi = min(nq, rank * nl), min(nq, (rank + 1) * nl)
-    # 1. front end: rotation and query planes of the whole batch; probes of this rank's
-    #    queries (padded with copies of the last query), all-gathered as [probes | g] rows.
-    qr = torch.empty((nq, dp), dtype=torch.float32, device=dev)
-    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
-    delta = torch.empty(nq, dtype=torch.float32, device=dev)
-    k1 = torch.empty(nq, dtype=torch.float32, device=dev)
-    stages.rotate_prep(t, qr, planes, delta, k1)
-    qloc = qr[lo:hi]
+    # 1. front end: this rank's queries (padded with copies of the last query) rotated and
+    #    coarse-quantised; rotated rows and [probes | g] rows all-gathered; planes of the batch.
+    qloc = t[lo:hi]
     if hi - lo < nl:
-        qloc = torch.cat([qloc, qr[nq - 1:].expand(nl - (hi - lo), dp)])
+        qloc = torch.cat([qloc, t[nq - 1:].expand(nl - (hi - lo), t.shape[1])])
+    qr_l = torch.empty((nl, dp), dtype=torch.float32, device=dev)
+    stages.rotate(qloc.contiguous(), qr_l)
     pl = torch.empty((nl, P), dtype=torch.int32, device=dev)
     gl = torch.empty((nl, P), dtype=torch.float32, device=dev)
-    stages.coarse(qloc.contiguous(), margin, pl, gl)
+    stages.coarse(qr_l, margin, pl, gl)
+    qr_all = torch.empty((world * nl, dp), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(qr_all, qr_l, group=group)
     send = torch.cat([pl, gl.view(torch.int32)], dim=1)
     recv = torch.empty((world * nl, 2 * P), dtype=torch.int32, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
+    qr = qr_all[:nq]
     probes, g = recv[:nq, :P], recv[:nq, P:].view(torch.float32)  # row stride 2P
+    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
+    delta = torch.empty(nq, dtype=torch.float32, device=dev)
+    k1 = torch.empty(nq, dtype=torch.float32, device=dev)
+    stages.prep(qr, planes, delta, k1)
     # 2. seed: the nearest probe, scanned by the rank that owns it; min over ranks of the R-th.
     ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
     da = torch.empty((nq, R), dtype=torch.float32, device=dev)

@@ -118,12 +118,13 @@ class _OracleStages:
     def __init__(self, O, ix, rank, world, owner=None):
         self.O, self.ix, self.rank, self.world, self.owner = O, ix, rank, world, owner
 
-    def rotate_prep(self, q, qr, planes, delta, k1):
+    def rotate(self, q, qr):
         import torch
-        O, ix = self.O, self.ix
-        Qr = O.rotate(q.numpy(), ix.P)
-        pl, de, kk, _ = O.query_prep(Qr, ix.t4)
-        qr.copy_(torch.from_numpy(Qr))
+        qr.copy_(torch.from_numpy(self.O.rotate(q.numpy(), self.ix.P)))
+
+    def prep(self, qr, planes, delta, k1):
+        import torch
+        pl, de, kk, _ = self.O.query_prep(qr.numpy(), self.ix.t4)
         planes.copy_(torch.from_numpy(np.ascontiguousarray(pl).view(np.int32).reshape(planes.shape)))
         delta.copy_(torch.from_numpy(de))
         k1.copy_(torch.from_numpy(kk))
@@ -186,8 +187,8 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy):
 @pytest.mark.parametrize("world,nq,prune,policy", [(2, 40, 1, "balanced"), (3, 7, 1, "round_robin"),
                                                    (2, 40, 0, "balanced")])
 def test_seeded_sharded_search_over_gloo(world, nq, prune, policy):
-    """The orchestration (queries split for the coarse quantiser and padded, probe rows
-    all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
+    """The orchestration (queries split for the rotation and coarse quantiser and padded, rotated
+    rows and probe rows all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
     merge of the oracle's per-shard searches with the shared seed.  With the prune off every
     shard keeps its exact top-R by estimate, so the shards' candidates contain the single-shard
     top-R and the reranked distances are, rank by rank, no larger than the single-shard's."""
