@@ -140,6 +140,16 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
 int rbq_save(rbq_index_t* index, const char* path);
 int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard_count, rbq_index_t** out);
 
+/* The reference's index file (IVFGPU::save / load_transposed, gpu_index/ivf_gpu.cu:367-461,
+ * 100-289, as written by ivf_rabitq::serialize, ivf_rabitq.cu:357-368): import a 1-bit,
+ * matmul-rotator file (its rotation, query constant, rotated centroids, codes, factors and ids
+ * are used as stored; lists are split over shards by shard_policy), optionally with the raw
+ * vectors X_host [n_x = num_vectors, D] (row = id) for the exact rerank — without them the
+ * index searches with rerank = 0 only.  Export writes an unsharded index in that format. */
+int rbq_import_reference(const char* path, int32_t device, const float* X_host, int64_t n_x, int32_t shard_rank,
+                         int32_t shard_count, int32_t shard_policy, rbq_index_t** out);
+int rbq_export_reference(rbq_index_t* index, const char* path);
+
 /* ---- introspection (parity tests) ------------------------------------------------------- */
 /* Host copies.  rotation: [Dp*Dp]; centroids: [K*D]; rotated centroids: [K*Dp]. */
 int rbq_get_rotation(rbq_index_t* index, float* P_host);

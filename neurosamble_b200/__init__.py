@@ -1,4 +1,4 @@
 """B200-native IVF-RaBitQ retrieval for Neurosamble (CUDA C-ABI library + FAISS-style API)."""
-from .index import IndexIVFRaBitQ, read_index, write_index
+from .index import IndexIVFRaBitQ, read_index, read_reference_index, write_index, write_reference_index
 
-__all__ = ["IndexIVFRaBitQ", "read_index", "write_index"]
+__all__ = ["IndexIVFRaBitQ", "read_index", "write_index", "read_reference_index", "write_reference_index"]

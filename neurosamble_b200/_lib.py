@@ -61,6 +61,8 @@ SIGNATURES = {
     "rbq_search_host": [_P, ctypes.POINTER(SearchParams), _P, _I64, _P, _P, _P],
     "rbq_save": [_P, ctypes.c_char_p],
     "rbq_load": [ctypes.c_char_p, _I32, _I32, _I32, ctypes.POINTER(_P)],
+    "rbq_import_reference": [ctypes.c_char_p, _I32, _P, _I64, _I32, _I32, _I32, ctypes.POINTER(_P)],
+    "rbq_export_reference": [_P, ctypes.c_char_p],
     "rbq_get_rotation": [_P, _P],
     "rbq_get_centroids": [_P, _P, _P],
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],

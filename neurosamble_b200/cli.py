@@ -107,7 +107,7 @@ def main(argv=None) -> int:
 
     def to_dev(x: np.ndarray) -> torch.Tensor:
         # fp16 rows cross PCIe at half the bytes and are widened on the device
-        return torch.from_numpy(np.ascontiguousarray(x)).to(dev, non_blocking=False).float()
+        return torch.from_numpy(np.require(x, requirements=["C", "W"])).to(dev, non_blocking=False).float()
 
     t0 = time.perf_counter()
     if world > 1:

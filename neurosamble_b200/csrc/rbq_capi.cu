@@ -8,11 +8,13 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <new>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "rbq_internal.cuh"
@@ -452,6 +454,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   RBQ_CHECK(nq >= 0, RBQ_ERR_INVALID, "search: negative query count");
   if (nq == 0) return;
   RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "search called before train / set_centroids");
+  RBQ_CHECK(params.rerank <= 0 || ix.has_raw, RBQ_ERR_STATE,
+            "exact rerank needs the raw vectors; this index was imported without them (use rerank = 0)");
   const SearchPlan sp = plan_search(ix, params, nq);
   const int64_t by_scores = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4));
   const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_scores, 65535ll * 64));
@@ -518,6 +522,55 @@ void write_dev(File& f, const T* p, size_t count)
   std::vector<T> h(count);
   if (count) RBQ_CUDA(cudaMemcpy(h.data(), p, count * sizeof(T), cudaMemcpyDeviceToHost));
   f.write(h.data(), count * sizeof(T));
+}
+
+struct RefFile {
+  uint64_t n = 0, D = 0, K = 0, ex_bits = 0;
+  float t4 = 0.0f, t8 = 0.0f;
+  std::vector<uint64_t> sizes;
+  std::vector<float> P, Crot, fac;
+  std::vector<uint32_t> codes, ids;
+};
+
+RefFile read_ref_file(const char* path)
+{
+  File f(path, "rb");
+  RefFile r;
+  f.read(&r.n, 8);
+  f.read(&r.D, 8);
+  f.read(&r.K, 8);
+  f.read(&r.ex_bits, 8);
+  RBQ_CHECK(r.D >= 1 && r.D <= 2048 && r.K >= 1 && r.K <= (1u << 24) && r.n < 0xFFFFFFFFull, RBQ_ERR_FORMAT,
+            "not a reference IVF-RaBitQ index (bad header): " + f.path);
+  RBQ_CHECK(r.ex_bits == 0, RBQ_ERR_FORMAT,
+            "reference index with " + std::to_string(r.ex_bits) + " extra bits: only 1-bit codes are supported");
+  unsigned char flag = 0;
+  f.read(&flag, 1);
+  f.read(&r.t4, 4);
+  f.read(&r.t8, 4);
+  r.sizes.resize(r.K);
+  f.read(r.sizes.data(), r.K * 8);
+  uint64_t tot = 0;
+  for (uint64_t c : r.sizes) tot += c;
+  RBQ_CHECK(tot == r.n, RBQ_ERR_FORMAT, "cluster sizes do not sum to num_vectors: " + f.path);
+  unsigned char kind = 0;
+  f.read(&kind, 1);
+  RBQ_CHECK(kind == 0, RBQ_ERR_FORMAT, "reference index uses the FHT-Kac rotator: only the matmul rotator is supported");
+  const uint64_t Dp = (r.D + 31) / 32 * 32, W = Dp / 32;
+  r.P.resize(Dp * Dp);
+  f.read(r.P.data(), r.P.size() * 4);
+  r.Crot.resize(r.K * Dp);
+  f.read(r.Crot.data(), r.Crot.size() * 4);
+  r.codes.resize(r.n * W);
+  f.read(r.codes.data(), r.codes.size() * 4);
+  r.fac.resize(r.n * 3);
+  f.read(r.fac.data(), r.fac.size() * 4);
+  std::vector<float> skip(r.n * 2);  // no long codes at 1 bit; the extra-bit factors are unused
+  f.read(skip.data(), skip.size() * 4);
+  r.ids.resize(r.n);
+  f.read(r.ids.data(), r.n * 4);
+  for (uint32_t id : r.ids) RBQ_CHECK(id < r.n, RBQ_ERR_FORMAT, "reference index id out of range: " + f.path);
+  return r;
 }
 
 }  // namespace
@@ -820,8 +873,9 @@ int rbq_save(rbq_index_t* index, const char* path)
     File f(path, "wb");
     f.write(kMagic, 8);
     f.write(&kFormatVersion, 4);
+    // hdr[7]: bit 0 trained, bit 1 no raw rows (an index imported without its vectors)
     int32_t hdr[8] = {ix.D, ix.Dp, ix.K, ix.kmeans_iters, ix.max_train_per_list, ix.shard_rank, ix.shard_count,
-                      ix.trained ? 1 : 0};
+                      (ix.trained ? 1 : 0) | (ix.has_raw ? 0 : 2)};
     f.write(hdr, sizeof(hdr));
     f.write(&ix.seed, 8);
     f.write(&ix.t4, 4);
@@ -915,6 +969,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.shard_rank = p.shard_rank;
       ix.shard_count = p.shard_count;
       ix.shard_policy = pol[0];
+      ix.has_raw = (hdr[7] & 2) == 0;
       ix.t4 = t4;
       ix.P_host.resize((size_t)Dp * Dp);
       f.read(ix.P_host.data(), ix.P_host.size() * 4);
@@ -925,7 +980,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.off_host.assign(K + 1, 0);
       ix.list_off = dev_alloc<int64_t>(K + 1);
       RBQ_CUDA(cudaMemset(ix.list_off, 0, (K + 1) * 8));
-      if (hdr[7]) {
+      if (hdr[7] & 1) {
         ix.C_host.resize((size_t)K * D);
         f.read(ix.C_host.data(), ix.C_host.size() * 4);
         install_centroids(ix, 0);
@@ -994,6 +1049,159 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       throw;
     }
     *out = h;
+  });
+}
+
+// ---------------------------------------------------------------------------------------
+// The reference's index file (IVFGPU::save, gpu_index/ivf_gpu.cu:367-461, read back by
+// load_transposed, :100-289), a format that has to be alike to exchange indexes:
+//   size_t num_vectors, num_dimensions, num_centroids, ex_bits; bool legacy flag;
+//   float const_scaling_factor_4bit, const_scaling_factor_8bit;  size_t cluster_sizes[K];
+//   rotator: uint8 kind (0 = matmul) + Dp x Dp f32 row-major (rotator_gpu.cu:93-112);
+//   rotated centroids K x Dp f32 (initializer_gpu.cu:54-64);
+//   1-bit codes n x Dp/32 u32, clusters in order, vector-major inside a cluster;
+//   factors n x {f_add, f_rescale, f_err} f32; long codes n x Dp*ex_bits/8 bytes;
+//   extra-bit factors n x 2 f32; ids n x u32; optional "RPR1" representatives block.
+// Only 1-bit files (ex_bits = 0) with the matmul rotator are accepted.
+// ---------------------------------------------------------------------------------------
+int rbq_import_reference(const char* path, int32_t device, const float* X_host, int64_t n_x, int32_t shard_rank,
+                         int32_t shard_count, int32_t shard_policy, rbq_index_t** out)
+{
+  return guarded([&] {
+    RBQ_CHECK(out, RBQ_ERR_INVALID, "null argument");
+    *out = nullptr;
+    RefFile r = read_ref_file(path);
+    RBQ_CHECK(!X_host || n_x == (int64_t)r.n, RBQ_ERR_INVALID,
+              "raw vectors: " + std::to_string(n_x) + " rows given, the index holds " + std::to_string(r.n));
+    rbq_index_params_t p;
+    rbq_index_params_default(&p);
+    p.dim = (int32_t)r.D;
+    p.n_lists = (int32_t)r.K;
+    p.seed = 0;
+    p.device = device;
+    p.shard_rank = shard_rank;
+    p.shard_count = shard_count;
+    p.shard_policy = shard_policy;
+    rbq_index_t* h = nullptr;
+    int st = rbq_index_create(&p, &h);
+    if (st != RBQ_OK) throw Error{st, g_last_error};
+    Index& ix = h->ix;
+    try {
+      DeviceGuard dg(ix.device);
+      const int D = ix.D, Dp = ix.Dp, W = ix.W, K = ix.K;
+      // the file's rotation, query constants and rotated centroids replace the seeded ones
+      std::memcpy(ix.P_host.data(), r.P.data(), r.P.size() * 4);
+      RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
+      ix.t4 = r.t4;
+      ix.t8 = r.t8;
+      // original-space centroids c = c_rot P^T (P orthogonal), first D columns, for assigning
+      // later adds; the search keeps the file's rotated centroids bit for bit
+      ix.C_host.assign((size_t)K * D, 0.0f);
+      for (int c = 0; c < K; ++c)
+        for (int d = 0; d < D; ++d) {
+          double acc = 0.0;
+          for (int j = 0; j < Dp; ++j) acc += (double)r.Crot[(size_t)c * Dp + j] * (double)r.P[(size_t)d * Dp + j];
+          ix.C_host[(size_t)c * D + d] = (float)acc;
+        }
+      install_centroids(ix, 0);
+      RBQ_CUDA(cudaMemcpy(ix.C_rot, r.Crot.data(), r.Crot.size() * 4, cudaMemcpyHostToDevice));
+      launch_row_norms(ix.C_rot, K, Dp, ix.C_rot_n2, 0);
+      RBQ_CUDA(cudaDeviceSynchronize());
+      // owners from the file's cluster sizes; rows of owned clusters, in ascending id
+      std::vector<int64_t> sizes(r.sizes.begin(), r.sizes.end());
+      install_owners(ix, list_owners(ix.shard_policy, sizes, ix.shard_count), true);
+      std::vector<std::pair<uint32_t, int64_t>> keep;  // (id, file row)
+      std::vector<uint32_t> lab_of_row(r.n);
+      int64_t row = 0;
+      for (int c = 0; c < K; ++c)
+        for (uint64_t i = 0; i < r.sizes[c]; ++i, ++row) {
+          lab_of_row[row] = (uint32_t)c;
+          if (ix.owner_host[c] == ix.shard_rank) keep.push_back({r.ids[row], row});
+        }
+      std::sort(keep.begin(), keep.end());
+      const int64_t m = (int64_t)keep.size();
+      std::vector<uint32_t> codes((size_t)m * W), ids(m), labs(m);
+      std::vector<float> fa(m), fr(m), fe(m), X(X_host ? (size_t)m * D : 0);
+      for (int64_t i = 0; i < m; ++i) {
+        const int64_t src = keep[i].second;
+        std::memcpy(&codes[(size_t)i * W], &r.codes[(size_t)src * W], (size_t)W * 4);
+        ids[i] = keep[i].first;
+        labs[i] = lab_of_row[src];
+        fa[i] = r.fac[src * 3 + 0];
+        fr[i] = r.fac[src * 3 + 1];
+        fe[i] = r.fac[src * 3 + 2];
+        if (X_host) std::memcpy(&X[(size_t)i * D], X_host + (size_t)keep[i].first * D, (size_t)D * 4);
+      }
+      ensure_id_capacity(ix, std::max<int64_t>((int64_t)r.n, 1));
+      ensure_row_capacity(ix, std::max<int64_t>(m, 1));
+      auto up = [&](void* dst, const void* src, size_t bytes) {
+        if (bytes) RBQ_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+      };
+      up(ix.codes_r, codes.data(), codes.size() * 4);
+      up(ix.ids_r, ids.data(), (size_t)m * 4);
+      up(ix.labels_r, labs.data(), (size_t)m * 4);
+      up(ix.fadd_r, fa.data(), (size_t)m * 4);
+      up(ix.frescale_r, fr.data(), (size_t)m * 4);
+      up(ix.ferr_r, fe.data(), (size_t)m * 4);
+      if (X_host) up(ix.X_r, X.data(), X.size() * 4);
+      ix.has_raw = X_host != nullptr;
+      std::vector<uint32_t> id2row(r.n, 0xFFFFFFFFu);
+      for (int64_t i = 0; i < m; ++i) id2row[ids[i]] = (uint32_t)i;
+      up(ix.id2row, id2row.data(), (size_t)r.n * 4);
+      ix.n_rows = m;
+      ix.n_total = (int64_t)r.n;
+      relayout(ix, 0);
+    } catch (...) {
+      rbq_index_free(h);
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int rbq_export_reference(rbq_index_t* index, const char* path)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null index");
+    Index& ix = index->ix;
+    RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "index is not trained");
+    RBQ_CHECK(ix.shard_count == 1, RBQ_ERR_STATE, "the reference format holds a whole index: export an unsharded one");
+    DeviceGuard dg(ix.device);
+    RBQ_CUDA(cudaDeviceSynchronize());
+    const uint64_t n = (uint64_t)ix.n_rows, D = (uint64_t)ix.D, K = (uint64_t)ix.K, ex = 0;
+    File f(path, "wb");
+    f.write(&n, 8);
+    f.write(&D, 8);
+    f.write(&K, 8);
+    f.write(&ex, 8);
+    const unsigned char flag = 1;
+    f.write(&flag, 1);
+    const float t8 = std::isnan(ix.t8) ? query_scale(ix.Dp, ix.seed, 7) : ix.t8;
+    f.write(&ix.t4, 4);
+    f.write(&t8, 4);
+    std::vector<uint64_t> sizes(K);
+    for (uint64_t c = 0; c < K; ++c) sizes[c] = (uint64_t)(ix.off_host[c + 1] - ix.off_host[c]);
+    f.write(sizes.data(), K * 8);
+    const unsigned char kind = 0;
+    f.write(&kind, 1);
+    f.write(ix.P_host.data(), ix.P_host.size() * 4);
+    write_dev(f, ix.C_rot, (size_t)K * ix.Dp);
+    write_dev(f, ix.codes, (size_t)n * ix.W);
+    std::vector<float> fa(n), fr(n), fe(n), fac(n * 3);
+    if (n) {
+      RBQ_CUDA(cudaMemcpy(fa.data(), ix.fadd, n * 4, cudaMemcpyDeviceToHost));
+      RBQ_CUDA(cudaMemcpy(fr.data(), ix.frescale, n * 4, cudaMemcpyDeviceToHost));
+      RBQ_CUDA(cudaMemcpy(fe.data(), ix.ferr, n * 4, cudaMemcpyDeviceToHost));
+    }
+    for (uint64_t i = 0; i < n; ++i) {
+      fac[i * 3 + 0] = fa[i];
+      fac[i * 3 + 1] = fr[i];
+      fac[i * 3 + 2] = fe[i];
+    }
+    f.write(fac.data(), fac.size() * 4);
+    const std::vector<float> exf(n * 2, 0.0f);
+    f.write(exf.data(), exf.size() * 4);
+    write_dev(f, ix.ids, (size_t)n);
   });
 }
 
@@ -1177,6 +1385,7 @@ int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t
     RBQ_CHECK(R >= 1 && R <= 4096 && k >= 1, RBQ_ERR_INVALID, "bad rerank parameters");
     if (nq == 0) return;
     Index& ix = index->ix;
+    RBQ_CHECK(ix.has_raw, RBQ_ERR_STATE, "exact rerank needs the raw vectors; this index was imported without them");
     DeviceGuard dg(ix.device);
     cudaStream_t s = as_stream(stream);
     Scratch sc(s);

@@ -239,3 +239,28 @@ def read_index(path: str, device: int | None = None, shard_rank: int = -1, shard
     out = _lib.IndexInfo()
     _lib.call("rbq_index_info", h, ctypes.byref(out))
     return IndexIVFRaBitQ(out.dim, out.n_lists, device=dev, metric=metric, _handle=h)
+
+
+def read_reference_index(path: str, X=None, device: int | None = None, shard_rank: int = 0, shard_count: int = 1,
+                         shard_policy: str = "round_robin", metric: str = "l2") -> IndexIVFRaBitQ:
+    """Import an index file written by the reference (cuVS ivf_rabitq serialize / IVFGPU::save,
+    1-bit codes, matmul rotator).  X (optional, [num_vectors, D] float32, row = id) supplies
+    the raw vectors of the exact rerank; without it the index searches with k_rerank = 0."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    xh = None
+    n_x = 0
+    if X is not None:
+        xh = np.ascontiguousarray(X.cpu().numpy() if isinstance(X, torch.Tensor) else X, dtype=np.float32)
+        n_x = xh.shape[0]
+    h = ctypes.c_void_p()
+    _lib.call("rbq_import_reference", str(path).encode(), dev,
+              xh.ctypes.data_as(ctypes.c_void_p) if xh is not None else None, n_x, int(shard_rank),
+              int(shard_count), _lib.SHARD_POLICIES[shard_policy], ctypes.byref(h))
+    out = _lib.IndexInfo()
+    _lib.call("rbq_index_info", h, ctypes.byref(out))
+    return IndexIVFRaBitQ(out.dim, out.n_lists, device=dev, metric=metric, _handle=h)
+
+
+def write_reference_index(index: IndexIVFRaBitQ, path: str) -> None:
+    """Write an unsharded index in the reference's file format (IVFGPU::save)."""
+    _lib.call("rbq_export_reference", index.handle, str(path).encode())
