@@ -148,13 +148,14 @@ void install_centroids(Index& ix, cudaStream_t s)
   ix.trained = true;
 }
 
-// Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d]: approximate fp32
-// shortlist, then the double-accumulated distance decides.
+// Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d]: approximate
+// shortlist (tcgen05 tf32 scores when d is a multiple of 32 and the rows are 16-byte aligned,
+// else fp32 SIMT), then the double-accumulated distance over the shortlist decides.
 void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, int d,
                    uint32_t* labels_out, cudaStream_t s)
 {
   const int K = ix.K;
-  const int m = std::min(K, 16);
+  const int m = std::min(K, 32);  // shortlist width: far beyond the tf32 ranking error
   const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65535 * 64, (256ll << 20) / ((int64_t)K * 4)));
   Scratch sc(s);
   const int64_t c0 = std::min(n, chunk);
@@ -163,7 +164,12 @@ void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, c
   int32_t* best = sc.get<int32_t>((size_t)c0);
   for (int64_t a = 0; a < n; a += chunk) {
     const int64_t cn = std::min(chunk, n - a);
-    launch_coarse_scores(A + a * d, cn, C, cn2, K, d, S, s);
+    const float* Aa = A + a * d;
+    if (coarse_tc_supported(d) && d % 32 == 0 && (reinterpret_cast<uintptr_t>(Aa) & 15u) == 0 &&
+        (reinterpret_cast<uintptr_t>(C) & 15u) == 0)
+      launch_coarse_scores_tc(Aa, cn, C, cn2, K, d, S, ix.dev_err, s);
+    else
+      launch_coarse_scores(Aa, cn, C, cn2, K, d, S, s);
     launch_topm_rows(S, cn, K, m, cand, s);
     launch_refine_topp(A + a * d, cn, C, d, cand, m, 1, best, nullptr, s);
     RBQ_CUDA(cudaMemcpyAsync(labels_out + a, best, cn * 4, cudaMemcpyDeviceToDevice, s));
@@ -632,6 +638,10 @@ void free_index_memory(Index& ix)
   dev_free(ix.id2row);
   dev_free(ix.dev_err);
   dev_free(ix.owner);
+  if (ix.copy_stream) {
+    cudaStreamDestroy(ix.copy_stream);
+    ix.copy_stream = nullptr;
+  }
   dev_free(ix.list_off);
   dev_free(ix.ids);
   dev_free(ix.codes);
@@ -845,14 +855,56 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
     cudaStream_t s = as_stream(stream);
+    const int k = params->k;
+    RBQ_CHECK(k >= 1, RBQ_ERR_INVALID, "search: k must be >= 1");
+    // Batches of >= 4096 queries run in two halves: the second half's upload and the first
+    // half's download (on a copy stream, ordered by events) overlap the search of the other
+    // half.  Halves of >= 2048 queries plan the same single-slice search as the whole batch,
+    // so the results do not depend on the split.
+    constexpr int64_t kMinChunk = 2048;
+    const int nch = nq >= 2 * kMinChunk ? 2 : 1;
     Scratch sc(s);
     float* q = sc.get<float>((size_t)nq * ix.D);
-    float* d = sc.get<float>((size_t)nq * params->k);
-    int64_t* i = sc.get<int64_t>((size_t)nq * params->k);
-    RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
-    run_search(ix, *params, q, nq, d, i, s, nullptr);
-    RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * params->k * 4, cudaMemcpyDeviceToHost, s));
-    RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * params->k * 8, cudaMemcpyDeviceToHost, s));
+    float* d = sc.get<float>((size_t)nq * k);
+    int64_t* i = sc.get<int64_t>((size_t)nq * k);
+    if (nch == 1) {
+      RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
+      run_search(ix, *params, q, nq, d, i, s, nullptr);
+      RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
+      RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
+    } else {
+      if (!ix.copy_stream) RBQ_CUDA(cudaStreamCreateWithFlags(&ix.copy_stream, cudaStreamNonBlocking));
+      cudaStream_t cs = ix.copy_stream;
+      std::vector<cudaEvent_t> ev(2 * nch + 2);
+      for (auto& e : ev) RBQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      try {
+        RBQ_CUDA(cudaEventRecord(ev[0], s));  // the scratch buffers exist on s
+        RBQ_CUDA(cudaStreamWaitEvent(cs, ev[0], 0));
+        std::vector<int64_t> b(nch + 1);
+        for (int c = 0; c <= nch; ++c) b[c] = nq * c / nch;
+        for (int c = 0; c < nch; ++c) {
+          RBQ_CUDA(cudaMemcpyAsync(q + b[c] * ix.D, Q_host + b[c] * ix.D, (size_t)(b[c + 1] - b[c]) * ix.D * 4,
+                                   cudaMemcpyHostToDevice, cs));
+          RBQ_CUDA(cudaEventRecord(ev[1 + c], cs));
+        }
+        for (int c = 0; c < nch; ++c) {
+          const int64_t n = b[c + 1] - b[c];
+          RBQ_CUDA(cudaStreamWaitEvent(s, ev[1 + c], 0));
+          run_search(ix, *params, q + b[c] * ix.D, n, d + b[c] * k, i + b[c] * k, s, nullptr);
+          RBQ_CUDA(cudaEventRecord(ev[1 + nch + c], s));
+          RBQ_CUDA(cudaStreamWaitEvent(cs, ev[1 + nch + c], 0));
+          RBQ_CUDA(cudaMemcpyAsync(dist_host + b[c] * k, d + b[c] * k, (size_t)n * k * 4, cudaMemcpyDeviceToHost, cs));
+          RBQ_CUDA(cudaMemcpyAsync(ids_host + b[c] * k, i + b[c] * k, (size_t)n * k * 8, cudaMemcpyDeviceToHost, cs));
+        }
+        RBQ_CUDA(cudaEventRecord(ev[2 * nch + 1], cs));
+        RBQ_CUDA(cudaStreamWaitEvent(s, ev[2 * nch + 1], 0));  // before the scratch is freed on s
+      } catch (...) {
+        cudaStreamSynchronize(cs);
+        for (auto& e : ev) cudaEventDestroy(e);
+        throw;
+      }
+      for (auto& e : ev) RBQ_CUDA(cudaEventDestroy(e));
+    }
     int code = 0;
     RBQ_CUDA(cudaMemcpyAsync(&code, ix.dev_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RBQ_CUDA(cudaStreamSynchronize(s));

@@ -124,6 +124,7 @@ struct Index {
   uint32_t* id2row = nullptr;    // [n_total] row of a global id, 0xFFFFFFFF if not on this shard
   int* dev_err = nullptr;        // [1] device-side error code (tensor-core waits that timed out)
   int32_t* owner = nullptr;      // [K] device copy of owner_host
+  cudaStream_t copy_stream = nullptr;  // host-buffer searches: uploads / downloads beside compute
 
   // Slot order (rebuilt after every add): list l owns slots [list_off[l], list_off[l+1]).
   int64_t* list_off = nullptr;   // [K+1]

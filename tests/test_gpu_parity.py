@@ -241,6 +241,18 @@ def test_search_host_matches_device_search(case):
     assert np.array_equal(i, ih) and np.array_equal(u32(d), u32(dh))
 
 
+def test_search_host_in_overlapped_chunks(case):
+    """Batches of >= 4096 host queries run in chunks whose copies overlap the search; the
+    results equal one device-side search of the whole batch."""
+    idx, oix, X, Q, C, lab = case
+    Qb = np.ascontiguousarray(np.tile(Q, (30, 1))[:8999])
+    Qb[300:] += np.float32(1e-3) * np.random.default_rng(3).standard_normal(Qb[300:].shape).astype(np.float32)
+    idx.nprobe, idx.k_rerank = 8, 40
+    d, i = idx.search(Qb, 10)
+    dh, ih = idx.search_host(Qb, 10)
+    assert np.array_equal(i, ih) and np.array_equal(u32(d), u32(dh))
+
+
 def test_torch_inputs_stay_on_device(case):
     torch = _torch()
     idx, oix, X, Q, C, lab = case
