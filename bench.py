@@ -71,11 +71,13 @@ REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_c
 
 
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled every 5 ms during the timed region,
-    read through NVML (read-only queries; nothing is set)."""
+    """SM clock and clock-event (throttle) reasons sampled every 10 ms during the timed region,
+    read through NVML (read-only queries; nothing is set).  Only rank 0 samples (its own GPU):
+    eight processes polling NVML at once slowed every rank's kernel launches."""
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, active: bool = True):
         self.gpu = gpu_index
+        self.active = active
         self.samples = []
         self.stop = threading.Event()
         self.t = None
@@ -88,6 +90,8 @@ class ClockSampler:
             return nv.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def __enter__(self):
+        if not self.active:
+            return self
         try:
             import pynvml as nv
             nv.nvmlInit()
@@ -101,7 +105,7 @@ class ClockSampler:
                                              int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
                     except Exception:
                         pass
-                    self.stop.wait(0.005)
+                    self.stop.wait(0.010)
 
             self.t = threading.Thread(target=run, daemon=True)
             self.t.start()
@@ -320,7 +324,7 @@ def run_ours(args, cfg):
     # Steps are queued back to back (the host runs ahead of the GPU, as a serving loop does);
     # each step's events bracket its search only, not the L2 flush before it.
     evs = []
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, active=rank == 0) as clk:
         for _ in range(args.steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
