@@ -321,12 +321,17 @@ def run_ours(args, cfg):
     barrier()
     launches0 = _lib.lib().rbq_kernel_launches()
     torch.cuda.nvtx.range_push("timed")
-    # Steps are queued back to back (the host runs ahead of the GPU, as a serving loop does);
-    # each step's events bracket its search only, not the L2 flush before it.
+    # Each step's events bracket its search only, not the L2 flush before it.  One GPU: steps are
+    # queued back to back (the host runs ahead, as a serving loop does).  Several: the ranks
+    # enter every step together through a barrier (which also drains the GPU), because queued
+    # steps let the ranks drift and a step's collectives then wait on the previous step's
+    # stragglers, which measured 20-50 % slower and varied from run to run.
     evs = []
     with ClockSampler(local, active=rank == 0) as clk:
         for _ in range(args.steps):
             flush.zero_()
+            if world > 1:
+                tdist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             step_device()

@@ -69,9 +69,9 @@ typedef struct {
   int32_t probe_split;   /* probe slices per query (0 = auto from nq and P)                    */
   int32_t cand_cap;      /* candidate buffer entries per slice (0 = default 1024)              */
   int32_t coarse_margin; /* extra lists kept by the approximate coarse pass (0 = default)      */
-  int32_t seeded;        /* two-phase scan: the nearest probed list first, its candidates and  */
-                         /* R-th estimate seed the scan of the rest; -1 = auto (on when the     */
-                         /* probes are split into slices), 0 = off (one pass), 1 = on           */
+  int32_t seeded;        /* every slice starts from the nearest probed list's bound seed      */
+                         /* (rbq_bound_seed); -1 = auto (on when the probes are split into      */
+                         /* slices), 0 = off (each slice seeds itself), 1 = on                  */
 } rbq_search_params_t;
 
 typedef struct {
@@ -199,6 +199,15 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
              int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
              uint64_t* stats_dev, void* stream);
+/* Bound seed per query: the R-th smallest RaBitQ upper bound est + f_err * sqrt(g) over the
+ * query's leading owned probed lists that hold >= R vectors (+inf if they hold fewer), the
+ * threshold a pruning scan starts from.  With nprobe = 1 it is the nearest list's seed that
+ * a sharded search all-reduces (min) and hands to rbq_scan as tau0.  tau_dev: f32[nq].
+ * No reference counterpart (the reference seeds with 1.45 x a centroid distance,
+ * searcher_gpu_common.cuh:178-193). */
+int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                   const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, void* stream);
 /* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
  * search time: a host program whose device memory is handed out up front by its own pool
  * (so a library cudaMalloc would fail or break its budget), or a latency-critical search

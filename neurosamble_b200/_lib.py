@@ -73,6 +73,7 @@ SIGNATURES = {
     "rbq_check_errors": [_P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
     "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "rbq_bound_seed": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P],
     "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P,
                          _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],

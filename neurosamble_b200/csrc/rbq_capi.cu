@@ -426,29 +426,25 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
   return sa;
 }
 
-// The list scan of a search: one pass over all probes in sp.slices slices, or (sp.seeded) two
-// phases.  Phase A scans each query's nearest probe alone (one slice; only if this shard owns
-// it) into keys_a [nq, R]; phase B scans probes 1..P-1 in sp.slices slices, slice 0 starting
-// from phase A's candidates and every slice from their R-th distance.  Without the seed every
-// slice starts at +inf and admits its first ~R + tile vectors unpruned.
+// The list scan of a search: one pass over all probes in sp.slices slices.  With sp.seeded
+// every slice starts from the bound seed of the query's nearest probe (computed first, by a
+// seed-only launch over that list) instead of finding its own: split slices then prune from
+// their first vector.
 void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const uint32_t* planes, const float* delta,
-                 const float* k1, int64_t nq, const int32_t* probes, const float* g, unsigned long long* keys_a,
+                 const float* k1, int64_t nq, const int32_t* probes, const float* g, float* tau_a,
                  unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, cudaStream_t s)
 {
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
                                 keys_s, stats);
-  if (sp.seeded && sp.P > 1) {
+  if (sp.seeded && sp.prune) {
     ScanArgs a0 = sa;
     a0.nprobe = 1;
     a0.pstride = sp.P;
     a0.slices = 1;
-    a0.out_keys = keys_a;
+    a0.stats = nullptr;
+    a0.tau_out = tau_a;
     launch_scan(a0, s);
-    sa.probes = probes + 1;
-    sa.g = g + 1;
-    sa.nprobe = sp.P - 1;
-    sa.pstride = sp.P;
-    sa.init_keys = keys_a;
+    sa.tau0 = tau_a;
   }
   launch_scan(sa, s);
   if (sp.slices > 1) launch_merge_keys(keys_s, nq, sp.slices, sp.R, keys, s);
@@ -476,7 +472,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   float* k1 = sc.get<float>(chunk);
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
   unsigned long long* keys = sp.slices > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : keys_s;
-  unsigned long long* keys_a = sp.seeded && sp.P > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : nullptr;
+  float* tau_a = sp.seeded ? sc.get<float>((size_t)chunk) : nullptr;
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
@@ -485,7 +481,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
     launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
     launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
-    search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, keys_a, keys_s, keys, stats, s);
+    search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
     if (params.rerank > 0)
       launch_rerank(ix.X_r, ix.id2row, ix.D, Qc, cn, keys, sp.R, sp.k, dist + a * sp.k, ids + a * sp.k, s);
     else
@@ -1413,6 +1409,28 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
     launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);
+  });
+}
+
+int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                   const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && tau_dev),
+              RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && (probe_stride == 0 || probe_stride >= nprobe), RBQ_ERR_INVALID,
+              "bad seed parameters");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
+    ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
+                                  1, 1, nullptr, nullptr);
+    sa.pstride = probe_stride;
+    sa.tau_out = tau_dev;
+    launch_scan(sa, as_stream(stream));
   });
 }
 

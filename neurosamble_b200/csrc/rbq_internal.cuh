@@ -203,6 +203,9 @@ struct ScanArgs {
   // min(tau0, their largest distance).
   const float* tau0 = nullptr;
   const unsigned long long* init_keys = nullptr;
+  // Seed-only launch (slices 1, prune on): write the slice's starting threshold to tau_out[q]
+  // (the bound seed, or +inf when its lists hold fewer than R vectors) and scan nothing.
+  float* tau_out = nullptr;
   unsigned long long* out_keys;  // [nq, slices, R]
   unsigned long long* stats;     // optional [2]: scanned, admitted
 };

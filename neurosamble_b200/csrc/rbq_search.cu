@@ -725,6 +725,10 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       __syncthreads();
     }
   }
+  if (a.tau_out) {  // seed-only launch: the slice's starting threshold is the answer
+    if (tid == 0) a.tau_out[q] = s_tau;
+    return;
+  }
   unsigned n_scan = 0, n_admit = 0;
   // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
   int cur = 0;
@@ -848,6 +852,8 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
   ScanArgs a = args;
   if (a.pstride == 0) a.pstride = a.nprobe;
   RBQ_CHECK(a.nprobe >= 1 && a.pstride >= a.nprobe, RBQ_ERR_INVALID, "scan: bad probe stride");
+  RBQ_CHECK(!a.tau_out || (a.slices == 1 && a.prune && !a.init_keys), RBQ_ERR_INVALID,
+            "scan: a seed-only launch takes one slice, the prune on and no initial candidates");
   RBQ_CHECK(a.cap >= a.R + kScanTile && (a.cap & (a.cap - 1)) == 0, RBQ_ERR_INVALID,
             "scan: cap must be a power of two >= R + tile");
   RBQ_CHECK(a.Dp == 32 * a.W, RBQ_ERR_INVALID, "scan: padded dim mismatch");

@@ -44,7 +44,8 @@ class IndexIVFRaBitQ:
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
-    scan seeded by the nearest list: -1 = auto, on when the probes are split; 0 off; 1 on).
+    scan slices start from the nearest list's bound seed: -1 = auto, on when the probes are split;
+    0 off; 1 on).
     """
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,

@@ -8,12 +8,12 @@ A search of a batch replicated on every rank runs in four steps:
 1. front end: rank r rotates and coarse-quantises queries [r*nl, (r+1)*nl)
    (nl = ceil(nq / world)); two all-gathers hand every rank the rotated queries and the
    [probes | g] rows of the whole batch, which every rank then 4-bit-quantises (cheap);
-2. seed: each rank scans the nearest probed list of the queries whose nearest list it owns;
-   an all-reduce (min) of the per-query R-th estimate gives every rank the threshold a
-   single GPU reaches after that list, so a shard prunes its lists as tightly as one GPU
-   prunes all of them (without it a shard far from the query admits most of its vectors);
-3. scan the remaining probes from that threshold, starting from the seed candidates, and
-   rerank the shard's candidates (only those under the threshold survive, ~R / world each);
+2. seed: each rank computes the bound seed (the R-th smallest RaBitQ upper bound) of the
+   nearest probed list of the queries whose nearest list it owns; an all-reduce (min) gives
+   every rank that threshold, so a shard prunes its lists as tightly as one GPU prunes all of
+   them (without it a shard far from the query admits most of its vectors);
+3. scan the shard's probed lists from that threshold and rerank the shard's candidates (only
+   those under the threshold survive, ~R / world per shard);
 4. the per-rank [nq, k] results cross NVLink in one all-gather (one packed buffer per rank)
    and are merged on the device by (distance, id).
 
@@ -181,6 +181,12 @@ class LibStages:
             _lib.call("rbq_coarse", self.h, _ptr(qr), qr.shape[0], probes.shape[1], margin, _ptr(probes), _ptr(g),
                       self.st)
 
+    def bound_seed(self, qr, planes, delta, k1, probes, g, R, cap, tau):
+        assert probes.stride(1) == 1 and g.stride() == probes.stride()
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_bound_seed", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0],
+                      _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), R, cap, _ptr(tau), self.st)
+
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
         """probes / g: [nq, p] views with unit column stride and one row stride."""
         assert probes.stride(1) == 1 and g.stride() == probes.stride()
@@ -232,21 +238,17 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)
-    # 2. seed: the nearest probe, scanned by the rank that owns it; min over ranks of the R-th.
-    ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
-    da = torch.empty((nq, R), dtype=torch.float32, device=dev)
-    stages.scan(qr, planes, delta, k1, probes[:, :1], g[:, :1], None, None, R, int(prune), 1, cap, ia, da, stats)
-    tau = da[:, R - 1].contiguous()
-    dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
-    # 3. the other probes from the shared threshold, starting from the seed candidates; rerank
-    #    this shard's candidates.
-    if P > 1:
-        mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
-        md = torch.empty((nq, R), dtype=torch.float32, device=dev)
-        stages.scan(qr, planes, delta, k1, probes[:, 1:], g[:, 1:], tau, (ia, da), R, int(prune), slices, cap, mi,
-                    md, stats)
-    else:
-        mi, md = ia, da
+    # 2. seed: the bound seed of the nearest probe, on the rank that owns it (+inf elsewhere);
+    #    min over ranks.
+    tau = None
+    if prune:
+        tau = torch.empty(nq, dtype=torch.float32, device=dev)
+        stages.bound_seed(qr, planes, delta, k1, probes[:, :1], g[:, :1], R, cap, tau)
+        dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
+    # 3. this shard's probed lists from the shared threshold; rerank its candidates.
+    mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
+    md = torch.empty((nq, R), dtype=torch.float32, device=dev)
+    stages.scan(qr, planes, delta, k1, probes, g, tau, None, R, int(prune), slices, cap, mi, md, stats)
     if k_rerank > 0:
         d = torch.empty((nq, k), dtype=torch.float32, device=dev)
         i = torch.empty((nq, k), dtype=torch.int64, device=dev)

@@ -65,6 +65,8 @@ def lib():
                                _f32p, _f32p, _i64, _i32p, _f32p, _i32, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_void_p,
                                _i64p, _f32p, _i64p]
+        L.orc_bound_seed.argtypes = [_i64p, _u32p, _f32p, _f32p, _f32p, _i32, _u32p, _f32p, _f32p, _i64, _i32p,
+                                     _f32p, _i32, _i32, _i32, _i32, ctypes.c_void_p, _f32p]
         L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
         L.orc_l2_exact.restype = ctypes.c_float
         L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
@@ -280,27 +282,39 @@ def merge_candidates(parts, R):
     return out_i.astype(np.int64), out_d
 
 
+def bound_seed(ix: OracleIndex, planes, delta, k1, probes, g, R, shard_rank=0, shard_count=1, owner=None):
+    """rbq_bound_seed: per query the R-th smallest upper bound est + f_err sqrt(g) over the
+    leading owned lists of `probes` holding >= R vectors (+inf if fewer)."""
+    probes, g = _c(probes, np.int32), _c(g, np.float32)
+    nq, nprobe = probes.shape
+    out = np.empty(nq, np.float32)
+    ow = None
+    if owner is not None:
+        owner = _c(owner, np.int32)
+        ow = owner.ctypes.data_as(ctypes.c_void_p)
+    if nq:
+        lib().orc_bound_seed(ix.list_off, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp,
+                             _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g, nprobe,
+                             R, shard_rank, shard_count, ow, out)
+    return out
+
+
 def seeded_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
                 slices=1, shard_rank=0, shard_count=1, with_stats=False, exchange=False, owner=None):
-    """The two-phase scan of rbq_search (seeded) and of the sharded search.
-
-    Phase A scans each query's nearest probed list alone (on the shard that owns it, one slice);
-    phase B scans the other probes in `slices` slices from phase A's R-th distance (+inf with
-    fewer than R candidates), slice 0 also starting from phase A's candidates, so phase B's
-    result is the answer.  exchange=False: the shard's own phase-A threshold (rbq_search on one
-    index).  exchange=True: the minimum of every shard's phase-A threshold, i.e. the owner's,
-    which is what the sharded search's all-reduce hands to every shard."""
-    A = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, shard_rank,
-             shard_count, with_stats=True, owner=owner)
-    if exchange and shard_count > 1:
-        tau = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, prune, 1, 0, 1)[1][:, R - 1]
+    """The seeded scan of rbq_search and of the sharded search: every slice starts from the
+    bound seed of the query's nearest probed list (bound_seed over probes[:, :1], on the shard
+    that owns that list).  exchange=False: the shard's own seed (+inf on the other shards);
+    exchange=True: the minimum over the shards, i.e. the owner's seed, which the sharded
+    search's all-reduce hands to every shard."""
+    if not prune:
+        return scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank, shard_count,
+                    with_stats=with_stats, owner=owner)
+    if exchange:
+        tau = bound_seed(ix, planes, delta, k1, probes[:, :1], g[:, :1], R)
     else:
-        tau = A[1][:, R - 1]
-    B = scan(ix, Qr, planes, delta, k1, probes[:, 1:], g[:, 1:], R, tile, cap, prune, slices, shard_rank,
-             shard_count, with_stats=True, tau0=tau, init=A[:2], owner=owner)
-    if with_stats:
-        return B[0], B[1], A[2] + B[2]
-    return B[0], B[1]
+        tau = bound_seed(ix, planes, delta, k1, probes[:, :1], g[:, :1], R, shard_rank, shard_count, owner)
+    return scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank, shard_count,
+                with_stats=with_stats, tau0=tau, owner=owner)
 
 
 def list_owners(policy: str, sizes, count: int) -> np.ndarray:
@@ -369,7 +383,7 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     planes, delta, k1, _ = query_prep(Qr, ix.t4)
     R = rerank_depth if rerank_depth > 0 else k
     two = slices > 1 if seeded < 0 else seeded > 0
-    if exchange or (two and nprobe > 1):
+    if exchange or two:
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
                           shard_count, with_stats=True, exchange=exchange, owner=owner)
     else:

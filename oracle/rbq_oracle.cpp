@@ -577,6 +577,46 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
   }
 }
 
+// Bound seed per query (rbq_bound_seed): the R-th smallest upper bound over the leading whole
+// owned lists of the given probes holding >= R vectors, +inf if they hold fewer.
+void orc_bound_seed(const int64_t* list_off, const uint32_t* codes, const float* fadd, const float* frescale,
+                    const float* ferr, int Dp, const uint32_t* planes, const float* delta, const float* k1, int64_t nq,
+                    const int32_t* probes, const float* gq, int nprobe, int R, int shard_rank, int shard_count,
+                    const int32_t* owner, float* tau_out)
+{
+  const int W = Dp / 32;
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t q = 0; q < nq; ++q) {
+    std::vector<int32_t> own_l;
+    std::vector<float> own_g;
+    for (int p = 0; p < nprobe; ++p) {
+      const int l = probes[q * nprobe + p];
+      if ((owner ? owner[l] : l % shard_count) == shard_rank) {
+        own_l.push_back(l);
+        own_g.push_back(gq[q * nprobe + p]);
+      }
+    }
+    std::vector<uint64_t> ub;
+    int64_t have = 0;
+    for (size_t i = 0; i < own_l.size() && have < R; ++i) {
+      const int l = own_l[i];
+      const float g = own_g[i];
+      for (int64_t s = list_off[l]; s < list_off[l + 1]; ++s, ++have) {
+        const int32_t acc = orc_popcount_ip(planes + (size_t)q * 4 * W, codes + (size_t)s * W, W);
+        const float ip = (float)acc * delta[q];
+        const float est = (fadd[s] + g) + frescale[s] * (ip + k1[q]);
+        ub.push_back(make_key(est + ferr[s] * sqrtf(g), (uint32_t)have));
+      }
+    }
+    if ((int64_t)ub.size() < R) {
+      tau_out[q] = INFINITY;
+    } else {
+      std::nth_element(ub.begin(), ub.begin() + (R - 1), ub.end());
+      tau_out[q] = from_ordered_bits((uint32_t)(ub[(size_t)R - 1] >> 32));
+    }
+  }
+}
+
 // Scan (a9-a11): for every query the top-R candidates by (estimated distance, id).
 // probes/g: [nq, nprobe] from orc_coarse.  tau0 (optional, [nq]): every slice of query q starts
 // with threshold tau0[q] instead of +inf (a threshold seeded by an earlier scan).  init_ids /

@@ -487,3 +487,28 @@ def test_merge_results_matches_oracle(oracle, parts, k):
     wi, wd = oracle.merge_candidates([(i[p], d[p]) for p in range(parts)], k)
     assert np.array_equal(oi.cpu().numpy(), wi)
     assert np.array_equal(u32(od.cpu().numpy()), u32(wd))
+
+
+@pytest.mark.parametrize("nprobe,R", [(1, 30), (1, 400), (5, 100)])
+def test_bound_seed_matches_oracle(oracle, case, nprobe, R):
+    """rbq_bound_seed: the R-th smallest upper bound over the leading whole lists holding >= R
+    vectors (+inf when the probes hold fewer), bit-exact; also on a shard, where a query whose
+    nearest list lives elsewhere gets +inf."""
+    torch = _torch()
+    idx, oix, X, Q, C, lab = case
+    nq = Q.shape[0]
+    Qr = oracle.rotate(Q, oix.P)
+    qr, planes, delta, k1 = _query_stage(idx, Qr)
+    P = 12
+    probes = torch.empty((nq, P), dtype=torch.int32, device="cuda")
+    g = torch.empty((nq, P), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), nq, P, 0, ptr(probes), ptr(g), stream())
+    p2, g2 = oracle.coarse(Qr, oix.c_rot, P)
+    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
+    tau = torch.empty(nq, dtype=torch.float32, device="cuda")
+    call("rbq_bound_seed", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, P,
+         R, 0, ptr(tau), stream())
+    want = oracle.bound_seed(oix, pl2, d2, k2, p2[:, :nprobe], g2[:, :nprobe], R)
+    got = tau.cpu().numpy()
+    assert np.array_equal(u32(got), u32(want))
+    assert np.isfinite(want).any() and (R < 300 or np.isinf(want).any())

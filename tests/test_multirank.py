@@ -135,6 +135,12 @@ class _OracleStages:
         probes.copy_(torch.from_numpy(p))
         g.copy_(torch.from_numpy(gg))
 
+    def bound_seed(self, qr, planes, delta, k1, probes, g, R, cap, tau):
+        import torch
+        t = self.O.bound_seed(self.ix, planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(), probes.numpy(),
+                              g.numpy(), R, shard_rank=self.rank, shard_count=self.world, owner=self.owner)
+        tau.copy_(torch.from_numpy(t))
+
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
         import torch
         oi, od = self.O.scan(self.ix, qr.numpy(), planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(),
