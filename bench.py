@@ -248,7 +248,7 @@ def run_ours(args, cfg):
     Xd = torch.from_numpy(X).to(dev)
     t = time.perf_counter()
     if world > 1:
-        from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ, gather_results, merge_results
+        from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ
         index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local)
         local_ix = index.local
     else:
