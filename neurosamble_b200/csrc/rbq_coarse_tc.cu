@@ -11,10 +11,11 @@
 // stored K-major with the 128-byte swizzle (16-byte unit u of row r of an 8-row atom lives at
 // u ^ r).  The operand tiles arrive by TMA (cp.async.bulk.tensor, 2-D tiles of the row-major
 // query and centroid matrices, zero fill past the last row; no multicast) into a ring of four
-// shared-memory stages, so up to four k-chunks are in flight while the tensor core works.  One
+// shared-memory stages, so up to three k-chunks are in flight while the tensor core works.  One
 // thread issues the loads and the MMAs: a stage is refilled once the MMAs that read it have
 // committed to its "empty" mbarrier.  The epilogue reads the accumulator with tcgen05.ld
-// (warp w: TMEM lanes 32*(w%4).., columns half w/4) and writes the scores.  Every mbarrier
+// (warp w: TMEM lanes 32*(w%4).., columns half w/4; lane = query row) and turns each 32 x 32
+// block through shared memory, so that every store writes 32 consecutive scores of one row.  Every mbarrier
 // wait is bounded: on time-out the kernel records an error code in err[0], waits (bounded)
 // for its copies and MMAs in flight, frees its TMEM and returns.
 #include <cuda.h>
@@ -35,7 +36,8 @@ constexpr int kTcN = 256;        // centroids per accumulator (TMEM columns)
 constexpr int kTcKc = 32;        // tf32 values per 128-byte smem row
 constexpr int kTcThreads = 256;
 constexpr int kTcStageBytes = (kTcM + kTcN) * 128;  // A chunk (16 KB) + B chunk (32 KB)
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 3;
+constexpr int kTcEpiPitch = 33;  // floats per row of a warp's 32 x 32 epilogue tile (bank-conflict free)
 constexpr uint32_t kWaitLimit = 1u << 26;           // bounded mbarrier polling
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const __grid_c
   // 1024-byte aligned stages (the swizzle pattern is taken from the address bits).
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  float* epi = reinterpret_cast<float*>(base + kTcStages * kTcStageBytes);  // [8 warps][32][kTcEpiPitch]
   __shared__ __align__(8) unsigned long long s_full[kTcStages], s_empty[kTcStages];
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
@@ -226,21 +229,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const __grid_c
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     {
       const int quarter = warp & 3, half = warp >> 2;
-      const int row = quarter * 32 + lane;
-      const int q = q0 + row;
+      float* tile = epi + warp * 32 * kTcEpiPitch;
 #pragma unroll 1
       for (int j = 0; j < (kTcN / 2) / 32; ++j) {
         const int col = half * (kTcN / 2) + j * 32;
         float v[32];
         tc_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col, v);
-        if (q < nq) {
-          float* out = S + (size_t)q * K + n0 + col;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = n0 + col + i;
-            if (c < K) out[i] = __ldg(cn2 + c) - 2.0f * v[i];
-          }
+        for (int i = 0; i < 32; ++i) tile[lane * kTcEpiPitch + i] = v[i];
+        __syncwarp();
+        const int c = n0 + col + lane;
+        const float cn = c < K ? __ldg(cn2 + c) : 0.0f;
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          const int q = q0 + quarter * 32 + r;
+          if (q < nq && c < K) S[(size_t)q * K + c] = cn - 2.0f * tile[r * kTcEpiPitch + lane];
         }
+        __syncwarp();
       }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -306,7 +311,7 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
   if (nq <= 0) return;
   RBQ_CHECK(coarse_tc_supported(dp), RBQ_ERR_INVALID, "coarse (tensor cores): padded dim must be a multiple of 32");
   RBQ_CHECK(nq <= 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "coarse (tensor cores): bad sizes");
-  const size_t smem = (size_t)kTcStages * kTcStageBytes + 1024;
+  const size_t smem = (size_t)kTcStages * kTcStageBytes + (size_t)(kTcThreads / 32) * 32 * kTcEpiPitch * 4 + 1024;
   RBQ_CUDA(cudaFuncSetAttribute(coarse_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const CUtensorMap tmQ = row_major_map(A, nq, dp, kTcM);
   const CUtensorMap tmC = row_major_map(C, K, dp, kTcN);
