@@ -389,7 +389,7 @@ def run_ours(args, cfg):
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
     seeded = world > 1 or args.seeded == 1
-    roof, roof_rr, _ = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
+    roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
     scan_share = round(roof["launch_ms"] / ms, 3)
 
     # ---- config 2's batch sweep (B = 1, 64, 1024): device-resident queries, same index
@@ -539,7 +539,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     roof_rr = {"bound": "hbm", "achieved": round(ach_r, 1), "peak": peak, "unit": "GB/s",
                "frac": round(ach_r / peak, 4), "kernel": "rbq rerank_kernel (+ id->key prologue)",
                "algorithmic_bytes_per_launch": rr_bytes, "launch_ms": round(rr_ms, 4)}
-    return roof, roof_rr, None
+    return roof, roof_rr
 
 
 def cpu_baseline(ix, X, Q, cfg, R):

@@ -80,18 +80,6 @@ def gather_results(dist_t: torch.Tensor, ids_t: torch.Tensor, group=None):
     return unpack_gathered(out, world, dist_t.shape[0], dist_t.shape[1])
 
 
-def merge_results(dist_all: torch.Tensor, ids_all: torch.Tensor):
-    """[parts, nq, k] on a CUDA device -> [nq, k] by (distance, id), in librbq.so."""
-    parts, nq, k = dist_all.shape
-    dev = dist_all.device.index
-    out_d = torch.empty((nq, k), dtype=torch.float32, device=dist_all.device)
-    out_i = torch.empty((nq, k), dtype=torch.int64, device=dist_all.device)
-    with torch.cuda.device(dev):
-        _lib.call("rbq_merge_results", _ptr(dist_all.contiguous()), _ptr(ids_all.contiguous()), parts, nq, k,
-                  _ptr(out_d), _ptr(out_i), _stream_ptr(dev))
-    return out_d, out_i
-
-
 class ShardedIndexIVFRaBitQ:
     """The IndexIVFRaBitQ API over `world` ranks of a process group (NCCL)."""
 
