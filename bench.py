@@ -186,7 +186,24 @@ def run_reference(args, cfg):
                           for a in range(0, cfg["n"], 65536)]).astype(np.uint32)
     oix = O.build(X, C, lab, P, t4)
     log(f"[reference] build {time.perf_counter() - t:.1f}s, threads={O.threads()}")
-    R = args.rerank or cfg["rerank"]
+    # the same recall rule as our arm: the smallest rerank depth on the ladder whose recall@k
+    # reaches the target, measured here on a 500-query sample against exact neighbours
+    recalls = {}
+    if args.rerank:
+        R = args.rerank
+    else:
+        ns = min(500, len(Q))
+        xn = (X * X).sum(1)
+        gt = np.concatenate([np.argpartition(xn[None, :] - 2.0 * (Q[a:a + 100] @ X.T), cfg["k"], axis=1)[:, :cfg["k"]]
+                             for a in range(0, ns, 100)])
+        R = RERANK_LADDER[-1]
+        for cand in RERANK_LADDER:
+            _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand)
+            recalls[cand] = O.recall(ids, gt)
+            if recalls[cand] >= RECALL_TARGET:
+                R = cand
+                break
+        log(f"[reference] recall@{cfg['k']} on {ns} queries by rerank depth: {recalls}; using R={R}")
     steps = []
     n_sample = None
     for s in range(args.warmup + args.steps):
@@ -199,7 +216,7 @@ def run_reference(args, cfg):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
-            "config": workload(cfg, R),
+            "config": dict(workload(cfg, R), recall_by_rerank_sample=recalls),
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
                              "sample": f"{n_sample} of {cfg['nq']} queries per step, same index and parameters"},
             "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
