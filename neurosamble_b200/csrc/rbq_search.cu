@@ -164,8 +164,10 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
 // Exact refine of the shortlist: g = |a - c|^2 with lane l of a warp summing double(a_j - c_j)^2
 // over j = l, l+32, ... and an xor butterfly (16..1) of double adds, rounded to float (the
 // oracle's orc_coarse / orc_assign distance); keep the p smallest (g, list id), ascending.
-// One CTA per query, one warp per candidate.
+// One CTA per query, one warp per candidate; with d = 32 * EPL the warp loads all EPL values
+// of two candidates before the arithmetic (EPL = 0: the generic loop for other d).
 // ---------------------------------------------------------------------------------------
+template <int EPL>
 __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restrict__ A, const float* __restrict__ C,
                                                           int d, const int32_t* __restrict__ cand, int m, int p,
                                                           int mp2, int32_t* __restrict__ probes,
@@ -179,18 +181,46 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
   for (int i = threadIdx.x; i < mp2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
-  for (int i = warp; i < m; i += nwarps) {
-    const int c = cand[q * m + i];
-    if (c < 0) continue;
-    const float* cr = C + (size_t)c * d;
-    double s = 0.0;
-    for (int j = lane; j < d; j += 32) {
-      const float df = __fsub_rn(__ldg(cr + j), a[j]);
-      s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
-    }
+  auto finish = [&](int i, int c, double s) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    if (lane == 0) keys[i] = make_key((float)s, (uint32_t)c);
+    if (lane == 0 && c >= 0) keys[i] = make_key((float)s, (uint32_t)c);
+  };
+  if constexpr (EPL > 0) {
+    for (int i0 = warp * 2; i0 < m; i0 += nwarps * 2) {
+      int c[2];
+      float x[2][EPL];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        c[u] = i0 + u < m ? cand[q * m + i0 + u] : -1;
+        const float* cr = C + (size_t)(c[u] < 0 ? 0 : c[u]) * d;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) x[u][e] = c[u] >= 0 ? __ldg(cr + lane + 32 * e) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        double s = 0.0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float df = __fsub_rn(x[u][e], a[lane + 32 * e]);
+          s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
+        }
+        finish(i0 + u, c[u], s);
+      }
+    }
+  } else {
+    for (int i = warp; i < m; i += nwarps) {
+      const int c = cand[q * m + i];
+      double s = 0.0;
+      if (c >= 0) {
+        const float* cr = C + (size_t)c * d;
+        for (int j = lane; j < d; j += 32) {
+          const float df = __fsub_rn(__ldg(cr + j), a[j]);
+          s = __dadd_rn(s, __dmul_rn((double)df, (double)df));
+        }
+      }
+      finish(i, c, s);
+    }
   }
   __syncthreads();
   block_bitonic_sort(keys, mp2);
@@ -206,6 +236,16 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   }
 }
 
+template <int EPL>
+static void launch_refine_e(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m, int p,
+                            int mp2, size_t smem, int32_t* probes, float* g, cudaStream_t s)
+{
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(refine_topp_kernel<EPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  refine_topp_kernel<EPL><<<(unsigned)nq, 256, smem, s>>>(A, C, d, cand, m, p, mp2, probes, g);
+  RBQ_LAUNCHED();
+}
+
 void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m, int p,
                         int32_t* probes, float* g, cudaStream_t s)
 {
@@ -213,10 +253,15 @@ void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const
   const int mp2 = next_pow2(m < 2 ? 2 : m);
   const size_t smem = (size_t)mp2 * 8 + (size_t)d * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "coarse: refine shortlist too large");
-  if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(refine_topp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  refine_topp_kernel<<<(unsigned)nq, 256, smem, s>>>(A, C, d, cand, m, p, mp2, probes, g);
-  RBQ_LAUNCHED();
+  switch (d % 32 == 0 ? d / 32 : 0) {
+    case 1: launch_refine_e<1>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 2: launch_refine_e<2>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 4: launch_refine_e<4>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 8: launch_refine_e<8>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 12: launch_refine_e<12>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 24: launch_refine_e<24>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    default: launch_refine_e<0>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+  }
 }
 
 // ---------------------------------------------------------------------------------------
