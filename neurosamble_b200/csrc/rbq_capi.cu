@@ -450,8 +450,9 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
   if (sp.slices > 1) launch_merge_keys(keys_s, nq, sp.slices, sp.R, keys, s);
 }
 
+// Qr_pre (optional): the batch already rotated ([nq, Dp]); the search then skips the rotation.
 void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, int64_t nq, float* dist, int64_t* ids,
-                cudaStream_t s, uint64_t* stats)
+                cudaStream_t s, uint64_t* stats, const float* Qr_pre = nullptr)
 {
   RBQ_CHECK(nq >= 0, RBQ_ERR_INVALID, "search: negative query count");
   if (nq == 0) return;
@@ -462,7 +463,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   const int64_t by_scores = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4));
   const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_scores, 65535ll * 64));
   Scratch sc(s);
-  float* Qr = sc.get<float>((size_t)chunk * ix.Dp);
+  float* Qr_buf = Qr_pre ? nullptr : sc.get<float>((size_t)chunk * ix.Dp);
   float* S = sc.get<float>((size_t)chunk * ix.K);
   int32_t* cand = sc.get<int32_t>((size_t)chunk * sp.m);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
@@ -476,7 +477,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
-    launch_rotate(Qc, cn, ix.D, ix.Dp, ix.P, Qr, s);
+    const float* Qr = Qr_pre ? Qr_pre + a * ix.Dp : Qr_buf;
+    if (!Qr_pre) launch_rotate(Qc, cn, ix.D, ix.Dp, ix.P, Qr_buf, s);
     launch_coarse_scores_tc(Qr, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
     launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
     launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
@@ -853,47 +855,37 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
     cudaStream_t s = as_stream(stream);
     const int k = params->k;
     RBQ_CHECK(k >= 1, RBQ_ERR_INVALID, "search: k must be >= 1");
-    // Batches of >= 4096 queries run in two halves: the second half's upload and the first
-    // half's download (on a copy stream, ordered by events) overlap the search of the other
-    // half.  Halves of >= 2048 queries plan the same single-slice search as the whole batch,
-    // so the results do not depend on the split.
-    constexpr int64_t kMinChunk = 2048;
-    const int nch = nq >= 2 * kMinChunk ? 2 : 1;
+    // Batches of >= 4096 queries are uploaded in two halves on a copy stream: the first half is
+    // rotated while the second crosses PCIe, then the whole batch is searched at once (the same
+    // plan and results as a device-side search of the batch).
+    constexpr int64_t kMinHalf = 2048;
     Scratch sc(s);
     float* q = sc.get<float>((size_t)nq * ix.D);
     float* d = sc.get<float>((size_t)nq * k);
     int64_t* i = sc.get<int64_t>((size_t)nq * k);
-    if (nch == 1) {
+    if (nq < 2 * kMinHalf) {
       RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
       run_search(ix, *params, q, nq, d, i, s, nullptr);
-      RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
-      RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
     } else {
       if (!ix.copy_stream) RBQ_CUDA(cudaStreamCreateWithFlags(&ix.copy_stream, cudaStreamNonBlocking));
       cudaStream_t cs = ix.copy_stream;
-      std::vector<cudaEvent_t> ev(2 * nch + 2);
+      float* qr = sc.get<float>((size_t)nq * ix.Dp);
+      cudaEvent_t ev[3];
       for (auto& e : ev) RBQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
       try {
+        const int64_t h = nq / 2;
         RBQ_CUDA(cudaEventRecord(ev[0], s));  // the scratch buffers exist on s
         RBQ_CUDA(cudaStreamWaitEvent(cs, ev[0], 0));
-        std::vector<int64_t> b(nch + 1);
-        for (int c = 0; c <= nch; ++c) b[c] = nq * c / nch;
-        for (int c = 0; c < nch; ++c) {
-          RBQ_CUDA(cudaMemcpyAsync(q + b[c] * ix.D, Q_host + b[c] * ix.D, (size_t)(b[c + 1] - b[c]) * ix.D * 4,
-                                   cudaMemcpyHostToDevice, cs));
-          RBQ_CUDA(cudaEventRecord(ev[1 + c], cs));
-        }
-        for (int c = 0; c < nch; ++c) {
-          const int64_t n = b[c + 1] - b[c];
-          RBQ_CUDA(cudaStreamWaitEvent(s, ev[1 + c], 0));
-          run_search(ix, *params, q + b[c] * ix.D, n, d + b[c] * k, i + b[c] * k, s, nullptr);
-          RBQ_CUDA(cudaEventRecord(ev[1 + nch + c], s));
-          RBQ_CUDA(cudaStreamWaitEvent(cs, ev[1 + nch + c], 0));
-          RBQ_CUDA(cudaMemcpyAsync(dist_host + b[c] * k, d + b[c] * k, (size_t)n * k * 4, cudaMemcpyDeviceToHost, cs));
-          RBQ_CUDA(cudaMemcpyAsync(ids_host + b[c] * k, i + b[c] * k, (size_t)n * k * 8, cudaMemcpyDeviceToHost, cs));
-        }
-        RBQ_CUDA(cudaEventRecord(ev[2 * nch + 1], cs));
-        RBQ_CUDA(cudaStreamWaitEvent(s, ev[2 * nch + 1], 0));  // before the scratch is freed on s
+        RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)h * ix.D * 4, cudaMemcpyHostToDevice, cs));
+        RBQ_CUDA(cudaEventRecord(ev[1], cs));
+        RBQ_CUDA(cudaMemcpyAsync(q + h * ix.D, Q_host + h * ix.D, (size_t)(nq - h) * ix.D * 4,
+                                 cudaMemcpyHostToDevice, cs));
+        RBQ_CUDA(cudaEventRecord(ev[2], cs));
+        RBQ_CUDA(cudaStreamWaitEvent(s, ev[1], 0));
+        launch_rotate(q, h, ix.D, ix.Dp, ix.P, qr, s);
+        RBQ_CUDA(cudaStreamWaitEvent(s, ev[2], 0));
+        launch_rotate(q + h * ix.D, nq - h, ix.D, ix.Dp, ix.P, qr + h * ix.Dp, s);
+        run_search(ix, *params, q, nq, d, i, s, nullptr, qr);
       } catch (...) {
         cudaStreamSynchronize(cs);
         for (auto& e : ev) cudaEventDestroy(e);
@@ -901,6 +893,8 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
       }
       for (auto& e : ev) RBQ_CUDA(cudaEventDestroy(e));
     }
+    RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
+    RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
     int code = 0;
     RBQ_CUDA(cudaMemcpyAsync(&code, ix.dev_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RBQ_CUDA(cudaStreamSynchronize(s));
