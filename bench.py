@@ -133,22 +133,28 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------
 # reference arm: the CPU restatement of the reference search, all host cores
 # --------------------------------------------------------------------------------------
-def kmeans_numpy(X, k, iters, per_list, seed):
-    """Training for the CPU arm (not timed): strided sample, BLAS assignment, Lloyd updates."""
+def blas_assign(A, C):
+    """Nearest centre by a BLAS argmin of |c|^2 - 2 a.c (the CPU arm's build; not timed)."""
+    out = np.empty(A.shape[0], np.uint32)
+    cn = (C * C).sum(1)[None, :]
+    for a in range(0, A.shape[0], 65536):
+        out[a:a + 65536] = np.argmin(cn - 2.0 * A[a:a + 65536] @ C.T, axis=1)
+    return out
+
+
+def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
+    """Training for the CPU arm (not timed): the strided sample the library trains on, then the
+    same trainer as our arm (balanced k-means restated in the oracle, or Lloyd), BLAS E steps."""
     n = X.shape[0]
     m = min(n, per_list * k)
     S = X[(np.arange(m, dtype=np.int64) * n) // m]
+    if kind == "balanced":
+        from oracle import oracle as O
+        return O.kmeans_balanced(S, k, iters, assign_fn=blas_assign)
     C = S[(np.arange(k, dtype=np.int64) * m) // k].copy()
 
-    def assign(A):
-        out = np.empty(A.shape[0], np.int64)
-        for a in range(0, A.shape[0], 65536):
-            blk = A[a:a + 65536]
-            out[a:a + 65536] = np.argmin((C * C).sum(1)[None, :] - 2.0 * blk @ C.T, axis=1)
-        return out
-
     for _ in range(iters):
-        lab = assign(S)
+        lab = blas_assign(S, C)
         sums = np.zeros((k, X.shape[1]), np.float64)
         np.add.at(sums, lab, S)
         cnt = np.bincount(lab, minlength=k)
@@ -180,7 +186,7 @@ def run_reference(args, cfg):
     P = O.make_rotation(dp, 7)
     t4 = O.query_scale(dp, 7)
     t = time.perf_counter()
-    C = kmeans_numpy(X, cfg["nlist"], 20, 256, cfg["seed"])
+    C = kmeans_numpy(X, cfg["nlist"], 20, 256, cfg["seed"], args.kmeans)
     cn = (C * C).sum(1)[None, :]
     lab = np.concatenate([np.argmin(cn - 2.0 * X[a:a + 65536] @ C.T, axis=1)
                           for a in range(0, cfg["n"], 65536)]).astype(np.uint32)
@@ -216,7 +222,7 @@ def run_reference(args, cfg):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
-            "config": dict(workload(cfg, R), recall_by_rerank_sample=recalls),
+            "config": dict(workload(cfg, R, args.kmeans), recall_by_rerank_sample=recalls),
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
                              "sample": f"{n_sample} of {cfg['nq']} queries per step, same index and parameters"},
             "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -228,11 +234,12 @@ def metric_name():
     return "queries/sec @ recall@10>=0.95, 1M x 256 IVF-RaBitQ (nlist 1024, nprobe 32, k 10)"
 
 
-def workload(cfg, R):
+def workload(cfg, R, kmeans):
     return {"workload": "BASELINE config 2: 1M x 256 f32, 4096-centre mixture sigma 0.25, L2-normalised; "
                         "10k perturbed-row queries; IVF-RaBitQ 1-bit codes, 4-bit queries",
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
-            "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)"}
+            "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
+            "kmeans": kmeans}
 
 
 # --------------------------------------------------------------------------------------
@@ -266,10 +273,10 @@ def run_ours(args, cfg):
     t = time.perf_counter()
     if world > 1:
         from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ
-        index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local)
+        index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans)
         local_ix = index.local
     else:
-        index = IndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local)
+        index = IndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans)
         local_ix = index
     index.train(Xd)
     index.add(Xd)
@@ -440,7 +447,9 @@ def run_ours(args, cfg):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes x 4-bit planes (popc) + f32",
                 "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
-                "config": dict(workload(cfg, R), parallelism=f"lists sharded l % {world}" if world > 1 else "1 GPU",
+                "config": dict(workload(cfg, R, args.kmeans),
+                               parallelism=(f"lists sharded over {world} GPUs (balanced by size^2)" if world > 1
+                                            else "1 GPU"),
                                recall_at_10=recalls.get(R), recall_by_rerank=recalls),
                 "clocks": clk.summary(),
                 "e2e": {"value": round(e2e, 2), "unit": "queries/s", "h2d_bytes_per_step": nq * cfg["d"] * 4,
@@ -586,6 +595,8 @@ def main():
     ap.add_argument("--nq", type=int, default=0, help="query batch override")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the B = 1 / 64 / 1024 sweep")
+    ap.add_argument("--kmeans", default="balanced", choices=["balanced", "lloyd"],
+                    help="coarse trainer of both arms (balanced: the reference's build algorithm)")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
                     help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()

@@ -48,7 +48,18 @@ typedef struct {
   int32_t shard_count;                  /* 1 = unsharded                                      */
   int32_t shard_policy;                 /* list -> rank map: RBQ_SHARD_ROUND_ROBIN (l % count) */
                                         /* or RBQ_SHARD_BALANCED (fixed at the first add)     */
+  int32_t kmeans_kind;                  /* RBQ_KMEANS_BALANCED (reference) or RBQ_KMEANS_LLOYD */
 } rbq_index_params_t;
+
+/* Coarse quantiser trainers.  BALANCED: hierarchical balanced k-means, the algorithm of
+ * cuvs::cluster::kmeans::fit(balanced_params) that build calls (ivf_rabitq.cu:141-147,
+ * src/cluster/detail/kmeans_balanced.cuh:443-1134): ~sqrt(K) mesoclusters, fine clusters
+ * per mesocluster in proportion to its size, then a fine-tuning pass; every EM pass moves
+ * the centres of clusters below a size threshold towards rows of large clusters.  Made
+ * deterministic (fixed rebalancing order, double-accumulated means).  LLOYD: plain Lloyd
+ * iterations from evenly strided initial rows. */
+#define RBQ_KMEANS_BALANCED 0
+#define RBQ_KMEANS_LLOYD 1
 
 /* List ownership across shards.  ROUND_ROBIN: list l on rank l % shard_count (the layout
  * BASELINE's sharded configuration names).  BALANCED: the lists, taken by decreasing size^2
@@ -83,6 +94,7 @@ typedef struct {
   int64_t device_bytes; /* index memory held on the device */
   int32_t shard_policy; /* RBQ_SHARD_*                      */
   int32_t owners_fixed; /* 1 once the list -> rank map is final (ROUND_ROBIN: always) */
+  int32_t kmeans_kind;  /* RBQ_KMEANS_*                     */
 } rbq_index_info_t;
 
 /* ---- errors / defaults ------------------------------------------------------------------ */
@@ -110,7 +122,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out);
 int rbq_index_free(rbq_index_t* index);
 int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out);
 
-/* Train the coarse quantiser (seeded Lloyd k-means on a strided sample) on device rows.
+/* Train the coarse quantiser (k-means of kind params.kmeans_kind on an evenly strided sample
+ * of at most max_train_points_per_cluster * K rows) on device rows.
  * Replaces the k-means part of build (src/neighbors/ivf_rabitq.cu:117-152).  Synchronises. */
 int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream);
 

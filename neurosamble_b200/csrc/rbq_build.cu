@@ -199,14 +199,20 @@ void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t
 
 // ---------------------------------------------------------------------------------------
 // k-means centroid update: C[c] = mean of member rows, members in the order given by
-// `order` (host counting sort), double accumulation; empty lists keep their centroid.
+// `order` (host counting sort), double accumulation.  Empty lists keep their centroid
+// (Lloyd) or become the zero vector (balanced k-means: the reference's division by a zero
+// size yields 0, kmeans_balanced.cuh:295-300).
 // ---------------------------------------------------------------------------------------
 __global__ void centroid_update_kernel(const float* __restrict__ X, int D, const int64_t* __restrict__ off,
-                                       const uint32_t* __restrict__ order, float* __restrict__ C)
+                                       const uint32_t* __restrict__ order, float* __restrict__ C, int zero_empty)
 {
   const int c = blockIdx.x;
   const int64_t a = off[c], b = off[c + 1];
-  if (b <= a) return;
+  if (b <= a) {
+    if (zero_empty)
+      for (int j = threadIdx.x; j < D; j += blockDim.x) C[(size_t)c * D + j] = 0.0f;
+    return;
+  }
   for (int j = threadIdx.x; j < D; j += blockDim.x) {
     double s = 0.0;
     for (int64_t m = a; m < b; ++m) s += (double)X[(size_t)order[m] * D + j];
@@ -215,9 +221,37 @@ __global__ void centroid_update_kernel(const float* __restrict__ X, int D, const
 }
 
 void launch_centroid_update(const float* X, int64_t /*n*/, int D, const uint32_t* /*labels*/, const int64_t* off,
-                            const uint32_t* order, int K, float* C, cudaStream_t s)
+                            const uint32_t* order, int K, float* C, bool zero_empty, cudaStream_t s)
 {
-  centroid_update_kernel<<<K, 128, 0, s>>>(X, D, off, order, C);
+  if (K <= 0) return;
+  centroid_update_kernel<<<K, 128, 0, s>>>(X, D, off, order, C, zero_empty ? 1 : 0);
+  RBQ_LAUNCHED();
+}
+
+// ---------------------------------------------------------------------------------------
+// Balanced k-means rebalancing (kmeans_balanced.cuh:443-496): a small cluster's centre moves
+// towards a row of a large cluster, C[l] = (wc * C[li] + 1 * X[i]) / (wc + 1), evaluated in
+// that order in round-to-nearest float arithmetic.  adj[4a .. 4a+3] = {l, li, i, wc}; the
+// host picked them (li is never an adjusted cluster, so the reads do not race the writes).
+// ---------------------------------------------------------------------------------------
+__global__ void adjust_centers_kernel(float* __restrict__ C, int D, const float* __restrict__ X,
+                                      const int64_t* __restrict__ adj)
+{
+  const int64_t* e = adj + 4 * (size_t)blockIdx.x;
+  const int64_t l = e[0], li = e[1], i = e[2];
+  const float wc = (float)e[3];
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float v = 0.0f;
+    v = __fadd_rn(v, __fmul_rn(wc, C[(size_t)li * D + j]));
+    v = __fadd_rn(v, __fmul_rn(1.0f, X[(size_t)i * D + j]));
+    C[(size_t)l * D + j] = __fdiv_rn(v, __fadd_rn(wc, 1.0f));
+  }
+}
+
+void launch_adjust_centers(float* C, int D, const float* X, const int64_t* adj, int n_adj, cudaStream_t s)
+{
+  if (n_adj <= 0) return;
+  adjust_centers_kernel<<<n_adj, 128, 0, s>>>(C, D, X, adj);
   RBQ_LAUNCHED();
 }
 

@@ -151,10 +151,9 @@ void install_centroids(Index& ix, cudaStream_t s)
 // Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d]: approximate
 // shortlist (tcgen05 tf32 scores when d is a multiple of 32 and the rows are 16-byte aligned,
 // else fp32 SIMT), then the double-accumulated distance over the shortlist decides.
-void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, int d,
+void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, int K, int d,
                    uint32_t* labels_out, cudaStream_t s)
 {
-  const int K = ix.K;
   const int m = std::min(K, 32);  // shortlist width: far beyond the tf32 ranking error
   const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65535 * 64, (256ll << 20) / ((int64_t)K * 4)));
   Scratch sc(s);
@@ -267,7 +266,7 @@ void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, 
   if (labels_dev) {
     RBQ_CUDA(cudaMemcpyAsync(lab, labels_dev, n * 4, cudaMemcpyDeviceToDevice, s));
   } else {
-    assign_labels(ix, X, n, ix.C, ix.C_n2, ix.D, lab, s);
+    assign_labels(ix, X, n, ix.C, ix.C_n2, ix.K, ix.D, lab, s);
   }
   std::vector<uint32_t> hl(n);
   RBQ_CUDA(cudaMemcpyAsync(hl.data(), lab, n * 4, cudaMemcpyDeviceToHost, s));
@@ -319,6 +318,237 @@ void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, 
   relayout(ix, s);
 }
 
+// ---------------------------------------------------------------------------------------
+// k-means.  One EM problem: rows X [n, D] (device), k centres C [k, D] (device), labels on
+// device and host, cluster sizes on the host.
+// ---------------------------------------------------------------------------------------
+struct KmProblem {
+  const float* X = nullptr;
+  int64_t n = 0;
+  int k = 0;
+  float* C = nullptr;
+  uint32_t* lab_d = nullptr;
+  float* cn2 = nullptr;
+  std::vector<uint32_t> lab;
+  std::vector<int64_t> size;
+};
+
+// E step: exact nearest centre of every row (ties -> lower id), labels copied to the host.
+void km_predict(const Index& ix, KmProblem& p, cudaStream_t s)
+{
+  launch_row_norms(p.C, p.k, ix.D, p.cn2, s);
+  assign_labels(ix, p.X, p.n, p.C, p.cn2, p.k, ix.D, p.lab_d, s);
+  p.lab.resize(p.n);
+  RBQ_CUDA(cudaMemcpyAsync(p.lab.data(), p.lab_d, p.n * 4, cudaMemcpyDeviceToHost, s));
+  RBQ_CUDA(cudaStreamSynchronize(s));
+}
+
+// M step: centres = means of their rows (members summed in ascending row order, in double),
+// sizes from the same labels.
+void km_update(const Index& ix, KmProblem& p, bool zero_empty, cudaStream_t s)
+{
+  std::vector<int64_t> off, order;
+  counting_sort(p.lab, p.k, off, order);
+  std::vector<uint32_t> ho(p.n);
+  for (int64_t i = 0; i < p.n; ++i) ho[i] = (uint32_t)order[i];
+  p.size.resize(p.k);
+  for (int c = 0; c < p.k; ++c) p.size[c] = off[c + 1] - off[c];
+  Scratch sc(s);
+  int64_t* off_d = sc.get<int64_t>(p.k + 1);
+  uint32_t* order_d = sc.get<uint32_t>(p.n);
+  RBQ_CUDA(cudaMemcpyAsync(off_d, off.data(), (p.k + 1) * 8, cudaMemcpyHostToDevice, s));
+  RBQ_CUDA(cudaMemcpyAsync(order_d, ho.data(), p.n * 4, cudaMemcpyHostToDevice, s));
+  launch_centroid_update(p.X, p.n, ix.D, p.lab_d, off_d, order_d, p.k, p.C, zero_empty, s);
+  RBQ_CUDA(cudaStreamSynchronize(s));  // the host vectors above are the copies' sources
+}
+
+// Stride of the rebalancing walk over the rows (the reference draws it from a cycle of 40
+// primes, kmeans_balanced.cuh:569-582): the next entry of a fixed cycle of 40 primes (the
+// smallest prime >= 61 + 64 t, t = 0..39) that does not divide n, so the walk i = stride *
+// j mod n reaches every row.  The cursor runs on across all EM passes of one training run.
+int64_t km_walk_stride(int& cursor, int64_t n)
+{
+  auto next_prime = [](int64_t x) {
+    for (;; ++x) {
+      bool prime = x > 1;
+      for (int64_t d = 2; d * d <= x && prime; ++d) prime = x % d != 0;
+      if (prime) return x;
+    }
+  };
+  for (;;) {
+    cursor = (cursor + 1) % 40;
+    const int64_t p = next_prime(61 + 64 * (int64_t)cursor);
+    if (n % p != 0) return p;
+  }
+}
+
+// Rebalancing (kmeans_balanced.cuh:498-591): every cluster of size <= (float)(n / k) * threshold,
+// taken in ascending id, moves its centre towards the next row of the walk whose cluster holds
+// >= n / k rows (one walk counter shared by all clusters).  Returns whether any centre moved.
+bool km_adjust(const Index& ix, KmProblem& p, float threshold, int& cursor, cudaStream_t s)
+{
+  const int64_t average = p.n / p.k;
+  const int64_t limit = (int64_t)((float)average * threshold);
+  const int64_t stride = km_walk_stride(cursor, p.n);
+  std::vector<int64_t> adj;
+  int64_t count = 0;
+  for (int l = 0; l < p.k; ++l) {
+    if (p.size[l] > limit) continue;
+    int64_t i;
+    do {
+      const int64_t old = count++;
+      i = (int64_t)(((__int128)stride * (old + 1)) % p.n);
+    } while (p.size[p.lab[i]] < average);
+    adj.insert(adj.end(), {(int64_t)l, (int64_t)p.lab[i], i, std::min<int64_t>(p.size[l], 7)});
+  }
+  if (adj.empty()) return false;
+  Scratch sc(s);
+  int64_t* adj_d = sc.get<int64_t>(adj.size());
+  RBQ_CUDA(cudaMemcpyAsync(adj_d, adj.data(), adj.size() * 8, cudaMemcpyHostToDevice, s));
+  launch_adjust_centers(p.C, ix.D, p.X, adj_d, (int)(adj.size() / 4), s);
+  RBQ_CUDA(cudaStreamSynchronize(s));
+  return true;
+}
+
+// EM with rebalancing (kmeans_balanced.cuh:593-704): n_iters passes of adjust (not on the
+// first pass) -> predict -> update; the first and then every pullback-th pass that moved a
+// centre adds one pass.
+void km_em(const Index& ix, KmProblem& p, int n_iters, int pullback, float threshold, int& cursor, cudaStream_t s)
+{
+  int counter = pullback;
+  for (int iter = 0; iter < n_iters; ++iter) {
+    if (iter > 0 && km_adjust(ix, p, threshold, cursor, s)) {
+      if (counter++ >= pullback) {
+        counter -= pullback;
+        ++n_iters;
+      }
+    }
+    km_predict(ix, p, s);
+    km_update(ix, p, true, s);
+  }
+}
+
+// Clusters from scratch (kmeans_balanced.cuh:706-757): labels i mod k, their means, then EM
+// (pullback 2, threshold 0.25).
+void km_build_clusters(const Index& ix, KmProblem& p, int n_iters, int& cursor, cudaStream_t s)
+{
+  p.lab.resize(p.n);
+  for (int64_t i = 0; i < p.n; ++i) p.lab[i] = (uint32_t)(i % p.k);
+  RBQ_CUDA(cudaMemcpyAsync(p.lab_d, p.lab.data(), p.n * 4, cudaMemcpyHostToDevice, s));
+  km_update(ix, p, true, s);
+  km_em(ix, p, n_iters, 2, 0.25f, cursor, s);
+}
+
+// Hierarchical balanced k-means (kmeans_balanced.cuh:759-1132) of the rows X [n, D] into K
+// centres C_out [K, D] (device).
+void train_balanced(const Index& ix, const float* X, int64_t n, int K, float* C_out, cudaStream_t s)
+{
+  const int D = ix.D, iters = ix.kmeans_iters;
+  int cursor = 0;
+  Scratch sc(s);
+  const int n_meso = std::min<int>(K, (int)(std::sqrt((double)K) + 0.5));
+  uint32_t* lab_d = sc.get<uint32_t>(n);
+  float* cn2 = sc.get<float>(K);
+  KmProblem meso;
+  meso.X = X;
+  meso.n = n;
+  meso.k = n_meso;
+  meso.C = sc.get<float>((size_t)n_meso * D);
+  meso.lab_d = lab_d;
+  meso.cn2 = cn2;
+  km_build_clusters(ix, meso, iters, cursor, s);
+
+  // Fine clusters per mesocluster, in proportion to its rows (kmeans_balanced.cuh:759-826).
+  std::vector<int64_t> nums(n_meso), csum(n_meso + 1, 0);
+  int64_t lists_rem = K, rows_rem = n, nonempty_rem = 0, size_max = 0, nums_max = 0;
+  for (int i = 0; i < n_meso; ++i) nonempty_rem += meso.size[i] > 0;
+  for (int i = 0; i < n_meso; ++i) {
+    if (i < n_meso - 1) {
+      if (meso.size[i] == 0) {
+        nums[i] = 0;
+      } else {
+        --nonempty_rem;
+        int64_t f = (int64_t)((double)(lists_rem * meso.size[i]) / (double)rows_rem + 0.5);
+        f = std::min<int64_t>(f, lists_rem - nonempty_rem);
+        nums[i] = std::max<int64_t>(f, 1);
+      }
+    } else {
+      nums[i] = lists_rem;
+    }
+    lists_rem -= nums[i];
+    rows_rem -= meso.size[i];
+    size_max = std::max(size_max, meso.size[i]);
+    nums_max = std::max(nums_max, nums[i]);
+    csum[i + 1] = csum[i] + nums[i];
+  }
+  RBQ_CHECK(csum[n_meso] == K, RBQ_ERR_INVALID, "balanced k-means: fine cluster counts do not add up");
+  // At most 2n / n_meso rows of one mesocluster train its fine clusters (kmeans_balanced.cuh:1068-1083).
+  size_max = std::min<int64_t>(size_max, (2 * n + n_meso - 1) / std::max(n_meso, 1));
+
+  // Fine clusters of each mesocluster (kmeans_balanced.cuh:828-946).
+  {
+    Scratch fs(s);
+    float* Xm = fs.get<float>((size_t)size_max * D);
+    int64_t* rows_d = fs.get<int64_t>(size_max);
+    float* Cm = fs.get<float>((size_t)std::max<int64_t>(nums_max, 1) * D);
+    std::vector<int64_t> rows;
+    for (int i = 0; i < n_meso; ++i) {
+      rows.clear();
+      for (int64_t j = 0; j < n && (int64_t)rows.size() < size_max; ++j)
+        if (meso.lab[j] == (uint32_t)i) rows.push_back(j);
+      if (rows.empty()) {
+        RBQ_CHECK(nums[i] == 0, RBQ_ERR_INVALID, "balanced k-means: an empty mesocluster was given fine clusters");
+        continue;
+      }
+      RBQ_CUDA(cudaMemcpyAsync(rows_d, rows.data(), rows.size() * 8, cudaMemcpyHostToDevice, s));
+      launch_gather_rows_f32(X, (int64_t)rows.size(), D, rows_d, Xm, s);
+      KmProblem fine;
+      fine.X = Xm;
+      fine.n = (int64_t)rows.size();
+      fine.k = (int)nums[i];
+      fine.C = Cm;
+      fine.lab_d = lab_d;
+      fine.cn2 = cn2;
+      km_build_clusters(ix, fine, iters, cursor, s);
+      RBQ_CUDA(cudaMemcpyAsync(C_out + (size_t)csum[i] * D, Cm, (size_t)nums[i] * D * 4, cudaMemcpyDeviceToDevice, s));
+      RBQ_CUDA(cudaStreamSynchronize(s));  // `rows` is the next upload's source
+    }
+  }
+
+  // Fine-tuning over all rows (kmeans_balanced.cuh:1096-1117): max(iters / 10, 2) passes,
+  // pullback 5, threshold 0.2.
+  KmProblem all;
+  all.X = X;
+  all.n = n;
+  all.k = K;
+  all.C = C_out;
+  all.lab_d = lab_d;
+  all.cn2 = cn2;
+  km_em(ix, all, std::max(iters / 10, 2), 5, 0.2f, cursor, s);
+}
+
+// Plain Lloyd iterations from the evenly strided rows i * n / K; empty lists keep their centre.
+void train_lloyd(const Index& ix, const float* X, int64_t n, int K, float* C, cudaStream_t s)
+{
+  Scratch sc(s);
+  std::vector<int64_t> ipick(K);
+  for (int k = 0; k < K; ++k) ipick[k] = (int64_t)(((__int128)k * n) / K);
+  int64_t* ipick_d = sc.get<int64_t>(K);
+  RBQ_CUDA(cudaMemcpyAsync(ipick_d, ipick.data(), K * 8, cudaMemcpyHostToDevice, s));
+  launch_gather_rows_f32(X, K, ix.D, ipick_d, C, s);
+  KmProblem p;
+  p.X = X;
+  p.n = n;
+  p.k = K;
+  p.C = C;
+  p.lab_d = sc.get<uint32_t>(n);
+  p.cn2 = sc.get<float>(K);
+  for (int it = 0; it < ix.kmeans_iters; ++it) {
+    km_predict(ix, p, s);
+    km_update(ix, p, false, s);
+  }
+}
+
 void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
 {
   const int K = ix.K, D = ix.D;
@@ -331,29 +561,11 @@ void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
   RBQ_CUDA(cudaMemcpyAsync(pick_d, pick.data(), n_train * 8, cudaMemcpyHostToDevice, s));
   float* Xs = sc.get<float>((size_t)n_train * D);
   launch_gather_rows_f32(X, n_train, D, pick_d, Xs, s);
-  std::vector<int64_t> ipick(K);
-  for (int k = 0; k < K; ++k) ipick[k] = (int64_t)(((__int128)k * n_train) / K);
-  int64_t* ipick_d = sc.get<int64_t>(K);
-  RBQ_CUDA(cudaMemcpyAsync(ipick_d, ipick.data(), K * 8, cudaMemcpyHostToDevice, s));
   float* C = sc.get<float>((size_t)K * D);
-  float* cn2 = sc.get<float>(K);
-  launch_gather_rows_f32(Xs, K, D, ipick_d, C, s);
-  uint32_t* lab = sc.get<uint32_t>(n_train);
-  int64_t* off_d = sc.get<int64_t>(K + 1);
-  uint32_t* order_d = sc.get<uint32_t>(n_train);
-  std::vector<uint32_t> hl(n_train), ho(n_train);
-  std::vector<int64_t> off, order;
-  for (int it = 0; it < ix.kmeans_iters; ++it) {
-    launch_row_norms(C, K, D, cn2, s);
-    assign_labels(ix, Xs, n_train, C, cn2, D, lab, s);
-    RBQ_CUDA(cudaMemcpyAsync(hl.data(), lab, n_train * 4, cudaMemcpyDeviceToHost, s));
-    RBQ_CUDA(cudaStreamSynchronize(s));
-    counting_sort(hl, K, off, order);
-    for (int64_t i = 0; i < n_train; ++i) ho[i] = (uint32_t)order[i];
-    RBQ_CUDA(cudaMemcpyAsync(off_d, off.data(), (K + 1) * 8, cudaMemcpyHostToDevice, s));
-    RBQ_CUDA(cudaMemcpyAsync(order_d, ho.data(), n_train * 4, cudaMemcpyHostToDevice, s));
-    launch_centroid_update(Xs, n_train, D, lab, off_d, order_d, K, C, s);
-  }
+  if (ix.kmeans_kind == RBQ_KMEANS_LLOYD)
+    train_lloyd(ix, Xs, n_train, K, C, s);
+  else
+    train_balanced(ix, Xs, n_train, K, C, s);
   ix.C_host.resize((size_t)K * D);
   RBQ_CUDA(cudaMemcpyAsync(ix.C_host.data(), C, (size_t)K * D * 4, cudaMemcpyDeviceToHost, s));
   RBQ_CUDA(cudaStreamSynchronize(s));
@@ -672,6 +884,7 @@ void rbq_index_params_default(rbq_index_params_t* p)
   p->shard_rank = 0;
   p->shard_count = 1;
   p->shard_policy = RBQ_SHARD_ROUND_ROBIN;
+  p->kmeans_kind = RBQ_KMEANS_BALANCED;
 }
 
 void rbq_search_params_default(rbq_search_params_t* p)
@@ -717,6 +930,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
               "bad k-means parameters");
     RBQ_CHECK(params->shard_policy == RBQ_SHARD_ROUND_ROBIN || params->shard_policy == RBQ_SHARD_BALANCED,
               RBQ_ERR_INVALID, "unknown shard policy");
+    RBQ_CHECK(params->kmeans_kind == RBQ_KMEANS_BALANCED || params->kmeans_kind == RBQ_KMEANS_LLOYD,
+              RBQ_ERR_INVALID, "unknown k-means kind");
     int ndev = 0;
     RBQ_CUDA(cudaGetDeviceCount(&ndev));
     RBQ_CHECK(params->device >= 0 && params->device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
@@ -731,6 +946,7 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
     ix.K = params->n_lists;
     ix.seed = params->seed;
     ix.kmeans_iters = params->kmeans_n_iters;
+    ix.kmeans_kind = params->kmeans_kind;
     ix.max_train_per_list = params->max_train_points_per_cluster;
     ix.shard_rank = params->shard_rank;
     ix.shard_count = params->shard_count;
@@ -789,6 +1005,7 @@ int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out)
                         (int64_t)ix.K * (ix.D + ix.Dp + 3) * 4 + (ix.K + 1) * 8;
     out->shard_policy = ix.shard_policy;
     out->owners_fixed = ix.owners_fixed ? 1 : 0;
+    out->kmeans_kind = ix.kmeans_kind;
   });
 }
 
@@ -915,9 +1132,10 @@ int rbq_save(rbq_index_t* index, const char* path)
     File f(path, "wb");
     f.write(kMagic, 8);
     f.write(&kFormatVersion, 4);
-    // hdr[7]: bit 0 trained, bit 1 no raw rows (an index imported without its vectors)
+    // hdr[7]: bit 0 trained, bit 1 no raw rows (an index imported without its vectors),
+    // bit 2 Lloyd k-means (else balanced)
     int32_t hdr[8] = {ix.D, ix.Dp, ix.K, ix.kmeans_iters, ix.max_train_per_list, ix.shard_rank, ix.shard_count,
-                      (ix.trained ? 1 : 0) | (ix.has_raw ? 0 : 2)};
+                      (ix.trained ? 1 : 0) | (ix.has_raw ? 0 : 2) | (ix.kmeans_kind == RBQ_KMEANS_LLOYD ? 4 : 0)};
     f.write(hdr, sizeof(hdr));
     f.write(&ix.seed, 8);
     f.write(&ix.t4, 4);
@@ -1007,6 +1225,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.K = K;
       ix.seed = seed;
       ix.kmeans_iters = p.kmeans_n_iters;
+      ix.kmeans_kind = (hdr[7] & 4) ? RBQ_KMEANS_LLOYD : RBQ_KMEANS_BALANCED;
       ix.max_train_per_list = p.max_train_points_per_cluster;
       ix.shard_rank = p.shard_rank;
       ix.shard_count = p.shard_count;

@@ -89,6 +89,7 @@ struct Index {
   int D = 0, Dp = 0, W = 0, K = 0;
   uint64_t seed = 0;
   int kmeans_iters = 20;
+  int kmeans_kind = RBQ_KMEANS_BALANCED;
   int max_train_per_list = 256;
   int shard_rank = 0, shard_count = 1;
   int shard_policy = RBQ_SHARD_ROUND_ROBIN;
@@ -226,7 +227,9 @@ void launch_rerank(const float* Xslots, const uint32_t* id2slot, int D, const fl
 
 // k-means helpers.
 void launch_centroid_update(const float* X, int64_t n, int D, const uint32_t* labels, const int64_t* off,
-                            const uint32_t* order, int K, float* C, cudaStream_t s);
+                            const uint32_t* order, int K, float* C, bool zero_empty, cudaStream_t s);
+// Balanced k-means: C[l] = (wc * C[li] + X[i]) / (wc + 1) for adj = {l, li, i, wc} x n_adj.
+void launch_adjust_centers(float* C, int D, const float* X, const int64_t* adj, int n_adj, cudaStream_t s);
 void launch_gather_rows_f32(const float* src, int64_t rows, int cols, const int64_t* src_row, float* dst,
                             cudaStream_t s);
 // dst[r*cols + j] = src[src_row[r]*cols + j] for 32-bit words.

@@ -38,7 +38,8 @@ class IndexIVFRaBitQ:
     """1-bit IVF-RaBitQ index with 4-bit query quantisation and optional exact rerank.
 
     Parameters mirror cuvs::neighbors::ivf_rabitq::index_params (ivf_rabitq.hpp:50-103):
-    ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``;
+    ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``,
+    ``kmeans`` ("balanced": the reference's hierarchical balanced k-means; "lloyd": plain Lloyd);
     a shard of a sharded index also takes ``shard_rank`` / ``shard_count`` and ``shard_policy``
     ("round_robin": list l on rank l % count; "balanced": lists spread by size^2 at the first add).
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
@@ -50,7 +51,7 @@ class IndexIVFRaBitQ:
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
                  max_train_points_per_cluster: int = 256, shard_rank: int = 0, shard_count: int = 1,
-                 metric: str = "l2", shard_policy: str = "round_robin", _handle=None):
+                 metric: str = "l2", shard_policy: str = "round_robin", kmeans: str = "balanced", _handle=None):
         if metric not in ("l2", "ip"):
             raise ValueError("metric must be 'l2' or 'ip'")
         self.d = int(d)
@@ -76,6 +77,9 @@ class IndexIVFRaBitQ:
         if shard_policy not in _lib.SHARD_POLICIES:
             raise ValueError(f"shard_policy must be one of {sorted(_lib.SHARD_POLICIES)}")
         p.shard_policy = _lib.SHARD_POLICIES[shard_policy]
+        if kmeans not in _lib.KMEANS_KINDS:
+            raise ValueError(f"kmeans must be one of {sorted(_lib.KMEANS_KINDS)}")
+        p.kmeans_kind = _lib.KMEANS_KINDS[kmeans]
         _lib.call("rbq_index_create", ctypes.byref(p), ctypes.byref(self._h))
 
     # -- lifecycle -----------------------------------------------------------------------

@@ -408,6 +408,138 @@ def recall(ids, gt) -> float:
     return hit / float(gt.size)
 
 
+def _km_update(X, lab, k, zero_empty, C):
+    """M step: means of member rows, summed in ascending row order in double; empty
+    clusters become zero (balanced) or keep their centre (Lloyd)."""
+    sums = np.zeros((k, X.shape[1]), np.float64)
+    np.add.at(sums, lab, X.astype(np.float64))
+    cnt = np.bincount(lab, minlength=k).astype(np.int64)
+    nz = cnt > 0
+    C = C.copy()
+    C[nz] = (sums[nz] / cnt[nz, None]).astype(np.float32)
+    if zero_empty:
+        C[~nz] = 0.0
+    return C, cnt
+
+
+def _km_stride(state, n):
+    """Rebalancing walk stride: the next of 40 primes (smallest prime >= 61 + 64 t) not dividing n."""
+    def next_prime(x):
+        while True:
+            if x > 1 and all(x % d for d in range(2, int(x ** 0.5) + 1)):
+                return x
+            x += 1
+    while True:
+        state[0] = (state[0] + 1) % 40
+        p = next_prime(61 + 64 * state[0])
+        if n % p:
+            return p
+
+
+def _km_adjust(X, C, lab, size, threshold, state):
+    """Rebalancing pass (kmeans_balanced.cuh:443-591, adjust_centers) in ascending cluster
+    order with one shared walk counter; centre math in float32, in the reference's order."""
+    n, k = X.shape[0], C.shape[0]
+    average = n // k
+    limit = int(np.float32(average) * np.float32(threshold))
+    stride = _km_stride(state, n)
+    count = 0
+    moved = False
+    C = C.copy()
+    for l in range(k):
+        if size[l] > limit:
+            continue
+        while True:
+            count += 1
+            i = (stride * count) % n
+            if size[lab[i]] >= average:
+                break
+        li = int(lab[i])
+        wc = np.float32(min(int(size[l]), 7))
+        v = np.float32(0.0) + wc * C[li]
+        v = v + np.float32(1.0) * X[i]
+        C[l] = v / (wc + np.float32(1.0))
+        moved = True
+    return C, moved
+
+
+def _km_em(X, C, n_iters, pullback, threshold, state, lab=None, size=None, assign_fn=None):
+    """EM with rebalancing (kmeans_balanced.cuh:593-704)."""
+    assign_fn = assign_fn or assign
+    k = C.shape[0]
+    counter = pullback
+    it = 0
+    while it < n_iters:
+        if it > 0:
+            C, moved = _km_adjust(X, C, lab, size, threshold, state)
+            if moved:
+                if counter >= pullback:
+                    counter -= pullback
+                    n_iters += 1
+                counter += 1
+        lab = assign_fn(X, C)
+        C, size = _km_update(X, lab, k, True, C)
+        it += 1
+    return C, lab, size
+
+
+def _km_build(X, k, iters, state, assign_fn=None):
+    """Labels i mod k, their means, then EM with pullback 2, threshold 0.25
+    (kmeans_balanced.cuh:706-757)."""
+    lab = (np.arange(X.shape[0]) % k).astype(np.uint32)
+    C, size = _km_update(X, lab, k, True, np.zeros((k, X.shape[1]), np.float32))
+    return _km_em(X, C, iters, 2, 0.25, state, lab, size, assign_fn)
+
+
+def kmeans_balanced(X, K, iters=20, assign_fn=None):
+    """Hierarchical balanced k-means (kmeans_balanced.cuh:759-1132), the deterministic
+    restatement the library trains with (rbq_train, RBQ_KMEANS_BALANCED): ~sqrt(K)
+    mesoclusters, fine clusters per mesocluster in proportion to its rows (at most 2n/n_meso
+    rows train them), then max(iters/10, 2) fine-tuning passes.  Returns C [K, D] float32.
+    assign_fn(X, C) -> uint32 labels replaces the exact E step (the bench's CPU arm passes a
+    BLAS argmin for speed at 1M rows)."""
+    X = _c(X, np.float32)
+    n, D = X.shape
+    state = [0]
+    n_meso = min(K, int(np.sqrt(float(K)) + 0.5))
+    _, mlab, msize = _km_build(X, n_meso, iters, state, assign_fn)
+    nums = np.zeros(n_meso, np.int64)
+    lists_rem, rows_rem = K, n
+    nonempty_rem = int((msize > 0).sum())
+    for i in range(n_meso):
+        if i < n_meso - 1:
+            if msize[i] == 0:
+                nums[i] = 0
+            else:
+                nonempty_rem -= 1
+                f = int(float(lists_rem * int(msize[i])) / float(rows_rem) + 0.5)
+                f = min(f, lists_rem - nonempty_rem)
+                nums[i] = max(f, 1)
+        else:
+            nums[i] = lists_rem
+        lists_rem -= int(nums[i])
+        rows_rem -= int(msize[i])
+    csum = np.concatenate([[0], np.cumsum(nums)])
+    size_max = min(int(msize.max()), (2 * n + n_meso - 1) // max(n_meso, 1))
+    C = np.zeros((K, D), np.float32)
+    for i in range(n_meso):
+        rows = np.nonzero(mlab == i)[0][:size_max]
+        if rows.size == 0:
+            assert nums[i] == 0
+            continue
+        Ci, _, _ = _km_build(X[rows], int(nums[i]), iters, state, assign_fn)
+        C[csum[i]:csum[i + 1]] = Ci
+    C, _, _ = _km_em(X, C, max(iters // 10, 2), 5, 0.2, state, assign_fn=assign_fn)
+    return C
+
+
+def train_sample(X, K, max_train_per_list=256):
+    """The evenly strided training sample rbq_train clusters: rows i * n / n_train."""
+    n = X.shape[0]
+    m = min(n, max_train_per_list * K)
+    return _c(X, np.float32)[(np.arange(m, dtype=np.int64) * n) // m]
+
+
 def kmeans(X, k, iters=10, seed=0):
     """Small deterministic Lloyd k-means for CPU-only tests (not the product's trainer)."""
     X = _c(X, np.float32)

@@ -512,3 +512,31 @@ def test_bound_seed_matches_oracle(oracle, case, nprobe, R):
     got = tau.cpu().numpy()
     assert np.array_equal(u32(got), u32(want))
     assert np.isfinite(want).any() and (R < 300 or np.isinf(want).any())
+
+
+@pytest.mark.parametrize("n,d,K,iters,mtp", [(8000, 32, 24, 6, 256), (8000, 64, 48, 10, 64), (3000, 100, 7, 3, 256)])
+def test_gpu_balanced_kmeans_matches_oracle(oracle, n, d, K, iters, mtp):
+    """rbq_train (RBQ_KMEANS_BALANCED) vs the oracle's restatement of the reference's
+    hierarchical balanced k-means on the same strided sample: centroids bit-exact."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    rng = np.random.default_rng(K)
+    cen = rng.normal(size=(40, d)).astype(np.float32)
+    w = 1.0 / np.arange(1, 41)
+    X = (cen[rng.choice(40, size=n, p=w / w.sum())] + 0.3 * rng.normal(size=(n, d))).astype(np.float32)
+    idx = IndexIVFRaBitQ(d, K, seed=5, kmeans_iters=iters, max_train_points_per_cluster=mtp)
+    assert idx.info().kmeans_kind == 0
+    idx.train(X)
+    C = idx.centroids()[0]
+    C2 = oracle.kmeans_balanced(oracle.train_sample(X, K, mtp), K, iters=iters)
+    assert np.array_equal(u32(C), u32(C2))
+
+
+def test_gpu_lloyd_kmeans_matches_oracle(oracle):
+    """RBQ_KMEANS_LLOYD vs the oracle's Lloyd iterations: centroids bit-exact."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, _ = mixture(6000, 64, 30, 0.3, 1, seed=4)
+    idx = IndexIVFRaBitQ(64, 20, seed=5, kmeans_iters=4, kmeans="lloyd")
+    assert idx.info().kmeans_kind == 1
+    idx.train(X)
+    C2, _ = oracle.kmeans(oracle.train_sample(X, 20), 20, iters=4)
+    assert np.array_equal(u32(idx.centroids()[0]), u32(C2))

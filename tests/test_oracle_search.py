@@ -196,3 +196,53 @@ def test_balanced_list_owners_restated(oracle):
         assert load.max() - load.min() <= float(sizes.max()) ** 2
     assert oracle.list_owners("balanced", [5, 5, 3], 2).tolist() == [0, 1, 0]
     assert oracle.list_owners("balanced", [3, 5, 5], 2).tolist() == [0, 0, 1]
+
+
+def _skewed(n=8000, d=32, nc=40, seed=0):
+    rng = np.random.default_rng(seed)
+    cen = rng.normal(size=(nc, d)).astype(np.float32)
+    w = 1.0 / np.arange(1, nc + 1)
+    a = rng.choice(nc, size=n, p=w / w.sum())
+    X = (cen[a] + 0.3 * rng.normal(size=(n, d))).astype(np.float32)
+    return X / np.linalg.norm(X, axis=1, keepdims=True)
+
+
+def test_balanced_kmeans_restated(oracle):
+    """Hierarchical balanced k-means (kmeans_balanced.cuh:759-1132) on a Zipf-skewed mixture:
+    deterministic, every list non-empty, and the largest list smaller than plain Lloyd's."""
+    X = _skewed()
+    K = 48
+    C1 = oracle.kmeans_balanced(X, K, iters=10)
+    C2 = oracle.kmeans_balanced(X, K, iters=10)
+    assert C1.dtype == np.float32 and C1.shape == (K, 32) and np.array_equal(C1, C2)
+    sb = np.bincount(oracle.assign(X, C1), minlength=K)
+    _, ll = oracle.kmeans(X, K, iters=10)
+    sl = np.bincount(ll, minlength=K)
+    assert sb.min() > 0 and sb.max() < sl.max()
+
+
+def test_balanced_kmeans_pieces(oracle):
+    """The rebalancing walk visits every row (its stride never divides n), a small cluster's
+    centre moves to (wc * c_big + x) / (wc + 1) in float32, and an empty cluster's centre is
+    zero after the M step."""
+    from oracle.oracle import _km_adjust, _km_stride, _km_update
+    for n in (1, 7, 61 * 67, 2 ** 20, 3 * 5 * 7 * 11 * 13 * 61):
+        p = _km_stride([0], n)
+        assert n % p != 0
+    X = np.arange(12, dtype=np.float32).reshape(6, 2)
+    lab = np.array([0, 0, 0, 0, 0, 1], np.uint32)
+    C, size = _km_update(X, lab, 3, True, np.full((3, 2), 5, np.float32))
+    assert size.tolist() == [5, 1, 0] and np.array_equal(C[2], [0, 0]) and np.array_equal(C[1], X[5])
+    # limit = int((6 // 3) * 0.25) = 0: only the empty cluster 2 moves, towards the first row
+    # of the walk whose cluster holds >= 2 rows; with wc = 0 it lands on that row.
+    C2, moved = _km_adjust(X, C, lab, size, 0.25, [0])
+    assert moved and np.array_equal(C2[:2], C[:2])
+    i = _km_stride([0], 6) % 6
+    assert lab[i] == 0 and np.array_equal(C2[2], X[i])
+    # threshold 0.5: limit 1, cluster 1 (one row) moves too, with wc = 1 and the walk's next row
+    C3, _ = _km_adjust(X, C, lab, size, 0.5, [0])
+    st = _km_stride([0], 6)
+    i1, i2 = st % 6, (2 * st) % 6
+    w = np.float32(1)
+    assert np.array_equal(C3[1], (np.float32(0) + w * C[0] + np.float32(1) * X[i1]) / (w + np.float32(1)))
+    assert np.array_equal(C3[2], X[i2])
