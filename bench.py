@@ -2,14 +2,17 @@
 """Benchmark: queries/sec of IVF-RaBitQ search on BASELINE config 2 (1M x 256, nlist 1024,
 nprobe 32, k 10, exact rerank, query batch 10,000), 1..8 B200 with lists sharded per GPU.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|4|5]
 
 One step = one search of one query batch.  `value` times the batch with queries resident
 in HBM (CUDA events, L2 flushed before every step); `e2e` times the C-ABI call with host
 buffers (rbq_search_host: H2D of the queries, search, D2H of distances and ids).  Under
-torchrun (N > 1) every rank holds the lists l % N == rank and the per-rank results are merged
-after one NCCL all-gather; times are the max over ranks.  `--impl reference` times the CPU
-restatement of the reference search (oracle/, all host cores) on the same workload.
+torchrun (N > 1) the lists are spread over the ranks by size (each list on one rank), every
+rank scans its own lists, and the per-rank results are merged after one NCCL all-gather; times
+are the max over ranks.  `--impl reference` times the CPU restatement of the reference search
+(oracle/, all host cores) on the same workload.  `--config 4` / `--config 5` run BASELINE's
+100M x 128 (nlist 65,536) and 20M x 768 (nlist 16,384) configurations with data generated on
+the device and recall measured on a 1,000-query sample (supplementary lines; no CPU baseline).
 """
 from __future__ import annotations
 
@@ -25,9 +28,16 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-# BASELINE config 2 (the metric's configuration).
+# BASELINE config 2 (the metric's configuration), and configs 4 and 5 (supplementary).
 CFG = dict(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, nlist=1024, nprobe=32, k=10,
-           rerank=100, seed=2024)
+           rerank=100, seed=2024, config=2, aniso=0, device_data=False, gt_sample=10_000)
+CONFIGS = {
+    2: CFG,
+    4: dict(n=100_000_000, d=128, centres=65536, sigma=0.3, nq=100_000, qsigma=0.05, nlist=65536, nprobe=64,
+            k=100, rerank=400, seed=4004, config=4, aniso=0, device_data=True, gt_sample=1000),
+    5: dict(n=20_000_000, d=768, centres=16384, sigma=0.2, nq=50_000, qsigma=0.05, nlist=16384, nprobe=128,
+            k=50, rerank=500, seed=5005, config=5, aniso=1, device_data=True, gt_sample=1000),
+}
 RERANK_LADDER = (100, 150, 200, 300, 400, 600, 800)
 RECALL_TARGET = 0.95
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -54,6 +64,45 @@ def make_data(cfg):
     Q = X[src] + np.float32(cfg["qsigma"]) * rng.standard_normal((cfg["nq"], d), dtype=np.float32)
     Q /= np.linalg.norm(Q, axis=1, keepdims=True)
     return X, np.ascontiguousarray(Q, np.float32)
+
+
+def make_data_device(cfg, dev):
+    """Config 4 / 5 data on the device (rbq_gen_mixture / rbq_gen_queries: seeded Philox mixture,
+    per-dim scale sqrt(1/(1+d/64)) when anisotropic, L2-normalised; queries = database rows +
+    N(0, qsigma) noise, renormalised)."""
+    import torch
+
+    from neurosamble_b200 import _lib
+    from neurosamble_b200.index import _ptr, _stream_ptr
+    n, d, nq = cfg["n"], cfg["d"], cfg["nq"]
+    X = torch.empty((n, d), dtype=torch.float32, device=dev)
+    Q = torch.empty((nq, d), dtype=torch.float32, device=dev)
+    st = _stream_ptr(dev.index)
+    _lib.call("rbq_gen_mixture", _ptr(X), n, d, cfg["centres"], cfg["sigma"], cfg["aniso"], 1, cfg["seed"], st)
+    _lib.call("rbq_gen_queries", _ptr(X), n, d, _ptr(Q), nq, cfg["qsigma"], 1, cfg["seed"] + 1, None, st)
+    torch.cuda.synchronize(dev)
+    return X, Q
+
+
+def exact_knn_device(Xd, Qs, k, rows=1 << 20, qblock=1000):
+    """Exact k nearest rows (fp32 |x|^2 - 2 q.x, running top-k over row chunks) of the sample Qs."""
+    import torch
+    out = []
+    for qa in range(0, Qs.shape[0], qblock):
+        q = Qs[qa:qa + qblock]
+        bd = bi = None
+        for a in range(0, Xd.shape[0], rows):
+            xb = Xd[a:a + rows]
+            s = (xb * xb).sum(1)[None, :] - 2.0 * (q @ xb.T)
+            d_, i_ = torch.topk(s, min(k, s.shape[1]), dim=1, largest=False)
+            i_ = i_ + a
+            if bd is not None:
+                d_, j = torch.topk(torch.cat([bd, d_], 1), k, dim=1, largest=False)
+                i_ = torch.gather(torch.cat([bi, i_], 1), 1, j)
+            bd, bi = d_, i_
+            del s
+        out.append(bi.cpu())
+    return torch.cat(out).numpy()
 
 
 def measured_peak():
@@ -218,7 +267,7 @@ def run_reference(args, cfg):
             steps.append(qps)
             n_sample = n
     value = float(np.mean(steps))
-    line = {"impl": "reference", "metric": metric_name(), "value": round(value, 2), "unit": "queries/s",
+    line = {"impl": "reference", "metric": metric_name(cfg), "value": round(value, 2), "unit": "queries/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
@@ -230,13 +279,20 @@ def run_reference(args, cfg):
     return 0
 
 
-def metric_name():
-    return "queries/sec @ recall@10>=0.95, 1M x 256 IVF-RaBitQ (nlist 1024, nprobe 32, k 10)"
+def _count(n):
+    return f"{n // 1_000_000}M" if n % 1_000_000 == 0 else str(n)
+
+
+def metric_name(cfg):
+    return (f"queries/sec @ recall@{cfg['k']}>=0.95, {_count(cfg['n'])} x {cfg['d']} IVF-RaBitQ "
+            f"(nlist {cfg['nlist']}, nprobe {cfg['nprobe']}, k {cfg['k']})")
 
 
 def workload(cfg, R, kmeans):
-    return {"workload": "BASELINE config 2: 1M x 256 f32, 4096-centre mixture sigma 0.25, L2-normalised; "
-                        "10k perturbed-row queries; IVF-RaBitQ 1-bit codes, 4-bit queries",
+    return {"workload": (f"BASELINE config {cfg['config']}: {_count(cfg['n'])} x {cfg['d']} f32, "
+                         f"{cfg['centres']}-centre {'anisotropic ' if cfg['aniso'] else ''}mixture sigma "
+                         f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ 1-bit "
+                         f"codes, 4-bit queries" + ("; data generated on the device" if cfg["device_data"] else "")),
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
             "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
             "kmeans": kmeans}
@@ -267,9 +323,15 @@ def run_ours(args, cfg):
         from datetime import timedelta
         tdist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     t = time.perf_counter()
-    X, Q = make_data(cfg)
+    if cfg["device_data"]:
+        X = None
+        Xd, Qd = make_data_device(cfg, dev)
+        Q = Qd.cpu().numpy()
+    else:
+        X, Q = make_data(cfg)
+        Xd = torch.from_numpy(X).to(dev)
+        Qd = torch.from_numpy(Q).to(dev)
     log(f"[rank {rank}] data {time.perf_counter() - t:.1f}s")
-    Xd = torch.from_numpy(X).to(dev)
     t = time.perf_counter()
     if world > 1:
         from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ
@@ -282,39 +344,40 @@ def run_ours(args, cfg):
     index.add(Xd)
     torch.cuda.synchronize()
     log(f"[rank {rank}] build {time.perf_counter() - t:.1f}s, local vectors {local_ix.info().n_local}")
-    del Xd
-    Qd = torch.from_numpy(Q).to(dev)
     index.nprobe = cfg["nprobe"]
     index.prune = True
     if world == 1:
         index.seeded = args.seeded
 
     # ---- recall at the config's rerank depth; raise R along the ladder until recall >= target
+    # (exact neighbours of the first gt_sample queries: all of config 2's, 1,000 at configs 4 / 5)
     gt = None
+    ns = min(cfg["gt_sample"], cfg["nq"])
     if rank == 0:
-        Xd = torch.from_numpy(X).to(dev)
-        xn = (Xd * Xd).sum(1)
-        gts = []
-        for a in range(0, cfg["nq"], 1000):
-            s = xn[None, :] - 2.0 * (Qd[a:a + 1000] @ Xd.T)
-            gts.append(torch.topk(s, cfg["k"], dim=1, largest=False).indices.cpu())
-        gt = torch.cat(gts).numpy()
-        del Xd, xn, s
-        torch.cuda.empty_cache()
+        t = time.perf_counter()
+        gt = exact_knn_device(Xd, Qd[:ns], cfg["k"])
+        log(f"[rank 0] exact neighbours of {ns} queries {time.perf_counter() - t:.1f}s")
+    del Xd
+    torch.cuda.empty_cache()
 
     def recall_of(ids):
-        hit = sum(len(set(a.tolist()) & set(b.tolist())) for a, b in zip(ids, gt))
+        hit = sum(len(set(a.tolist()) & set(b.tolist())) for a, b in zip(ids[:ns], gt))
         return hit / gt.size
 
     R = args.rerank or cfg["rerank"]
     recalls = {}
-    ladder = [R] if args.rerank else list(RERANK_LADDER)
+    if args.rerank:
+        ladder = [R]
+    elif cfg["config"] == 2:
+        ladder = list(RERANK_LADDER)
+    else:
+        ladder = [min(4096, int(R * f)) for f in (1, 1.5, 2, 3, 4)]
     for cand in ladder:
         index.k_rerank = cand
         d, i = index.search(Qd, cfg["k"])
         ok = torch.zeros(1, dtype=torch.int32, device=dev)
         if rank == 0:
-            recalls[cand] = recall_of(i.cpu().numpy())
+            recalls[cand] = round(recall_of(i.cpu().numpy()), 5)
             ok[0] = int(recalls[cand] >= RECALL_TARGET)
         if world > 1:
             tdist.broadcast(ok, src=0)
@@ -418,7 +481,7 @@ def run_ours(args, cfg):
 
     # ---- config 2's batch sweep (B = 1, 64, 1024): device-resident queries, same index
     sweep = None
-    if world == 1 and not args.no_sweep:
+    if world == 1 and not args.no_sweep and cfg["config"] == 2:
         sweep = {}
         for B in (1, 64, 1024):
             qb = Qd[:B]
@@ -437,20 +500,20 @@ def run_ours(args, cfg):
         sweep["10000"] = {"queries_per_s": round(value, 1), "ms_per_batch": round(ms, 4)}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and X is not None:
         cpu = cpu_baseline(local_ix, X, Q, cfg, R)
 
     if world > 1:
         tdist.barrier()
     if rank == 0:
-        line = {"metric": metric_name(), "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
+        line = {"metric": metric_name(cfg), "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes x 4-bit planes (popc) + f32",
-                "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
+                "data": f"synthetic (seeded Gaussian mixture, BASELINE config {cfg['config']})",
                 "config": dict(workload(cfg, R, args.kmeans),
                                parallelism=(f"lists sharded over {world} GPUs (balanced by size^2)" if world > 1
                                             else "1 GPU"),
-                               recall_at_10=recalls.get(R), recall_by_rerank=recalls),
+                               recall_by_rerank=recalls, **{f"recall_at_{k}": recalls.get(R)}),
                 "clocks": clk.summary(),
                 "e2e": {"value": round(e2e, 2), "unit": "queries/s", "h2d_bytes_per_step": nq * cfg["d"] * 4,
                         "d2h_bytes_per_step": nq * k * 12},
@@ -490,8 +553,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     _lib.call("rbq_coarse", h, _ptr(qr), nq, P, 0, _ptr(probes), _ptr(g), st)
     _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), st)
     torch.cuda.synchronize(dev)
-    off = ix.export_lists()["list_off"]
-    sizes = np.diff(off)
+    sizes = np.diff(ix.list_offsets())
     pr = probes.cpu().numpy()
     owned = ix.list_owners()[pr] == info.shard_rank
     vec = int(sizes[pr][owned].sum())
@@ -549,7 +611,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     peak, kind = measured_peak()
     traffic = None
     tf = os.path.join(HERE, "profiles", "scan_traffic.json")
-    if os.path.exists(tf):
+    if os.path.exists(tf) and cfg.get("config", 2) == 2:  # the capture is of config 2's scan
         try:
             with open(tf) as f:
                 traffic = json.load(f).get("bytes_per_launch_scaled_to_bench")
@@ -597,17 +659,24 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the B = 1 / 64 / 1024 sweep")
     ap.add_argument("--kmeans", default="balanced", choices=["balanced", "lloyd"],
                     help="coarse trainer of both arms (balanced: the reference's build algorithm)")
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
+                    help="BASELINE configuration (2: the metric's; 4 / 5: supplementary, data on the device)")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
                     help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = dict(CFG)
+    cfg = dict(CONFIGS[args.config])
     if args.n:
         cfg["n"] = args.n
     if args.nq:
         cfg["nq"] = args.nq
     if args.impl == "reference":
+        if cfg["device_data"]:
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"config {args.config}: the CPU port needs "
+                                  "the whole raw store and a CPU-built index on the host; run at config 2"}))
+            return 0
         return run_reference(args, cfg)
     return run_ours(args, cfg)
 

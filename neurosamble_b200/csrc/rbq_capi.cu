@@ -491,11 +491,11 @@ void train_balanced(const Index& ix, const float* X, int64_t n, int K, float* C_
     float* Xm = fs.get<float>((size_t)size_max * D);
     int64_t* rows_d = fs.get<int64_t>(size_max);
     float* Cm = fs.get<float>((size_t)std::max<int64_t>(nums_max, 1) * D);
+    std::vector<int64_t> moff, morder;  // rows of each mesocluster, ascending
+    counting_sort(meso.lab, n_meso, moff, morder);
     std::vector<int64_t> rows;
     for (int i = 0; i < n_meso; ++i) {
-      rows.clear();
-      for (int64_t j = 0; j < n && (int64_t)rows.size() < size_max; ++j)
-        if (meso.lab[j] == (uint32_t)i) rows.push_back(j);
+      rows.assign(morder.begin() + moff[i], morder.begin() + std::min(moff[i + 1], moff[i] + size_max));
       if (rows.empty()) {
         RBQ_CHECK(nums[i] == 0, RBQ_ERR_INVALID, "balanced k-means: an empty mesocluster was given fine clusters");
         continue;
@@ -672,12 +672,16 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   RBQ_CHECK(params.rerank <= 0 || ix.has_raw, RBQ_ERR_STATE,
             "exact rerank needs the raw vectors; this index was imported without them (use rerank = 0)");
   const SearchPlan sp = plan_search(ix, params, nq);
-  const int64_t by_scores = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4));
-  const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_scores, 65535ll * 64));
+  // The scan and rerank run over chunks bounded by the candidate keys (1 GiB); inside one, the
+  // front end (rotation, coarse scores, top-m, refine) runs over sub-chunks bounded by the
+  // [sub-chunk, K] score matrix (512 MiB), so a large K does not cut the scan into small grids.
+  const int64_t by_keys = std::max<int64_t>(1, (1ll << 30) / ((int64_t)sp.slices * sp.R * 8));
+  const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_keys, 65535ll * 64));
+  const int64_t fe_chunk = std::min<int64_t>(chunk, std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4)));
   Scratch sc(s);
   float* Qr_buf = Qr_pre ? nullptr : sc.get<float>((size_t)chunk * ix.Dp);
-  float* S = sc.get<float>((size_t)chunk * ix.K);
-  int32_t* cand = sc.get<int32_t>((size_t)chunk * sp.m);
+  float* S = sc.get<float>((size_t)fe_chunk * ix.K);
+  int32_t* cand = sc.get<int32_t>((size_t)fe_chunk * sp.m);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
   float* g = sc.get<float>((size_t)chunk * sp.P);
   uint32_t* planes = sc.get<uint32_t>((size_t)chunk * 4 * ix.W);
@@ -690,10 +694,14 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
     const float* Qr = Qr_pre ? Qr_pre + a * ix.Dp : Qr_buf;
-    if (!Qr_pre) launch_rotate(Qc, cn, ix.D, ix.Dp, ix.P, Qr_buf, s);
-    launch_coarse_scores_tc(Qr, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
-    launch_topm_rows(S, cn, ix.K, sp.m, cand, s);
-    launch_refine_topp(Qr, cn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes, g, s);
+    for (int64_t b = 0; b < cn; b += fe_chunk) {
+      const int64_t fn = std::min(fe_chunk, cn - b);
+      const float* Qrb = Qr + b * ix.Dp;
+      if (!Qr_pre) launch_rotate(Qc + b * ix.D, fn, ix.D, ix.Dp, ix.P, Qr_buf + b * ix.Dp, s);
+      launch_coarse_scores_tc(Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
+      launch_topm_rows(S, fn, ix.K, sp.m, cand, s);
+      launch_refine_topp(Qrb, fn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes + b * sp.P, g + b * sp.P, s);
+    }
     launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
     search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
     if (params.rerank > 0)

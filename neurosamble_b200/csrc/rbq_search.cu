@@ -103,10 +103,13 @@ void launch_coarse_scores(const float* A, int64_t nq, const float* C, const floa
 }
 
 // ---------------------------------------------------------------------------------------
-// Per row of S [nq, K]: the m smallest (score, column) keys.  The row is taken in chunks of up
-// to kTopmChunk keys appended behind the running m survivors; a radix select keeps the m
-// smallest of each buffer (block_keep_smallest).  Order of the m output columns is
-// unspecified; the exact refine below ranks them.
+// Per row of S [nq, K]: the m smallest (score, column) keys.  The row streams through in rounds
+// of 256 * KPER keys; a key is appended to the shared buffer only while it is below the m-th
+// smallest key kept so far (keys are distinct, so no key at or above it can be among the m
+// smallest), and a radix select (block_keep_smallest) cuts the buffer back to m keys when the
+// next round might not fit.  After the first cut few keys pass, so a long row costs one read
+// and about two selections.  Order of the m output columns is unspecified; the exact refine
+// below ranks them.
 // ---------------------------------------------------------------------------------------
 constexpr int kTopmChunk = 4096;
 
@@ -114,34 +117,59 @@ __device__ unsigned long long block_keep_smallest(const unsigned long long* src,
                                                   unsigned long long* dst, unsigned* hist, int* misc,
                                                   unsigned long long* kmax, int* cnt);
 
+template <int KPER>
 __global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict__ S, int K, int m, int buf,
                                                         int32_t* __restrict__ cand)
 {
-  extern __shared__ unsigned long long tk[];  // [2 * buf]
+  extern __shared__ unsigned long long tk[];  // [2 * buf], buf >= m + 256 * KPER
   __shared__ unsigned s_hist[256];
-  __shared__ int s_misc[3], s_cnt;
+  __shared__ int s_misc[3], s_cnt, s_fill;
   __shared__ unsigned long long s_kmax;
   unsigned long long* cur = tk;
   unsigned long long* nxt = tk + buf;
   const int64_t q = blockIdx.x;
   const float* row = S + q * K;
-  int filled = 0;  // survivors at the front of `cur`
-  for (int c0 = 0; c0 < K;) {
-    const int take = min(buf - filled, K - c0);
-    for (int i = threadIdx.x; i < take; i += blockDim.x)
-      cur[filled + i] = make_key(__ldg(row + c0 + i), (uint32_t)(c0 + i));
-    __syncthreads();
-    const int n = filled + take;
-    c0 += take;
-    if (n > m) {
-      block_keep_smallest(cur, n, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+  const int lane = threadIdx.x & 31;
+  const int step = 256 * KPER;
+  unsigned long long thr = kEmptyKey;  // the m-th smallest key kept so far (none: all ones)
+  int filled = 0;                      // keys at the front of `cur`
+  if (threadIdx.x == 0) s_fill = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < K; c0 += step) {
+    if (filled + step > buf) {  // block-uniform; filled > m here because buf >= m + step
+      thr = block_keep_smallest(cur, filled, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
       unsigned long long* t = cur;
       cur = nxt;
       nxt = t;
       filled = m;
-    } else {
-      filled = n;
+      if (threadIdx.x == 0) s_fill = m;
+      __syncthreads();
     }
+    float v[KPER];
+#pragma unroll
+    for (int r = 0; r < KPER; ++r) {
+      const int i = c0 + r * 256 + threadIdx.x;
+      v[r] = i < K ? __ldg(row + i) : 0.0f;
+    }
+#pragma unroll
+    for (int r = 0; r < KPER; ++r) {
+      const int i = c0 + r * 256 + threadIdx.x;
+      const unsigned long long key = make_key(v[r], (uint32_t)i);
+      const bool keep = i < K && key < thr;
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&s_fill, __popc(bal));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (keep) cur[base + __popc(bal & ((1u << lane) - 1u))] = key;
+    }
+    __syncthreads();
+    filled = s_fill;
+    __syncthreads();  // every thread has read s_fill before the next round appends
+  }
+  if (filled > m) {
+    block_keep_smallest(cur, filled, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+    cur = nxt;
+    filled = m;
     __syncthreads();
   }
   for (int i = threadIdx.x; i < m; i += blockDim.x)
@@ -152,11 +180,18 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
 {
   if (nq <= 0) return;
   RBQ_CHECK(m >= 1 && m <= kTopmChunk / 2, RBQ_ERR_INVALID, "coarse: shortlist size out of range");
-  const int buf = std::min(kTopmChunk, std::max(2 * m, K));
-  const size_t smem = (size_t)buf * 2 * 8;
-  if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  topm_rows_kernel<<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+  if (K > kTopmChunk) {  // long rows: 2048 keys a round into a 4096-key buffer
+    const int buf = kTopmChunk;
+    const size_t smem = (size_t)buf * 2 * 8;
+    RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    topm_rows_kernel<8><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+  } else {
+    const int buf = std::max(std::max(2 * m, K), m + 256);
+    const size_t smem = (size_t)buf * 2 * 8;
+    if (smem > 48 * 1024)
+      RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    topm_rows_kernel<1><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+  }
   RBQ_LAUNCHED();
 }
 

@@ -221,6 +221,12 @@ class IndexIVFRaBitQ:
         _lib.call("rbq_export_lists", self._h, *(a.ctypes.data_as(ctypes.c_void_p) for a in (off, ids, codes, fa, fr, fe)))
         return {"list_off": off, "ids": ids, "codes": codes, "fadd": fa, "frescale": fr, "ferr": fe}
 
+    def list_offsets(self) -> np.ndarray:
+        """[nlist + 1] int64: list l holds this shard's slots [off[l], off[l + 1])."""
+        off = np.empty(self.nlist + 1, np.int64)
+        _lib.call("rbq_export_lists", self._h, off.ctypes.data_as(ctypes.c_void_p), None, None, None, None, None)
+        return off
+
     def list_owners(self) -> np.ndarray:
         """[nlist] int32: the shard holding each list (-1 before a balanced map is fixed)."""
         own = np.empty(self.nlist, np.int32)

@@ -540,3 +540,33 @@ def test_gpu_lloyd_kmeans_matches_oracle(oracle):
     idx.train(X)
     C2, _ = oracle.kmeans(oracle.train_sample(X, 20), 20, iters=4)
     assert np.array_equal(u32(idx.centroids()[0]), u32(C2))
+
+
+def test_search_front_end_subchunks_equal_small_batches(oracle):
+    """K = 8192: the coarse front end of a 40,000-query search runs in three [16384, K] score
+    sub-chunks under one scan (and the long-row top-m path); the probes equal the oracle's and
+    the results equal the same queries searched 5,000 at a time."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(60000, 32, 500, 0.3, 40000, seed=9)
+    K = 8192
+    idx = IndexIVFRaBitQ(32, K, seed=2)
+    C = np.ascontiguousarray(X[::7][:K])
+    idx.set_centroids(C)
+    idx.add(X)
+    torch = _torch()
+    nq, P = 400, 8
+    dp = idx.info().padded_dim
+    qr = torch.empty((nq, dp), dtype=torch.float32, device="cuda")
+    q = dev(Q[:nq])
+    call("rbq_rotate", idx.handle, ptr(q), nq, ptr(qr), stream())
+    probes = torch.empty((nq, P), dtype=torch.int32, device="cuda")
+    g = torch.empty((nq, P), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), nq, P, 0, ptr(probes), ptr(g), stream())
+    torch.cuda.synchronize()
+    p2, g2 = oracle.coarse(qr.cpu().numpy(), idx.centroids()[1], P)
+    assert np.array_equal(probes.cpu().numpy(), p2) and np.array_equal(u32(g.cpu().numpy()), u32(g2))
+    idx.nprobe, idx.k_rerank = P, 20
+    d, i = idx.search(Q, 10)
+    parts = [idx.search(Q[a:a + 5000], 10) for a in range(0, 40000, 5000)]
+    assert np.array_equal(i, np.concatenate([p[1] for p in parts]))
+    assert np.array_equal(u32(d), u32(np.concatenate([p[0] for p in parts])))
