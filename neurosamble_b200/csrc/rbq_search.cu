@@ -185,12 +185,12 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
     const size_t smem = (size_t)buf * 2 * 8;
     RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     topm_rows_kernel<8><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
-  } else {
-    const int buf = std::max(std::max(2 * m, K), m + 256);
+  } else {  // rows of up to 4096 keys: 1024 a round, so K <= 1024 is one fill and one selection
+    const int buf = std::max(std::max(2 * m, K), m + 1024);
     const size_t smem = (size_t)buf * 2 * 8;
     if (smem > 48 * 1024)
-      RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    topm_rows_kernel<1><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+      RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    topm_rows_kernel<4><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
   }
   RBQ_LAUNCHED();
 }
