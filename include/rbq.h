@@ -127,6 +127,13 @@ int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out);
  * Replaces the k-means part of build (src/neighbors/ivf_rabitq.cu:117-152).  Synchronises. */
 int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream);
 
+/* One-call build, ivf_rabitq::build (ivf_rabitq.cu:32-194): with C_host (caller-given centroids
+ * [K, D], host memory) the centroids are installed, else k-means trains on X_dev; then the n
+ * rows are added (labels_dev: caller-given lists, only together with C_host).  d must equal the
+ * index's dim.  Synchronises. */
+int rbq_build(rbq_index_t* index, const float* X_dev, int64_t n, int32_t d, const float* C_host,
+              const uint32_t* labels_dev, void* stream);
+
 /* Install caller-given centroids [K, D] (host memory) instead of training.  Synchronises. */
 int rbq_set_centroids(rbq_index_t* index, const float* C_host, int32_t n_lists);
 

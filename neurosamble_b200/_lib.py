@@ -57,6 +57,7 @@ SIGNATURES = {
     "rbq_index_info": [_P, ctypes.POINTER(IndexInfo)],
     "rbq_train": [_P, _P, _I64, _P],
     "rbq_set_centroids": [_P, _P, _I32],
+    "rbq_build": [_P, _P, _I64, _I32, _P, _P, _P],
     "rbq_add": [_P, _P, _I64, _P, _P],
     "rbq_search": [_P, ctypes.POINTER(SearchParams), _P, _I64, _P, _P, _P],
     "rbq_search_host": [_P, ctypes.POINTER(SearchParams), _P, _I64, _P, _P, _P],

@@ -12,8 +12,10 @@ results are appended to ``neighbors.i64`` (int64 [N, topk]) and ``dists.f32`` (f
 Additions: ``--encode_dir`` reads the encoder's shard manifest instead of one flat file;
 ``--rerank R`` re-ranks the top R estimates with exact fp32 distances (0 keeps the reference
 behaviour); ``--metric ip`` writes inner products 1 - d/2 of unit vectors (FAISS's IP view,
-descending) instead of squared L2.  Under torchrun (WORLD_SIZE > 1, one rank per GPU) the
-lists are sharded over the ranks and rank 0 writes the files.
+descending) instead of squared L2; ``--gpus N`` shards the lists over N GPUs of this node by
+relaunching the same command as N processes through torch.distributed.run (127.0.0.1, a free
+port).  Under torchrun (WORLD_SIZE > 1, one rank per GPU) the lists are sharded over the
+ranks and rank 0 writes the files.
 
 Accepted for compatibility: ``--bits 1`` and ``--search_mode QUANT4`` only (the 1-bit QUANT4
 path is the one this library implements; other values exit with status 2); ``--strategy
@@ -27,6 +29,8 @@ from __future__ import annotations
 
 import argparse
 import os
+import socket
+import subprocess
 import sys
 import time
 
@@ -57,7 +61,20 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--rerank", type=int, default=0)
     ap.add_argument("--metric", default="l2", choices=["l2", "ip"])
     ap.add_argument("--seed", type=int, default=7, help="rotation / query-scale seed")
+    ap.add_argument("--gpus", type=int, default=1, help="GPUs of this node to shard the lists over")
     return ap.parse_args(argv)
+
+
+def relaunch_cmd(argv, gpus: int, port: int):
+    """The torch.distributed.run command that runs this CLI as `gpus` ranks of one node."""
+    return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={gpus}",
+            "--master-addr=127.0.0.1", f"--master-port={port}", "-m", "neurosamble_b200.cli", *argv]
+
+
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def check_args(a: argparse.Namespace) -> str:
@@ -66,6 +83,8 @@ def check_args(a: argparse.Namespace) -> str:
         return "need --emb <fp16 file> --n <N> [--d 384] (or --encode_dir <dir>)"
     if a.emb and a.n <= 0:
         return "need --emb <fp16 file> --n <N> [--d 384]"
+    if a.gpus < 1:
+        return "--gpus must be >= 1"
     if a.bits != 1:
         return f"--bits {a.bits}: only 1-bit RaBitQ codes are implemented"
     if a.search_mode != "QUANT4":
@@ -85,6 +104,8 @@ def main(argv=None) -> int:
     if err:
         print(err, file=sys.stderr)
         return 2
+    if a.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        return subprocess.call(relaunch_cmd(list(sys.argv[1:] if argv is None else argv), a.gpus, _free_port()))
     import torch
     import torch.distributed as dist
 

@@ -1035,6 +1035,27 @@ int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream)
   });
 }
 
+int rbq_build(rbq_index_t* index, const float* X_dev, int64_t n, int32_t d, const float* C_host,
+              const uint32_t* labels_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(index && X_dev, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(d == ix.D, RBQ_ERR_INVALID, "build: dim " + std::to_string(d) + " != index dim " + std::to_string(ix.D));
+    RBQ_CHECK(!labels_dev || C_host, RBQ_ERR_INVALID, "build: labels need the centroids they refer to");
+    RBQ_CHECK(ix.n_total == 0, RBQ_ERR_STATE, "build: index already holds vectors");
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    if (C_host) {
+      ix.C_host.assign(C_host, C_host + (size_t)ix.K * ix.D);
+      install_centroids(ix, s);
+    } else {
+      train_kmeans(ix, X_dev, n, s);
+    }
+    add_rows(ix, X_dev, n, labels_dev, s);
+  });
+}
+
 int rbq_set_centroids(rbq_index_t* index, const float* C_host, int32_t n_lists)
 {
   return guarded([&] {

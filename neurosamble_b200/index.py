@@ -128,7 +128,8 @@ class IndexIVFRaBitQ:
 
     # -- build ---------------------------------------------------------------------------
     def train(self, x) -> None:
-        """Seeded Lloyd k-means (nlist centroids) on a strided sample of x."""
+        """k-means (nlist centroids; balanced unless kmeans="lloyd") on an evenly strided sample
+        of at most max_train_points_per_cluster * nlist rows of x."""
         t, _ = self._to_device(x)
         with torch.cuda.device(self.device):
             _lib.call("rbq_train", self._h, _ptr(t), t.shape[0], _stream_ptr(self.device))
@@ -140,19 +141,38 @@ class IndexIVFRaBitQ:
             raise RuntimeError(f"centroids must be [{self.nlist}, {self.d}]")
         _lib.call("rbq_set_centroids", self._h, c.ctypes.data_as(ctypes.c_void_p), self.nlist)
 
+    def _labels(self, labels, n: int):
+        if labels is None:
+            return None
+        lab = torch.as_tensor(np.asarray(labels.cpu() if isinstance(labels, torch.Tensor) else labels,
+                                         dtype=np.int64).astype(np.uint32).view(np.int32))
+        lab = lab.to(f"cuda:{self.device}")
+        if lab.numel() != n:
+            raise RuntimeError("labels must have one entry per row")
+        return lab
+
     def add(self, x, labels=None) -> None:
         """Append rows (ids continue from ntotal); labels (optional) fix their lists."""
         t, _ = self._to_device(x)
-        lab = None
-        if labels is not None:
-            lab = torch.as_tensor(np.asarray(labels.cpu() if isinstance(labels, torch.Tensor) else labels,
-                                             dtype=np.int64).astype(np.uint32).view(np.int32))
-            lab = lab.to(f"cuda:{self.device}")
-            if lab.numel() != t.shape[0]:
-                raise RuntimeError("labels must have one entry per row")
+        lab = self._labels(labels, t.shape[0])
         with torch.cuda.device(self.device):
             _lib.call("rbq_add", self._h, _ptr(t), t.shape[0], _ptr(lab) if lab is not None else None,
                       _stream_ptr(self.device))
+
+    def build(self, x, centroids=None, labels=None) -> None:
+        """train (or the given centroids) + add in one call (rbq_build; ivf_rabitq::build)."""
+        t, _ = self._to_device(x)
+        c = None
+        if centroids is not None:
+            c = np.ascontiguousarray(np.asarray(
+                centroids.detach().cpu() if isinstance(centroids, torch.Tensor) else centroids, dtype=np.float32))
+            if c.shape != (self.nlist, self.d):
+                raise RuntimeError(f"centroids must be [{self.nlist}, {self.d}]")
+        lab = self._labels(labels, t.shape[0])
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_build", self._h, _ptr(t), t.shape[0], self.d,
+                      c.ctypes.data_as(ctypes.c_void_p) if c is not None else None,
+                      _ptr(lab) if lab is not None else None, _stream_ptr(self.device))
 
     # -- search --------------------------------------------------------------------------
     def search_params(self, k: int) -> _lib.SearchParams:

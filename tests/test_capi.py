@@ -21,7 +21,7 @@ def declared_symbols():
 
 def test_header_declares_entry_points():
     syms = declared_symbols()
-    assert "rbq_search" in syms and "rbq_build" not in syms
+    assert "rbq_search" in syms and "rbq_build" in syms and "rbq_last_error" in syms
     assert len(syms) >= 25
 
 

@@ -570,3 +570,28 @@ def test_search_front_end_subchunks_equal_small_batches(oracle):
     parts = [idx.search(Q[a:a + 5000], 10) for a in range(0, 40000, 5000)]
     assert np.array_equal(i, np.concatenate([p[1] for p in parts]))
     assert np.array_equal(u32(d), u32(np.concatenate([p[0] for p in parts])))
+
+
+def test_build_equals_train_or_centroids_then_add(oracle):
+    """rbq_build (ivf_rabitq::build): with centroids it equals set_centroids + add, without
+    them train + add (same lists, ids, codes); labels need the centroids they refer to."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, _ = mixture(6000, 64, 30, 0.3, 1, seed=12)
+    a = IndexIVFRaBitQ(64, 24, seed=4, kmeans_iters=3)
+    a.build(X)
+    b = IndexIVFRaBitQ(64, 24, seed=4, kmeans_iters=3)
+    b.train(X)
+    b.add(X)
+    ea, eb = a.export_lists(), b.export_lists()
+    assert all(np.array_equal(ea[key], eb[key]) for key in ("list_off", "ids", "codes"))
+    C = b.centroids()[0]
+    lab = oracle.assign(X, C)
+    c = IndexIVFRaBitQ(64, 24, seed=4)
+    c.build(X, centroids=C, labels=lab)
+    ec = c.export_lists()
+    assert all(np.array_equal(ec[key], eb[key]) for key in ("list_off", "ids", "codes"))
+    d = IndexIVFRaBitQ(64, 24, seed=4)
+    with pytest.raises(RuntimeError, match="labels need the centroids"):
+        d.build(X, labels=lab)
+    with pytest.raises(RuntimeError, match="already holds"):
+        c.build(X, centroids=C)

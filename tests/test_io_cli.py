@@ -127,3 +127,14 @@ def test_cli_end_to_end_matches_the_library(tmp_path, metric, rerank):
     assert cli.main(args) == 0  # reuses i.rbq
     n2, d2 = read_neighbors(str(tmp_path / "n.i64"), str(tmp_path / "d.f32"), 3000, 10)
     assert np.array_equal(np.array(n2), n1) and np.array_equal(np.array(d2).view(np.uint32), d1.view(np.uint32))
+
+
+def test_cli_gpus_relaunches_through_torchrun():
+    from neurosamble_b200 import cli
+    a = cli.parse_args(["--emb", "x.f16", "--n", "10", "--gpus", "4"])
+    assert a.gpus == 4 and cli.check_args(a) == ""
+    cmd = cli.relaunch_cmd(["--emb", "x.f16", "--n", "10", "--gpus", "4"], 4, 29555)
+    assert cmd[1:3] == ["-m", "torch.distributed.run"]
+    assert "--nproc-per-node=4" in cmd and "--master-addr=127.0.0.1" in cmd and "--master-port=29555" in cmd
+    assert cmd[cmd.index("-m", 3):][:2] == ["-m", "neurosamble_b200.cli"] and cmd[-2:] == ["--gpus", "4"]
+    assert cli.check_args(cli.parse_args(["--emb", "x", "--n", "1", "--gpus", "0"])) == "--gpus must be >= 1"
