@@ -265,6 +265,12 @@ int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t
 int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t parts, int64_t nq, int32_t k,
                       float* out_dist_dev, int64_t* out_ids_dev, void* stream);
 
+/* ---- fault injection (tests) --------------------------------------------------------------- */
+/* Host-side: the (after+1)-th device allocation the library makes from now on fails with
+ * RBQ_ERR_OOM exactly as a failed cudaMalloc would (one shot; after < 0 turns it off).  Used to
+ * test out-of-memory handling without exhausting a shared GPU; the GPU is not touched. */
+int rbq_debug_fail_alloc(int64_t after);
+
 /* ---- synthetic data (benchmarks and tests) ---------------------------------------------- */
 /* X [n, D]: row i = centre[h(i) % n_centres] + sigma * N(0,1) per dim, centres ~ N(0,1)
  * (per-dim scale sqrt(1/(1+d/64)) when aniso), L2-normalised when normalize. */

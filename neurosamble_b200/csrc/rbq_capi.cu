@@ -4,6 +4,7 @@
 // Every entry point catches everything, stores a message for rbq_last_error() and returns
 // a status code; nothing throws across the ABI and nothing exits or traps.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include <algorithm>
@@ -27,6 +28,29 @@ namespace rbq {
 namespace {
 
 thread_local std::string g_last_error;
+
+// NVTX range for the scope (entry points and search / training stages; free without a tool).
+struct Range {
+  explicit Range(const char* name) { nvtxRangePushA(name); }
+  ~Range() { nvtxRangePop(); }
+};
+
+// Host-side fault injection for tests (rbq_debug_fail_alloc): the device allocation that takes
+// the counter from 0 fails as a failed cudaMalloc would; -1 = off.
+std::atomic<int64_t> g_fail_alloc_after{-1};
+
+void maybe_inject_alloc_failure(size_t bytes)
+{
+  int64_t v = g_fail_alloc_after.load();
+  while (v >= 0) {
+    if (g_fail_alloc_after.compare_exchange_weak(v, v - 1)) {
+      if (v == 0)
+        throw Error{RBQ_ERR_OOM, "device allocation of " + std::to_string(bytes) +
+                                     " bytes failed (injected by rbq_debug_fail_alloc)"};
+      return;
+    }
+  }
+}
 
 // Switches to `dev` for the scope and restores the caller's device.
 struct DeviceGuard {
@@ -66,6 +90,7 @@ template <typename T>
 T* dev_alloc(size_t count)
 {
   if (count == 0) count = 1;
+  maybe_inject_alloc_failure(count * sizeof(T));
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, count * sizeof(T));
   if (e != cudaSuccess) {
@@ -92,6 +117,7 @@ struct Scratch {
   T* get(size_t count)
   {
     if (count == 0) count = 1;
+    maybe_inject_alloc_failure(count * sizeof(T));
     void* p = nullptr;
     cudaError_t e = cudaMallocAsync(&p, count * sizeof(T), s);
     if (e != cudaSuccess) {
@@ -446,6 +472,7 @@ void train_balanced(const Index& ix, const float* X, int64_t n, int K, float* C_
   const int D = ix.D, iters = ix.kmeans_iters;
   int cursor = 0;
   Scratch sc(s);
+  Range r("rbq balanced k-means");
   const int n_meso = std::min<int>(K, (int)(std::sqrt((double)K) + 0.5));
   uint32_t* lab_d = sc.get<uint32_t>(n);
   float* cn2 = sc.get<float>(K);
@@ -695,6 +722,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     const float* Qc = Q + a * ix.D;
     const float* Qr = Qr_pre ? Qr_pre + a * ix.Dp : Qr_buf;
     for (int64_t b = 0; b < cn; b += fe_chunk) {
+      Range r("rbq front end (rotate, coarse, top-m, refine)");
       const int64_t fn = std::min(fe_chunk, cn - b);
       const float* Qrb = Qr + b * ix.Dp;
       if (!Qr_pre) launch_rotate(Qc + b * ix.D, fn, ix.D, ix.Dp, ix.P, Qr_buf + b * ix.Dp, s);
@@ -703,7 +731,11 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       launch_refine_topp(Qrb, fn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes + b * sp.P, g + b * sp.P, s);
     }
     launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
-    search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
+    {
+      Range r("rbq scan");
+      search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
+    }
+    Range r("rbq rerank / result");
     if (params.rerank > 0)
       launch_rerank(ix.X_r, ix.id2row, ix.D, Qc, cn, keys, sp.R, sp.k, dist + a * sp.k, ids + a * sp.k, s);
     else
@@ -878,6 +910,12 @@ const char* rbq_last_error(void) { return g_last_error.c_str(); }
 
 int rbq_version(void) { return 1; }
 
+int rbq_debug_fail_alloc(int64_t after)
+{
+  g_fail_alloc_after.store(after < 0 ? -1 : after);
+  return RBQ_OK;
+}
+
 uint64_t rbq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 void rbq_index_params_default(rbq_index_params_t* p)
@@ -1029,6 +1067,7 @@ int rbq_get_list_owners(rbq_index_t* index, int32_t* owners)
 int rbq_train(rbq_index_t* index, const float* X_dev, int64_t n, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_train");
     RBQ_CHECK(index && X_dev, RBQ_ERR_INVALID, "null argument");
     DeviceGuard dg(index->ix.device);
     train_kmeans(index->ix, X_dev, n, as_stream(stream));
@@ -1039,6 +1078,7 @@ int rbq_build(rbq_index_t* index, const float* X_dev, int64_t n, int32_t d, cons
               const uint32_t* labels_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_build");
     RBQ_CHECK(index && X_dev, RBQ_ERR_INVALID, "null argument");
     Index& ix = index->ix;
     RBQ_CHECK(d == ix.D, RBQ_ERR_INVALID, "build: dim " + std::to_string(d) + " != index dim " + std::to_string(ix.D));
@@ -1072,6 +1112,7 @@ int rbq_set_centroids(rbq_index_t* index, const float* C_host, int32_t n_lists)
 int rbq_add(rbq_index_t* index, const float* X_dev, int64_t n, const uint32_t* labels_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_add");
     RBQ_CHECK(index && (X_dev || n == 0), RBQ_ERR_INVALID, "null argument");
     DeviceGuard dg(index->ix.device);
     add_rows(index->ix, X_dev, n, labels_dev, as_stream(stream));
@@ -1082,6 +1123,7 @@ int rbq_search(rbq_index_t* index, const rbq_search_params_t* params, const floa
                float* dist_dev, int64_t* ids_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_search");
     RBQ_CHECK(index && params, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Q_dev && dist_dev && ids_dev), RBQ_ERR_INVALID, "null buffer");
     DeviceGuard dg(index->ix.device);
@@ -1093,6 +1135,7 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
                     float* dist_host, int64_t* ids_host, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_search_host");
     RBQ_CHECK(index && params, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Q_host && dist_host && ids_host), RBQ_ERR_INVALID, "null buffer");
     if (nq == 0) return;
@@ -1154,6 +1197,7 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
 int rbq_save(rbq_index_t* index, const char* path)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_save");
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null index");
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
@@ -1189,6 +1233,7 @@ int rbq_save(rbq_index_t* index, const char* path)
 int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard_count, rbq_index_t** out)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_load");
     RBQ_CHECK(out, RBQ_ERR_INVALID, "null argument");
     *out = nullptr;
     File f(path, "rb");
@@ -1358,6 +1403,7 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
                          int32_t shard_count, int32_t shard_policy, rbq_index_t** out)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_import_reference");
     RBQ_CHECK(out, RBQ_ERR_INVALID, "null argument");
     *out = nullptr;
     RefFile r = read_ref_file(path);
@@ -1539,6 +1585,7 @@ int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint3
 int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_rotate");
     RBQ_CHECK(index && (n == 0 || (X_dev && Y_dev)), RBQ_ERR_INVALID, "null argument");
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
@@ -1550,6 +1597,7 @@ int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t
                    float* k1_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_query_prep");
     RBQ_CHECK(index && (nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev)), RBQ_ERR_INVALID,
               "null argument");
     Index& ix = index->ix;
@@ -1595,6 +1643,7 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
                int32_t* probes_dev, float* g_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_coarse");
     RBQ_CHECK(index && (nq == 0 || (Qr_dev && probes_dev && g_dev)), RBQ_ERR_INVALID, "null argument");
     Index& ix = index->ix;
     RBQ_CHECK(ix.trained, RBQ_ERR_STATE, "index is not trained");
@@ -1624,6 +1673,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_scan");
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && cand_ids_dev &&
                           cand_dist_dev),
@@ -1659,6 +1709,7 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
                    int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_bound_seed");
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && tau_dev),
               RBQ_ERR_INVALID, "null buffer");
@@ -1692,6 +1743,7 @@ int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t
                float* dist_dev, int64_t* ids_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_rerank");
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Q_dev && cand_ids_dev && dist_dev && ids_dev), RBQ_ERR_INVALID, "null buffer");
     RBQ_CHECK(R >= 1 && R <= 4096 && k >= 1, RBQ_ERR_INVALID, "bad rerank parameters");
@@ -1711,6 +1763,7 @@ int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t par
                       float* out_dist_dev, int64_t* out_ids_dev, void* stream)
 {
   return guarded([&] {
+    Range nvtx_range("rbq_merge_results");
     RBQ_CHECK(parts >= 1 && k >= 1 && nq >= 0, RBQ_ERR_INVALID, "bad merge parameters");
     RBQ_CHECK(nq == 0 || (dist_dev && ids_dev && out_dist_dev && out_ids_dev), RBQ_ERR_INVALID, "null buffer");
     launch_merge_results(dist_dev, ids_dev, parts, nq, k, out_dist_dev, out_ids_dev, as_stream(stream));

@@ -595,3 +595,42 @@ def test_build_equals_train_or_centroids_then_add(oracle):
         d.build(X, labels=lab)
     with pytest.raises(RuntimeError, match="already holds"):
         c.build(X, centroids=C)
+
+
+def test_injected_allocation_failure_is_reported_and_leaves_the_index_usable():
+    """Out-of-memory handling without exhausting the shared GPU: rbq_debug_fail_alloc makes one
+    device allocation fail as cudaMalloc would; the call returns RBQ_ERR_OOM (RuntimeError),
+    the next call succeeds with the same results, and a failed create leaves no handle."""
+    from neurosamble_b200 import IndexIVFRaBitQ, _lib
+    L = _lib.lib()
+    X, Q = mixture(8000, 64, 30, 0.3, 300, seed=13)
+    idx = IndexIVFRaBitQ(64, 32, seed=4, kmeans_iters=3)
+    idx.build(X)
+    idx.nprobe, idx.k_rerank = 8, 30
+    d0, i0 = idx.search(Q, 10)
+    try:
+        for after in (0, 1, 3):
+            assert L.rbq_debug_fail_alloc(after) == 0
+            with pytest.raises(RuntimeError, match="out of device memory.*injected"):
+                idx.search(Q, 10)
+            d1, i1 = idx.search(Q, 10)  # one shot: the hook is off again
+            assert np.array_equal(i1, i0) and np.array_equal(u32(d1), u32(d0))
+        L.rbq_debug_fail_alloc(0)
+        with pytest.raises(RuntimeError, match="out of device memory"):
+            IndexIVFRaBitQ(64, 16, seed=1)
+    finally:
+        L.rbq_debug_fail_alloc(-1)
+
+
+def test_search_is_deterministic_run_to_run():
+    """The same batch searched twice (single pass and split into slices) gives identical bits."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(20000, 128, 50, 0.3, 257, seed=14)
+    idx = IndexIVFRaBitQ(128, 64, seed=4, kmeans_iters=3)
+    idx.build(X)
+    idx.nprobe, idx.k_rerank = 12, 50
+    for split in (0, 4):
+        idx.probe_split = split
+        a = idx.search(Q, 10)
+        b = idx.search(Q, 10)
+        assert np.array_equal(a[1], b[1]) and np.array_equal(u32(a[0]), u32(b[0]))
