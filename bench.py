@@ -551,7 +551,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     g = torch.empty((nq, P), dtype=torch.float32, device=dev)
     _lib.call("rbq_rotate", h, _ptr(Qd), nq, _ptr(qr), st)
     _lib.call("rbq_coarse", h, _ptr(qr), nq, P, 0, _ptr(probes), _ptr(g), st)
-    _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), st)
+    _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), 4, st)
     torch.cuda.synchronize(dev)
     sizes = np.diff(ix.list_offsets())
     pr = probes.cpu().numpy()
@@ -578,7 +578,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
         _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pp), _ptr(gg), npr,
                   pp.stride(0), _ptr(tau) if tau is not None else None, _ptr(init[0]) if init else None,
                   _ptr(init[1]) if init else None, R, 1, 1, 0, _ptr(ids_t), _ptr(dist_t),
-                  _ptr(stats_t) if stats_t is not None else None, st)
+                  _ptr(stats_t) if stats_t is not None else None, 4, st)
 
     ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
     dist = torch.empty((nq, R), dtype=torch.float32, device=dev)

@@ -83,6 +83,8 @@ typedef struct {
   int32_t seeded;        /* every slice starts from the nearest probed list's bound seed      */
                          /* (rbq_bound_seed); -1 = auto (on when the probes are split into      */
                          /* slices), 0 = off (each slice seeds itself), 1 = on                  */
+  int32_t query_bits;    /* query code width: 4 = QUANT4 (default; 0 means 4), 8 = QUANT8       */
+                         /* (search_mode, ivf_rabitq.hpp:111-120; ivf_rabitq.cu:313-345)        */
 } rbq_search_params_t;
 
 typedef struct {
@@ -184,11 +186,13 @@ int rbq_get_list_owners(rbq_index_t* index, int32_t* owners);
 /* ---- stage entry points (device pointers; parity tests and the sharded driver) ----------- */
 /* Y [n, Dp] = pad(X [n, D]) * P.  Replaces RotatorGPU::rotate (rotator_gpu.cu:162-176). */
 int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, void* stream);
-/* 4-bit query quantisation: planes [nq, 4, W], delta [nq], k1 [nq] (= -0.5 sum q).
- * Replaces exrabitq_quantize_query (searcher_gpu_quantize_query.cu:655-793) and
- * computeQueryFactorsWarpKernel (gpu_index/ivf_gpu.cu:1451-1490). */
+/* B-bit query quantisation, B = query_bits (4 = QUANT4 with t4, 8 = QUANT8 with t8; 0 means
+ * 4): planes [nq, B, W], delta [nq], k1 [nq] (= -0.5 sum q).  Replaces exrabitq_quantize_query
+ * (searcher_gpu_quantize_query.cu:655-793) and computeQueryFactorsWarpKernel
+ * (gpu_index/ivf_gpu.cu:1451-1490).  The scan entry points below take the same query_bits
+ * as the planes they are given. */
 int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev,
-                   float* delta_dev, float* k1_dev, void* stream);
+                   float* delta_dev, float* k1_dev, int32_t query_bits, void* stream);
 /* Approximate coarse scores S [nq, K] = |c_rot|^2 - 2 <q_rot, c_rot> (the shortlist ranking).
  * tensor_cores = 1: tcgen05 kind::tf32 MMA (the search path); 0: fp32 CUDA-core reference.
  * Replaces the -2 Q C^T GEMM + add_norms of PrepareClusterSearchInputs
@@ -218,7 +222,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
              int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
              int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
-             uint64_t* stats_dev, void* stream);
+             uint64_t* stats_dev, int32_t query_bits, void* stream);
 /* Bound seed per query: the R-th smallest RaBitQ upper bound est + f_err * sqrt(g) over the
  * query's leading owned probed lists that hold >= R vectors (+inf if they hold fewer), the
  * threshold a pruning scan starts from.  With nprobe = 1 it is the nearest list's seed that
@@ -227,7 +231,8 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
  * searcher_gpu_common.cuh:178-193). */
 int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
                    const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, void* stream);
+                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, int32_t query_bits,
+                   void* stream);
 /* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
  * search time: a host program whose device memory is handed out up front by its own pool
  * (so a library cudaMalloc would fail or break its budget), or a latency-critical search
@@ -249,13 +254,15 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
 int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
                      const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
                      int32_t probe_stride, const float* tau0_dev, int32_t R, int32_t prune, int32_t slices, int32_t cand_cap,
-                     int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev, void* stream);
+                     int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev, int32_t query_bits,
+                     void* stream);
 /* Phase-1 estimator of one query against every vector of list `list`: integer popcount
  * inner product acc, estimate est and lower bound low (slot order of the list).  Replaces the
  * phase-1 loop of computeInnerProductsWithBitwiseBlockSort (searcher_gpu_quantize_query.cu:
- * 233-281) for inspection; planes_dev is one query's [4, W] planes. */
+ * 233-281) for inspection; planes_dev is one query's [query_bits, W] planes. */
 int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float delta, float k1, float g,
-                       int32_t list, int32_t* acc_dev, float* est_dev, float* low_dev, void* stream);
+                       int32_t list, int32_t* acc_dev, float* est_dev, float* low_dev, int32_t query_bits,
+                       void* stream);
 /* Exact fp32 rerank of candidates [nq, R] (id -1 = empty) in the original space -> top-k.
  * Semantics of cuvs::neighbors::refine (src/neighbors/refine/refine_device.cuh:31-150). */
 int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t* cand_ids_dev, int32_t R,

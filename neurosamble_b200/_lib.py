@@ -26,7 +26,7 @@ class IndexParams(ctypes.Structure):
 class SearchParams(ctypes.Structure):
     _fields_ = [("n_probes", ctypes.c_int32), ("k", ctypes.c_int32), ("rerank", ctypes.c_int32),
                 ("prune", ctypes.c_int32), ("probe_split", ctypes.c_int32), ("cand_cap", ctypes.c_int32),
-                ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32)]
+                ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32), ("query_bits", ctypes.c_int32)]
 
 
 class IndexInfo(ctypes.Structure):
@@ -51,7 +51,7 @@ SIGNATURES = {
     "rbq_search_params_default": [ctypes.POINTER(SearchParams)],
     "rbq_make_rotation": [_I32, _U64, _P],
     "rbq_query_scale": [_I32, _U64, _I32, _P],
-    "rbq_list_estimates": [_P, _P, _F32, _F32, _F32, _I32, _P, _P, _P, _P],
+    "rbq_list_estimates": [_P, _P, _F32, _F32, _F32, _I32, _P, _P, _P, _I32, _P],
     "rbq_index_create": [ctypes.POINTER(IndexParams), ctypes.POINTER(_P)],
     "rbq_index_free": [_P],
     "rbq_index_info": [_P, ctypes.POINTER(IndexInfo)],
@@ -70,14 +70,15 @@ SIGNATURES = {
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
     "rbq_get_list_owners": [_P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],
-    "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _P],
+    "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _I32, _P],
     "rbq_coarse_scores": [_P, _P, _I64, _P, _I32, _P],
     "rbq_check_errors": [_P],
     "rbq_coarse": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
-    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
-    "rbq_bound_seed": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P],
+    "rbq_scan": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32,
+                 _P],
+    "rbq_bound_seed": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _I32, _P],
     "rbq_scan_noalloc": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P,
-                         _P],
+                         _I32, _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "rbq_merge_results": [_P, _P, _I32, _I64, _I32, _P, _P, _P],
     "rbq_debug_fail_alloc": [_I64],

@@ -17,8 +17,8 @@ relaunching the same command as N processes through torch.distributed.run (127.0
 port).  Under torchrun (WORLD_SIZE > 1, one rank per GPU) the lists are sharded over the
 ranks and rank 0 writes the files.
 
-Accepted for compatibility: ``--bits 1`` and ``--search_mode QUANT4`` only (the 1-bit QUANT4
-path is the one this library implements; other values exit with status 2); ``--strategy
+Accepted for compatibility: ``--bits 1`` only and ``--search_mode QUANT4`` or ``QUANT8`` (4- or
+8-bit query codes; LUT16 / LUT32 exit with status 2); ``--strategy
 none`` turns the error-bound prune off, ``centroid_reorder`` keeps it on, with this library's
 threshold seeds in place of the reference's centroid-distance seed (``--reorder_scale`` is
 accepted and has no effect); ``--stream`` / ``--stream_batch`` (the build always streams
@@ -87,8 +87,8 @@ def check_args(a: argparse.Namespace) -> str:
         return "--gpus must be >= 1"
     if a.bits != 1:
         return f"--bits {a.bits}: only 1-bit RaBitQ codes are implemented"
-    if a.search_mode != "QUANT4":
-        return f"--search_mode {a.search_mode}: only QUANT4 (4-bit query) is implemented"
+    if a.search_mode not in ("QUANT4", "QUANT8"):
+        return f"--search_mode {a.search_mode}: only QUANT4 and QUANT8 (4- / 8-bit query codes) are implemented"
     if a.topk < 1 or a.batch < 1 or a.nprobe < 1 or a.nlist < 1 or a.rerank < 0:
         return "--topk, --batch, --nprobe, --nlist must be >= 1 and --rerank >= 0"
     return ""
@@ -159,6 +159,7 @@ def main(argv=None) -> int:
     index.nprobe = a.nprobe
     index.k_rerank = a.rerank
     index.prune = a.strategy != "none"
+    index.query_bits = 8 if a.search_mode == "QUANT8" else 4
 
     t1 = time.perf_counter()
     writer = NeighborWriter(a.out_nbr, a.out_dist, a.topk) if rank == 0 else None

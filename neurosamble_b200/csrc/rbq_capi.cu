@@ -602,8 +602,26 @@ void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
 struct SearchPlan {
   int P, k, R, cap, slices, m;
   int prune;
+  int qbits;    // query code width: 4 (QUANT4) or 8 (QUANT8)
   bool seeded;  // two-phase scan (search_scan)
 };
+
+int query_bits_of(int32_t bits)
+{
+  const int qb = bits == 0 ? 4 : bits;
+  RBQ_CHECK(qb == 4 || qb == 8, RBQ_ERR_INVALID, "query bits must be 4 (QUANT4) or 8 (QUANT8)");
+  return qb;
+}
+
+// Scale constant of the query code width: t4 (const_scaling_factor_4bit, best rescale for 3
+// extra bits) or t8 (const_scaling_factor_8bit, 7 extra bits; quantizer_gpu.cuh:81-85), the
+// latter computed on first use unless an imported reference file supplied it.
+float query_t(Index& ix, int qbits)
+{
+  if (qbits == 4) return ix.t4;
+  if (std::isnan(ix.t8)) ix.t8 = query_scale(ix.Dp, ix.seed, 7);
+  return ix.t8;
+}
 
 SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq)
 {
@@ -627,6 +645,7 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(16, sp.P / 2);
   sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
   sp.prune = p.prune ? 1 : 0;
+  sp.qbits = query_bits_of(p.query_bits);
   sp.seeded = p.seeded < 0 ? sp.slices > 1 : p.seeded > 0;
   return sp;
 }
@@ -634,9 +653,10 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
 // Scan arguments of one query batch against this shard's lists (probes: [nq, nprobe]).
 ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* planes, const float* delta,
                          const float* k1, int64_t nq, const int32_t* probes, const float* g, int nprobe, int R,
-                         int cap, int prune, int slices, unsigned long long* out_keys, uint64_t* stats)
+                         int cap, int prune, int slices, unsigned long long* out_keys, uint64_t* stats, int qbits)
 {
   ScanArgs sa;
+  sa.qbits = qbits;
   sa.list_off = ix.list_off;
   sa.ids = ix.ids;
   sa.codes = ix.codes;
@@ -674,7 +694,7 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
                  unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, cudaStream_t s)
 {
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
-                                keys_s, stats);
+                                keys_s, stats, sp.qbits);
   if (sp.seeded && sp.prune) {
     ScanArgs a0 = sa;
     a0.nprobe = 1;
@@ -711,7 +731,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   int32_t* cand = sc.get<int32_t>((size_t)fe_chunk * sp.m);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
   float* g = sc.get<float>((size_t)chunk * sp.P);
-  uint32_t* planes = sc.get<uint32_t>((size_t)chunk * 4 * ix.W);
+  uint32_t* planes = sc.get<uint32_t>((size_t)chunk * sp.qbits * ix.W);
+  const float qt = query_t(ix, sp.qbits);
   float* delta = sc.get<float>(chunk);
   float* k1 = sc.get<float>(chunk);
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
@@ -730,7 +751,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       launch_topm_rows(S, fn, ix.K, sp.m, cand, s);
       launch_refine_topp(Qrb, fn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes + b * sp.P, g + b * sp.P, s);
     }
-    launch_query_prep(Qr, cn, ix.Dp, ix.t4, planes, delta, k1, s);
+    launch_query_prep(Qr, cn, ix.Dp, qt, sp.qbits, planes, delta, k1, s);
     {
       Range r("rbq scan");
       search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
@@ -937,6 +958,7 @@ void rbq_search_params_default(rbq_search_params_t* p)
 {
   if (!p) return;
   p->n_probes = 20;
+  p->query_bits = 4;
   p->k = 10;
   p->rerank = 0;
   p->prune = 1;
@@ -1594,7 +1616,7 @@ int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, 
 }
 
 int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev, float* delta_dev,
-                   float* k1_dev, void* stream)
+                   float* k1_dev, int32_t query_bits, void* stream)
 {
   return guarded([&] {
     Range nvtx_range("rbq_query_prep");
@@ -1602,7 +1624,8 @@ int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t
               "null argument");
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
-    launch_query_prep(Qr_dev, nq, ix.Dp, ix.t4, planes_dev, delta_dev, k1_dev, as_stream(stream));
+    const int qb = query_bits_of(query_bits);
+    launch_query_prep(Qr_dev, nq, ix.Dp, query_t(ix, qb), qb, planes_dev, delta_dev, k1_dev, as_stream(stream));
   });
 }
 
@@ -1670,7 +1693,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
              int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R, int32_t prune,
              int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev, uint64_t* stats_dev,
-             void* stream)
+             int32_t query_bits, void* stream)
 {
   return guarded([&] {
     Range nvtx_range("rbq_scan");
@@ -1690,7 +1713,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     unsigned long long* ks = sc.get<unsigned long long>((size_t)nq * slices * R);
     unsigned long long* k2 = slices > 1 ? sc.get<unsigned long long>((size_t)nq * R) : ks;
     ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
-                                  prune, slices, ks, stats_dev);
+                                  prune, slices, ks, stats_dev, query_bits_of(query_bits));
     sa.tau0 = tau0_dev;
     sa.pstride = probe_stride;
     if (init_ids_dev) {
@@ -1706,7 +1729,7 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
 
 int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
                    const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
-                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, void* stream)
+                   int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, int32_t query_bits, void* stream)
 {
   return guarded([&] {
     Range nvtx_range("rbq_bound_seed");
@@ -1720,7 +1743,7 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
     DeviceGuard dg(ix.device);
     const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
     ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
-                                  1, 1, nullptr, nullptr);
+                                  1, 1, nullptr, nullptr, query_bits_of(query_bits));
     sa.pstride = probe_stride;
     sa.tau_out = tau_dev;
     launch_scan(sa, as_stream(stream));
@@ -1728,14 +1751,15 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
 }
 
 int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float delta, float k1, float g, int32_t list,
-                       int32_t* acc_dev, float* est_dev, float* low_dev, void* stream)
+                       int32_t* acc_dev, float* est_dev, float* low_dev, int32_t query_bits, void* stream)
 {
   return guarded([&] {
     RBQ_CHECK(index && planes_dev && acc_dev && est_dev && low_dev, RBQ_ERR_INVALID, "null argument");
     Index& ix = index->ix;
     RBQ_CHECK(list >= 0 && list < ix.K, RBQ_ERR_INVALID, "list out of range");
     DeviceGuard dg(ix.device);
-    launch_list_estimates(ix, planes_dev, delta, k1, g, list, acc_dev, est_dev, low_dev, as_stream(stream));
+    launch_list_estimates(ix, planes_dev, query_bits_of(query_bits), delta, k1, g, list, acc_dev, est_dev, low_dev,
+                          as_stream(stream));
   });
 }
 
@@ -1825,7 +1849,7 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
                                 const float* g_dev, int32_t nprobe, int32_t probe_stride, const float* tau0_dev,
                                 int32_t R, int32_t prune,
                                 int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
-                                uint64_t* stats_dev, void* stream)
+                                uint64_t* stats_dev, int32_t query_bits, void* stream)
 {
   return guarded([&] {
     RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
@@ -1850,7 +1874,7 @@ extern "C" int rbq_scan_noalloc(rbq_index_t* index, const float* Qr_dev, const u
     unsigned long long* k2 = slices > 1 ? reinterpret_cast<unsigned long long*>(base + keys_bytes) : ks;
     const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
     ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
-                                  prune, slices, ks, stats_dev);
+                                  prune, slices, ks, stats_dev, query_bits_of(query_bits));
     sa.tau0 = tau0_dev;
     sa.pstride = probe_stride;
     launch_scan(sa, s);

@@ -170,8 +170,9 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
 // Exact refine: g = sum_j double(a_j - c_j)^2 for the m candidates, then top-p by (g, id).
 void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m,
                         int p, int32_t* probes, float* g, cudaStream_t s);
-// 4-bit query planes, delta and k1.
-void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* planes, float* delta,
+// B-bit query planes (B = qbits: 4 for QUANT4, 8 for QUANT8; planes [nq, B, W]), delta and k1;
+// t is the index's scale constant for that width (t4 or t8).
+void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t, int qbits, uint32_t* planes, float* delta,
                        float* k1, cudaStream_t s);
 
 struct ScanArgs {
@@ -184,7 +185,8 @@ struct ScanArgs {
   int64_t n_slots;  // vectors on the shard (the scan indexes slots with 32-bit ints)
   int Dp, W;
   const float* Qr;
-  const uint32_t* planes;
+  const uint32_t* planes;  // [nq, qbits, W]
+  int qbits = 4;           // query code width: 4 (QUANT4) or 8 (QUANT8)
   const float* delta;
   const float* k1;
   int64_t nq;
@@ -213,8 +215,8 @@ struct ScanArgs {
 constexpr int kScanTile = 512;  // vectors per scan tile (256 threads x 2)
 void launch_scan(const ScanArgs& a, cudaStream_t s);
 // Phase-1 dump for one query and one list.
-void launch_list_estimates(const Index& ix, const uint32_t* planes, float delta, float k1, float g, int list,
-                           int32_t* acc, float* est, float* low, cudaStream_t s);
+void launch_list_estimates(const Index& ix, const uint32_t* planes, int qbits, float delta, float k1, float g,
+                           int list, int32_t* acc, float* est, float* low, cudaStream_t s);
 // Merge [nq, parts, R] keys -> [nq, R] keys (ascending).
 void launch_merge_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,
                        cudaStream_t s);

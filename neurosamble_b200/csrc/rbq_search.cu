@@ -300,21 +300,25 @@ void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const
 }
 
 // ---------------------------------------------------------------------------------------
-// 4-bit query quantisation (exrabitq_quantize_query<256> with EX_BITS = 4,
-// searcher_gpu_quantize_query.cu:655-793) and k1 = -0.5 * sum q (ivf_gpu.cu:1451-1490).
-// One thread per query; sums are double accumulations in dimension order.  A block of 32
-// queries first stages its rows in shared memory (coalesced loads; rows padded by one float so
-// that the 32 threads reading column j hit 32 banks).
-//   code_j = clamp(rint(t4 * (q_j * (1/|q|))), -8, 7)
+// QB-bit query quantisation (exrabitq_quantize_query<256> with EX_BITS = num_bits = QB,
+// searcher_gpu_quantize_query.cu:655-793; QUANT4: QB = 4, scale t4; QUANT8: QB = 8, scale t8)
+// and k1 = -0.5 * sum q (ivf_gpu.cu:1451-1490).  One thread per query; sums are double
+// accumulations in dimension order.  A block of 32 queries first stages its rows in shared
+// memory (coalesced loads; rows padded by one float so that the 32 threads reading column j
+// hit 32 banks).
+//   code_j = clamp(rint(t * (q_j * (1/|q|))), -2^(QB-1), 2^(QB-1) - 1)
 //   delta = (|q| / |code|) * (<q, code> / (|q| * |code|))   (0 if either norm <= 1e-6)
-//   plane b, word w, bit 31-j = bit b of (code_{32w+j} & 0xF)
+//   plane b, word w, bit 31-j = bit b of the QB-bit two's complement of code_{32w+j}
 // ---------------------------------------------------------------------------------------
 constexpr int kPrepQueries = 32;
 
+template <int QB>
 __global__ void __launch_bounds__(kPrepQueries) query_prep_kernel(const float* __restrict__ Qr, int64_t nq, int Dp,
-                                                                  float t4, uint32_t* __restrict__ planes,
+                                                                  float t, uint32_t* __restrict__ planes,
                                                                   float* __restrict__ delta, float* __restrict__ k1)
 {
+  constexpr int kHi = (1 << (QB - 1)) - 1, kLo = -(1 << (QB - 1));
+  constexpr uint32_t kMask = (1u << QB) - 1u;
   extern __shared__ float rows[];  // [kPrepQueries][Dp + 1]
   const int64_t q0 = (int64_t)blockIdx.x * kPrepQueries;
   const int nb = (int)(nq - q0 < kPrepQueries ? nq - q0 : kPrepQueries);
@@ -334,29 +338,27 @@ __global__ void __launch_bounds__(kPrepQueries) query_prep_kernel(const float* _
   const float norm = sqrtf((float)s2);
   const float norm_inv = (norm > 0.0f) ? (1.0f / norm) : 0.0f;
   const int W = Dp >> 5;
-  uint32_t* pl = planes + q * 4 * W;
+  uint32_t* pl = planes + q * QB * W;
   double ipd = 0.0;
   long long xs = 0;
   for (int w = 0; w < W; ++w) {
-    uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-    for (int b = 0; b < 32; ++b) {
-      const int j = (w << 5) + b;
+    uint32_t p[QB];
+#pragma unroll
+    for (int b = 0; b < QB; ++b) p[b] = 0u;
+    for (int j32 = 0; j32 < 32; ++j32) {
+      const int j = (w << 5) + j32;
       const float val = x[j] * norm_inv;
-      int cv = __float2int_rn(t4 * val);
-      cv = cv > 7 ? 7 : (cv < -8 ? -8 : cv);
+      int cv = __float2int_rn(t * val);
+      cv = cv > kHi ? kHi : (cv < kLo ? kLo : cv);
       ipd += (double)x[j] * (double)cv;
       xs += (long long)(cv * cv);
-      const uint32_t u = (uint32_t)cv & 0xFu;
-      const int sh = 31 - b;
-      p0 |= (u & 1u) << sh;
-      p1 |= ((u >> 1) & 1u) << sh;
-      p2 |= ((u >> 2) & 1u) << sh;
-      p3 |= ((u >> 3) & 1u) << sh;
+      const uint32_t u = (uint32_t)cv & kMask;
+      const int sh = 31 - j32;
+#pragma unroll
+      for (int b = 0; b < QB; ++b) p[b] |= ((u >> b) & 1u) << sh;
     }
-    pl[0 * W + w] = p0;
-    pl[1 * W + w] = p1;
-    pl[2 * W + w] = p2;
-    pl[3 * W + w] = p3;
+#pragma unroll
+    for (int b = 0; b < QB; ++b) pl[b * W + w] = p[b];
   }
   const float ip = (float)ipd;
   const float xu_sq = (float)xs;
@@ -370,15 +372,22 @@ __global__ void __launch_bounds__(kPrepQueries) query_prep_kernel(const float* _
   k1[q] = ((float)s1) * -0.5f;
 }
 
-void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* planes, float* delta, float* k1,
-                       cudaStream_t s)
+void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t, int qbits, uint32_t* planes, float* delta,
+                       float* k1, cudaStream_t s)
 {
   if (nq <= 0) return;
+  RBQ_CHECK(qbits == 4 || qbits == 8, RBQ_ERR_INVALID, "query bits must be 4 (QUANT4) or 8 (QUANT8)");
   const size_t smem = (size_t)kPrepQueries * (Dp + 1) * sizeof(float);
-  if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(query_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  query_prep_kernel<<<(unsigned)ceil_div(nq, kPrepQueries), kPrepQueries, smem, s>>>(Qr, nq, Dp, t4, planes, delta,
-                                                                                       k1);
+  const unsigned grid = (unsigned)ceil_div(nq, kPrepQueries);
+  if (qbits == 4) {
+    if (smem > 48 * 1024)
+      RBQ_CUDA(cudaFuncSetAttribute(query_prep_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    query_prep_kernel<4><<<grid, kPrepQueries, smem, s>>>(Qr, nq, Dp, t, planes, delta, k1);
+  } else {
+    if (smem > 48 * 1024)
+      RBQ_CUDA(cudaFuncSetAttribute(query_prep_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    query_prep_kernel<8><<<grid, kPrepQueries, smem, s>>>(Qr, nq, Dp, t, planes, delta, k1);
+  }
   RBQ_LAUNCHED();
 }
 
@@ -553,10 +562,22 @@ __device__ __forceinline__ int32_t signed_dot4(const PF& P, const uint32_t (&c)[
 }
 
 // Whole vector: chunks of 8 words (or one 4-word chunk), else one popcount per plane word.
-template <int W, typename PF>
+// QB = 8 (QUANT8, searcher_gpu_quantize_query.cu:253-262 with NumBits = 8): one popcount per
+// plane word, sum_w [sum_{b<7} popc(P_b & c) << b - popc(P_7 & c) << 7].
+template <int W, int QB = 4, typename PF>
 __device__ __forceinline__ int32_t signed_dot(const PF& P, const uint32_t (&c)[W])
 {
-  if constexpr (W % 8 == 0) {
+  if constexpr (QB == 8) {
+    int32_t acc = 0;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      int32_t pos = 0;
+#pragma unroll
+      for (int b = 0; b < 7; ++b) pos += __popc(P(b, w) & c[w]) << b;
+      acc += pos - (__popc(P(7, w) & c[w]) << 7);
+    }
+    return acc;
+  } else if constexpr (W % 8 == 0) {
     int32_t acc = 0;
 #pragma unroll
     for (int k = 0; k < W / 8; ++k) {
@@ -666,7 +687,7 @@ constexpr int scan_min_blocks()
   return W <= 8 ? 6 : 4;
 }
 
-template <int W>
+template <int W, int QB>
 __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kernel(const ScanArgs a)
 {
   constexpr int NB = 4 * W;
@@ -677,8 +698,8 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   int* lbase = pre + (a.nprobe + 1);                                            // [nprobe]
   float* lg = reinterpret_cast<float*>(lbase + a.nprobe);                       // [nprobe]
   float* lsq = lg + a.nprobe;                                                   // [nprobe]
-  uint32_t* pl = reinterpret_cast<uint32_t*>(lsq + a.nprobe);                  // [4 * W]
-  float* qsT = reinterpret_cast<float*>(pl + 4 * W);                            // [8 * NB]
+  uint32_t* pl = reinterpret_cast<uint32_t*>(lsq + a.nprobe);                  // [QB * W]
+  float* qsT = reinterpret_cast<float*>(pl + QB * W);                           // [8 * NB]
   __shared__ int s_count, s_nl, s_misc[3], s_cnt2;
   __shared__ float s_tau;
   __shared__ unsigned s_hist[256];
@@ -692,7 +713,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     const int jj = i / NB, j = i - jj * NB;
     qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
   }
-  for (int j = tid; j < 4 * W; j += kScanThreads) pl[j] = a.planes[q * 4 * W + j];
+  for (int j = tid; j < QB * W; j += kScanThreads) pl[j] = a.planes[q * QB * W + j];
   if (warp == 0) {
     // The slice's lists: owned probes (owner[l] == shard_rank) with owned-rank in
     // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
@@ -785,7 +806,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
         const int slot = lbase[c] + (f - pre[c]);
         uint32_t cw[W];
         load_code<W>(a.codes, slot, cw);
-        const int32_t acc = signed_dot<W>(P, cw);
+        const int32_t acc = signed_dot<W, QB>(P, cw);
         const float base_d = __fadd_rn(__ldg(a.fadd + slot), lg[c]);
         const float ip = __fmul_rn((float)acc, delta);
         const float est = __fadd_rn(base_d, __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(ip, k1)));
@@ -837,7 +858,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
         const int slot = sadj + f;
         uint32_t c[W];
         load_code<W>(a.codes, slot, c);
-        const int32_t acc = signed_dot<W>(P, c);
+        const int32_t acc = signed_dot<W, QB>(P, c);
         const float fr = __ldg(a.frescale + slot);
         const float base_d = __fadd_rn(__ldg(a.fadd + slot), gc);
         const float ip = __fmul_rn((float)acc, delta);
@@ -911,19 +932,28 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   }
 }
 
-template <int W>
-static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
+template <int W, int QB>
+static void launch_scan_wq(const ScanArgs& a, cudaStream_t s)
 {
   constexpr int NB = 4 * W;
   const size_t smem = (size_t)a.cap * 8 * 2 + (size_t)(2 * a.nprobe + 1) * 4 + (size_t)2 * a.nprobe * 4 +
-                      (size_t)4 * W * 4 + (size_t)8 * NB * 4;
+                      (size_t)QB * W * 4 + (size_t)8 * NB * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "scan: shared memory budget exceeded (cap/nprobe too large)");
   if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t blocks = a.nq * a.slices;
   RBQ_CHECK(blocks <= 0x7fffffff, RBQ_ERR_INVALID, "scan: grid too large");
-  scan_kernel<W><<<(unsigned)blocks, kScanThreads, smem, s>>>(a);
+  scan_kernel<W, QB><<<(unsigned)blocks, kScanThreads, smem, s>>>(a);
   RBQ_LAUNCHED();
+}
+
+template <int W>
+static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
+{
+  if (a.qbits == 8)
+    launch_scan_wq<W, 8>(a, s);
+  else
+    launch_scan_wq<W, 4>(a, s);
 }
 
 void launch_scan(const ScanArgs& args, cudaStream_t s)
@@ -937,6 +967,7 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
   RBQ_CHECK(a.cap >= a.R + kScanTile && (a.cap & (a.cap - 1)) == 0, RBQ_ERR_INVALID,
             "scan: cap must be a power of two >= R + tile");
   RBQ_CHECK(a.Dp == 32 * a.W, RBQ_ERR_INVALID, "scan: padded dim mismatch");
+  RBQ_CHECK(a.qbits == 4 || a.qbits == 8, RBQ_ERR_INVALID, "scan: query bits must be 4 (QUANT4) or 8 (QUANT8)");
   RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
             "scan: more than 2^31 vectors on one shard");
   switch (a.W) {
@@ -1319,9 +1350,9 @@ void launch_merge_results(const float* dist, const int64_t* ids, int parts, int6
 template <int W>
 __global__ void list_estimates_kernel(const uint32_t* __restrict__ codes, const float* __restrict__ fadd,
                                       const float* __restrict__ frescale, const float* __restrict__ ferr,
-                                      int64_t base, int64_t n, const uint32_t* __restrict__ planes, float delta,
-                                      float k1, float g, int32_t* __restrict__ acc_out, float* __restrict__ est_out,
-                                      float* __restrict__ low_out)
+                                      int64_t base, int64_t n, const uint32_t* __restrict__ planes, int qbits,
+                                      float delta, float k1, float g, int32_t* __restrict__ acc_out,
+                                      float* __restrict__ est_out, float* __restrict__ low_out)
 {
   const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= n) return;
@@ -1329,12 +1360,9 @@ __global__ void list_estimates_kernel(const uint32_t* __restrict__ codes, const 
   uint32_t c[W];
   load_code<W>(codes, slot, c);
   int32_t acc = 0;
-#pragma unroll
   for (int w = 0; w < W; ++w) {
-    acc += __popc(planes[0 * W + w] & c[w]);
-    acc += __popc(planes[1 * W + w] & c[w]) << 1;
-    acc += __popc(planes[2 * W + w] & c[w]) << 2;
-    acc -= __popc(planes[3 * W + w] & c[w]) << 3;
+    for (int b = 0; b < qbits - 1; ++b) acc += __popc(planes[b * W + w] & c[w]) << b;
+    acc -= __popc(planes[(qbits - 1) * W + w] & c[w]) << (qbits - 1);
   }
   const float base_d = __fadd_rn(fadd[slot], g);
   const float ip = __fmul_rn((float)acc, delta);
@@ -1345,16 +1373,17 @@ __global__ void list_estimates_kernel(const uint32_t* __restrict__ codes, const 
   low_out[v] = low;
 }
 
-void launch_list_estimates(const Index& ix, const uint32_t* planes, float delta, float k1, float g, int list,
-                           int32_t* acc, float* est, float* low, cudaStream_t s)
+void launch_list_estimates(const Index& ix, const uint32_t* planes, int qbits, float delta, float k1, float g,
+                           int list, int32_t* acc, float* est, float* low, cudaStream_t s)
 {
+  RBQ_CHECK(qbits == 4 || qbits == 8, RBQ_ERR_INVALID, "estimates: query bits must be 4 or 8");
   const int64_t base = ix.off_host[list], n = ix.off_host[list + 1] - base;
   if (n <= 0) return;
   const unsigned grid = (unsigned)ceil_div(n, 128);
 #define RBQ_LE_CASE(WW)                                                                                     \
   case WW:                                                                                                  \
     list_estimates_kernel<WW><<<grid, 128, 0, s>>>(ix.codes, ix.fadd, ix.frescale, ix.ferr, base, n, planes, \
-                                                   delta, k1, g, acc, est, low);                            \
+                                                   qbits, delta, k1, g, acc, est, low);                     \
     break;
   switch (ix.W) {
     RBQ_LE_CASE(1)

@@ -46,7 +46,7 @@ class IndexIVFRaBitQ:
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
     scan slices start from the nearest list's bound seed: -1 = auto, on when the probes are split;
-    0 off; 1 on).
+    0 off; 1 on), ``query_bits`` (4: QUANT4, the reference CLI's default; 8: QUANT8).
     """
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
@@ -65,6 +65,7 @@ class IndexIVFRaBitQ:
         self.cand_cap = 0
         self.coarse_margin = 0
         self.seeded = -1
+        self.query_bits = 4
         self._h = ctypes.c_void_p()
         if _handle is not None:
             self._h = _handle
@@ -182,6 +183,7 @@ class IndexIVFRaBitQ:
         sp.prune, sp.probe_split = int(bool(self.prune)), int(self.probe_split)
         sp.cand_cap, sp.coarse_margin = int(self.cand_cap), int(self.coarse_margin)
         sp.seeded = int(self.seeded)
+        sp.query_bits = int(self.query_bits)
         return sp
 
     def search(self, x, k: int):

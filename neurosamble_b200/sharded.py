@@ -94,12 +94,12 @@ class ShardedIndexIVFRaBitQ:
         self.device = self.local.device
 
     def __getattr__(self, name):
-        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin"):
+        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits"):
             return getattr(self.local, name)
         raise AttributeError(name)
 
     def __setattr__(self, name, value):
-        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin"):
+        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits"):
             setattr(self.local, name, value)
         else:
             object.__setattr__(self, name, value)
@@ -140,7 +140,8 @@ class ShardedIndexIVFRaBitQ:
             loc = self.local
             d, i = sharded_search(LibStages(loc), t, int(k), int(loc.nprobe), int(loc.k_rerank), bool(loc.prune),
                                   int(loc.probe_split), int(loc.cand_cap), int(loc.coarse_margin),
-                                  loc.info().padded_dim, self.rank, self.world, self.group, stats)
+                                  loc.info().padded_dim, self.rank, self.world, self.group, stats,
+                                  query_bits=int(loc.query_bits))
             if loc.metric == "ip":
                 d = 1.0 - 0.5 * d
         if on_dev:
@@ -161,8 +162,10 @@ class LibStages:
             _lib.call("rbq_rotate", self.h, _ptr(q), q.shape[0], _ptr(qr), self.st)
 
     def prep(self, qr, planes, delta, k1):
+        """planes: [nq, bits, W]; bits (4 or 8) is the query code width."""
         with torch.cuda.device(self.device):
-            _lib.call("rbq_query_prep", self.h, _ptr(qr), qr.shape[0], _ptr(planes), _ptr(delta), _ptr(k1), self.st)
+            _lib.call("rbq_query_prep", self.h, _ptr(qr), qr.shape[0], _ptr(planes), _ptr(delta), _ptr(k1),
+                      planes.shape[1], self.st)
 
     def coarse(self, qr, margin, probes, g):
         with torch.cuda.device(self.device):
@@ -173,7 +176,8 @@ class LibStages:
         assert probes.stride(1) == 1 and g.stride() == probes.stride()
         with torch.cuda.device(self.device):
             _lib.call("rbq_bound_seed", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0],
-                      _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), R, cap, _ptr(tau), self.st)
+                      _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), R, cap, _ptr(tau), planes.shape[1],
+                      self.st)
 
     def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
         """probes / g: [nq, p] views with unit column stride and one row stride."""
@@ -182,7 +186,8 @@ class LibStages:
             _lib.call("rbq_scan", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0], _ptr(probes),
                       _ptr(g), probes.shape[1], probes.stride(0), _ptr(tau0) if tau0 is not None else None,
                       _ptr(init[0]) if init is not None else None, _ptr(init[1]) if init is not None else None, R,
-                      prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None, self.st)
+                      prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None,
+                      planes.shape[1], self.st)
 
     def merge(self, d, ids, out_d, out_i):
         with torch.cuda.device(self.device):
@@ -196,7 +201,8 @@ class LibStages:
 
 
 def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, prune: bool, probe_split: int,
-                   cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None):
+                   cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None,
+                   query_bits: int = 4):
     """The four steps of a sharded search (module docstring) for the batch t [nq, D] that
     every rank passes; `stages` computes (LibStages: librbq.so), this function moves data."""
     dev = t.device
@@ -222,7 +228,7 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     dist.all_gather_into_tensor(recv, send, group=group)
     qr = qr_all[:nq]
     probes, g = recv[:nq, :P], recv[:nq, P:].view(torch.float32)  # row stride 2P
-    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
+    planes = torch.empty((nq, query_bits, dp // 32), dtype=torch.int32, device=dev)
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)

@@ -5,9 +5,10 @@ The reference exposes its CUDA code to Python as JIT-compiled torch extensions
 torch user finds them, ``torch.ops.rbq.<name>``, each a thin wrapper of one ``rbq_*`` entry
 point of include/rbq.h:
 
-  search(h, q, k, nprobe, rerank, prune, probe_split, seeded) -> (dist [n, k] f32, ids [n, k] i64)
+  search(h, q, k, nprobe, rerank, prune, probe_split, seeded, query_bits=4)
+                                             -> (dist [n, k] f32, ids [n, k] i64)
   rotate(h, x)                               -> xr [n, Dp]                         (rbq_rotate)
-  query_prep(h, qr)                          -> (planes [n, 4, Dp/32] i32, delta [n], k1 [n])
+  query_prep(h, qr, bits=4)                  -> (planes [n, bits, Dp/32] i32, delta [n], k1 [n])
   coarse(h, qr, nprobe, margin)              -> (probes [n, nprobe] i32, g [n, nprobe] f32)
   scan(h, qr, planes, delta, k1, probes, g, R, prune, slices, cand_cap, tau0)
                                              -> (cand_ids [n, R] i64, cand_dist [n, R] f32)
@@ -15,7 +16,9 @@ point of include/rbq.h:
   rerank(h, q, cand_ids, k)                  -> (dist [n, k] f32, ids [n, k] i64)
   merge_results(dist [p, n, k], ids [p, n, k]) -> (dist [n, k], ids [n, k])
 
-``h`` is the index handle as an int (``IndexIVFRaBitQ.handle.value``).  Inputs are CUDA tensors
+``h`` is the index handle as an int (``IndexIVFRaBitQ.handle.value``).  ``bits`` / ``query_bits``
+is the query code width, 4 (QUANT4) or 8 (QUANT8); scan and bound_seed take it from the
+planes' shape.  Inputs are CUDA tensors
 on the index's device (made contiguous here); outputs are allocated by PyTorch on that device,
 and the work is enqueued on ``torch.cuda.current_stream()`` of it, without synchronising.
 Distances are squared L2, ascending; missing results have id -1 and distance +inf.  A failed
@@ -64,13 +67,13 @@ def _dp(d: int) -> int:
 
 @custom_op("rbq::search", mutates_args=())
 def search(handle: int, q: Tensor, k: int, nprobe: int, rerank: int, prune: bool, probe_split: int,
-           seeded: int) -> Pair:
+           seeded: int, query_bits: int = 4) -> Pair:
     q = _cuda(q, torch.float32, "q")
     n = q.shape[0]
     sp = _lib.SearchParams()
     _lib.lib().rbq_search_params_default(ctypes.byref(sp))
     sp.n_probes, sp.k, sp.rerank, sp.prune = nprobe, k, rerank, int(prune)
-    sp.probe_split, sp.seeded = probe_split, seeded
+    sp.probe_split, sp.seeded, sp.query_bits = probe_split, seeded, query_bits
     dist = torch.empty((n, k), dtype=torch.float32, device=q.device)
     ids = torch.empty((n, k), dtype=torch.int64, device=q.device)
     with torch.cuda.device(q.device):
@@ -79,7 +82,7 @@ def search(handle: int, q: Tensor, k: int, nprobe: int, rerank: int, prune: bool
 
 
 @search.register_fake
-def _(handle, q, k, nprobe, rerank, prune, probe_split, seeded):
+def _(handle, q, k, nprobe, rerank, prune, probe_split, seeded, query_bits=4):
     n = q.shape[0]
     return q.new_empty((n, k)), q.new_empty((n, k), dtype=torch.int64)
 
@@ -98,22 +101,28 @@ def _(handle, x):
     return x.new_empty((x.shape[0], _dp(x.shape[1])))
 
 
+def _bits(bits: int) -> int:
+    if bits not in (4, 8):
+        raise RuntimeError(f"rbq: query bits must be 4 (QUANT4) or 8 (QUANT8), got {bits}")
+    return bits
+
+
 @custom_op("rbq::query_prep", mutates_args=())
-def query_prep(handle: int, qr: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
+def query_prep(handle: int, qr: Tensor, bits: int = 4) -> Tuple[Tensor, Tensor, Tensor]:
     qr = _cuda(qr, torch.float32, "qr")
     n, dp = qr.shape
-    planes = torch.empty((n, 4, dp // 32), dtype=torch.int32, device=qr.device)
+    planes = torch.empty((n, _bits(bits), dp // 32), dtype=torch.int32, device=qr.device)
     delta = torch.empty(n, dtype=torch.float32, device=qr.device)
     k1 = torch.empty(n, dtype=torch.float32, device=qr.device)
     with torch.cuda.device(qr.device):
-        _lib.call("rbq_query_prep", _h(handle), _p(qr), n, _p(planes), _p(delta), _p(k1), _st(qr))
+        _lib.call("rbq_query_prep", _h(handle), _p(qr), n, _p(planes), _p(delta), _p(k1), bits, _st(qr))
     return planes, delta, k1
 
 
 @query_prep.register_fake
-def _(handle, qr):
+def _(handle, qr, bits=4):
     n, dp = qr.shape
-    return qr.new_empty((n, 4, dp // 32), dtype=torch.int32), qr.new_empty(n), qr.new_empty(n)
+    return qr.new_empty((n, _bits(bits), dp // 32), dtype=torch.int32), qr.new_empty(n), qr.new_empty(n)
 
 
 @custom_op("rbq::coarse", mutates_args=())
@@ -150,7 +159,8 @@ def scan(handle: int, qr: Tensor, planes: Tensor, delta: Tensor, k1: Tensor, pro
     dist = torch.empty((n, R), dtype=torch.float32, device=qr.device)
     with torch.cuda.device(qr.device):
         _lib.call("rbq_scan", _h(handle), _p(qr), _p(planes), _p(delta), _p(k1), n, _p(probes), _p(g), nprobe,
-                  nprobe, _p(tau0), None, None, R, int(prune), slices, cand_cap, _p(ids), _p(dist), None, _st(qr))
+                  nprobe, _p(tau0), None, None, R, int(prune), slices, cand_cap, _p(ids), _p(dist), None,
+                  _bits(planes.shape[1]), _st(qr))
     return ids, dist
 
 
@@ -168,7 +178,7 @@ def bound_seed(handle: int, qr: Tensor, planes: Tensor, delta: Tensor, k1: Tenso
     tau = torch.empty(n, dtype=torch.float32, device=qr.device)
     with torch.cuda.device(qr.device):
         _lib.call("rbq_bound_seed", _h(handle), _p(qr), _p(planes), _p(delta), _p(k1), n, _p(probes), _p(g),
-                  nprobe, nprobe, R, cand_cap, _p(tau), _st(qr))
+                  nprobe, nprobe, R, cand_cap, _p(tau), _bits(planes.shape[1]), _st(qr))
     return tau
 
 

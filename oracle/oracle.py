@@ -54,9 +54,9 @@ def lib():
         L.orc_quantize_one.argtypes = [_f32p, _f32p, _i32, _u32p, _f32p]
         L.orc_build.argtypes = [_f32p, _i64, _i32, _i32, _f32p, _f32p, _i32, _u32p,
                                 _i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _f32p]
-        L.orc_query_prep.argtypes = [_f32p, _i64, _i32, ctypes.c_float, _u32p, _f32p, _f32p, _i8p]
+        L.orc_query_prep.argtypes = [_f32p, _i64, _i32, ctypes.c_float, _i32, _u32p, _f32p, _f32p, _i8p]
         L.orc_coarse.argtypes = [_f32p, _i64, _f32p, _i32, _i32, _i32, _i32p, _f32p]
-        L.orc_popcount_ip.argtypes = [_u32p, _u32p, _i32]
+        L.orc_popcount_ip.argtypes = [_u32p, _u32p, _i32, _i32]
         L.orc_popcount_ip.restype = ctypes.c_int32
         L.orc_estimate.argtypes = [_f32p, ctypes.c_float, ctypes.c_int32, ctypes.c_float, ctypes.c_float, _f32p]
         L.orc_exact_ip.argtypes = [_f32p, _u32p, _i32]
@@ -64,9 +64,9 @@ def lib():
         L.orc_scan.argtypes = [_i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _i32, _f32p, _u32p,
                                _f32p, _f32p, _i64, _i32p, _f32p, _i32, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_void_p,
-                               _i64p, _f32p, _i64p]
+                               _i64p, _f32p, _i64p, _i32]
         L.orc_bound_seed.argtypes = [_i64p, _u32p, _f32p, _f32p, _f32p, _i32, _u32p, _f32p, _f32p, _i64, _i32p,
-                                     _f32p, _i32, _i32, _i32, _i32, ctypes.c_void_p, _f32p]
+                                     _f32p, _i32, _i32, _i32, _i32, ctypes.c_void_p, _f32p, _i32]
         L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
         L.orc_l2_exact.restype = ctypes.c_float
         L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
@@ -160,6 +160,7 @@ class OracleIndex:
 
     def __init__(self, d, dp, k, list_off, ids, codes, fadd, frescale, ferr, c_rot, P, t4, X):
         self.d, self.dp, self.k = d, dp, k
+        self.t8 = None  # 8-bit query scale (QUANT8), query_scale(dp, seed, 7) of the index
         self.list_off, self.ids, self.codes = list_off, ids, codes
         self.fadd, self.frescale, self.ferr = fadd, frescale, ferr
         self.c_rot, self.P, self.t4, self.X = c_rot, P, t4, X
@@ -184,16 +185,27 @@ def build(X, C, labels, P, t4) -> OracleIndex:
     return OracleIndex(d, dp, k, list_off, ids, codes, fadd, fres, ferr, c_rot, P, t4, X)
 
 
-def query_prep(Qr, t4: float):
+def query_prep(Qr, t4: float, bits: int = 4):
+    """Planes [nq, bits, W], delta, k1 and int8 codes of bits-bit query codes (4: QUANT4 with t4,
+    8: QUANT8 with t8)."""
+    assert bits in (4, 8)
     Qr = _c(Qr, np.float32)
     nq, dp = Qr.shape
     w = dp // 32
-    planes = np.empty((nq, 4, w), np.uint32)
+    planes = np.empty((nq, bits, w), np.uint32)
     delta = np.empty(nq, np.float32)
     k1 = np.empty(nq, np.float32)
     codes = np.empty((nq, dp), np.int8)
-    lib().orc_query_prep(Qr, nq, dp, np.float32(t4), planes, delta, k1, codes)
+    lib().orc_query_prep(Qr, nq, dp, np.float32(t4), bits, planes, delta, k1, codes)
     return planes, delta, k1, codes
+
+
+def _bits_of(planes, nq, w) -> int:
+    """Query code width of planes [nq, bits, w] (or the same words flattened)."""
+    planes = np.asarray(planes)
+    if planes.ndim == 3:
+        return int(planes.shape[1])
+    return 4 if nq == 0 else int(planes.size // (nq * w))
 
 
 def coarse(Qr, Cr, nprobe: int):
@@ -206,8 +218,10 @@ def coarse(Qr, Cr, nprobe: int):
 
 
 def popcount_ip(planes, code) -> int:
+    """planes: one query's [bits, W] planes (bits = planes.size / W)."""
     code = _c(code, np.uint32)
-    return int(lib().orc_popcount_ip(_c(planes, np.uint32), code, code.size))
+    planes = _c(planes, np.uint32)
+    return int(lib().orc_popcount_ip(planes, code, code.size, planes.size // code.size))
 
 
 def estimate(f3, g, acc, delta, k1):
@@ -250,7 +264,7 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
         lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
                        _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g,
                        nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, ow,
-                       out_ids, out_d, stats)
+                       out_ids, out_d, stats, _bits_of(planes, nq, ix.dp // 32))
     elif init is not None:
         out_ids[:], out_d[:] = merge_candidates([(init_i, init_d)], R)
     else:
@@ -295,7 +309,7 @@ def bound_seed(ix: OracleIndex, planes, delta, k1, probes, g, R, shard_rank=0, s
     if nq:
         lib().orc_bound_seed(ix.list_off, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp,
                              _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g, nprobe,
-                             R, shard_rank, shard_count, ow, out)
+                             R, shard_rank, shard_count, ow, out, _bits_of(planes, nq, ix.dp // 32))
     return out
 
 
@@ -370,17 +384,20 @@ def assign(X, C) -> np.ndarray:
 
 
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
-           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None):
+           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None, query_bits=4):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 
     seeded (rbq_search_params_t.seeded): -1 scans in two phases (seeded_scan) when the probes
     are split into slices > 1, 0 never, 1 always; exchange=True is the sharded search's
     pipeline (two phases, threshold shared by all shards).  rerank_depth == 0 returns the
-    scan's top-k estimates (the reference behaviour)."""
+    scan's top-k estimates (the reference behaviour).  query_bits 8 (QUANT8) quantises the
+    queries to 8 bits with ix.t8 (set it to query_scale(dp, seed, 7) of the index)."""
     Q = _c(Q, np.float32)
     Qr = rotate(Q, ix.P)
     probes, g = coarse(Qr, ix.c_rot, nprobe)
-    planes, delta, k1, _ = query_prep(Qr, ix.t4)
+    if query_bits == 8 and getattr(ix, "t8", None) is None:
+        raise ValueError("QUANT8 needs the index's 8-bit scale: set ix.t8 = query_scale(dp, seed, 7)")
+    planes, delta, k1, _ = query_prep(Qr, ix.t4 if query_bits == 4 else ix.t8, query_bits)
     R = rerank_depth if rerank_depth > 0 else k
     two = slices > 1 if seeded < 0 else seeded > 0
     if exchange or two:

@@ -331,13 +331,18 @@ void orc_build(const float* X, int64_t n, int D, int Dp, const float* P, const f
   }
 }
 
-// Query preparation (a8 + k1xSumq).  Input: rotated queries [nq, Dp].
-// Outputs: planes [nq, 4, W] (plane b word w, dim 32w+j -> bit 31-j of (code & 0xF) >> b),
-// delta [nq], k1 [nq] (= -0.5 * sum q), codes_out [nq, Dp] int8 (optional).
-void orc_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* planes, float* delta,
+// Query preparation (a8 + k1xSumq) with B = qbits-bit codes (QUANT4: B = 4 and t = t4;
+// QUANT8: B = 8 and t = t8; exrabitq_quantize_query with EX_BITS = num_bits,
+// searcher_gpu_quantize_query.cu:716-723, 774-791).  Input: rotated queries [nq, Dp].
+// Outputs: planes [nq, B, W] (plane b word w, dim 32w+j -> bit 31-j of the B-bit two's
+// complement of code_j, shifted right by b), delta [nq], k1 [nq] (= -0.5 * sum q), codes_out
+// [nq, Dp] int8 (optional).
+void orc_query_prep(const float* Qr, int64_t nq, int Dp, float t4, int qbits, uint32_t* planes, float* delta,
                     float* k1, int8_t* codes_out)
 {
   const int W = Dp / 32;
+  const int hi = (1 << (qbits - 1)) - 1, lo = -(1 << (qbits - 1));
+  const uint32_t mask = (1u << qbits) - 1u;
 #pragma omp parallel
   {
     std::vector<int> code(Dp);
@@ -357,8 +362,8 @@ void orc_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* pla
         float val = x[j] * norm_inv;
         float tv = t4 * val;
         int cv = (int)std::nearbyint(tv);  // round half to even (default FE_TONEAREST)
-        if (cv > 7) cv = 7;
-        if (cv < -8) cv = -8;
+        if (cv > hi) cv = hi;
+        if (cv < lo) cv = lo;
         code[j] = cv;
         ipd += (double)x[j] * (double)cv;
         xs += (long long)cv * cv;
@@ -375,11 +380,11 @@ void orc_query_prep(const float* Qr, int64_t nq, int Dp, float t4, uint32_t* pla
       }
       delta[q] = dl;
       k1[q] = ((float)s1) * -0.5f;
-      uint32_t* pl = planes + (size_t)q * 4 * W;
-      for (int i = 0; i < 4 * W; ++i) pl[i] = 0u;
+      uint32_t* pl = planes + (size_t)q * qbits * W;
+      for (int i = 0; i < qbits * W; ++i) pl[i] = 0u;
       for (int j = 0; j < Dp; ++j) {
-        uint32_t u = (uint32_t)code[j] & 0xFu;
-        for (int b = 0; b < 4; ++b)
+        uint32_t u = (uint32_t)code[j] & mask;
+        for (int b = 0; b < qbits; ++b)
           if ((u >> b) & 1u) pl[b * W + (j >> 5)] |= (1u << (31 - (j & 31)));
       }
       if (codes_out)
@@ -433,15 +438,16 @@ void orc_coarse(const float* Qr, int64_t nq, const float* Cr, int K, int Dp, int
   }
 }
 
-// Signed 4-bit x 1-bit popcount inner product of one vector (a10 phase 1,
-// searcher_gpu_quantize_query.cu:253-262): sum_w sum_{b<3} popc(P_b & c) << b - popc(P_3 & c) << 3.
-int32_t orc_popcount_ip(const uint32_t* planes, const uint32_t* code, int W)
+// Signed B-bit x 1-bit popcount inner product of one vector (a10 phase 1,
+// searcher_gpu_quantize_query.cu:253-262 with NumBits = B = qbits):
+// sum_w sum_{b<B-1} popc(P_b & c) << b - popc(P_{B-1} & c) << (B-1).
+int32_t orc_popcount_ip(const uint32_t* planes, const uint32_t* code, int W, int qbits)
 {
   int32_t acc = 0;
   for (int w = 0; w < W; ++w) {
     uint32_t c = code[w];
-    for (int b = 0; b < 3; ++b) acc += __builtin_popcount(planes[b * W + w] & c) << b;
-    acc -= __builtin_popcount(planes[3 * W + w] & c) << 3;
+    for (int b = 0; b < qbits - 1; ++b) acc += __builtin_popcount(planes[b * W + w] & c) << b;
+    acc -= __builtin_popcount(planes[(qbits - 1) * W + w] & c) << (qbits - 1);
   }
   return acc;
 }
@@ -495,6 +501,7 @@ struct ScanIndex {
   const float* fadd;
   const float* frescale;
   const float* ferr;
+  int qbits;  // query code width (planes per query)
 };
 
 // One slice of one query's probes.  Mirrors the CUDA scan kernel's schedule exactly.
@@ -528,7 +535,7 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
       while (pre[c + 1] <= f) ++c;
       const float g = probe_g[c];
       const int64_t s = ix.list_off[probe_l[c]] + (f - pre[c]);
-      const int32_t acc = orc_popcount_ip(pl, ix.codes + (size_t)s * W, W);
+      const int32_t acc = orc_popcount_ip(pl, ix.codes + (size_t)s * W, W, ix.qbits);
       const float ip = (float)acc * delta;
       const float base_d = ix.fadd[s] + g;
       const float est = base_d + ix.frescale[s] * (ip + k1);
@@ -547,7 +554,7 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
       const float sqrt_g = sqrtf(g);
       const int64_t s = ix.list_off[probe_l[cur]] + (f - pre[cur]);
       const uint32_t* code = ix.codes + (size_t)s * W;
-      int32_t acc = orc_popcount_ip(pl, code, W);
+      int32_t acc = orc_popcount_ip(pl, code, W, ix.qbits);
       float ip = (float)acc * delta;
       float base_d = ix.fadd[s] + g;
       float est = base_d + ix.frescale[s] * (ip + k1);
@@ -582,7 +589,7 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
 void orc_bound_seed(const int64_t* list_off, const uint32_t* codes, const float* fadd, const float* frescale,
                     const float* ferr, int Dp, const uint32_t* planes, const float* delta, const float* k1, int64_t nq,
                     const int32_t* probes, const float* gq, int nprobe, int R, int shard_rank, int shard_count,
-                    const int32_t* owner, float* tau_out)
+                    const int32_t* owner, float* tau_out, int qbits)
 {
   const int W = Dp / 32;
 #pragma omp parallel for schedule(dynamic, 16)
@@ -602,7 +609,7 @@ void orc_bound_seed(const int64_t* list_off, const uint32_t* codes, const float*
       const int l = own_l[i];
       const float g = own_g[i];
       for (int64_t s = list_off[l]; s < list_off[l + 1]; ++s, ++have) {
-        const int32_t acc = orc_popcount_ip(planes + (size_t)q * 4 * W, codes + (size_t)s * W, W);
+        const int32_t acc = orc_popcount_ip(planes + (size_t)q * qbits * W, codes + (size_t)s * W, W, qbits);
         const float ip = (float)acc * delta[q];
         const float est = (fadd[s] + g) + frescale[s] * (ip + k1[q]);
         ub.push_back(make_key(est + ferr[s] * sqrtf(g), (uint32_t)have));
@@ -632,10 +639,10 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
               const float* delta, const float* k1, int64_t nq, const int32_t* probes, const float* gq,
               int nprobe, const float* tau0, const int64_t* init_ids, const float* init_dist, int R, int tile,
               int cap, int prune, int slices, int shard_rank, int shard_count, const int32_t* owner,
-              int64_t* out_ids, float* out_dist, int64_t* stats)
+              int64_t* out_ids, float* out_dist, int64_t* stats, int qbits)
 {
   const int W = Dp / 32;
-  ScanIndex ix{list_off, ids, codes, fadd, frescale, ferr};
+  ScanIndex ix{list_off, ids, codes, fadd, frescale, ferr, qbits};
   int64_t tot[2] = {0, 0};
 #pragma omp parallel
   {
@@ -664,7 +671,7 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
             init.push_back(make_key(init_dist[q * R + r], (uint32_t)init_ids[q * R + r]));
       for (int s = 0; s < slices; ++s) {
         int a = (int)(((int64_t)s * m) / slices), b = (int)(((int64_t)(s + 1) * m) / slices);
-        scan_slice(ix, W, Qr + (size_t)q * Dp, planes + (size_t)q * 4 * W, delta[q], k1[q],
+        scan_slice(ix, W, Qr + (size_t)q * Dp, planes + (size_t)q * qbits * W, delta[q], k1[q],
                    own_l.data() + a, own_g.data() + a, b - a, tau0 ? tau0[q] : INFINITY, s == 0 ? init : none,
                    R, tile, cap, prune, keys, loc);
         all.insert(all.end(), keys.begin(), keys.end());

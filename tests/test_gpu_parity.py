@@ -100,14 +100,14 @@ def test_gpu_assignment_matches_oracle(oracle, case):
     assert np.array_equal(ex["ids"], oix.ids)
 
 
-def _query_stage(idx, Qr_np):
+def _query_stage(idx, Qr_np, bits=4):
     torch = _torch()
     nq, dp = Qr_np.shape
     qr = dev(Qr_np)
-    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device="cuda")
+    planes = torch.empty((nq, bits, dp // 32), dtype=torch.int32, device="cuda")
     delta = torch.empty(nq, dtype=torch.float32, device="cuda")
     k1 = torch.empty(nq, dtype=torch.float32, device="cuda")
-    call("rbq_query_prep", idx.handle, ptr(qr), nq, ptr(planes), ptr(delta), ptr(k1), stream())
+    call("rbq_query_prep", idx.handle, ptr(qr), nq, ptr(planes), ptr(delta), ptr(k1), planes.shape[1], stream())
     return qr, planes, delta, k1
 
 
@@ -152,7 +152,7 @@ def test_popcount_inner_products_and_estimates_bit_exact(oracle, case):
             low = torch.empty(n, dtype=torch.float32, device="cuda")
             g = np.float32(0.37 + 0.01 * l)
             call("rbq_list_estimates", idx.handle, ptr(planes[q]), float(dl[q]), float(kk[q]), float(g), l, ptr(acc),
-                 ptr(est), ptr(low), stream())
+                 ptr(est), ptr(low), 4, stream())
             acc_np, est_np, low_np = acc.cpu().numpy(), est.cpu().numpy(), low.cpu().numpy()
             for v in range(n):
                 s = int(oix.list_off[l]) + v
@@ -163,11 +163,11 @@ def test_popcount_inner_products_and_estimates_bit_exact(oracle, case):
                 assert u32(np.float32(e)) == u32(est_np[v]) and u32(np.float32(lo)) == u32(low_np[v])
 
 
-def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
+def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0, bits=4):
     torch = _torch()
     nq = Q.shape[0]
     Qr = oracle.rotate(Q, oix.P)
-    qr, planes, delta, k1 = _query_stage(idx, Qr)
+    qr, planes, delta, k1 = _query_stage(idx, Qr, bits)
     probes = torch.empty((nq, nprobe), dtype=torch.int32, device="cuda")
     g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
     call("rbq_coarse", idx.handle, ptr(qr), nq, nprobe, 0, ptr(probes), ptr(g), stream())
@@ -175,9 +175,9 @@ def _scan(idx, oracle, oix, Q, nprobe, R, prune, slices, cap=0):
     dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
     stats = torch.zeros(2, dtype=torch.int64, device="cuda")
     call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, 0, None, None, None, R,
-         prune, slices, cap, ptr(ids), ptr(dist), ptr(stats), stream())
+         prune, slices, cap, ptr(ids), ptr(dist), ptr(stats), bits, stream())
     p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
-    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
+    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4 if bits == 4 else oracle.query_scale(oix.dp, 7, 7), bits)
     cap_o = oracle.default_cap(R, cap)
     oi, od, ost = oracle.scan(oix, Qr, pl2, d2, k2, p2, g2, R, oracle.SCAN_TILE, cap_o, prune, slices, with_stats=True)
     return ids.cpu().numpy(), dist.cpu().numpy(), stats.cpu().numpy(), oi, od, ost
@@ -428,7 +428,7 @@ def test_scan_from_a_seeded_threshold(oracle, case):
             dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
             init = (ptr(ti), ptr(td)) if with_init else (None, None)
             call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(pb), ptr(gb),
-                 nprobe - 1, nprobe, ptr(t0), *init, R, 1, slices, 0, ptr(ids), ptr(dist), None, stream())
+                 nprobe - 1, nprobe, ptr(t0), *init, R, 1, slices, 0, ptr(ids), ptr(dist), None, 4, stream())
             oi, od = oracle.scan(oix, Qr, pl2, d2, k2, p2[:, 1:], g2[:, 1:], R, prune=1, slices=slices, tau0=tau,
                                  init=(ai, ad) if with_init else None)
             assert np.array_equal(ids.cpu().numpy(), oi)
@@ -507,7 +507,7 @@ def test_bound_seed_matches_oracle(oracle, case, nprobe, R):
     pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4)
     tau = torch.empty(nq, dtype=torch.float32, device="cuda")
     call("rbq_bound_seed", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, P,
-         R, 0, ptr(tau), stream())
+         R, 0, ptr(tau), 4, stream())
     want = oracle.bound_seed(oix, pl2, d2, k2, p2[:, :nprobe], g2[:, :nprobe], R)
     got = tau.cpu().numpy()
     assert np.array_equal(u32(got), u32(want))
@@ -634,3 +634,66 @@ def test_search_is_deterministic_run_to_run():
         a = idx.search(Q, 10)
         b = idx.search(Q, 10)
         assert np.array_equal(a[1], b[1]) and np.array_equal(u32(a[0]), u32(b[0]))
+
+
+
+# ---- QUANT8 (search_mode::QUANT8: 8-bit query codes, scale t8 = best rescale for 7 extra bits)
+def test_quant8_query_planes_bit_exact(oracle, case):
+    idx, oix, X, Q, C, lab = case
+    Qr = oracle.rotate(Q, oix.P)
+    _, planes, delta, k1 = _query_stage(idx, Qr, 8)
+    p2, d2, k2, codes = oracle.query_prep(Qr, oracle.query_scale(128, 7, 7), 8)
+    assert planes.shape[1] == 8 and np.array_equal(u32(planes.cpu().numpy()), p2)
+    assert np.array_equal(u32(delta.cpu().numpy()), u32(d2)) and np.array_equal(u32(k1.cpu().numpy()), u32(k2))
+    assert codes.min() < -8 or codes.max() > 7  # the 8-bit range is used
+
+
+@pytest.mark.parametrize("prune,slices,R", [(1, 1, 40), (0, 1, 40), (1, 4, 40), (1, 1, 100)])
+def test_quant8_scan_candidates_bit_exact(oracle, case, prune, slices, R):
+    idx, oix, X, Q, C, lab = case
+    gi, gd, gst, oi, od, ost = _scan(idx, oracle, oix, Q, 8, R, prune, slices, 0, bits=8)
+    assert np.array_equal(gi, oi) and np.array_equal(u32(gd), u32(od))
+    assert gst.tolist() == ost.tolist()
+
+
+@pytest.mark.parametrize("nprobe,R,seeded", [(8, 40, -1), (16, 40, 1), (4, 0, 0)])
+def test_quant8_search_end_to_end(oracle, case, nprobe, R, seeded):
+    idx, oix, X, Q, C, lab = case
+    oix.t8 = oracle.query_scale(128, 7, 7)
+    idx.nprobe, idx.k_rerank, idx.prune, idx.seeded, idx.query_bits = nprobe, R, True, seeded, 8
+    try:
+        d, i = idx.search(Q, 10)
+    finally:
+        idx.query_bits, idx.seeded = 4, -1
+    d2, i2 = oracle.search(oix, Q, 10, nprobe, R, prune=1, seeded=seeded, query_bits=8)
+    assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    if R:
+        d4, i4 = oracle.search(oix, Q, 10, nprobe, R, prune=1, seeded=seeded)
+        _, gt = oracle.knn_exact(X, Q, 10)
+        assert oracle.recall(i, gt) >= oracle.recall(i4, gt) - 0.02
+
+
+def test_quant8_stage_ops_compose_to_the_search(case):
+    torch = _torch()
+    idx, oix, X, Q, C, lab = case
+    h, P, R, k = idx.handle.value, 8, 40, 10
+    q = dev(Q)
+    ops = torch.ops.rbq
+    qr = ops.rotate(h, q)
+    probes, g = ops.coarse(h, qr, P, 0)
+    planes, delta, k1 = ops.query_prep(h, qr, 8)
+    cand, _ = ops.scan(h, qr, planes, delta, k1, probes, g, R, True, 1, 0, None)
+    d, i = ops.rerank(h, q, cand, k)
+    d2, i2 = ops.search(h, q, k, P, R, True, 1, 0, 8)
+    torch.cuda.synchronize()
+    assert torch.equal(i, i2) and np.array_equal(u32(d.cpu().numpy()), u32(d2.cpu().numpy()))
+
+
+def test_query_bits_are_checked(case):
+    idx, oix, X, Q, C, lab = case
+    idx.query_bits = 5
+    try:
+        with pytest.raises(RuntimeError, match="QUANT4.*QUANT8"):
+            idx.search(Q[:3], 5)
+    finally:
+        idx.query_bits = 4

@@ -138,3 +138,9 @@ def test_cli_gpus_relaunches_through_torchrun():
     assert "--nproc-per-node=4" in cmd and "--master-addr=127.0.0.1" in cmd and "--master-port=29555" in cmd
     assert cmd[cmd.index("-m", 3):][:2] == ["-m", "neurosamble_b200.cli"] and cmd[-2:] == ["--gpus", "4"]
     assert cli.check_args(cli.parse_args(["--emb", "x", "--n", "1", "--gpus", "0"])) == "--gpus must be >= 1"
+
+
+def test_cli_accepts_quant8():
+    from neurosamble_b200 import cli
+    assert cli.check_args(cli.parse_args(["--emb", "x.f16", "--n", "10", "--search_mode", "QUANT8"])) == ""
+    assert "QUANT8" in cli.check_args(cli.parse_args(["--emb", "x.f16", "--n", "10", "--search_mode", "LUT32"]))

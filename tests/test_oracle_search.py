@@ -246,3 +246,46 @@ def test_balanced_kmeans_pieces(oracle):
     w = np.float32(1)
     assert np.array_equal(C3[1], (np.float32(0) + w * C[0] + np.float32(1) * X[i1]) / (w + np.float32(1)))
     assert np.array_equal(C3[2], X[i2])
+
+
+
+def test_quant8_planes_reconstruct_codes_and_tighten_the_estimate(oracle, small):
+    """8-bit query codes (QUANT8): within [-128, 127], their two's-complement planes rebuild
+    them, the popcount inner product equals sum code_j * bit_j, and acc * delta tracks the
+    exact <q, bits> more closely than the 4-bit codes do."""
+    ix = small[0]
+    rng = np.random.default_rng(5)
+    Q = rng.standard_normal((40, ix.d)).astype(np.float32)
+    Qr = oracle.rotate(Q, ix.P)
+    t8 = oracle.query_scale(ix.dp, 11, 7)
+    p8, d8, k8, c8 = oracle.query_prep(Qr, t8, 8)
+    p4, d4, k4, c4 = oracle.query_prep(Qr, ix.t4, 4)
+    assert p8.shape[1] == 8 and c8.min() >= -128 and c8.max() <= 127 and np.abs(c8).max() > 7
+    assert np.array_equal(k8, k4)
+    w = ix.dp // 32
+    bit = ((p8[:, :, :, None] >> (31 - np.arange(32, dtype=np.uint32))) & 1).transpose(0, 2, 3, 1)
+    bit = bit.reshape(Q.shape[0], ix.dp, 8).astype(np.int64)
+    rebuilt = (bit[:, :, :7] << np.arange(7)).sum(-1) - (bit[:, :, 7] << 7)
+    assert np.array_equal(rebuilt, c8.astype(np.int64))
+    err4 = err8 = 0.0
+    for q in range(Q.shape[0]):
+        for s in range(0, ix.codes.shape[0], 97):
+            code = ix.codes[s]
+            bits = ((code[:, None] >> (31 - np.arange(32, dtype=np.uint32))) & 1).reshape(-1).astype(np.int64)
+            a8 = oracle.popcount_ip(p8[q], code)
+            assert a8 == int((c8[q].astype(np.int64) * bits).sum())
+            exact = float((Qr[q].astype(np.float64) * bits).sum())
+            err8 += abs(a8 * float(d8[q]) - exact)
+            err4 += abs(oracle.popcount_ip(p4[q], code) * float(d4[q]) - exact)
+    assert err8 < 0.25 * err4
+
+
+def test_query_scale_8bit_matches_the_library(oracle):
+    """t8 (const_scaling_factor_8bit, best rescale with 7 extra bits) from the library's host
+    math equals the oracle's restatement bit for bit."""
+    import ctypes
+    from neurosamble_b200 import _lib
+    for dp in (32, 128, 256):
+        t = ctypes.c_float()
+        assert _lib.lib().rbq_query_scale(dp, 7, 7, ctypes.byref(t)) == 0
+        assert np.float32(t.value).view(np.uint32) == np.float32(oracle.query_scale(dp, 7, 7)).view(np.uint32)

@@ -37,7 +37,7 @@ def test_size_rule_rejects_before_touching_the_index():
     buf = ctypes.c_void_p(1)
     nq, R = 9000, 512  # 9000 * 512 * 8 bytes > 32 MiB
     st = L.rbq_scan_noalloc(dummy, buf, buf, buf, buf, nq, buf, buf, 8, 0, None, R, 1, 1, 0, buf, buf, None,
-                            None)
+                            4, None)
     assert st == 1
     msg = L.rbq_last_error().decode()
     assert "static scratch holds 33554432 bytes" in msg
@@ -58,7 +58,7 @@ def _stage(idx, Q, nprobe):
     g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
     _lib.call("rbq_rotate", idx.handle, _p(q), nq, _p(qr), s)
     _lib.call("rbq_coarse", idx.handle, _p(qr), nq, nprobe, 0, _p(probes), _p(g), s)
-    _lib.call("rbq_query_prep", idx.handle, _p(qr), nq, _p(planes), _p(delta), _p(k1), s)
+    _lib.call("rbq_query_prep", idx.handle, _p(qr), nq, _p(planes), _p(delta), _p(k1), 4, s)
     return qr, planes, delta, k1, probes, g
 
 
@@ -73,7 +73,7 @@ def _run(idx, name, st, nprobe, R, prune, slices):
     stats = torch.zeros(2, dtype=torch.int64, device="cuda")
     init = (None, None) if name == "rbq_scan" else ()  # rbq_scan's initial candidates: none
     _lib.call(name, idx.handle, _p(qr), _p(planes), _p(delta), _p(k1), nq, _p(probes), _p(g), nprobe, 0, None, *init, R,
-              prune, slices, 0, _p(ids), _p(dist), _p(stats), _stream_ptr(idx.device))
+              prune, slices, 0, _p(ids), _p(dist), _p(stats), 4, _stream_ptr(idx.device))
     torch.cuda.synchronize()
     return ids.cpu().numpy(), dist.cpu().numpy(), stats.cpu().numpy()
 
@@ -116,6 +116,6 @@ def test_noalloc_scan_refuses_batches_beyond_the_scratch():
     ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
     dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
     st = _lib.lib().rbq_scan_noalloc(idx.handle, _p(qr), _p(planes), _p(delta), _p(k1), nq, _p(probes), _p(g),
-                                     nprobe, 0, None, R, 1, 1, 0, _p(ids), _p(dist), None,
+                                     nprobe, 0, None, R, 1, 1, 0, _p(ids), _p(dist), None, 4,
                                      _stream_ptr(idx.device))
     assert st == 1 and b"static scratch" in _lib.lib().rbq_last_error()
