@@ -216,11 +216,11 @@ def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
     """Time the oracle search on a bounded query sample sized to ~budget_s of CPU work."""
     probe = min(len(Q), 200)
     t0 = time.perf_counter()
-    O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R)
+    O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"])
     per_q = (time.perf_counter() - t0) / probe
     n = int(min(len(Q), max(probe, budget_s / max(per_q, 1e-9))))
     t0 = time.perf_counter()
-    d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R)
+    d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"])
     dt = time.perf_counter() - t0
     return n / dt, n, dt, i
 
@@ -240,6 +240,7 @@ def run_reference(args, cfg):
     lab = np.concatenate([np.argmin(cn - 2.0 * X[a:a + 65536] @ C.T, axis=1)
                           for a in range(0, cfg["n"], 65536)]).astype(np.uint32)
     oix = O.build(X, C, lab, P, t4)
+    oix.t8 = O.query_scale(dp, 7, 7)
     log(f"[reference] build {time.perf_counter() - t:.1f}s, threads={O.threads()}")
     # the same recall rule as our arm: the smallest rerank depth on the ladder whose recall@k
     # reaches the target, measured here on a 500-query sample against exact neighbours
@@ -253,7 +254,7 @@ def run_reference(args, cfg):
                              for a in range(0, ns, 100)])
         R = RERANK_LADDER[-1]
         for cand in RERANK_LADDER:
-            _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand)
+            _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand, query_bits=cfg["query_bits"])
             recalls[cand] = O.recall(ids, gt)
             if recalls[cand] >= RECALL_TARGET:
                 R = cand
@@ -295,7 +296,7 @@ def workload(cfg, R, kmeans):
                          f"codes, 4-bit queries" + ("; data generated on the device" if cfg["device_data"] else "")),
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
             "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
-            "kmeans": kmeans}
+            "kmeans": kmeans, "search_mode": "QUANT8" if cfg.get("query_bits", 4) == 8 else "QUANT4"}
 
 
 # --------------------------------------------------------------------------------------
@@ -346,6 +347,7 @@ def run_ours(args, cfg):
     log(f"[rank {rank}] build {time.perf_counter() - t:.1f}s, local vectors {local_ix.info().n_local}")
     index.nprobe = cfg["nprobe"]
     index.prune = True
+    index.query_bits = cfg["query_bits"]
     if world == 1:
         index.seeded = args.seeded
 
@@ -544,14 +546,15 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     dp = info.padded_dim
     h, st = ix.handle, _stream_ptr(dev.index)
     qr = torch.empty((nq, dp), dtype=torch.float32, device=dev)
-    planes = torch.empty((nq, 4, dp // 32), dtype=torch.int32, device=dev)
+    qb = cfg["query_bits"]
+    planes = torch.empty((nq, qb, dp // 32), dtype=torch.int32, device=dev)
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     probes = torch.empty((nq, P), dtype=torch.int32, device=dev)
     g = torch.empty((nq, P), dtype=torch.float32, device=dev)
     _lib.call("rbq_rotate", h, _ptr(Qd), nq, _ptr(qr), st)
     _lib.call("rbq_coarse", h, _ptr(qr), nq, P, 0, _ptr(probes), _ptr(g), st)
-    _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), 4, st)
+    _lib.call("rbq_query_prep", h, _ptr(qr), nq, _ptr(planes), _ptr(delta), _ptr(k1), qb, st)
     torch.cuda.synchronize(dev)
     sizes = np.diff(ix.list_offsets())
     pr = probes.cpu().numpy()
@@ -578,7 +581,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
         _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pp), _ptr(gg), npr,
                   pp.stride(0), _ptr(tau) if tau is not None else None, _ptr(init[0]) if init else None,
                   _ptr(init[1]) if init else None, R, 1, 1, 0, _ptr(ids_t), _ptr(dist_t),
-                  _ptr(stats_t) if stats_t is not None else None, 4, st)
+                  _ptr(stats_t) if stats_t is not None else None, qb, st)
 
     ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
     dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
@@ -641,6 +644,7 @@ def cpu_baseline(ix, X, Q, cfg, R):
     # the oracle's index arrays are the GPU index's own (same layout, same bytes)
     oix = O.OracleIndex(cfg["d"], info.padded_dim, cfg["nlist"], ex["list_off"], ex["ids"], ex["codes"], ex["fadd"],
                         ex["frescale"], ex["ferr"], Cr, ix.rotation(), ix.query_scale, X)
+    oix.t8 = O.query_scale(info.padded_dim, int(info.seed), 7)
     qps, n_s, dt, _ = cpu_search_timed(O, oix, Q, cfg, R, budget_s=15.0)
     return {"value": round(qps, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
             "sample": f"{n_s} of {cfg['nq']} queries ({dt:.1f}s), same index bytes and parameters"}
@@ -659,6 +663,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the B = 1 / 64 / 1024 sweep")
     ap.add_argument("--kmeans", default="balanced", choices=["balanced", "lloyd"],
                     help="coarse trainer of both arms (balanced: the reference's build algorithm)")
+    ap.add_argument("--query-bits", type=int, default=4, choices=[4, 8],
+                    help="query code width of both arms: 4 (QUANT4, the reference CLI's default) or 8 (QUANT8)")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
                     help="BASELINE configuration (2: the metric's; 4 / 5: supplementary, data on the device)")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
@@ -667,6 +673,7 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     cfg = dict(CONFIGS[args.config])
+    cfg["query_bits"] = args.query_bits
     if args.n:
         cfg["n"] = args.n
     if args.nq:
