@@ -85,6 +85,11 @@ typedef struct {
                          /* slices), 0 = off (each slice seeds itself), 1 = on                  */
   int32_t query_bits;    /* query code width: 4 = QUANT4 (default; 0 means 4), 8 = QUANT8       */
                          /* (search_mode, ivf_rabitq.hpp:111-120; ivf_rabitq.cu:313-345)        */
+  int32_t graph;         /* 1: the first search of a batch size (and these parameters) is       */
+                         /* captured as a CUDA graph and later ones replay it: copy in, one     */
+                         /* graph launch, copy out (small batches are launch-bound).  Up to 8   */
+                         /* graphs per index; adding, training or setting centroids drops them. */
+                         /* 0 (default): launch the kernels one by one.                         */
 } rbq_search_params_t;
 
 typedef struct {

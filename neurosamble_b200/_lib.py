@@ -26,7 +26,8 @@ class IndexParams(ctypes.Structure):
 class SearchParams(ctypes.Structure):
     _fields_ = [("n_probes", ctypes.c_int32), ("k", ctypes.c_int32), ("rerank", ctypes.c_int32),
                 ("prune", ctypes.c_int32), ("probe_split", ctypes.c_int32), ("cand_cap", ctypes.c_int32),
-                ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32), ("query_bits", ctypes.c_int32)]
+                ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32), ("query_bits", ctypes.c_int32),
+                ("graph", ctypes.c_int32)]
 
 
 class IndexInfo(ctypes.Structure):

@@ -158,6 +158,7 @@ void dev_grow(T*& p, size_t keep, size_t count)
 
 void install_centroids(Index& ix, cudaStream_t s)
 {
+  drop_graphs(ix);
   dev_free(ix.C);
   dev_free(ix.C_rot);
   dev_free(ix.C_rot_n2);
@@ -215,6 +216,7 @@ void counting_sort(const std::vector<uint32_t>& lab, int K, std::vector<int64_t>
 // Rebuild slot-order arrays from the row-order storage.
 void relayout(Index& ix, cudaStream_t s)
 {
+  drop_graphs(ix);
   std::vector<uint32_t> lab(ix.n_rows);
   if (ix.n_rows)
     RBQ_CUDA(cudaMemcpyAsync(lab.data(), ix.labels_r, ix.n_rows * 4, cudaMemcpyDeviceToHost, s));
@@ -764,6 +766,61 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   }
 }
 
+// The captured search of batch size nq and parameters p (p.graph ignored): found in the
+// index's cache or captured now.  The capture runs run_search on a private stream into the
+// graph's own buffers, so its scratch allocations become graph allocation / free nodes and
+// every replay allocates and frees its own.
+Index::SearchGraph& search_graph(Index& ix, const rbq_search_params_t& params, int64_t nq)
+{
+  rbq_search_params_t key = params;
+  key.graph = 0;
+  for (auto& g : ix.graphs)
+    if (g.nq == nq && std::memcmp(&g.p, &key, sizeof key) == 0) return g;
+  plan_search(ix, key, nq);  // argument errors before any allocation
+  if (ix.graphs.size() >= 8) {
+    Index::SearchGraph& old = ix.graphs.front();
+    if (old.exec) cudaGraphExecDestroy(old.exec);
+    dev_free(old.q);
+    dev_free(old.d);
+    dev_free(old.i);
+    ix.graphs.erase(ix.graphs.begin());
+  }
+  Index::SearchGraph g;
+  g.nq = nq;
+  g.p = key;
+  cudaStream_t cs = nullptr;
+  cudaGraph_t graph = nullptr;
+  try {
+    g.q = dev_alloc<float>((size_t)nq * ix.D);
+    g.d = dev_alloc<float>((size_t)nq * key.k);
+    g.i = dev_alloc<int64_t>((size_t)nq * key.k);
+    RBQ_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    RBQ_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
+    try {
+      run_search(ix, key, g.q, nq, g.d, g.i, cs, nullptr);
+    } catch (...) {
+      cudaStreamEndCapture(cs, &graph);
+      throw;
+    }
+    RBQ_CUDA(cudaStreamEndCapture(cs, &graph));
+    RBQ_CUDA(cudaGraphInstantiate(&g.exec, graph, 0));
+    cudaGraphDestroy(graph);
+    graph = nullptr;
+    cudaStreamDestroy(cs);
+    cs = nullptr;
+  } catch (...) {
+    if (graph) cudaGraphDestroy(graph);
+    if (cs) cudaStreamDestroy(cs);
+    cudaGetLastError();
+    dev_free(g.q);
+    dev_free(g.d);
+    dev_free(g.i);
+    throw;
+  }
+  ix.graphs.push_back(g);
+  return ix.graphs.back();
+}
+
 // ---------------------------------------------------------------------------------------
 // Persistence: "RBQB200\0", version, dims, seed, t4, P, C, then this shard's rows.
 // ---------------------------------------------------------------------------------------
@@ -892,8 +949,20 @@ void install_owners(Index& ix, const std::vector<int32_t>& owners, bool fixed)
   ix.owners_fixed = fixed;
 }
 
+void drop_graphs(Index& ix)
+{
+  for (auto& g : ix.graphs) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    dev_free(g.q);
+    dev_free(g.d);
+    dev_free(g.i);
+  }
+  ix.graphs.clear();
+}
+
 void free_index_memory(Index& ix)
 {
+  drop_graphs(ix);
   dev_free(ix.P);
   dev_free(ix.C);
   dev_free(ix.C_rot);
@@ -1149,7 +1218,17 @@ int rbq_search(rbq_index_t* index, const rbq_search_params_t* params, const floa
     RBQ_CHECK(index && params, RBQ_ERR_INVALID, "null argument");
     RBQ_CHECK(nq == 0 || (Q_dev && dist_dev && ids_dev), RBQ_ERR_INVALID, "null buffer");
     DeviceGuard dg(index->ix.device);
-    run_search(index->ix, *params, Q_dev, nq, dist_dev, ids_dev, as_stream(stream), nullptr);
+    Index& ix = index->ix;
+    cudaStream_t s = as_stream(stream);
+    if (params->graph && nq > 0) {
+      Index::SearchGraph& g = search_graph(ix, *params, nq);
+      RBQ_CUDA(cudaMemcpyAsync(g.q, Q_dev, (size_t)nq * ix.D * 4, cudaMemcpyDeviceToDevice, s));
+      RBQ_CUDA(cudaGraphLaunch(g.exec, s));
+      RBQ_CUDA(cudaMemcpyAsync(dist_dev, g.d, (size_t)nq * params->k * 4, cudaMemcpyDeviceToDevice, s));
+      RBQ_CUDA(cudaMemcpyAsync(ids_dev, g.i, (size_t)nq * params->k * 8, cudaMemcpyDeviceToDevice, s));
+      return;
+    }
+    run_search(ix, *params, Q_dev, nq, dist_dev, ids_dev, s, nullptr);
   });
 }
 
@@ -1170,42 +1249,50 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
     // rotated while the second crosses PCIe, then the whole batch is searched at once (the same
     // plan and results as a device-side search of the batch).
     constexpr int64_t kMinHalf = 2048;
-    Scratch sc(s);
-    float* q = sc.get<float>((size_t)nq * ix.D);
-    float* d = sc.get<float>((size_t)nq * k);
-    int64_t* i = sc.get<int64_t>((size_t)nq * k);
-    if (nq < 2 * kMinHalf) {
-      RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
-      run_search(ix, *params, q, nq, d, i, s, nullptr);
+    if (params->graph) {  // the captured search reads and writes its own buffers
+      Index::SearchGraph& g = search_graph(ix, *params, nq);
+      RBQ_CUDA(cudaMemcpyAsync(g.q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
+      RBQ_CUDA(cudaGraphLaunch(g.exec, s));
+      RBQ_CUDA(cudaMemcpyAsync(dist_host, g.d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
+      RBQ_CUDA(cudaMemcpyAsync(ids_host, g.i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
     } else {
-      if (!ix.copy_stream) RBQ_CUDA(cudaStreamCreateWithFlags(&ix.copy_stream, cudaStreamNonBlocking));
-      cudaStream_t cs = ix.copy_stream;
-      float* qr = sc.get<float>((size_t)nq * ix.Dp);
-      cudaEvent_t ev[3];
-      for (auto& e : ev) RBQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-      try {
-        const int64_t h = nq / 2;
-        RBQ_CUDA(cudaEventRecord(ev[0], s));  // the scratch buffers exist on s
-        RBQ_CUDA(cudaStreamWaitEvent(cs, ev[0], 0));
-        RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)h * ix.D * 4, cudaMemcpyHostToDevice, cs));
-        RBQ_CUDA(cudaEventRecord(ev[1], cs));
-        RBQ_CUDA(cudaMemcpyAsync(q + h * ix.D, Q_host + h * ix.D, (size_t)(nq - h) * ix.D * 4,
-                                 cudaMemcpyHostToDevice, cs));
-        RBQ_CUDA(cudaEventRecord(ev[2], cs));
-        RBQ_CUDA(cudaStreamWaitEvent(s, ev[1], 0));
-        launch_rotate(q, h, ix.D, ix.Dp, ix.P, qr, s);
-        RBQ_CUDA(cudaStreamWaitEvent(s, ev[2], 0));
-        launch_rotate(q + h * ix.D, nq - h, ix.D, ix.Dp, ix.P, qr + h * ix.Dp, s);
-        run_search(ix, *params, q, nq, d, i, s, nullptr, qr);
-      } catch (...) {
-        cudaStreamSynchronize(cs);
-        for (auto& e : ev) cudaEventDestroy(e);
-        throw;
+      Scratch sc(s);
+      float* q = sc.get<float>((size_t)nq * ix.D);
+      float* d = sc.get<float>((size_t)nq * k);
+      int64_t* i = sc.get<int64_t>((size_t)nq * k);
+      if (nq < 2 * kMinHalf) {
+        RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
+        run_search(ix, *params, q, nq, d, i, s, nullptr);
+      } else {
+        if (!ix.copy_stream) RBQ_CUDA(cudaStreamCreateWithFlags(&ix.copy_stream, cudaStreamNonBlocking));
+        cudaStream_t cs = ix.copy_stream;
+        float* qr = sc.get<float>((size_t)nq * ix.Dp);
+        cudaEvent_t ev[3];
+        for (auto& e : ev) RBQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        try {
+          const int64_t h = nq / 2;
+          RBQ_CUDA(cudaEventRecord(ev[0], s));  // the scratch buffers exist on s
+          RBQ_CUDA(cudaStreamWaitEvent(cs, ev[0], 0));
+          RBQ_CUDA(cudaMemcpyAsync(q, Q_host, (size_t)h * ix.D * 4, cudaMemcpyHostToDevice, cs));
+          RBQ_CUDA(cudaEventRecord(ev[1], cs));
+          RBQ_CUDA(cudaMemcpyAsync(q + h * ix.D, Q_host + h * ix.D, (size_t)(nq - h) * ix.D * 4,
+                                   cudaMemcpyHostToDevice, cs));
+          RBQ_CUDA(cudaEventRecord(ev[2], cs));
+          RBQ_CUDA(cudaStreamWaitEvent(s, ev[1], 0));
+          launch_rotate(q, h, ix.D, ix.Dp, ix.P, qr, s);
+          RBQ_CUDA(cudaStreamWaitEvent(s, ev[2], 0));
+          launch_rotate(q + h * ix.D, nq - h, ix.D, ix.Dp, ix.P, qr + h * ix.Dp, s);
+          run_search(ix, *params, q, nq, d, i, s, nullptr, qr);
+        } catch (...) {
+          cudaStreamSynchronize(cs);
+          for (auto& e : ev) cudaEventDestroy(e);
+          throw;
+        }
+        for (auto& e : ev) RBQ_CUDA(cudaEventDestroy(e));
       }
-      for (auto& e : ev) RBQ_CUDA(cudaEventDestroy(e));
+      RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
+      RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
     }
-    RBQ_CUDA(cudaMemcpyAsync(dist_host, d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
-    RBQ_CUDA(cudaMemcpyAsync(ids_host, i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
     int code = 0;
     RBQ_CUDA(cudaMemcpyAsync(&code, ix.dev_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RBQ_CUDA(cudaStreamSynchronize(s));

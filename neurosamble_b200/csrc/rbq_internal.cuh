@@ -127,6 +127,19 @@ struct Index {
   int32_t* owner = nullptr;      // [K] device copy of owner_host
   cudaStream_t copy_stream = nullptr;  // host-buffer searches: uploads / downloads beside compute
 
+  // Searches captured as CUDA graphs (rbq_search_params_t.graph): one per batch size and search
+  // parameters, reading and writing their own device buffers; dropped whenever the index's
+  // arrays change (add, train, set_centroids, free).
+  struct SearchGraph {
+    int64_t nq = 0;
+    rbq_search_params_t p{};
+    cudaGraphExec_t exec = nullptr;
+    float* q = nullptr;
+    float* d = nullptr;
+    int64_t* i = nullptr;
+  };
+  std::vector<SearchGraph> graphs;
+
   // Slot order (rebuilt after every add): list l owns slots [list_off[l], list_off[l+1]).
   int64_t* list_off = nullptr;   // [K+1]
   uint32_t* ids = nullptr;       // [n_rows] global ids
@@ -137,6 +150,8 @@ struct Index {
 };
 
 void free_index_memory(Index& ix);
+// Destroys the index's captured search graphs (their pointers into the index go stale).
+void drop_graphs(Index& ix);
 // The list -> rank map of a policy for list sizes `sizes` (ROUND_ROBIN ignores them).
 std::vector<int32_t> list_owners(int policy, const std::vector<int64_t>& sizes, int count);
 // Uploads the map (allocating the device copy on first use); fixed = final for later adds.

@@ -46,7 +46,8 @@ class IndexIVFRaBitQ:
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
     scan slices start from the nearest list's bound seed: -1 = auto, on when the probes are split;
-    0 off; 1 on), ``query_bits`` (4: QUANT4, the reference CLI's default; 8: QUANT8).
+    0 off; 1 on), ``query_bits`` (4: QUANT4, the reference CLI's default; 8: QUANT8),
+    ``use_graph`` (replay each batch size's search from a captured CUDA graph; small batches).
     """
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
@@ -66,6 +67,7 @@ class IndexIVFRaBitQ:
         self.coarse_margin = 0
         self.seeded = -1
         self.query_bits = 4
+        self.use_graph = False
         self._h = ctypes.c_void_p()
         if _handle is not None:
             self._h = _handle
@@ -184,6 +186,7 @@ class IndexIVFRaBitQ:
         sp.cand_cap, sp.coarse_margin = int(self.cand_cap), int(self.coarse_margin)
         sp.seeded = int(self.seeded)
         sp.query_bits = int(self.query_bits)
+        sp.graph = int(bool(self.use_graph))
         return sp
 
     def search(self, x, k: int):

@@ -697,3 +697,52 @@ def test_query_bits_are_checked(case):
             idx.search(Q[:3], 5)
     finally:
         idx.query_bits = 4
+
+
+def test_graph_search_replays_bit_exact(case):
+    """use_graph: the first search of a batch size is captured as a CUDA graph, later ones
+    replay it (new inputs copied in, results copied out); a replay launches no kernel of its
+    own and returns the bits of a plain search, on the device and the host-buffer paths."""
+    import ctypes
+    torch = _torch()
+    from neurosamble_b200 import _lib
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune, idx.seeded = 8, 40, True, -1
+    L = _lib.lib()
+    try:
+        for B in (1, 7, 64):
+            idx.use_graph = False
+            want = [idx.search(Q[a:a + B], 10) for a in (0, B, 2 * B)]
+            idx.use_graph = True
+            got = [idx.search(Q[a:a + B], 10) for a in (0, B, 2 * B)]
+            for (d0, i0), (d1, i1) in zip(want, got):
+                assert np.array_equal(i0, i1) and np.array_equal(u32(d0), u32(d1))
+            n0 = L.rbq_kernel_launches()
+            d2, i2 = idx.search(Q[B:2 * B], 10)
+            assert L.rbq_kernel_launches() == n0  # a replay: no kernels launched one by one
+            assert np.array_equal(i2, want[1][1])
+            sp = idx.search_params(10)
+            dh = np.empty((B, 10), np.float32)
+            ih = np.empty((B, 10), np.int64)
+            qh = np.ascontiguousarray(Q[2 * B:3 * B])
+            call("rbq_search_host", idx.handle, ctypes.byref(sp), qh.ctypes.data_as(ctypes.c_void_p), B,
+                 dh.ctypes.data_as(ctypes.c_void_p), ih.ctypes.data_as(ctypes.c_void_p), stream())
+            assert np.array_equal(ih, want[2][1]) and np.array_equal(u32(dh), u32(want[2][0]))
+    finally:
+        idx.use_graph = False
+    torch.cuda.synchronize()
+
+
+def test_graphs_are_dropped_when_the_index_changes(oracle):
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(8000, 64, 30, 0.3, 16, seed=15)
+    idx = IndexIVFRaBitQ(64, 16, seed=4, kmeans_iters=3)
+    idx.build(X[:5000])
+    idx.nprobe, idx.k_rerank, idx.use_graph = 4, 20, True
+    d1, i1 = idx.search(Q, 5)
+    idx.add(X[5000:])  # reallocates the lists: the captured search must not be replayed
+    d2, i2 = idx.search(Q, 5)
+    idx.use_graph = False
+    d3, i3 = idx.search(Q, 5)
+    assert np.array_equal(i2, i3) and np.array_equal(u32(d2), u32(d3))
+    assert (i3 >= 5000).any() and not (i1 >= 5000).any()
