@@ -289,3 +289,13 @@ def test_query_scale_8bit_matches_the_library(oracle):
         t = ctypes.c_float()
         assert _lib.lib().rbq_query_scale(dp, 7, 7, ctypes.byref(t)) == 0
         assert np.float32(t.value).view(np.uint32) == np.float32(oracle.query_scale(dp, 7, 7)).view(np.uint32)
+
+
+@pytest.mark.parametrize("n,K,iters", [(50, 1, 5), (16, 16, 5), (17, 16, 3), (100, 99, 2), (300, 40, 0), (1000, 3, 20)])
+def test_balanced_kmeans_edge_cases(oracle, n, K, iters):
+    """One list, as many lists as rows, zero iterations, mesoclusters with fewer rows than
+    their share of fine clusters: finite centres, every list non-empty."""
+    X = np.random.default_rng(n * K).standard_normal((n, 8)).astype(np.float32)
+    C = oracle.kmeans_balanced(X, K, iters)
+    assert C.shape == (K, 8) and np.isfinite(C).all()
+    assert (np.bincount(oracle.assign(X, C), minlength=K) > 0).all()
