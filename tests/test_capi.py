@@ -87,3 +87,15 @@ def test_product_has_no_oracle_dependency():
             if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
                 text = open(os.path.join(dirpath, f), errors="ignore").read()
                 assert "oracle" not in re.sub(r"(#|//).*", "", text).lower() or f == "build_ext.py", f
+
+
+def test_parameter_defaults():
+    """Host-only: the defaults a C caller gets (reference defaults where one exists)."""
+    L = _lib.lib()
+    ip = _lib.IndexParams()
+    L.rbq_index_params_default(ctypes.byref(ip))
+    assert (ip.n_lists, ip.seed, ip.kmeans_n_iters, ip.max_train_points_per_cluster) == (1024, 7, 20, 256)
+    assert (ip.shard_count, ip.shard_policy, ip.kmeans_kind) == (1, 0, 0)  # round robin, balanced k-means
+    sp = _lib.SearchParams()
+    L.rbq_search_params_default(ctypes.byref(sp))
+    assert (sp.n_probes, sp.k, sp.rerank, sp.prune, sp.seeded, sp.query_bits, sp.graph) == (20, 10, 0, 1, -1, 4, 0)

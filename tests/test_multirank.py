@@ -124,7 +124,8 @@ class _OracleStages:
 
     def prep(self, qr, planes, delta, k1):
         import torch
-        pl, de, kk, _ = self.O.query_prep(qr.numpy(), self.ix.t4)
+        bits = planes.shape[1]
+        pl, de, kk, _ = self.O.query_prep(qr.numpy(), self.ix.t4 if bits == 4 else self.ix.t8, bits)
         planes.copy_(torch.from_numpy(np.ascontiguousarray(pl).view(np.int32).reshape(planes.shape)))
         delta.copy_(torch.from_numpy(de))
         k1.copy_(torch.from_numpy(kk))
@@ -165,7 +166,7 @@ class _OracleStages:
         out_i.copy_(torch.from_numpy(ii))
 
 
-def _seeded_worker(rank, world, port, outdir, nq, prune, policy):
+def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits):
     import torch
     import torch.distributed as dist
 
@@ -181,18 +182,19 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy):
     P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
     C, lab = O.kmeans(X, 24, iters=3)
     ix = O.build(X, C, lab, P, t4)
+    ix.t8 = O.query_scale(64, 3, 7)
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
     d, i = sharded_search(_OracleStages(O, ix, rank, world, owner), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0,
-                          64, rank, world)
+                          64, rank, world, query_bits=bits)
     with open(os.path.join(outdir, f"rank{rank}.pkl"), "wb") as f:
         pickle.dump((d.numpy(), i.numpy()), f)
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,nq,prune,policy", [(2, 40, 1, "balanced"), (3, 7, 1, "round_robin"),
-                                                   (2, 40, 0, "balanced")])
-def test_seeded_sharded_search_over_gloo(world, nq, prune, policy):
+@pytest.mark.parametrize("world,nq,prune,policy,bits", [(2, 40, 1, "balanced", 4), (3, 7, 1, "round_robin", 4),
+                                                        (2, 40, 0, "balanced", 4), (2, 40, 1, "balanced", 8)])
+def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits):
     """The orchestration (queries split for the rotation and coarse quantiser and padded, rotated
     rows and probe rows all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
     merge of the oracle's per-shard searches with the shared seed.  With the prune off every
@@ -203,17 +205,18 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune, policy):
     from neurosamble_b200.sharded import plan
 
     with tempfile.TemporaryDirectory() as td:
-        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy), nprocs=world, join=True)
+        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy, bits), nprocs=world, join=True)
         res = [pickle.load(open(os.path.join(td, f"rank{r}.pkl"), "rb")) for r in range(world)]
     X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
     Q = Q[:nq]
     P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
     C, lab = O.kmeans(X, 24, iters=3)
     ix = O.build(X, C, lab, P, t4)
+    ix.t8 = O.query_scale(64, 3, 7)
     slices = plan(nq, 8, 10, 60, 0, 0, world)[1]
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
     parts = [O.search(ix, Q, 10, 8, 60, prune=prune, slices=slices, shard_rank=r, shard_count=world, exchange=True,
-                      owner=owner) for r in range(world)]
+                      owner=owner, query_bits=bits) for r in range(world)]
     want_i, want_d = O.merge_candidates([(p[1], p[0]) for p in parts], 10)
     for d, i in res:
         assert np.array_equal(i, want_i)
