@@ -271,7 +271,8 @@ def run_reference(args, cfg):
     line = {"impl": "reference", "metric": metric_name(cfg), "value": round(value, 2), "unit": "queries/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32+u32", "data": "synthetic (seeded Gaussian mixture, BASELINE config 2)",
+            "vs_baseline": None, "dtype": "f32+u32",
+            "data": f"synthetic (seeded Gaussian mixture, BASELINE config {cfg['config']})",
             "config": dict(workload(cfg, R, args.kmeans), recall_by_rerank_sample=recalls),
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
                              "sample": f"{n_sample} of {cfg['nq']} queries per step, same index and parameters"},
@@ -293,7 +294,8 @@ def workload(cfg, R, kmeans):
     return {"workload": (f"BASELINE config {cfg['config']}: {_count(cfg['n'])} x {cfg['d']} f32, "
                          f"{cfg['centres']}-centre {'anisotropic ' if cfg['aniso'] else ''}mixture sigma "
                          f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ 1-bit "
-                         f"codes, 4-bit queries" + ("; data generated on the device" if cfg["device_data"] else "")),
+                         f"codes, {cfg.get('query_bits', 4)}-bit queries"
+                         + ("; data generated on the device" if cfg["device_data"] else "")),
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
             "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
             "kmeans": kmeans, "search_mode": "QUANT8" if cfg.get("query_bits", 4) == 8 else "QUANT4"}
