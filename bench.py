@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: queries/sec of IVF-RaBitQ search on BASELINE config 2 (1M x 256, nlist 1024,
+"""Benchmark: queries/sec of IVF-RaBitQ search on benchmark config 2 (1M x 256, nlist 1024,
 nprobe 32, k 10, exact rerank, query batch 10,000), 1..8 B200 with lists sharded per GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|4|5]
@@ -10,7 +10,7 @@ buffers (rbq_search_host: H2D of the queries, search, D2H of distances and ids).
 torchrun (N > 1) the lists are spread over the ranks by size (each list on one rank), every
 rank scans its own lists, and the per-rank results are merged after one NCCL all-gather; times
 are the max over ranks.  `--impl reference` times the CPU restatement of the reference search
-(oracle/, all host cores) on the same workload.  `--config 4` / `--config 5` run BASELINE's
+(oracle/, all host cores) on the same workload.  `--config 4` / `--config 5` run the benchmark's
 100M x 128 (nlist 65,536) and 20M x 768 (nlist 16,384) configurations with data generated on
 the device and recall measured on a 1,000-query sample (supplementary lines; no CPU baseline).
 """
@@ -28,7 +28,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-# BASELINE config 2 (the metric's configuration), and configs 4 and 5 (supplementary).
+# Benchmark config 2 (the metric's configuration), and configs 4 and 5 (supplementary).
 CFG = dict(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, nlist=1024, nprobe=32, k=10,
            rerank=100, seed=2024, config=2, aniso=0, device_data=False, gt_sample=10_000)
 CONFIGS = {
@@ -674,7 +674,7 @@ def main():
     ap.add_argument("--query-bits", type=int, default=4, choices=[4, 8],
                     help="query code width of both arms: 4 (QUANT4, the reference CLI's default) or 8 (QUANT8)")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
-                    help="BASELINE configuration (2: the metric's; 4 / 5: supplementary, data on the device)")
+                    help="benchmark configuration (2: the metric's; 4 / 5: supplementary, data on the device)")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
                     help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()

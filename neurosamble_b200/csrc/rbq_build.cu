@@ -273,7 +273,7 @@ void launch_gather_rows_f32(const float* src, int64_t rows, int cols, const int6
 }
 
 // ---------------------------------------------------------------------------------------
-// Synthetic data for the benchmark configurations (2, 4, 5).
+// Synthetic data for the benchmark configurations (configs 1, 2, 4, 5).
 // Philox-4x32-10 counters; normals by Box-Muller in double (CUDA's log/sincos).
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void philox_dev(uint32_t k0, uint32_t k1, uint32_t c[4])

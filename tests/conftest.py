@@ -32,7 +32,7 @@ def pytest_collection_modifyitems(config, items):
 
 
 def mixture(n, d, n_centres, sigma, nq, qsigma=0.05, seed=0, normalize=True):
-    """Seeded Gaussian-mixture rows and perturbed-row queries (BASELINE config shapes)."""
+    """Seeded Gaussian-mixture rows and perturbed-row queries (benchmark config shapes)."""
     rng = np.random.default_rng(seed)
     cent = rng.standard_normal((n_centres, d)).astype(np.float32)
     X = cent[rng.integers(0, n_centres, n)] + np.float32(sigma) * rng.standard_normal((n, d)).astype(np.float32)

@@ -339,7 +339,7 @@ def test_gpu_kmeans_is_deterministic():
 
 
 def test_config1_parity_and_recall(oracle):
-    """BASELINE config 1 shape at full size: 100k x 128, K = 256, P = 16, k = 10, R = 40."""
+    """Benchmark config 1 shape at full size: 100k x 128, K = 256, P = 16, k = 10, R = 40."""
     from neurosamble_b200 import IndexIVFRaBitQ
     X, Q = mixture(100000, 128, 256, 0.3, 1000, seed=11)
     idx = IndexIVFRaBitQ(128, 256, seed=7, kmeans_iters=10)
