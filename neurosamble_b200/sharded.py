@@ -123,6 +123,16 @@ class ShardedIndexIVFRaBitQ:
         """Every rank passes the same rows; each keeps the rows of its own lists."""
         self.local.add(x, labels)
 
+    def build(self, x, centroids=None, labels=None) -> None:
+        """train (or the given centroids, on every rank) + add, as IndexIVFRaBitQ.build."""
+        if centroids is None:
+            if labels is not None:
+                raise RuntimeError("build: labels need the centroids they refer to")
+            self.train(x)
+        else:
+            self.local.set_centroids(centroids)
+        self.add(x, labels)
+
     def search_local(self, x, k: int):
         t, _ = self.local._to_device(x)
         d, i = self.local.search(t, k)
