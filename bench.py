@@ -222,7 +222,7 @@ def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
     t0 = time.perf_counter()
     d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"])
     dt = time.perf_counter() - t0
-    return n / dt, n, dt, i
+    return n / dt, n, dt, (d, i)
 
 
 def run_reference(args, cfg):
@@ -316,7 +316,10 @@ def run_ours(args, cfg):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
+    if world > 1 and "NCCL_DEBUG" not in os.environ:
+        # NCCL's communicator set-up lines (ranks, devices, NVLS) go to stderr, so stdout carries
+        # only the JSON line while the log still shows every rank joining
+        os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
@@ -401,8 +404,11 @@ def run_ours(args, cfg):
             tdist.barrier()
         torch.cuda.synchronize(dev)
 
+    last = {}
+
     def step_device():
         d, i = index.search(Qd, k)
+        last["r"] = (d, i)
         return d, i
 
     # ---- value: device-resident queries
@@ -511,7 +517,8 @@ def run_ours(args, cfg):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and X is not None:
-        cpu = cpu_baseline(local_ix, X, Q, cfg, R)
+        gd, gi = last["r"]
+        cpu = cpu_baseline(local_ix, X, Q, cfg, R, (gd.cpu().numpy(), gi.cpu().numpy()))
 
     if world > 1:
         tdist.barrier()
@@ -620,17 +627,22 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     n_valid = int((ids >= 0).sum().item())
     rr_bytes = n_valid * (4 * d + 8)
     peak, kind = measured_peak()
-    traffic = None
+    # DRAM traffic cannot be read inside a plain run: it comes from a stored ncu capture of the
+    # same kernel and workload (profiles/scan_traffic.json), and the line says so
+    traffic, traffic_src = None, None
     tf = os.path.join(HERE, "profiles", "scan_traffic.json")
-    if os.path.exists(tf) and cfg.get("config", 2) == 2:  # the capture is of config 2's scan
+    if os.path.exists(tf):
         try:
             with open(tf) as f:
-                traffic = json.load(f).get("bytes_per_launch_scaled_to_bench")
+                tj = json.load(f)
+            if tj.get("config", 2) == cfg.get("config", 2):
+                traffic = tj.get("bytes_per_launch_scaled_to_bench")
+                traffic_src = "stored ncu capture (profiles/scan_traffic.json), not measured in this run"
         except Exception:
             traffic = None
     ach = scan_bytes / (scan_ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-            "traffic": traffic, "peak_kind": kind,
+            "traffic": traffic, "traffic_source": traffic_src, "peak_kind": kind,
             "kernel": "rbq scan_kernel (+ key->id epilogue)" + (", 2 launches: seed list + rest" if seeded else ""),
             "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
             "launch_ms": round(scan_ms, 4), "prune_admitted_fraction": round(admitted / max(1, scanned), 4)}
@@ -641,9 +653,11 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     return roof, roof_rr
 
 
-def cpu_baseline(ix, X, Q, cfg, R):
+def cpu_baseline(ix, X, Q, cfg, R, gpu_result=None):
     """The oracle (the CPU restatement of the reference search), all host cores, on a bounded
-    sample of the same batch against the same index."""
+    sample of the same batch against the same index.  With gpu_result = (dist, ids) of the
+    timed GPU search of the whole batch, the oracle's answers for the sample are compared with
+    the GPU's for the same queries (the line's `parity` object)."""
     from oracle import oracle as O
     ex = ix.export_lists()
     C, Cr = ix.centroids()
@@ -653,9 +667,34 @@ def cpu_baseline(ix, X, Q, cfg, R):
     oix = O.OracleIndex(cfg["d"], info.padded_dim, cfg["nlist"], ex["list_off"], ex["ids"], ex["codes"], ex["fadd"],
                         ex["frescale"], ex["ferr"], Cr, ix.rotation(), ix.query_scale, X)
     oix.t8 = O.query_scale(info.padded_dim, int(info.seed), 7)
-    qps, n_s, dt, _ = cpu_search_timed(O, oix, Q, cfg, R, budget_s=15.0)
-    return {"value": round(qps, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
-            "sample": f"{n_s} of {cfg['nq']} queries ({dt:.1f}s), same index bytes and parameters"}
+    qps, n_s, dt, (od, oi) = cpu_search_timed(O, oix, Q, cfg, R, budget_s=15.0)
+    out = {"value": round(qps, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
+           "sample": f"{n_s} of {cfg['nq']} queries ({dt:.1f}s), same index bytes and parameters"}
+    if gpu_result is not None:
+        out["parity"] = parity_of(gpu_result[0][:n_s], gpu_result[1][:n_s], od, oi)
+    return out
+
+
+def parity_of(gd, gi, od, oi, rel_tol=1e-4):
+    """GPU result against the oracle's for the same queries on the same index bytes: ids equal,
+    distance bits equal, the largest relative distance error over finite entries, and the ids
+    that differ outside distance ties within rel_tol (the north star's tie rule)."""
+    gd = np.asarray(gd, np.float32)
+    od = np.asarray(od, np.float32)
+    gi = np.asarray(gi)
+    oi = np.asarray(oi)
+    fin = np.isfinite(gd) & np.isfinite(od)
+    rel = np.abs(gd[fin].astype(np.float64) - od[fin]) / np.maximum(np.abs(od[fin].astype(np.float64)), 1e-30)
+    diff_rows = np.nonzero((gi != oi).any(axis=1))[0]
+    untied = 0
+    for r in diff_rows:  # a differing id is a tie if its distance equals the other side's within rel_tol
+        for j in np.nonzero(gi[r] != oi[r])[0]:
+            if abs(float(gd[r, j]) - float(od[r, j])) > rel_tol * max(abs(float(od[r, j])), 1e-30):
+                untied += 1
+    return {"n": int(gi.shape[0]), "k": int(gi.shape[1]), "ids_equal": bool(np.array_equal(gi, oi)),
+            "dist_bits_equal": bool(np.array_equal(gd.view(np.uint32), od.view(np.uint32))),
+            "max_rel_err": float(rel.max()) if rel.size else 0.0, "rows_differing": int(diff_rows.size),
+            "ids_differing_outside_ties": int(untied), "rel_tol": rel_tol}
 
 
 def main():

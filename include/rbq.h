@@ -89,6 +89,10 @@ typedef struct {
                          /* captured as a CUDA graph and later ones replay it: copy in, one     */
                          /* graph launch, copy out (small batches are launch-bound).  Up to 8   */
                          /* graphs per index; adding, training or setting centroids drops them. */
+                         /* A graph reads and writes buffers of its own: replays of one graph   */
+                         /* issued on different streams are serialised (each replay's copy-in   */
+                         /* waits for the previous replay's copy-out).  Like every call on one  */
+                         /* index, they must come from one host thread at a time.               */
                          /* 0 (default): launch the kernels one by one.                         */
 } rbq_search_params_t;
 
@@ -249,7 +253,10 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
  *   - needs nq*slices*R*8 bytes, plus nq*R*8 when slices > 1 (each part rounded up to 256);
  *     anything larger is rejected with RBQ_ERR_INVALID before any work is queued;
  *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
- *     with that device current; make that first call before any stream capture;
+ *     with that device current; make that first call before any stream capture.  The address
+ *     is kept with the id of the context it belongs to and looked up again (by the next call,
+ *     which then counts as a first call) when the device's context has been re-created, as
+ *     after cudaDeviceReset;
  *   - all calls share the one array and it keeps the last call's contents (nothing in it has
  *     to start at zero: every key read is written earlier in the same call); calls that can
  *     overlap on the GPU (other streams, other host threads, same device) race on it and must

@@ -3,6 +3,7 @@
 //
 // Every entry point catches everything, stores a message for rbq_last_error() and returns
 // a status code; nothing throws across the ABI and nothing exits or traps.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
@@ -780,6 +781,7 @@ Index::SearchGraph& search_graph(Index& ix, const rbq_search_params_t& params, i
   if (ix.graphs.size() >= 8) {
     Index::SearchGraph& old = ix.graphs.front();
     if (old.exec) cudaGraphExecDestroy(old.exec);
+    if (old.done) cudaEventDestroy(old.done);
     dev_free(old.q);
     dev_free(old.d);
     dev_free(old.i);
@@ -794,6 +796,7 @@ Index::SearchGraph& search_graph(Index& ix, const rbq_search_params_t& params, i
     g.q = dev_alloc<float>((size_t)nq * ix.D);
     g.d = dev_alloc<float>((size_t)nq * key.k);
     g.i = dev_alloc<int64_t>((size_t)nq * key.k);
+    RBQ_CUDA(cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming));
     RBQ_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     RBQ_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed));
     try {
@@ -811,6 +814,8 @@ Index::SearchGraph& search_graph(Index& ix, const rbq_search_params_t& params, i
   } catch (...) {
     if (graph) cudaGraphDestroy(graph);
     if (cs) cudaStreamDestroy(cs);
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.done) cudaEventDestroy(g.done);
     cudaGetLastError();
     dev_free(g.q);
     dev_free(g.d);
@@ -953,6 +958,7 @@ void drop_graphs(Index& ix)
 {
   for (auto& g : ix.graphs) {
     if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.done) cudaEventDestroy(g.done);
     dev_free(g.q);
     dev_free(g.d);
     dev_free(g.i);
@@ -1222,10 +1228,12 @@ int rbq_search(rbq_index_t* index, const rbq_search_params_t* params, const floa
     cudaStream_t s = as_stream(stream);
     if (params->graph && nq > 0) {
       Index::SearchGraph& g = search_graph(ix, *params, nq);
+      RBQ_CUDA(cudaStreamWaitEvent(s, g.done, 0));  // the previous replay's results are out
       RBQ_CUDA(cudaMemcpyAsync(g.q, Q_dev, (size_t)nq * ix.D * 4, cudaMemcpyDeviceToDevice, s));
       RBQ_CUDA(cudaGraphLaunch(g.exec, s));
       RBQ_CUDA(cudaMemcpyAsync(dist_dev, g.d, (size_t)nq * params->k * 4, cudaMemcpyDeviceToDevice, s));
       RBQ_CUDA(cudaMemcpyAsync(ids_dev, g.i, (size_t)nq * params->k * 8, cudaMemcpyDeviceToDevice, s));
+      RBQ_CUDA(cudaEventRecord(g.done, s));
       return;
     }
     run_search(ix, *params, Q_dev, nq, dist_dev, ids_dev, s, nullptr);
@@ -1251,10 +1259,12 @@ int rbq_search_host(rbq_index_t* index, const rbq_search_params_t* params, const
     constexpr int64_t kMinHalf = 2048;
     if (params->graph) {  // the captured search reads and writes its own buffers
       Index::SearchGraph& g = search_graph(ix, *params, nq);
+      RBQ_CUDA(cudaStreamWaitEvent(s, g.done, 0));  // the previous replay's results are out
       RBQ_CUDA(cudaMemcpyAsync(g.q, Q_host, (size_t)nq * ix.D * 4, cudaMemcpyHostToDevice, s));
       RBQ_CUDA(cudaGraphLaunch(g.exec, s));
       RBQ_CUDA(cudaMemcpyAsync(dist_host, g.d, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
       RBQ_CUDA(cudaMemcpyAsync(ids_host, g.i, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
+      RBQ_CUDA(cudaEventRecord(g.done, s));
     } else {
       Scratch sc(s);
       float* q = sc.get<float>((size_t)nq * ix.D);
@@ -1913,19 +1923,57 @@ static __device__ __align__(256) unsigned char rbq_noalloc_scratch[RBQ_NOALLOC_S
 
 namespace {
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+// Per device: the address and the unique id of the context it was looked up in.  A context
+// destroyed and created again (cudaDeviceReset) has a new id, so the address is looked up again
+// instead of being used stale.
+struct NoallocSlot {
+  unsigned long long ctx_id = 0;
+  void* addr = nullptr;
+};
+NoallocSlot g_noalloc[64];
+
+// Unique id of the calling thread's current context (cuCtxGetCurrent + cuCtxGetId through the
+// runtime's driver entry points; no link-time libcuda).
+unsigned long long current_context_id()
+{
+  typedef CUresult (*GetCurrentFn)(CUcontext*);
+  typedef CUresult (*GetIdFn)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+  });
+  RBQ_CHECK(get_current && get_id, RBQ_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are not available from the driver");
+  CUcontext c = nullptr;
+  RBQ_CHECK(get_current(&c) == CUDA_SUCCESS && c, RBQ_ERR_CUDA, "no current CUDA context");
+  unsigned long long id = 0;
+  RBQ_CHECK(get_id(c, &id) == CUDA_SUCCESS, RBQ_ERR_CUDA, "cuCtxGetId failed");
+  return id;
+}
 
 // Device address of the scratch array on `device`, which must be the current device.
 unsigned char* noalloc_scratch_address(int device)
 {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   RBQ_CHECK(device >= 0 && device < 64, RBQ_ERR_INVALID, "device ordinal out of range");
-  if (!g_noalloc_addr[device]) {
+  const unsigned long long ctx = current_context_id();
+  NoallocSlot& slot = g_noalloc[device];
+  if (!slot.addr || slot.ctx_id != ctx) {
     void* p = nullptr;
     RBQ_CUDA(cudaGetSymbolAddress(&p, rbq_noalloc_scratch));
-    g_noalloc_addr[device] = p;
+    slot.addr = p;
+    slot.ctx_id = ctx;
   }
-  return static_cast<unsigned char*>(g_noalloc_addr[device]);
+  return static_cast<unsigned char*>(slot.addr);
 }
 
 inline size_t round_up_256(size_t v) { return (v + 255) / 256 * 256; }

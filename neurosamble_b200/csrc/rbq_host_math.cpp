@@ -51,8 +51,10 @@ double normal_at(uint64_t seed, uint32_t stream, uint64_t i)
 }
 
 // Start fraction of the rescale search per extra-bit count; the reference's table
-// (quantizer_gpu.cu:862-872), which must be alike for t4 to mean the same thing.
-const double kStartFraction[9] = {0, 0.15, 0.20, 0.52, 0.59, 0.71, 0.75, 0.77, 0.81};
+// (quantizer_gpu.cu:875-885), which must be alike for t4 to mean the same thing.
+// Held as float like the reference's std::array<float, 9>, so t_end is multiplied by the
+// double value of each float constant (0.15f, not 0.15).
+const float kStartFraction[9] = {0.0f, 0.15f, 0.20f, 0.52f, 0.59f, 0.71f, 0.75f, 0.77f, 0.81f};
 
 // Scale t maximising <floor(t*o)+0.5, o> / |floor(t*o)+0.5| over the critical points where a
 // coordinate's level steps up (levels capped at 2^ex_bits - 1).  Same search as the

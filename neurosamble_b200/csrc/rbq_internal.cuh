@@ -137,6 +137,9 @@ struct Index {
     float* q = nullptr;
     float* d = nullptr;
     int64_t* i = nullptr;
+    // Recorded after a replay's results are copied out; the next replay's copy into q waits on
+    // it, so replays issued on different streams cannot overwrite each other's buffers.
+    cudaEvent_t done = nullptr;
   };
   std::vector<SearchGraph> graphs;
 

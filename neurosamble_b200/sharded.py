@@ -124,7 +124,10 @@ class ShardedIndexIVFRaBitQ:
         self.local.add(x, labels)
 
     def build(self, x, centroids=None, labels=None) -> None:
-        """train (or the given centroids, on every rank) + add, as IndexIVFRaBitQ.build."""
+        """train (or the given centroids, on every rank) + add, as IndexIVFRaBitQ.build; like
+        rbq_build it refuses an index that already holds vectors."""
+        if self.ntotal != 0:
+            raise RuntimeError("build: the index already holds vectors (use add)")
         if centroids is None:
             if labels is not None:
                 raise RuntimeError("build: labels need the centroids they refer to")

@@ -112,9 +112,10 @@ inline void rotate_row(const float* x, const float* P, int Dp, float* y, double*
   for (int j = 0; j < Dp; ++j) y[j] = (float)acc[j];
 }
 
-// kTightStart of the reference (quantizer_gpu.cu:862-872): the start fraction of the
+// kTightStart of the reference (quantizer_gpu.cu:875-885): the start fraction of the
 // rescale search per extra-bit count.  A table that has to be alike.
-const double kTightStart[9] = {0, 0.15, 0.20, 0.52, 0.59, 0.71, 0.75, 0.77, 0.81};
+// float, as the reference's std::array<float, 9>: t_end is multiplied by (double)0.15f.
+const float kTightStart[9] = {0.0f, 0.15f, 0.20f, 0.52f, 0.59f, 0.71f, 0.75f, 0.77f, 0.81f};
 
 // Restatement of best_rescale_factor (quantizer_gpu.cu:887-943): the scale t that maximises
 // <o_bar, o> / |o_bar| over the codes o_bar = floor(t*o) (ex_bits magnitude levels).

@@ -358,6 +358,58 @@ def test_config1_parity_and_recall(oracle):
     assert oracle.recall(i, gt) == oracle.recall(i2, gt)
 
 
+def _config2_data(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, seed=2024):
+    """Benchmark config 2's generator (the bench's make_data): float32 mixture rows in chunks."""
+    rng = np.random.default_rng(seed)
+    cent = rng.standard_normal((centres, d), dtype=np.float32)
+    X = np.empty((n, d), np.float32)
+    for a in range(0, n, 1 << 17):
+        b = min(n, a + (1 << 17))
+        X[a:b] = cent[rng.integers(0, centres, b - a)]
+        X[a:b] += np.float32(sigma) * rng.standard_normal((b - a, d), dtype=np.float32)
+        X[a:b] /= np.linalg.norm(X[a:b], axis=1, keepdims=True)
+    src = rng.integers(0, n, nq)
+    Q = X[src] + np.float32(qsigma) * rng.standard_normal((nq, d), dtype=np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    return X, np.ascontiguousarray(Q, np.float32)
+
+
+def test_config2_parity_at_full_size(oracle):
+    """The headline configuration at full size: 1M x 256, K = 1024 (balanced k-means, the
+    default trainer), P = 32, k = 10, R = 200 (the depth the benchmark settles on).  The whole
+    10,000-query batch is searched on the GPU, as the benchmark does; the oracle builds its own
+    index from the rows, the GPU's centroids and the assignment, and searches the first 300
+    queries.  Codes, factors, ids, distances and recall must agree exactly."""
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = _config2_data()
+    idx = IndexIVFRaBitQ(256, 1024, seed=7)
+    idx.train(X)
+    idx.add(X)
+    C, _ = idx.centroids()
+    ex = idx.export_lists()
+    # the GPU's assignment, read back from its lists, checked on a sample of rows (the exact
+    # assignment of all 1M rows on the CPU would dominate the test's time)
+    lab = np.repeat(np.arange(1024, dtype=np.uint32), np.diff(ex["list_off"]))[np.argsort(ex["ids"], kind="stable")]
+    rows = np.arange(0, X.shape[0], 997)
+    assert np.array_equal(oracle.assign(X[rows], C), lab[rows])
+    oix = oracle.build(X, C, lab, idx.rotation(), idx.query_scale)
+    assert np.array_equal(ex["list_off"], oix.list_off) and np.array_equal(ex["ids"], oix.ids)
+    assert np.array_equal(ex["codes"], oix.codes)
+    for f in ("fadd", "frescale", "ferr"):
+        assert np.array_equal(u32(ex[f]), u32(getattr(oix, f))), f
+    idx.nprobe, idx.k_rerank = 32, 200
+    d, i = idx.search(Q, 10)
+    ns = 300
+    d2, i2 = oracle.search(oix, Q[:ns], 10, 32, 200, prune=1)
+    assert np.array_equal(i[:ns], i2)
+    assert np.array_equal(u32(d[:ns]), u32(d2))
+    fin = np.isfinite(d2)
+    assert np.all(np.abs(d[:ns][fin] - d2[fin]) <= REL_TOL * np.abs(d2[fin]))
+    _, gt = oracle.knn_exact(X, Q[:ns], 10)
+    r_gpu, r_orc = oracle.recall(i[:ns], gt), oracle.recall(i2, gt)
+    assert r_gpu == r_orc and r_gpu >= 0.95
+
+
 @pytest.mark.parametrize("d,K,nq", [(256, 1024, 300), (128, 300, 129), (32, 64, 1), (768, 256, 200), (100, 40, 7)])
 def test_tensor_core_scores_match_fp32(oracle, d, K, nq):
     """tcgen05 kind::tf32 scores vs the fp32 CUDA-core scores; tf32 keeps 10 mantissa bits, so
@@ -728,6 +780,39 @@ def test_graph_search_replays_bit_exact(case):
             call("rbq_search_host", idx.handle, ctypes.byref(sp), qh.ctypes.data_as(ctypes.c_void_p), B,
                  dh.ctypes.data_as(ctypes.c_void_p), ih.ctypes.data_as(ctypes.c_void_p), stream())
             assert np.array_equal(ih, want[2][1]) and np.array_equal(u32(dh), u32(want[2][0]))
+    finally:
+        idx.use_graph = False
+    torch.cuda.synchronize()
+
+
+def test_graph_replays_on_two_streams_do_not_share_results(case):
+    """Replays of one captured search issued back to back on two streams (no sync between):
+    each stream must get its own batch's results, bit-equal to plain searches, although the
+    graph's input and output buffers are shared."""
+    torch = _torch()
+    from neurosamble_b200 import _lib
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune, idx.seeded = 8, 40, True, -1
+    B = 64
+    batches = [dev(Q[a:a + B]) for a in range(0, 4 * B, B)]
+    idx.use_graph = False
+    want = [idx.search(Q[a:a + B], 10) for a in range(0, 4 * B, B)]
+    sp = idx.search_params(10)
+    sp.graph = 1
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [(torch.empty((B, 10), dtype=torch.float32, device="cuda"),
+             torch.empty((B, 10), dtype=torch.int64, device="cuda")) for _ in batches]
+    try:
+        call("rbq_search", idx.handle, ctypes.byref(sp), ptr(batches[0]), B, ptr(outs[0][0]), ptr(outs[0][1]),
+             stream())  # captures the graph
+        for rep in range(3):
+            for j, qb in enumerate(batches):
+                st = streams[j % 2]
+                _lib.call("rbq_search", idx.handle, ctypes.byref(sp), ptr(qb), B, ptr(outs[j][0]), ptr(outs[j][1]),
+                       ctypes.c_void_p(st.cuda_stream))
+            torch.cuda.synchronize()
+            for (d0, i0), (d1, i1) in zip(want, outs):
+                assert np.array_equal(i0, i1.cpu().numpy()) and np.array_equal(u32(d0), u32(d1.cpu().numpy()))
     finally:
         idx.use_graph = False
     torch.cuda.synchronize()

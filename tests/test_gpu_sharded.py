@@ -51,10 +51,33 @@ def _rank_main(rank, world, port, outdir):
     d, i = idx.search(Q, 10, stats=st)
     stats = [torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}") for _ in range(world)]
     dist.all_gather(stats, st)
+    # build(): with the given centroids and labels, and by training (rank 0 trains, the table is
+    # broadcast), against train() + add() on the same rows; a second build is refused
+    same = []
+    b1 = ShardedIndexIVFRaBitQ(128, 64, seed=7, device=rank)
+    b1.build(X, centroids=C, labels=lab)
+    b1.nprobe, b1.k_rerank, b1.probe_split = 12, 40, 1
+    d1, i1 = b1.search(Q, 10)
+    same.append(np.array_equal(i1, i) and np.array_equal(d1.view(np.uint32), d.view(np.uint32)))
+    try:
+        b1.build(X)
+        same.append(False)
+    except RuntimeError:
+        same.append(True)
+    b2 = ShardedIndexIVFRaBitQ(128, 64, seed=7, device=rank, kmeans_iters=4)
+    b2.build(X)
+    b3 = ShardedIndexIVFRaBitQ(128, 64, seed=7, device=rank, kmeans_iters=4)
+    b3.train(X)
+    b3.add(X)
+    for b in (b2, b3):
+        b.nprobe, b.k_rerank, b.probe_split = 12, 40, 1
+    d2, i2 = b2.search(Q, 10)
+    d3, i3 = b3.search(Q, 10)
+    same.append(np.array_equal(i2, i3) and np.array_equal(d2.view(np.uint32), d3.view(np.uint32)))
     if rank == 0:
         with open(os.path.join(outdir, "res.pkl"), "wb") as f:
             pickle.dump((d, i, C, lab, idx.local.rotation(), idx.local.query_scale, X, Q, idx.local.list_owners(),
-                         [s.cpu().numpy() for s in stats]), f)
+                         [s.cpu().numpy() for s in stats], same), f)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -64,7 +87,8 @@ def test_two_gpu_sharded_search_matches_oracle(oracle):
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(_rank_main, args=(2, _port(), td), nprocs=2, join=True)
-        d, i, C, lab, P, t4, X, Q, owners, stats = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
+        d, i, C, lab, P, t4, X, Q, owners, stats, same = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
+    assert same == [True, True, True], same  # build() == train() / centroids + add(); rebuild refused
     oix = oracle.build(X, C, lab, P, t4)
     want = oracle.list_owners("balanced", np.bincount(lab, minlength=64), 2)
     assert np.array_equal(owners, want)  # the default policy of the sharded index

@@ -80,7 +80,7 @@ def _run(idx, name, st, nprobe, R, prune, slices):
 
 @pytest.mark.gpu
 def test_noalloc_scan_matches_scan_on_two_calls_in_a_row():
-    from neurosamble_b200 import IndexIVFRaBitQ
+    from neurosamble_b200 import IndexIVFRaBitQ, _lib
     X, Q = mixture(20000, 128, 40, 0.3, 400, seed=21)
     idx = IndexIVFRaBitQ(128, 64, seed=7, kmeans_iters=5)
     idx.train(X)
@@ -90,7 +90,14 @@ def test_noalloc_scan_matches_scan_on_two_calls_in_a_row():
         assert _round256(len(Qc) * slices * R * 8) + (_round256(len(Qc) * R * 8) if slices > 1 else 0) <= SCRATCH_BYTES
         st = _stage(idx, Qc, nprobe)
         ref = _run(idx, "rbq_scan", st, nprobe, R, prune, slices)
-        got = _run(idx, "rbq_scan_noalloc", st, nprobe, R, prune, slices)
+        # arm the library's allocation-failure injection: the very next device allocation it
+        # makes would fail with RBQ_ERR_OOM, so a successful call proves that it made none
+        L = _lib.lib()
+        assert L.rbq_debug_fail_alloc(0) == 0
+        try:
+            got = _run(idx, "rbq_scan_noalloc", st, nprobe, R, prune, slices)
+        finally:
+            L.rbq_debug_fail_alloc(-1)
         assert np.array_equal(got[0], ref[0])
         assert np.array_equal(got[1].view(np.uint32), ref[1].view(np.uint32))  # the tests' tolerance: bit-exact
         assert np.array_equal(got[2], ref[2])
