@@ -114,6 +114,10 @@ int rbq_version(void);
 /* Kernels this library has launched in this process (all devices).  No reference
  * counterpart: lets a benchmark count the library's launches inside a timed region. */
 uint64_t rbq_kernel_launches(void);
+/* Vectors per scan tile: the prune threshold tightens between tiles, and every candidate buffer
+ * holds at least R + tile keys (cap = max(pow2(cand_cap or 1024), pow2(R + tile))).  Callers that
+ * plan scans themselves (a sharded search) read it here.  No reference counterpart. */
+int rbq_scan_tile(void);
 void rbq_index_params_default(rbq_index_params_t* p);
 void rbq_search_params_default(rbq_search_params_t* p);
 

@@ -48,6 +48,7 @@ SIGNATURES = {
     "rbq_last_error": [],
     "rbq_version": [],
     "rbq_kernel_launches": [],
+    "rbq_scan_tile": [],
     "rbq_index_params_default": [ctypes.POINTER(IndexParams)],
     "rbq_search_params_default": [ctypes.POINTER(SearchParams)],
     "rbq_make_rotation": [_I32, _U64, _P],

@@ -694,10 +694,15 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
 // their first vector.
 void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const uint32_t* planes, const float* delta,
                  const float* k1, int64_t nq, const int32_t* probes, const float* g, float* tau_a,
-                 unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, cudaStream_t s)
+                 unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, int32_t* qorder_buf,
+                 cudaStream_t s)
 {
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
                                 keys_s, stats, sp.qbits);
+  if (qorder_buf && nq >= kQueryOrderMinBatch) {  // [K + 2] counts, then [nq] order
+    launch_query_order(probes, nq, sp.P, ix.K, qorder_buf, qorder_buf + ix.K + 2, s);
+    sa.qorder = qorder_buf + ix.K + 2;
+  }
   if (sp.seeded && sp.prune) {
     ScanArgs a0 = sa;
     a0.nprobe = 1;
@@ -705,6 +710,7 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
     a0.slices = 1;
     a0.stats = nullptr;
     a0.tau_out = tau_a;
+    a0.qorder = sa.qorder;
     launch_scan(a0, s);
     sa.tau0 = tau_a;
   }
@@ -741,6 +747,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
   unsigned long long* keys = sp.slices > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : keys_s;
   float* tau_a = sp.seeded ? sc.get<float>((size_t)chunk) : nullptr;
+  int32_t* qorder = chunk >= kQueryOrderMinBatch ? sc.get<int32_t>((size_t)ix.K + 2 + chunk) : nullptr;
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
@@ -757,7 +764,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     launch_query_prep(Qr, cn, ix.Dp, qt, sp.qbits, planes, delta, k1, s);
     {
       Range r("rbq scan");
-      search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, s);
+      search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, qorder, s);
     }
     Range r("rbq rerank / result");
     if (params.rerank > 0)
@@ -1013,6 +1020,8 @@ int rbq_debug_fail_alloc(int64_t after)
 }
 
 uint64_t rbq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int rbq_scan_tile(void) { return rbq::kScanTile; }
 
 void rbq_index_params_default(rbq_index_params_t* p)
 {
@@ -1817,6 +1826,11 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
       unsigned long long* ik = sc.get<unsigned long long>((size_t)nq * R);
       launch_cands_to_keys(init_ids_dev, init_dist_dev, nq * R, ik, s);
       sa.init_keys = ik;
+    }
+    if (nq >= kQueryOrderMinBatch) {
+      int32_t* qo = sc.get<int32_t>((size_t)ix.K + 2 + nq);
+      launch_query_order(probes_dev, nq, probe_stride > 0 ? probe_stride : nprobe, ix.K, qo, qo + ix.K + 2, s);
+      sa.qorder = qo + ix.K + 2;
     }
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);

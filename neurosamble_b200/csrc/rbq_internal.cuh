@@ -229,8 +229,25 @@ struct ScanArgs {
   float* tau_out = nullptr;
   unsigned long long* out_keys;  // [nq, slices, R]
   unsigned long long* stats;     // optional [2]: scanned, admitted
+  // Optional [nq] visiting order: block i scans query qorder[i / slices] (a permutation of
+  // 0..nq-1).  Only the order in which queries run changes; every query's result is its own.
+  const int32_t* qorder = nullptr;
 };
-constexpr int kScanTile = 512;  // vectors per scan tile (256 threads x 2)
+// qorder[0..nq) = the queries sorted by their nearest probe probes[q * pstride] (ascending list id;
+// queries without probes last), so that queries searching the same region of the index run at
+// the same time and share its lists in L2.  counts: scratch of K + 2 ints.  The order inside
+// one list's bucket is unspecified.
+void launch_query_order(const int32_t* probes, int64_t nq, int pstride, int K, int32_t* counts, int32_t* qorder,
+                        cudaStream_t s);
+// The scan sorts queries (launch_query_order) for batches of at least this many.
+#ifndef RBQ_QUERY_ORDER_MIN_BATCH
+#define RBQ_QUERY_ORDER_MIN_BATCH 2048
+#endif
+constexpr int64_t kQueryOrderMinBatch = RBQ_QUERY_ORDER_MIN_BATCH;
+#ifndef RBQ_SCAN_TILE
+#define RBQ_SCAN_TILE 1024
+#endif
+constexpr int kScanTile = RBQ_SCAN_TILE;  // vectors per scan tile (256 threads x tile / 256)
 void launch_scan(const ScanArgs& a, cudaStream_t s);
 // Phase-1 dump for one query and one list.
 void launch_list_estimates(const Index& ix, const uint32_t* planes, int qbits, float delta, float k1, float g,

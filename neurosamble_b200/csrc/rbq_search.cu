@@ -395,10 +395,14 @@ void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t, int qbits, 
 // The list scan (computeInnerProductsWithBitwiseBlockSort<4, false, false>,
 // searcher_gpu_quantize_query.cu:172-626, re-designed).  One CTA of 256 threads per
 // (query, probe slice).  The slice's lists form one flat sequence of vectors (probe order,
-// slot order inside a list) walked in tiles of kScanTile = 512 vectors that run across list
-// boundaries; thread t takes vectors t and t + 256 of each tile.
-//   phase 1 (per thread; query planes broadcast from shared memory, carry-save popcounts)
+// slot order inside a list) walked in tiles of kScanTile = 1024 vectors that run across list
+// boundaries; thread t takes vectors t, t + 256, t + 512 and t + 768 of each tile (tiles of 512
+// paid twice the barriers and threshold checks per vector; at 2048 the key buffers outgrow the
+// shared memory of six resident blocks).
+//   phase 1 (per thread; query planes broadcast from shared memory as 16-byte loads)
 //            acc = sum_w [sum_{b<3} popc(P_b & c) << b  -  popc(P_3 & c) << 3]   (exact int)
+//            summed by carry-save adders (two three-input logic ops each) and popcounts weighted
+//            by integer multiply-adds, which keeps the logic pipe for the adders
 //            est = (f_add + g) + f_rescale * (acc * delta + k1);  low = est - f_err * sqrt(g)
 //            admit if !prune || low < tau
 //   phase 2 (per warp)  right after each round of phase 1, the warp's admitted vectors are
@@ -473,17 +477,38 @@ __device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ code
 // a plane (and the carries of the plane below) collapse into one word per weight before any
 // popcount.  The integer result equals sum_w [sum_{b<3} popc(P_b & c) << b - popc(P_3 & c) << 3].
 // ---------------------------------------------------------------------------------------
+// Any three-input bitwise function in one instruction: LUT is its truth table over the inputs
+// a = 0xF0, b = 0xCC, c = 0xAA (PTX lop3.b32).
+template <unsigned LUT>
+__device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c)
+{
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+  return d;
+}
+// Full adder: carry = majority(a, b, c), sum = a ^ b ^ c; two instructions.
 __device__ __forceinline__ void csa(uint32_t& h, uint32_t& l, uint32_t a, uint32_t b, uint32_t c)
 {
-  const uint32_t u = a ^ b;
-  h = (a & b) | (u & c);
-  l = u ^ c;
+  h = lop3<0xE8>(a, b, c);
+  l = lop3<0x96>(a, b, c);
 }
 __device__ __forceinline__ void hadd(uint32_t& h, uint32_t& l, uint32_t a, uint32_t b)
 {
   h = a & b;
   l = a ^ b;
 }
+// Half adder of x and (p & c) with the AND folded in: carry x & p & c, sum x ^ (p & c).
+__device__ __forceinline__ void hadd_and(uint32_t& h, uint32_t& l, uint32_t x, uint32_t p, uint32_t c)
+{
+  h = lop3<0x80>(x, p, c);
+  l = lop3<0x78>(x, p, c);
+}
+
+// Weights of the popcounts of the adder outputs (weight 1, 2, 4, 8, 16, 32) and of plane 3 (-8).
+// Held in constant memory and never written, so the weighted sum compiles to integer
+// multiply-adds reading the weight from the constant bank (the multiply-add pipe), not to
+// shifts and adds on the integer logic pipe that the adders keep busy.
+__constant__ int32_t c_popc_weight[8] = {1, 2, 4, 8, 16, 32, -8, 0};
 
 // Eight words: P(b, w) returns plane b word w of the chunk, c the chunk's code words.
 template <typename PF>
@@ -532,33 +557,92 @@ __device__ __forceinline__ int32_t signed_dot8(const PF& P, const uint32_t (&c)[
   return pos - 8 * neg;
 }
 
+// The same eight-word sum with the plane words fetched as 16-byte groups G(b, h) (plane b,
+// words 4h..4h+3) in the order the adders consume them, so at most one group of plane words is
+// live at a time.
+template <typename GF>
+__device__ __forceinline__ int32_t signed_dot8_grouped(const GF& G, const uint32_t (&c)[8])
+{
+  uint4 g = G(0, 0);
+  uint32_t o1 = g.x & c[0], k0, k1, k2, k3;  // weight 1 (plane 0)
+  csa(k0, o1, o1, g.y & c[1], g.z & c[2]);
+  uint32_t t = g.w & c[3];
+  g = G(0, 1);
+  csa(k1, o1, o1, t, g.x & c[4]);
+  csa(k2, o1, o1, g.y & c[5], g.z & c[6]);
+  hadd_and(k3, o1, o1, g.w, c[7]);
+  g = G(1, 0);
+  uint32_t o2 = k0, m0, m1, m2, m3, m4, m5;  // weight 2 (carries + plane 1)
+  csa(m0, o2, o2, k1, k2);
+  csa(m1, o2, o2, k3, g.x & c[0]);
+  csa(m2, o2, o2, g.y & c[1], g.z & c[2]);
+  t = g.w & c[3];
+  g = G(1, 1);
+  csa(m3, o2, o2, t, g.x & c[4]);
+  csa(m4, o2, o2, g.y & c[5], g.z & c[6]);
+  hadd_and(m5, o2, o2, g.w, c[7]);
+  g = G(2, 0);
+  uint32_t o4 = m0, n0, n1, n2, n3, n4, n5, n6;  // weight 4 (carries + plane 2)
+  csa(n0, o4, o4, m1, m2);
+  csa(n1, o4, o4, m3, m4);
+  csa(n2, o4, o4, m5, g.x & c[0]);
+  csa(n3, o4, o4, g.y & c[1], g.z & c[2]);
+  t = g.w & c[3];
+  g = G(2, 1);
+  csa(n4, o4, o4, t, g.x & c[4]);
+  csa(n5, o4, o4, g.y & c[5], g.z & c[6]);
+  hadd_and(n6, o4, o4, g.w, c[7]);
+  uint32_t o8 = n0, r0, r1, r2;  // weight 8
+  csa(r0, o8, o8, n1, n2);
+  csa(r1, o8, o8, n3, n4);
+  csa(r2, o8, o8, n5, n6);
+  uint32_t o16 = r0, t0;  // weight 16, 32
+  csa(t0, o16, o16, r1, r2);
+  const int32_t* wt = c_popc_weight;
+  int32_t acc = __popc(o1) * wt[0];
+  acc = __popc(o2) * wt[1] + acc;
+  acc = __popc(o4) * wt[2] + acc;
+  acc = __popc(o8) * wt[3] + acc;
+  acc = __popc(o16) * wt[4] + acc;
+  acc = __popc(t0) * wt[5] + acc;
+  g = G(3, 0);  // plane 3 (weight -8): one popcount per word
+  acc = __popc(g.x & c[0]) * wt[6] + acc;
+  acc = __popc(g.y & c[1]) * wt[6] + acc;
+  acc = __popc(g.z & c[2]) * wt[6] + acc;
+  acc = __popc(g.w & c[3]) * wt[6] + acc;
+  g = G(3, 1);
+  acc = __popc(g.x & c[4]) * wt[6] + acc;
+  acc = __popc(g.y & c[5]) * wt[6] + acc;
+  acc = __popc(g.z & c[6]) * wt[6] + acc;
+  acc = __popc(g.w & c[7]) * wt[6] + acc;
+  return acc;
+}
+
 template <typename PF>
 __device__ __forceinline__ int32_t signed_dot4(const PF& P, const uint32_t (&c)[4])
 {
-  uint32_t a[4], b[4], d[4], e[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    a[w] = P(0, w) & c[w];
-    b[w] = P(1, w) & c[w];
-    d[w] = P(2, w) & c[w];
-    e[w] = P(3, w) & c[w];
-  }
-  uint32_t o1 = a[0], k0, k1;
-  csa(k0, o1, o1, a[1], a[2]);
-  hadd(k1, o1, o1, a[3]);
-  uint32_t o2 = k0, m0, m1, m2;
-  csa(m0, o2, o2, k1, b[0]);
-  csa(m1, o2, o2, b[1], b[2]);
-  hadd(m2, o2, o2, b[3]);
-  uint32_t o4 = m0, n0, n1, n2;
+  uint32_t o1 = P(0, 0) & c[0], k0, k1;  // weight 1 (plane 0)
+  csa(k0, o1, o1, P(0, 1) & c[1], P(0, 2) & c[2]);
+  hadd_and(k1, o1, o1, P(0, 3), c[3]);
+  uint32_t o2 = k0, m0, m1, m2;  // weight 2 (carries + plane 1)
+  csa(m0, o2, o2, k1, P(1, 0) & c[0]);
+  csa(m1, o2, o2, P(1, 1) & c[1], P(1, 2) & c[2]);
+  hadd_and(m2, o2, o2, P(1, 3), c[3]);
+  uint32_t o4 = m0, n0, n1, n2;  // weight 4 (carries + plane 2)
   csa(n0, o4, o4, m1, m2);
-  csa(n1, o4, o4, d[0], d[1]);
-  csa(n2, o4, o4, d[2], d[3]);
-  uint32_t o8 = n0, r0;
+  csa(n1, o4, o4, P(2, 0) & c[0], P(2, 1) & c[1]);
+  csa(n2, o4, o4, P(2, 2) & c[2], P(2, 3) & c[3]);
+  uint32_t o8 = n0, r0;  // weight 8, 16
   csa(r0, o8, o8, n1, n2);
-  const int32_t pos = __popc(o1) + 2 * __popc(o2) + 4 * __popc(o4) + 8 * __popc(o8) + 16 * __popc(r0);
-  const int32_t neg = __popc(e[0]) + __popc(e[1]) + __popc(e[2]) + __popc(e[3]);
-  return pos - 8 * neg;
+  const int32_t* wt = c_popc_weight;
+  int32_t acc = __popc(o1) * wt[0];
+  acc = __popc(o2) * wt[1] + acc;
+  acc = __popc(o4) * wt[2] + acc;
+  acc = __popc(o8) * wt[3] + acc;
+  acc = __popc(r0) * wt[4] + acc;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) acc = __popc(P(3, w) & c[w]) * wt[6] + acc;  // plane 3 (weight -8)
+  return acc;
 }
 
 // Whole vector: chunks of 8 words (or one 4-word chunk), else one popcount per plane word.
@@ -601,6 +685,46 @@ __device__ __forceinline__ int32_t signed_dot(const PF& P, const uint32_t (&c)[W
     }
     return s0 + 2 * s1 + 4 * s2 - 8 * s3;
   }
+}
+
+// The query's planes live at the start of the scan's shared memory (16-byte aligned), so when
+// W % 4 == 0 each group of four plane words is one 16-byte shared load instead of four.
+template <int W, int QB>
+__device__ __forceinline__ int32_t dot_smem(const uint32_t* __restrict__ pl, const uint32_t (&c)[W])
+{
+  if constexpr (QB == 4 && W == 8) {
+    int32_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < W / 8; ++k) {
+      uint32_t cc[8];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) cc[w] = c[8 * k + w];
+      auto G = [&](int b, int h) -> uint4 { return reinterpret_cast<const uint4*>(pl + b * W + 8 * k)[h]; };
+      acc += signed_dot8_grouped(G, cc);
+    }
+    return acc;
+  } else if constexpr (QB == 4 && W == 4) {
+    const uint4 g0 = reinterpret_cast<const uint4*>(pl)[0], g1 = reinterpret_cast<const uint4*>(pl)[1];
+    const uint4 g2 = reinterpret_cast<const uint4*>(pl)[2], g3 = reinterpret_cast<const uint4*>(pl)[3];
+    auto P = [&](int b, int w) -> uint32_t {
+      const uint4& v = b == 0 ? g0 : (b == 1 ? g1 : (b == 2 ? g2 : g3));
+      return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+    };
+    return signed_dot4(P, c);
+  } else {
+    auto P = [&](int b, int w) -> uint32_t { return pl[b * W + w]; };
+    return signed_dot<W, QB>(P, c);
+  }
+}
+
+// acc of the vector at `slot`.
+template <int W, int QB>
+__device__ __forceinline__ int32_t dot_vector(const uint32_t* __restrict__ codes, int64_t slot,
+                                              const uint32_t* __restrict__ pl)
+{
+  uint32_t c[W];
+  load_code<W>(codes, slot, c);
+  return dot_smem<W, QB>(pl, c);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -679,12 +803,15 @@ __device__ unsigned long long block_keep_smallest(const unsigned long long* src,
   return *kmax;
 }
 
+#ifndef RBQ_SCAN_MINB8
+#define RBQ_SCAN_MINB8 6
+#endif
 // Resident CTAs per SM the scan is compiled for: occupancy hides the L2 latency of the code
 // loads, so vectors up to 256 dims get 6 CTAs (40 registers, no spill); wider ones 4.
 template <int W>
 constexpr int scan_min_blocks()
 {
-  return W <= 8 ? 6 : 4;
+  return (W <= 4 || W == 8) ? RBQ_SCAN_MINB8 : (W < 8 ? 5 : 4);
 }
 
 template <int W, int QB>
@@ -692,21 +819,23 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
 {
   constexpr int NB = 4 * W;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);  // [cap]
+  // planes first (16-byte aligned); QB*W + 8*NB words = 4W(QB + 32) bytes keep the keys 8-aligned
+  uint32_t* pl = reinterpret_cast<uint32_t*>(smem_raw);                        // [QB * W]
+  float* qsT = reinterpret_cast<float*>(pl + QB * W);                           // [8 * NB]
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(qsT + 8 * NB);  // [cap]
   unsigned long long* keys2 = keys + a.cap;                                    // [cap]
   int* pre = reinterpret_cast<int*>(keys2 + a.cap);                            // [nprobe + 1]
   int* lbase = pre + (a.nprobe + 1);                                            // [nprobe]
   float* lg = reinterpret_cast<float*>(lbase + a.nprobe);                       // [nprobe]
   float* lsq = lg + a.nprobe;                                                   // [nprobe]
-  uint32_t* pl = reinterpret_cast<uint32_t*>(lsq + a.nprobe);                  // [QB * W]
-  float* qsT = reinterpret_cast<float*>(pl + QB * W);                           // [8 * NB]
   __shared__ int s_count, s_nl, s_misc[3], s_cnt2;
   __shared__ float s_tau;
   __shared__ unsigned s_hist[256];
   __shared__ unsigned long long s_kmax;
 
-  const int64_t q = blockIdx.x / a.slices;
-  const int slice = blockIdx.x - (int)(q * a.slices);
+  const int64_t qi = blockIdx.x / a.slices;
+  const int slice = blockIdx.x - (int)(qi * a.slices);
+  const int64_t q = a.qorder ? (int64_t)a.qorder[qi] : qi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   for (int i = tid; i < 8 * NB; i += kScanThreads) {
@@ -789,7 +918,6 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const int total = pre[nl];
   const float delta = a.delta[q];
   const float k1 = a.k1[q];
-  auto P = [&](int b, int w) -> uint32_t { return pl[b * W + w]; };  // shared-memory broadcast
   // Bound seed: a pruning slice with no threshold and no candidates yet starts from the R-th
   // smallest upper bound est + f_err * sqrt(g) over its leading whole lists holding at least R
   // vectors (the RaBitQ error bound: R of them are that close), instead of admitting its first
@@ -804,9 +932,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       for (int f = c0 + tid; f < c1; f += kScanThreads) {
         while (pre[c + 1] <= f) ++c;
         const int slot = lbase[c] + (f - pre[c]);
-        uint32_t cw[W];
-        load_code<W>(a.codes, slot, cw);
-        const int32_t acc = signed_dot<W, QB>(P, cw);
+        const int32_t acc = dot_vector<W, QB>(a.codes, slot, pl);
         const float base_d = __fadd_rn(__ldg(a.fadd + slot), lg[c]);
         const float ip = __fmul_rn((float)acc, delta);
         const float est = __fadd_rn(base_d, __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(ip, k1)));
@@ -830,7 +956,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     if (tid == 0) a.tau_out[q] = s_tau;
     return;
   }
-  unsigned n_scan = 0, n_admit = 0;
+  unsigned n_admit = 0;
   // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
   int cur = 0;
   int nxt = nl > 0 ? pre[1] : 0;
@@ -856,15 +982,12 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
           sqc = lsq[cur];
         }
         const int slot = sadj + f;
-        uint32_t c[W];
-        load_code<W>(a.codes, slot, c);
-        const int32_t acc = signed_dot<W, QB>(P, c);
+        const int32_t acc = dot_vector<W, QB>(a.codes, slot, pl);
         const float fr = __ldg(a.frescale + slot);
         const float base_d = __fadd_rn(__ldg(a.fadd + slot), gc);
         const float ip = __fmul_rn((float)acc, delta);
         const float est = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(ip, k1)));
         const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
-        ++n_scan;
         if (!a.prune || low < tau) {
           ++n_admit;
           surv = true;
@@ -919,16 +1042,11 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   block_bitonic_sort(keys, r2);
   unsigned long long* out = a.out_keys + ((size_t)q * a.slices + slice) * a.R;
   for (int i = tid; i < a.R; i += kScanThreads) out[i] = i < cnt ? keys[i] : kEmptyKey;
-  if (a.stats) {
-    unsigned long long s0 = n_scan, s1 = n_admit;
-    for (int off = 16; off; off >>= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-    }
-    if (lane == 0) {
-      atomicAdd(a.stats + 0, s0);
-      atomicAdd(a.stats + 1, s1);
-    }
+  if (a.stats) {  // every vector of the slice is scanned once: the block adds `total`
+    unsigned long long s1 = n_admit;
+    for (int off = 16; off; off >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+    if (lane == 0) atomicAdd(a.stats + 1, s1);
+    if (tid == 0) atomicAdd(a.stats + 0, (unsigned long long)total);
   }
 }
 
@@ -983,6 +1101,71 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
     case 32: launch_scan_w<32>(a, s); break;
     default: throw Error{RBQ_ERR_INVALID, "scan: unsupported padded dimension"};
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// Query visiting order for the scan: a counting sort of the queries by their nearest probe.
+// counts[l] (l < K) counts queries whose nearest list is l, counts[K] those without a probe;
+// an exclusive prefix sum turns the counts into bucket starts, and the scatter hands out slots
+// inside a bucket in arrival order.
+// ---------------------------------------------------------------------------------------
+__global__ void query_order_hist_kernel(const int32_t* __restrict__ probes, int64_t nq, int pstride, int K,
+                                        int32_t* __restrict__ counts)
+{
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const int32_t l = probes[q * pstride];
+  atomicAdd(counts + (l >= 0 && l < K ? l : K), 1);
+}
+
+// Exclusive prefix sum of counts[0..n) in place, one block of 1024 threads: each thread sums a
+// contiguous run, a block scan of the run totals gives each run's start.
+__global__ void __launch_bounds__(1024) exclusive_scan_kernel(int32_t* __restrict__ counts, int n)
+{
+  __shared__ int32_t s_tot[1024];
+  const int t = threadIdx.x;
+  const int per = (n + 1023) / 1024;
+  const int b = min(n, t * per), e = min(n, b + per);
+  int32_t sum = 0;
+  for (int i = b; i < e; ++i) sum += counts[i];
+  s_tot[t] = sum;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int32_t v = t >= off ? s_tot[t - off] : 0;
+    __syncthreads();
+    s_tot[t] += v;
+    __syncthreads();
+  }
+  int32_t run = s_tot[t] - sum;
+  for (int i = b; i < e; ++i) {
+    const int32_t c = counts[i];
+    counts[i] = run;
+    run += c;
+  }
+}
+
+__global__ void query_order_scatter_kernel(const int32_t* __restrict__ probes, int64_t nq, int pstride, int K,
+                                           int32_t* __restrict__ starts, int32_t* __restrict__ qorder)
+{
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const int32_t l = probes[q * pstride];
+  qorder[atomicAdd(starts + (l >= 0 && l < K ? l : K), 1)] = (int32_t)q;
+}
+
+void launch_query_order(const int32_t* probes, int64_t nq, int pstride, int K, int32_t* counts, int32_t* qorder,
+                        cudaStream_t s)
+{
+  if (nq <= 0) return;
+  RBQ_CHECK(nq < 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "query order: bad sizes");
+  RBQ_CUDA(cudaMemsetAsync(counts, 0, (size_t)(K + 1) * sizeof(int32_t), s));
+  const unsigned grid = (unsigned)ceil_div(nq, 256);
+  query_order_hist_kernel<<<grid, 256, 0, s>>>(probes, nq, pstride, K, counts);
+  RBQ_LAUNCHED();
+  exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, K + 1);
+  RBQ_LAUNCHED();
+  query_order_scatter_kernel<<<grid, 256, 0, s>>>(probes, nq, pstride, K, counts, qorder);
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------

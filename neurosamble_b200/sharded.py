@@ -31,7 +31,7 @@ import torch.distributed as dist
 from . import _lib
 from .index import IndexIVFRaBitQ, _ptr, _stream_ptr
 
-SCAN_TILE = 512  # vectors per scan tile (kScanTile in the library)
+SCAN_TILE = _lib.lib().rbq_scan_tile()  # vectors per scan tile (kScanTile in the library)
 
 
 def _pow2(v: int) -> int:

@@ -86,9 +86,9 @@ def pad_dim(d: int) -> int:
     return (d + 31) // 32 * 32
 
 
-# Scan schedule constants shared with the CUDA library: vectors per tile (256 threads x 2
+# Scan schedule constants shared with the CUDA library: vectors per tile (256 threads x 4
 # vectors) and the candidate-buffer size rule cap = max(pow2(cand_cap or 1024), pow2(R + tile)).
-SCAN_TILE = 512
+SCAN_TILE = 1024
 
 
 def _pow2(v: int) -> int:

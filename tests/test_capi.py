@@ -99,3 +99,12 @@ def test_parameter_defaults():
     sp = _lib.SearchParams()
     L.rbq_search_params_default(ctypes.byref(sp))
     assert (sp.n_probes, sp.k, sp.rerank, sp.prune, sp.seeded, sp.query_bits, sp.graph) == (20, 10, 0, 1, -1, 4, 0)
+
+
+def test_scan_tile_is_one_constant():
+    """The scan tile decides when the prune threshold tightens and how large candidate buffers
+    are; the library, the oracle and the sharded planner must use the same value."""
+    from neurosamble_b200 import _lib, sharded
+    from oracle import oracle as O
+    t = _lib.lib().rbq_scan_tile()
+    assert t == O.SCAN_TILE == sharded.SCAN_TILE == 1024
