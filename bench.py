@@ -33,6 +33,9 @@ CFG = dict(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05,
            rerank=100, seed=2024, config=2, aniso=0, device_data=False, gt_sample=10_000)
 CONFIGS = {
     2: CFG,
+    3: dict(n=200_000, d=256, centres=0, sigma=0.0, nq=200_000, qsigma=0.0, nlist=2048, nprobe=48, k=20,
+            rerank=200, seed=3003, config=3, aniso=0, device_data=True, gt_sample=10_000, generator="reads",
+            genome_len=10_000_000, read_len=5000),
     4: dict(n=100_000_000, d=128, centres=65536, sigma=0.3, nq=100_000, qsigma=0.05, nlist=65536, nprobe=64,
             k=100, rerank=400, seed=4004, config=4, aniso=0, device_data=True, gt_sample=1000),
     5: dict(n=20_000_000, d=768, centres=16384, sigma=0.2, nq=50_000, qsigma=0.05, nlist=16384, nprobe=128,
@@ -82,6 +85,22 @@ def make_data_device(cfg, dev):
     _lib.call("rbq_gen_queries", _ptr(X), n, d, _ptr(Q), nq, cfg["qsigma"], 1, cfg["seed"] + 1, None, st)
     torch.cuda.synchronize(dev)
     return X, Q
+
+
+def make_data_reads(cfg, dev, rank=0, world=1):
+    """Config 3: embeddings of simulated reads (bench_reads.make_read_embeddings); each rank
+    encodes its share of the read batches and a sum all-reduce assembles the whole set (rows
+    of other ranks' batches are zero).  The queries are the reads themselves."""
+    import torch
+
+    import bench_reads
+    X, _, _ = bench_reads.make_read_embeddings(cfg["n"], cfg["read_len"], cfg["genome_len"], cfg["seed"], dev,
+                                               d=cfg["d"], rank=rank, world=world, log=log)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.all_reduce(X, op=tdist.ReduceOp.SUM)
+    torch.cuda.synchronize(dev)
+    return X, X[:cfg["nq"]]
 
 
 def exact_knn_device(Xd, Qs, k, rows=1 << 20, qblock=1000):
@@ -230,7 +249,14 @@ def run_reference(args, cfg):
     if rank != 0:
         return 0
     from oracle import oracle as O
-    X, Q = make_data(cfg)
+    if cfg.get("generator") == "reads":  # the inputs come from the signal encoder (GPU); not timed
+        import torch
+        Xd, _ = make_data_reads(cfg, torch.device("cuda:0"))
+        X = Xd.cpu().numpy()
+        Q = X[:cfg["nq"]]
+        del Xd
+    else:
+        X, Q = make_data(cfg)
     dp = O.pad_dim(cfg["d"])
     P = O.make_rotation(dp, 7)
     t4 = O.query_scale(dp, 7)
@@ -272,13 +298,19 @@ def run_reference(args, cfg):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 * cfg["nq"] / value, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32+u32",
-            "data": f"synthetic (seeded Gaussian mixture, BASELINE config {cfg['config']})",
+            "data": data_label(cfg),
             "config": dict(workload(cfg, R, args.kmeans), recall_by_rerank_sample=recalls),
             "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
                              "sample": f"{n_sample} of {cfg['nq']} queries per step, same index and parameters"},
             "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def data_label(cfg):
+    if cfg.get("generator") == "reads":
+        return "synthetic (simulated reads embedded by a seeded random-init signal encoder, BASELINE config 3)"
+    return f"synthetic (seeded Gaussian mixture, BASELINE config {cfg['config']})"
 
 
 def _count(n):
@@ -291,6 +323,17 @@ def metric_name(cfg):
 
 
 def workload(cfg, R, kmeans):
+    if cfg.get("generator") == "reads":
+        return {"workload": (f"BASELINE config 3: read-overlap retrieval, {cfg['n']} simulated reads of "
+                             f"{cfg['read_len']} bp from a seeded {cfg['genome_len'] // 1_000_000} Mbp genome (50% "
+                             "reverse-complemented, 8% errors 4:2:2 sub:ins:del), synthetic 6-mer pore-model signal, "
+                             "2000/1000 windows, seeded random-init signal encoder (d 256) under fp16 autocast, "
+                             "mean-pooled per read, L2-normalised, fp16 -> fp32; the read set queried against itself; "
+                             f"IVF-RaBitQ 1-bit codes, {cfg.get('query_bits', 4)}-bit queries; data generated on the "
+                             "device"),
+                "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
+                "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
+                "kmeans": kmeans, "search_mode": "QUANT8" if cfg.get("query_bits", 4) == 8 else "QUANT4"}
     return {"workload": (f"BASELINE config {cfg['config']}: {_count(cfg['n'])} x {cfg['d']} f32, "
                          f"{cfg['centres']}-centre {'anisotropic ' if cfg['aniso'] else ''}mixture sigma "
                          f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ 1-bit "
@@ -329,7 +372,11 @@ def run_ours(args, cfg):
         from datetime import timedelta
         tdist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     t = time.perf_counter()
-    if cfg["device_data"]:
+    if cfg.get("generator") == "reads":
+        Xd, Qd = make_data_reads(cfg, dev, rank, world)
+        X = Xd.cpu().numpy()
+        Q = X[:cfg["nq"]]
+    elif cfg["device_data"]:
         X = None
         Xd, Qd = make_data_device(cfg, dev)
         Q = Qd.cpu().numpy()
@@ -526,7 +573,7 @@ def run_ours(args, cfg):
         line = {"metric": metric_name(cfg), "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes x 4-bit planes (popc) + f32",
-                "data": f"synthetic (seeded Gaussian mixture, BASELINE config {cfg['config']})",
+                "data": data_label(cfg),
                 "config": dict(workload(cfg, R, args.kmeans),
                                parallelism=(f"lists sharded over {world} GPUs (balanced by size^2)" if world > 1
                                             else "1 GPU"),
@@ -713,7 +760,8 @@ def main():
     ap.add_argument("--query-bits", type=int, default=4, choices=[4, 8],
                     help="query code width of both arms: 4 (QUANT4, the reference CLI's default) or 8 (QUANT8)")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
-                    help="benchmark configuration (2: the metric's; 4 / 5: supplementary, data on the device)")
+                    help="benchmark configuration (2: the metric's; 3: read overlap; 4 / 5: supplementary, data on "
+                         "the device)")
     ap.add_argument("--seeded", type=int, default=-1, choices=[-1, 0, 1],
                     help="1 GPU: two-phase scan seeded by the nearest list (-1: the library's auto rule)")
     args = ap.parse_args()
@@ -726,7 +774,7 @@ def main():
     if args.nq:
         cfg["nq"] = args.nq
     if args.impl == "reference":
-        if cfg["device_data"]:
+        if cfg["device_data"] and cfg.get("generator") != "reads":
             if int(os.environ.get("RANK", "0")) == 0:
                 print(json.dumps({"impl": "reference", "unavailable": f"config {args.config}: the CPU port needs "
                                   "the whole raw store and a CPU-built index on the host; run at config 2"}))
