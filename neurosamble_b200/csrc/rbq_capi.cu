@@ -163,14 +163,17 @@ void install_centroids(Index& ix, cudaStream_t s)
   dev_free(ix.C);
   dev_free(ix.C_rot);
   dev_free(ix.C_rot_n2);
+  dev_free(ix.C_rot_n2_max);
   dev_free(ix.C_n2);
   ix.C = dev_alloc<float>((size_t)ix.K * ix.D);
   ix.C_rot = dev_alloc<float>((size_t)ix.K * ix.Dp);
   ix.C_rot_n2 = dev_alloc<float>(ix.K);
+  ix.C_rot_n2_max = dev_alloc<float>(1);
   ix.C_n2 = dev_alloc<float>(ix.K);
   RBQ_CUDA(cudaMemcpyAsync(ix.C, ix.C_host.data(), ix.C_host.size() * 4, cudaMemcpyHostToDevice, s));
   launch_rotate(ix.C, ix.K, ix.D, ix.Dp, ix.P, ix.C_rot, s);
   launch_row_norms(ix.C_rot, ix.K, ix.Dp, ix.C_rot_n2, s);
+  launch_max_reduce(ix.C_rot_n2, ix.K, ix.C_rot_n2_max, s);
   launch_row_norms(ix.C, ix.K, ix.D, ix.C_n2, s);
   RBQ_CUDA(cudaStreamSynchronize(s));
   ix.trained = true;
@@ -179,27 +182,51 @@ void install_centroids(Index& ix, cudaStream_t s)
 // Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d]: approximate
 // shortlist (tcgen05 tf32 scores when d is a multiple of 32 and the rows are 16-byte aligned,
 // else fp32 SIMT), then the double-accumulated distance over the shortlist decides.
+}  // namespace
+
+// Exact top-p probes of rows A [n, d] among C [K, d] (double distances, ties to the lower id):
+// approximate scores (tcgen05 tf32 when d is a multiple of 32 and the operands are 16-byte
+// aligned, else fp32 SIMT) shortlist the m best per row, the exact distance over the shortlist
+// decides, and rows whose shortlist the score error bound cannot vouch for (the m-th shortlisted
+// score is not clear of the p-th by twice the bound) are recomputed over all K lists.  Scratch:
+// S [n, K], cand [n, m], bounds [n], unsafe [1 + n]; cmax2 = max_l |c_l|^2 (device scalar).
+void coarse_probes(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, const float* cmax2,
+                   int K, int d, int m, int p, float* S, int32_t* cand, float2* bounds, int* unsafe, int32_t* probes,
+                   float* g, cudaStream_t s)
+{
+  if (n <= 0) return;
+  RBQ_CUDA(cudaMemsetAsync(unsafe, 0, sizeof(int), s));
+  if (coarse_tc_supported(d) && d % 32 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(C) & 15u) == 0)
+    launch_coarse_scores_tc(A, n, C, cn2, K, d, S, ix.dev_err, s);
+  else
+    launch_coarse_scores(A, n, C, cn2, K, d, S, s);
+  launch_topm_rows(S, n, K, m, cand, s, p, bounds);
+  launch_refine_topp(A, n, C, d, cand, m, p, probes, g, s, bounds, cmax2, unsafe);
+  launch_refine_all(A, n, C, d, K, p, unsafe, probes, g, s);
+}
+
+namespace {
+
+// Exact nearest centroid (ties -> lower id) of rows A [n, d] among C [K, d] (coarse_probes with
+// p = 1 over a shortlist of 32).
 void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, int K, int d,
                    uint32_t* labels_out, cudaStream_t s)
 {
-  const int m = std::min(K, 32);  // shortlist width: far beyond the tf32 ranking error
+  const int m = std::min(K, 32);
   const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65535 * 64, (256ll << 20) / ((int64_t)K * 4)));
   Scratch sc(s);
   const int64_t c0 = std::min(n, chunk);
   float* S = sc.get<float>((size_t)c0 * K);
   int32_t* cand = sc.get<int32_t>((size_t)c0 * m);
-  int32_t* best = sc.get<int32_t>((size_t)c0);
+  float2* bounds = sc.get<float2>((size_t)c0);
+  int* unsafe = sc.get<int>((size_t)c0 + 1);
+  float* cmax2 = sc.get<float>(1);
+  launch_max_reduce(cn2, K, cmax2, s);
   for (int64_t a = 0; a < n; a += chunk) {
     const int64_t cn = std::min(chunk, n - a);
-    const float* Aa = A + a * d;
-    if (coarse_tc_supported(d) && d % 32 == 0 && (reinterpret_cast<uintptr_t>(Aa) & 15u) == 0 &&
-        (reinterpret_cast<uintptr_t>(C) & 15u) == 0)
-      launch_coarse_scores_tc(Aa, cn, C, cn2, K, d, S, ix.dev_err, s);
-    else
-      launch_coarse_scores(Aa, cn, C, cn2, K, d, S, s);
-    launch_topm_rows(S, cn, K, m, cand, s);
-    launch_refine_topp(A + a * d, cn, C, d, cand, m, 1, best, nullptr, s);
-    RBQ_CUDA(cudaMemcpyAsync(labels_out + a, best, cn * 4, cudaMemcpyDeviceToDevice, s));
+    coarse_probes(ix, A + a * d, cn, C, cn2, cmax2, K, d, m, 1, S, cand, bounds, unsafe,
+                  reinterpret_cast<int32_t*>(labels_out + a), nullptr, s);
   }
 }
 
@@ -738,6 +765,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   float* Qr_buf = Qr_pre ? nullptr : sc.get<float>((size_t)chunk * ix.Dp);
   float* S = sc.get<float>((size_t)fe_chunk * ix.K);
   int32_t* cand = sc.get<int32_t>((size_t)fe_chunk * sp.m);
+  float2* bounds = sc.get<float2>((size_t)fe_chunk);
+  int* unsafe = sc.get<int>((size_t)fe_chunk + 1);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
   float* g = sc.get<float>((size_t)chunk * sp.P);
   uint32_t* planes = sc.get<uint32_t>((size_t)chunk * sp.qbits * ix.W);
@@ -757,9 +786,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       const int64_t fn = std::min(fe_chunk, cn - b);
       const float* Qrb = Qr + b * ix.Dp;
       if (!Qr_pre) launch_rotate(Qc + b * ix.D, fn, ix.D, ix.Dp, ix.P, Qr_buf + b * ix.Dp, s);
-      launch_coarse_scores_tc(Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
-      launch_topm_rows(S, fn, ix.K, sp.m, cand, s);
-      launch_refine_topp(Qrb, fn, ix.C_rot, ix.Dp, cand, sp.m, sp.P, probes + b * sp.P, g + b * sp.P, s);
+      coarse_probes(ix, Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, sp.m, sp.P, S, cand, bounds,
+                    unsafe, probes + b * sp.P, g + b * sp.P, s);
     }
     launch_query_prep(Qr, cn, ix.Dp, qt, sp.qbits, planes, delta, k1, s);
     {
@@ -980,6 +1008,7 @@ void free_index_memory(Index& ix)
   dev_free(ix.C);
   dev_free(ix.C_rot);
   dev_free(ix.C_rot_n2);
+  dev_free(ix.C_rot_n2_max);
   dev_free(ix.C_n2);
   dev_free(ix.X_r);
   dev_free(ix.codes_r);
@@ -1570,6 +1599,7 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
       install_centroids(ix, 0);
       RBQ_CUDA(cudaMemcpy(ix.C_rot, r.Crot.data(), r.Crot.size() * 4, cudaMemcpyHostToDevice));
       launch_row_norms(ix.C_rot, K, Dp, ix.C_rot_n2, 0);
+      launch_max_reduce(ix.C_rot_n2, K, ix.C_rot_n2_max, 0);
       RBQ_CUDA(cudaDeviceSynchronize());
       // owners from the file's cluster sizes; rows of owned clusters, in ascending id
       std::vector<int64_t> sizes(r.sizes.begin(), r.sizes.end());
@@ -1785,12 +1815,12 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
     Scratch sc(s);
     float* S = sc.get<float>((size_t)chunk * ix.K);
     int32_t* cand = sc.get<int32_t>((size_t)chunk * m);
+    float2* bounds = sc.get<float2>((size_t)chunk);
+    int* unsafe = sc.get<int>((size_t)chunk + 1);
     for (int64_t a = 0; a < nq; a += chunk) {
       const int64_t cn = std::min(chunk, nq - a);
-      launch_coarse_scores_tc(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.K, ix.Dp, S, ix.dev_err, s);
-      launch_topm_rows(S, cn, ix.K, m, cand, s);
-      launch_refine_topp(Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.Dp, cand, m, nprobe, probes_dev + a * nprobe,
-                         g_dev + a * nprobe, s);
+      coarse_probes(ix, Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, m, nprobe, S,
+                    cand, bounds, unsafe, probes_dev + a * nprobe, g_dev + a * nprobe, s);
     }
   });
 }

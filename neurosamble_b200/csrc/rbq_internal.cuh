@@ -110,6 +110,7 @@ struct Index {
   float* C = nullptr;          // [K*D]
   float* C_rot = nullptr;      // [K*Dp]
   float* C_rot_n2 = nullptr;   // [K] |c_rot|^2 (float, for the approximate coarse pass)
+  float* C_rot_n2_max = nullptr;  // device scalar: max of C_rot_n2 (error bound of the coarse shortlist)
   float* C_n2 = nullptr;       // [K] |c|^2 (original space, for assignment)
 
   // Row order: append-only storage of this shard's vectors, in the order they were added.
@@ -183,11 +184,22 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
                              int* err, cudaStream_t s);
 void launch_coarse_scores(const float* A, int64_t nq, const float* C, const float* c_n2, int K, int d,
                           float* S, cudaStream_t s);
-// Per row of S [nq, K]: top-m (score, id) keys ascending -> cand [nq, m].
-void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s);
-// Exact refine: g = sum_j double(a_j - c_j)^2 for the m candidates, then top-p by (g, id).
+// Per row of S [nq, K]: the m smallest (score, id) keys -> cand [nq, m] (any order).  With
+// bounds, also (p-th smallest score, m-th smallest score) per row (+inf when all K are kept).
+void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s, int p = 0,
+                      float2* bounds = nullptr);
+// Exact refine: g = sum_j double(a_j - c_j)^2 for the m candidates, then top-p by (g, id).  With
+// bounds (from launch_topm_rows), cmax2 (max |c|^2, device scalar) and unsafe ([1 + nq] ints,
+// unsafe[0] = 0 on entry), queries whose shortlist may miss a true top-p list under the tf32
+// error bound are appended to unsafe.
 void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m,
-                        int p, int32_t* probes, float* g, cudaStream_t s);
+                        int p, int32_t* probes, float* g, cudaStream_t s, const float2* bounds = nullptr,
+                        const float* cmax2 = nullptr, int* unsafe = nullptr);
+// Exact top-p over all K lists for the queries queued in unsafe; overwrites their probes / g.
+void launch_refine_all(const float* A, int64_t nq, const float* C, int d, int K, int p, const int* unsafe,
+                       int32_t* probes, float* g, cudaStream_t s);
+// *out = max of v[0..n).
+void launch_max_reduce(const float* v, int n, float* out, cudaStream_t s);
 // B-bit query planes (B = qbits: 4 for QUANT4, 8 for QUANT8; planes [nq, B, W]), delta and k1;
 // t is the index's scale constant for that width (t4 or t8).
 void launch_query_prep(const float* Qr, int64_t nq, int Dp, float t, int qbits, uint32_t* planes, float* delta,

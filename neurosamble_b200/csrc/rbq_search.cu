@@ -119,7 +119,7 @@ __device__ unsigned long long block_keep_smallest(const unsigned long long* src,
 
 template <int KPER>
 __global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict__ S, int K, int m, int buf,
-                                                        int32_t* __restrict__ cand)
+                                                        int32_t* __restrict__ cand, int p, float2* __restrict__ bounds)
 {
   extern __shared__ unsigned long long tk[];  // [2 * buf], buf >= m + 256 * KPER
   __shared__ unsigned s_hist[256];
@@ -133,11 +133,13 @@ __global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict_
   const int step = 256 * KPER;
   unsigned long long thr = kEmptyKey;  // the m-th smallest key kept so far (none: all ones)
   int filled = 0;                      // keys at the front of `cur`
+  bool cut = false;                    // a selection has run (thr is the m-th smallest so far)
   if (threadIdx.x == 0) s_fill = 0;
   __syncthreads();
   for (int c0 = 0; c0 < K; c0 += step) {
     if (filled + step > buf) {  // block-uniform; filled > m here because buf >= m + step
       thr = block_keep_smallest(cur, filled, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+      cut = true;
       unsigned long long* t = cur;
       cur = nxt;
       nxt = t;
@@ -167,16 +169,30 @@ __global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict_
     __syncthreads();  // every thread has read s_fill before the next round appends
   }
   if (filled > m) {
-    block_keep_smallest(cur, filled, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+    thr = block_keep_smallest(cur, filled, m, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+    cut = true;
+    unsigned long long* t = cur;
     cur = nxt;
+    nxt = t;
     filled = m;
     __syncthreads();
   }
   for (int i = threadIdx.x; i < m; i += blockDim.x)
     cand[q * m + i] = i < filled ? (int32_t)(cur[i] & 0xFFFFFFFFu) : -1;
+  if (bounds) {  // (p-th smallest score, m-th smallest score; +inf when every column is kept)
+    __syncthreads();
+    float sp = __int_as_float(0x7f800000);
+    if (filled >= p && p >= 1) {
+      const unsigned long long kp = block_keep_smallest(cur, filled, p, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+      sp = from_ordered_bits((uint32_t)(kp >> 32));
+    }
+    if (threadIdx.x == 0)
+      bounds[q] = make_float2(sp, cut ? from_ordered_bits((uint32_t)(thr >> 32)) : __int_as_float(0x7f800000));
+  }
 }
 
-void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s)
+void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s, int p,
+                      float2* bounds)
 {
   if (nq <= 0) return;
   RBQ_CHECK(m >= 1 && m <= kTopmChunk / 2, RBQ_ERR_INVALID, "coarse: shortlist size out of range");
@@ -184,13 +200,13 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
     const int buf = kTopmChunk;
     const size_t smem = (size_t)buf * 2 * 8;
     RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    topm_rows_kernel<8><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+    topm_rows_kernel<8><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand, p, bounds);
   } else {  // rows of up to 4096 keys: 1024 a round, so K <= 1024 is one fill and one selection
     const int buf = std::max(std::max(2 * m, K), m + 1024);
     const size_t smem = (size_t)buf * 2 * 8;
     if (smem > 48 * 1024)
       RBQ_CUDA(cudaFuncSetAttribute(topm_rows_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    topm_rows_kernel<4><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand);
+    topm_rows_kernel<4><<<(unsigned)nq, 256, smem, s>>>(S, K, m, buf, cand, p, bounds);
   }
   RBQ_LAUNCHED();
 }
@@ -202,11 +218,22 @@ void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, c
 // One CTA per query, one warp per candidate; with d = 32 * EPL the warp loads all EPL values
 // of two candidates before the arithmetic (EPL = 0: the generic loop for other d).
 // ---------------------------------------------------------------------------------------
+// Bound on |tf32 score - exact score| for a query of squared norm qn2 against centroids of
+// squared norm <= cmax2: the tensor core truncates each operand to tf32 (relative error 2^-10
+// each, so 2^-9 per product), adds d products in fp32, and the score is |c|^2 - 2 <q, c>.  Twice
+// that estimate, plus an absolute term for the float rounding of the exact distances.
+__device__ __forceinline__ float tf32_score_bound(float qn2, float cmax2, int d)
+{
+  const float rel = 0.0078125f + (float)d * 4.76837158e-7f;  // 2^-7 + d * 2^-21
+  return rel * sqrtf(qn2 * cmax2) + 1.90734863e-6f * (qn2 + cmax2);  // + 2^-19 (|q|^2 + |c|^2)
+}
+
 template <int EPL>
 __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restrict__ A, const float* __restrict__ C,
                                                           int d, const int32_t* __restrict__ cand, int m, int p,
                                                           int mp2, int32_t* __restrict__ probes,
-                                                          float* __restrict__ gout)
+                                                          float* __restrict__ gout, const float2* __restrict__ bounds,
+                                                          const float* __restrict__ cmax2, int* __restrict__ unsafe)
 {
   extern __shared__ unsigned char smem_raw[];
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);
@@ -216,6 +243,20 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
   for (int i = threadIdx.x; i < mp2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
+  if (bounds && warp == 0) {
+    // The shortlist holds every column whose tf32 score is below its m-th smallest score b.y; the
+    // exact top p all have tf32 scores <= (p-th smallest) + 2E.  If b.y is not above that, a true
+    // probe may lie outside the shortlist: the query is queued for the exact pass over all lists.
+    float v = 0.0f;
+    for (int j = lane; j < d; j += 32) v = __fadd_rn(v, __fmul_rn(a[j], a[j]));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (lane == 0) {
+      const float2 b = bounds[q];
+      const float e = tf32_score_bound(v, *cmax2, d);
+      if (!(b.y > b.x + 2.0f * e)) unsafe[1 + atomicAdd(unsafe, 1)] = (int)q;
+    }
+  }
   auto finish = [&](int i, int c, double s) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
@@ -273,30 +314,145 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
 
 template <int EPL>
 static void launch_refine_e(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m, int p,
-                            int mp2, size_t smem, int32_t* probes, float* g, cudaStream_t s)
+                            int mp2, size_t smem, int32_t* probes, float* g, const float2* bounds,
+                            const float* cmax2, int* unsafe, cudaStream_t s)
 {
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(refine_topp_kernel<EPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  refine_topp_kernel<EPL><<<(unsigned)nq, 256, smem, s>>>(A, C, d, cand, m, p, mp2, probes, g);
+  refine_topp_kernel<EPL><<<(unsigned)nq, 256, smem, s>>>(A, C, d, cand, m, p, mp2, probes, g, bounds, cmax2,
+                                                          unsafe);
   RBQ_LAUNCHED();
 }
 
 void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m, int p,
-                        int32_t* probes, float* g, cudaStream_t s)
+                        int32_t* probes, float* g, cudaStream_t s, const float2* bounds, const float* cmax2,
+                        int* unsafe)
 {
   if (nq <= 0) return;
+  RBQ_CHECK(!bounds || (cmax2 && unsafe), RBQ_ERR_INVALID, "coarse: the shortlist check needs cmax2 and a queue");
   const int mp2 = next_pow2(m < 2 ? 2 : m);
   const size_t smem = (size_t)mp2 * 8 + (size_t)d * 4;
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "coarse: refine shortlist too large");
+#define RBQ_REFINE_CASE(E) \
+  launch_refine_e<E>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, bounds, cmax2, unsafe, s)
   switch (d % 32 == 0 ? d / 32 : 0) {
-    case 1: launch_refine_e<1>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    case 2: launch_refine_e<2>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    case 4: launch_refine_e<4>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    case 8: launch_refine_e<8>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    case 12: launch_refine_e<12>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    case 24: launch_refine_e<24>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
-    default: launch_refine_e<0>(A, nq, C, d, cand, m, p, mp2, smem, probes, g, s); break;
+    case 1: RBQ_REFINE_CASE(1); break;
+    case 2: RBQ_REFINE_CASE(2); break;
+    case 4: RBQ_REFINE_CASE(4); break;
+    case 8: RBQ_REFINE_CASE(8); break;
+    case 12: RBQ_REFINE_CASE(12); break;
+    case 24: RBQ_REFINE_CASE(24); break;
+    default: RBQ_REFINE_CASE(0); break;
   }
+#undef RBQ_REFINE_CASE
+}
+
+// ---------------------------------------------------------------------------------------
+// Exact probes of the queued queries (unsafe[0] = count, unsafe[1..] = query ids) over all K
+// lists: the same per-centroid double distance as refine_topp_kernel (lane l sums j = l, l+32, ...,
+// xor butterfly, rounded to float), the p smallest (g, list id) kept in shared memory by a
+// radix select whenever the buffer fills, then sorted.  Persistent blocks take queued queries
+// in turn; a block with none left returns at once.
+// ---------------------------------------------------------------------------------------
+constexpr int kRefineAllChunk = 2048;
+
+__global__ void __launch_bounds__(256) refine_all_kernel(const float* __restrict__ A, const float* __restrict__ C,
+                                                         int d, int K, int p, int buf, const int* __restrict__ unsafe,
+                                                         int32_t* __restrict__ probes, float* __restrict__ gout)
+{
+  extern __shared__ unsigned char smem_raw[];
+  unsigned long long* cur = reinterpret_cast<unsigned long long*>(smem_raw);  // [buf]
+  unsigned long long* nxt = cur + buf;                                         // [buf]
+  float* a = reinterpret_cast<float*>(nxt + buf);                               // [d]
+  __shared__ unsigned s_hist[256];
+  __shared__ int s_misc[3], s_cnt;
+  __shared__ unsigned long long s_kmax;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int n_unsafe = unsafe[0];
+  for (int u = blockIdx.x; u < n_unsafe; u += gridDim.x) {
+    const int64_t q = unsafe[1 + u];
+    __syncthreads();
+    for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
+    __syncthreads();
+    int filled = 0;
+    for (int c0 = 0; c0 < K; c0 += kRefineAllChunk) {
+      const int c1 = min(K, c0 + kRefineAllChunk);
+      for (int c = c0 + warp; c < c1; c += nwarps) {
+        const float* cr = C + (size_t)c * d;
+        double sacc = 0.0;
+        for (int j = lane; j < d; j += 32) {
+          const float df = __fsub_rn(__ldg(cr + j), a[j]);
+          sacc = __dadd_rn(sacc, __dmul_rn((double)df, (double)df));
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) sacc = __dadd_rn(sacc, __shfl_xor_sync(0xffffffffu, sacc, off));
+        if (lane == 0) cur[filled + (c - c0)] = make_key((float)sacc, (uint32_t)c);
+      }
+      filled += c1 - c0;
+      __syncthreads();
+      if (filled > p && (filled + kRefineAllChunk > buf || c1 == K)) {
+        block_keep_smallest(cur, filled, p, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+        unsigned long long* t = cur;
+        cur = nxt;
+        nxt = t;
+        filled = p;
+        __syncthreads();
+      }
+    }
+    int n2 = 2;
+    while (n2 < filled) n2 <<= 1;
+    for (int i = filled + threadIdx.x; i < n2; i += blockDim.x) cur[i] = kEmptyKey;
+    __syncthreads();
+    block_bitonic_sort(cur, n2);
+    for (int i = threadIdx.x; i < p; i += blockDim.x) {
+      const unsigned long long key = i < filled ? cur[i] : kEmptyKey;
+      probes[q * p + i] = key == kEmptyKey ? -1 : (int32_t)(key & 0xFFFFFFFFu);
+      if (gout) gout[q * p + i] = key == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(key >> 32));
+    }
+    // the buffers must be back in their original roles for the next query
+    if (cur != reinterpret_cast<unsigned long long*>(smem_raw)) {
+      nxt = cur;
+      cur = reinterpret_cast<unsigned long long*>(smem_raw);
+    }
+  }
+}
+
+void launch_refine_all(const float* A, int64_t nq, const float* C, int d, int K, int p, const int* unsafe,
+                       int32_t* probes, float* g, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  const int buf = std::max(next_pow2(p), p + kRefineAllChunk);  // room for a chunk and the final sort
+  const size_t smem = (size_t)buf * 8 * 2 + (size_t)d * 4;
+  RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "coarse: exact probe pass too large (nprobe / dim)");
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(refine_all_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const unsigned grid = (unsigned)std::min<int64_t>(nq, 148 * 4);
+  refine_all_kernel<<<grid, 256, smem, s>>>(A, C, d, K, p, buf, unsafe, probes, g);
+  RBQ_LAUNCHED();
+}
+
+// max_l C_n2[l] into *out (one block).
+__global__ void __launch_bounds__(1024) max_reduce_kernel(const float* __restrict__ v, int n, float* __restrict__ out)
+{
+  __shared__ float s_m[32];
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, v[i]);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    mx = threadIdx.x < (blockDim.x >> 5) ? s_m[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (threadIdx.x == 0) *out = mx;
+  }
+}
+
+void launch_max_reduce(const float* v, int n, float* out, cudaStream_t s)
+{
+  max_reduce_kernel<<<1, 1024, 0, s>>>(v, n, out);
+  RBQ_LAUNCHED();
 }
 
 // ---------------------------------------------------------------------------------------

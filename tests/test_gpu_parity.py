@@ -358,6 +358,49 @@ def test_config1_parity_and_recall(oracle):
     assert oracle.recall(i, gt) == oracle.recall(i2, gt)
 
 
+def _near_duplicates(n, d, nq, spread, seed):
+    """Rows that all point almost the same way (a common unit vector plus a small spread), like
+    the mean-pooled embeddings of a randomly initialised encoder: every centroid is nearly
+    equidistant from every query, so tf32 rounding reorders the coarse scores."""
+    rng = np.random.default_rng(seed)
+    base = rng.standard_normal(d).astype(np.float32)
+    X = base[None, :] + np.float32(spread) * rng.standard_normal((n, d)).astype(np.float32)
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    Q = X[rng.integers(0, n, nq)] + np.float32(spread / 4) * rng.standard_normal((nq, d)).astype(np.float32)
+    Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    return np.ascontiguousarray(X), np.ascontiguousarray(Q)
+
+
+@pytest.mark.parametrize("spread", [1e-2, 1e-3])
+def test_near_duplicate_rows_keep_exact_probes_and_search(oracle, spread):
+    """With the tf32 score error comparable to the gaps between centroid distances, the
+    shortlist's error bound sends queries to the exact pass over all lists: probes, the nearest-
+    centroid assignment and the whole search still equal the oracle's exact computation."""
+    torch = _torch()
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = _near_duplicates(20000, 256, 500, spread, seed=17)
+    idx = IndexIVFRaBitQ(256, 128, seed=7, kmeans_iters=4)
+    idx.train(X)
+    idx.add(X)
+    C, _ = idx.centroids()
+    ex = idx.export_lists()
+    lab = np.repeat(np.arange(128, dtype=np.uint32), np.diff(ex["list_off"]))[np.argsort(ex["ids"], kind="stable")]
+    assert np.array_equal(lab, oracle.assign(X, C))  # GPU assignment = exact nearest centroid
+    oix = oracle.build(X, C, lab, idx.rotation(), idx.query_scale)
+    Qr = oracle.rotate(Q, oix.P)
+    for nprobe in (8, 48):
+        probes = torch.empty((len(Q), nprobe), dtype=torch.int32, device="cuda")
+        g = torch.empty((len(Q), nprobe), dtype=torch.float32, device="cuda")
+        call("rbq_coarse", idx.handle, ptr(dev(Qr)), len(Q), nprobe, 0, ptr(probes), ptr(g), stream())
+        p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
+        assert np.array_equal(probes.cpu().numpy(), p2)
+        assert np.array_equal(u32(g.cpu().numpy()), u32(g2))
+    idx.nprobe, idx.k_rerank = 48, 200
+    d, i = idx.search(Q, 20)
+    d2, i2 = oracle.search(oix, Q, 20, 48, 200, prune=1)
+    assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+
+
 def _config2_data(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, seed=2024):
     """Benchmark config 2's generator (the bench's make_data): float32 mixture rows in chunks."""
     rng = np.random.default_rng(seed)
