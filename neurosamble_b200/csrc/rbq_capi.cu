@@ -188,20 +188,74 @@ void install_centroids(Index& ix, cudaStream_t s)
 // approximate scores (tcgen05 tf32 when d is a multiple of 32 and the operands are 16-byte
 // aligned, else fp32 SIMT) shortlist the m best per row, the exact distance over the shortlist
 // decides, and rows whose shortlist the score error bound cannot vouch for (the m-th shortlisted
-// score is not clear of the p-th by twice the bound) are recomputed over all K lists.  Scratch:
-// S [n, K], cand [n, m], bounds [n], unsafe [1 + n]; cmax2 = max_l |c_l|^2 (device scalar).
+// score is not clear of the p-th by twice the bound) are recomputed over all K lists.  For
+// K >= kFusedCoarseMinK on tensor cores the scores and the shortlist come from one fused kernel
+// (rowbuf: its per-row candidate buffers) and S is not used; otherwise S [n, K] holds the scores.
+// cand [n, m], bounds [n], unsafe [1 + n]; cmax2 = max_l |c_l|^2 (device scalar).
+constexpr int kFusedCoarseMinK = 2048;
+
+bool coarse_uses_tc(const float* A, const float* C, int d)
+{
+  return coarse_tc_supported(d) && d % 32 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0 &&
+         (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+}
+
+// Scratch of coarse_probes for up to n rows: fused (rowbuf keys) or two-kernel (S floats).
+struct CoarseScratch {
+  float* S = nullptr;
+  unsigned long long* rowbuf = nullptr;
+  int32_t* cand = nullptr;
+  float2* bounds = nullptr;
+  int* unsafe = nullptr;
+};
+
+bool coarse_fused(int K, int d, int m)
+{
+  return K >= kFusedCoarseMinK && coarse_tc_supported(d) && d % 32 == 0 && m < K && m <= coarse_topm_max_shortlist();
+}
+
+// Rows per coarse_probes call: the [rows, K] scores (two-kernel) or the per-row candidate
+// buffers (fused) stay within 512 MiB.
+int64_t coarse_rows_per_call(const float* A, const float* C, int K, int d, int m, int64_t n)
+{
+  const bool fused = coarse_fused(K, d, m) && coarse_uses_tc(A, C, d);
+  const int64_t per_row = fused ? (int64_t)coarse_topm_row_cap(m) * 8 : (int64_t)K * 4;
+  return std::min<int64_t>(n, std::max<int64_t>(128, (512ll << 20) / per_row));
+}
+
+// A, C: the rows' and centroids' base pointers (the fused kernel reads both by TMA; d % 32 == 0
+// keeps every row block of A as aligned as its base).
+CoarseScratch coarse_scratch(Scratch& sc, const float* A, const float* C, int K, int d, int m, int64_t rows)
+{
+  CoarseScratch cs;
+  if (coarse_fused(K, d, m) && coarse_uses_tc(A, C, d))
+    cs.rowbuf = sc.get<unsigned long long>((size_t)ceil_div(rows, 128) * 128 * coarse_topm_row_cap(m));
+  else
+    cs.S = sc.get<float>((size_t)rows * K);
+  cs.cand = sc.get<int32_t>((size_t)rows * m);
+  cs.bounds = sc.get<float2>((size_t)rows);
+  cs.unsafe = sc.get<int>((size_t)rows + 1);
+  return cs;
+}
+
 void coarse_probes(const Index& ix, const float* A, int64_t n, const float* C, const float* cn2, const float* cmax2,
-                   int K, int d, int m, int p, float* S, int32_t* cand, float2* bounds, int* unsafe, int32_t* probes,
-                   float* g, cudaStream_t s)
+                   int K, int d, int m, int p, const CoarseScratch& cs, int32_t* probes, float* g, cudaStream_t s)
 {
   if (n <= 0) return;
-  RBQ_CUDA(cudaMemsetAsync(unsafe, 0, sizeof(int), s));
-  if (coarse_tc_supported(d) && d % 32 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0 &&
-      (reinterpret_cast<uintptr_t>(C) & 15u) == 0)
-    launch_coarse_scores_tc(A, n, C, cn2, K, d, S, ix.dev_err, s);
-  else
-    launch_coarse_scores(A, n, C, cn2, K, d, S, s);
-  launch_topm_rows(S, n, K, m, cand, s, p, bounds);
+  RBQ_CUDA(cudaMemsetAsync(cs.unsafe, 0, sizeof(int), s));
+  int32_t* cand = cs.cand;
+  float2* bounds = cs.bounds;
+  int* unsafe = cs.unsafe;
+  if (coarse_uses_tc(A, C, d) && cs.rowbuf && m < K) {
+    launch_coarse_topm_tc(A, n, C, cn2, K, d, m, p, cs.rowbuf, cand, bounds, ix.dev_err, s);
+  } else {
+    RBQ_CHECK(cs.S != nullptr, RBQ_ERR_INVALID, "coarse: no score buffer");
+    if (coarse_uses_tc(A, C, d))
+      launch_coarse_scores_tc(A, n, C, cn2, K, d, cs.S, ix.dev_err, s);
+    else
+      launch_coarse_scores(A, n, C, cn2, K, d, cs.S, s);
+    launch_topm_rows(cs.S, n, K, m, cand, s, p, bounds);
+  }
   launch_refine_topp(A, n, C, d, cand, m, p, probes, g, s, bounds, cmax2, unsafe);
   launch_refine_all(A, n, C, d, K, p, unsafe, probes, g, s);
 }
@@ -214,19 +268,15 @@ void assign_labels(const Index& ix, const float* A, int64_t n, const float* C, c
                    uint32_t* labels_out, cudaStream_t s)
 {
   const int m = std::min(K, 32);
-  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(65535 * 64, (256ll << 20) / ((int64_t)K * 4)));
+  const int64_t chunk = std::min<int64_t>(65535 * 64, coarse_rows_per_call(A, C, K, d, m, n));
   Scratch sc(s);
-  const int64_t c0 = std::min(n, chunk);
-  float* S = sc.get<float>((size_t)c0 * K);
-  int32_t* cand = sc.get<int32_t>((size_t)c0 * m);
-  float2* bounds = sc.get<float2>((size_t)c0);
-  int* unsafe = sc.get<int>((size_t)c0 + 1);
+  const CoarseScratch cs = coarse_scratch(sc, A, C, K, d, m, std::min(n, chunk));
   float* cmax2 = sc.get<float>(1);
   launch_max_reduce(cn2, K, cmax2, s);
   for (int64_t a = 0; a < n; a += chunk) {
     const int64_t cn = std::min(chunk, n - a);
-    coarse_probes(ix, A + a * d, cn, C, cn2, cmax2, K, d, m, 1, S, cand, bounds, unsafe,
-                  reinterpret_cast<int32_t*>(labels_out + a), nullptr, s);
+    coarse_probes(ix, A + a * d, cn, C, cn2, cmax2, K, d, m, 1, cs, reinterpret_cast<int32_t*>(labels_out + a),
+                  nullptr, s);
   }
 }
 
@@ -760,13 +810,11 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   // [sub-chunk, K] score matrix (512 MiB), so a large K does not cut the scan into small grids.
   const int64_t by_keys = std::max<int64_t>(1, (1ll << 30) / ((int64_t)sp.slices * sp.R * 8));
   const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_keys, 65535ll * 64));
-  const int64_t fe_chunk = std::min<int64_t>(chunk, std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4)));
   Scratch sc(s);
   float* Qr_buf = Qr_pre ? nullptr : sc.get<float>((size_t)chunk * ix.Dp);
-  float* S = sc.get<float>((size_t)fe_chunk * ix.K);
-  int32_t* cand = sc.get<int32_t>((size_t)fe_chunk * sp.m);
-  float2* bounds = sc.get<float2>((size_t)fe_chunk);
-  int* unsafe = sc.get<int>((size_t)fe_chunk + 1);
+  const int64_t fe_chunk = coarse_rows_per_call(Qr_pre ? Qr_pre : Qr_buf, ix.C_rot, ix.K, ix.Dp, sp.m, chunk);
+  const CoarseScratch cs =
+      coarse_scratch(sc, Qr_pre ? Qr_pre : Qr_buf, ix.C_rot, ix.K, ix.Dp, sp.m, fe_chunk);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
   float* g = sc.get<float>((size_t)chunk * sp.P);
   uint32_t* planes = sc.get<uint32_t>((size_t)chunk * sp.qbits * ix.W);
@@ -786,8 +834,8 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       const int64_t fn = std::min(fe_chunk, cn - b);
       const float* Qrb = Qr + b * ix.Dp;
       if (!Qr_pre) launch_rotate(Qc + b * ix.D, fn, ix.D, ix.Dp, ix.P, Qr_buf + b * ix.Dp, s);
-      coarse_probes(ix, Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, sp.m, sp.P, S, cand, bounds,
-                    unsafe, probes + b * sp.P, g + b * sp.P, s);
+      coarse_probes(ix, Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, sp.m, sp.P, cs,
+                    probes + b * sp.P, g + b * sp.P, s);
     }
     launch_query_prep(Qr, cn, ix.Dp, qt, sp.qbits, planes, delta, k1, s);
     {
@@ -1811,16 +1859,13 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
     DeviceGuard dg(ix.device);
     cudaStream_t s = as_stream(stream);
     const int m = std::min(ix.K, std::min(nprobe + (margin > 0 ? margin : std::max(16, nprobe / 2)), 1024));
-    const int64_t chunk = std::min<int64_t>(nq, std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.K * 4)));
+    const int64_t chunk = coarse_rows_per_call(Qr_dev, ix.C_rot, ix.K, ix.Dp, m, nq);
     Scratch sc(s);
-    float* S = sc.get<float>((size_t)chunk * ix.K);
-    int32_t* cand = sc.get<int32_t>((size_t)chunk * m);
-    float2* bounds = sc.get<float2>((size_t)chunk);
-    int* unsafe = sc.get<int>((size_t)chunk + 1);
+    const CoarseScratch cs = coarse_scratch(sc, Qr_dev, ix.C_rot, ix.K, ix.Dp, m, chunk);
     for (int64_t a = 0; a < nq; a += chunk) {
       const int64_t cn = std::min(chunk, nq - a);
-      coarse_probes(ix, Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, m, nprobe, S,
-                    cand, bounds, unsafe, probes_dev + a * nprobe, g_dev + a * nprobe, s);
+      coarse_probes(ix, Qr_dev + a * ix.Dp, cn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, m, nprobe, cs,
+                    probes_dev + a * nprobe, g_dev + a * nprobe, s);
     }
   });
 }

@@ -267,6 +267,326 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const __grid_c
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Fused scores + shortlist for large K (the [queries, K] score matrix never leaves the SM).
+//
+// CTA: 192 threads, 128 queries against all K centroids in chunks of kTcN = 256.  Warp 4 (one
+// lane) streams the operand k-chunks by TMA into a ring of four stages; warp 5 (one lane) issues
+// the tf32 MMAs of chunk t into accumulator t % 2 (two accumulators, all 512 TMEM columns), so
+// the MMAs of one chunk overlap the epilogue of the previous one; warps 0-3 are the epilogue,
+// thread r owning query row r (TMEM lane r).  Per chunk an epilogue thread reads its 256 scores
+// S = |c|^2 - 2 <q, c> (the same arithmetic as coarse_tc_kernel), and appends the (score,
+// column) key to its row's buffer in global memory only when it is below the row's threshold
+// (the m-th smallest key kept so far).  When a buffer could overflow, its warp cuts it to the m
+// smallest by a cooperative radix select and the threshold tightens; a threshold is never below
+// the final m-th smallest key, so the result is the m smallest keys of the row, as
+// topm_rows_kernel's.  At the end each row writes its m columns (any order) and (p-th smallest
+// score, m-th smallest score).  Every wait is bounded and a failed wait makes all roles stop.
+// ---------------------------------------------------------------------------------------
+constexpr int kFtThreads = 192;
+constexpr int kFtStages = 4;
+constexpr int kFtProducerWarp = 4, kFtMmaWarp = 5;
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// mbar_wait that also gives up as soon as another role has reported a failure.
+__device__ __forceinline__ bool mbar_wait_or_fail(uint32_t bar, uint32_t parity, volatile int* fail)
+{
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 1023u) == 1023u && *fail) return false;
+  }
+  return false;
+}
+
+// Ascending bitonic sort of the 32 * KPL keys a warp holds in registers: element e = lane * KPL + j
+// lives in k[j] of lane `lane`.  Partners closer than KPL are in the same lane; farther ones are
+// exchanged by shuffles.
+template <int KPL>
+__device__ __forceinline__ void warp_bitonic_sort(unsigned long long (&k)[KPL], int lane)
+{
+  constexpr int N = 32 * KPL;
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int dist = size >> 1; dist > 0; dist >>= 1) {
+      if (dist >= KPL) {
+        const int lx = dist / KPL;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+          const int e = lane * KPL + j;
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, k[j], lx);
+          const bool up = (e & size) == 0, lower = (lane & lx) == 0;
+          const bool take_min = lower == up;
+          k[j] = take_min ? (o < k[j] ? o : k[j]) : (o > k[j] ? o : k[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+          const int jp = j ^ dist;
+          if (jp > j) {
+            const int e = lane * KPL + j;
+            const bool up = (e & size) == 0;
+            const unsigned long long a = k[j], b = k[jp];
+            const bool sw = up ? (a > b) : (a < b);
+            k[j] = sw ? b : a;
+            k[jp] = sw ? a : b;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Sorts the n <= 32 * KPL distinct keys buf[0..n) (global memory) by the whole warp and writes back
+// the `keep` smallest, ascending, to buf[0..keep); returns the `want`-th smallest key
+// (kEmptyKey if n < want).
+template <int KPL>
+__device__ unsigned long long warp_sort_keys(unsigned long long* buf, int n, int keep, int want, int lane)
+{
+  unsigned long long k[KPL];
+#pragma unroll
+  for (int j = 0; j < KPL; ++j) {
+    const int e = lane * KPL + j;
+    k[j] = e < n ? buf[e] : kEmptyKey;
+  }
+  warp_bitonic_sort<KPL>(k, lane);
+  __syncwarp();  // every lane has read its keys before any is overwritten
+  unsigned long long r = kEmptyKey;
+#pragma unroll
+  for (int j = 0; j < KPL; ++j) {
+    const int e = lane * KPL + j;
+    if (e < keep && e < n) buf[e] = k[j];
+    if (e == want - 1) r = k[j];
+  }
+  const int src = (want - 1) / KPL;
+  return want >= 1 && want <= n ? __shfl_sync(0xffffffffu, r, src) : kEmptyKey;
+}
+
+template <int KPL>
+__global__ void __launch_bounds__(kFtThreads, 1)
+    coarse_topm_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, int nq,
+                          const float* __restrict__ cn2, int K, int dp, int m, int p, int cap,
+                          unsigned long long* __restrict__ rowbuf, int32_t* __restrict__ cand,
+                          float2* __restrict__ bounds, int* __restrict__ err)
+{
+  extern __shared__ unsigned char tc_smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  float* cn2s = reinterpret_cast<float*>(base + kFtStages * kTcStageBytes);  // [2][kTcN]
+  __shared__ __align__(8) unsigned long long s_full[kFtStages], s_empty[kFtStages], s_accf[2], s_acce[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_fail;
+  __shared__ int s_issued, s_consumed;
+  __shared__ int s_ok[2][4];  // epilogue warps' wait results, by chunk parity
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = blockIdx.x * kTcM;
+  const int nkc = dp / kTcKc;
+  const int n_chunks = (K + kTcN - 1) / kTcN;
+  const int total = n_chunks * nkc;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"((uint32_t)(2 * kTcN)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == kFtProducerWarp * 32) {
+    for (int i = 0; i < kFtStages; ++i) {
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&s_empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s_accf[i]), 1);
+      mbar_init(smem_u32(&s_acce[i]), 4);
+    }
+    s_fail = 0;
+    s_issued = 0;
+    s_consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmC)) : "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem;
+
+  if (warp == kFtProducerWarp) {
+    if (lane == 0) {
+      int c = 0;
+      for (; c < total; ++c) {
+        const int st = c % kFtStages;
+        if (c >= kFtStages &&
+            !mbar_wait_or_fail(smem_u32(&s_empty[st]), (uint32_t)((c / kFtStages - 1) & 1), &s_fail)) {
+          atomicExch(err, 11);
+          s_fail = 1;
+          break;
+        }
+        const int t = c / nkc, kc = c - t * nkc;
+        unsigned char* a_blk = base + st * kTcStageBytes;
+        const uint32_t full = smem_u32(&s_full[st]);
+        mbar_expect_tx(full, (uint32_t)kTcStageBytes);
+        tma_load_2d(smem_u32(a_blk), &tmQ, kc * kTcKc, q0, full);
+        tma_load_2d(smem_u32(a_blk + kTcM * 128), &tmC, kc * kTcKc, t * kTcN, full);
+      }
+      s_issued = c;
+    }
+  } else if (warp == kFtMmaWarp) {
+    if (lane == 0) {
+      int c = 0;
+      bool ok = true;
+      for (int t = 0; t < n_chunks && ok; ++t) {
+        const int b = t & 1;
+        if (t >= 2 && !mbar_wait_or_fail(smem_u32(&s_acce[b]), (uint32_t)(((t >> 1) - 1) & 1), &s_fail)) {
+          ok = false;
+          atomicExch(err, 12);
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + (uint32_t)(b * kTcN);
+        for (int kc = 0; kc < nkc; ++kc, ++c) {
+          const int st = c % kFtStages;
+          if (!mbar_wait_or_fail(smem_u32(&s_full[st]), (uint32_t)((c / kFtStages) & 1), &s_fail)) {
+            ok = false;
+            atomicExch(err, 13);
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(base + st * kTcStageBytes), b_addr = a_addr + kTcM * 128;
+#pragma unroll
+          for (int ks = 0; ks < kTcKc / 8; ++ks)
+            tc_mma(acc, sw128_desc(a_addr + ks * 32), sw128_desc(b_addr + ks * 32), kTcIdesc,
+                   (kc > 0 || ks > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&s_empty[st]));
+        }
+        if (ok) tc_commit(smem_u32(&s_accf[b]));
+      }
+      s_consumed = c;
+      if (!ok) s_fail = 1;
+    }
+  } else {
+    // epilogue: thread r of warps 0-3 owns query row r
+    const int row = warp * 32 + lane;
+    const int64_t q = (int64_t)q0 + row;
+    const bool active = q < nq;
+    unsigned long long* rb = rowbuf + ((size_t)blockIdx.x * kTcM + row) * cap;
+    // thr: the m-th smallest key kept so far (kEmptyKey: none yet); thr_s its score.  A column
+    // is appended when its score is <= thr_s: that keeps every key below thr, and the ties
+    // above it only add keys a later cut removes.
+    unsigned long long thr = kEmptyKey;
+    float thr_s = __int_as_float(0x7f800000);
+    int cnt = 0;
+    bool cut = false;
+    for (int t = 0; t < n_chunks; ++t) {
+      const int b = t & 1, n0 = t * kTcN;
+      // stage |c|^2 of the chunk (two buffers: a buffer is rewritten two chunks later, after every
+      // epilogue thread has passed the next chunk's barrier)
+      for (int i = row; i < kTcN; i += 128) cn2s[b * kTcN + i] = n0 + i < K ? __ldg(cn2 + n0 + i) : 0.0f;
+      if (lane == 0) {
+        const bool okw = mbar_wait_or_fail(smem_u32(&s_accf[b]), (uint32_t)((t >> 1) & 1), &s_fail);
+        s_ok[b][warp] = okw ? 1 : 0;
+        if (!okw) atomicExch(err, 14);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // every epilogue warp takes the same decision (a lone warp leaving would strand the others
+      // at the next named barrier); s_ok[b] is rewritten two chunks later, after the next barrier
+      if (!(s_ok[b][0] && s_ok[b][1] && s_ok[b][2] && s_ok[b][3])) {
+        s_fail = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const float* cs = cn2s + b * kTcN;
+#pragma unroll 1
+      for (int j = 0; j < kTcN / 32; ++j) {
+        float v[32];
+        tc_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * kTcN + 32 * j), v);
+        // score = |c|^2 - 2 acc, one rounding (2 acc is exact): the arithmetic of coarse_tc_kernel
+        const int cb = n0 + 32 * j;
+        unsigned pm = 0u;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = __fmaf_rn(-2.0f, v[i], cs[32 * j + i]);
+          pm |= (v[i] <= thr_s ? 1u : 0u) << i;
+        }
+        if (!active || cb >= K) pm = 0u;
+        else if (cb + 32 > K) pm &= (1u << (K - cb)) - 1u;
+        // append the passing columns: only the columns some lane of the warp passes are visited
+        unsigned any = __reduce_or_sync(0xffffffffu, pm);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (any & (1u << i)) {
+            if ((pm >> i) & 1u) rb[cnt++] = make_key(v[i], (uint32_t)(cb + i));
+          }
+        }
+        unsigned full = __ballot_sync(0xffffffffu, cnt > cap - 32);
+        while (full) {  // cut each full row of the warp to its m smallest keys
+          const int L = __ffs(full) - 1;
+          full &= full - 1;
+          const int n = __shfl_sync(0xffffffffu, cnt, L);
+          unsigned long long* lb = rowbuf + ((size_t)blockIdx.x * kTcM + warp * 32 + L) * cap;
+          const unsigned long long kth = warp_sort_keys<KPL>(lb, n, m, m, lane);
+          if (lane == L) {
+            thr = kth;
+            thr_s = from_ordered_bits((uint32_t)(kth >> 32));
+            cnt = m;
+            cut = true;
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s_acce[b]));
+    }
+    if (!s_fail) {
+      // final cut to m, then the p-th smallest of the m (not compacted)
+      // final: each row sorted, its m smallest kept (ascending); the p-th and m-th scores
+      unsigned act = __ballot_sync(0xffffffffu, active);
+      while (act) {
+        const int L = __ffs(act) - 1;
+        act &= act - 1;
+        const int n = __shfl_sync(0xffffffffu, cnt, L);
+        unsigned long long* lb = rowbuf + ((size_t)blockIdx.x * kTcM + warp * 32 + L) * cap;
+        const int64_t qL = (int64_t)q0 + warp * 32 + L;
+        const unsigned long long kp = warp_sort_keys<KPL>(lb, n, m, p, lane);
+        __syncwarp();
+        const int kept = n < m ? n : m;
+        for (int i = lane; i < m; i += 32) cand[qL * m + i] = i < kept ? (int32_t)(lb[i] & 0xFFFFFFFFu) : -1;
+        // the m-th smallest key: when more than m columns were ever kept (cut or n > m) the row
+        // dropped columns above it; a row that saw every column keeps +inf
+        const bool cutL = (__shfl_sync(0xffffffffu, (int)cut, L) != 0) || n > m;
+        const unsigned long long km = n >= m ? lb[m - 1] : kEmptyKey;
+        if (lane == 0)
+          bounds[qL] = make_float2(kp == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(kp >> 32)),
+                                   cutL ? from_ordered_bits((uint32_t)(km >> 32)) : __int_as_float(0x7f800000));
+      }
+    }
+  }
+  __syncthreads();
+  // On failure: wait (bounded) for the copies and MMAs still in flight, then free TMEM.
+  if (s_fail && tid == kFtProducerWarp * 32) {
+    for (int c = s_consumed; c < s_issued; ++c)
+      mbar_wait(smem_u32(&s_full[c % kFtStages]), (uint32_t)((c / kFtStages) & 1));
+    if (s_consumed > 0) {
+      const int last = s_consumed - 1;
+      mbar_wait(smem_u32(&s_empty[last % kFtStages]), (uint32_t)((last / kFtStages) & 1));
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * kTcN)));
+  }
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 {
@@ -302,6 +622,44 @@ CUtensorMap row_major_map(const float* ptr, int64_t rows, int dp, int box_rows)
 }
 
 }  // namespace
+
+// Candidate keys per row the fused shortlist keeps: room for m keys, as many new ones and one
+// 32-column group, rounded to the warp (a cut sorts the row's keys in registers, cap / 32 per
+// lane).  Twice that buffer halved the cuts but cost more in appends and larger sorts.
+int coarse_topm_row_cap(int m) { return (2 * m + 64 + 31) / 32 * 32; }
+constexpr int kFtMaxCap = 32 * 32;  // m <= 480
+
+void launch_coarse_topm_tc(const float* A, int64_t nq, const float* C, const float* cn2, int K, int dp, int m, int p,
+                           unsigned long long* rowbuf, int32_t* cand, float2* bounds, int* err, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  RBQ_CHECK(coarse_tc_supported(dp), RBQ_ERR_INVALID, "coarse (tensor cores): padded dim must be a multiple of 32");
+  RBQ_CHECK(nq <= 0x7fffffff && K >= 1 && m >= 1 && m <= K && p >= 1 && p <= m, RBQ_ERR_INVALID,
+            "coarse (fused shortlist): bad sizes");
+  const int cap = coarse_topm_row_cap(m);
+  RBQ_CHECK(cap <= kFtMaxCap, RBQ_ERR_INVALID, "coarse (fused shortlist): shortlist too long");
+  const size_t smem = (size_t)kFtStages * kTcStageBytes + (size_t)2 * kTcN * 4 + 1024;
+  const CUtensorMap tmQ = row_major_map(A, nq, dp, kTcM);
+  const CUtensorMap tmC = row_major_map(C, K, dp, kTcN);
+  const unsigned grid = (unsigned)ceil_div(nq, kTcM);
+#define RBQ_FT_LAUNCH(KPL)                                                                                        \
+  {                                                                                                               \
+    RBQ_CUDA(cudaFuncSetAttribute(coarse_topm_tc_kernel<KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                                  (int)smem));                                                                    \
+    coarse_topm_tc_kernel<KPL><<<grid, kFtThreads, smem, s>>>(tmQ, tmC, (int)nq, cn2, K, dp, m, p, cap, rowbuf,  \
+                                                             cand, bounds, err);                                  \
+  }
+  if (cap <= 8 * 32)
+    RBQ_FT_LAUNCH(8)
+  else if (cap <= 16 * 32)
+    RBQ_FT_LAUNCH(16)
+  else
+    RBQ_FT_LAUNCH(32)
+#undef RBQ_FT_LAUNCH
+  RBQ_LAUNCHED();
+}
+
+int coarse_topm_max_shortlist() { return (kFtMaxCap - 64) / 2; }
 
 bool coarse_tc_supported(int dp) { return dp % kTcKc == 0 && dp >= kTcKc && dp <= 4096; }
 

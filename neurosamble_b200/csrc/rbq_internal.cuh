@@ -180,6 +180,13 @@ void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t
 // Approximate scores S[q, c] = |c|^2 - 2 <a_q, c> for ranking (fp32).
 // Same scores on the tensor cores (tcgen05 kind::tf32); err[0] is set if a wait timed out.
 bool coarse_tc_supported(int dp);
+// Fused tensor-core scores + m-best shortlist for large K: cand [nq, m] (any order) and bounds
+// [nq] as launch_topm_rows gives them, without writing the [nq, K] scores.  rowbuf: scratch of
+// ceil(nq / 128) * 128 * coarse_topm_row_cap(m) keys.
+int coarse_topm_row_cap(int m);
+int coarse_topm_max_shortlist();  // the largest m the fused kernel takes
+void launch_coarse_topm_tc(const float* A, int64_t nq, const float* C, const float* cn2, int K, int dp, int m, int p,
+                           unsigned long long* rowbuf, int32_t* cand, float2* bounds, int* err, cudaStream_t s);
 void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const float* cn2, int K, int dp, float* S,
                              int* err, cudaStream_t s);
 void launch_coarse_scores(const float* A, int64_t nq, const float* C, const float* c_n2, int K, int d,

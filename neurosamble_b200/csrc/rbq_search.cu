@@ -350,9 +350,11 @@ void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const
 // ---------------------------------------------------------------------------------------
 // Exact probes of the queued queries (unsafe[0] = count, unsafe[1..] = query ids) over all K
 // lists: the same per-centroid double distance as refine_topp_kernel (lane l sums j = l, l+32, ...,
-// xor butterfly, rounded to float), the p smallest (g, list id) kept in shared memory by a
-// radix select whenever the buffer fills, then sorted.  Persistent blocks take queued queries
-// in turn; a block with none left returns at once.
+// xor butterfly, rounded to float).  Lists stream through in chunks; a (g, list id) key is kept
+// only while it is below the p-th smallest key kept so far, and a radix select cuts the buffer
+// back to p keys when the next chunk might not fit, so a long row costs about one selection per
+// few chunks.  The p kept keys are sorted and written.  Persistent blocks take queued queries in
+// turn; a block with none left returns at once.
 // ---------------------------------------------------------------------------------------
 constexpr int kRefineAllChunk = 2048;
 
@@ -361,19 +363,23 @@ __global__ void __launch_bounds__(256) refine_all_kernel(const float* __restrict
                                                          int32_t* __restrict__ probes, float* __restrict__ gout)
 {
   extern __shared__ unsigned char smem_raw[];
-  unsigned long long* cur = reinterpret_cast<unsigned long long*>(smem_raw);  // [buf]
-  unsigned long long* nxt = cur + buf;                                         // [buf]
-  float* a = reinterpret_cast<float*>(nxt + buf);                               // [d]
+  unsigned long long* const buf0 = reinterpret_cast<unsigned long long*>(smem_raw);  // [buf]
+  unsigned long long* const buf1 = buf0 + buf;                                       // [buf]
+  float* a = reinterpret_cast<float*>(buf1 + buf);                                    // [d]
   __shared__ unsigned s_hist[256];
-  __shared__ int s_misc[3], s_cnt;
+  __shared__ int s_misc[3], s_cnt, s_fill;
   __shared__ unsigned long long s_kmax;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int n_unsafe = unsafe[0];
   for (int u = blockIdx.x; u < n_unsafe; u += gridDim.x) {
     const int64_t q = unsafe[1 + u];
+    unsigned long long* cur = buf0;
+    unsigned long long* nxt = buf1;
     __syncthreads();
     for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
+    if (threadIdx.x == 0) s_fill = 0;
     __syncthreads();
+    unsigned long long thr = kEmptyKey;  // the p-th smallest key kept so far
     int filled = 0;
     for (int c0 = 0; c0 < K; c0 += kRefineAllChunk) {
       const int c1 = min(K, c0 + kRefineAllChunk);
@@ -386,18 +392,20 @@ __global__ void __launch_bounds__(256) refine_all_kernel(const float* __restrict
         }
 #pragma unroll
         for (int off = 16; off; off >>= 1) sacc = __dadd_rn(sacc, __shfl_xor_sync(0xffffffffu, sacc, off));
-        if (lane == 0) cur[filled + (c - c0)] = make_key((float)sacc, (uint32_t)c);
+        const unsigned long long key = make_key((float)sacc, (uint32_t)c);
+        if (lane == 0 && key < thr) cur[atomicAdd(&s_fill, 1)] = key;
       }
-      filled += c1 - c0;
       __syncthreads();
+      filled = s_fill;
       if (filled > p && (filled + kRefineAllChunk > buf || c1 == K)) {
-        block_keep_smallest(cur, filled, p, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
+        thr = block_keep_smallest(cur, filled, p, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
         unsigned long long* t = cur;
         cur = nxt;
         nxt = t;
         filled = p;
-        __syncthreads();
+        if (threadIdx.x == 0) s_fill = p;
       }
+      __syncthreads();
     }
     int n2 = 2;
     while (n2 < filled) n2 <<= 1;
@@ -408,11 +416,6 @@ __global__ void __launch_bounds__(256) refine_all_kernel(const float* __restrict
       const unsigned long long key = i < filled ? cur[i] : kEmptyKey;
       probes[q * p + i] = key == kEmptyKey ? -1 : (int32_t)(key & 0xFFFFFFFFu);
       if (gout) gout[q * p + i] = key == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(key >> 32));
-    }
-    // the buffers must be back in their original roles for the next query
-    if (cur != reinterpret_cast<unsigned long long*>(smem_raw)) {
-      nxt = cur;
-      cur = reinterpret_cast<unsigned long long*>(smem_raw);
     }
   }
 }
@@ -889,6 +892,17 @@ __device__ __forceinline__ int32_t dot_vector(const uint32_t* __restrict__ codes
 // those are copied to dst[0..R) (any order) and the largest of them (the R-th smallest key) is
 // returned.  hist: 256 shared counters; misc: 3 shared ints; kmax, cnt: shared scratch.
 // ---------------------------------------------------------------------------------------
+// hist[bin] += 1 for every lane with `take`, one shared atomic per distinct bin of the warp:
+// keys that share their leading bytes (close distances) would otherwise serialise up to 32
+// atomics on one counter.
+__device__ __forceinline__ void hist_add_aggregated(unsigned* hist, bool take, unsigned bin, int lane)
+{
+  const unsigned active = __ballot_sync(0xffffffffu, take);
+  if (!take) return;
+  const unsigned peers = __match_any_sync(active, bin);
+  if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+}
+
 __device__ unsigned long long block_keep_smallest(const unsigned long long* src, int n, int R,
                                                   unsigned long long* dst, unsigned* hist, int* misc,
                                                   unsigned long long* kmax, int* cnt)
@@ -899,9 +913,10 @@ __device__ unsigned long long block_keep_smallest(const unsigned long long* src,
   for (int shift = 56; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-      const unsigned long long k = src[i];
-      if ((k & pmask) == prefix) atomicAdd(&hist[(unsigned)(k >> shift) & 255u], 1u);
+    for (int i0 = tid - lane; i0 < n; i0 += blockDim.x) {  // warp-uniform trip count
+      const int i = i0 + lane;
+      const unsigned long long k = i < n ? src[i] : 0ull;
+      hist_add_aggregated(hist, i < n && (k & pmask) == prefix, (unsigned)(k >> shift) & 255u, lane);
     }
     __syncthreads();
     if (tid < 32) {

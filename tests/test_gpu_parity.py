@@ -401,6 +401,31 @@ def test_near_duplicate_rows_keep_exact_probes_and_search(oracle, spread):
     assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
 
 
+@pytest.mark.parametrize("d,K,nq,nprobes", [(128, 2500, 300, (1, 30, 200)), (256, 4096, 129, (8, 64)),
+                                             (96, 3000, 77, (16,))])
+def test_fused_coarse_shortlist_probes_bit_exact(oracle, d, K, nq, nprobes):
+    """K >= 2048 takes the fused tensor-core scores + shortlist kernel (no [nq, K] score matrix):
+    probes and their exact distances equal the oracle's exact top-P, for ragged K and batches."""
+    torch = _torch()
+    from neurosamble_b200 import IndexIVFRaBitQ
+    X, Q = mixture(K * 4, d, K, 0.2, nq, seed=23)
+    idx = IndexIVFRaBitQ(d, K, seed=7)
+    C = X[np.arange(K) * 4].copy()
+    idx.set_centroids(C)
+    P = idx.rotation()
+    dp = P.shape[0]
+    Cr = oracle.rotate(C, P)
+    Qr = oracle.rotate(Q, P)
+    for nprobe in nprobes:
+        probes = torch.empty((nq, nprobe), dtype=torch.int32, device="cuda")
+        g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
+        call("rbq_coarse", idx.handle, ptr(dev(Qr)), nq, nprobe, 0, ptr(probes), ptr(g), stream())
+        p2, g2 = oracle.coarse(Qr, Cr, nprobe)
+        assert np.array_equal(probes.cpu().numpy(), p2), nprobe
+        assert np.array_equal(u32(g.cpu().numpy()), u32(g2)), nprobe
+    assert dp % 32 == 0
+
+
 def _config2_data(n=1_000_000, d=256, centres=4096, sigma=0.25, nq=10_000, qsigma=0.05, seed=2024):
     """Benchmark config 2's generator (the bench's make_data): float32 mixture rows in chunks."""
     rng = np.random.default_rng(seed)
