@@ -531,6 +531,20 @@ def run_ours(args, cfg):
         e2e_s = float(t_max.item())
     e2e = nq / e2e_s
 
+    # ---- N > 1: one more search with CUDA events at its stage boundaries (front end, the three
+    # collectives, scan, rerank, merge); rank 0's milliseconds and the max over ranks
+    stages_ms = None
+    if world > 1:
+        tdist.barrier()
+        tm = {}
+        index.search(Qd, k, timings=tm)
+        names = list(tm)
+        vals = torch.tensor([tm[n] for n in names], dtype=torch.float64, device=dev)
+        vmax = vals.clone()
+        tdist.all_reduce(vmax, op=tdist.ReduceOp.MAX)
+        stages_ms = {"rank0": {n: round(float(v), 4) for n, v in zip(names, vals.tolist())},
+                     "max_over_ranks": {n: round(float(v), 4) for n, v in zip(names, vmax.tolist())}}
+
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
     seeded = world > 1 or args.seeded == 1
     roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
@@ -584,6 +598,7 @@ def run_ours(args, cfg):
                 "gpu_launches": int(launches),
                 "roofline": roof, "roofline_rerank": roof_rr, "scan_share_of_step": scan_share,
                 "batch_sweep": sweep, "batch_sweep_graph": sweep_graph,
+                "stages_ms": stages_ms,
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -287,6 +287,13 @@ int rbq_rerank(rbq_index_t* index, const float* Q_dev, int64_t nq, const int64_t
  * merge after the NCCL all-gather of a list-sharded search. */
 int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t parts, int64_t nq, int32_t k,
                       float* out_dist_dev, int64_t* out_ids_dev, void* stream);
+/* Results (dist f32, id i64; id < 0 = empty) -> 8-byte keys: (order-preserving bits of dist) << 32 |
+ * id, all ones when empty.  A sharded search all-gathers these instead of the 12-byte pairs and
+ * merges them with rbq_merge_result_keys ([parts, nq, k] keys, same output as rbq_merge_results).
+ * No reference counterpart (the reference has no multi-GPU search, rabitq_search.cu:11). */
+int rbq_pack_results(const float* dist_dev, const int64_t* ids_dev, int64_t n, uint64_t* keys_dev, void* stream);
+int rbq_merge_result_keys(const uint64_t* keys_dev, int32_t parts, int64_t nq, int32_t k, float* out_dist_dev,
+                          int64_t* out_ids_dev, void* stream);
 
 /* ---- fault injection (tests) --------------------------------------------------------------- */
 /* Host-side: the (after+1)-th device allocation the library makes from now on fails with

@@ -83,6 +83,8 @@ SIGNATURES = {
                          _I32, _P],
     "rbq_rerank": [_P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "rbq_merge_results": [_P, _P, _I32, _I64, _I32, _P, _P, _P],
+    "rbq_pack_results": [_P, _P, _I64, _P, _P],
+    "rbq_merge_result_keys": [_P, _I32, _I64, _I32, _P, _P, _P],
     "rbq_debug_fail_alloc": [_I64],
     "rbq_gen_mixture": [_P, _I64, _I32, _I32, _F32, _I32, _I32, _U64, _P],
     "rbq_gen_queries": [_P, _I64, _I32, _P, _I64, _F32, _I32, _U64, _P, _P],

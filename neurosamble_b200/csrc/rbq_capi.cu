@@ -1980,6 +1980,26 @@ int rbq_merge_results(const float* dist_dev, const int64_t* ids_dev, int32_t par
   });
 }
 
+int rbq_pack_results(const float* dist_dev, const int64_t* ids_dev, int64_t n, uint64_t* keys_dev, void* stream)
+{
+  return guarded([&] {
+    RBQ_CHECK(n >= 0 && (n == 0 || (dist_dev && ids_dev && keys_dev)), RBQ_ERR_INVALID, "null buffer");
+    launch_cands_to_keys(ids_dev, dist_dev, n, reinterpret_cast<unsigned long long*>(keys_dev), as_stream(stream));
+  });
+}
+
+int rbq_merge_result_keys(const uint64_t* keys_dev, int32_t parts, int64_t nq, int32_t k, float* out_dist_dev,
+                          int64_t* out_ids_dev, void* stream)
+{
+  return guarded([&] {
+    Range nvtx_range("rbq_merge_result_keys");
+    RBQ_CHECK(parts >= 1 && k >= 1 && nq >= 0, RBQ_ERR_INVALID, "bad merge parameters");
+    RBQ_CHECK(nq == 0 || (keys_dev && out_dist_dev && out_ids_dev), RBQ_ERR_INVALID, "null buffer");
+    launch_merge_results(nullptr, nullptr, parts, nq, k, out_dist_dev, out_ids_dev, as_stream(stream),
+                         reinterpret_cast<const unsigned long long*>(keys_dev));
+  });
+}
+
 int rbq_gen_mixture(float* X_dev, int64_t n, int32_t D, int32_t n_centres, float sigma, int32_t aniso,
                     int32_t normalize, uint64_t seed, void* stream)
 {

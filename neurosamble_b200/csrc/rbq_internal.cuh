@@ -299,8 +299,9 @@ void launch_ids_to_keys(const int64_t* ids, int64_t n, unsigned long long* keys,
 void launch_cands_to_keys(const int64_t* ids, const float* dist, int64_t n, unsigned long long* keys, cudaStream_t s);
 void launch_keys_to_ids(const unsigned long long* keys, int64_t n, int64_t* ids, float* dist, cudaStream_t s);
 // k-way merge of [parts, nq, k] results.
+// keys (optional): the results already packed as keys [parts, nq, k]; dist and ids unused.
 void launch_merge_results(const float* dist, const int64_t* ids, int parts, int64_t nq, int k, float* out_dist,
-                          int64_t* out_ids, cudaStream_t s);
+                          int64_t* out_ids, cudaStream_t s, const unsigned long long* keys = nullptr);
 
 // Synthetic data (benchmarks): Gaussian mixture rows, optionally normalised.
 void launch_gen_mixture(float* X, int64_t n, int D, int n_centres, float sigma, int aniso, int normalize,

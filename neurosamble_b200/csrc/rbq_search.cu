@@ -1594,11 +1594,23 @@ void launch_keys_to_ids(const unsigned long long* keys, int64_t n, int64_t* ids,
   RBQ_LAUNCHED();
 }
 
+// Per-shard results [parts, nq, k] as keys: from (dist, id) pairs (id < 0 = empty), or already
+// packed (keys != nullptr; what a sharded search all-gathers, 8 bytes a result instead of 12).
+struct ResultSource {
+  const float* dist;
+  const int64_t* ids;
+  const unsigned long long* keys;
+  __device__ __forceinline__ unsigned long long at(size_t i) const
+  {
+    if (keys) return keys[i];
+    return ids[i] >= 0 ? make_key(dist[i], (uint32_t)ids[i]) : kEmptyKey;
+  }
+};
+
 // k-way merge of per-shard results [parts, nq, k] by (distance, id): the on-device merge that
 // follows the all-gather of a list-sharded search.
-__global__ void __launch_bounds__(256) merge_results_kernel(const float* __restrict__ dist,
-                                                            const int64_t* __restrict__ ids, int parts, int64_t nq,
-                                                            int k, int n2, float* __restrict__ out_dist,
+__global__ void __launch_bounds__(256) merge_results_kernel(const ResultSource src, int parts, int64_t nq, int k,
+                                                            int n2, float* __restrict__ out_dist,
                                                             int64_t* __restrict__ out_ids)
 {
   extern __shared__ unsigned long long mr[];
@@ -1607,8 +1619,7 @@ __global__ void __launch_bounds__(256) merge_results_kernel(const float* __restr
     unsigned long long key = kEmptyKey;
     if (i < parts * k) {
       const int p = i / k, r = i - p * k;
-      const size_t at = ((size_t)p * nq + q) * k + r;
-      if (ids[at] >= 0) key = make_key(dist[at], (uint32_t)ids[at]);
+      key = src.at(((size_t)p * nq + q) * k + r);
     }
     mr[i] = key;
   }
@@ -1625,9 +1636,8 @@ __global__ void __launch_bounds__(256) merge_results_kernel(const float* __restr
 // takes the k smallest keys by k rounds of a warp-wide minimum; the lowest lane holding the
 // minimum drops one copy of it, so the result equals the sort's first k.
 template <int L>
-__global__ void __launch_bounds__(256) merge_results_warp_kernel(const float* __restrict__ dist,
-                                                                 const int64_t* __restrict__ ids, int parts,
-                                                                 int64_t nq, int k, float* __restrict__ out_dist,
+__global__ void __launch_bounds__(256) merge_results_warp_kernel(const ResultSource src, int parts, int64_t nq,
+                                                                 int k, float* __restrict__ out_dist,
                                                                  int64_t* __restrict__ out_ids)
 {
   const int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -1641,8 +1651,7 @@ __global__ void __launch_bounds__(256) merge_results_warp_kernel(const float* __
     v[i] = kEmptyKey;
     if (e < n) {
       const int p = e / k, r = e - p * k;
-      const size_t at = ((size_t)p * nq + q) * k + r;
-      if (ids[at] >= 0) v[i] = make_key(dist[at], (uint32_t)ids[at]);
+      v[i] = src.at(((size_t)p * nq + q) * k + r);
     }
   }
   for (int o = 0; o < k; ++o) {
@@ -1677,17 +1686,18 @@ __global__ void __launch_bounds__(256) merge_results_warp_kernel(const float* __
 }
 
 void launch_merge_results(const float* dist, const int64_t* ids, int parts, int64_t nq, int k, float* out_dist,
-                          int64_t* out_ids, cudaStream_t s)
+                          int64_t* out_ids, cudaStream_t s, const unsigned long long* keys)
 {
   if (nq <= 0) return;
+  const ResultSource src{dist, ids, keys};
   if ((int64_t)parts * k <= 32 * 8) {
     const unsigned grid = (unsigned)ceil_div(nq * 32, 256);
     if (parts * k <= 32 * 2)
-      merge_results_warp_kernel<2><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+      merge_results_warp_kernel<2><<<grid, 256, 0, s>>>(src, parts, nq, k, out_dist, out_ids);
     else if (parts * k <= 32 * 4)
-      merge_results_warp_kernel<4><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+      merge_results_warp_kernel<4><<<grid, 256, 0, s>>>(src, parts, nq, k, out_dist, out_ids);
     else
-      merge_results_warp_kernel<8><<<grid, 256, 0, s>>>(dist, ids, parts, nq, k, out_dist, out_ids);
+      merge_results_warp_kernel<8><<<grid, 256, 0, s>>>(src, parts, nq, k, out_dist, out_ids);
     RBQ_LAUNCHED();
     return;
   }
@@ -1696,7 +1706,7 @@ void launch_merge_results(const float* dist, const int64_t* ids, int parts, int6
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "merge: parts * k too large");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(merge_results_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  merge_results_kernel<<<(unsigned)nq, 256, smem, s>>>(dist, ids, parts, nq, k, n2, out_dist, out_ids);
+  merge_results_kernel<<<(unsigned)nq, 256, smem, s>>>(src, parts, nq, k, n2, out_dist, out_ids);
   RBQ_LAUNCHED();
 }
 

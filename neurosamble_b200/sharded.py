@@ -51,33 +51,16 @@ def plan(nq: int, nprobe: int, k: int, k_rerank: int, probe_split: int, cand_cap
     return R, sl, cap
 
 
-def pack_results(dist_t: torch.Tensor, ids_t: torch.Tensor) -> torch.Tensor:
-    """One byte buffer per rank: [dist f32 (nq*k) | pad to 16 B | ids i64 (nq*k)]."""
-    n = dist_t.numel()
-    off = (n * 4 + 15) // 16 * 16
-    buf = torch.empty(off + n * 8, dtype=torch.uint8, device=dist_t.device)
-    buf[: n * 4].view(torch.float32).copy_(dist_t.reshape(-1))
-    buf[off: off + n * 8].view(torch.int64).copy_(ids_t.reshape(-1))
-    return buf
-
-
-def unpack_gathered(out: torch.Tensor, world: int, nq: int, k: int):
-    """[world * bytes] gathered buffers -> (dist [world, nq, k], ids [world, nq, k])."""
-    n = nq * k
-    off = (n * 4 + 15) // 16 * 16
-    per = out.view(world, -1)
-    d = per[:, : n * 4].contiguous().view(torch.float32).view(world, nq, k)
-    i = per[:, off: off + n * 8].contiguous().view(torch.int64).view(world, nq, k)
-    return d, i
-
-
-def gather_results(dist_t: torch.Tensor, ids_t: torch.Tensor, group=None):
-    """All-gather every rank's [nq, k] results with a single collective."""
+def gather_result_keys(stages, dist_t: torch.Tensor, ids_t: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather every rank's [nq, k] results with a single collective, each result packed as
+    one 8-byte key ((order-preserving distance bits) << 32 | id): [world, nq, k] int64."""
     world = dist.get_world_size(group)
-    buf = pack_results(dist_t, ids_t)
-    out = torch.empty(world * buf.numel(), dtype=torch.uint8, device=buf.device)
-    dist.all_gather_into_tensor(out, buf, group=group)
-    return unpack_gathered(out, world, dist_t.shape[0], dist_t.shape[1])
+    nq, k = dist_t.shape
+    keys = torch.empty((nq, k), dtype=torch.int64, device=dist_t.device)
+    stages.pack(dist_t, ids_t, keys)
+    out = torch.empty((world * nq, k), dtype=torch.int64, device=dist_t.device)
+    dist.all_gather_into_tensor(out, keys, group=group)
+    return out.view(world, nq, k)
 
 
 class ShardedIndexIVFRaBitQ:
@@ -141,11 +124,12 @@ class ShardedIndexIVFRaBitQ:
         d, i = self.local.search(t, k)
         return d, i
 
-    def search(self, x, k: int, stats: torch.Tensor | None = None):
+    def search(self, x, k: int, stats: torch.Tensor | None = None, timings: dict | None = None):
         """(D [nq, k], I [nq, k]) of the whole index for a batch every rank passes.
 
         stats (optional int64[2] on this rank's device) accumulates this rank's vectors
-        scanned / admitted by the prune."""
+        scanned / admitted by the prune; timings (optional dict) receives this rank's
+        milliseconds per stage."""
         t, on_dev = self.local._to_device(x)
         if self.world == 1:
             d, i = self.local.search(t, k)
@@ -154,7 +138,7 @@ class ShardedIndexIVFRaBitQ:
             d, i = sharded_search(LibStages(loc), t, int(k), int(loc.nprobe), int(loc.k_rerank), bool(loc.prune),
                                   int(loc.probe_split), int(loc.cand_cap), int(loc.coarse_margin),
                                   loc.info().padded_dim, self.rank, self.world, self.group, stats,
-                                  query_bits=int(loc.query_bits))
+                                  query_bits=int(loc.query_bits), timings=timings)
             if loc.metric == "ip":
                 d = 1.0 - 0.5 * d
         if on_dev:
@@ -207,18 +191,54 @@ class LibStages:
             _lib.call("rbq_merge_results", _ptr(d), _ptr(ids), d.shape[0], d.shape[1], d.shape[2], _ptr(out_d),
                       _ptr(out_i), self.st)
 
+    def pack(self, d, ids, keys):
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_pack_results", _ptr(d), _ptr(ids), d.numel(), _ptr(keys), self.st)
+
+    def merge_keys(self, keys, out_d, out_i):
+        """keys [parts, nq, k] (rbq_pack_results) -> top-k by (dist, id)."""
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_merge_result_keys", _ptr(keys), keys.shape[0], keys.shape[1], keys.shape[2], _ptr(out_d),
+                      _ptr(out_i), self.st)
+
     def rerank(self, q, cand, k, out_d, out_i):
         with torch.cuda.device(self.device):
             _lib.call("rbq_rerank", self.h, _ptr(q), q.shape[0], _ptr(cand), cand.shape[1], k, _ptr(out_d),
                       _ptr(out_i), self.st)
 
 
+class _StageClock:
+    """CUDA events at the stage boundaries of one sharded search (timings=dict): after the search,
+    timings[stage] = milliseconds on this rank's current stream."""
+
+    def __init__(self, timings, device):
+        self.t = timings
+        self.ev = []
+        self.on = timings is not None and device.type == "cuda"
+
+    def mark(self, name):
+        if self.on:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.ev.append((name, e))
+
+    def finish(self):
+        if not self.on:
+            return
+        self.ev[-1][1].synchronize()
+        for (_, a), (name, b) in zip(self.ev, self.ev[1:]):
+            self.t[name] = self.t.get(name, 0.0) + a.elapsed_time(b)
+
+
 def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, prune: bool, probe_split: int,
                    cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None,
-                   query_bits: int = 4):
+                   query_bits: int = 4, timings=None):
     """The four steps of a sharded search (module docstring) for the batch t [nq, D] that
-    every rank passes; `stages` computes (LibStages: librbq.so), this function moves data."""
+    every rank passes; `stages` computes (LibStages: librbq.so), this function moves data.
+    timings (optional dict) receives this rank's milliseconds per stage."""
     dev = t.device
+    clk = _StageClock(timings, dev)
+    clk.mark("start")
     nq = t.shape[0]
     P = nprobe
     R, slices, cap = plan(nq, P, k, k_rerank, probe_split, cand_cap, world)
@@ -234,37 +254,47 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     pl = torch.empty((nl, P), dtype=torch.int32, device=dev)
     gl = torch.empty((nl, P), dtype=torch.float32, device=dev)
     stages.coarse(qr_l, margin, pl, gl)
+    clk.mark("front_end (rotate + coarse, own queries)")
     qr_all = torch.empty((world * nl, dp), dtype=torch.float32, device=dev)
     dist.all_gather_into_tensor(qr_all, qr_l, group=group)
     send = torch.cat([pl, gl.view(torch.int32)], dim=1)
     recv = torch.empty((world * nl, 2 * P), dtype=torch.int32, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
+    clk.mark("all_gather (rotated rows, probes)")
     qr = qr_all[:nq]
     probes, g = recv[:nq, :P], recv[:nq, P:].view(torch.float32)  # row stride 2P
     planes = torch.empty((nq, query_bits, dp // 32), dtype=torch.int32, device=dev)
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)
+    clk.mark("query planes")
     # 2. seed: the bound seed of the nearest probe, on the rank that owns it (+inf elsewhere);
     #    min over ranks.
     tau = None
     if prune:
         tau = torch.empty(nq, dtype=torch.float32, device=dev)
         stages.bound_seed(qr, planes, delta, k1, probes[:, :1], g[:, :1], R, cap, tau)
+        clk.mark("bound seed")
         dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
+        clk.mark("all_reduce (seed)")
     # 3. this shard's probed lists from the shared threshold; rerank its candidates.
     mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
     md = torch.empty((nq, R), dtype=torch.float32, device=dev)
     stages.scan(qr, planes, delta, k1, probes, g, tau, None, R, int(prune), slices, cap, mi, md, stats)
+    clk.mark("scan")
     if k_rerank > 0:
         d = torch.empty((nq, k), dtype=torch.float32, device=dev)
         i = torch.empty((nq, k), dtype=torch.int64, device=dev)
         stages.rerank(t, mi, k, d, i)
     else:
         d, i = md[:, :k].contiguous(), mi[:, :k].contiguous()
-    # 4. one all-gather of the per-rank top-k, merged by (distance, id).
-    dall, iall = gather_results(d, i, group)
+    clk.mark("rerank")
+    # 4. one all-gather of the per-rank top-k (8-byte keys), merged by (distance, id).
+    kall = gather_result_keys(stages, d, i, group)
+    clk.mark("all_gather (results)")
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_i = torch.empty((nq, k), dtype=torch.int64, device=dev)
-    stages.merge(dall.contiguous(), iall.contiguous(), out_d, out_i)
+    stages.merge_keys(kall, out_d, out_i)
+    clk.mark("merge")
+    clk.finish()
     return out_d, out_i

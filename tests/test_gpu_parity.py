@@ -607,6 +607,13 @@ def test_merge_results_matches_oracle(oracle, parts, k):
     wi, wd = oracle.merge_candidates([(i[p], d[p]) for p in range(parts)], k)
     assert np.array_equal(oi.cpu().numpy(), wi)
     assert np.array_equal(u32(od.cpu().numpy()), u32(wd))
+    # the same merge from 8-byte result keys (what a sharded search all-gathers)
+    keys = torch.empty((parts, nq, k), dtype=torch.int64, device="cuda")
+    call("rbq_pack_results", ptr(dd), ptr(ii), parts * nq * k, ptr(keys), stream())
+    assert np.array_equal(keys.cpu().numpy().view(np.uint64), oracle._keys(i, d))
+    call("rbq_merge_result_keys", ptr(keys), parts, nq, k, ptr(od), ptr(oi), stream())
+    assert np.array_equal(oi.cpu().numpy(), wi)
+    assert np.array_equal(u32(od.cpu().numpy()), u32(wd))
 
 
 @pytest.mark.parametrize("nprobe,R", [(1, 30), (1, 400), (5, 100)])

@@ -1,8 +1,8 @@
 """List-sharded search across ranks, on CPU with gloo (world size 2).
 
 Each rank runs the oracle's sharded search for its own lists (l % 2 == rank), the per-rank
-[nq, k] results travel through the product's single-buffer all-gather
-(neurosamble_b200.sharded.gather_results), and rank 0 merges them by (distance, id).  The
+[nq, k] results travel through the product's single all-gather of 8-byte result keys
+(neurosamble_b200.sharded.gather_result_keys), and rank 0 merges them by (distance, id).  The
 merged result must equal the merge computed without any collective, and every rank must
 receive identical bytes.  A second test makes a rank leave before the collective: the other
 rank's all-gather must fail within the process group's short timeout (failure detected on
@@ -39,13 +39,33 @@ def _merge(dists, ids, k):
     return np.array(out_d, np.float32), np.array(out_i, np.int64)
 
 
+class _KeyPacker:
+    """The packing stage of LibStages (rbq_pack_results), restated on CPU tensors."""
+
+    def __init__(self, O):
+        self.O = O
+
+    def pack(self, d, ids, keys):
+        import torch
+        keys.copy_(torch.from_numpy(self.O._keys(ids.numpy(), d.numpy()).view(np.int64)))
+
+
+def _unkey(keys):
+    kk = np.ascontiguousarray(keys).view(np.uint64)
+    empty = kk == np.uint64(0xFFFFFFFFFFFFFFFF)
+    ids = np.where(empty, -1, (kk & np.uint64(0xFFFFFFFF)).astype(np.int64))
+    ob = (kk >> np.uint64(32)).astype(np.uint32)
+    d = np.where(empty, np.inf, np.where(ob & 0x80000000, ob & 0x7FFFFFFF, ~ob).astype(np.uint32).view(np.float32))
+    return d.astype(np.float32), ids
+
+
 def _worker(rank, world, port, outdir):
     import torch
     import torch.distributed as dist
 
     from conftest import mixture
     from oracle import oracle as O
-    from neurosamble_b200.sharded import gather_results
+    from neurosamble_b200.sharded import gather_result_keys
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -55,9 +75,10 @@ def _worker(rank, world, port, outdir):
     C, lab = O.kmeans(X, 16, iters=3)
     ix = O.build(X, C, lab, P, t4)
     d, i = O.search(ix, Q, 10, 6, 30, shard_rank=rank, shard_count=world)
-    gd, gi = gather_results(torch.from_numpy(d), torch.from_numpy(i))
+    kall = gather_result_keys(_KeyPacker(O), torch.from_numpy(d), torch.from_numpy(i))
+    gd, gi = _unkey(kall.numpy())
     with open(os.path.join(outdir, f"rank{rank}.pkl"), "wb") as f:
-        pickle.dump({"local": (d, i), "gathered": (gd.numpy(), gi.numpy())}, f)
+        pickle.dump({"local": (d, i), "gathered": (gd, gi)}, f)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -83,7 +104,8 @@ def _leaver(rank, world, port, outdir):
     import torch
     import torch.distributed as dist
 
-    from neurosamble_b200.sharded import gather_results
+    from oracle import oracle as O
+    from neurosamble_b200.sharded import gather_result_keys
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -92,7 +114,7 @@ def _leaver(rank, world, port, outdir):
         return  # leaves between steps: never joins the collective
     err = ""
     try:
-        gather_results(torch.zeros((3, 2)), torch.zeros((3, 2), dtype=torch.int64))
+        gather_result_keys(_KeyPacker(O), torch.zeros((3, 2)), torch.zeros((3, 2), dtype=torch.int64))
     except Exception as e:  # noqa: BLE001
         err = type(e).__name__ + ": " + str(e)[:200]
     with open(os.path.join(outdir, "rank0.txt"), "w") as f:
@@ -158,6 +180,19 @@ class _OracleStages:
         mi, md = self.O.merge_candidates([(ids[p].numpy(), d[p].numpy()) for p in range(d.shape[0])], d.shape[2])
         out_d.copy_(torch.from_numpy(md))
         out_i.copy_(torch.from_numpy(mi))
+
+    def pack(self, d, ids, keys):
+        import torch
+        keys.copy_(torch.from_numpy(self.O._keys(ids.numpy(), d.numpy()).view(np.int64)))
+
+    def merge_keys(self, keys, out_d, out_i):
+        import torch
+        kk = keys.numpy().view(np.uint64)
+        empty = kk == np.uint64(0xFFFFFFFFFFFFFFFF)
+        ids = np.where(empty, -1, (kk & np.uint64(0xFFFFFFFF)).astype(np.int64))
+        ob = (kk >> np.uint64(32)).astype(np.uint32)
+        d = np.where(empty, np.inf, np.where(ob & 0x80000000, ob & 0x7FFFFFFF, ~ob).astype(np.uint32).view(np.float32))
+        self.merge(torch.from_numpy(d.astype(np.float32)), torch.from_numpy(ids), out_d, out_i)
 
     def rerank(self, q, cand, k, out_d, out_i):
         import torch
