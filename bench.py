@@ -359,7 +359,9 @@ def run_ours(args, cfg):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1 and "NCCL_DEBUG" not in os.environ:
+    if world > 1:
+        log(f"[rank {rank}] NCCL_DEBUG={os.environ.get('NCCL_DEBUG')!r} NCCL_DEBUG_FILE={os.environ.get('NCCL_DEBUG_FILE')!r}")
+    if world > 1 and os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
         # NCCL's communicator set-up lines (ranks, devices, NVLS) go to stderr, so stdout carries
         # only the JSON line while the log still shows every rank joining
         os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")

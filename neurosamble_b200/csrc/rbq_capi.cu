@@ -722,7 +722,7 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   sl = std::min(sl, own);
   sl = std::min(sl, std::max(1, 8192 / sp.R));
   sp.slices = std::max(1, sl);
-  const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(16, sp.P / 2);
+  const int margin = p.coarse_margin > 0 ? p.coarse_margin : std::max(32, sp.P / 2);
   sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
   sp.prune = p.prune ? 1 : 0;
   sp.qbits = query_bits_of(p.query_bits);
@@ -1858,7 +1858,7 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
     if (nq == 0) return;
     DeviceGuard dg(ix.device);
     cudaStream_t s = as_stream(stream);
-    const int m = std::min(ix.K, std::min(nprobe + (margin > 0 ? margin : std::max(16, nprobe / 2)), 1024));
+    const int m = std::min(ix.K, std::min(nprobe + (margin > 0 ? margin : std::max(32, nprobe / 2)), 1024));
     const int64_t chunk = coarse_rows_per_call(Qr_dev, ix.C_rot, ix.K, ix.Dp, m, nq);
     Scratch sc(s);
     const CoarseScratch cs = coarse_scratch(sc, Qr_dev, ix.C_rot, ix.K, ix.Dp, m, chunk);

@@ -280,8 +280,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) coarse_tc_kernel(const __grid_c
 // (the m-th smallest key kept so far).  When a buffer could overflow, its warp cuts it to the m
 // smallest by a cooperative radix select and the threshold tightens; a threshold is never below
 // the final m-th smallest key, so the result is the m smallest keys of the row, as
-// topm_rows_kernel's.  At the end each row writes its m columns (any order) and (p-th smallest
-// score, m-th smallest score).  Every wait is bounded and a failed wait makes all roles stop.
+// topm_rows_kernel's.  At the end each row writes its m columns (ascending) and its m-th smallest
+// score.  Every wait is bounded and a failed wait makes all roles stop.
 // ---------------------------------------------------------------------------------------
 constexpr int kFtThreads = 192;
 constexpr int kFtStages = 4;
@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(kFtThreads, 1)
         const int n = __shfl_sync(0xffffffffu, cnt, L);
         unsigned long long* lb = rowbuf + ((size_t)blockIdx.x * kTcM + warp * 32 + L) * cap;
         const int64_t qL = (int64_t)q0 + warp * 32 + L;
-        const unsigned long long kp = warp_sort_keys<KPL>(lb, n, m, p, lane);
+        warp_sort_keys<KPL>(lb, n, m, m, lane);
         __syncwarp();
         const int kept = n < m ? n : m;
         for (int i = lane; i < m; i += 32) cand[qL * m + i] = i < kept ? (int32_t)(lb[i] & 0xFFFFFFFFu) : -1;
@@ -565,8 +565,7 @@ __global__ void __launch_bounds__(kFtThreads, 1)
         const bool cutL = (__shfl_sync(0xffffffffu, (int)cut, L) != 0) || n > m;
         const unsigned long long km = n >= m ? lb[m - 1] : kEmptyKey;
         if (lane == 0)
-          bounds[qL] = make_float2(kp == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(kp >> 32)),
-                                   cutL ? from_ordered_bits((uint32_t)(km >> 32)) : __int_as_float(0x7f800000));
+          bounds[qL] = make_float2(0.0f, cutL ? from_ordered_bits((uint32_t)(km >> 32)) : __int_as_float(0x7f800000));
       }
     }
   }

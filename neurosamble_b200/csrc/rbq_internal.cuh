@@ -192,13 +192,14 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
 void launch_coarse_scores(const float* A, int64_t nq, const float* C, const float* c_n2, int K, int d,
                           float* S, cudaStream_t s);
 // Per row of S [nq, K]: the m smallest (score, id) keys -> cand [nq, m] (any order).  With
-// bounds, also (p-th smallest score, m-th smallest score) per row (+inf when all K are kept).
+// bounds, also the row's m-th smallest score in bounds[q].y (+inf when all K are kept).
 void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s, int p = 0,
                       float2* bounds = nullptr);
 // Exact refine: g = sum_j double(a_j - c_j)^2 for the m candidates, then top-p by (g, id).  With
 // bounds (from launch_topm_rows), cmax2 (max |c|^2, device scalar) and unsafe ([1 + nq] ints,
-// unsafe[0] = 0 on entry), queries whose shortlist may miss a true top-p list under the tf32
-// error bound are appended to unsafe.
+// unsafe[0] = 0 on entry), queries whose shortlist may miss a true top-p list are appended to
+// unsafe: a list outside the shortlist has exact distance >= |q|^2 + (m-th tf32 score) - E (E the
+// tf32 score error bound), which must exceed the p-th exact distance found.
 void launch_refine_topp(const float* A, int64_t nq, const float* C, int d, const int32_t* cand, int m,
                         int p, int32_t* probes, float* g, cudaStream_t s, const float2* bounds = nullptr,
                         const float* cmax2 = nullptr, int* unsafe = nullptr);

@@ -179,16 +179,9 @@ __global__ void __launch_bounds__(256) topm_rows_kernel(const float* __restrict_
   }
   for (int i = threadIdx.x; i < m; i += blockDim.x)
     cand[q * m + i] = i < filled ? (int32_t)(cur[i] & 0xFFFFFFFFu) : -1;
-  if (bounds) {  // (p-th smallest score, m-th smallest score; +inf when every column is kept)
-    __syncthreads();
-    float sp = __int_as_float(0x7f800000);
-    if (filled >= p && p >= 1) {
-      const unsigned long long kp = block_keep_smallest(cur, filled, p, nxt, s_hist, s_misc, &s_kmax, &s_cnt);
-      sp = from_ordered_bits((uint32_t)(kp >> 32));
-    }
-    if (threadIdx.x == 0)
-      bounds[q] = make_float2(sp, cut ? from_ordered_bits((uint32_t)(thr >> 32)) : __int_as_float(0x7f800000));
-  }
+  // .y: the m-th smallest score (+inf when every column is kept); .x is not used
+  if (bounds && threadIdx.x == 0)
+    bounds[q] = make_float2(0.0f, cut ? from_ordered_bits((uint32_t)(thr >> 32)) : __int_as_float(0x7f800000));
 }
 
 void launch_topm_rows(const float* S, int64_t nq, int K, int m, int32_t* cand, cudaStream_t s, int p,
@@ -228,6 +221,19 @@ __device__ __forceinline__ float tf32_score_bound(float qn2, float cmax2, int d)
   return rel * sqrtf(qn2 * cmax2) + 1.90734863e-6f * (qn2 + cmax2);  // + 2^-19 (|q|^2 + |c|^2)
 }
 
+// The shortlist holds every column whose tf32 score is below its m-th smallest tf32 score sm, so a
+// list outside it has exact score >= sm - E and exact distance >= |q|^2 + sm - E.  If that is above
+// the p-th smallest exact distance gp found inside the shortlist (with slack for the float
+// roundings of the distances), no outside list can be among the true p nearest.
+__device__ __forceinline__ bool shortlist_is_safe(float qn2, float sm, float gp, float cmax2, int d)
+{
+  if (!(sm < __int_as_float(0x7f800000))) return true;  // every column was shortlisted
+  if (!(gp < __int_as_float(0x7f800000))) return false;  // fewer than p candidates
+  const float e = tf32_score_bound(qn2, cmax2, d);
+  const float slack = 9.53674316e-7f * (qn2 + fabsf(sm) + gp);  // 2^-20 of the magnitudes
+  return qn2 + sm - e - slack > gp;
+}
+
 template <int EPL>
 __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restrict__ A, const float* __restrict__ C,
                                                           int d, const int32_t* __restrict__ cand, int m, int p,
@@ -243,20 +249,6 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   for (int j = threadIdx.x; j < d; j += blockDim.x) a[j] = A[q * d + j];
   for (int i = threadIdx.x; i < mp2; i += blockDim.x) keys[i] = kEmptyKey;
   __syncthreads();
-  if (bounds && warp == 0) {
-    // The shortlist holds every column whose tf32 score is below its m-th smallest score b.y; the
-    // exact top p all have tf32 scores <= (p-th smallest) + 2E.  If b.y is not above that, a true
-    // probe may lie outside the shortlist: the query is queued for the exact pass over all lists.
-    float v = 0.0f;
-    for (int j = lane; j < d; j += 32) v = __fadd_rn(v, __fmul_rn(a[j], a[j]));
-#pragma unroll
-    for (int off = 16; off; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-    if (lane == 0) {
-      const float2 b = bounds[q];
-      const float e = tf32_score_bound(v, *cmax2, d);
-      if (!(b.y > b.x + 2.0f * e)) unsafe[1 + atomicAdd(unsafe, 1)] = (int)q;
-    }
-  }
   auto finish = [&](int i, int c, double s) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
@@ -300,6 +292,17 @@ __global__ void __launch_bounds__(256) refine_topp_kernel(const float* __restric
   }
   __syncthreads();
   block_bitonic_sort(keys, mp2);
+  if (bounds && warp == 0) {  // queue the query for the exact pass if the shortlist may miss a probe
+    double v = 0.0;
+    for (int j = lane; j < d; j += 32) v = __dadd_rn(v, __dmul_rn((double)a[j], (double)a[j]));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (lane == 0) {
+      const unsigned long long kp = p <= mp2 ? keys[p - 1] : kEmptyKey;
+      const float gp = kp == kEmptyKey ? __int_as_float(0x7f800000) : from_ordered_bits((uint32_t)(kp >> 32));
+      if (!shortlist_is_safe((float)v, bounds[q].y, gp, *cmax2, d)) unsafe[1 + atomicAdd(unsafe, 1)] = (int)q;
+    }
+  }
   for (int i = threadIdx.x; i < p; i += blockDim.x) {
     const unsigned long long key = keys[i];
     if (key == kEmptyKey) {
