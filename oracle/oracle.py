@@ -67,6 +67,10 @@ def lib():
                                _i64p, _f32p, _i64p, _i32]
         L.orc_bound_seed.argtypes = [_i64p, _u32p, _f32p, _f32p, _f32p, _i32, _u32p, _f32p, _f32p, _i64, _i32p,
                                      _f32p, _i32, _i32, _i32, _i32, ctypes.c_void_p, _f32p, _i32]
+        L.orc_float_to_half.argtypes = [ctypes.c_void_p, _i64, ctypes.c_void_p]
+        L.orc_float_to_half.restype = None
+        L.orc_half_to_float.argtypes = [ctypes.c_void_p, _i64, ctypes.c_void_p]
+        L.orc_half_to_float.restype = None
         L.orc_l2_exact.argtypes = [_f32p, _f32p, _i32]
         L.orc_l2_exact.restype = ctypes.c_float
         L.orc_rerank.argtypes = [_f32p, _i32, _f32p, _i64, _i64p, _i32, _i32, _f32p, _i64p]
@@ -235,11 +239,16 @@ def exact_ip(q, code) -> float:
     return float(lib().orc_exact_ip(_c(q, np.float32), code, code.size))
 
 
+LUT_MODES = (16, 32)  # query_bits values of the LUT16 / LUT32 search modes
+
+
 def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, prune=1,
-         slices=1, shard_rank=0, shard_count=1, with_stats=False, tau0=None, init=None, owner=None):
+         slices=1, shard_rank=0, shard_count=1, with_stats=False, tau0=None, init=None, owner=None, mode=None):
     """rbq_scan: top-R (ids, estimated distances) per query.  tau0 [nq] seeds every slice's
     threshold; init = (ids, dist) [nq, R] are an earlier scan's candidates slice 0 starts from;
-    owner [K] (default l % shard_count) is the list -> shard map."""
+    owner [K] (default l % shard_count) is the list -> shard map.  mode 16 / 32 (LUT16 / LUT32)
+    ranks by the query-table estimate instead of the planes' popcounts (planes then hold the
+    4-bit codes the query preparation made, unused); default: the planes' code width."""
     Qr = _c(Qr, np.float32)
     nq = Qr.shape[0]
     probes, g = _c(probes, np.int32), _c(g, np.float32)
@@ -264,7 +273,7 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
         lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
                        _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g,
                        nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, ow,
-                       out_ids, out_d, stats, _bits_of(planes, nq, ix.dp // 32))
+                       out_ids, out_d, stats, mode if mode else _bits_of(planes, nq, ix.dp // 32))
     elif init is not None:
         out_ids[:], out_d[:] = merge_candidates([(init_i, init_d)], R)
     else:
@@ -391,14 +400,24 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     are split into slices > 1, 0 never, 1 always; exchange=True is the sharded search's
     pipeline (two phases, threshold shared by all shards).  rerank_depth == 0 returns the
     scan's top-k estimates (the reference behaviour).  query_bits 8 (QUANT8) quantises the
-    queries to 8 bits with ix.t8 (set it to query_scale(dp, seed, 7) of the index)."""
+    queries to 8 bits with ix.t8 (set it to query_scale(dp, seed, 7) of the index); 16 / 32
+    (LUT16 / LUT32) estimate with fp16 / fp32 tables of the float query (one pass, no seed)."""
     Q = _c(Q, np.float32)
     Qr = rotate(Q, ix.P)
     probes, g = coarse(Qr, ix.c_rot, nprobe)
     if query_bits == 8 and getattr(ix, "t8", None) is None:
         raise ValueError("QUANT8 needs the index's 8-bit scale: set ix.t8 = query_scale(dp, seed, 7)")
-    planes, delta, k1, _ = query_prep(Qr, ix.t4 if query_bits == 4 else ix.t8, query_bits)
+    planes, delta, k1, _ = query_prep(Qr, ix.t8 if query_bits == 8 else ix.t4, 8 if query_bits == 8 else 4)
     R = rerank_depth if rerank_depth > 0 else k
+    if query_bits in LUT_MODES:  # the table estimate is final: one pass, no seed
+        res = scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank, shard_count,
+                   with_stats=True, owner=owner, mode=query_bits)
+        cand, cd = res[0], res[1]
+        if rerank_depth > 0:
+            dist, ids = rerank(ix.X, Q, cand, k)
+        else:
+            dist, ids = cd[:, :k].copy(), cand[:, :k].copy()
+        return (dist, ids, res[2]) if with_stats else (dist, ids)
     two = slices > 1 if seeded < 0 else seeded > 0
     if exchange or two:
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
@@ -414,6 +433,21 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     if with_stats:
         return dist, ids, res[2]
     return dist, ids
+
+
+def float_to_half_bits(x) -> np.ndarray:
+    """The oracle's fp32 -> fp16 rounding (round to nearest, ties to even) as uint16 bits."""
+    x = _c(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().orc_float_to_half(x.ctypes.data_as(ctypes.c_void_p), x.size, out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+def half_bits_to_float(h) -> np.ndarray:
+    h = np.ascontiguousarray(h, np.uint16)
+    out = np.empty(h.shape, np.float32)
+    lib().orc_half_to_float(h.ctypes.data_as(ctypes.c_void_p), h.size, out.ctypes.data_as(ctypes.c_void_p))
+    return out
 
 
 def recall(ids, gt) -> float:

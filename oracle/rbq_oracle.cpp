@@ -495,6 +495,103 @@ float orc_exact_ip(const float* q, const uint32_t* code, int W)
   return v[0];
 }
 
+// fp32 -> IEEE binary16, round to nearest, ties to even (the rounding of CUDA's __float2half),
+// and back (exact).  Written from the IEEE 754 encodings.
+static uint16_t float_to_half_rn(float f)
+{
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const uint32_t ex = (x >> 23) & 0xFFu;
+  uint32_t man = x & 0x7FFFFFu;
+  if (ex == 0xFFu) return (uint16_t)(sign | 0x7C00u | (man ? 0x200u | (man >> 13) : 0u));  // inf / nan
+  const int e = (int)ex - 127 + 15;  // half exponent
+  if (e >= 31) return (uint16_t)(sign | 0x7C00u);  // overflow -> inf
+  if (e <= 0) {  // half subnormal or zero
+    if (e < -10) return (uint16_t)sign;  // rounds to zero
+    man |= 0x800000u;  // implicit bit
+    const int shift = 14 - e;  // bits dropped: 13 + (1 - e)
+    const uint32_t half_man = man >> shift;
+    const uint32_t rem = man & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+    uint32_t r = half_man;
+    if (rem > halfway || (rem == halfway && (half_man & 1u))) ++r;
+    return (uint16_t)(sign | r);  // a carry into the exponent field gives the smallest normal: correct
+  }
+  uint32_t r = ((uint32_t)e << 10) | (man >> 13);
+  const uint32_t rem = man & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) ++r;  // a carry may reach the exponent / inf: correct
+  return (uint16_t)(sign | r);
+}
+
+static float half_to_float(uint16_t h)
+{
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t ex = (h >> 10) & 0x1Fu;
+  uint32_t man = h & 0x3FFu;
+  uint32_t x;
+  if (ex == 0) {
+    if (man == 0) {
+      x = sign;
+    } else {  // subnormal: normalise
+      int e = -1;
+      do {
+        man <<= 1;
+        ++e;
+      } while (!(man & 0x400u));
+      x = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FFu) << 13);
+    }
+  } else if (ex == 0x1Fu) {
+    x = sign | 0x7F800000u | (man << 13);
+  } else {
+    x = sign | ((ex - 15 + 127) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &x, 4);
+  return f;
+}
+
+// LUT16 / LUT32 query tables (precomputeAllLUTs and precomputeAllLUTs_fp16_simple,
+// searcher_gpu.cu:65-108 and searcher_gpu_shared_mem_opt.cu:520-549): for chunk c (dims
+// 4c..4c+3) and 4-bit pattern p, the fp32 sum from 0, in dimension order, of q[4c + b] over the b
+// with bit 3-b of p set; LUT16 stores it rounded to fp16.  Returned as floats.
+static void lut_tables(const float* qr, int Dp, bool half, std::vector<float>& lut)
+{
+  const int chunks = Dp / 4;
+  lut.assign((size_t)chunks * 16, 0.0f);
+  for (int c = 0; c < chunks; ++c)
+    for (int p = 0; p < 16; ++p) {
+      float sum = 0.0f;
+      for (int b = 0; b < 4; ++b)
+        if (p & (1 << (3 - b))) sum += qr[4 * c + b];
+      lut[(size_t)c * 16 + p] = half ? half_to_float(float_to_half_rn(sum)) : sum;
+    }
+}
+
+// <bits, q> by the tables: words in order, nibbles from the top (bit 31) down, added one by one
+// (computeInnerProductsWithLUT16Opt, searcher_gpu_shared_mem_opt.cu:165-177).
+static float lut_ip(const std::vector<float>& lut, const uint32_t* code, int W)
+{
+  float ip = 0.0f;
+  for (int w = 0; w < W; ++w)
+    for (int ci = 0; ci < 8; ++ci) {
+      const int pattern = (int)((code[w] >> (28 - 4 * ci)) & 0xFu);
+      ip += lut[(size_t)(w * 8 + ci) * 16 + pattern];
+    }
+  return ip;
+}
+
+inline bool is_lut_mode(int qbits) { return qbits == 16 || qbits == 32; }
+
+// The fp16 conversions on their own, for checking them against another implementation.
+void orc_float_to_half(const float* x, int64_t n, uint16_t* out)
+{
+  for (int64_t i = 0; i < n; ++i) out[i] = float_to_half_rn(x[i]);
+}
+void orc_half_to_float(const uint16_t* h, int64_t n, float* out)
+{
+  for (int64_t i = 0; i < n; ++i) out[i] = half_to_float(h[i]);
+}
+
 struct ScanIndex {
   const int64_t* list_off;
   const uint32_t* ids;
@@ -527,7 +624,10 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
   const int64_t total = pre[np];
   // Bound seed: a pruning slice with no threshold and no candidates yet starts from the R-th
   // smallest upper bound est + f_err * sqrt(g) over its leading whole lists holding >= R vectors.
-  if (prune && std::isinf(tau) && keys.empty() && total >= R) {
+  const bool lut = is_lut_mode(ix.qbits);
+  std::vector<float> table;
+  if (lut) lut_tables(qr, W * 32, ix.qbits == 16, table);
+  if (!lut && prune && std::isinf(tau) && keys.empty() && total >= R) {
     int64_t nb = 0;
     for (int i = 1; i <= np && nb < R; ++i) nb = pre[i];
     std::vector<uint64_t> ub((size_t)nb);
@@ -555,12 +655,21 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
       const float sqrt_g = sqrtf(g);
       const int64_t s = ix.list_off[probe_l[cur]] + (f - pre[cur]);
       const uint32_t* code = ix.codes + (size_t)s * W;
+      ++n_scanned;
+      if (lut) {  // LUT16 / LUT32: the table estimate is the candidate's distance
+        const float ip = lut_ip(table, code, W);
+        const float est = (ix.fadd[s] + g) + ix.frescale[s] * (ip + k1);
+        if (est <= tau) {
+          ++n_admit;
+          keys.push_back(make_key(est, ix.ids[s]));
+        }
+        continue;
+      }
       int32_t acc = orc_popcount_ip(pl, code, W, ix.qbits);
       float ip = (float)acc * delta;
       float base_d = ix.fadd[s] + g;
       float est = base_d + ix.frescale[s] * (ip + k1);
       float low = est - ix.ferr[s] * sqrt_g;
-      ++n_scanned;
       if (!prune || low < tau) {
         ++n_admit;
         float eip = orc_exact_ip(qr, code, W);
@@ -672,7 +781,7 @@ void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* code
             init.push_back(make_key(init_dist[q * R + r], (uint32_t)init_ids[q * R + r]));
       for (int s = 0; s < slices; ++s) {
         int a = (int)(((int64_t)s * m) / slices), b = (int)(((int64_t)(s + 1) * m) / slices);
-        scan_slice(ix, W, Qr + (size_t)q * Dp, planes + (size_t)q * qbits * W, delta[q], k1[q],
+        scan_slice(ix, W, Qr + (size_t)q * Dp, planes + (size_t)q * (is_lut_mode(qbits) ? 4 : qbits) * W, delta[q], k1[q],
                    own_l.data() + a, own_g.data() + a, b - a, tau0 ? tau0[q] : INFINITY, s == 0 ? init : none,
                    R, tile, cap, prune, keys, loc);
         all.insert(all.end(), keys.begin(), keys.end());

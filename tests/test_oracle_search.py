@@ -299,3 +299,43 @@ def test_balanced_kmeans_edge_cases(oracle, n, K, iters):
     C = oracle.kmeans_balanced(X, K, iters)
     assert C.shape == (K, 8) and np.isfinite(C).all()
     assert (np.bincount(oracle.assign(X, C), minlength=K) > 0).all()
+
+
+def test_fp16_rounding_of_the_lut16_tables():
+    """LUT16 rounds its table entries to fp16 as CUDA's __float2half does (nearest, ties to even);
+    the oracle's own conversion must agree with IEEE (numpy) on normal, subnormal, halfway,
+    overflow and special values, and convert back exactly."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    hv = np.arange(0, 1 << 15, dtype=np.uint16).view(np.float16).astype(np.float32)
+    hv = hv[np.isfinite(hv)]
+    xs = np.concatenate([
+        rng.standard_normal(100000).astype(np.float32) * np.float32(10.0) ** rng.integers(-9, 6, 100000).astype(np.float32),
+        np.arange(1, 4000, dtype=np.float32) * np.float32(2.0 ** -25),
+        hv, ((hv[:-1] + hv[1:]) / 2).astype(np.float32), -hv,
+        np.array([0.0, -0.0, 65504, 65519.99, 65520, 1e9, -1e9, np.inf, -np.inf], np.float32)])
+    with np.errstate(over="ignore"):
+        want = xs.astype(np.float16).view(np.uint16)
+    got = O.float_to_half_bits(xs)
+    assert np.array_equal(got, want)
+    back = O.half_bits_to_float(got)
+    assert np.array_equal(back.view(np.uint32), got.view(np.float16).astype(np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("mode", [16, 32])
+def test_lut_modes_rank_by_the_table_estimate(mode):
+    """LUT16 / LUT32 return the top k by the table estimate with R = 0: with one slice and with
+    several (each slice keeps its own top k, merged), and the same set as scoring every probed
+    vector with the tables and sorting."""
+    from conftest import mixture
+    from oracle import oracle as O
+    X, Q = mixture(5000, 64, 12, 0.3, 20, seed=3)
+    P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
+    C, lab = O.kmeans(X, 16, iters=3)
+    ix = O.build(X, C, lab, P, t4)
+    d1, i1 = O.search(ix, Q, 10, 6, 0, query_bits=mode)
+    d3, i3 = O.search(ix, Q, 10, 6, 0, query_bits=mode, slices=3)
+    assert np.array_equal(i1, i3) and np.array_equal(d1.view(np.uint32), d3.view(np.uint32))
+    assert np.all(np.diff(d1, axis=1) >= 0)
+    _, gt = O.knn_exact(X, Q, 10)
+    assert O.recall(i1, gt) > 0.3
