@@ -83,8 +83,12 @@ typedef struct {
   int32_t seeded;        /* every slice starts from the nearest probed list's bound seed      */
                          /* (rbq_bound_seed); -1 = auto (on when the probes are split into      */
                          /* slices), 0 = off (each slice seeds itself), 1 = on                  */
-  int32_t query_bits;    /* query code width: 4 = QUANT4 (default; 0 means 4), 8 = QUANT8       */
-                         /* (search_mode, ivf_rabitq.hpp:111-120; ivf_rabitq.cu:313-345)        */
+  int32_t query_bits;    /* search mode (search_mode, ivf_rabitq.hpp:111-120; ivf_rabitq.cu:      */
+                         /* 294-345): 4 = QUANT4 (default; 0 means 4), 8 = QUANT8 (popcount     */
+                         /* estimator over 4- / 8-bit query codes), 16 = LUT16, 32 = LUT32      */
+                         /* (the estimate from fp16 / fp32 tables of the float query, one entry */
+                         /* per 4-dim code nibble; it is the candidate's distance, so there is  */
+                         /* no exact pass, no error-bound prune and no bound seed)             */
   int32_t graph;         /* 1: the first search of a batch size (and these parameters) is       */
                          /* captured as a CUDA graph and later ones replay it: copy in, one     */
                          /* graph launch, copy out (small batches are launch-bound).  Up to 8   */
@@ -203,7 +207,8 @@ int rbq_rotate(rbq_index_t* index, const float* X_dev, int64_t n, float* Y_dev, 
  * 4): planes [nq, B, W], delta [nq], k1 [nq] (= -0.5 sum q).  Replaces exrabitq_quantize_query
  * (searcher_gpu_quantize_query.cu:655-793) and computeQueryFactorsWarpKernel
  * (gpu_index/ivf_gpu.cu:1451-1490).  The scan entry points below take the same query_bits
- * as the planes they are given. */
+ * as the planes they are given.  query_bits 16 / 32 (LUT16 / LUT32) prepare 4-bit planes: those
+ * modes read only k1, and their scan builds its tables from the rotated query itself. */
 int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t* planes_dev,
                    float* delta_dev, float* k1_dev, int32_t query_bits, void* stream);
 /* Approximate coarse scores S [nq, K] = |c_rot|^2 - 2 <q_rot, c_rot> (the shortlist ranking).
@@ -230,7 +235,10 @@ int rbq_coarse(rbq_index_t* index, const float* Qr_dev, int64_t nq, int32_t npro
  *     all R are present).
  * Query q's probes are probes_dev[q * probe_stride + p], p < nprobe (g alike; probe_stride
  * 0 = nprobe), so the two phases can read columns 0 and 1.. of one [nq, P] array.
- * stats_dev (optional, u64[2]) accumulates vectors scanned / admitted by the prune. */
+ * stats_dev (optional, u64[2]) accumulates vectors scanned / admitted by the prune.
+ * query_bits 16 / 32 (LUT16 / LUT32, computeInnerProductsWithLUT16Opt,
+ * searcher_gpu_shared_mem_opt.cu:36-200): the candidates are the top R by the table estimate
+ * (prune has no effect; "admitted" counts the estimates kept below the running threshold). */
 int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
              const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
              int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,

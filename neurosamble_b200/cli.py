@@ -17,8 +17,9 @@ relaunching the same command as N processes through torch.distributed.run (127.0
 port).  Under torchrun (WORLD_SIZE > 1, one rank per GPU) the lists are sharded over the
 ranks and rank 0 writes the files.
 
-Accepted for compatibility: ``--bits 1`` only and ``--search_mode QUANT4`` or ``QUANT8`` (4- or
-8-bit query codes; LUT16 / LUT32 exit with status 2); ``--strategy
+Accepted for compatibility: ``--bits 1`` only and ``--search_mode`` QUANT4 / QUANT8 (popcount
+estimator over 4- or 8-bit query codes) or LUT16 / LUT32 (fp16 / fp32 tables of the float query,
+the estimate is the candidate distance); ``--strategy
 none`` turns the error-bound prune off, ``centroid_reorder`` keeps it on, with this library's
 threshold seeds in place of the reference's centroid-distance seed (``--reorder_scale`` is
 accepted and has no effect); ``--stream`` / ``--stream_batch`` (the build always streams
@@ -35,6 +36,9 @@ import sys
 import time
 
 import numpy as np
+
+# --search_mode -> IndexIVFRaBitQ.query_bits (search_mode, ivf_rabitq.hpp:113-118)
+SEARCH_MODES = {"QUANT4": 4, "QUANT8": 8, "LUT16": 16, "LUT32": 32}
 
 
 def parse_args(argv=None) -> argparse.Namespace:
@@ -87,8 +91,8 @@ def check_args(a: argparse.Namespace) -> str:
         return "--gpus must be >= 1"
     if a.bits != 1:
         return f"--bits {a.bits}: only 1-bit RaBitQ codes are implemented"
-    if a.search_mode not in ("QUANT4", "QUANT8"):
-        return f"--search_mode {a.search_mode}: only QUANT4 and QUANT8 (4- / 8-bit query codes) are implemented"
+    if a.search_mode not in SEARCH_MODES:
+        return f"--search_mode {a.search_mode}: one of {', '.join(SEARCH_MODES)}"
     if a.topk < 1 or a.batch < 1 or a.nprobe < 1 or a.nlist < 1 or a.rerank < 0:
         return "--topk, --batch, --nprobe, --nlist must be >= 1 and --rerank >= 0"
     return ""
@@ -159,7 +163,7 @@ def main(argv=None) -> int:
     index.nprobe = a.nprobe
     index.k_rerank = a.rerank
     index.prune = a.strategy != "none"
-    index.query_bits = 8 if a.search_mode == "QUANT8" else 4
+    index.query_bits = SEARCH_MODES[a.search_mode]
 
     t1 = time.perf_counter()
     writer = NeighborWriter(a.out_nbr, a.out_dist, a.topk) if rank == 0 else None

@@ -682,16 +682,23 @@ void train_kmeans(Index& ix, const float* X, int64_t n, cudaStream_t s)
 struct SearchPlan {
   int P, k, R, cap, slices, m;
   int prune;
-  int qbits;    // query code width: 4 (QUANT4) or 8 (QUANT8)
+  int qbits;    // search mode: 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)
   bool seeded;  // two-phase scan (search_scan)
 };
 
+// Search mode of query_bits (0 means 4): 4 / 8 = QUANT4 / QUANT8 (popcount estimator over 4- or
+// 8-bit query codes), 16 / 32 = LUT16 / LUT32 (fp16 / fp32 tables of the float query).
 int query_bits_of(int32_t bits)
 {
   const int qb = bits == 0 ? 4 : bits;
-  RBQ_CHECK(qb == 4 || qb == 8, RBQ_ERR_INVALID, "query bits must be 4 (QUANT4) or 8 (QUANT8)");
+  RBQ_CHECK(qb == 4 || qb == 8 || qb == 16 || qb == 32, RBQ_ERR_INVALID,
+            "query bits must be 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)");
   return qb;
 }
+
+// Code width of the query preparation for a search mode: the LUT modes use only its k1 (and
+// take the 4-bit planes it also makes).
+int prep_bits_of(int qbits) { return qbits == 8 ? 8 : 4; }
 
 // Scale constant of the query code width: t4 (const_scaling_factor_4bit, best rescale for 3
 // extra bits) or t8 (const_scaling_factor_8bit, 7 extra bits; quantizer_gpu.cuh:81-85), the
@@ -726,7 +733,7 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   sp.m = std::min(ix.K, std::min(sp.P + margin, 1024));
   sp.prune = p.prune ? 1 : 0;
   sp.qbits = query_bits_of(p.query_bits);
-  sp.seeded = p.seeded < 0 ? sp.slices > 1 : p.seeded > 0;
+  sp.seeded = sp.qbits < 16 && (p.seeded < 0 ? sp.slices > 1 : p.seeded > 0);  // no bound seed in LUT modes
   return sp;
 }
 
@@ -817,8 +824,9 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       coarse_scratch(sc, Qr_pre ? Qr_pre : Qr_buf, ix.C_rot, ix.K, ix.Dp, sp.m, fe_chunk);
   int32_t* probes = sc.get<int32_t>((size_t)chunk * sp.P);
   float* g = sc.get<float>((size_t)chunk * sp.P);
-  uint32_t* planes = sc.get<uint32_t>((size_t)chunk * sp.qbits * ix.W);
-  const float qt = query_t(ix, sp.qbits);
+  const int pb = prep_bits_of(sp.qbits);
+  uint32_t* planes = sc.get<uint32_t>((size_t)chunk * pb * ix.W);
+  const float qt = query_t(ix, pb);
   float* delta = sc.get<float>(chunk);
   float* k1 = sc.get<float>(chunk);
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
@@ -837,7 +845,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
       coarse_probes(ix, Qrb, fn, ix.C_rot, ix.C_rot_n2, ix.C_rot_n2_max, ix.K, ix.Dp, sp.m, sp.P, cs,
                     probes + b * sp.P, g + b * sp.P, s);
     }
-    launch_query_prep(Qr, cn, ix.Dp, qt, sp.qbits, planes, delta, k1, s);
+    launch_query_prep(Qr, cn, ix.Dp, qt, pb, planes, delta, k1, s);
     {
       Range r("rbq scan");
       search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, qorder, s);
@@ -1808,7 +1816,7 @@ int rbq_query_prep(rbq_index_t* index, const float* Qr_dev, int64_t nq, uint32_t
               "null argument");
     Index& ix = index->ix;
     DeviceGuard dg(ix.device);
-    const int qb = query_bits_of(query_bits);
+    const int qb = prep_bits_of(query_bits_of(query_bits));
     launch_query_prep(Qr_dev, nq, ix.Dp, query_t(ix, qb), qb, planes_dev, delta_dev, k1_dev, as_stream(stream));
   });
 }
@@ -1944,6 +1952,7 @@ int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float del
     Index& ix = index->ix;
     RBQ_CHECK(list >= 0 && list < ix.K, RBQ_ERR_INVALID, "list out of range");
     DeviceGuard dg(ix.device);
+    RBQ_CHECK(query_bits_of(query_bits) <= 8, RBQ_ERR_INVALID, "list estimates: popcount modes only (4 or 8)");
     launch_list_estimates(ix, planes_dev, query_bits_of(query_bits), delta, k1, g, list, acc_dev, est_dev, low_dev,
                           as_stream(stream));
   });

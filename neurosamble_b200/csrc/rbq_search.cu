@@ -4,6 +4,7 @@
 // Compiled with -fmad=false.  The estimator, the prune test, the exact 1-bit distance and the
 // rerank distance are evaluated in the operation order written here, which is also the order
 // of the CPU oracle (oracle/rbq_oracle.cpp), so estimates and ids agree bit for bit.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -988,15 +989,48 @@ constexpr int scan_min_blocks()
   return (W <= 4 || W == 8) ? RBQ_SCAN_MINB8 : (W < 8 ? 5 : 4);
 }
 
+// Bytes at the start of the scan's shared memory before the key buffers: the query planes and
+// the byte-transposed query (popcount modes), or the query tables (LUT16: fp16, LUT32: fp32
+// entries, 16 per 4-dim chunk).  All multiples of 16.
+template <int W, int QB>
+constexpr int scan_head_bytes()
+{
+  return QB == 16 ? 32 * W * 8 : (QB == 32 ? 32 * W * 16 : 4 * W * (QB + 32));
+}
+
+// <bits, q> by the query tables: words in order, nibbles from the top (bit 31) down, added one
+// by one (computeInnerProductsWithLUT16Opt, searcher_gpu_shared_mem_opt.cu:165-177).
+template <int W, int QB>
+__device__ __forceinline__ float lut_ip(const unsigned char* __restrict__ tab, const uint32_t (&c)[W])
+{
+  float ip = 0.0f;
+#pragma unroll
+  for (int w = 0; w < W; ++w)
+#pragma unroll
+    for (int ci = 0; ci < 8; ++ci) {
+      const int e = (w * 8 + ci) * 16 + (int)((c[w] >> (28 - 4 * ci)) & 0xFu);
+      float v;
+      if constexpr (QB == 16)
+        v = __half2float(reinterpret_cast<const __half*>(tab)[e]);
+      else
+        v = reinterpret_cast<const float*>(tab)[e];
+      ip = __fadd_rn(ip, v);
+    }
+  return ip;
+}
+
 template <int W, int QB>
 __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kernel(const ScanArgs a)
 {
   constexpr int NB = 4 * W;
+  constexpr bool kLut = QB >= 16;    // LUT16 / LUT32: the table estimate is the distance
+  constexpr int PB = kLut ? 4 : QB;  // plane words per code word (unused by the LUT modes)
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // planes first (16-byte aligned); QB*W + 8*NB words = 4W(QB + 32) bytes keep the keys 8-aligned
   uint32_t* pl = reinterpret_cast<uint32_t*>(smem_raw);                        // [QB * W]
-  float* qsT = reinterpret_cast<float*>(pl + QB * W);                           // [8 * NB]
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(qsT + 8 * NB);  // [cap]
+  float* qsT = reinterpret_cast<float*>(pl + PB * W);                           // [8 * NB]
+  unsigned char* tab = smem_raw;                                                // LUT modes
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + scan_head_bytes<W, QB>());  // [cap]
   unsigned long long* keys2 = keys + a.cap;                                    // [cap]
   int* pre = reinterpret_cast<int*>(keys2 + a.cap);                            // [nprobe + 1]
   int* lbase = pre + (a.nprobe + 1);                                            // [nprobe]
@@ -1012,11 +1046,29 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const int64_t q = a.qorder ? (int64_t)a.qorder[qi] : qi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  for (int i = tid; i < 8 * NB; i += kScanThreads) {
-    const int jj = i / NB, j = i - jj * NB;
-    qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
+  if constexpr (kLut) {
+    // query tables (precomputeAllLUTs / precomputeAllLUTs_fp16_simple, searcher_gpu.cu:65-108,
+    // searcher_gpu_shared_mem_opt.cu:520-549): chunk c, pattern p -> fp32 sum from 0, in dimension
+    // order, of q[4c + b] over the b with bit 3 - b of p set (LUT16: rounded to fp16)
+    const float* qv = a.Qr + q * (32 * W);
+    for (int i = tid; i < 8 * W * 16; i += kScanThreads) {
+      const int c = i >> 4, pat = i & 15;
+      float sum = 0.0f;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        if (pat & (8 >> b)) sum = __fadd_rn(sum, qv[4 * c + b]);
+      if constexpr (QB == 16)
+        reinterpret_cast<__half*>(tab)[i] = __float2half_rn(sum);
+      else
+        reinterpret_cast<float*>(tab)[i] = sum;
+    }
+  } else {
+    for (int i = tid; i < 8 * NB; i += kScanThreads) {
+      const int jj = i / NB, j = i - jj * NB;
+      qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
+    }
+    for (int j = tid; j < QB * W; j += kScanThreads) pl[j] = a.planes[q * QB * W + j];
   }
-  for (int j = tid; j < QB * W; j += kScanThreads) pl[j] = a.planes[q * QB * W + j];
   if (warp == 0) {
     // The slice's lists: owned probes (owner[l] == shard_rank) with owned-rank in
     // [pb, pe); per list its first slot, g, sqrt(g) and the running start pre[] of the flat
@@ -1097,7 +1149,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   // vectors (the RaBitQ error bound: R of them are that close), instead of admitting its first
   // tile whole.  The bounds stream through the key buffer in tiles, cut to the R smallest
   // whenever the buffer would overflow.
-  if (a.prune && isinf(s_tau) && s_count == 0 && total >= a.R) {
+  if (!kLut && a.prune && isinf(s_tau) && s_count == 0 && total >= a.R) {
     int nb = 0;
     for (int i = 1; i <= nl && nb < a.R; ++i) nb = pre[i];
     int c = 0, cnt = 0;
@@ -1156,20 +1208,33 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
           sqc = lsq[cur];
         }
         const int slot = sadj + f;
-        const int32_t acc = dot_vector<W, QB>(a.codes, slot, pl);
-        const float fr = __ldg(a.frescale + slot);
-        const float base_d = __fadd_rn(__ldg(a.fadd + slot), gc);
-        const float ip = __fmul_rn((float)acc, delta);
-        const float est = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(ip, k1)));
-        const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
-        if (!a.prune || low < tau) {
-          ++n_admit;
-          surv = true;
-          sslot = slot;
-          sbase = base_d;
-          sfr = fr;
+        if constexpr (kLut) {
+          uint32_t c[W];
+          load_code<W>(a.codes, slot, c);
+          const float ip = lut_ip<W, QB>(tab, c);
+          const float est = __fadd_rn(__fadd_rn(__ldg(a.fadd + slot), gc),
+                                      __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(ip, k1)));
+          if (est <= tau) {
+            ++n_admit;
+            keys[atomicAdd(&s_count, 1)] = make_key(est, __ldg(a.ids + slot));
+          }
+        } else {
+          const int32_t acc = dot_vector<W, QB>(a.codes, slot, pl);
+          const float fr = __ldg(a.frescale + slot);
+          const float base_d = __fadd_rn(__ldg(a.fadd + slot), gc);
+          const float ip = __fmul_rn((float)acc, delta);
+          const float est = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(ip, k1)));
+          const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
+          if (!a.prune || low < tau) {
+            ++n_admit;
+            surv = true;
+            sslot = slot;
+            sbase = base_d;
+            sfr = fr;
+          }
         }
       }
+      if constexpr (kLut) continue;  // no exact pass: the table estimate is the distance
       // phase 2: the warp's admitted vectors of this round, one at a time, all lanes.
       unsigned mask = __ballot_sync(0xffffffffu, surv);
       while (mask) {
@@ -1227,9 +1292,8 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
 template <int W, int QB>
 static void launch_scan_wq(const ScanArgs& a, cudaStream_t s)
 {
-  constexpr int NB = 4 * W;
   const size_t smem = (size_t)a.cap * 8 * 2 + (size_t)(2 * a.nprobe + 1) * 4 + (size_t)2 * a.nprobe * 4 +
-                      (size_t)QB * W * 4 + (size_t)8 * NB * 4;
+                      (size_t)scan_head_bytes<W, QB>();
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "scan: shared memory budget exceeded (cap/nprobe too large)");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -1242,10 +1306,12 @@ static void launch_scan_wq(const ScanArgs& a, cudaStream_t s)
 template <int W>
 static void launch_scan_w(const ScanArgs& a, cudaStream_t s)
 {
-  if (a.qbits == 8)
-    launch_scan_wq<W, 8>(a, s);
-  else
-    launch_scan_wq<W, 4>(a, s);
+  switch (a.qbits) {
+    case 8: launch_scan_wq<W, 8>(a, s); break;
+    case 16: launch_scan_wq<W, 16>(a, s); break;
+    case 32: launch_scan_wq<W, 32>(a, s); break;
+    default: launch_scan_wq<W, 4>(a, s); break;
+  }
 }
 
 void launch_scan(const ScanArgs& args, cudaStream_t s)
@@ -1259,7 +1325,9 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
   RBQ_CHECK(a.cap >= a.R + kScanTile && (a.cap & (a.cap - 1)) == 0, RBQ_ERR_INVALID,
             "scan: cap must be a power of two >= R + tile");
   RBQ_CHECK(a.Dp == 32 * a.W, RBQ_ERR_INVALID, "scan: padded dim mismatch");
-  RBQ_CHECK(a.qbits == 4 || a.qbits == 8, RBQ_ERR_INVALID, "scan: query bits must be 4 (QUANT4) or 8 (QUANT8)");
+  RBQ_CHECK(a.qbits == 4 || a.qbits == 8 || a.qbits == 16 || a.qbits == 32, RBQ_ERR_INVALID,
+            "scan: query bits must be 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)");
+  RBQ_CHECK(!(a.tau_out && a.qbits >= 16), RBQ_ERR_INVALID, "scan: the LUT modes have no bound seed");
   RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
             "scan: more than 2^31 vectors on one shard");
   switch (a.W) {

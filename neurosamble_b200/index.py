@@ -46,7 +46,8 @@ class IndexIVFRaBitQ:
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
     scan slices start from the nearest list's bound seed: -1 = auto, on when the probes are split;
-    0 off; 1 on), ``query_bits`` (4: QUANT4, the reference CLI's default; 8: QUANT8),
+    0 off; 1 on), ``query_bits`` (the search mode: 4 QUANT4, the reference CLI's default;
+    8 QUANT8; 16 LUT16 and 32 LUT32, the estimate from fp16 / fp32 tables of the float query),
     ``use_graph`` (replay each batch size's search from a captured CUDA graph; small batches).
     """
 

@@ -176,15 +176,16 @@ class LibStages:
                       _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), R, cap, _ptr(tau), planes.shape[1],
                       self.st)
 
-    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
-        """probes / g: [nq, p] views with unit column stride and one row stride."""
+    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats, mode=0):
+        """probes / g: [nq, p] views with unit column stride and one row stride; mode 16 / 32
+        scans by LUT16 / LUT32 tables (default: the planes' code width)."""
         assert probes.stride(1) == 1 and g.stride() == probes.stride()
         with torch.cuda.device(self.device):
             _lib.call("rbq_scan", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0], _ptr(probes),
                       _ptr(g), probes.shape[1], probes.stride(0), _ptr(tau0) if tau0 is not None else None,
                       _ptr(init[0]) if init is not None else None, _ptr(init[1]) if init is not None else None, R,
                       prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None,
-                      planes.shape[1], self.st)
+                      mode or planes.shape[1], self.st)
 
     def merge(self, d, ids, out_d, out_i):
         with torch.cuda.device(self.device):
@@ -263,7 +264,8 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     clk.mark("all_gather (rotated rows, probes)")
     qr = qr_all[:nq]
     probes, g = recv[:nq, :P], recv[:nq, P:].view(torch.float32)  # row stride 2P
-    planes = torch.empty((nq, query_bits, dp // 32), dtype=torch.int32, device=dev)
+    lut = query_bits in (16, 32)  # LUT16 / LUT32: tables of the float query, no seed
+    planes = torch.empty((nq, 8 if query_bits == 8 else 4, dp // 32), dtype=torch.int32, device=dev)
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)
@@ -271,7 +273,7 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     # 2. seed: the bound seed of the nearest probe, on the rank that owns it (+inf elsewhere);
     #    min over ranks.
     tau = None
-    if prune:
+    if prune and not lut:
         tau = torch.empty(nq, dtype=torch.float32, device=dev)
         stages.bound_seed(qr, planes, delta, k1, probes[:, :1], g[:, :1], R, cap, tau)
         clk.mark("bound seed")
@@ -280,7 +282,8 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     # 3. this shard's probed lists from the shared threshold; rerank its candidates.
     mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
     md = torch.empty((nq, R), dtype=torch.float32, device=dev)
-    stages.scan(qr, planes, delta, k1, probes, g, tau, None, R, int(prune), slices, cap, mi, md, stats)
+    stages.scan(qr, planes, delta, k1, probes, g, tau, None, R, int(prune), slices, cap, mi, md, stats,
+                mode=query_bits if lut else 0)
     clk.mark("scan")
     if k_rerank > 0:
         d = torch.empty((nq, k), dtype=torch.float32, device=dev)

@@ -16,9 +16,10 @@ point of include/rbq.h:
   rerank(h, q, cand_ids, k)                  -> (dist [n, k] f32, ids [n, k] i64)
   merge_results(dist [p, n, k], ids [p, n, k]) -> (dist [n, k], ids [n, k])
 
-``h`` is the index handle as an int (``IndexIVFRaBitQ.handle.value``).  ``bits`` / ``query_bits``
-is the query code width, 4 (QUANT4) or 8 (QUANT8); scan and bound_seed take it from the
-planes' shape.  Inputs are CUDA tensors
+``h`` is the index handle as an int (``IndexIVFRaBitQ.handle.value``).  ``query_bits`` of search
+is the search mode: 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32); ``bits`` of query_prep is
+the query code width, 4 or 8, and scan and bound_seed take it from the planes' shape (the stage
+operators cover the two popcount modes).  Inputs are CUDA tensors
 on the index's device (made contiguous here); outputs are allocated by PyTorch on that device,
 and the work is enqueued on ``torch.cuda.current_stream()`` of it, without synchronising.
 Distances are squared L2, ascending; missing results have id -1 and distance +inf.  A failed

@@ -826,6 +826,49 @@ def test_query_bits_are_checked(case):
         idx.query_bits = 4
 
 
+@pytest.mark.parametrize("mode", [16, 32])
+@pytest.mark.parametrize("slices,R", [(1, 40), (3, 100)])
+def test_lut_scan_candidates_bit_exact(oracle, case, mode, slices, R):
+    """LUT16 / LUT32 (computeInnerProductsWithLUT16Opt): the scan's candidates are the top R by
+    the table estimate, bit for bit the oracle's tables (fp16 rounding included) and sums."""
+    torch = _torch()
+    idx, oix, X, Q, C, lab = case
+    Qr = oracle.rotate(Q, oix.P)
+    nq, nprobe = Qr.shape[0], 8
+    qr, planes, delta, k1 = _query_stage(idx, Qr, 4)
+    probes = torch.empty((nq, nprobe), dtype=torch.int32, device="cuda")
+    g = torch.empty((nq, nprobe), dtype=torch.float32, device="cuda")
+    call("rbq_coarse", idx.handle, ptr(qr), nq, nprobe, 0, ptr(probes), ptr(g), stream())
+    ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+    dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    call("rbq_scan", idx.handle, ptr(qr), ptr(planes), ptr(delta), ptr(k1), nq, ptr(probes), ptr(g), nprobe, 0, None,
+         None, None, R, 1, slices, 0, ptr(ids), ptr(dist), ptr(stats), mode, stream())
+    p2, g2 = oracle.coarse(Qr, oix.c_rot, nprobe)
+    pl2, d2, k2, _ = oracle.query_prep(Qr, oix.t4, 4)
+    oi, od, ost = oracle.scan(oix, Qr, pl2, d2, k2, p2, g2, R, slices=slices, with_stats=True, mode=mode)
+    assert np.array_equal(ids.cpu().numpy(), oi)
+    assert np.array_equal(u32(dist.cpu().numpy()), u32(od))
+    assert stats.cpu().tolist() == ost.tolist()
+
+
+@pytest.mark.parametrize("mode", [16, 32])
+@pytest.mark.parametrize("R", [0, 40])
+def test_lut_search_end_to_end(oracle, case, mode, R):
+    """The LUT16 / LUT32 search (estimates returned as they are with R = 0, as the reference
+    does, or reranked exactly) equals the oracle's, for one and several probe slices."""
+    idx, oix, X, Q, C, lab = case
+    idx.nprobe, idx.k_rerank, idx.prune, idx.seeded, idx.query_bits = 8, R, True, -1, mode
+    try:
+        for qs in (Q, Q[:5]):
+            d, i = idx.search(qs, 10)
+            sl = max(1, min(512 // len(qs), 8)) if len(qs) < 512 else 1
+            d2, i2 = oracle.search(oix, qs, 10, 8, R, slices=sl, query_bits=mode)
+            assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    finally:
+        idx.query_bits = 4
+
+
 def test_graph_search_replays_bit_exact(case):
     """use_graph: the first search of a batch size is captured as a CUDA graph, later ones
     replay it (new inputs copied in, results copied out); a replay launches no kernel of its

@@ -75,7 +75,7 @@ def test_neighbor_files_round_trip(tmp_path):
     ([], "need --emb"),
     (["--emb", "x.f16"], "need --emb"),
     (["--emb", "x.f16", "--n", "10", "--bits", "2"], "only 1-bit"),
-    (["--emb", "x.f16", "--n", "10", "--search_mode", "LUT16"], "only QUANT4"),
+    (["--emb", "x.f16", "--n", "10", "--search_mode", "LUT64"], "one of QUANT4, QUANT8, LUT16, LUT32"),
     (["--emb", "x.f16", "--n", "10", "--topk", "0"], "--topk"),
 ])
 def test_cli_rejects_unsupported_flags(argv, msg, capsys):
@@ -140,7 +140,8 @@ def test_cli_gpus_relaunches_through_torchrun():
     assert cli.check_args(cli.parse_args(["--emb", "x", "--n", "1", "--gpus", "0"])) == "--gpus must be >= 1"
 
 
-def test_cli_accepts_quant8():
+def test_cli_accepts_every_search_mode():
     from neurosamble_b200 import cli
-    assert cli.check_args(cli.parse_args(["--emb", "x.f16", "--n", "10", "--search_mode", "QUANT8"])) == ""
-    assert "QUANT8" in cli.check_args(cli.parse_args(["--emb", "x.f16", "--n", "10", "--search_mode", "LUT32"]))
+    for mode in ("QUANT4", "QUANT8", "LUT16", "LUT32"):
+        assert cli.check_args(cli.parse_args(["--emb", "x.f16", "--n", "10", "--search_mode", mode])) == ""
+    assert cli.SEARCH_MODES == {"QUANT4": 4, "QUANT8": 8, "LUT16": 16, "LUT32": 32}

@@ -164,14 +164,14 @@ class _OracleStages:
                               g.numpy(), R, shard_rank=self.rank, shard_count=self.world, owner=self.owner)
         tau.copy_(torch.from_numpy(t))
 
-    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats):
+    def scan(self, qr, planes, delta, k1, probes, g, tau0, init, R, prune, slices, cap, ids, d, stats, mode=0):
         import torch
         oi, od = self.O.scan(self.ix, qr.numpy(), planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(),
                              probes.numpy(), g.numpy(), R, cap=cap, prune=prune, slices=slices,
                              shard_rank=self.rank, shard_count=self.world,
                              tau0=tau0.numpy() if tau0 is not None else None,
                              init=(init[0].numpy(), init[1].numpy()) if init is not None else None,
-                             owner=self.owner)
+                             owner=self.owner, mode=mode or None)
         ids.copy_(torch.from_numpy(oi))
         d.copy_(torch.from_numpy(od))
 
@@ -228,7 +228,8 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits):
 
 
 @pytest.mark.parametrize("world,nq,prune,policy,bits", [(2, 40, 1, "balanced", 4), (3, 7, 1, "round_robin", 4),
-                                                        (2, 40, 0, "balanced", 4), (2, 40, 1, "balanced", 8)])
+                                                        (2, 40, 0, "balanced", 4), (2, 40, 1, "balanced", 8),
+                                                        (2, 40, 1, "balanced", 16), (3, 9, 1, "round_robin", 32)])
 def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits):
     """The orchestration (queries split for the rotation and coarse quantiser and padded, rotated
     rows and probe rows all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
