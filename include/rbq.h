@@ -49,7 +49,19 @@ typedef struct {
   int32_t shard_policy;                 /* list -> rank map: RBQ_SHARD_ROUND_ROBIN (l % count) */
                                         /* or RBQ_SHARD_BALANCED (fixed at the first add)     */
   int32_t kmeans_kind;                  /* RBQ_KMEANS_BALANCED (reference) or RBQ_KMEANS_LLOYD */
+  int32_t raw_store;                    /* where the raw fp32 rows of the exact rerank live:  */
+                                        /* RBQ_RAW_DEVICE (HBM, default) or RBQ_RAW_HOST      */
+                                        /* (pinned host memory the GPU reads over PCIe: an   */
+                                        /* index whose N*D*4 raw bytes exceed the GPU's      */
+                                        /* memory keeps only codes, factors and ids in HBM;  */
+                                        /* the rerank then reads R rows per query over the   */
+                                        /* bus).  Loaded and imported indexes use the device. */
 } rbq_index_params_t;
+
+/* Raw-row stores (rbq_index_params_t.raw_store).  The reference builds from a host dataset in
+ * batches (construct_on_gpu_streaming, gpu_index/ivf_gpu.cu:814-1066) and keeps no raw rows. */
+#define RBQ_RAW_DEVICE 0
+#define RBQ_RAW_HOST 1
 
 /* Coarse quantiser trainers.  BALANCED: hierarchical balanced k-means, the algorithm of
  * cuvs::cluster::kmeans::fit(balanced_params) that build calls (ivf_rabitq.cu:141-147,

@@ -20,7 +20,7 @@ class IndexParams(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_int32), ("n_lists", ctypes.c_int32), ("seed", ctypes.c_uint64),
                 ("kmeans_n_iters", ctypes.c_int32), ("max_train_points_per_cluster", ctypes.c_int32),
                 ("device", ctypes.c_int32), ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32),
-                ("shard_policy", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32)]
+                ("shard_policy", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32), ("raw_store", ctypes.c_int32)]
 
 
 class SearchParams(ctypes.Structure):
@@ -39,6 +39,7 @@ class IndexInfo(ctypes.Structure):
 
 SHARD_POLICIES = {"round_robin": 0, "balanced": 1}
 KMEANS_KINDS = {"balanced": 0, "lloyd": 1}
+RAW_STORES = {"device": 0, "host": 1}
 
 
 # name -> argtypes (all functions return int status unless listed in _RESTYPES)

@@ -66,6 +66,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--metric", default="l2", choices=["l2", "ip"])
     ap.add_argument("--seed", type=int, default=7, help="rotation / query-scale seed")
     ap.add_argument("--gpus", type=int, default=1, help="GPUs of this node to shard the lists over")
+    ap.add_argument("--raw_store", default="device", choices=["device", "host"],
+                    help="where the rerank's raw fp32 rows live: HBM, or pinned host memory read over PCIe "
+                         "(raw sets larger than the GPU's memory)")
     return ap.parse_args(argv)
 
 
@@ -138,7 +141,8 @@ def main(argv=None) -> int:
     if world > 1:
         from .sharded import ShardedIndexIVFRaBitQ
         index = ShardedIndexIVFRaBitQ(D, a.nlist, seed=a.seed, device=local, kmeans_iters=a.kmeans_iters,
-                                      max_train_points_per_cluster=a.train_per_cluster, metric=a.metric)
+                                      max_train_points_per_cluster=a.train_per_cluster, metric=a.metric,
+                                      raw_store=a.raw_store)
         built = False
     elif a.index and os.path.exists(a.index):
         index = read_index(a.index, device=local, metric=a.metric)
@@ -146,7 +150,8 @@ def main(argv=None) -> int:
         built = True
     else:
         index = IndexIVFRaBitQ(D, a.nlist, seed=a.seed, device=local, kmeans_iters=a.kmeans_iters,
-                               max_train_points_per_cluster=a.train_per_cluster, metric=a.metric)
+                               max_train_points_per_cluster=a.train_per_cluster, metric=a.metric,
+                               raw_store=a.raw_store)
         built = False
     if not built:
         m = min(N, a.train_per_cluster * a.nlist)

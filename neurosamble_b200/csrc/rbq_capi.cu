@@ -332,12 +332,47 @@ void relayout(Index& ix, cudaStream_t s)
   RBQ_CUDA(cudaStreamSynchronize(s));
 }
 
+// The raw-row store: HBM, or pinned host memory mapped into the device's address space (the
+// GPU reads and writes it through the same pointer).
+float* raw_alloc(const Index& ix, size_t count)
+{
+  if (!ix.raw_on_host) return dev_alloc<float>(count);
+  if (count == 0) count = 1;
+  maybe_inject_alloc_failure(count * sizeof(float));
+  void* p = nullptr;
+  const cudaError_t e = cudaHostAlloc(&p, count * sizeof(float), cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw Error{RBQ_ERR_OOM, std::string("cudaHostAlloc of ") + std::to_string(count * sizeof(float)) +
+                                 " bytes failed: " + cudaGetErrorString(e)};
+  }
+  void* dp = nullptr;
+  RBQ_CUDA(cudaHostGetDevicePointer(&dp, p, 0));
+  RBQ_CHECK(dp == p, RBQ_ERR_CUDA, "mapped host memory has a different device address (no unified addressing)");
+  return static_cast<float*>(p);
+}
+
+void raw_free(const Index& ix, float*& p)
+{
+  if (!p) return;
+  if (ix.raw_on_host)
+    cudaFreeHost(p);
+  else
+    cudaFree(p);
+  p = nullptr;
+}
+
 void ensure_row_capacity(Index& ix, int64_t need)
 {
   if (need <= ix.cap_rows) return;
   int64_t cap = std::max<int64_t>(need, ix.cap_rows + ix.cap_rows / 2);
   const size_t keep = (size_t)ix.n_rows;
-  dev_grow(ix.X_r, keep * ix.D, (size_t)cap * ix.D);
+  {
+    float* np = raw_alloc(ix, (size_t)cap * ix.D);
+    if (ix.X_r && keep) RBQ_CUDA(cudaMemcpy(np, ix.X_r, keep * ix.D * 4, cudaMemcpyDefault));
+    raw_free(ix, ix.X_r);
+    ix.X_r = np;
+  }
   dev_grow(ix.codes_r, keep * ix.W, (size_t)cap * ix.W);
   dev_grow(ix.fadd_r, keep, cap);
   dev_grow(ix.frescale_r, keep, cap);
@@ -400,16 +435,24 @@ void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, 
     const int64_t r0 = ix.n_rows;
     int64_t* src = sc.get<int64_t>(m);
     RBQ_CUDA(cudaMemcpyAsync(src, own.data(), m * 8, cudaMemcpyHostToDevice, s));
-    launch_gather_rows_f32(X, m, ix.D, src, ix.X_r + (size_t)r0 * ix.D, s);
+    if (!ix.raw_on_host) launch_gather_rows_f32(X, m, ix.D, src, ix.X_r + (size_t)r0 * ix.D, s);
     RBQ_CUDA(cudaMemcpyAsync(ix.labels_r + r0, own_lab.data(), m * 4, cudaMemcpyHostToDevice, s));
     RBQ_CUDA(cudaMemcpyAsync(ix.ids_r + r0, own_ids.data(), m * 4, cudaMemcpyHostToDevice, s));
-    // Rotate + quantise in chunks to bound the rotated-row scratch.
+    // Rotate + quantise in chunks to bound the rotated-row scratch.  A host store receives each
+    // chunk's raw rows from a device copy the chunk is quantised from (one trip over the bus).
     const int64_t chunk = std::max<int64_t>(1, (512ll << 20) / ((int64_t)ix.Dp * 4));
     float* Y = sc.get<float>((size_t)std::min(chunk, m) * ix.Dp);
+    float* Xs = ix.raw_on_host ? sc.get<float>((size_t)std::min(chunk, m) * ix.D) : nullptr;
     for (int64_t a = 0; a < m; a += chunk) {
       const int64_t cn = std::min(chunk, m - a);
       const int64_t r = r0 + a;
-      launch_rotate(ix.X_r + (size_t)r * ix.D, cn, ix.D, ix.Dp, ix.P, Y, s);
+      const float* rows = ix.X_r + (size_t)r * ix.D;
+      if (ix.raw_on_host) {
+        launch_gather_rows_f32(X, cn, ix.D, src + a, Xs, s);
+        RBQ_CUDA(cudaMemcpyAsync(ix.X_r + (size_t)r * ix.D, Xs, (size_t)cn * ix.D * 4, cudaMemcpyDeviceToHost, s));
+        rows = Xs;
+      }
+      launch_rotate(rows, cn, ix.D, ix.Dp, ix.P, Y, s);
       launch_quantize(Y, cn, ix.Dp, ix.C_rot, ix.labels_r + r, ix.codes_r + (size_t)r * ix.W, ix.fadd_r + r,
                       ix.frescale_r + r, ix.ferr_r + r, s);
     }
@@ -950,7 +993,7 @@ template <typename T>
 void write_dev(File& f, const T* p, size_t count)
 {
   std::vector<T> h(count);
-  if (count) RBQ_CUDA(cudaMemcpy(h.data(), p, count * sizeof(T), cudaMemcpyDeviceToHost));
+  if (count) RBQ_CUDA(cudaMemcpy(h.data(), p, count * sizeof(T), cudaMemcpyDefault));  // device or mapped host
   f.write(h.data(), count * sizeof(T));
 }
 
@@ -1066,7 +1109,7 @@ void free_index_memory(Index& ix)
   dev_free(ix.C_rot_n2);
   dev_free(ix.C_rot_n2_max);
   dev_free(ix.C_n2);
-  dev_free(ix.X_r);
+  raw_free(ix, ix.X_r);
   dev_free(ix.codes_r);
   dev_free(ix.fadd_r);
   dev_free(ix.frescale_r);
@@ -1121,6 +1164,7 @@ void rbq_index_params_default(rbq_index_params_t* p)
   p->shard_count = 1;
   p->shard_policy = RBQ_SHARD_ROUND_ROBIN;
   p->kmeans_kind = RBQ_KMEANS_BALANCED;
+  p->raw_store = RBQ_RAW_DEVICE;
 }
 
 void rbq_search_params_default(rbq_search_params_t* p)
@@ -1169,6 +1213,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
               RBQ_ERR_INVALID, "unknown shard policy");
     RBQ_CHECK(params->kmeans_kind == RBQ_KMEANS_BALANCED || params->kmeans_kind == RBQ_KMEANS_LLOYD,
               RBQ_ERR_INVALID, "unknown k-means kind");
+    RBQ_CHECK(params->raw_store == RBQ_RAW_DEVICE || params->raw_store == RBQ_RAW_HOST, RBQ_ERR_INVALID,
+              "unknown raw store (RBQ_RAW_DEVICE or RBQ_RAW_HOST)");
     int ndev = 0;
     RBQ_CUDA(cudaGetDeviceCount(&ndev));
     RBQ_CHECK(params->device >= 0 && params->device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
@@ -1184,6 +1230,7 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
     ix.seed = params->seed;
     ix.kmeans_iters = params->kmeans_n_iters;
     ix.kmeans_kind = params->kmeans_kind;
+    ix.raw_on_host = params->raw_store == RBQ_RAW_HOST;
     ix.max_train_per_list = params->max_train_points_per_cluster;
     ix.shard_rank = params->shard_rank;
     ix.shard_count = params->shard_count;

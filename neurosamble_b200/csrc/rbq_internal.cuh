@@ -94,6 +94,7 @@ struct Index {
   int shard_rank = 0, shard_count = 1;
   int shard_policy = RBQ_SHARD_ROUND_ROBIN;
   bool has_raw = true;              // X_r holds the raw rows (false for an index imported without them)
+  bool raw_on_host = false;         // X_r is pinned, mapped host memory (RBQ_RAW_HOST), else HBM
   float t8 = 0.0f / 0.0f;           // 8-bit query constant of an imported reference file (NaN: derive)
   bool owners_fixed = false;
   std::vector<int32_t> owner_host;  // [K] rank holding list l

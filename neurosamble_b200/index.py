@@ -41,7 +41,9 @@ class IndexIVFRaBitQ:
     ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``,
     ``kmeans`` ("balanced": the reference's hierarchical balanced k-means; "lloyd": plain Lloyd);
     a shard of a sharded index also takes ``shard_rank`` / ``shard_count`` and ``shard_policy``
-    ("round_robin": list l on rank l % count; "balanced": lists spread by size^2 at the first add).
+    ("round_robin": list l on rank l % count; "balanced": lists spread by size^2 at the first add);
+    ``raw_store`` ("device": the exact rerank's raw fp32 rows in HBM; "host": in pinned host
+    memory read over PCIe, for a raw set larger than the GPU's memory).
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
@@ -53,7 +55,8 @@ class IndexIVFRaBitQ:
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
                  max_train_points_per_cluster: int = 256, shard_rank: int = 0, shard_count: int = 1,
-                 metric: str = "l2", shard_policy: str = "round_robin", kmeans: str = "balanced", _handle=None):
+                 metric: str = "l2", shard_policy: str = "round_robin", kmeans: str = "balanced",
+                 raw_store: str = "device", _handle=None):
         if metric not in ("l2", "ip"):
             raise ValueError("metric must be 'l2' or 'ip'")
         self.d = int(d)
@@ -84,6 +87,9 @@ class IndexIVFRaBitQ:
         if kmeans not in _lib.KMEANS_KINDS:
             raise ValueError(f"kmeans must be one of {sorted(_lib.KMEANS_KINDS)}")
         p.kmeans_kind = _lib.KMEANS_KINDS[kmeans]
+        if raw_store not in _lib.RAW_STORES:
+            raise ValueError(f"raw_store must be one of {sorted(_lib.RAW_STORES)}")
+        p.raw_store = _lib.RAW_STORES[raw_store]
         _lib.call("rbq_index_create", ctypes.byref(p), ctypes.byref(self._h))
 
     # -- lifecycle -----------------------------------------------------------------------

@@ -869,6 +869,33 @@ def test_lut_search_end_to_end(oracle, case, mode, R):
         idx.query_bits = 4
 
 
+def test_host_raw_store_gives_the_device_store_results(oracle, tmp_path):
+    """raw_store="host": the raw rows live in pinned host memory (the rerank reads them over
+    PCIe) so only codes, factors and ids need HBM.  Built in several adds, the index searches,
+    saves and reloads bit-equal to the same index with its rows in HBM."""
+    from neurosamble_b200 import IndexIVFRaBitQ, read_index, write_index
+    X, Q = mixture(12000, 96, 30, 0.3, 150, seed=41)
+    res = []
+    for store in ("device", "host"):
+        idx = IndexIVFRaBitQ(96, 48, seed=7, kmeans_iters=4, raw_store=store)
+        idx.train(X)
+        for a in range(0, len(X), 5000):
+            idx.add(X[a:a + 5000])
+        idx.nprobe, idx.k_rerank = 12, 60
+        res.append(idx.search(Q, 10))
+        if store == "host":
+            write_index(idx, str(tmp_path / "h.rbq"))
+            back = read_index(str(tmp_path / "h.rbq"))
+            back.nprobe, back.k_rerank = 12, 60
+            res.append(back.search(Q, 10))
+    for d, i in res[1:]:
+        assert np.array_equal(i, res[0][1]) and np.array_equal(u32(d), u32(res[0][0]))
+    C, _ = idx.centroids()
+    oix = oracle.build(X, C, oracle.assign(X, C), idx.rotation(), idx.query_scale)
+    d2, i2 = oracle.search(oix, Q, 10, 12, 60)
+    assert np.array_equal(res[0][1], i2) and np.array_equal(u32(res[0][0]), u32(d2))
+
+
 def test_graph_search_replays_bit_exact(case):
     """use_graph: the first search of a batch size is captured as a CUDA graph, later ones
     replay it (new inputs copied in, results copied out); a replay launches no kernel of its
