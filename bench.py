@@ -317,6 +317,9 @@ def _count(n):
     return f"{n // 1_000_000}M" if n % 1_000_000 == 0 else str(n)
 
 
+SEARCH_MODES = {4: "QUANT4", 8: "QUANT8", 16: "LUT16", 32: "LUT32"}
+
+
 def metric_name(cfg):
     return (f"queries/sec @ recall@{cfg['k']}>=0.95, {_count(cfg['n'])} x {cfg['d']} IVF-RaBitQ "
             f"(nlist {cfg['nlist']}, nprobe {cfg['nprobe']}, k {cfg['k']})")
@@ -333,7 +336,7 @@ def workload(cfg, R, kmeans):
                              "device"),
                 "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
                 "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
-                "kmeans": kmeans, "search_mode": "QUANT8" if cfg.get("query_bits", 4) == 8 else "QUANT4"}
+                "kmeans": kmeans, "search_mode": SEARCH_MODES[cfg.get("query_bits", 4)]}
     return {"workload": (f"BASELINE config {cfg['config']}: {_count(cfg['n'])} x {cfg['d']} f32, "
                          f"{cfg['centres']}-centre {'anisotropic ' if cfg['aniso'] else ''}mixture sigma "
                          f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ 1-bit "
@@ -341,7 +344,7 @@ def workload(cfg, R, kmeans):
                          + ("; data generated on the device" if cfg["device_data"] else "")),
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
             "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
-            "kmeans": kmeans, "search_mode": "QUANT8" if cfg.get("query_bits", 4) == 8 else "QUANT4"}
+            "kmeans": kmeans, "search_mode": SEARCH_MODES[cfg.get("query_bits", 4)]}
 
 
 # --------------------------------------------------------------------------------------
@@ -548,7 +551,7 @@ def run_ours(args, cfg):
                      "max_over_ranks": {n: round(float(v), 4) for n, v in zip(names, vmax.tolist())}}
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
-    seeded = world > 1 or args.seeded == 1
+    seeded = (world > 1 or args.seeded == 1) and cfg["query_bits"] < 16  # LUT modes: one pass, no seed
     roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
     scan_share = round(roof["launch_ms"] / ms, 3)
 
@@ -626,7 +629,8 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     h, st = ix.handle, _stream_ptr(dev.index)
     qr = torch.empty((nq, dp), dtype=torch.float32, device=dev)
     qb = cfg["query_bits"]
-    planes = torch.empty((nq, qb, dp // 32), dtype=torch.int32, device=dev)
+    lut = qb in (16, 32)  # LUT16 / LUT32 scan from 4-bit planes' k1 and tables of the float query
+    planes = torch.empty((nq, 8 if qb == 8 else 4, dp // 32), dtype=torch.int32, device=dev)
     delta = torch.empty(nq, dtype=torch.float32, device=dev)
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     probes = torch.empty((nq, P), dtype=torch.int32, device=dev)
@@ -639,7 +643,7 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     pr = probes.cpu().numpy()
     owned = ix.list_owners()[pr] == info.shard_rank
     vec = int(sizes[pr][owned].sum())
-    scan_bytes = vec * (d // 8 + 12)
+    scan_bytes = vec * (d // 8 + (8 if lut else 12))  # the table estimate reads no error factor
     stream = torch.cuda.current_stream(dev)
     stats = torch.zeros(2, dtype=torch.int64, device=dev)
 
@@ -774,8 +778,12 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the B = 1 / 64 / 1024 sweep")
     ap.add_argument("--kmeans", default="balanced", choices=["balanced", "lloyd"],
                     help="coarse trainer of both arms (balanced: the reference's build algorithm)")
-    ap.add_argument("--query-bits", type=int, default=4, choices=[4, 8],
-                    help="query code width of both arms: 4 (QUANT4, the reference CLI's default) or 8 (QUANT8)")
+    ap.add_argument("--query-bits", type=int, default=4, choices=sorted(SEARCH_MODES),
+                    help="search mode of both arms: 4 (QUANT4, the reference CLI's default), 8 (QUANT8), "
+                         "16 (LUT16) or 32 (LUT32)")
+    ap.add_argument("--nlist", type=int, default=0,
+                    help="list count override (reduced-size cases of a configuration's shape; mixtures keep "
+                         "one centre per list)")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
                     help="benchmark configuration (2: the metric's; 3: read overlap; 4 / 5: supplementary, data on "
                          "the device)")
@@ -790,6 +798,10 @@ def main():
         cfg["n"] = args.n
     if args.nq:
         cfg["nq"] = args.nq
+    if args.nlist:
+        if cfg.get("centres") == cfg["nlist"]:
+            cfg["centres"] = args.nlist
+        cfg["nlist"] = args.nlist
     if args.impl == "reference":
         if cfg["device_data"] and cfg.get("generator") != "reads":
             if int(os.environ.get("RANK", "0")) == 0:
