@@ -36,7 +36,7 @@ extern "C" {
 typedef struct rbq_index rbq_index_t;
 
 /* Build-time parameters.  Replaces cuvs::neighbors::ivf_rabitq::index_params
- * (ivf_rabitq.hpp:50-103) for the 1-bit (bits_per_dim = 1) configuration. */
+ * (ivf_rabitq.hpp:50-103). */
 typedef struct {
   int32_t dim;                          /* D; padded internally to Dp = ceil(D/32)*32       */
   int32_t n_lists;                      /* K (n_lists)                                        */
@@ -56,6 +56,14 @@ typedef struct {
                                         /* memory keeps only codes, factors and ids in HBM;  */
                                         /* the rerank then reads R rows per query over the   */
                                         /* bus).  Loaded and imported indexes use the device. */
+  int32_t bits_per_dim;                 /* code bits per dimension, 1..9 (index_params.      */
+                                        /* bits_per_dim, ivf_rabitq.cu:388-393).  1: 1-bit   */
+                                        /* RaBitQ codes.  b > 1 adds ExRaBitQ's b - 1 extra  */
+                                        /* bits per dimension (quantizer_gpu.cu:347-468) and  */
+                                        /* two factors per vector: the scan admits by the     */
+                                        /* 1-bit estimate's error bound as before and ranks   */
+                                        /* the admitted vectors by the extra-bit distance     */
+                                        /* (searcher_gpu_quantize_query.cu:405-473).  Default 1. */
 } rbq_index_params_t;
 
 /* Raw-row stores (rbq_index_params_t.raw_store).  The reference builds from a host dataset in
@@ -122,6 +130,8 @@ typedef struct {
   int32_t shard_policy; /* RBQ_SHARD_*                      */
   int32_t owners_fixed; /* 1 once the list -> rank map is final (ROUND_ROBIN: always) */
   int32_t kmeans_kind;  /* RBQ_KMEANS_*                     */
+  int32_t bits_per_dim; /* 1 + extra bits per dimension     */
+  float ex_scale;       /* data scale of the extra-bit codes (0 at 1 bit) */
 } rbq_index_info_t;
 
 /* ---- errors / defaults ------------------------------------------------------------------ */
@@ -192,9 +202,10 @@ int rbq_save(rbq_index_t* index, const char* path);
 int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard_count, rbq_index_t** out);
 
 /* The reference's index file (IVFGPU::save / load_transposed, gpu_index/ivf_gpu.cu:367-461,
- * 100-289, as written by ivf_rabitq::serialize, ivf_rabitq.cu:357-368): import a 1-bit,
- * matmul-rotator file (its rotation, query constant, rotated centroids, codes, factors and ids
- * are used as stored; lists are split over shards by shard_policy), optionally with the raw
+ * 100-289, as written by ivf_rabitq::serialize, ivf_rabitq.cu:357-368): import a
+ * matmul-rotator file with 0..8 extra bits (its rotation, query constants, rotated centroids,
+ * codes, long codes, factors and ids are used as stored; lists are split over shards by
+ * shard_policy), optionally with the raw
  * vectors X_host [n_x = num_vectors, D] (row = id) for the exact rerank — without them the
  * index searches with rerank = 0 only.  Export writes an unsharded index in that format. */
 int rbq_import_reference(const char* path, int32_t device, const float* X_host, int64_t n_x, int32_t shard_rank,
@@ -209,6 +220,10 @@ int rbq_get_centroids(rbq_index_t* index, float* C_host, float* C_rot_host);
  * f_add / f_rescale / f_err [n_local].  Any output may be NULL. */
 int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint32_t* codes, float* fadd,
                      float* frescale, float* ferr);
+/* The extra bits of an index with bits_per_dim > 1, in the same slot order: ex_codes
+ * [n_local, ex, W] (plane p word w, dim 32w+j -> bit 31-j = bit p of the dim's extra-bit code,
+ * ex = bits_per_dim - 1), f_ex_add / f_ex_rescale [n_local].  Any output may be NULL. */
+int rbq_export_ex_lists(rbq_index_t* index, uint32_t* ex_codes, float* fexadd, float* fexr);
 /* owners [K]: the rank holding each list (-1 while a BALANCED map awaits the first add). */
 int rbq_get_list_owners(rbq_index_t* index, int32_t* owners);
 

@@ -20,7 +20,8 @@ class IndexParams(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_int32), ("n_lists", ctypes.c_int32), ("seed", ctypes.c_uint64),
                 ("kmeans_n_iters", ctypes.c_int32), ("max_train_points_per_cluster", ctypes.c_int32),
                 ("device", ctypes.c_int32), ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32),
-                ("shard_policy", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32), ("raw_store", ctypes.c_int32)]
+                ("shard_policy", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32), ("raw_store", ctypes.c_int32),
+                ("bits_per_dim", ctypes.c_int32)]
 
 
 class SearchParams(ctypes.Structure):
@@ -35,7 +36,8 @@ class IndexInfo(ctypes.Structure):
                 ("shard_rank", ctypes.c_int32), ("shard_count", ctypes.c_int32), ("trained", ctypes.c_int32),
                 ("n_total", ctypes.c_int64), ("n_local", ctypes.c_int64), ("query_scale", ctypes.c_float),
                 ("seed", ctypes.c_uint64), ("device_bytes", ctypes.c_int64), ("shard_policy", ctypes.c_int32),
-                ("owners_fixed", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32)]
+                ("owners_fixed", ctypes.c_int32), ("kmeans_kind", ctypes.c_int32), ("bits_per_dim", ctypes.c_int32),
+                ("ex_scale", ctypes.c_float)]
 
 SHARD_POLICIES = {"round_robin": 0, "balanced": 1}
 KMEANS_KINDS = {"balanced": 0, "lloyd": 1}
@@ -71,6 +73,7 @@ SIGNATURES = {
     "rbq_get_rotation": [_P, _P],
     "rbq_get_centroids": [_P, _P, _P],
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
+    "rbq_export_ex_lists": [_P, _P, _P, _P],
     "rbq_get_list_owners": [_P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],
     "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _I32, _P],

@@ -175,6 +175,79 @@ void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, cons
   RBQ_LAUNCHED();
 }
 
+// ---------------------------------------------------------------------------------------
+// ExRaBitQ extra bits (bits_per_dim = ex + 1), one thread per row: the fast-quantize branch of
+// quantize_batch_opt (exrabitq_fused_kernel_batch, quantizer_gpu.cu:347-468) on the normalised
+// residual xn = r / |r| of subtract_normalize_binarize_Kernel (:109-172).  Per dim:
+//   e = min(int(t * |xn| + 1e-5), 2^ex - 1); stored x = e where the 1-bit code is 1, else
+//   2^ex - 1 - e; centred code xu = (bit * 2^ex + x) - (2^ex - 1/2);
+//   ip_norm = sum (e + 1/2) |xn|, ip_resi = sum r xu, ip_cent = sum c xu (double, dim order);
+//   f_ex_add = |r|^2 + (2 |r|^2 ip_cent) / ip_resi (0 -> +inf); f_ex_rescale = -2 |r| / ip_norm.
+// The top bit of the code is the stored 1-bit code (r > 0) in the factors too; the reference
+// uses r >= 0 there, which differs only where a residual coordinate is exactly zero.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) quantize_ex_kernel(const float* __restrict__ Y, int64_t n, int Dp,
+                                                          const float* __restrict__ C_rot,
+                                                          const uint32_t* __restrict__ labels, int ex, float t,
+                                                          uint32_t* __restrict__ planes, float* __restrict__ fexadd,
+                                                          float* __restrict__ fexr)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* y = Y + i * Dp;
+  const float* c = C_rot + (size_t)labels[i] * Dp;
+  double l2d = 0.0;
+  for (int j = 0; j < Dp; ++j) {
+    const float r = __fsub_rn(y[j], c[j]);
+    l2d += (double)r * (double)r;
+  }
+  const float l2_sqr = (float)l2d;
+  const float norm = sqrtf(l2_sqr);
+  const int W = Dp >> 5;
+  const int mask = (1 << ex) - 1;
+  const float shift = __fsub_rn((float)(1 << ex), 0.5f);
+  double ipn = 0.0, ipr = 0.0, ipc = 0.0;
+  uint32_t* out = planes + (size_t)i * ex * W;
+  for (int w = 0; w < W; ++w) {
+    uint32_t pw[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    for (int b = 0; b < 32; ++b) {
+      const int j = (w << 5) + b;
+      const float r = __fsub_rn(y[j], c[j]);
+      const int bit = (norm > 0.0f && r > 0.0f) ? 1 : 0;
+      const float xn = norm > 0.0f ? __fdiv_rn(r, norm) : 0.0f;
+      const float a = fabsf(xn);
+      int e = (int)__fadd_rn(__fmul_rn(t, a), 1e-5f);
+      if (e > mask) e = mask;
+      ipn += (double)__fmul_rn(__fadd_rn((float)e, 0.5f), a);
+      const int x = bit ? e : mask - e;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) pw[p] |= (uint32_t)((x >> p) & 1) << (31 - b);
+      const float xu = __fsub_rn((float)((bit << ex) | x), shift);
+      ipr += (double)r * (double)xu;
+      ipc += (double)c[j] * (double)xu;
+    }
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+      if (p < ex) out[p * W + w] = pw[p];
+  }
+  const float ip_resi = (float)ipr, ip_cent = (float)ipc, ip_norm = (float)ipn;
+  const float denom = ip_resi == 0.0f ? __int_as_float(0x7f800000) : ip_resi;
+  const float l2_norm = sqrtf(fmaxf(l2_sqr, 0.0f));
+  fexadd[i] = __fadd_rn(l2_sqr, __fdiv_rn(__fmul_rn(__fmul_rn(2.0f, l2_sqr), ip_cent), denom));
+  float inv = __fdiv_rn(1.0f, ip_norm);
+  if (!isfinite(inv)) inv = 1.0f;
+  fexr[i] = __fmul_rn(__fmul_rn(-2.0f, l2_norm), inv);
+}
+
+void launch_quantize_ex(const float* Y, int64_t n, int Dp, const float* C_rot, const uint32_t* labels, int ex,
+                        float t, uint32_t* planes, float* fexadd, float* fexr, cudaStream_t s)
+{
+  if (n <= 0 || ex <= 0) return;
+  quantize_ex_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, s>>>(Y, n, Dp, C_rot, labels, ex, t, planes, fexadd,
+                                                                fexr);
+  RBQ_LAUNCHED();
+}
+
 // Row squared norms (float accumulation; only used to rank candidates approximately).
 __global__ void row_norms_kernel(const float* __restrict__ A, int64_t n, int d, float* __restrict__ out)
 {

@@ -308,6 +308,9 @@ void relayout(Index& ix, cudaStream_t s)
   dev_free(ix.fadd);
   dev_free(ix.frescale);
   dev_free(ix.ferr);
+  dev_free(ix.ex_codes);
+  dev_free(ix.fexadd);
+  dev_free(ix.fexr);
   const size_t n = (size_t)ix.n_rows;
   ix.list_off = dev_alloc<int64_t>(ix.K + 1);
   ix.ids = dev_alloc<uint32_t>(n);
@@ -315,6 +318,11 @@ void relayout(Index& ix, cudaStream_t s)
   ix.fadd = dev_alloc<float>(n);
   ix.frescale = dev_alloc<float>(n);
   ix.ferr = dev_alloc<float>(n);
+  if (ix.ex_bits > 0) {
+    ix.ex_codes = dev_alloc<uint32_t>(n * ix.ex_bits * ix.W);
+    ix.fexadd = dev_alloc<float>(n);
+    ix.fexr = dev_alloc<float>(n);
+  }
   RBQ_CUDA(cudaMemcpyAsync(ix.list_off, off.data(), (ix.K + 1) * 8, cudaMemcpyHostToDevice, s));
   if (n) {
     Scratch sc(s);
@@ -328,6 +336,13 @@ void relayout(Index& ix, cudaStream_t s)
                            reinterpret_cast<uint32_t*>(ix.frescale), s);
     launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.ferr_r), ix.n_rows, 1, ord,
                            reinterpret_cast<uint32_t*>(ix.ferr), s);
+    if (ix.ex_bits > 0) {
+      launch_gather_rows_u32(ix.ex_codes_r, ix.n_rows, ix.ex_bits * ix.W, ord, ix.ex_codes, s);
+      launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.fexadd_r), ix.n_rows, 1, ord,
+                             reinterpret_cast<uint32_t*>(ix.fexadd), s);
+      launch_gather_rows_u32(reinterpret_cast<const uint32_t*>(ix.fexr_r), ix.n_rows, 1, ord,
+                             reinterpret_cast<uint32_t*>(ix.fexr), s);
+    }
   }
   RBQ_CUDA(cudaStreamSynchronize(s));
 }
@@ -377,6 +392,11 @@ void ensure_row_capacity(Index& ix, int64_t need)
   dev_grow(ix.fadd_r, keep, cap);
   dev_grow(ix.frescale_r, keep, cap);
   dev_grow(ix.ferr_r, keep, cap);
+  if (ix.ex_bits > 0) {
+    dev_grow(ix.ex_codes_r, keep * ix.ex_bits * ix.W, (size_t)cap * ix.ex_bits * ix.W);
+    dev_grow(ix.fexadd_r, keep, cap);
+    dev_grow(ix.fexr_r, keep, cap);
+  }
   dev_grow(ix.labels_r, keep, cap);
   dev_grow(ix.ids_r, keep, cap);
   ix.cap_rows = cap;
@@ -455,6 +475,8 @@ void add_rows(Index& ix, const float* X, int64_t n, const uint32_t* labels_dev, 
       launch_rotate(rows, cn, ix.D, ix.Dp, ix.P, Y, s);
       launch_quantize(Y, cn, ix.Dp, ix.C_rot, ix.labels_r + r, ix.codes_r + (size_t)r * ix.W, ix.fadd_r + r,
                       ix.frescale_r + r, ix.ferr_r + r, s);
+      launch_quantize_ex(Y, cn, ix.Dp, ix.C_rot, ix.labels_r + r, ix.ex_bits, ix.tex,
+                         ix.ex_codes_r + (size_t)r * ix.ex_bits * ix.W, ix.fexadd_r + r, ix.fexr_r + r, s);
     }
     // id2row for this call's id range [n_total, n_total + n): ids are contiguous per call.
     std::vector<uint32_t> id2row_new(n, 0xFFFFFFFFu);
@@ -753,6 +775,18 @@ float query_t(Index& ix, int qbits)
   return ix.t8;
 }
 
+// Data scale of the extra-bit codes (construct_on_gpu, ivf_gpu.cu:629-644, fast quantize): the
+// 4-bit query scale for 3 extra bits, the 8-bit one for 7, else the best-rescale mean for the
+// extra-bit count (the reference computes that one from a time-seeded generator,
+// quantizer_gpu.cu:1357-1435; here it comes from the index seed, so builds repeat).
+float ex_scale_of(Index& ix)
+{
+  if (ix.ex_bits <= 0) return 0.0f;
+  if (ix.ex_bits == 3) return ix.t4;
+  if (ix.ex_bits == 7) return query_t(ix, 8);
+  return query_scale(ix.Dp, ix.seed, ix.ex_bits);
+}
+
 SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq)
 {
   RBQ_CHECK(p.k >= 1, RBQ_ERR_INVALID, "search: k must be >= 1");
@@ -793,6 +827,12 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
   sa.fadd = ix.fadd;
   sa.frescale = ix.frescale;
   sa.ferr = ix.ferr;
+  if (ix.ex_bits > 0) {
+    sa.ex_codes = ix.ex_codes;
+    sa.fexadd = ix.fexadd;
+    sa.fexr = ix.fexr;
+    sa.ex_bits = ix.ex_bits;
+  }
   sa.n_slots = ix.n_rows;
   sa.Dp = ix.Dp;
   sa.W = ix.W;
@@ -964,7 +1004,9 @@ Index::SearchGraph& search_graph(Index& ix, const rbq_search_params_t& params, i
 // Persistence: "RBQB200\0", version, dims, seed, t4, P, C, then this shard's rows.
 // ---------------------------------------------------------------------------------------
 const char kMagic[8] = {'R', 'B', 'Q', 'B', '2', '0', '0', '\0'};
-constexpr uint32_t kFormatVersion = 2;  // 2 adds the shard policy and list -> rank map
+// 2 adds the shard policy and list -> rank map; 3 the extra-bit count and scale after the map and
+// the extra-bit planes and factors after the 1-bit factors
+constexpr uint32_t kFormatVersion = 3;
 
 struct File {
   FILE* f = nullptr;
@@ -1001,9 +1043,42 @@ struct RefFile {
   uint64_t n = 0, D = 0, K = 0, ex_bits = 0;
   float t4 = 0.0f, t8 = 0.0f;
   std::vector<uint64_t> sizes;
-  std::vector<float> P, Crot, fac;
+  std::vector<float> P, Crot, fac, exfac;
   std::vector<uint32_t> codes, ids;
+  std::vector<uint8_t> long_codes;  // n x Dp * ex_bits / 8
 };
+
+// The reference's long code of one vector (extra-bit codes of Dp dims, ex bits each, one
+// MSB-first bit stream: exrabitq_fused_kernel_batch's packing, quantizer_gpu.cu:470-505, read
+// back by extract_code, searcher_gpu_common.cuh:72-81) <-> this library's planes [ex, W].
+void long_code_to_planes(const uint8_t* lc, int Dp, int ex, uint32_t* planes)
+{
+  const int W = Dp / 32;
+  std::fill(planes, planes + (size_t)ex * W, 0u);
+  for (int j = 0; j < Dp; ++j) {
+    uint32_t x = 0;
+    for (int b = 0; b < ex; ++b) {
+      const size_t pos = (size_t)j * ex + b;
+      x = (x << 1) | ((lc[pos >> 3] >> (7 - (pos & 7))) & 1u);
+    }
+    for (int p = 0; p < ex; ++p)
+      if ((x >> p) & 1u) planes[(size_t)p * W + (j >> 5)] |= 1u << (31 - (j & 31));
+  }
+}
+
+void planes_to_long_code(const uint32_t* planes, int Dp, int ex, uint8_t* lc)
+{
+  const int W = Dp / 32;
+  std::fill(lc, lc + (size_t)Dp * ex / 8, (uint8_t)0);
+  for (int j = 0; j < Dp; ++j) {
+    uint32_t x = 0;
+    for (int p = 0; p < ex; ++p) x |= ((planes[(size_t)p * W + (j >> 5)] >> (31 - (j & 31))) & 1u) << p;
+    for (int b = 0; b < ex; ++b) {
+      const size_t pos = (size_t)j * ex + b;
+      if ((x >> (ex - 1 - b)) & 1u) lc[pos >> 3] |= (uint8_t)(1u << (7 - (pos & 7)));
+    }
+  }
+}
 
 RefFile read_ref_file(const char* path)
 {
@@ -1015,8 +1090,8 @@ RefFile read_ref_file(const char* path)
   f.read(&r.ex_bits, 8);
   RBQ_CHECK(r.D >= 1 && r.D <= 2048 && r.K >= 1 && r.K <= (1u << 24) && r.n < 0xFFFFFFFFull, RBQ_ERR_FORMAT,
             "not a reference IVF-RaBitQ index (bad header): " + f.path);
-  RBQ_CHECK(r.ex_bits == 0, RBQ_ERR_FORMAT,
-            "reference index with " + std::to_string(r.ex_bits) + " extra bits: only 1-bit codes are supported");
+  RBQ_CHECK(r.ex_bits <= 8, RBQ_ERR_FORMAT,
+            "reference index with " + std::to_string(r.ex_bits) + " extra bits: at most 8 are supported");
   unsigned char flag = 0;
   f.read(&flag, 1);
   f.read(&r.t4, 4);
@@ -1038,8 +1113,10 @@ RefFile read_ref_file(const char* path)
   f.read(r.codes.data(), r.codes.size() * 4);
   r.fac.resize(r.n * 3);
   f.read(r.fac.data(), r.fac.size() * 4);
-  std::vector<float> skip(r.n * 2);  // no long codes at 1 bit; the extra-bit factors are unused
-  f.read(skip.data(), skip.size() * 4);
+  r.long_codes.resize(r.n * (Dp * r.ex_bits / 8));
+  f.read(r.long_codes.data(), r.long_codes.size());
+  r.exfac.resize(r.n * 2);  // {f_ex_add, f_ex_rescale}; written but unused at 1 bit
+  f.read(r.exfac.data(), r.exfac.size() * 4);
   r.ids.resize(r.n);
   f.read(r.ids.data(), r.n * 4);
   for (uint32_t id : r.ids) RBQ_CHECK(id < r.n, RBQ_ERR_FORMAT, "reference index id out of range: " + f.path);
@@ -1114,6 +1191,9 @@ void free_index_memory(Index& ix)
   dev_free(ix.fadd_r);
   dev_free(ix.frescale_r);
   dev_free(ix.ferr_r);
+  dev_free(ix.ex_codes_r);
+  dev_free(ix.fexadd_r);
+  dev_free(ix.fexr_r);
   dev_free(ix.labels_r);
   dev_free(ix.ids_r);
   dev_free(ix.id2row);
@@ -1129,6 +1209,9 @@ void free_index_memory(Index& ix)
   dev_free(ix.fadd);
   dev_free(ix.frescale);
   dev_free(ix.ferr);
+  dev_free(ix.ex_codes);
+  dev_free(ix.fexadd);
+  dev_free(ix.fexr);
 }
 
 }  // namespace rbq
@@ -1165,6 +1248,7 @@ void rbq_index_params_default(rbq_index_params_t* p)
   p->shard_policy = RBQ_SHARD_ROUND_ROBIN;
   p->kmeans_kind = RBQ_KMEANS_BALANCED;
   p->raw_store = RBQ_RAW_DEVICE;
+  p->bits_per_dim = 1;
 }
 
 void rbq_search_params_default(rbq_search_params_t* p)
@@ -1215,6 +1299,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
               RBQ_ERR_INVALID, "unknown k-means kind");
     RBQ_CHECK(params->raw_store == RBQ_RAW_DEVICE || params->raw_store == RBQ_RAW_HOST, RBQ_ERR_INVALID,
               "unknown raw store (RBQ_RAW_DEVICE or RBQ_RAW_HOST)");
+    RBQ_CHECK(params->bits_per_dim >= 1 && params->bits_per_dim <= 9, RBQ_ERR_INVALID,
+              "bits_per_dim must be in [1, 9]");
     int ndev = 0;
     RBQ_CUDA(cudaGetDeviceCount(&ndev));
     RBQ_CHECK(params->device >= 0 && params->device < ndev, RBQ_ERR_INVALID, "device ordinal out of range");
@@ -1241,6 +1327,8 @@ int rbq_index_create(const rbq_index_params_t* params, rbq_index_t** out)
       ix.P_host.resize((size_t)ix.Dp * ix.Dp);
       make_rotation(ix.Dp, ix.seed, ix.P_host.data());
       ix.t4 = query_scale(ix.Dp, ix.seed, 3);
+      ix.ex_bits = params->bits_per_dim - 1;
+      ix.tex = ex_scale_of(ix);
       ix.P = dev_alloc<float>(ix.P_host.size());
       ix.dev_err = dev_alloc<int>(1);
       RBQ_CUDA(cudaMemset(ix.dev_err, 0, sizeof(int)));
@@ -1284,12 +1372,15 @@ int rbq_index_info(rbq_index_t* index, rbq_index_info_t* out)
     out->n_local = ix.n_rows;
     out->query_scale = ix.t4;
     out->seed = ix.seed;
-    const int64_t per_row = (int64_t)ix.D * 4 + (int64_t)ix.W * 4 * 2 + 12 * 2 + 4 * 3;
+    const int64_t per_row = (int64_t)ix.D * 4 + (int64_t)ix.W * 4 * 2 + 12 * 2 + 4 * 3 +
+                            ((int64_t)ix.ex_bits * ix.W * 4 + 8) * 2 * (ix.ex_bits > 0);
     out->device_bytes = ix.cap_rows * per_row + ix.cap_ids * 4 + (int64_t)ix.Dp * ix.Dp * 4 +
                         (int64_t)ix.K * (ix.D + ix.Dp + 3) * 4 + (ix.K + 1) * 8;
     out->shard_policy = ix.shard_policy;
     out->owners_fixed = ix.owners_fixed ? 1 : 0;
     out->kmeans_kind = ix.kmeans_kind;
+    out->bits_per_dim = ix.ex_bits + 1;
+    out->ex_scale = ix.tex;
   });
 }
 
@@ -1477,6 +1568,9 @@ int rbq_save(rbq_index_t* index, const char* path)
     const int32_t pol[2] = {ix.shard_policy, ix.owners_fixed ? 1 : 0};
     f.write(pol, sizeof(pol));
     f.write(ix.owner_host.data(), (size_t)ix.K * 4);
+    const int32_t exb = ix.ex_bits;
+    f.write(&exb, 4);
+    f.write(&ix.tex, 4);
     f.write(ix.P_host.data(), ix.P_host.size() * 4);
     if (ix.trained) f.write(ix.C_host.data(), ix.C_host.size() * 4);
     const size_t n = (size_t)ix.n_rows;
@@ -1486,6 +1580,11 @@ int rbq_save(rbq_index_t* index, const char* path)
     write_dev(f, ix.fadd_r, n);
     write_dev(f, ix.frescale_r, n);
     write_dev(f, ix.ferr_r, n);
+    if (ix.ex_bits > 0) {
+      write_dev(f, ix.ex_codes_r, n * ix.ex_bits * ix.W);
+      write_dev(f, ix.fexadd_r, n);
+      write_dev(f, ix.fexr_r, n);
+    }
     write_dev(f, ix.X_r, n * ix.D);
   });
 }
@@ -1502,7 +1601,7 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
     RBQ_CHECK(std::memcmp(magic, kMagic, 8) == 0, RBQ_ERR_FORMAT, "not an RBQB200 index file: " + f.path);
     uint32_t ver = 0;
     f.read(&ver, 4);
-    RBQ_CHECK(ver == 1 || ver == kFormatVersion, RBQ_ERR_FORMAT, "unsupported index file version");
+    RBQ_CHECK(ver >= 1 && ver <= kFormatVersion, RBQ_ERR_FORMAT, "unsupported index file version");
     int32_t hdr[8];
     f.read(hdr, sizeof(hdr));
     uint64_t seed;
@@ -1525,6 +1624,13 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
                 "corrupt shard policy");
       file_owner.resize(K);
       f.read(file_owner.data(), (size_t)K * 4);
+    }
+    int32_t exb = 0;
+    float tex = 0.0f;
+    if (ver >= 3) {
+      f.read(&exb, 4);
+      f.read(&tex, 4);
+      RBQ_CHECK(exb >= 0 && exb <= 8, RBQ_ERR_FORMAT, "corrupt extra-bit count");
     }
     if (shard_count <= 0) {
       shard_count = file_count;
@@ -1566,6 +1672,8 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       ix.shard_policy = pol[0];
       ix.has_raw = (hdr[7] & 2) == 0;
       ix.t4 = t4;
+      ix.ex_bits = exb;
+      ix.tex = tex;
       ix.P_host.resize((size_t)Dp * Dp);
       f.read(ix.P_host.data(), ix.P_host.size() * 4);
       ix.P = dev_alloc<float>(ix.P_host.size());
@@ -1589,6 +1697,14 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       f.read(fa.data(), fa.size() * 4);
       f.read(fr.data(), fr.size() * 4);
       f.read(fe.data(), fe.size() * 4);
+      const int EW = exb * W;
+      std::vector<uint32_t> xc((size_t)n_rows * EW);
+      std::vector<float> xa(exb ? n_rows : 0), xr(exb ? n_rows : 0);
+      if (exb) {
+        f.read(xc.data(), xc.size() * 4);
+        f.read(xa.data(), xa.size() * 4);
+        f.read(xr.data(), xr.size() * 4);
+      }
       f.read(X.data(), X.size() * 4);
       for (int64_t i = 0; i < n_rows; ++i)
         RBQ_CHECK(lab[i] < (uint32_t)K && ids[i] < (uint64_t)n_total, RBQ_ERR_FORMAT, "corrupt row data");
@@ -1631,6 +1747,13 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
       up(ix.fadd_r, fa2.data(), m * 4);
       up(ix.frescale_r, fr2.data(), m * 4);
       up(ix.ferr_r, fe2.data(), m * 4);
+      if (exb) {
+        const auto xc2 = pick_u32(xc, EW);
+        const auto xa2 = pick_f32(xa, 1), xr2 = pick_f32(xr, 1);
+        up(ix.ex_codes_r, xc2.data(), (size_t)m * EW * 4);
+        up(ix.fexadd_r, xa2.data(), m * 4);
+        up(ix.fexr_r, xr2.data(), m * 4);
+      }
       up(ix.X_r, x2.data(), (size_t)m * D * 4);
       std::vector<uint32_t> id2row(n_total, 0xFFFFFFFFu);
       for (int64_t i = 0; i < m; ++i) id2row[i2[i]] = (uint32_t)i;
@@ -1657,7 +1780,8 @@ int rbq_load(const char* path, int32_t device, int32_t shard_rank, int32_t shard
 //   1-bit codes n x Dp/32 u32, clusters in order, vector-major inside a cluster;
 //   factors n x {f_add, f_rescale, f_err} f32; long codes n x Dp*ex_bits/8 bytes;
 //   extra-bit factors n x 2 f32; ids n x u32; optional "RPR1" representatives block.
-// Only 1-bit files (ex_bits = 0) with the matmul rotator are accepted.
+// Files with up to 8 extra bits (bits_per_dim <= 9) and the matmul rotator are accepted; extra
+// bits are converted between the long-code bit stream and this library's planes.
 // ---------------------------------------------------------------------------------------
 int rbq_import_reference(const char* path, int32_t device, const float* X_host, int64_t n_x, int32_t shard_rank,
                          int32_t shard_count, int32_t shard_policy, rbq_index_t** out)
@@ -1678,6 +1802,7 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
     p.shard_rank = shard_rank;
     p.shard_count = shard_count;
     p.shard_policy = shard_policy;
+    p.bits_per_dim = (int32_t)r.ex_bits + 1;
     rbq_index_t* h = nullptr;
     int st = rbq_index_create(&p, &h);
     if (st != RBQ_OK) throw Error{st, g_last_error};
@@ -1690,6 +1815,7 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
       RBQ_CUDA(cudaMemcpy(ix.P, ix.P_host.data(), ix.P_host.size() * 4, cudaMemcpyHostToDevice));
       ix.t4 = r.t4;
       ix.t8 = r.t8;
+      ix.tex = ex_scale_of(ix);
       // original-space centroids c = c_rot P^T (P orthogonal), first D columns, for assigning
       // later adds; the search keeps the file's rotated centroids bit for bit
       ix.C_host.assign((size_t)K * D, 0.0f);
@@ -1719,8 +1845,17 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
       const int64_t m = (int64_t)keep.size();
       std::vector<uint32_t> codes((size_t)m * W), ids(m), labs(m);
       std::vector<float> fa(m), fr(m), fe(m), X(X_host ? (size_t)m * D : 0);
+      const int ex = ix.ex_bits;
+      const size_t lcb = (size_t)Dp * ex / 8;
+      std::vector<uint32_t> xc((size_t)m * ex * W);
+      std::vector<float> xa(ex ? m : 0), xr(ex ? m : 0);
       for (int64_t i = 0; i < m; ++i) {
         const int64_t src = keep[i].second;
+        if (ex) {
+          long_code_to_planes(&r.long_codes[(size_t)src * lcb], Dp, ex, &xc[(size_t)i * ex * W]);
+          xa[i] = r.exfac[src * 2 + 0];
+          xr[i] = r.exfac[src * 2 + 1];
+        }
         std::memcpy(&codes[(size_t)i * W], &r.codes[(size_t)src * W], (size_t)W * 4);
         ids[i] = keep[i].first;
         labs[i] = lab_of_row[src];
@@ -1740,6 +1875,11 @@ int rbq_import_reference(const char* path, int32_t device, const float* X_host, 
       up(ix.fadd_r, fa.data(), (size_t)m * 4);
       up(ix.frescale_r, fr.data(), (size_t)m * 4);
       up(ix.ferr_r, fe.data(), (size_t)m * 4);
+      if (ex) {
+        up(ix.ex_codes_r, xc.data(), xc.size() * 4);
+        up(ix.fexadd_r, xa.data(), (size_t)m * 4);
+        up(ix.fexr_r, xr.data(), (size_t)m * 4);
+      }
       if (X_host) up(ix.X_r, X.data(), X.size() * 4);
       ix.has_raw = X_host != nullptr;
       std::vector<uint32_t> id2row(r.n, 0xFFFFFFFFu);
@@ -1765,7 +1905,7 @@ int rbq_export_reference(rbq_index_t* index, const char* path)
     RBQ_CHECK(ix.shard_count == 1, RBQ_ERR_STATE, "the reference format holds a whole index: export an unsharded one");
     DeviceGuard dg(ix.device);
     RBQ_CUDA(cudaDeviceSynchronize());
-    const uint64_t n = (uint64_t)ix.n_rows, D = (uint64_t)ix.D, K = (uint64_t)ix.K, ex = 0;
+    const uint64_t n = (uint64_t)ix.n_rows, D = (uint64_t)ix.D, K = (uint64_t)ix.K, ex = (uint64_t)ix.ex_bits;
     File f(path, "wb");
     f.write(&n, 8);
     f.write(&D, 8);
@@ -1796,7 +1936,21 @@ int rbq_export_reference(rbq_index_t* index, const char* path)
       fac[i * 3 + 2] = fe[i];
     }
     f.write(fac.data(), fac.size() * 4);
-    const std::vector<float> exf(n * 2, 0.0f);
+    std::vector<float> exf(n * 2, 0.0f);
+    if (ex && n) {
+      const size_t EW = (size_t)ex * ix.W, lcb = (size_t)ix.Dp * ex / 8;
+      std::vector<uint32_t> xc(n * EW);
+      std::vector<uint8_t> lc(n * lcb);
+      RBQ_CUDA(cudaMemcpy(xc.data(), ix.ex_codes, xc.size() * 4, cudaMemcpyDeviceToHost));
+      for (uint64_t i = 0; i < n; ++i) planes_to_long_code(&xc[i * EW], ix.Dp, (int)ex, &lc[i * lcb]);
+      f.write(lc.data(), lc.size());
+      RBQ_CUDA(cudaMemcpy(fa.data(), ix.fexadd, n * 4, cudaMemcpyDeviceToHost));
+      RBQ_CUDA(cudaMemcpy(fr.data(), ix.fexr, n * 4, cudaMemcpyDeviceToHost));
+      for (uint64_t i = 0; i < n; ++i) {
+        exf[i * 2 + 0] = fa[i];
+        exf[i * 2 + 1] = fr[i];
+      }
+    }
     f.write(exf.data(), exf.size() * 4);
     write_dev(f, ix.ids, (size_t)n);
   });
@@ -1840,6 +1994,22 @@ int rbq_export_lists(rbq_index_t* index, int64_t* list_off, uint32_t* ids, uint3
     if (fadd) RBQ_CUDA(cudaMemcpy(fadd, ix.fadd, n * 4, cudaMemcpyDeviceToHost));
     if (frescale) RBQ_CUDA(cudaMemcpy(frescale, ix.frescale, n * 4, cudaMemcpyDeviceToHost));
     if (ferr) RBQ_CUDA(cudaMemcpy(ferr, ix.ferr, n * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int rbq_export_ex_lists(rbq_index_t* index, uint32_t* ex_codes, float* fexadd, float* fexr)
+{
+  return guarded([&] {
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    Index& ix = index->ix;
+    RBQ_CHECK(ix.ex_bits > 0, RBQ_ERR_STATE, "the index has 1-bit codes only (bits_per_dim = 1)");
+    DeviceGuard dg(ix.device);
+    RBQ_CUDA(cudaDeviceSynchronize());
+    const size_t n = (size_t)ix.n_rows;
+    if (n == 0) return;
+    if (ex_codes) RBQ_CUDA(cudaMemcpy(ex_codes, ix.ex_codes, n * ix.ex_bits * ix.W * 4, cudaMemcpyDeviceToHost));
+    if (fexadd) RBQ_CUDA(cudaMemcpy(fexadd, ix.fexadd, n * 4, cudaMemcpyDeviceToHost));
+    if (fexr) RBQ_CUDA(cudaMemcpy(fexr, ix.fexr, n * 4, cudaMemcpyDeviceToHost));
   });
 }
 

@@ -100,6 +100,10 @@ struct Index {
   std::vector<int32_t> owner_host;  // [K] rank holding list l
   float t4 = 0.0f;
   bool trained = false;
+  // ExRaBitQ (bits_per_dim = ex_bits + 1): ex_bits extra bits per dimension beyond the 1-bit
+  // code, quantised with data scale tex (0 extra bits: 1-bit codes only).
+  int ex_bits = 0;
+  float tex = 0.0f;
 
   std::vector<float> P_host;       // [Dp*Dp] rotation (row-major)
   std::vector<float> C_host;       // [K*D] centroids, original space
@@ -121,6 +125,9 @@ struct Index {
   float* fadd_r = nullptr;       // [n_rows]
   float* frescale_r = nullptr;   // [n_rows]
   float* ferr_r = nullptr;       // [n_rows]
+  uint32_t* ex_codes_r = nullptr;  // [n_rows*ex_bits*W] extra-bit planes (ex_bits > 0)
+  float* fexadd_r = nullptr;       // [n_rows]
+  float* fexr_r = nullptr;         // [n_rows]
   uint32_t* labels_r = nullptr;  // [n_rows]
   uint32_t* ids_r = nullptr;     // [n_rows] global ids
   int64_t cap_ids = 0;
@@ -152,6 +159,11 @@ struct Index {
   float* fadd = nullptr;         // [n_rows]
   float* frescale = nullptr;     // [n_rows]
   float* ferr = nullptr;         // [n_rows]
+  // Extra bits (ex_bits > 0): one vector = ex_bits planes of W words (plane p word w, dim 32w+j
+  // -> bit 31-j = bit p of the dim's extra-bit code), then the two extra-bit factors.
+  uint32_t* ex_codes = nullptr;  // [n_rows*ex_bits*W]
+  float* fexadd = nullptr;       // [n_rows]
+  float* fexr = nullptr;         // [n_rows]
 };
 
 void free_index_memory(Index& ix);
@@ -176,6 +188,10 @@ void launch_rotate(const float* X, int64_t n, int D, int Dp, const float* P, flo
 // 1-bit codes + factors of rotated rows Y against rotated centroids of their labels.
 void launch_quantize(const float* Y, int64_t n, int Dp, const float* C_rot, const uint32_t* labels,
                      uint32_t* codes, float* fadd, float* frescale, float* ferr, cudaStream_t s);
+// ExRaBitQ extra-bit planes [n, ex, W] and factors f_ex_add / f_ex_rescale of rotated rows Y
+// (data scale t), against the rotated centroids of their labels.
+void launch_quantize_ex(const float* Y, int64_t n, int Dp, const float* C_rot, const uint32_t* labels, int ex,
+                        float t, uint32_t* planes, float* fexadd, float* fexr, cudaStream_t s);
 // Row squared norms (float, any order) of A[n, d].
 void launch_row_norms(const float* A, int64_t n, int d, float* out, cudaStream_t s);
 // Approximate scores S[q, c] = |c|^2 - 2 <a_q, c> for ranking (fp32).
@@ -221,6 +237,11 @@ struct ScanArgs {
   const float* fadd;
   const float* frescale;
   const float* ferr;
+  // ExRaBitQ: an admitted vector's distance is the extra-bit one (ex_bits > 0; null otherwise)
+  const uint32_t* ex_codes = nullptr;  // [n_slots, ex_bits, W]
+  const float* fexadd = nullptr;
+  const float* fexr = nullptr;
+  int ex_bits = 0;
   int64_t n_slots;  // vectors on the shard (the scan indexes slots with 32-bit ints)
   int Dp, W;
   const float* Qr;

@@ -633,6 +633,39 @@ __device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ code
   return v;
 }
 
+// <x, q> of the extra-bit code x at `slot` (planes [ex, W], plane p = bit p of every dim's
+// code), computed by the whole warp: lane l takes code bytes j = l, l + 32, ...; per byte, planes
+// p = ex-1 down to 0 add 2^p * bsum_p(j) (the sum of q over the set bits of byte j of plane p, bit
+// 7 first, from 0) to the lane's value; an xor butterfly combines the lanes.
+template <int W>
+__device__ __forceinline__ float warp_ex_ip(const uint32_t* __restrict__ ex_codes, int64_t slot, int ex,
+                                            const float* __restrict__ qsT, int lane)
+{
+  constexpr int NB = 4 * W;
+  constexpr int M = (NB + 31) / 32;
+  const unsigned char* cb = reinterpret_cast<const unsigned char*>(ex_codes + slot * ex * W);
+  float v = 0.0f;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int j = lane + 32 * m;
+    if (j < NB) {
+      float qv[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) qv[jj] = qsT[jj * NB + j];
+      for (int p = ex - 1; p >= 0; --p) {
+        const uint32_t u8 = __ldg(cb + p * NB + (j ^ 3));
+        float b = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) b = ((u8 >> (7 - jj)) & 1u) ? __fadd_rn(b, qv[jj]) : b;
+        v = __fadd_rn(v, __fmul_rn((float)(1 << p), b));
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
 // ---------------------------------------------------------------------------------------
 // Signed 4-bit x 1-bit inner product with few popcounts.  The AND-ed plane words are summed
 // bit-sliced with carry-save adders (Harley-Seal): a full adder turns three words of weight w
@@ -989,13 +1022,19 @@ constexpr int scan_min_blocks()
   return (W <= 4 || W == 8) ? RBQ_SCAN_MINB8 : (W < 8 ? 5 : 4);
 }
 
-// Bytes at the start of the scan's shared memory before the key buffers: the query planes and
-// the byte-transposed query (popcount modes), or the query tables (LUT16: fp16, LUT32: fp32
-// entries, 16 per 4-dim chunk).  All multiples of 16.
+// Bytes at the start of the scan's shared memory before the key buffers: the query planes
+// (popcount modes) or the query tables (LUT16: fp16, LUT32: fp32 entries, 16 per 4-dim chunk),
+// then the byte-transposed query (8 * 4W floats; in the LUT modes only filled for extra-bit
+// codes).  All multiples of 16.
+template <int W, int QB>
+constexpr int scan_table_bytes()
+{
+  return QB == 16 ? 256 * W : (QB == 32 ? 512 * W : 4 * W * QB);
+}
 template <int W, int QB>
 constexpr int scan_head_bytes()
 {
-  return QB == 16 ? 32 * W * 8 : (QB == 32 ? 32 * W * 16 : 4 * W * (QB + 32));
+  return scan_table_bytes<W, QB>() + 128 * W;
 }
 
 // <bits, q> by the query tables: words in order, nibbles from the top (bit 31) down, added one
@@ -1024,12 +1063,11 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
 {
   constexpr int NB = 4 * W;
   constexpr bool kLut = QB >= 16;    // LUT16 / LUT32: the table estimate is the distance
-  constexpr int PB = kLut ? 4 : QB;  // plane words per code word (unused by the LUT modes)
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // planes first (16-byte aligned); QB*W + 8*NB words = 4W(QB + 32) bytes keep the keys 8-aligned
   uint32_t* pl = reinterpret_cast<uint32_t*>(smem_raw);                        // [QB * W]
-  float* qsT = reinterpret_cast<float*>(pl + PB * W);                           // [8 * NB]
   unsigned char* tab = smem_raw;                                                // LUT modes
+  float* qsT = reinterpret_cast<float*>(smem_raw + scan_table_bytes<W, QB>());  // [8 * NB]
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + scan_head_bytes<W, QB>());  // [cap]
   unsigned long long* keys2 = keys + a.cap;                                    // [cap]
   int* pre = reinterpret_cast<int*>(keys2 + a.cap);                            // [nprobe + 1]
@@ -1062,6 +1100,11 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       else
         reinterpret_cast<float*>(tab)[i] = sum;
     }
+    if (a.ex_bits > 0)
+      for (int i = tid; i < 8 * NB; i += kScanThreads) {
+        const int jj = i / NB, j = i - jj * NB;
+        qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
+      }
   } else {
     for (int i = tid; i < 8 * NB; i += kScanThreads) {
       const int jj = i / NB, j = i - jj * NB;
@@ -1144,6 +1187,10 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const int total = pre[nl];
   const float delta = a.delta[q];
   const float k1 = a.k1[q];
+  // extra-bit estimator constants: 2^ex and kb = -(2^(ex+1) - 1)/2 * sum q = k1 * (2^(ex+1) - 1)
+  // (computeQueryFactorsWarpKernel, ivf_gpu.cu:1450-1490)
+  const float ex_scale = (float)(1 << a.ex_bits);
+  const float kb = __fmul_rn(k1, (float)((2 << a.ex_bits) - 1));
   // Bound seed: a pruning slice with no threshold and no candidates yet starts from the R-th
   // smallest upper bound est + f_err * sqrt(g) over its leading whole lists holding at least R
   // vectors (the RaBitQ error bound: R of them are that close), instead of admitting its first
@@ -1214,9 +1261,20 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
           const float ip = lut_ip<W, QB>(tab, c);
           const float est = __fadd_rn(__fadd_rn(__ldg(a.fadd + slot), gc),
                                       __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(ip, k1)));
-          if (est <= tau) {
-            ++n_admit;
-            keys[atomicAdd(&s_count, 1)] = make_key(est, __ldg(a.ids + slot));
+          if (a.ex_bits == 0) {
+            if (est <= tau) {
+              ++n_admit;
+              keys[atomicAdd(&s_count, 1)] = make_key(est, __ldg(a.ids + slot));
+            }
+          } else {  // extra bits: the table estimate's error bound admits (sbase = g, sfr = ip)
+            const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
+            if (!a.prune || low < tau) {
+              ++n_admit;
+              surv = true;
+              sslot = slot;
+              sbase = gc;
+              sfr = ip;
+            }
           }
         } else {
           const int32_t acc = dot_vector<W, QB>(a.codes, slot, pl);
@@ -1229,12 +1287,14 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
             ++n_admit;
             surv = true;
             sslot = slot;
-            sbase = base_d;
+            sbase = a.ex_bits ? gc : base_d;  // extra bits: the distance starts from f_ex_add + g
             sfr = fr;
           }
         }
       }
-      if constexpr (kLut) continue;  // no exact pass: the table estimate is the distance
+      if constexpr (kLut) {
+        if (a.ex_bits == 0) continue;  // no exact pass: the table estimate is the distance
+      }
       // phase 2: the warp's admitted vectors of this round, one at a time, all lanes.
       unsigned mask = __ballot_sync(0xffffffffu, surv);
       while (mask) {
@@ -1243,8 +1303,22 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
         const int slot = __shfl_sync(0xffffffffu, sslot, src);
         const float base_d = __shfl_sync(0xffffffffu, sbase, src);
         const float fr = __shfl_sync(0xffffffffu, sfr, src);
-        const float eip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
-        const float dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
+        float dist;
+        if (a.ex_bits == 0) {
+          const float eip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
+          dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
+        } else {
+          // the extra-bit distance (f_ex_add + g) + f_ex_rescale * ((2^ex ip + ip_x) + kb), ip the
+          // 1-bit inner product: exact, or the table one (carried in fr) in the LUT modes
+          float ip;
+          if constexpr (kLut)
+            ip = fr;
+          else
+            ip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
+          const float ipx = warp_ex_ip<W>(a.ex_codes, slot, a.ex_bits, qsT, lane);
+          const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, ip), ipx), kb);
+          dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), base_d), __fmul_rn(__ldg(a.fexr + slot), T));
+        }
         if (lane == 0 && dist <= tau) {
           const int at = atomicAdd(&s_count, 1);
           keys[at] = make_key(dist, __ldg(a.ids + slot));

@@ -35,7 +35,8 @@ def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
 
 
 class IndexIVFRaBitQ:
-    """1-bit IVF-RaBitQ index with 4-bit query quantisation and optional exact rerank.
+    """IVF-RaBitQ index (1-bit codes, or ExRaBitQ with extra bits) with 4-bit query quantisation
+    and optional exact rerank.
 
     Parameters mirror cuvs::neighbors::ivf_rabitq::index_params (ivf_rabitq.hpp:50-103):
     ``nlist`` (n_lists), ``kmeans_iters`` (kmeans_n_iters), ``max_train_points_per_cluster``,
@@ -43,7 +44,9 @@ class IndexIVFRaBitQ:
     a shard of a sharded index also takes ``shard_rank`` / ``shard_count`` and ``shard_policy``
     ("round_robin": list l on rank l % count; "balanced": lists spread by size^2 at the first add);
     ``raw_store`` ("device": the exact rerank's raw fp32 rows in HBM; "host": in pinned host
-    memory read over PCIe, for a raw set larger than the GPU's memory).
+    memory read over PCIe, for a raw set larger than the GPU's memory); ``bits_per_dim`` (1: 1-bit
+    RaBitQ codes; 2..9: ExRaBitQ, the vectors the 1-bit estimate admits are ranked by the
+    distance of their (bits_per_dim)-bit codes).
     Search attributes mirror search_params (ivf_rabitq.hpp:178-228) and FAISS: ``nprobe``,
     ``k_rerank`` (exact fp32 rerank depth R, 0 = estimator order as in the reference),
     ``prune`` (RaBitQ error-bound prune), ``probe_split`` (0 = auto), ``seeded`` (two-phase
@@ -56,7 +59,7 @@ class IndexIVFRaBitQ:
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
                  max_train_points_per_cluster: int = 256, shard_rank: int = 0, shard_count: int = 1,
                  metric: str = "l2", shard_policy: str = "round_robin", kmeans: str = "balanced",
-                 raw_store: str = "device", _handle=None):
+                 raw_store: str = "device", bits_per_dim: int = 1, _handle=None):
         if metric not in ("l2", "ip"):
             raise ValueError("metric must be 'l2' or 'ip'")
         self.d = int(d)
@@ -90,6 +93,7 @@ class IndexIVFRaBitQ:
         if raw_store not in _lib.RAW_STORES:
             raise ValueError(f"raw_store must be one of {sorted(_lib.RAW_STORES)}")
         p.raw_store = _lib.RAW_STORES[raw_store]
+        p.bits_per_dim = int(bits_per_dim)
         _lib.call("rbq_index_create", ctypes.byref(p), ctypes.byref(self._h))
 
     # -- lifecycle -----------------------------------------------------------------------
@@ -251,7 +255,14 @@ class IndexIVFRaBitQ:
         codes = np.empty((n, w), np.uint32)
         fa, fr, fe = (np.empty(n, np.float32) for _ in range(3))
         _lib.call("rbq_export_lists", self._h, *(a.ctypes.data_as(ctypes.c_void_p) for a in (off, ids, codes, fa, fr, fe)))
-        return {"list_off": off, "ids": ids, "codes": codes, "fadd": fa, "frescale": fr, "ferr": fe}
+        out = {"list_off": off, "ids": ids, "codes": codes, "fadd": fa, "frescale": fr, "ferr": fe}
+        ex = int(inf.bits_per_dim) - 1
+        if ex > 0:
+            xc = np.empty((n, ex, w), np.uint32)
+            xa, xr = np.empty(n, np.float32), np.empty(n, np.float32)
+            _lib.call("rbq_export_ex_lists", self._h, *(a.ctypes.data_as(ctypes.c_void_p) for a in (xc, xa, xr)))
+            out.update(ex_bits=ex, ex_codes=xc, fexadd=xa, fexr=xr, ex_scale=float(inf.ex_scale))
+        return out
 
     def list_offsets(self) -> np.ndarray:
         """[nlist + 1] int64: list l holds this shard's slots [off[l], off[l + 1])."""
@@ -264,6 +275,10 @@ class IndexIVFRaBitQ:
         own = np.empty(self.nlist, np.int32)
         _lib.call("rbq_get_list_owners", self._h, own.ctypes.data_as(ctypes.c_void_p))
         return own
+
+    @property
+    def bits_per_dim(self) -> int:
+        return int(self.info().bits_per_dim)
 
     @property
     def query_scale(self) -> float:

@@ -64,7 +64,11 @@ def lib():
         L.orc_scan.argtypes = [_i64p, _u32p, _u32p, _f32p, _f32p, _f32p, _i32, _f32p, _u32p,
                                _f32p, _f32p, _i64, _i32p, _f32p, _i32, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_void_p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.c_void_p,
-                               _i64p, _f32p, _i64p, _i32]
+                               _i64p, _f32p, _i64p, _i32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _i32]
+        L.orc_quantize_ex_one.argtypes = [_f32p, _f32p, _i32, _i32, ctypes.c_float, _u32p, _f32p]
+        L.orc_quantize_ex.argtypes = [_f32p, _i64, _i32, _f32p, _u32p, _i32, ctypes.c_float, _u32p, _f32p, _f32p]
+        L.orc_ex_ip.argtypes = [_f32p, _u32p, _i32, _i32]
+        L.orc_ex_ip.restype = ctypes.c_float
         L.orc_bound_seed.argtypes = [_i64p, _u32p, _f32p, _f32p, _f32p, _i32, _u32p, _f32p, _f32p, _i64, _i32p,
                                      _f32p, _i32, _i32, _i32, _i32, ctypes.c_void_p, _f32p, _i32]
         L.orc_float_to_half.argtypes = [ctypes.c_void_p, _i64, ctypes.c_void_p]
@@ -159,6 +163,46 @@ def quantize_one(y, c):
     return code, f3
 
 
+def quantize_ex_one(y, c, ex_bits: int, t: float):
+    """ExRaBitQ extra-bit planes [ex_bits, W] and (f_ex_add, f_ex_rescale) of one rotated vector."""
+    y, c = _c(y, np.float32), _c(c, np.float32)
+    dp = y.size
+    planes = np.empty((ex_bits, dp // 32), np.uint32)
+    f2 = np.empty(2, np.float32)
+    lib().orc_quantize_ex_one(y, c, dp, ex_bits, np.float32(t), planes, f2)
+    return planes, f2
+
+
+def quantize_ex(Y, c_rot, labels, ex_bits: int, t: float):
+    """Extra-bit planes [n, ex_bits, W], f_ex_add [n], f_ex_rescale [n] of rotated rows Y."""
+    Y = _c(Y, np.float32)
+    n, dp = Y.shape
+    planes = np.empty((n, ex_bits, dp // 32), np.uint32)
+    fa = np.empty(n, np.float32)
+    fr = np.empty(n, np.float32)
+    if n:
+        lib().orc_quantize_ex(Y, n, dp, _c(c_rot, np.float32), _c(labels, np.uint32), ex_bits, np.float32(t),
+                              planes, fa, fr)
+    return planes, fa, fr
+
+
+def ex_ip(q, planes) -> float:
+    """<extra-bit code, q> of one vector's planes [ex_bits, W] in the scan's summation order."""
+    planes = _c(planes, np.uint32)
+    ex, w = planes.shape
+    return float(lib().orc_ex_ip(_c(q, np.float32), planes, w, ex))
+
+
+def ex_scale(dp: int, seed: int, ex_bits: int, t4: float, t8=None) -> float:
+    """The data scale of ex_bits extra bits: the 4-bit query scale at 3, the 8-bit one at 7
+    (ivf_gpu.cu:629-644), else the best-rescale mean for ex_bits (query_scale)."""
+    if ex_bits == 3:
+        return float(t4)
+    if ex_bits == 7:
+        return float(t8) if t8 is not None else query_scale(dp, seed, 7)
+    return query_scale(dp, seed, ex_bits)
+
+
 class OracleIndex:
     """Index arrays in list-slot order, as the CUDA library lays them out in HBM."""
 
@@ -168,9 +212,19 @@ class OracleIndex:
         self.list_off, self.ids, self.codes = list_off, ids, codes
         self.fadd, self.frescale, self.ferr = fadd, frescale, ferr
         self.c_rot, self.P, self.t4, self.X = c_rot, P, t4, X
+        # ExRaBitQ (bits_per_dim = ex_bits + 1 > 1): planes [n, ex_bits, W], factors [n], slot order
+        self.ex_bits, self.ex_codes, self.fexadd, self.fexr, self.tex = 0, None, None, None, None
+
+    def set_ex(self, ex_bits, ex_codes, fexadd, fexr, tex=None):
+        self.ex_bits = int(ex_bits)
+        self.ex_codes = _c(ex_codes, np.uint32).reshape(-1, ex_bits, self.dp // 32)
+        self.fexadd, self.fexr, self.tex = _c(fexadd, np.float32), _c(fexr, np.float32), tex
+        return self
 
 
-def build(X, C, labels, P, t4) -> OracleIndex:
+def build(X, C, labels, P, t4, bits_per_dim=1, tex=None) -> OracleIndex:
+    """Index of X with the given centroids and labels; bits_per_dim > 1 adds ExRaBitQ extra bits
+    with data scale tex (default t4, the 4-bit query scale, which the reference uses at 4 bits)."""
     X = _c(X, np.float32)
     C = _c(C, np.float32)
     n, d = X.shape
@@ -184,9 +238,17 @@ def build(X, C, labels, P, t4) -> OracleIndex:
     fres = np.empty(n, np.float32)
     ferr = np.empty(n, np.float32)
     c_rot = np.empty((k, dp), np.float32)
-    lib().orc_build(X, n, d, dp, _c(P, np.float32), C, k, _c(labels, np.uint32), list_off, ids,
+    labels = _c(labels, np.uint32)
+    lib().orc_build(X, n, d, dp, _c(P, np.float32), C, k, labels, list_off, ids,
                     codes, fadd, fres, ferr, c_rot)
-    return OracleIndex(d, dp, k, list_off, ids, codes, fadd, fres, ferr, c_rot, P, t4, X)
+    ix = OracleIndex(d, dp, k, list_off, ids, codes, fadd, fres, ferr, c_rot, P, t4, X)
+    if bits_per_dim > 1:
+        ex = bits_per_dim - 1
+        t = float(t4) if tex is None else float(tex)
+        Y = rotate(X[ids.astype(np.int64)], P)
+        planes, fa, fr = quantize_ex(Y, c_rot, labels[ids.astype(np.int64)], ex, t)
+        ix.set_ex(ex, planes, fa, fr, t)
+    return ix
 
 
 def query_prep(Qr, t4: float, bits: int = 4):
@@ -273,7 +335,7 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
         lib().orc_scan(ix.list_off, ix.ids, ix.codes.reshape(-1), ix.fadd, ix.frescale, ix.ferr, ix.dp, Qr,
                        _c(planes, np.uint32), _c(delta, np.float32), _c(k1, np.float32), nq, probes, g,
                        nprobe, t0, i0, d0, R, tile, cap, prune, slices, shard_rank, shard_count, ow,
-                       out_ids, out_d, stats, mode if mode else _bits_of(planes, nq, ix.dp // 32))
+                       out_ids, out_d, stats, mode if mode else _bits_of(planes, nq, ix.dp // 32), *_ex_args(ix))
     elif init is not None:
         out_ids[:], out_d[:] = merge_candidates([(init_i, init_d)], R)
     else:
@@ -282,6 +344,15 @@ def scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, c
     if with_stats:
         return out_ids, out_d, stats
     return out_ids, out_d
+
+
+def _ex_args(ix):
+    """The trailing ExRaBitQ arguments of orc_scan (null pointers for a 1-bit index)."""
+    ex = getattr(ix, "ex_bits", 0)
+    if not ex:
+        return None, None, None, 0
+    return (ix.ex_codes.ctypes.data_as(ctypes.c_void_p), ix.fexadd.ctypes.data_as(ctypes.c_void_p),
+            ix.fexr.ctypes.data_as(ctypes.c_void_p), ex)
 
 
 def _keys(ids, d):

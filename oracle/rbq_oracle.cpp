@@ -298,6 +298,78 @@ void orc_quantize_one(const float* y, const float* c, int Dp, uint32_t* code, fl
   f3[2] = 2.0f * tmp_err;
 }
 
+// ExRaBitQ extra bits (bits_per_dim = ex + 1 > 1) of one rotated vector y against rotated
+// centroid c: the fast-quantize branch of quantize_batch_opt (exrabitq_fused_kernel_batch,
+// quantizer_gpu.cu:347-468) on the normalised residual of subtract_normalize_binarize_Kernel
+// (:109-172).  t is the data scale (construct_on_gpu, ivf_gpu.cu:629-644: the 4-bit query scale
+// for ex = 3, the 8-bit one for ex = 7).  Per dim j, with r = y - c, xn = r / |r| (0 if |r| = 0):
+//   e_j = min(int(t * |xn_j| + 1e-5), 2^ex - 1);   stored x_j = e_j if bit_j else 2^ex - 1 - e_j
+//   (bit_j is the 1-bit code), so the whole (ex+1)-bit code u_j = bit_j * 2^ex + x_j and its
+//   centred value xu_j = u_j - (2^ex - 1/2);
+//   ip_norm = sum (e_j + 1/2) |xn_j|,  ip_resi = sum r_j xu_j,  ip_cent = sum c_j xu_j  (double
+//   sums in dim order, rounded to float);
+//   f_ex_add = |r|^2 + (2 |r|^2 ip_cent) / ip_resi  (ip_resi = 0 -> +inf);
+//   f_ex_rescale = -2 |r| / ip_norm  (1 / ip_norm not finite -> 1).
+// The reference sets the code's top bit from r_j >= 0 in the factors and from r_j > 0 in the
+// 1-bit code; here both use bit_j, so an exactly zero residual coordinate counts the same in
+// both.  planes [ex, W]: plane p word w, dim 32w+j -> bit 31-j = bit p of x_j.
+void orc_quantize_ex_one(const float* y, const float* c, int Dp, int ex, float t, uint32_t* planes, float* f2)
+{
+  double l2d = 0.0;
+  for (int j = 0; j < Dp; ++j) {
+    float r = y[j] - c[j];
+    l2d += (double)r * (double)r;
+  }
+  const float l2_sqr = (float)l2d;
+  const float norm = sqrtf(l2_sqr);
+  const int W = Dp / 32;
+  const int mask = (1 << ex) - 1;
+  const float shift = (float)(1 << ex) - 0.5f;
+  for (int i = 0; i < ex * W; ++i) planes[i] = 0u;
+  double ipn = 0.0, ipr = 0.0, ipc = 0.0;
+  for (int j = 0; j < Dp; ++j) {
+    const float r = y[j] - c[j];
+    const int bit = (norm > 0.0f && r > 0.0f) ? 1 : 0;
+    const float xn = norm > 0.0f ? r / norm : 0.0f;
+    const float a = fabsf(xn);
+    const float ta = t * a;
+    int e = (int)(ta + 1e-5f);
+    if (e > mask) e = mask;
+    const float en = (float)e + 0.5f;
+    ipn += (double)(en * a);
+    const int x = bit ? e : mask - e;
+    for (int b = 0; b < ex; ++b)
+      if ((x >> b) & 1) planes[b * W + (j >> 5)] |= 1u << (31 - (j & 31));
+    const float xu = (float)((bit << ex) | x) - shift;
+    ipr += (double)r * (double)xu;
+    ipc += (double)c[j] * (double)xu;
+  }
+  const float ip_resi = (float)ipr, ip_cent = (float)ipc, ip_norm = (float)ipn;
+  const float denom = ip_resi == 0.0f ? INFINITY : ip_resi;
+  const float l2_norm = sqrtf(fmaxf(l2_sqr, 0.0f));
+  const float num = (2.0f * l2_sqr) * ip_cent;
+  f2[0] = l2_sqr + num / denom;
+  float inv = 1.0f / ip_norm;
+  if (!std::isfinite(inv)) inv = 1.0f;
+  f2[1] = (-2.0f * l2_norm) * inv;
+}
+
+// Extra-bit codes of n rotated rows Y [n, Dp] against the rotated centroids of their labels:
+// planes [n, ex, W], f_ex_add [n], f_ex_rescale [n].
+void orc_quantize_ex(const float* Y, int64_t n, int Dp, const float* c_rot, const uint32_t* labels, int ex,
+                     float t, uint32_t* planes, float* fexadd, float* fexr)
+{
+  const int W = Dp / 32;
+#pragma omp parallel for schedule(dynamic, 256)
+  for (int64_t i = 0; i < n; ++i) {
+    float f2[2];
+    orc_quantize_ex_one(Y + (size_t)i * Dp, c_rot + (size_t)labels[i] * Dp, Dp, ex, t,
+                        planes + (size_t)i * ex * W, f2);
+    fexadd[i] = f2[0];
+    fexr[i] = f2[1];
+  }
+}
+
 // Build (a2 inputs, a3-a5): labels/centroids given.  Lists are a stable counting sort of
 // the labels (ids ascending inside a list).  Outputs are in list-slot order:
 //   list_off [K+1], ids [n] (global ids), codes [n*W] (vector-major), f_add/f_rescale/f_err [n],
@@ -495,6 +567,38 @@ float orc_exact_ip(const float* q, const uint32_t* code, int W)
   return v[0];
 }
 
+// <x, q> of a vector's extra-bit code x (planes [ex, W]) in the order of the CUDA scan's warp:
+// lane l takes code bytes j = l, l+32, ... (< 4W); per byte, planes p = ex-1 down to 0 add
+// 2^p * byte_sum(plane p, j) to the lane's value; xor butterfly; lane 0's value.  The extra-bit
+// distance of the scan (the WithEx branch, searcher_gpu_quantize_query.cu:405-473):
+//   d = (f_ex_add + g) + f_ex_rescale * ((2^ex * ip + ip_x) + kb),  kb = k1 * (2^(ex+1) - 1)
+// with ip the vector's 1-bit inner product (exact, or the table one in the LUT modes) and
+// kb = -(2^(ex+1) - 1)/2 * sum q (computeQueryFactorsWarpKernel, ivf_gpu.cu:1450-1490).
+float orc_ex_ip(const float* q, const uint32_t* planes, int W, int ex)
+{
+  const int NB = 4 * W;
+  float v[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int j = l; j < NB; j += 32)
+      for (int p = ex - 1; p >= 0; --p) s = s + (float)(1 << p) * byte_sum(q, planes + (size_t)p * W, j);
+    v[l] = s;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    float nv[32];
+    for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ off];
+    for (int l = 0; l < 32; ++l) v[l] = nv[l];
+  }
+  return v[0];
+}
+
+static inline float ex_distance(float fexadd, float fexr, float g, float ip, float ipx, int ex, float k1)
+{
+  const float kb = k1 * (float)((2 << ex) - 1);
+  const float T = ((float)(1 << ex) * ip + ipx) + kb;
+  return (fexadd + g) + fexr * T;
+}
+
 // fp32 -> IEEE binary16, round to nearest, ties to even (the rounding of CUDA's __float2half),
 // and back (exact).  Written from the IEEE 754 encodings.
 static uint16_t float_to_half_rn(float f)
@@ -600,6 +704,11 @@ struct ScanIndex {
   const float* frescale;
   const float* ferr;
   int qbits;  // query code width (planes per query)
+  // ExRaBitQ extra bits (ex = 0: 1-bit codes only): planes [n, ex, W], f_ex_add, f_ex_rescale
+  const uint32_t* ex_codes;
+  const float* fexadd;
+  const float* fexr;
+  int ex;
 };
 
 // One slice of one query's probes.  Mirrors the CUDA scan kernel's schedule exactly.
@@ -659,9 +768,21 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
       if (lut) {  // LUT16 / LUT32: the table estimate is the candidate's distance
         const float ip = lut_ip(table, code, W);
         const float est = (ix.fadd[s] + g) + ix.frescale[s] * (ip + k1);
-        if (est <= tau) {
+        if (ix.ex == 0) {
+          if (est <= tau) {
+            ++n_admit;
+            keys.push_back(make_key(est, ix.ids[s]));
+          }
+          continue;
+        }
+        // with extra bits the table estimate's error bound admits, the extra-bit distance ranks
+        // (searcher_gpu_shared_mem_opt.cu:303-310, 359-420)
+        const float low = est - ix.ferr[s] * sqrt_g;
+        if (!prune || low < tau) {
           ++n_admit;
-          keys.push_back(make_key(est, ix.ids[s]));
+          const float ipx = orc_ex_ip(qr, ix.ex_codes + (size_t)s * ix.ex * W, W, ix.ex);
+          const float dist = ex_distance(ix.fexadd[s], ix.fexr[s], g, ip, ipx, ix.ex, k1);
+          if (dist <= tau) keys.push_back(make_key(dist, ix.ids[s]));
         }
         continue;
       }
@@ -673,7 +794,13 @@ static void scan_slice(const ScanIndex& ix, int W, const float* qr, const uint32
       if (!prune || low < tau) {
         ++n_admit;
         float eip = orc_exact_ip(qr, code, W);
-        float dist = base_d + ix.frescale[s] * (eip + k1);
+        float dist;
+        if (ix.ex > 0) {
+          const float ipx = orc_ex_ip(qr, ix.ex_codes + (size_t)s * ix.ex * W, W, ix.ex);
+          dist = ex_distance(ix.fexadd[s], ix.fexr[s], g, eip, ipx, ix.ex, k1);
+        } else {
+          dist = base_d + ix.frescale[s] * (eip + k1);
+        }
         if (dist <= tau) keys.push_back(make_key(dist, ix.ids[s]));
       }
     }
@@ -744,15 +871,18 @@ void orc_bound_seed(const int64_t* list_off, const uint32_t* codes, const float*
 // owned[floor(s*m/S) : floor((s+1)*m/S)]), each scanned with its own threshold, then merged.
 // Outputs out_ids [nq, R] (int64, -1 pad) and out_dist [nq, R] (+inf pad).
 // stats (optional, int64[2]): vectors scanned, vectors admitted by the prune.
+// ex_codes / fexadd / fexr (optional, ExRaBitQ index with ex_bits extra bits, slot order): an
+// admitted vector's distance is the extra-bit distance (orc_ex_ip) instead of the 1-bit one.
 void orc_scan(const int64_t* list_off, const uint32_t* ids, const uint32_t* codes, const float* fadd,
               const float* frescale, const float* ferr, int Dp, const float* Qr, const uint32_t* planes,
               const float* delta, const float* k1, int64_t nq, const int32_t* probes, const float* gq,
               int nprobe, const float* tau0, const int64_t* init_ids, const float* init_dist, int R, int tile,
               int cap, int prune, int slices, int shard_rank, int shard_count, const int32_t* owner,
-              int64_t* out_ids, float* out_dist, int64_t* stats, int qbits)
+              int64_t* out_ids, float* out_dist, int64_t* stats, int qbits, const uint32_t* ex_codes,
+              const float* fexadd, const float* fexr, int ex_bits)
 {
   const int W = Dp / 32;
-  ScanIndex ix{list_off, ids, codes, fadd, frescale, ferr, qbits};
+  ScanIndex ix{list_off, ids, codes, fadd, frescale, ferr, qbits, ex_codes, fexadd, fexr, ex_codes ? ex_bits : 0};
   int64_t tot[2] = {0, 0};
 #pragma omp parallel
   {

@@ -201,7 +201,7 @@ class _OracleStages:
         out_i.copy_(torch.from_numpy(ii))
 
 
-def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits):
+def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits, bpd):
     import torch
     import torch.distributed as dist
 
@@ -216,7 +216,7 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits):
     Q = Q[:nq]
     P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
     C, lab = O.kmeans(X, 24, iters=3)
-    ix = O.build(X, C, lab, P, t4)
+    ix = O.build(X, C, lab, P, t4, bits_per_dim=bpd)
     ix.t8 = O.query_scale(64, 3, 7)
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
     d, i = sharded_search(_OracleStages(O, ix, rank, world, owner), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0,
@@ -227,10 +227,11 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,nq,prune,policy,bits", [(2, 40, 1, "balanced", 4), (3, 7, 1, "round_robin", 4),
-                                                        (2, 40, 0, "balanced", 4), (2, 40, 1, "balanced", 8),
-                                                        (2, 40, 1, "balanced", 16), (3, 9, 1, "round_robin", 32)])
-def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits):
+@pytest.mark.parametrize("world,nq,prune,policy,bits,bpd", [
+    (2, 40, 1, "balanced", 4, 1), (3, 7, 1, "round_robin", 4, 1), (2, 40, 0, "balanced", 4, 1),
+    (2, 40, 1, "balanced", 8, 1), (2, 40, 1, "balanced", 16, 1), (3, 9, 1, "round_robin", 32, 1),
+    (2, 40, 1, "balanced", 4, 4), (3, 9, 1, "round_robin", 16, 3)])
+def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits, bpd):
     """The orchestration (queries split for the rotation and coarse quantiser and padded, rotated
     rows and probe rows all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
     merge of the oracle's per-shard searches with the shared seed.  With the prune off every
@@ -241,13 +242,14 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits):
     from neurosamble_b200.sharded import plan
 
     with tempfile.TemporaryDirectory() as td:
-        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy, bits), nprocs=world, join=True)
+        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy, bits, bpd), nprocs=world,
+                 join=True)
         res = [pickle.load(open(os.path.join(td, f"rank{r}.pkl"), "rb")) for r in range(world)]
     X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
     Q = Q[:nq]
     P, t4 = O.make_rotation(64, 3), O.query_scale(64, 3)
     C, lab = O.kmeans(X, 24, iters=3)
-    ix = O.build(X, C, lab, P, t4)
+    ix = O.build(X, C, lab, P, t4, bits_per_dim=bpd)
     ix.t8 = O.query_scale(64, 3, 7)
     slices = plan(nq, 8, 10, 60, 0, 0, world)[1]
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)

@@ -35,7 +35,8 @@ def parse_reference(path):
     exf, o = take(np.float32, n * 2)
     ids, o = take(np.uint32, n)
     return dict(n=n, D=D, K=K, ex=ex, flag=flag, t4=t4, t8=t8, sizes=sizes, kind=kind, P=P.reshape(Dp, Dp),
-                C=C.reshape(K, Dp), codes=codes.reshape(n, W), fac=fac.reshape(n, 3), ids=ids, end=o, size=len(b))
+                C=C.reshape(K, Dp), codes=codes.reshape(n, W), fac=fac.reshape(n, 3), ids=ids, end=o, size=len(b),
+                long_codes=lc.reshape(n, Dp * ex // 8), exf=exf.reshape(n, 2))
 
 
 def _header(n, D, K, ex, kind=0):
@@ -45,7 +46,8 @@ def _header(n, D, K, ex, kind=0):
 
 @pytest.mark.parametrize("blob,msg", [
     (b"\x00" * 12, b"truncated"),
-    (_header(8, 32, 2, 2), b"extra bits"),
+    (_header(8, 32, 2, 9), b"extra bits"),
+    (_header(8, 32, 2, 3), b"truncated"),
     (_header(8, 32, 2, 0, kind=1), b"FHT-Kac"),
     (_header(8, 32, 2, 0) + b"\x00" * 100, b"truncated"),
     (struct.pack("<4Q", 8, 0, 2, 0) + b"\x00" * 64, b"bad header"),
