@@ -231,15 +231,26 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
     return C
 
 
+def list_scan_used(cfg, world=1):
+    """Whether the library's search of the whole batch takes the list scan (its auto rule:
+    popcount modes, padded dim <= 768, nq * nprobe >= 16 * nlist; the sharded search scans by
+    tiles).  The CPU oracle is told the same, so that its sample answers like the full batch."""
+    dp = (cfg["d"] + 31) // 32 * 32
+    kind = cfg.get("scan_kind", 0)
+    able = world == 1 and cfg["query_bits"] in (4, 8) and dp <= 768
+    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 16 * cfg["nlist"]))
+
+
 def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
     """Time the oracle search on a bounded query sample sized to ~budget_s of CPU work."""
+    sk = 2 if list_scan_used(cfg) else 1
     probe = min(len(Q), 200)
     t0 = time.perf_counter()
-    O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"])
+    O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"], scan_kind=sk)
     per_q = (time.perf_counter() - t0) / probe
     n = int(min(len(Q), max(probe, budget_s / max(per_q, 1e-9))))
     t0 = time.perf_counter()
-    d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"])
+    d, i = O.search(oix, Q[:n], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"], scan_kind=sk)
     dt = time.perf_counter() - t0
     return n / dt, n, dt, (d, i)
 
@@ -265,7 +276,8 @@ def run_reference(args, cfg):
     cn = (C * C).sum(1)[None, :]
     lab = np.concatenate([np.argmin(cn - 2.0 * X[a:a + 65536] @ C.T, axis=1)
                           for a in range(0, cfg["n"], 65536)]).astype(np.uint32)
-    oix = O.build(X, C, lab, P, t4)
+    bpd = cfg.get("bits_per_dim", 1)
+    oix = O.build(X, C, lab, P, t4, bits_per_dim=bpd, tex=O.ex_scale(dp, 7, bpd - 1, t4) if bpd > 1 else None)
     oix.t8 = O.query_scale(dp, 7, 7)
     log(f"[reference] build {time.perf_counter() - t:.1f}s, threads={O.threads()}")
     # the same recall rule as our arm: the smallest rerank depth on the ladder whose recall@k
@@ -280,7 +292,8 @@ def run_reference(args, cfg):
                              for a in range(0, ns, 100)])
         R = RERANK_LADDER[-1]
         for cand in RERANK_LADDER:
-            _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand, query_bits=cfg["query_bits"])
+            _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand, query_bits=cfg["query_bits"],
+                              scan_kind=2 if list_scan_used(cfg) else 1)
             recalls[cand] = O.recall(ids, gt)
             if recalls[cand] >= RECALL_TARGET:
                 R = cand
@@ -320,6 +333,11 @@ def _count(n):
 SEARCH_MODES = {4: "QUANT4", 8: "QUANT8", 16: "LUT16", 32: "LUT32"}
 
 
+def _codes(cfg):
+    b = cfg.get("bits_per_dim", 1)
+    return "1-bit codes" if b == 1 else f"{b}-bit ExRaBitQ codes"
+
+
 def metric_name(cfg):
     return (f"queries/sec @ recall@{cfg['k']}>=0.95, {_count(cfg['n'])} x {cfg['d']} IVF-RaBitQ "
             f"(nlist {cfg['nlist']}, nprobe {cfg['nprobe']}, k {cfg['k']})")
@@ -332,15 +350,15 @@ def workload(cfg, R, kmeans):
                              "reverse-complemented, 8% errors 4:2:2 sub:ins:del), synthetic 6-mer pore-model signal, "
                              "2000/1000 windows, seeded random-init signal encoder (d 256) under fp16 autocast, "
                              "mean-pooled per read, L2-normalised, fp16 -> fp32; the read set queried against itself; "
-                             f"IVF-RaBitQ 1-bit codes, {cfg.get('query_bits', 4)}-bit queries; data generated on the "
+                             f"IVF-RaBitQ {_codes(cfg)}, {cfg.get('query_bits', 4)}-bit queries; data generated on the "
                              "device"),
                 "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
                 "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
                 "kmeans": kmeans, "search_mode": SEARCH_MODES[cfg.get("query_bits", 4)]}
     return {"workload": (f"BASELINE config {cfg['config']}: {_count(cfg['n'])} x {cfg['d']} f32, "
                          f"{cfg['centres']}-centre {'anisotropic ' if cfg['aniso'] else ''}mixture sigma "
-                         f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ 1-bit "
-                         f"codes, {cfg.get('query_bits', 4)}-bit queries"
+                         f"{cfg['sigma']}, L2-normalised; {cfg['nq']} perturbed-row queries; IVF-RaBitQ "
+                         f"{_codes(cfg)}, {cfg.get('query_bits', 4)}-bit queries"
                          + ("; data generated on the device" if cfg["device_data"] else "")),
             "n": cfg["n"], "dim": cfg["d"], "nlist": cfg["nlist"], "nprobe": cfg["nprobe"], "k": cfg["k"],
             "rerank": R, "query_batch": cfg["nq"], "l2": "flushed before every step (256 MB write)",
@@ -393,10 +411,12 @@ def run_ours(args, cfg):
     t = time.perf_counter()
     if world > 1:
         from neurosamble_b200.sharded import ShardedIndexIVFRaBitQ
-        index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans)
+        index = ShardedIndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans,
+                                      bits_per_dim=cfg.get("bits_per_dim", 1))
         local_ix = index.local
     else:
-        index = IndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans)
+        index = IndexIVFRaBitQ(cfg["d"], cfg["nlist"], seed=7, device=local, kmeans=args.kmeans,
+                               bits_per_dim=cfg.get("bits_per_dim", 1))
         local_ix = index
     index.train(Xd)
     index.add(Xd)
@@ -407,6 +427,7 @@ def run_ours(args, cfg):
     index.query_bits = cfg["query_bits"]
     if world == 1:
         index.seeded = args.seeded
+        index.scan_kind = args.scan_kind
 
     # ---- recall at the config's rerank depth; raise R along the ladder until recall >= target
     # (exact neighbours of the first gt_sample queries: all of config 2's, 1,000 at configs 4 / 5)
@@ -552,7 +573,8 @@ def run_ours(args, cfg):
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
     seeded = (world > 1 or args.seeded == 1) and cfg["query_bits"] < 16  # LUT modes: one pass, no seed
-    roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded)
+    lists = list_scan_used(cfg, world)
+    roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded, lists)
     scan_share = round(roof["launch_ms"] / ms, 3)
 
     # ---- config 2's batch sweep (B = 1, 64, 1024): device-resident queries, same index
@@ -591,11 +613,15 @@ def run_ours(args, cfg):
     if rank == 0:
         line = {"metric": metric_name(cfg), "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes x 4-bit planes (popc) + f32",
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": ("s8 query codes x u8 code bits (tcgen05 i8) + f32" if lists
+                          else "u32 codes x 4-bit planes (popc) + f32"),
                 "data": data_label(cfg),
                 "config": dict(workload(cfg, R, args.kmeans),
                                parallelism=(f"lists sharded over {world} GPUs (balanced by size^2)" if world > 1
                                             else "1 GPU"),
+                               scan=("list scan (fixed thresholds, tensor-core list GEMM)" if lists
+                                     else "tile scan"),
                                recall_by_rerank=recalls, **{f"recall_at_{k}": recalls.get(R)}),
                 "clocks": clk.summary(),
                 "e2e": {"value": round(e2e, 2), "unit": "queries/s", "h2d_bytes_per_step": nq * cfg["d"] * 4,
@@ -611,9 +637,10 @@ def run_ours(args, cfg):
     return 0
 
 
-def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
-    """Time rbq_scan and rbq_rerank alone on the batch, as the search runs them (seeded: the
-    nearest probe, then the others from the threshold it gives, all-reduced across shards);
+def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded, lists=False):
+    """Time the scan and rbq_rerank alone on the batch, as the search runs them (lists: the bound
+    seeds and the tensor-core list scan; seeded: the nearest probe, then the others from the
+    threshold it gives, all-reduced across shards; else one tile scan);
     algorithmic bytes from the actual probed list sizes: sum n_l (D/8 + 12) for the scan,
     (4D + 8) per candidate the rerank holds."""
     import ctypes
@@ -668,7 +695,19 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
 
     ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
     dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
-    if seeded:  # the search's two phases: the nearest probe, then the rest from the shared seed
+    if lists:  # bound seeds over the leading probed lists, then the list scan from them
+        tau_l = torch.empty(nq, dtype=torch.float32, device=dev)
+
+        def run_lists(stats_t):
+            _lib.call("rbq_bound_seed", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g),
+                      P, P, R, 0, _ptr(tau_l), qb, st)
+            _lib.call("rbq_scan_lists", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g),
+                      P, P, _ptr(tau_l), R, _ptr(ids), _ptr(dist), _ptr(stats_t) if stats_t is not None else None,
+                      qb, st)
+
+        run_lists(stats)
+        scan_ms = timed(lambda: run_lists(None))
+    elif seeded:  # the search's two phases: the nearest probe, then the rest from the shared seed
         ia = torch.empty((nq, R), dtype=torch.int64, device=dev)
         da = torch.empty((nq, R), dtype=torch.float32, device=dev)
         pa, ga = probes[:, :1], g[:, :1]  # strided column views, row stride P
@@ -711,7 +750,12 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded):
     ach = scan_bytes / (scan_ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
             "traffic": traffic, "traffic_source": traffic_src, "peak_kind": kind,
-            "kernel": "rbq scan_kernel (+ key->id epilogue)" + (", 2 launches: seed list + rest" if seeded else ""),
+            "kernel": ("rbq list scan: bound seeds, tcgen05 kind::i8 list GEMM + admission, exact pass per query"
+                       if lists else "rbq scan_kernel (+ key->id epilogue)"
+                       + (", 2 launches: seed list + rest" if seeded else "")),
+            "accounting": ("algorithmic bytes per query summed over the batch; the list scan reads each list once "
+                           "for up to 128 of its queries, so the fraction can exceed 1" if lists else
+                           "algorithmic bytes per query summed over the batch"),
             "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
             "launch_ms": round(scan_ms, 4), "prune_admitted_fraction": round(admitted / max(1, scanned), 4)}
     ach_r = rr_bytes / (rr_ms / 1000.0) / 1e9
@@ -735,6 +779,8 @@ def cpu_baseline(ix, X, Q, cfg, R, gpu_result=None):
     oix = O.OracleIndex(cfg["d"], info.padded_dim, cfg["nlist"], ex["list_off"], ex["ids"], ex["codes"], ex["fadd"],
                         ex["frescale"], ex["ferr"], Cr, ix.rotation(), ix.query_scale, X)
     oix.t8 = O.query_scale(info.padded_dim, int(info.seed), 7)
+    if info.bits_per_dim > 1:
+        oix.set_ex(ex["ex_bits"], ex["ex_codes"], ex["fexadd"], ex["fexr"], ex["ex_scale"])
     qps, n_s, dt, (od, oi) = cpu_search_timed(O, oix, Q, cfg, R, budget_s=15.0)
     out = {"value": round(qps, 2), "unit": "queries/s", "cores": O.threads(), "kind": "port",
            "sample": f"{n_s} of {cfg['nq']} queries ({dt:.1f}s), same index bytes and parameters"}
@@ -781,6 +827,10 @@ def main():
     ap.add_argument("--query-bits", type=int, default=4, choices=sorted(SEARCH_MODES),
                     help="search mode of both arms: 4 (QUANT4, the reference CLI's default), 8 (QUANT8), "
                          "16 (LUT16) or 32 (LUT32)")
+    ap.add_argument("--bits", type=int, default=1, choices=range(1, 10),
+                    help="code bits per dimension of both arms (1: RaBitQ; 2..9: ExRaBitQ extra bits)")
+    ap.add_argument("--scan-kind", type=int, default=0, choices=[0, 1, 2],
+                    help="0: the library's choice (the list scan for large batches), 1: the tile scan, 2: the list scan")
     ap.add_argument("--nlist", type=int, default=0,
                     help="list count override (reduced-size cases of a configuration's shape; mixtures keep "
                          "one centre per list)")
@@ -794,6 +844,8 @@ def main():
         args.warmup = 3
     cfg = dict(CONFIGS[args.config])
     cfg["query_bits"] = args.query_bits
+    cfg["bits_per_dim"] = args.bits
+    cfg["scan_kind"] = args.scan_kind
     if args.n:
         cfg["n"] = args.n
     if args.nq:

@@ -118,6 +118,19 @@ typedef struct {
                          /* waits for the previous replay's copy-out).  Like every call on one  */
                          /* index, they must come from one host thread at a time.               */
                          /* 0 (default): launch the kernels one by one.                         */
+  int32_t scan_kind;     /* the list scan's schedule.  1: the tile scan (each query walks its   */
+                         /* probed lists in tiles of rbq_scan_tile() vectors, the threshold     */
+                         /* tightening between tiles).  2: the list scan: every query's        */
+                         /* threshold is fixed at its bound seed over the leading probed lists  */
+                         /* holding >= R vectors, and each probed list is scored against all    */
+                         /* the batch's queries that probe it in one int8 GEMM on the tensor    */
+                         /* cores (4- or 8-bit query codes x code bits, exactly the popcount    */
+                         /* estimator's integers, as the reference scans one (list, query) pair */
+                         /* per block, searcher_gpu_quantize_query.cu:172-300); the admitted    */
+                         /* vectors' exact distances then rank per query.  Needs QUANT4 /       */
+                         /* QUANT8, the prune on and a padded dim <= 768.  0 (default, auto):   */
+                         /* the list scan when nq * n_probes >= 16 * n_lists (the lists are     */
+                         /* shared by many queries), else the tile scan.                        */
 } rbq_search_params_t;
 
 typedef struct {
@@ -271,6 +284,19 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
              int32_t probe_stride, const float* tau0_dev, const int64_t* init_ids_dev, const float* init_dist_dev, int32_t R,
              int32_t prune, int32_t slices, int32_t cand_cap, int64_t* cand_ids_dev, float* cand_dist_dev,
              uint64_t* stats_dev, int32_t query_bits, void* stream);
+/* The list scan with fixed thresholds (rbq_search_params_t.scan_kind = 2) as a stage: every query
+ * admits a vector of its probed lists (this shard's) while the vector's lower bound is below
+ * tau0_dev[q] (no tightening), keeps the admitted vectors whose distance is <= tau0_dev[q], and
+ * returns its R smallest (distance, id) candidates, ascending (id -1 / +inf past the last).
+ * Each probed list is scored against all the queries that probe it by an int8 GEMM on the
+ * tensor cores (tcgen05 kind::i8: query codes x code bits = the popcount estimator's integers);
+ * the prune is always on.  query_bits 4 or 8 (the planes' width); padded dim <= 768.  stats_dev
+ * (optional): += (vectors scanned, vectors admitted).  Replaces the reference's pair-per-block
+ * scan (computeInnerProductsWithBitwiseBlockSort, searcher_gpu_quantize_query.cu:172-626). */
+int rbq_scan_lists(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                   const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                   int32_t probe_stride, const float* tau0_dev, int32_t R, int64_t* cand_ids_dev, float* cand_dist_dev,
+                   uint64_t* stats_dev, int32_t query_bits, void* stream);
 /* Bound seed per query: the R-th smallest RaBitQ upper bound est + f_err * sqrt(g) over the
  * query's leading owned probed lists that hold >= R vectors (+inf if they hold fewer), the
  * threshold a pruning scan starts from.  With nprobe = 1 it is the nearest list's seed that

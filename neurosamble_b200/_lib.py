@@ -28,7 +28,7 @@ class SearchParams(ctypes.Structure):
     _fields_ = [("n_probes", ctypes.c_int32), ("k", ctypes.c_int32), ("rerank", ctypes.c_int32),
                 ("prune", ctypes.c_int32), ("probe_split", ctypes.c_int32), ("cand_cap", ctypes.c_int32),
                 ("coarse_margin", ctypes.c_int32), ("seeded", ctypes.c_int32), ("query_bits", ctypes.c_int32),
-                ("graph", ctypes.c_int32)]
+                ("graph", ctypes.c_int32), ("scan_kind", ctypes.c_int32)]
 
 
 class IndexInfo(ctypes.Structure):
@@ -74,6 +74,7 @@ SIGNATURES = {
     "rbq_get_centroids": [_P, _P, _P],
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
     "rbq_export_ex_lists": [_P, _P, _P, _P],
+    "rbq_scan_lists": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _P, _P, _P, _I32, _P],
     "rbq_get_list_owners": [_P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],
     "rbq_query_prep": [_P, _P, _I64, _P, _P, _P, _I32, _P],

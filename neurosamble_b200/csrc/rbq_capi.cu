@@ -749,7 +749,33 @@ struct SearchPlan {
   int prune;
   int qbits;    // search mode: 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)
   bool seeded;  // two-phase scan (search_scan)
+  bool lists;   // list scan on the tensor cores with a fixed per-query threshold
+  int lcap;     // its candidate row per query
 };
+
+// The list scan (fixed threshold, tensor cores) serves batches whose probed lists are shared by
+// at least this many queries on average; smaller batches take the tile scan.
+constexpr int64_t kListScanMinPairsPerList = 16;
+
+// Whether a search takes the list scan: scan_kind 2 asks for it, 0 (auto) takes it for popcount
+// modes with the prune on when nq * P >= kListScanMinPairsPerList * K; 1 is the tile scan.
+bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K)
+{
+  RBQ_CHECK(scan_kind >= 0 && scan_kind <= 2, RBQ_ERR_INVALID,
+            "scan_kind must be 0 (auto), 1 (tile scan) or 2 (list scan)");
+  const bool able = (qbits == 4 || qbits == 8) && prune && list_scan_tc_supported(dp);
+  RBQ_CHECK(scan_kind != 2 || able, RBQ_ERR_INVALID,
+            "list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768");
+  if (scan_kind == 2) return true;
+  return scan_kind == 0 && able && nq * (int64_t)P >= kListScanMinPairsPerList * K;
+}
+
+int list_scan_cap(int R)
+{
+  int c = 2048;
+  while (c < 2 * R) c <<= 1;
+  return c;
+}
 
 // Search mode of query_bits (0 means 4): 4 / 8 = QUANT4 / QUANT8 (popcount estimator over 4- or
 // 8-bit query codes), 16 / 32 = LUT16 / LUT32 (fp16 / fp32 tables of the float query).
@@ -811,6 +837,12 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   sp.prune = p.prune ? 1 : 0;
   sp.qbits = query_bits_of(p.query_bits);
   sp.seeded = sp.qbits < 16 && (p.seeded < 0 ? sp.slices > 1 : p.seeded > 0);  // no bound seed in LUT modes
+  sp.lists = use_list_scan(p.scan_kind, sp.qbits, sp.prune, ix.Dp, nq, sp.P, ix.K);
+  sp.lcap = list_scan_cap(sp.R);
+  if (sp.lists) {
+    sp.slices = 1;
+    sp.seeded = false;
+  }
   return sp;
 }
 
@@ -859,13 +891,117 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
 // every slice starts from the bound seed of the query's nearest probe (computed first, by a
 // seed-only launch over that list) instead of finding its own: split slices then prune from
 // their first vector.
+// Scratch of a list scan over nq queries with P probe columns.
+struct ListScanScratch {
+  int8_t* qcodes;
+  int32_t *list_start, *item_start, *cursor, *pair_q, *cand_cnt;
+  float* pair_g;
+  unsigned long long* cand;
+};
+
+ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int P, int cap)
+{
+  ListScanScratch w;
+  w.qcodes = sc.get<int8_t>((size_t)nq * ix.Dp);
+  w.list_start = sc.get<int32_t>((size_t)ix.K + 1);
+  w.item_start = sc.get<int32_t>((size_t)ix.K + 1);
+  w.cursor = sc.get<int32_t>((size_t)ix.K + 1);
+  w.pair_q = sc.get<int32_t>((size_t)nq * P);
+  w.pair_g = sc.get<float>((size_t)nq * P);
+  w.cand_cnt = sc.get<int32_t>((size_t)nq);
+  w.cand = sc.get<unsigned long long>((size_t)nq * cap);
+  return w;
+}
+
+// The list scan: fixed thresholds tau0 [nq] (every query admits while low < tau0), the
+// tensor-core pass over all (list, query) pairs, the exact pass per query, and the
+// fixed-threshold tile scan for queries whose candidate row overflowed.  out_keys [nq, R].
+void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbits, const float* delta,
+               const float* k1, int64_t nq, const int32_t* probes, const float* g, int nprobe, int pstride,
+               const float* tau0, int R, int cap, const ListScanScratch& w, unsigned long long* out_keys,
+               uint64_t* stats, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  launch_planes_to_codes(planes, nq, ix.W, qbits, w.qcodes, s);
+  launch_list_pairs(probes, g, nq, nprobe, pstride, ix.owner, ix.shard_rank, ix.K, w.list_start, w.item_start,
+                    w.cursor, w.pair_q, w.pair_g, s);
+  RBQ_CUDA(cudaMemsetAsync(w.cand_cnt, 0, (size_t)nq * sizeof(int32_t), s));
+  ListScanArgs la;
+  la.list_off = ix.list_off;
+  la.codes = ix.codes;
+  la.fadd = ix.fadd;
+  la.frescale = ix.frescale;
+  la.ferr = ix.ferr;
+  la.W = ix.W;
+  la.Dp = ix.Dp;
+  la.qcodes = w.qcodes;
+  la.delta = delta;
+  la.k1 = k1;
+  la.tau0 = tau0;
+  la.pair_q = w.pair_q;
+  la.pair_g = w.pair_g;
+  la.list_start = w.list_start;
+  la.item_start = w.item_start;
+  la.K = ix.K;
+  la.cand = w.cand;
+  la.cand_cnt = w.cand_cnt;
+  la.cap = cap;
+  la.stats = reinterpret_cast<unsigned long long*>(stats);
+  la.err = ix.dev_err;
+  // at most one partial item per list beyond nq * nprobe / 128 full ones
+  const int64_t max_items = ix.K + (nq * nprobe) / kListScanRows + 1;
+  launch_list_scan_tc(la, max_items, s);
+  ExactArgs ea;
+  ea.codes = ix.codes;
+  ea.fadd = ix.fadd;
+  ea.frescale = ix.frescale;
+  ea.ids = ix.ids;
+  if (ix.ex_bits > 0) {
+    ea.ex_codes = ix.ex_codes;
+    ea.fexadd = ix.fexadd;
+    ea.fexr = ix.fexr;
+    ea.ex_bits = ix.ex_bits;
+  }
+  ea.W = ix.W;
+  ea.Qr = Qr;
+  ea.k1 = k1;
+  ea.tau0 = tau0;
+  ea.cand = w.cand;
+  ea.cand_cnt = w.cand_cnt;
+  ea.cap = cap;
+  ea.R = R;
+  ea.nq = nq;
+  ea.out_keys = out_keys;
+  launch_exact_topr(ea, s);
+  // rows that overflowed: the tile scan with the same fixed thresholds (its blocks for the other
+  // queries return at once; the list scan already counted every admitted vector)
+  ScanArgs fa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, nprobe, R,
+                                std::max(next_pow2(1024), next_pow2(R + kScanTile)), 1, 1, out_keys, nullptr, qbits);
+  fa.pstride = pstride;
+  fa.tau0 = tau0;
+  fa.fixed_tau = 1;
+  fa.over_cnt = w.cand_cnt;
+  fa.over_cap = cap;
+  launch_scan(fa, s);
+}
+
 void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const uint32_t* planes, const float* delta,
                  const float* k1, int64_t nq, const int32_t* probes, const float* g, float* tau_a,
                  unsigned long long* keys_s, unsigned long long* keys, uint64_t* stats, int32_t* qorder_buf,
-                 cudaStream_t s)
+                 const ListScanScratch* lw, cudaStream_t s)
 {
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
                                 keys_s, stats, sp.qbits);
+  if (sp.lists) {  // thresholds: the bound seed over the leading probed lists holding >= R vectors
+    ScanArgs a0 = sa;
+    a0.slices = 1;
+    a0.stats = nullptr;
+    a0.tau_out = tau_a;
+    launch_scan(a0, s);
+    list_scan(ix, Qr, planes, sp.qbits, delta, k1, nq, probes, g, sp.P, sp.P, tau_a, sp.R, sp.lcap, *lw, keys,
+              stats, s);
+    return;
+  }
   if (qorder_buf && nq >= kQueryOrderMinBatch) {  // [K + 2] counts, then [nq] order
     launch_query_order(probes, nq, sp.P, ix.K, qorder_buf, qorder_buf + ix.K + 2, s);
     sa.qorder = qorder_buf + ix.K + 2;
@@ -898,7 +1034,9 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   // The scan and rerank run over chunks bounded by the candidate keys (1 GiB); inside one, the
   // front end (rotation, coarse scores, top-m, refine) runs over sub-chunks bounded by the
   // [sub-chunk, K] score matrix (512 MiB), so a large K does not cut the scan into small grids.
-  const int64_t by_keys = std::max<int64_t>(1, (1ll << 30) / ((int64_t)sp.slices * sp.R * 8));
+  // (the list scan's candidate rows: 2 GiB)
+  int64_t by_keys = std::max<int64_t>(1, (1ll << 30) / ((int64_t)sp.slices * sp.R * 8));
+  if (sp.lists) by_keys = std::min<int64_t>(by_keys, std::max<int64_t>(1, (1ll << 31) / ((int64_t)sp.lcap * 8)));
   const int64_t chunk = std::min<int64_t>(nq, std::min<int64_t>(by_keys, 65535ll * 64));
   Scratch sc(s);
   float* Qr_buf = Qr_pre ? nullptr : sc.get<float>((size_t)chunk * ix.Dp);
@@ -914,8 +1052,10 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   float* k1 = sc.get<float>(chunk);
   unsigned long long* keys_s = sc.get<unsigned long long>((size_t)chunk * sp.slices * sp.R);
   unsigned long long* keys = sp.slices > 1 ? sc.get<unsigned long long>((size_t)chunk * sp.R) : keys_s;
-  float* tau_a = sp.seeded ? sc.get<float>((size_t)chunk) : nullptr;
+  float* tau_a = sp.seeded || sp.lists ? sc.get<float>((size_t)chunk) : nullptr;
   int32_t* qorder = chunk >= kQueryOrderMinBatch ? sc.get<int32_t>((size_t)ix.K + 2 + chunk) : nullptr;
+  ListScanScratch lw{};
+  if (sp.lists) lw = list_scan_scratch(sc, ix, chunk, sp.P, sp.lcap);
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
@@ -931,7 +1071,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
     launch_query_prep(Qr, cn, ix.Dp, qt, pb, planes, delta, k1, s);
     {
       Range r("rbq scan");
-      search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, qorder, s);
+      search_scan(ix, sp, Qr, planes, delta, k1, cn, probes, g, tau_a, keys_s, keys, stats, qorder, &lw, s);
     }
     Range r("rbq rerank / result");
     if (params.rerank > 0)
@@ -1263,6 +1403,8 @@ void rbq_search_params_default(rbq_search_params_t* p)
   p->cand_cap = 0;
   p->coarse_margin = 0;
   p->seeded = -1;
+  p->graph = 0;
+  p->scan_kind = 0;
 }
 
 int rbq_make_rotation(int32_t padded_dim, uint64_t seed, float* P_host)
@@ -2135,6 +2277,36 @@ int rbq_scan(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev
     launch_scan(sa, s);
     if (slices > 1) launch_merge_keys(ks, nq, slices, R, k2, s);
     launch_keys_to_ids(k2, nq * R, cand_ids_dev, cand_dist_dev, s);
+  });
+}
+
+int rbq_scan_lists(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                   const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                   int32_t probe_stride, const float* tau0_dev, int32_t R, int64_t* cand_ids_dev, float* cand_dist_dev,
+                   uint64_t* stats_dev, int32_t query_bits, void* stream)
+{
+  return guarded([&] {
+    Range nvtx_range("rbq_scan_lists");
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && tau0_dev &&
+                          cand_ids_dev && cand_dist_dev),
+              RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && (probe_stride == 0 || probe_stride >= nprobe), RBQ_ERR_INVALID,
+              "bad scan parameters");
+    Index& ix = index->ix;
+    const int qb = query_bits_of(query_bits);
+    RBQ_CHECK((qb == 4 || qb == 8) && list_scan_tc_supported(ix.Dp), RBQ_ERR_INVALID,
+              "list scan: needs QUANT4 / QUANT8 planes and a padded dim <= 768");
+    if (nq == 0) return;
+    DeviceGuard dg(ix.device);
+    cudaStream_t s = as_stream(stream);
+    const int cap = list_scan_cap(R);
+    Scratch sc(s);
+    unsigned long long* keys = sc.get<unsigned long long>((size_t)nq * R);
+    const ListScanScratch w = list_scan_scratch(sc, ix, nq, nprobe, cap);
+    list_scan(ix, Qr_dev, planes_dev, qb, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe,
+              probe_stride > 0 ? probe_stride : nprobe, tau0_dev, R, cap, w, keys, stats_dev, s);
+    launch_keys_to_ids(keys, nq * R, cand_ids_dev, cand_dist_dev, s);
   });
 }
 

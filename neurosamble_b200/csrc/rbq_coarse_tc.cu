@@ -586,6 +586,231 @@ __global__ void __launch_bounds__(kFtThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// List scan on the tensor cores.  One CTA (256 threads) per work item: up to 128 queries
+// probing one list (the accumulator's 128 rows = TMEM lanes) against all of the list's vectors,
+// in tiles of 128 vectors (accumulator columns).  Operands are int8 in shared memory, K-major
+// with the 128-byte swizzle, one 128-byte chunk of dimensions per [rows x 128 B] region: A holds
+// the queries' codes (copied once), B the tile's code bits expanded to bytes 0 / 1 (rewritten
+// per tile).  One thread issues the kind::i8 MMAs (K = 32 bytes each) and commits them to an
+// mbarrier; then the 8 warps read the int32 accumulator (warp w: TMEM lanes 32 (w % 4).., column
+// half w / 4), form the estimate and its lower bound from the integer exactly as the popcount
+// scan does, and append the admitted vectors (low < tau0[q]) to their query's candidate row.
+// The wait on the MMAs is bounded: on time-out the kernel records an error code, waits once more
+// (bounded) for the MMAs, frees its TMEM and returns.
+// ---------------------------------------------------------------------------------------
+constexpr int kLsM = kListScanRows;  // queries per work item
+constexpr int kLsN = 128;            // vectors per tile
+constexpr int kLsThreads = 256;
+constexpr int kLsMaxChunks = 6;      // padded dimension <= 768 (A + B = 192 KB)
+// kind::i8: D s32 (2), A s8 (1), B s8 (1), both K-major, N = 128, M = 128.
+constexpr uint32_t kLsIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLsN >> 3) << 17) |
+                              ((uint32_t)(kLsM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t acc)
+{
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(dtmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void tc_ld32_u(uint32_t taddr, uint32_t (&r)[32])
+{
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The 32 code bits of one word (dim 32w + j -> bit 31 - j) as 32 bytes 0 / 1, byte j = dim 32w + j:
+// after the bit reversal bit j is dim j, and a multiply spreads each nibble's 4 bits into the low
+// bits of 4 bytes (the products do not overlap, so nothing carries).
+__device__ __forceinline__ void expand_word(uint32_t c, uint32_t (&o)[8])
+{
+  const uint32_t r = __brev(c);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = (((r >> (4 * i)) & 0xFu) * 0x00204081u) & 0x01010101u;
+}
+
+__global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScanArgs a)
+{
+  extern __shared__ unsigned char ls_smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(ls_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int Kc = (a.Dp + 127) >> 7;
+  unsigned char* As = base;                    // [Kc][kLsM rows][128 B]
+  unsigned char* Bs = base + Kc * kLsM * 128;  // [Kc][kLsN rows][128 B]
+  __shared__ int s_q[kLsM];
+  __shared__ float s_g[kLsM], s_sg[kLsM], s_dl[kLsM], s_k1[kLsM], s_tau[kLsM];
+  __shared__ uint32_t s_slot[kLsN];
+  __shared__ float s_fa[kLsN], s_fr[kLsN], s_fe[kLsN];
+  __shared__ __align__(8) unsigned long long s_bar;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail, s_l, s_p0, s_rows;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {  // work item -> list (the last list whose first item is <= blockIdx.x), pairs
+    const int b = blockIdx.x;
+    int l = -1;
+    if (b < a.item_start[a.K]) {
+      int lo = 0, hi = a.K - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.item_start[mid] <= b)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      l = lo;
+      const int p0 = a.list_start[l] + (b - a.item_start[l]) * kLsM;
+      s_p0 = p0;
+      s_rows = min(kLsM, a.list_start[l + 1] - p0);
+    }
+    s_l = l;
+  }
+  __syncthreads();
+  const int l = s_l;
+  if (l < 0) return;
+  const int rows = s_rows, p0 = s_p0;
+  const int64_t lb = a.list_off[l];
+  const int nl = (int)(a.list_off[l + 1] - lb);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"((uint32_t)kLsN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(smem_u32(&s_bar), 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int r = tid; r < kLsM; r += kLsThreads) {
+    if (r < rows) {
+      const int q = a.pair_q[p0 + r];
+      const float g = a.pair_g[p0 + r];
+      s_q[r] = q;
+      s_g[r] = g;
+      s_sg[r] = sqrtf(g);
+      s_dl[r] = a.delta[q];
+      s_k1[r] = a.k1[q];
+      s_tau[r] = a.tau0[q];
+    } else {
+      s_q[r] = 0;
+      s_g[r] = s_sg[r] = s_dl[r] = s_k1[r] = 0.0f;
+      s_tau[r] = -__int_as_float(0x7f800000);  // admits nothing
+    }
+  }
+  __syncthreads();
+  // A: the queries' codes; rows past `rows` and bytes past Dp are zero.
+  for (int i = tid; i < kLsM * Kc * 8; i += kLsThreads) {
+    const int r = i / (Kc * 8), u = i - r * (Kc * 8);
+    const int byte = u << 4;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows && byte < a.Dp) v = __ldg(reinterpret_cast<const uint4*>(a.qcodes + (size_t)s_q[r] * a.Dp + byte));
+    *reinterpret_cast<uint4*>(As + (u >> 3) * (kLsM * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4)) = v;
+  }
+  // B: the padding past Dp in the last chunk stays zero for every tile.
+  if (a.Dp < Kc * 128)
+    for (int i = tid; i < kLsN * 8; i += kLsThreads) {
+      const int v = i >> 3, u = i & 7;
+      if ((Kc - 1) * 128 + (u << 4) >= a.Dp)
+        *reinterpret_cast<uint4*>(Bs + (Kc - 1) * (kLsN * 128) + v * 128 + ((u ^ (v & 7)) << 4)) =
+            make_uint4(0u, 0u, 0u, 0u);
+    }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int row = quarter * 32 + lane;
+  const bool row_ok = row < rows;
+  const int q = s_q[row];
+  const float g = s_g[row], sg = s_sg[row], dl = s_dl[row], kk = s_k1[row], tau = s_tau[row];
+  const unsigned long long gbits = (unsigned long long)__float_as_uint(g) << 32;
+  unsigned long long n_admit = 0;
+  int tile = 0;
+  for (int t0 = 0; t0 < nl; t0 += kLsN, ++tile) {
+    const int tn = min(kLsN, nl - t0);
+    for (int i = tid; i < kLsN * a.W; i += kLsThreads) {
+      const int v = i / a.W, w = i - v * a.W;
+      uint32_t o[8];
+      expand_word(v < tn ? __ldg(a.codes + (lb + t0 + v) * a.W + w) : 0u, o);
+      const int byte = w << 5, u0 = (byte & 127) >> 4;
+      unsigned char* rowp = Bs + (byte >> 7) * (kLsN * 128) + v * 128;
+      *reinterpret_cast<uint4*>(rowp + ((u0 ^ (v & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ (v & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+    for (int v = tid; v < tn; v += kLsThreads) {
+      const int64_t slot = lb + t0 + v;
+      s_slot[v] = (uint32_t)slot;
+      s_fa[v] = __ldg(a.fadd + slot);
+      s_fr[v] = __ldg(a.frescale + slot);
+      s_fe[v] = __ldg(a.ferr + slot);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_addr = smem_u32(As), b_addr = smem_u32(Bs);
+      for (int c = 0; c < Kc; ++c)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)  // 32 int8 values (32 bytes) per MMA
+          tc_mma_i8(tmem, sw128_desc(a_addr + c * (kLsM * 128) + ks * 32),
+                    sw128_desc(b_addr + c * (kLsN * 128) + ks * 32), kLsIdesc, (c > 0 || ks > 0) ? 1u : 0u);
+      tc_commit(smem_u32(&s_bar));
+      if (!mbar_wait(smem_u32(&s_bar), (uint32_t)(tile & 1))) {
+        s_fail = 1;
+        atomicExch(a.err, 4);
+      }
+    }
+    __syncthreads();
+    if (s_fail) break;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int col0 = half * (kLsN / 2) + j * 32;
+      uint32_t acc[32];
+      tc_ld32_u(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, acc);
+      if (row_ok && col0 < tn) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = col0 + i;
+          const float ip = __fmul_rn((float)(int32_t)acc[i], dl);
+          const float base_d = __fadd_rn(s_fa[col], g);
+          const float est = __fadd_rn(base_d, __fmul_rn(s_fr[col], __fadd_rn(ip, kk)));
+          const float low = __fsub_rn(est, __fmul_rn(s_fe[col], sg));
+          if (col < tn && low < tau) {
+            ++n_admit;
+            const int pos = atomicAdd(a.cand_cnt + q, 1);
+            if (pos < a.cap) a.cand[(size_t)q * a.cap + pos] = gbits | s_slot[col];
+          }
+        }
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+  }
+  if (s_fail && tid == 0) mbar_wait(smem_u32(&s_bar), (uint32_t)(tile & 1));
+  if (a.stats) {
+    unsigned long long s1 = n_admit;
+    for (int off = 16; off; off >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+    if (lane == 0 && s1) atomicAdd(a.stats + 1, s1);
+    if (tid == 0) atomicAdd(a.stats + 0, (unsigned long long)rows * (unsigned long long)nl);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kLsN));
+  }
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 {
@@ -675,6 +900,21 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
   // one CTA per (128 queries, 256-centroid chunk)
   const dim3 grid((unsigned)ceil_div(nq, kTcM), (unsigned)std::min<int64_t>(ceil_div(K, kTcN), 65535));
   coarse_tc_kernel<<<grid, kTcThreads, smem, s>>>(tmQ, tmC, (int)nq, cn2, K, dp, S, err);
+  RBQ_LAUNCHED();
+}
+
+bool list_scan_tc_supported(int dp) { return dp % 32 == 0 && dp >= 32 && dp <= kLsMaxChunks * 128; }
+
+void launch_list_scan_tc(const ListScanArgs& a, int64_t max_items, cudaStream_t s)
+{
+  if (max_items <= 0) return;
+  RBQ_CHECK(list_scan_tc_supported(a.Dp), RBQ_ERR_INVALID, "list scan: padded dim must be a multiple of 32, <= 768");
+  RBQ_CHECK(max_items <= 0x7fffffff, RBQ_ERR_INVALID, "list scan: too many work items");
+  const int Kc = (a.Dp + 127) / 128;
+  // at least a quarter of the shared memory per CTA: at most 4 CTAs (4 x 128 TMEM columns) per SM
+  const size_t smem = std::max<size_t>((size_t)Kc * (kLsM + kLsN) * 128 + 1024, 56 * 1024);
+  RBQ_CUDA(cudaFuncSetAttribute(list_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  list_scan_tc_kernel<<<(unsigned)max_items, kLsThreads, smem, s>>>(a);
   RBQ_LAUNCHED();
 }
 

@@ -274,7 +274,79 @@ struct ScanArgs {
   // Optional [nq] visiting order: block i scans query qorder[i / slices] (a permutation of
   // 0..nq-1).  Only the order in which queries run changes; every query's result is its own.
   const int32_t* qorder = nullptr;
+  // Fixed-threshold scan (the list scan's semantics): the prune admits a vector while
+  // low < tau0[q] (+inf when tau0 is null), however far the kept candidates have tightened the
+  // threshold; only the keep test and the buffer cuts use the running threshold.
+  int fixed_tau = 0;
+  // Optional: only queries whose admitted count over_cnt[q] exceeds over_cap run (the list
+  // scan's candidate rows that overflowed); the other blocks return at once.
+  const int32_t* over_cnt = nullptr;
+  int over_cap = 0;
 };
+// ---------------------------------------------------------------------------------------
+// List scan on the tensor cores (fixed per-query threshold).  For every (list, query) pair of
+// the batch: acc = <query code, vector bits> as an int8 GEMM on tcgen05 (kind::i8; exactly the
+// popcount estimator's integer), est = (f_add + g) + f_rescale * (acc * delta + k1),
+// low = est - f_err * sqrt(g); a vector with low < tau0[q] is appended to its query's candidate
+// row: cand[q * cap + i] = (float bits of g) << 32 | slot.  cand_cnt[q] counts every admitted
+// vector, also past cap (an overflowed row).
+// ---------------------------------------------------------------------------------------
+struct ListScanArgs {
+  const int64_t* list_off;
+  const uint32_t* codes;
+  const float* fadd;
+  const float* frescale;
+  const float* ferr;
+  int W, Dp;
+  const int8_t* qcodes;  // [nq, Dp] query codes
+  const float* delta;
+  const float* k1;
+  const float* tau0;          // [nq] fixed thresholds
+  const int32_t* pair_q;      // (list, query) pairs in list order: the query
+  const float* pair_g;        //   and its coarse distance to the list
+  const int32_t* list_start;  // [K + 1] first pair of list l
+  const int32_t* item_start;  // [K + 1] first work item of list l (128 pairs per item)
+  int K;
+  unsigned long long* cand;  // [nq, cap]
+  int32_t* cand_cnt;         // [nq]
+  int cap;
+  unsigned long long* stats;  // optional [2]: scanned, admitted
+  int* err;
+};
+bool list_scan_tc_supported(int dp);
+constexpr int kListScanRows = 128;  // (list, query) pairs per work item
+void launch_list_scan_tc(const ListScanArgs& a, int64_t max_items, cudaStream_t s);
+// The work plan of a list scan: codes of the queries ([nq, Dp] int8, from planes [nq, QB, W]),
+// the (list, query) pairs of this shard's probed lists bucketed by list, and the work items.
+void launch_planes_to_codes(const uint32_t* planes, int64_t nq, int W, int QB, int8_t* codes, cudaStream_t s);
+void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int nprobe, int pstride,
+                       const int32_t* owner, int rank, int K, int32_t* list_start, int32_t* item_start,
+                       int32_t* cursor, int32_t* pair_q, float* pair_g, cudaStream_t s);
+// Exact pass of the list scan: per query the candidates of its row (1-bit exact distance, or
+// the extra-bit distance), kept while dist <= tau0[q], cut to the R smallest keys -> out_keys
+// [nq, R].  Rows that overflowed (cand_cnt > cap) are left to the fixed-threshold tile scan.
+struct ExactArgs {
+  const uint32_t* codes;
+  const float* fadd;
+  const float* frescale;
+  const uint32_t* ids;
+  const uint32_t* ex_codes = nullptr;
+  const float* fexadd = nullptr;
+  const float* fexr = nullptr;
+  int ex_bits = 0;
+  int W;
+  const float* Qr;  // [nq, Dp]
+  const float* k1;
+  const float* tau0;
+  const unsigned long long* cand;
+  const int32_t* cand_cnt;
+  int cap;
+  int R;
+  int64_t nq;
+  unsigned long long* out_keys;
+};
+void launch_exact_topr(const ExactArgs& a, cudaStream_t s);
+
 // qorder[0..nq) = the queries sorted by their nearest probe probes[q * pstride] (ascending list id;
 // queries without probes last), so that queries searching the same region of the index run at
 // the same time and share its lists in L2.  counts: scratch of K + 2 ints.  The order inside

@@ -1083,6 +1083,9 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const int slice = blockIdx.x - (int)(qi * a.slices);
   const int64_t q = a.qorder ? (int64_t)a.qorder[qi] : qi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (a.over_cnt && a.over_cnt[q] <= a.over_cap) return;  // only the list scan's overflowed rows
+  // fixed-threshold scan: admission against tau0[q] throughout
+  const float tau_fix = a.tau0 ? a.tau0[q] : __int_as_float(0x7f800000);
 
   if constexpr (kLut) {
     // query tables (precomputeAllLUTs / precomputeAllLUTs_fp16_simple, searcher_gpu.cu:65-108,
@@ -1196,7 +1199,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   // vectors (the RaBitQ error bound: R of them are that close), instead of admitting its first
   // tile whole.  The bounds stream through the key buffer in tiles, cut to the R smallest
   // whenever the buffer would overflow.
-  if (!kLut && a.prune && isinf(s_tau) && s_count == 0 && total >= a.R) {
+  if (!kLut && a.prune && !a.fixed_tau && isinf(s_tau) && s_count == 0 && total >= a.R) {
     int nb = 0;
     for (int i = 1; i <= nl && nb < a.R; ++i) nb = pre[i];
     int c = 0, cnt = 0;
@@ -1238,6 +1241,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
 
   for (int t0 = 0; t0 < total; t0 += kScanTile) {
     const float tau = s_tau;
+    const float tau_adm = a.fixed_tau ? tau_fix : tau;
 #pragma unroll
     for (int u = 0; u < kScanVpt; ++u) {
       const int f = t0 + u * kScanThreads + tid;
@@ -1268,7 +1272,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
             }
           } else {  // extra bits: the table estimate's error bound admits (sbase = g, sfr = ip)
             const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
-            if (!a.prune || low < tau) {
+            if (!a.prune || low < tau_adm) {
               ++n_admit;
               surv = true;
               sslot = slot;
@@ -1283,7 +1287,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
           const float ip = __fmul_rn((float)acc, delta);
           const float est = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(ip, k1)));
           const float low = __fsub_rn(est, __fmul_rn(__ldg(a.ferr + slot), sqc));
-          if (!a.prune || low < tau) {
+          if (!a.prune || low < tau_adm) {
             ++n_admit;
             surv = true;
             sslot = slot;
@@ -1402,6 +1406,8 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
   RBQ_CHECK(a.qbits == 4 || a.qbits == 8 || a.qbits == 16 || a.qbits == 32, RBQ_ERR_INVALID,
             "scan: query bits must be 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)");
   RBQ_CHECK(!(a.tau_out && a.qbits >= 16), RBQ_ERR_INVALID, "scan: the LUT modes have no bound seed");
+  RBQ_CHECK(!a.fixed_tau || (a.slices == 1 && !a.init_keys && !a.tau_out), RBQ_ERR_INVALID,
+            "scan: a fixed-threshold scan takes one slice and no initial candidates");
   RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
             "scan: more than 2^31 vectors on one shard");
   switch (a.W) {
@@ -1481,6 +1487,196 @@ void launch_query_order(const int32_t* probes, int64_t nq, int pstride, int K, i
   exclusive_scan_kernel<<<1, 1024, 0, s>>>(counts, K + 1);
   RBQ_LAUNCHED();
   query_order_scatter_kernel<<<grid, 256, 0, s>>>(probes, nq, pstride, K, counts, qorder);
+  RBQ_LAUNCHED();
+}
+
+// ---------------------------------------------------------------------------------------
+// List-scan plan.  codes[q, 32w + j] = the query's signed code of dim 32w + j read back from its
+// planes (sum_{b < QB-1} bit_b << b - bit_{QB-1} << (QB-1)), one thread per (query, word).
+// ---------------------------------------------------------------------------------------
+__global__ void planes_to_codes_kernel(const uint32_t* __restrict__ planes, int64_t nq, int W, int QB,
+                                       int8_t* __restrict__ codes)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * W) return;
+  const int64_t q = i / W;
+  const int w = (int)(i - q * W);
+  uint32_t p[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) p[b] = b < QB ? __brev(planes[(q * QB + b) * W + w]) : 0u;  // bit j = dim j
+  uint32_t o[8];
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    uint32_t word = 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * j4 + k;
+      int v = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (b < QB) v += (int)((p[b] >> j) & 1u) << b;
+      if ((p[QB - 1] >> j) & 1u) v -= 2 << (QB - 1);  // the top plane weighs -2^(QB-1)
+      word |= ((uint32_t)v & 0xFFu) << (8 * k);
+    }
+    o[j4] = word;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(codes + q * (32 * W) + 32 * w);
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+void launch_planes_to_codes(const uint32_t* planes, int64_t nq, int W, int QB, int8_t* codes, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  RBQ_CHECK(QB == 4 || QB == 8, RBQ_ERR_INVALID, "query codes: 4- or 8-bit planes");
+  planes_to_codes_kernel<<<(unsigned)ceil_div(nq * W, 256), 256, 0, s>>>(planes, nq, W, QB, codes);
+  RBQ_LAUNCHED();
+}
+
+// The (list, query) pairs of this shard's probed lists, bucketed by list: counts, their
+// exclusive prefix sum (list_start), work items of up to kListScanRows pairs per list and their
+// prefix sum (item_start), then the pairs (query, g) in arrival order inside a list.
+__global__ void list_pairs_hist_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe, int pstride,
+                                       const int32_t* __restrict__ owner, int rank, int32_t* __restrict__ cnt)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * nprobe) return;
+  const int64_t q = i / nprobe;
+  const int l = probes[q * pstride + (i - q * nprobe)];
+  if (l >= 0 && __ldg(owner + l) == rank) atomicAdd(cnt + l, 1);
+}
+
+__global__ void list_items_kernel(const int32_t* __restrict__ list_start, int K, int32_t* __restrict__ item_cnt)
+{
+  const int l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l < K) item_cnt[l] = (list_start[l + 1] - list_start[l] + kListScanRows - 1) / kListScanRows;
+  if (l == K) item_cnt[K] = 0;
+}
+
+__global__ void list_pairs_scatter_kernel(const int32_t* __restrict__ probes, const float* __restrict__ g, int64_t nq,
+                                          int nprobe, int pstride, const int32_t* __restrict__ owner, int rank,
+                                          int32_t* __restrict__ cursor, int32_t* __restrict__ pair_q,
+                                          float* __restrict__ pair_g)
+{
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq * nprobe) return;
+  const int64_t q = i / nprobe;
+  const int64_t e = q * pstride + (i - q * nprobe);
+  const int l = probes[e];
+  if (l < 0 || __ldg(owner + l) != rank) return;
+  const int pos = atomicAdd(cursor + l, 1);
+  pair_q[pos] = (int32_t)q;
+  pair_g[pos] = g[e];
+}
+
+void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int nprobe, int pstride,
+                       const int32_t* owner, int rank, int K, int32_t* list_start, int32_t* item_start,
+                       int32_t* cursor, int32_t* pair_q, float* pair_g, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  RBQ_CHECK(nq * nprobe < 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "list scan: too many (list, query) pairs");
+  RBQ_CUDA(cudaMemsetAsync(list_start, 0, (size_t)(K + 1) * sizeof(int32_t), s));
+  const unsigned grid = (unsigned)ceil_div(nq * nprobe, 256);
+  list_pairs_hist_kernel<<<grid, 256, 0, s>>>(probes, nq, nprobe, pstride, owner, rank, list_start);
+  RBQ_LAUNCHED();
+  exclusive_scan_kernel<<<1, 1024, 0, s>>>(list_start, K + 1);
+  RBQ_LAUNCHED();
+  list_items_kernel<<<(unsigned)ceil_div(K + 1, 256), 256, 0, s>>>(list_start, K, item_start);
+  RBQ_LAUNCHED();
+  exclusive_scan_kernel<<<1, 1024, 0, s>>>(item_start, K + 1);
+  RBQ_LAUNCHED();
+  RBQ_CUDA(cudaMemcpyAsync(cursor, list_start, (size_t)(K + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+  list_pairs_scatter_kernel<<<grid, 256, 0, s>>>(probes, g, nq, nprobe, pstride, owner, rank, cursor, pair_q, pair_g);
+  RBQ_LAUNCHED();
+}
+
+// Exact pass of the list scan, one block per query: the candidates of its row, taken one at a
+// time by a warp (the exact 1-bit inner product of the tile scan, or the extra-bit distance),
+// kept while dist <= tau0[q]; the R smallest keys, ascending, go to out_keys.  The admitted set
+// does not depend on the order the list scan found it in, so neither does the result.
+constexpr int kExactThreads = 256;
+
+__global__ void __launch_bounds__(kExactThreads) exact_topr_kernel(const ExactArgs a)
+{
+  const int64_t q = blockIdx.x;
+  const int n = a.cand_cnt[q];
+  if (n > a.cap) return;  // overflowed row: the fixed-threshold tile scan answers this query
+  extern __shared__ __align__(16) unsigned char ex_smem_raw[];
+  const int W = a.W, NB = 4 * W;
+  float* qsT = reinterpret_cast<float*>(ex_smem_raw);                                  // [8 * NB]
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(ex_smem_raw + 128 * W);  // [cap]
+  unsigned long long* keys2 = keys + a.cap;                                            // [cap]
+  __shared__ int s_count, s_misc[3], s_cnt2;
+  __shared__ unsigned s_hist[256];
+  __shared__ unsigned long long s_kmax;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 8 * NB; i += kExactThreads) {
+    const int jj = i / NB, j = i - jj * NB;
+    qsT[i] = a.Qr[q * (8 * NB) + 8 * j + jj];
+  }
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+  const float k1 = a.k1[q];
+  const float tau = a.tau0[q];
+  const float ex_scale = (float)(1 << a.ex_bits);
+  const float kb = __fmul_rn(k1, (float)((2 << a.ex_bits) - 1));
+  const unsigned long long* row = a.cand + q * a.cap;
+  for (int c = warp; c < n; c += kExactThreads / 32) {
+    const unsigned long long e = row[c];
+    const int slot = (int)(uint32_t)e;
+    const float g = __uint_as_float((uint32_t)(e >> 32));
+    float eip;
+    switch (W) {  // the exact inner product is unrolled per word count
+#define RBQ_EXACT_W(w) \
+  case w: eip = warp_exact_ip<w>(a.codes, slot, qsT, lane); break;
+      RBQ_EXACT_W(1) RBQ_EXACT_W(2) RBQ_EXACT_W(3) RBQ_EXACT_W(4) RBQ_EXACT_W(6) RBQ_EXACT_W(8) RBQ_EXACT_W(12)
+      RBQ_EXACT_W(16) RBQ_EXACT_W(24)
+#undef RBQ_EXACT_W
+      default: eip = 0.0f;
+    }
+    float dist;
+    if (a.ex_bits == 0) {
+      dist = __fadd_rn(__fadd_rn(__ldg(a.fadd + slot), g), __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(eip, k1)));
+    } else {
+      float ipx;
+      switch (W) {
+#define RBQ_EX_W(w) \
+  case w: ipx = warp_ex_ip<w>(a.ex_codes, slot, a.ex_bits, qsT, lane); break;
+        RBQ_EX_W(1) RBQ_EX_W(2) RBQ_EX_W(3) RBQ_EX_W(4) RBQ_EX_W(6) RBQ_EX_W(8) RBQ_EX_W(12) RBQ_EX_W(16) RBQ_EX_W(24)
+#undef RBQ_EX_W
+        default: ipx = 0.0f;
+      }
+      const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, eip), ipx), kb);
+      dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), g), __fmul_rn(__ldg(a.fexr + slot), T));
+    }
+    if (lane == 0 && dist <= tau) keys[atomicAdd(&s_count, 1)] = make_key(dist, __ldg(a.ids + slot));
+  }
+  __syncthreads();
+  int cnt = s_count;
+  if (cnt > a.R) {
+    block_keep_smallest(keys, cnt, a.R, keys2, s_hist, s_misc, &s_kmax, &s_cnt2);
+    keys = keys2;
+    cnt = a.R;
+  }
+  int r2 = 2;
+  while (r2 < cnt) r2 <<= 1;
+  for (int i = cnt + tid; i < r2; i += kExactThreads) keys[i] = kEmptyKey;
+  __syncthreads();
+  block_bitonic_sort(keys, r2);
+  unsigned long long* out = a.out_keys + q * a.R;
+  for (int i = tid; i < a.R; i += kExactThreads) out[i] = i < cnt ? keys[i] : kEmptyKey;
+}
+
+void launch_exact_topr(const ExactArgs& a, cudaStream_t s)
+{
+  if (a.nq <= 0) return;
+  RBQ_CHECK(a.W >= 1 && a.W <= 24, RBQ_ERR_INVALID, "list scan: padded dim above 768");
+  RBQ_CHECK(a.cap >= a.R && a.cap <= 8192, RBQ_ERR_INVALID, "list scan: candidate row size");
+  // keys2 holds the cut (R keys) and the sort pads to a power of two: 2 * cap keys suffice
+  const size_t smem = (size_t)128 * a.W + (size_t)a.cap * 16;
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(exact_topr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  exact_topr_kernel<<<(unsigned)a.nq, kExactThreads, smem, s>>>(a);
   RBQ_LAUNCHED();
 }
 

@@ -53,7 +53,9 @@ class IndexIVFRaBitQ:
     scan slices start from the nearest list's bound seed: -1 = auto, on when the probes are split;
     0 off; 1 on), ``query_bits`` (the search mode: 4 QUANT4, the reference CLI's default;
     8 QUANT8; 16 LUT16 and 32 LUT32, the estimate from fp16 / fp32 tables of the float query),
-    ``use_graph`` (replay each batch size's search from a captured CUDA graph; small batches).
+    ``use_graph`` (replay each batch size's search from a captured CUDA graph; small batches),
+    ``scan_kind`` (0 auto; 1 the tile scan; 2 the list scan: fixed per-query thresholds, each probed
+    list scored against all its queries by an int8 GEMM on the tensor cores).
     """
 
     def __init__(self, d: int, nlist: int, seed: int = 7, device: int | None = None, kmeans_iters: int = 20,
@@ -75,6 +77,7 @@ class IndexIVFRaBitQ:
         self.seeded = -1
         self.query_bits = 4
         self.use_graph = False
+        self.scan_kind = 0
         self._h = ctypes.c_void_p()
         if _handle is not None:
             self._h = _handle
@@ -198,6 +201,7 @@ class IndexIVFRaBitQ:
         sp.seeded = int(self.seeded)
         sp.query_bits = int(self.query_bits)
         sp.graph = int(bool(self.use_graph))
+        sp.scan_kind = int(self.scan_kind)
         return sp
 
     def search(self, x, k: int):

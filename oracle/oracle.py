@@ -463,8 +463,35 @@ def assign(X, C) -> np.ndarray:
     return labels
 
 
+# The list scan (rbq_search_params_t.scan_kind): batches whose probed lists are shared by at least
+# this many queries on average take it under scan_kind 0 (auto).
+LIST_SCAN_MIN_PAIRS_PER_LIST = 16
+
+
+def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K) -> bool:
+    """The library's choice between the tile scan and the list scan (fixed thresholds)."""
+    able = query_bits in (4, 8) and bool(prune) and dp % 32 == 0 and dp <= 768
+    if scan_kind == 2:
+        if not able:
+            raise ValueError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
+        return True
+    return scan_kind == 0 and able and nq * nprobe >= LIST_SCAN_MIN_PAIRS_PER_LIST * K
+
+
+def list_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tau0, shard_rank=0, shard_count=1,
+              with_stats=False, owner=None):
+    """The list scan's result: every query admits a vector while its lower bound is below the
+    fixed tau0[q] (no tightening), keeps the admitted vectors whose distance is <= tau0[q] and
+    returns the R smallest (distance, id) keys.  One tile spanning all probed lists gives exactly
+    that in scan(); a cut to R along the way cannot change the R smallest."""
+    return scan(ix, Qr, planes, delta, k1, probes, g, R, tile=1 << 30, cap=(1 << 30) + (1 << 20), prune=1,
+                slices=1, shard_rank=shard_rank, shard_count=shard_count, with_stats=with_stats, tau0=tau0,
+                owner=owner)
+
+
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
-           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None, query_bits=4):
+           shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None, query_bits=4,
+           scan_kind=0):
     """Full search pipeline: rotate -> coarse -> query prep -> scan -> rerank.
 
     seeded (rbq_search_params_t.seeded): -1 scans in two phases (seeded_scan) when the probes
@@ -472,7 +499,10 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     pipeline (two phases, threshold shared by all shards).  rerank_depth == 0 returns the
     scan's top-k estimates (the reference behaviour).  query_bits 8 (QUANT8) quantises the
     queries to 8 bits with ix.t8 (set it to query_scale(dp, seed, 7) of the index); 16 / 32
-    (LUT16 / LUT32) estimate with fp16 / fp32 tables of the float query (one pass, no seed)."""
+    (LUT16 / LUT32) estimate with fp16 / fp32 tables of the float query (one pass, no seed).
+    scan_kind (rbq_search_params_t.scan_kind): 0 auto, 1 tile scan, 2 list scan (thresholds fixed
+    at the bound seed over the leading probed lists holding >= R vectors); the sharded search's
+    pipeline (exchange=True) scans by tiles."""
     Q = _c(Q, np.float32)
     Qr = rotate(Q, ix.P)
     probes, g = coarse(Qr, ix.c_rot, nprobe)
@@ -490,7 +520,11 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
             dist, ids = cd[:, :k].copy(), cand[:, :k].copy()
         return (dist, ids, res[2]) if with_stats else (dist, ids)
     two = slices > 1 if seeded < 0 else seeded > 0
-    if exchange or two:
+    if not exchange and uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k):
+        tau = bound_seed(ix, planes, delta, k1, probes, g, R, shard_rank, shard_count, owner)
+        res = list_scan(ix, Qr, planes, delta, k1, probes, g, R, tau, shard_rank, shard_count, with_stats=True,
+                        owner=owner)
+    elif exchange or two:
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
                           shard_count, with_stats=True, exchange=exchange, owner=owner)
     else:

@@ -317,8 +317,8 @@ def test_gpu_extra_bits_save_load_and_reference_files(oracle, ex_case, tmp_path)
     assert f["ex"] == 3 and f["end"] == f["size"]
     # the bit stream of every vector restated from the planes
     dp, n = oix.dp, ex["ex_codes"].shape[0]
-    bits = np.unpackbits(ex["ex_codes"].view(np.uint8).reshape(n, 3, -1, 4)[:, :, :, ::-1].reshape(n, 3, dp), axis=-1)
-    bits = bits.reshape(n, 3, dp)  # [vector, plane p, dim] = bit p of the dim's code
+    bits = np.unpackbits(ex["ex_codes"].view(np.uint8).reshape(n, 3, -1, 4)[:, :, :, ::-1].reshape(n, 3, dp // 8),
+                         axis=-1)  # [vector, plane p, dim] = bit p of the dim's code
     stream = np.stack([bits[:, 2], bits[:, 1], bits[:, 0]], axis=-1).reshape(n, dp * 3)  # MSB first
     assert np.array_equal(f["long_codes"], np.packbits(stream, axis=-1))
     assert np.array_equal(u32(f["exf"][:, 0]), u32(ex["fexadd"])) and np.array_equal(u32(f["exf"][:, 1]), u32(ex["fexr"]))

@@ -1,0 +1,202 @@
+"""The list scan (rbq_search_params_t.scan_kind = 2): fixed per-query thresholds and a tensor-core
+int8 GEMM per probed list (query codes x code bits), then the exact pass per query.
+
+Its result is defined by the oracle's `list_scan`: admit while low < tau0 (the bound seed over
+the leading probed lists holding >= R vectors), keep the admitted vectors with distance <= tau0,
+return the R smallest keys.  CPU tests pin that definition against the tile scan; GPU tests
+compare the library with it bit for bit."""
+import numpy as np
+import pytest
+
+from conftest import mixture
+
+
+def u32(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+# ------------------------------------------------------------------------------------------
+# CPU: the definition
+# ------------------------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def small(oracle):
+    X, Q = mixture(30000, 128, 60, 0.3, 200, seed=21)
+    C, _ = oracle.kmeans(X[::5], 48, iters=4)
+    lab = oracle.assign(X, C)
+    P, t4 = oracle.make_rotation(128, 7), oracle.query_scale(128, 7)
+    return oracle.build(X, C, lab, P, t4), X, Q
+
+
+def test_fixed_threshold_keeps_the_tile_scan_answer(oracle, small):
+    """With thresholds fixed at the bound seed the admitted set contains the tile scan's (whose
+    threshold only tightens from that seed), and the top R agree on this data."""
+    ix, X, Q = small
+    Qr = oracle.rotate(Q, ix.P)
+    probes, g = oracle.coarse(Qr, ix.c_rot, 8)
+    pl, de, k1, _ = oracle.query_prep(Qr, ix.t4, 4)
+    R = 40
+    tau = oracle.bound_seed(ix, pl, de, k1, probes, g, R)
+    assert np.isfinite(tau).all()
+    ti, td, ts = oracle.scan(ix, Qr, pl, de, k1, probes, g, R, with_stats=True, tau0=tau)
+    li, ld, ls = oracle.list_scan(ix, Qr, pl, de, k1, probes, g, R, tau, with_stats=True)
+    assert ls[0] == ts[0] and ls[1] >= ts[1]
+    assert np.array_equal(li, ti) and np.array_equal(u32(ld), u32(td))
+
+
+def test_auto_rule():
+    from oracle import oracle as O
+    assert O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)      # 312 queries per list
+    assert not O.uses_list_scan(0, 4, 1, 256, 64, 32, 1024)     # 2 per list: the tile scan
+    assert not O.uses_list_scan(0, 16, 1, 256, 10000, 32, 1024)  # LUT modes scan by tiles
+    assert not O.uses_list_scan(0, 4, 0, 256, 10000, 32, 1024)   # no prune: nothing to fix
+    assert not O.uses_list_scan(1, 4, 1, 256, 10000, 32, 1024)
+    assert O.uses_list_scan(2, 8, 1, 768, 1, 1, 1024)
+    with pytest.raises(ValueError):
+        O.uses_list_scan(2, 4, 1, 1024, 1, 1, 8)
+
+
+# ------------------------------------------------------------------------------------------
+# GPU
+# ------------------------------------------------------------------------------------------
+def _index(oracle, X, C, lab, bits=1):
+    from neurosamble_b200 import IndexIVFRaBitQ
+    idx = IndexIVFRaBitQ(X.shape[1], C.shape[0], seed=7, bits_per_dim=bits)
+    idx.set_centroids(C)
+    idx.add(X, labels=lab)
+    oix = oracle.build(X, C, lab, idx.rotation(), idx.query_scale, bits_per_dim=bits,
+                       tex=idx.info().ex_scale if bits > 1 else None)
+    oix.t8 = oracle.query_scale(oix.dp, 7, 7)
+    return idx, oix
+
+
+@pytest.fixture(scope="module")
+def gcase(oracle):
+    X, Q = mixture(30000, 128, 60, 0.3, 400, seed=23)
+    C, _ = oracle.kmeans(X[::5], 48, iters=4)
+    lab = oracle.assign(X, C)
+    idx, oix = _index(oracle, X, C, lab)
+    return idx, oix, X, Q, C, lab
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits,R,nprobe", [(4, 40, 8), (4, 100, 16), (8, 40, 8), (4, 10, 48)])
+def test_list_scan_stage_bit_exact(oracle, gcase, bits, R, nprobe):
+    """rbq_scan_lists against the oracle's list scan from the same thresholds: candidates,
+    distances and the scanned / admitted counters."""
+    import torch
+    from neurosamble_b200 import _lib
+    from neurosamble_b200.index import _ptr, _stream_ptr
+    idx, oix, X, Q, C, lab = gcase
+    Qr = oracle.rotate(Q, oix.P)
+    nq = Qr.shape[0]
+    pl, de, k1, _ = oracle.query_prep(Qr, oix.t4 if bits == 4 else oix.t8, bits)
+    probes, g = oracle.coarse(Qr, oix.c_rot, nprobe)
+    tau = oracle.bound_seed(oix, pl, de, k1, probes, g, R)
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).cuda()
+    qr, pld, ded, k1d = t(Qr, np.float32), t(pl, np.int32), t(de, np.float32), t(k1, np.float32)
+    pd, gd, taud = t(probes, np.int32), t(g, np.float32), t(tau, np.float32)
+    ids = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+    dist = torch.empty((nq, R), dtype=torch.float32, device="cuda")
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    _lib.call("rbq_scan_lists", idx.handle, _ptr(qr), _ptr(pld), _ptr(ded), _ptr(k1d), nq, _ptr(pd), _ptr(gd),
+              nprobe, 0, _ptr(taud), R, _ptr(ids), _ptr(dist), _ptr(stats), bits, _stream_ptr(idx.device))
+    torch.cuda.synchronize()
+    oi, od, ost = oracle.list_scan(oix, Qr, pl, de, k1, probes, g, R, tau, with_stats=True)
+    assert np.array_equal(ids.cpu().numpy(), oi)
+    assert np.array_equal(u32(dist.cpu().numpy()), u32(od))
+    assert stats.cpu().tolist() == ost.tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits,R", [(4, 0), (4, 40), (8, 40), (4, 200)])
+def test_list_scan_search_bit_exact(oracle, gcase, bits, R):
+    idx, oix, X, Q, C, lab = gcase
+    idx.nprobe, idx.k_rerank, idx.query_bits, idx.scan_kind = 12, R, bits, 2
+    try:
+        for qs in (Q, Q[:3]):
+            d, i = idx.search(qs, 10)
+            d2, i2 = oracle.search(oix, qs, 10, 12, R, query_bits=bits, scan_kind=2)
+            assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+        _, gt = oracle.knn_exact(X, Q, 10)
+        if R >= 40:
+            assert oracle.recall(idx.search(Q, 10)[1], gt) > 0.9
+    finally:
+        idx.query_bits, idx.scan_kind = 4, 0
+
+
+@pytest.mark.gpu
+def test_auto_scan_choice_matches_the_oracle(oracle, gcase):
+    """scan_kind 0: 400 queries x 12 probes over 48 lists take the list scan, 5 queries the tile
+    scan; both searches equal the oracle's with the same rule."""
+    idx, oix, X, Q, C, lab = gcase
+    idx.nprobe, idx.k_rerank, idx.scan_kind = 12, 40, 0
+    assert oracle.uses_list_scan(0, 4, 1, 128, len(Q), 12, 48)
+    assert not oracle.uses_list_scan(0, 4, 1, 128, 5, 12, 48)
+    for qs in (Q, Q[:5]):
+        d, i = idx.search(qs, 10)
+        d2, i2 = oracle.search(oix, qs, 10, 12, 40)
+        assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("d", [32, 96, 100, 256, 768])
+def test_list_scan_other_dimensions(oracle, d):
+    """Padded dims that fill part of a 128-byte chunk (32, 96), one or more chunks (128, 256) and
+    six chunks (768)."""
+    X, Q = mixture(6000, d, 20, 0.3, 120, seed=d)
+    C, _ = oracle.kmeans(X[::3], 16, iters=3)
+    lab = oracle.assign(X, C)
+    idx, oix = _index(oracle, X, C, lab)
+    idx.nprobe, idx.k_rerank, idx.scan_kind = 6, 30, 2
+    d1, i1 = idx.search(Q, 10)
+    d2, i2 = oracle.search(oix, Q, 10, 6, 30, scan_kind=2)
+    assert np.array_equal(i1, i2) and np.array_equal(u32(d1), u32(d2))
+
+
+@pytest.mark.gpu
+def test_list_scan_extra_bits(oracle):
+    X, Q = mixture(20000, 128, 40, 0.3, 300, seed=31)
+    C, _ = oracle.kmeans(X[::4], 40, iters=3)
+    lab = oracle.assign(X, C)
+    idx, oix = _index(oracle, X, C, lab, bits=4)
+    idx.nprobe, idx.k_rerank, idx.scan_kind = 8, 0, 2
+    d1, i1 = idx.search(Q, 10)
+    d2, i2 = oracle.search(oix, Q, 10, 8, 0, scan_kind=2)
+    assert np.array_equal(i1, i2) and np.array_equal(u32(d1), u32(d2))
+
+
+@pytest.mark.gpu
+def test_overflowed_rows_take_the_fixed_threshold_tile_scan(oracle):
+    """Uniform random vectors in 128 dims are nearly equidistant: the bound seed admits most of
+    a query's 20,000 probed vectors, far past the 2,048-entry candidate row, so those queries are
+    answered by the tile scan under the same fixed thresholds, with the same result."""
+    import torch
+    from neurosamble_b200 import _lib
+    from neurosamble_b200.index import _ptr, _stream_ptr
+    rng = np.random.default_rng(4)
+    X = rng.standard_normal((20000, 128)).astype(np.float32)
+    Q = rng.standard_normal((40, 128)).astype(np.float32)
+    C, _ = oracle.kmeans(X[::4], 16, iters=3)
+    lab = oracle.assign(X, C)
+    idx, oix = _index(oracle, X, C, lab)
+    idx.nprobe, idx.k_rerank, idx.scan_kind = 16, 10, 2
+    d1, i1 = idx.search(Q, 10)
+    d2, i2, st = oracle.search(oix, Q, 10, 16, 10, scan_kind=2, with_stats=True)
+    assert st[1] > 2048 * 4  # several rows overflowed
+    assert np.array_equal(i1, i2) and np.array_equal(u32(d1), u32(d2))
+    # the stage's counters count every admitted vector once, overflowed rows included
+    Qr = oracle.rotate(Q, oix.P)
+    pl, de, k1, _ = oracle.query_prep(Qr, oix.t4, 4)
+    probes, g = oracle.coarse(Qr, oix.c_rot, 16)
+    tau = oracle.bound_seed(oix, pl, de, k1, probes, g, 10)
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).cuda()
+    ids = torch.empty((40, 10), dtype=torch.int64, device="cuda")
+    dist = torch.empty((40, 10), dtype=torch.float32, device="cuda")
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    _lib.call("rbq_scan_lists", idx.handle, _ptr(t(Qr, np.float32)), _ptr(t(pl, np.int32)), _ptr(t(de, np.float32)),
+              _ptr(t(k1, np.float32)), 40, _ptr(t(probes, np.int32)), _ptr(t(g, np.float32)), 16, 0,
+              _ptr(t(tau, np.float32)), 10, _ptr(ids), _ptr(dist), _ptr(stats), 4, _stream_ptr(idx.device))
+    torch.cuda.synchronize()
+    oi, od, ost = oracle.list_scan(oix, Qr, pl, de, k1, probes, g, 10, tau, with_stats=True)
+    assert np.array_equal(ids.cpu().numpy(), oi) and np.array_equal(u32(dist.cpu().numpy()), u32(od))
+    assert stats.cpu().tolist() == ost.tolist()
