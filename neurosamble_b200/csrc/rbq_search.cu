@@ -1537,13 +1537,13 @@ void launch_planes_to_codes(const uint32_t* planes, int64_t nq, int W, int QB, i
 // exclusive prefix sum (list_start), work items of up to kListScanRows pairs per list and their
 // prefix sum (item_start), then the pairs (query, g) in arrival order inside a list.
 __global__ void list_pairs_hist_kernel(const int32_t* __restrict__ probes, int64_t nq, int nprobe, int pstride,
-                                       const int32_t* __restrict__ owner, int rank, int32_t* __restrict__ cnt)
+                                       const int32_t* __restrict__ owner, int rank, int K, int32_t* __restrict__ cnt)
 {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nq * nprobe) return;
   const int64_t q = i / nprobe;
   const int l = probes[q * pstride + (i - q * nprobe)];
-  if (l >= 0 && __ldg(owner + l) == rank) atomicAdd(cnt + l, 1);
+  if (l >= 0 && l < K && __ldg(owner + l) == rank) atomicAdd(cnt + l, 1);
 }
 
 __global__ void list_items_kernel(const int32_t* __restrict__ list_start, int K, int32_t* __restrict__ item_cnt)
@@ -1554,7 +1554,7 @@ __global__ void list_items_kernel(const int32_t* __restrict__ list_start, int K,
 }
 
 __global__ void list_pairs_scatter_kernel(const int32_t* __restrict__ probes, const float* __restrict__ g, int64_t nq,
-                                          int nprobe, int pstride, const int32_t* __restrict__ owner, int rank,
+                                          int nprobe, int pstride, const int32_t* __restrict__ owner, int rank, int K,
                                           int32_t* __restrict__ cursor, int32_t* __restrict__ pair_q,
                                           float* __restrict__ pair_g)
 {
@@ -1563,7 +1563,7 @@ __global__ void list_pairs_scatter_kernel(const int32_t* __restrict__ probes, co
   const int64_t q = i / nprobe;
   const int64_t e = q * pstride + (i - q * nprobe);
   const int l = probes[e];
-  if (l < 0 || __ldg(owner + l) != rank) return;
+  if (l < 0 || l >= K || __ldg(owner + l) != rank) return;
   const int pos = atomicAdd(cursor + l, 1);
   pair_q[pos] = (int32_t)q;
   pair_g[pos] = g[e];
@@ -1577,7 +1577,7 @@ void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int np
   RBQ_CHECK(nq * nprobe < 0x7fffffff && K >= 1, RBQ_ERR_INVALID, "list scan: too many (list, query) pairs");
   RBQ_CUDA(cudaMemsetAsync(list_start, 0, (size_t)(K + 1) * sizeof(int32_t), s));
   const unsigned grid = (unsigned)ceil_div(nq * nprobe, 256);
-  list_pairs_hist_kernel<<<grid, 256, 0, s>>>(probes, nq, nprobe, pstride, owner, rank, list_start);
+  list_pairs_hist_kernel<<<grid, 256, 0, s>>>(probes, nq, nprobe, pstride, owner, rank, K, list_start);
   RBQ_LAUNCHED();
   exclusive_scan_kernel<<<1, 1024, 0, s>>>(list_start, K + 1);
   RBQ_LAUNCHED();
@@ -1586,7 +1586,8 @@ void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int np
   exclusive_scan_kernel<<<1, 1024, 0, s>>>(item_start, K + 1);
   RBQ_LAUNCHED();
   RBQ_CUDA(cudaMemcpyAsync(cursor, list_start, (size_t)(K + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
-  list_pairs_scatter_kernel<<<grid, 256, 0, s>>>(probes, g, nq, nprobe, pstride, owner, rank, cursor, pair_q, pair_g);
+  list_pairs_scatter_kernel<<<grid, 256, 0, s>>>(probes, g, nq, nprobe, pstride, owner, rank, K, cursor, pair_q,
+                                                  pair_g);
   RBQ_LAUNCHED();
 }
 
