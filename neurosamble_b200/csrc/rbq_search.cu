@@ -1950,22 +1950,67 @@ struct ResultSource {
 };
 
 // k-way merge of per-shard results [parts, nq, k] by (distance, id): the on-device merge that
-// follows the all-gather of a list-sharded search.
+// follows the all-gather of a list-sharded search.  Shard results arrive sorted (a search returns
+// its rows ascending); then an element at rank r of part p lands at r plus, per other part, the
+// number of its keys below (parts after p) or up to (parts before p) the element, found by binary
+// search in shared memory, and only the elements landing below k are written (one barrier
+// instead of a sort).  Rows that are not ascending take the block-wide bitonic sort.
+__device__ __forceinline__ int keys_below(const unsigned long long* row, int k, unsigned long long e, bool or_equal)
+{
+  int lo = 0, hi = k;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (row[mid] < e || (or_equal && row[mid] == e))
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
 __global__ void __launch_bounds__(256) merge_results_kernel(const ResultSource src, int parts, int64_t nq, int k,
                                                             int n2, float* __restrict__ out_dist,
                                                             int64_t* __restrict__ out_ids)
 {
   extern __shared__ unsigned long long mr[];
+  __shared__ int s_unsorted;
   const int64_t q = blockIdx.x;
+  const int n = parts * k;
+  if (threadIdx.x == 0) s_unsorted = 0;
   for (int i = threadIdx.x; i < n2; i += blockDim.x) {
     unsigned long long key = kEmptyKey;
-    if (i < parts * k) {
+    if (i < n) {
       const int p = i / k, r = i - p * k;
       key = src.at(((size_t)p * nq + q) * k + r);
     }
     mr[i] = key;
   }
   __syncthreads();
+  bool bad = false;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (i % k != 0 && mr[i - 1] > mr[i]) bad = true;
+  if (bad) s_unsorted = 1;
+  __syncthreads();
+  if (!s_unsorted) {
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+      out_ids[q * k + i] = -1;
+      out_dist[q * k + i] = __int_as_float(0x7f800000);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long e = mr[i];
+      if (e == kEmptyKey) continue;
+      const int p = i / k;
+      int pos = i - p * k;
+      for (int o = 0; o < parts && pos < k; ++o)
+        if (o != p) pos += keys_below(mr + o * k, k, e, o < p);
+      if (pos < k) {
+        out_ids[q * k + pos] = (int64_t)(e & 0xFFFFFFFFu);
+        out_dist[q * k + pos] = from_ordered_bits((uint32_t)(e >> 32));
+      }
+    }
+    return;
+  }
   block_bitonic_sort(mr, n2);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     const unsigned long long key = mr[i];

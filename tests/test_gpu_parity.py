@@ -588,10 +588,12 @@ def test_balanced_shards_follow_the_restated_map(oracle, case, tmp_path):
     assert np.array_equal(read_index(str(path), shard_rank=1, shard_count=3).list_owners(), want)
 
 
-@pytest.mark.parametrize("parts,k", [(2, 10), (8, 10), (3, 40), (8, 30), (8, 100)])
-def test_merge_results_matches_oracle(oracle, parts, k):
+@pytest.mark.parametrize("parts,k,sorted_rows", [(2, 10, 0), (8, 10, 0), (3, 40, 0), (8, 30, 0), (8, 100, 0),
+                                                (8, 100, 1), (3, 40, 1), (5, 64, 1)])
+def test_merge_results_matches_oracle(oracle, parts, k, sorted_rows):
     """rbq_merge_results ([parts, nq, k] -> [nq, k] by (distance, id)): the warp path for small
-    merges and the block sort for large ones, with empty slots and a key present in two parts."""
+    merges; for large ones the rank merge of ascending rows (what shards return) and the block
+    sort of unordered ones; with empty slots and a key present in two parts."""
     torch = _torch()
     rng = np.random.default_rng(parts * 1000 + k)
     nq = 77
@@ -600,6 +602,9 @@ def test_merge_results_matches_oracle(oracle, parts, k):
     i[:, ::3, k // 2:] = -1
     d[:, ::3, k // 2:] = np.inf
     d[0, 1, 0], i[0, 1, 0] = d[parts - 1, 1, 1], i[parts - 1, 1, 1]  # duplicate key
+    if sorted_rows:  # each part's row ascending by key, as a search returns it
+        order = np.argsort(oracle._keys(i, d), axis=2, kind="stable")
+        d, i = np.take_along_axis(d, order, 2), np.take_along_axis(i, order, 2)
     od = torch.empty((nq, k), dtype=torch.float32, device="cuda")
     oi = torch.empty((nq, k), dtype=torch.int64, device="cuda")
     dd, ii = torch.from_numpy(d).cuda(), torch.from_numpy(i).cuda()
