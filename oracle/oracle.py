@@ -463,19 +463,15 @@ def assign(X, C) -> np.ndarray:
     return labels
 
 
-# The list scan (rbq_search_params_t.scan_kind): batches whose probed lists are shared by at least
-# this many queries on average take it under scan_kind 0 (auto).
-LIST_SCAN_MIN_PAIRS_PER_LIST = 16
-
-
 def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K) -> bool:
-    """The library's choice between the tile scan and the list scan (fixed thresholds)."""
+    """The library's choice between the tile scan and the list scan (fixed thresholds): the list
+    scan when scan_kind is 2, the tile scan under 0 (auto) and 1."""
     able = query_bits in (4, 8) and bool(prune) and dp % 32 == 0 and dp <= 768
     if scan_kind == 2:
         if not able:
             raise ValueError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
         return True
-    return scan_kind == 0 and able and nq * nprobe >= LIST_SCAN_MIN_PAIRS_PER_LIST * K
+    return False
 
 
 def list_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tau0, shard_rank=0, shard_count=1,

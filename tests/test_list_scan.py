@@ -45,10 +45,7 @@ def test_fixed_threshold_keeps_the_tile_scan_answer(oracle, small):
 
 def test_auto_rule():
     from oracle import oracle as O
-    assert O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)      # 312 queries per list
-    assert not O.uses_list_scan(0, 4, 1, 256, 64, 32, 1024)     # 2 per list: the tile scan
-    assert not O.uses_list_scan(0, 16, 1, 256, 10000, 32, 1024)  # LUT modes scan by tiles
-    assert not O.uses_list_scan(0, 4, 0, 256, 10000, 32, 1024)   # no prune: nothing to fix
+    assert not O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)  # auto: the tile scan
     assert not O.uses_list_scan(1, 4, 1, 256, 10000, 32, 1024)
     assert O.uses_list_scan(2, 8, 1, 768, 1, 1, 1024)
     with pytest.raises(ValueError):
@@ -127,17 +124,19 @@ def test_list_scan_search_bit_exact(oracle, gcase, bits, R):
 
 
 @pytest.mark.gpu
-def test_auto_scan_choice_matches_the_oracle(oracle, gcase):
-    """scan_kind 0: 400 queries x 12 probes over 48 lists take the list scan, 5 queries the tile
-    scan; both searches equal the oracle's with the same rule."""
+def test_scan_kinds_match_the_oracle(oracle, gcase):
+    """scan_kind 0 (auto: the tile scan), 1 and 2 each equal the oracle's search of that kind."""
     idx, oix, X, Q, C, lab = gcase
-    idx.nprobe, idx.k_rerank, idx.scan_kind = 12, 40, 0
-    assert oracle.uses_list_scan(0, 4, 1, 128, len(Q), 12, 48)
-    assert not oracle.uses_list_scan(0, 4, 1, 128, 5, 12, 48)
-    for qs in (Q, Q[:5]):
-        d, i = idx.search(qs, 10)
-        d2, i2 = oracle.search(oix, qs, 10, 12, 40)
-        assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    idx.nprobe, idx.k_rerank = 12, 40
+    try:
+        for kind in (0, 1, 2):
+            idx.scan_kind = kind
+            for qs in (Q, Q[:5]):
+                d, i = idx.search(qs, 10)
+                d2, i2 = oracle.search(oix, qs, 10, 12, 40, scan_kind=kind)
+                assert np.array_equal(i, i2) and np.array_equal(u32(d), u32(d2))
+    finally:
+        idx.scan_kind = 0
 
 
 @pytest.mark.gpu
