@@ -42,6 +42,14 @@ CONFIGS = {
             k=50, rerank=500, seed=5005, config=5, aniso=1, device_data=True, gt_sample=1000),
 }
 RERANK_LADDER = (100, 150, 200, 300, 400, 600, 800)
+
+
+def rerank_ladder(cfg):
+    """Rerank depths tried in order until recall reaches the target.  Extra-bit codes estimate
+    closely enough that no rerank (0, the reference's own output) or a short one may do."""
+    if cfg.get("bits_per_dim", 1) > 1:
+        return (0, 20, 50) + RERANK_LADDER
+    return RERANK_LADDER
 RECALL_TARGET = 0.95
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -232,12 +240,14 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
 
 
 def list_scan_used(cfg, world=1):
-    """Whether the library's search of the whole batch takes the list scan (scan_kind 2, popcount
-    modes, padded dim <= 768; the sharded search scans by tiles).  The CPU oracle is told the
-    same."""
+    """Whether the library's search of the whole batch takes the list scan (its auto rule:
+    popcount modes, padded dim <= 768, nq * nprobe >= 16 * nlist; scan_kind 1 / 2 force the tile /
+    list scan; the sharded search scans by tiles).  The CPU oracle is told the same, so that its
+    sample answers like the full batch."""
     dp = (cfg["d"] + 31) // 32 * 32
+    kind = cfg.get("scan_kind", 0)
     able = world == 1 and cfg["query_bits"] in (4, 8) and dp <= 768
-    return able and cfg.get("scan_kind", 0) == 2
+    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 16 * cfg["nlist"]))
 
 
 def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
@@ -289,8 +299,8 @@ def run_reference(args, cfg):
         xn = (X * X).sum(1)
         gt = np.concatenate([np.argpartition(xn[None, :] - 2.0 * (Q[a:a + 100] @ X.T), cfg["k"], axis=1)[:, :cfg["k"]]
                              for a in range(0, ns, 100)])
-        R = RERANK_LADDER[-1]
-        for cand in RERANK_LADDER:
+        R = rerank_ladder(cfg)[-1]
+        for cand in rerank_ladder(cfg):
             _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand, query_bits=cfg["query_bits"],
                               scan_kind=2 if list_scan_used(cfg) else 1)
             recalls[cand] = O.recall(ids, gt)
@@ -448,7 +458,7 @@ def run_ours(args, cfg):
     if args.rerank:
         ladder = [R]
     elif cfg["config"] == 2:
-        ladder = list(RERANK_LADDER)
+        ladder = list(rerank_ladder(cfg))
     else:
         ladder = [min(4096, int(R * f)) for f in (1, 1.5, 2, 3, 4)]
     for cand in ladder:
@@ -636,12 +646,14 @@ def run_ours(args, cfg):
     return 0
 
 
-def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded, lists=False):
+def scan_roofline(ix, Qd, cfg, R_search, flush, steps, dev, seeded, lists=False):
     """Time the scan and rbq_rerank alone on the batch, as the search runs them (lists: the bound
     seeds and the tensor-core list scan; seeded: the nearest probe, then the others from the
     threshold it gives, all-reduced across shards; else one tile scan);
     algorithmic bytes from the actual probed list sizes: sum n_l (D/8 + 12) for the scan,
-    (4D + 8) per candidate the rerank holds."""
+    (4D + 8) per candidate the rerank holds.  Without a rerank (R_search 0) the scan keeps k
+    candidates and there is no rerank line."""
+    R = max(R_search, cfg["k"])
     import ctypes
 
     import torch
@@ -729,7 +741,8 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded, lists=False):
     scanned, admitted = (int(v) for v in stats.cpu().tolist())
     od = torch.empty((nq, cfg["k"]), dtype=torch.float32, device=dev)
     oi = torch.empty((nq, cfg["k"]), dtype=torch.int64, device=dev)
-    rr_ms = timed(lambda: _lib.call("rbq_rerank", h, _ptr(Qd), nq, _ptr(ids), R, cfg["k"], _ptr(od), _ptr(oi), st))
+    rr_ms = timed(lambda: _lib.call("rbq_rerank", h, _ptr(Qd), nq, _ptr(ids), R, cfg["k"], _ptr(od), _ptr(oi), st)) \
+        if R_search > 0 else None
     n_valid = int((ids >= 0).sum().item())
     rr_bytes = n_valid * (4 * d + 8)
     peak, kind = measured_peak()
@@ -757,6 +770,8 @@ def scan_roofline(ix, Qd, cfg, R, flush, steps, dev, seeded, lists=False):
                            "algorithmic bytes per query summed over the batch"),
             "algorithmic_bytes_per_launch": scan_bytes, "probed_vectors_per_launch": vec,
             "launch_ms": round(scan_ms, 4), "prune_admitted_fraction": round(admitted / max(1, scanned), 4)}
+    if rr_ms is None:
+        return roof, None
     ach_r = rr_bytes / (rr_ms / 1000.0) / 1e9
     roof_rr = {"bound": "hbm", "achieved": round(ach_r, 1), "peak": peak, "unit": "GB/s",
                "frac": round(ach_r / peak, 4), "kernel": "rbq rerank_kernel (+ id->key prologue)",
@@ -829,7 +844,7 @@ def main():
     ap.add_argument("--bits", type=int, default=1, choices=range(1, 10),
                     help="code bits per dimension of both arms (1: RaBitQ; 2..9: ExRaBitQ extra bits)")
     ap.add_argument("--scan-kind", type=int, default=0, choices=[0, 1, 2],
-                    help="0: the library's choice (the tile scan), 1: the tile scan, 2: the list scan")
+                    help="0: the library's choice (the list scan for large batches), 1: the tile scan, 2: the list scan")
     ap.add_argument("--nlist", type=int, default=0,
                     help="list count override (reduced-size cases of a configuration's shape; mixtures keep "
                          "one centre per list)")

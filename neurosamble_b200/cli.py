@@ -17,7 +17,9 @@ relaunching the same command as N processes through torch.distributed.run (127.0
 port).  Under torchrun (WORLD_SIZE > 1, one rank per GPU) the lists are sharded over the
 ranks and rank 0 writes the files.
 
-Accepted for compatibility: ``--bits 1`` only and ``--search_mode`` QUANT4 / QUANT8 (popcount
+``--bits B`` (1..9, as the reference's ``bits_per_dim``): 1-bit RaBitQ codes, or ExRaBitQ codes with
+B - 1 extra bits per dimension whose distance ranks the vectors the 1-bit estimate admits;
+``--search_mode`` QUANT4 / QUANT8 (popcount
 estimator over 4- or 8-bit query codes) or LUT16 / LUT32 (fp16 / fp32 tables of the float query,
 the estimate is the candidate distance); ``--strategy
 none`` turns the error-bound prune off, ``centroid_reorder`` keeps it on, with this library's
@@ -92,8 +94,8 @@ def check_args(a: argparse.Namespace) -> str:
         return "need --emb <fp16 file> --n <N> [--d 384]"
     if a.gpus < 1:
         return "--gpus must be >= 1"
-    if a.bits != 1:
-        return f"--bits {a.bits}: only 1-bit RaBitQ codes are implemented"
+    if not 1 <= a.bits <= 9:
+        return f"--bits {a.bits}: bits per dimension must be in [1, 9]"
     if a.search_mode not in SEARCH_MODES:
         return f"--search_mode {a.search_mode}: one of {', '.join(SEARCH_MODES)}"
     if a.topk < 1 or a.batch < 1 or a.nprobe < 1 or a.nlist < 1 or a.rerank < 0:
@@ -142,7 +144,7 @@ def main(argv=None) -> int:
         from .sharded import ShardedIndexIVFRaBitQ
         index = ShardedIndexIVFRaBitQ(D, a.nlist, seed=a.seed, device=local, kmeans_iters=a.kmeans_iters,
                                       max_train_points_per_cluster=a.train_per_cluster, metric=a.metric,
-                                      raw_store=a.raw_store)
+                                      raw_store=a.raw_store, bits_per_dim=a.bits)
         built = False
     elif a.index and os.path.exists(a.index):
         index = read_index(a.index, device=local, metric=a.metric)
@@ -151,7 +153,7 @@ def main(argv=None) -> int:
     else:
         index = IndexIVFRaBitQ(D, a.nlist, seed=a.seed, device=local, kmeans_iters=a.kmeans_iters,
                                max_train_points_per_cluster=a.train_per_cluster, metric=a.metric,
-                               raw_store=a.raw_store)
+                               raw_store=a.raw_store, bits_per_dim=a.bits)
         built = False
     if not built:
         m = min(N, a.train_per_cluster * a.nlist)

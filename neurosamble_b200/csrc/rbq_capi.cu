@@ -753,9 +753,13 @@ struct SearchPlan {
   int lcap;     // its candidate row per query
 };
 
-// Whether a search takes the list scan: scan_kind 2 asks for it; 0 (auto) and 1 take the tile
-// scan, which measures faster at the benchmark shapes (config 2: 4.2 ms against 4.6 ms for the
-// list scan's seed, tensor-core pass, exact pass and overflow rows).
+// The list scan serves batches whose probed lists are shared by at least this many queries on
+// average (at the benchmark shapes it beats the tile scan by 1.4x at D = 128 and 256 and 3.1x at
+// D = 768); smaller batches take the tile scan.
+constexpr int64_t kListScanMinPairsPerList = 16;
+
+// Whether a search takes the list scan: scan_kind 2 asks for it, 1 for the tile scan; 0 (auto)
+// takes the list scan for popcount modes with the prune on when nq * P >= 16 K.
 bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K)
 {
   RBQ_CHECK(scan_kind >= 0 && scan_kind <= 2, RBQ_ERR_INVALID,
@@ -763,10 +767,8 @@ bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int 
   const bool able = (qbits == 4 || qbits == 8) && prune && list_scan_tc_supported(dp);
   RBQ_CHECK(scan_kind != 2 || able, RBQ_ERR_INVALID,
             "list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768");
-  (void)nq;
-  (void)P;
-  (void)K;
-  return scan_kind == 2;
+  if (scan_kind == 2) return true;
+  return scan_kind == 0 && able && nq * (int64_t)P >= kListScanMinPairsPerList * K;
 }
 
 int list_scan_cap(int R)
@@ -838,8 +840,8 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   sp.seeded = sp.qbits < 16 && (p.seeded < 0 ? sp.slices > 1 : p.seeded > 0);  // no bound seed in LUT modes
   sp.lists = use_list_scan(p.scan_kind, sp.qbits, sp.prune, ix.Dp, nq, sp.P, ix.K);
   sp.lcap = list_scan_cap(sp.R);
-  if (sp.lists) {
-    sp.slices = 1;
+  if (sp.lists) {  // two key rows per query: the nearest probe's tile scan and the list scan
+    sp.slices = 2;
     sp.seeded = false;
   }
   return sp;
@@ -891,14 +893,19 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
 // seed-only launch over that list) instead of finding its own: split slices then prune from
 // their first vector.
 // Scratch of a list scan over nq queries with P probe columns.
+// Slices of the tile scan that answers the queries whose candidate row overflowed (their
+// lists split four ways, so that a far query's many admitted vectors spread over four blocks).
+constexpr int kListFallbackSlices = 4;
+
 struct ListScanScratch {
   int8_t* qcodes;
   int32_t *list_start, *item_start, *cursor, *pair_q, *cand_cnt;
   float* pair_g;
   unsigned long long* cand;
+  unsigned long long* fall;  // [nq, kListFallbackSlices, R] keys of the overflowed queries' slices
 };
 
-ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int P, int cap)
+ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int P, int cap, int R)
 {
   ListScanScratch w;
   w.qcodes = sc.get<int8_t>((size_t)nq * ix.Dp);
@@ -909,6 +916,7 @@ ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int 
   w.pair_g = sc.get<float>((size_t)nq * P);
   w.cand_cnt = sc.get<int32_t>((size_t)nq);
   w.cand = sc.get<unsigned long long>((size_t)nq * cap);
+  w.fall = sc.get<unsigned long long>((size_t)nq * kListFallbackSlices * R);
   return w;
 }
 
@@ -918,7 +926,7 @@ ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int 
 void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbits, const float* delta,
                const float* k1, int64_t nq, const int32_t* probes, const float* g, int nprobe, int pstride,
                const float* tau0, int R, int cap, const ListScanScratch& w, unsigned long long* out_keys,
-               uint64_t* stats, cudaStream_t s)
+               uint64_t* stats, cudaStream_t s, int out_slices = 1, int out_slice = 0)
 {
   if (nq <= 0) return;
   launch_planes_to_codes(planes, nq, ix.W, qbits, w.qcodes, s);
@@ -971,17 +979,22 @@ void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbi
   ea.R = R;
   ea.nq = nq;
   ea.out_keys = out_keys;
+  ea.out_slices = out_slices;
+  ea.out_slice = out_slice;
   launch_exact_topr(ea, s);
-  // rows that overflowed: the tile scan with the same fixed thresholds (its blocks for the other
-  // queries return at once; the list scan already counted every admitted vector)
+  // rows that overflowed: the tile scan with the same fixed thresholds, in slices merged into the
+  // query's row (its blocks for the other queries return at once; the list scan already counted
+  // every admitted vector).  Slices keep the answer: each holds the R best of its part of a set.
+  const int fs = std::min(nprobe, kListFallbackSlices);
   ScanArgs fa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, nprobe, R,
-                                std::max(next_pow2(1024), next_pow2(R + kScanTile)), 1, 1, out_keys, nullptr, qbits);
+                                std::max(next_pow2(1024), next_pow2(R + kScanTile)), 1, fs, w.fall, nullptr, qbits);
   fa.pstride = pstride;
   fa.tau0 = tau0;
   fa.fixed_tau = 1;
   fa.over_cnt = w.cand_cnt;
   fa.over_cap = cap;
   launch_scan(fa, s);
+  launch_merge_sorted_keys(w.fall, nq, fs, R, out_keys, out_slices, out_slice, w.cand_cnt, cap, s);
 }
 
 void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const uint32_t* planes, const float* delta,
@@ -991,14 +1004,32 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
 {
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
                                 keys_s, stats, sp.qbits);
-  if (sp.lists) {  // thresholds: the bound seed over the leading probed lists holding >= R vectors
+  if (sp.lists) {
+    // 1. the bound seed over the leading probed lists holding >= R vectors
     ScanArgs a0 = sa;
     a0.slices = 1;
     a0.stats = nullptr;
     a0.tau_out = tau_a;
     launch_scan(a0, s);
-    list_scan(ix, Qr, planes, sp.qbits, delta, k1, nq, probes, g, sp.P, sp.P, tau_a, sp.R, sp.lcap, *lw, keys,
-              stats, s);
+    // 2. the tile scan of the nearest probe from that seed -> keys_s[q][0]
+    ScanArgs aa = sa;
+    aa.nprobe = 1;
+    aa.pstride = sp.P;
+    aa.slices = 1;
+    aa.tau0 = tau_a;
+    aa.out_keys = keys_s;
+    aa.out_slices = sp.P > 1 ? 2 : 1;
+    launch_scan(aa, s);
+    if (sp.P == 1) {
+      RBQ_CUDA(cudaMemcpyAsync(keys, keys_s, (size_t)nq * sp.R * 8, cudaMemcpyDeviceToDevice, s));
+      return;
+    }
+    // 3. the threshold fixed for the other probes: the seed, or the nearest list's R-th distance
+    launch_tighten_tau(keys_s, nq, 2 * sp.R, sp.R, tau_a, s);
+    // 4. the list scan of probes 1..P-1 -> keys_s[q][1]; 5. the R smallest of both
+    list_scan(ix, Qr, planes, sp.qbits, delta, k1, nq, probes + 1, g + 1, sp.P - 1, sp.P, tau_a, sp.R, sp.lcap,
+              *lw, keys_s, stats, s, 2, 1);
+    launch_merge_sorted_keys(keys_s, nq, 2, sp.R, keys, 1, 0, nullptr, 0, s);
     return;
   }
   if (qorder_buf && nq >= kQueryOrderMinBatch) {  // [K + 2] counts, then [nq] order
@@ -1054,7 +1085,7 @@ void run_search(Index& ix, const rbq_search_params_t& params, const float* Q, in
   float* tau_a = sp.seeded || sp.lists ? sc.get<float>((size_t)chunk) : nullptr;
   int32_t* qorder = chunk >= kQueryOrderMinBatch ? sc.get<int32_t>((size_t)ix.K + 2 + chunk) : nullptr;
   ListScanScratch lw{};
-  if (sp.lists) lw = list_scan_scratch(sc, ix, chunk, sp.P, sp.lcap);
+  if (sp.lists) lw = list_scan_scratch(sc, ix, chunk, sp.P, sp.lcap, sp.R);
   for (int64_t a = 0; a < nq; a += chunk) {
     const int64_t cn = std::min(chunk, nq - a);
     const float* Qc = Q + a * ix.D;
@@ -2302,7 +2333,7 @@ int rbq_scan_lists(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
     const int cap = list_scan_cap(R);
     Scratch sc(s);
     unsigned long long* keys = sc.get<unsigned long long>((size_t)nq * R);
-    const ListScanScratch w = list_scan_scratch(sc, ix, nq, nprobe, cap);
+    const ListScanScratch w = list_scan_scratch(sc, ix, nq, nprobe, cap, R);
     list_scan(ix, Qr_dev, planes_dev, qb, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe,
               probe_stride > 0 ? probe_stride : nprobe, tau0_dev, R, cap, w, keys, stats_dev, s);
     launch_keys_to_ids(keys, nq * R, cand_ids_dev, cand_dist_dev, s);

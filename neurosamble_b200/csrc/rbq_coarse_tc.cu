@@ -589,23 +589,30 @@ __global__ void __launch_bounds__(kFtThreads, 1)
 // ---------------------------------------------------------------------------------------
 // List scan on the tensor cores.  One CTA (256 threads) per work item: up to 128 queries
 // probing one list (the accumulator's 128 rows = TMEM lanes) against all of the list's vectors,
-// in tiles of 128 vectors (accumulator columns).  Operands are int8 in shared memory, K-major
-// with the 128-byte swizzle, one 128-byte chunk of dimensions per [rows x 128 B] region: A holds
-// the queries' codes (copied once), B the tile's code bits expanded to bytes 0 / 1 (rewritten
-// per tile).  One thread issues the kind::i8 MMAs (K = 32 bytes each) and commits them to an
-// mbarrier; then the 8 warps read the int32 accumulator (warp w: TMEM lanes 32 (w % 4).., column
-// half w / 4), form the estimate and its lower bound from the integer exactly as the popcount
-// scan does, and append the admitted vectors (low < tau0[q]) to their query's candidate row.
-// The wait on the MMAs is bounded: on time-out the kernel records an error code, waits once more
-// (bounded) for the MMAs, frees its TMEM and returns.
+// in tiles of N vectors (accumulator columns; N = 128, or 64 above 512 padded dims).  Operands
+// are int8 in shared memory, K-major with the 128-byte swizzle, one 128-byte chunk of dimensions
+// per [rows x 128 B] region: A holds the queries' codes (copied once), B a tile's code bits
+// expanded to bytes 0 / 1.  The tiles are pipelined with one block barrier each: in step t every
+// thread expands tile t + 1 into the other B buffer (from code words it loaded during step t - 1)
+// and issues the loads of tile t + 2; after the barrier one thread issues tile t + 1's kind::i8
+// MMAs into the other TMEM accumulator, and every thread waits for tile t's MMAs and reads its
+// accumulator (warp w: TMEM lanes 32 (w % 4).., column half w / 4), forms the estimate and its
+// lower bound from the integer exactly as the popcount scan does, and appends admitted vectors
+// (low < tau0[q]) to their query's candidate row.  Column data (factors, slot) is kept for three
+// tiles, so the single barrier separates every writer from its readers.  Every mbarrier wait is
+// bounded; on time-out the kernel records an error code, stops, waits (bounded) for the MMAs it
+// issued, frees its TMEM and returns.
 // ---------------------------------------------------------------------------------------
 constexpr int kLsM = kListScanRows;  // queries per work item
-constexpr int kLsN = 128;            // vectors per tile
 constexpr int kLsThreads = 256;
-constexpr int kLsMaxChunks = 6;      // padded dimension <= 768 (A + B = 192 KB)
-// kind::i8: D s32 (2), A s8 (1), B s8 (1), both K-major, N = 128, M = 128.
-constexpr uint32_t kLsIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLsN >> 3) << 17) |
-                              ((uint32_t)(kLsM >> 4) << 24);
+constexpr int kLsMaxChunks = 6;      // padded dimension <= 768
+
+// kind::i8: D s32 (2), A s8 (1), B s8 (1), both K-major, N, M = 128.
+template <int N>
+constexpr uint32_t ls_idesc()
+{
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kLsM >> 4) << 24);
+}
 
 __device__ __forceinline__ void tc_mma_i8(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t acc)
@@ -639,19 +646,21 @@ __device__ __forceinline__ void expand_word(uint32_t c, uint32_t (&o)[8])
   for (int i = 0; i < 8; ++i) o[i] = (((r >> (4 * i)) & 0xFu) * 0x00204081u) & 0x01010101u;
 }
 
+template <int N>
 __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScanArgs a)
 {
+  constexpr int kWpt = N * 24 / kLsThreads;  // code words per thread per tile (W <= 24)
   extern __shared__ unsigned char ls_smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(ls_smem_raw) + 1023) & ~(uintptr_t)1023);
   const int Kc = (a.Dp + 127) >> 7;
-  unsigned char* As = base;                    // [Kc][kLsM rows][128 B]
-  unsigned char* Bs = base + Kc * kLsM * 128;  // [Kc][kLsN rows][128 B]
+  unsigned char* As = base;                           // [Kc][kLsM rows][128 B]
+  unsigned char* Bs0 = base + Kc * kLsM * 128;        // [2][Kc][N rows][128 B]
+  const int b_stride = Kc * N * 128;
   __shared__ int s_q[kLsM];
   __shared__ float s_g[kLsM], s_sg[kLsM], s_dl[kLsM], s_k1[kLsM], s_tau[kLsM];
-  __shared__ uint32_t s_slot[kLsN];
-  __shared__ float s_fa[kLsN], s_fr[kLsN], s_fe[kLsN];
-  __shared__ __align__(8) unsigned long long s_bar;
+  __shared__ float4 s_col[3][N];  // per tile column: f_add, f_rescale, f_err, slot bits
+  __shared__ __align__(8) unsigned long long s_bar[2];
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail, s_l, s_p0, s_rows;
 
@@ -681,13 +690,15 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
   const int rows = s_rows, p0 = s_p0;
   const int64_t lb = a.list_off[l];
   const int nl = (int)(a.list_off[l + 1] - lb);
+  const int W = a.W;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"((uint32_t)kLsN));
+                 "r"((uint32_t)(2 * N)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(smem_u32(&s_bar), 1);
+    mbar_init(smem_u32(&s_bar[0]), 1);
+    mbar_init(smem_u32(&s_bar[1]), 1);
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -716,18 +727,70 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
     if (r < rows && byte < a.Dp) v = __ldg(reinterpret_cast<const uint4*>(a.qcodes + (size_t)s_q[r] * a.Dp + byte));
     *reinterpret_cast<uint4*>(As + (u >> 3) * (kLsM * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4)) = v;
   }
-  // B: the padding past Dp in the last chunk stays zero for every tile.
+  // B: the padding past Dp in the last chunk stays zero in both buffers.
   if (a.Dp < Kc * 128)
-    for (int i = tid; i < kLsN * 8; i += kLsThreads) {
-      const int v = i >> 3, u = i & 7;
+    for (int i = tid; i < 2 * N * 8; i += kLsThreads) {
+      const int bb = i / (N * 8), v = (i >> 3) % N, u = i & 7;
       if ((Kc - 1) * 128 + (u << 4) >= a.Dp)
-        *reinterpret_cast<uint4*>(Bs + (Kc - 1) * (kLsN * 128) + v * 128 + ((u ^ (v & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(Bs0 + bb * b_stride + (Kc - 1) * (N * 128) + v * 128 + ((u ^ (v & 7)) << 4)) =
             make_uint4(0u, 0u, 0u, 0u);
     }
+  const int ntiles = (nl + N - 1) / N;
+  uint32_t cw[kWpt];
+  auto load_codes = [&](int t) {  // code words of tile t into registers (0 past the list)
+    const int t0 = t * N;
+#pragma unroll
+    for (int j = 0; j < kWpt; ++j) {
+      const int i = tid + j * kLsThreads;
+      const int v = i / W;
+      cw[j] = (i < N * W && t0 + v < nl) ? __ldg(a.codes + (lb + t0) * W + i) : 0u;
+    }
+  };
+  auto store_tile = [&](int t) {  // expand tile t into B[t % 2], its column data into s_col[t % 3]
+    unsigned char* Bs = Bs0 + (t & 1) * b_stride;
+    const int t0 = t * N;
+#pragma unroll
+    for (int j = 0; j < kWpt; ++j) {
+      const int i = tid + j * kLsThreads;
+      if (i < N * W) {
+        const int v = i / W, w = i - v * W;
+        uint32_t o[8];
+        expand_word(cw[j], o);
+        const int byte = w << 5, u0 = (byte & 127) >> 4;
+        unsigned char* rowp = Bs + (byte >> 7) * (N * 128) + v * 128;
+        *reinterpret_cast<uint4*>(rowp + ((u0 ^ (v & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ (v & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+    for (int v = tid; v < N; v += kLsThreads)
+      if (t0 + v < nl) {
+        const int64_t slot = lb + t0 + v;
+        s_col[t % 3][v] = make_float4(__ldg(a.fadd + slot), __ldg(a.frescale + slot), __ldg(a.ferr + slot),
+                                      __uint_as_float((uint32_t)slot));
+      }
+  };
+  auto issue = [&](int t) {  // thread 0: tile t's MMAs into accumulator t % 2, committed to s_bar[t % 2]
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t a_addr = smem_u32(As), b_addr = smem_u32(Bs0 + (t & 1) * b_stride);
+    const uint32_t d = s_tmem + (uint32_t)((t & 1) * N);
+    for (int c = 0; c < Kc; ++c)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)  // 32 int8 values (32 bytes) per MMA
+        tc_mma_i8(d, sw128_desc(a_addr + c * (kLsM * 128) + ks * 32), sw128_desc(b_addr + c * (N * 128) + ks * 32),
+                  ls_idesc<N>(), (c > 0 || ks > 0) ? 1u : 0u);
+    tc_commit(smem_u32(&s_bar[t & 1]));
+  };
+  if (ntiles > 0) {
+    load_codes(0);
+    store_tile(0);
+    if (ntiles > 1) load_codes(1);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
+  if (tid == 0 && ntiles > 0) issue(0);
   const int quarter = warp & 3, half = warp >> 2;
   const int row = quarter * 32 + lane;
   const bool row_ok = row < rows;
@@ -735,79 +798,64 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
   const float g = s_g[row], sg = s_sg[row], dl = s_dl[row], kk = s_k1[row], tau = s_tau[row];
   const unsigned long long gbits = (unsigned long long)__float_as_uint(g) << 32;
   unsigned long long n_admit = 0;
-  int tile = 0;
-  for (int t0 = 0; t0 < nl; t0 += kLsN, ++tile) {
-    const int tn = min(kLsN, nl - t0);
-    for (int i = tid; i < kLsN * a.W; i += kLsThreads) {
-      const int v = i / a.W, w = i - v * a.W;
-      uint32_t o[8];
-      expand_word(v < tn ? __ldg(a.codes + (lb + t0 + v) * a.W + w) : 0u, o);
-      const int byte = w << 5, u0 = (byte & 127) >> 4;
-      unsigned char* rowp = Bs + (byte >> 7) * (kLsN * 128) + v * 128;
-      *reinterpret_cast<uint4*>(rowp + ((u0 ^ (v & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-      *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ (v & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+  int issued = ntiles > 0 ? 1 : 0;
+  for (int t = 0; t < ntiles; ++t) {
+    if (t + 1 < ntiles) {
+      store_tile(t + 1);  // B[(t+1) % 2] was read by tile t - 1's MMAs, which every thread waited for
+      if (t + 2 < ntiles) load_codes(t + 2);
     }
-    for (int v = tid; v < tn; v += kLsThreads) {
-      const int64_t slot = lb + t0 + v;
-      s_slot[v] = (uint32_t)slot;
-      s_fa[v] = __ldg(a.fadd + slot);
-      s_fr[v] = __ldg(a.frescale + slot);
-      s_fe[v] = __ldg(a.ferr + slot);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy stores -> MMA reads
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_addr = smem_u32(As), b_addr = smem_u32(Bs);
-      for (int c = 0; c < Kc; ++c)
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)  // 32 int8 values (32 bytes) per MMA
-          tc_mma_i8(tmem, sw128_desc(a_addr + c * (kLsM * 128) + ks * 32),
-                    sw128_desc(b_addr + c * (kLsN * 128) + ks * 32), kLsIdesc, (c > 0 || ks > 0) ? 1u : 0u);
-      tc_commit(smem_u32(&s_bar));
-      if (!mbar_wait(smem_u32(&s_bar), (uint32_t)(tile & 1))) {
-        s_fail = 1;
-        atomicExch(a.err, 4);
-      }
-    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (s_fail) break;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (tid == 0 && t + 1 < ntiles) {
+      issue(t + 1);  // accumulator (t+1) % 2 was last read in step t - 1, before this barrier
+      ++issued;
+    }
+    if (!mbar_wait(smem_u32(&s_bar[t & 1]), (uint32_t)((t >> 1) & 1))) {
+      s_fail = 1;
+      atomicExch(a.err, 4);
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int tn = min(N, nl - t * N);
+    const float4* col = s_col[t % 3];
 #pragma unroll 1
-    for (int j = 0; j < 2; ++j) {
-      const int col0 = half * (kLsN / 2) + j * 32;
+    for (int j = 0; j < N / 64; ++j) {
+      const int col0 = half * (N / 2) + j * 32;
       uint32_t acc[32];
-      tc_ld32_u(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, acc);
+      tc_ld32_u(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((t & 1) * N + col0), acc);
       if (row_ok && col0 < tn) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int col = col0 + i;
+          const float4 c = col[col0 + i];
           const float ip = __fmul_rn((float)(int32_t)acc[i], dl);
-          const float base_d = __fadd_rn(s_fa[col], g);
-          const float est = __fadd_rn(base_d, __fmul_rn(s_fr[col], __fadd_rn(ip, kk)));
-          const float low = __fsub_rn(est, __fmul_rn(s_fe[col], sg));
-          if (col < tn && low < tau) {
+          const float base_d = __fadd_rn(c.x, g);
+          const float est = __fadd_rn(base_d, __fmul_rn(c.y, __fadd_rn(ip, kk)));
+          const float low = __fsub_rn(est, __fmul_rn(c.z, sg));
+          if (low < tau && col0 + i < tn) {
             ++n_admit;
             const int pos = atomicAdd(a.cand_cnt + q, 1);
-            if (pos < a.cap) a.cand[(size_t)q * a.cap + pos] = gbits | s_slot[col];
+            if (pos < a.cap) a.cand[(size_t)q * a.cap + pos] = gbits | __float_as_uint(c.w);
           }
         }
       }
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
   }
-  if (s_fail && tid == 0) mbar_wait(smem_u32(&s_bar), (uint32_t)(tile & 1));
+  // on failure: wait (bounded) for the last MMAs issued before freeing the accumulators
+  __syncthreads();
+  if (s_fail && tid == 0 && issued > 0) mbar_wait(smem_u32(&s_bar[(issued - 1) & 1]), (uint32_t)(((issued - 1) >> 1) & 1));
   if (a.stats) {
     unsigned long long s1 = n_admit;
     for (int off = 16; off; off >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, off);
     if (lane == 0 && s1) atomicAdd(a.stats + 1, s1);
     if (tid == 0) atomicAdd(a.stats + 0, (unsigned long long)rows * (unsigned long long)nl);
   }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kLsN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * N)));
   }
 }
 
@@ -905,17 +953,27 @@ void launch_coarse_scores_tc(const float* A, int64_t nq, const float* C, const f
 
 bool list_scan_tc_supported(int dp) { return dp % 32 == 0 && dp >= 32 && dp <= kLsMaxChunks * 128; }
 
+template <int N>
+static void launch_list_scan_tc_n(const ListScanArgs& a, int64_t max_items, cudaStream_t s)
+{
+  const int Kc = (a.Dp + 127) / 128;
+  // A, two B buffers; at least a quarter of the shared memory per CTA, so that at most two CTAs
+  // (2 x 2N <= 512 TMEM columns) share an SM
+  const size_t smem = std::max<size_t>((size_t)Kc * (kLsM + 2 * N) * 128 + 1024, 80 * 1024);
+  RBQ_CUDA(cudaFuncSetAttribute(list_scan_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  list_scan_tc_kernel<N><<<(unsigned)max_items, kLsThreads, smem, s>>>(a);
+  RBQ_LAUNCHED();
+}
+
 void launch_list_scan_tc(const ListScanArgs& a, int64_t max_items, cudaStream_t s)
 {
   if (max_items <= 0) return;
   RBQ_CHECK(list_scan_tc_supported(a.Dp), RBQ_ERR_INVALID, "list scan: padded dim must be a multiple of 32, <= 768");
   RBQ_CHECK(max_items <= 0x7fffffff, RBQ_ERR_INVALID, "list scan: too many work items");
-  const int Kc = (a.Dp + 127) / 128;
-  // at least a quarter of the shared memory per CTA: at most 4 CTAs (4 x 128 TMEM columns) per SM
-  const size_t smem = std::max<size_t>((size_t)Kc * (kLsM + kLsN) * 128 + 1024, 56 * 1024);
-  RBQ_CUDA(cudaFuncSetAttribute(list_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  list_scan_tc_kernel<<<(unsigned)max_items, kLsThreads, smem, s>>>(a);
-  RBQ_LAUNCHED();
+  if (a.Dp <= 512)
+    launch_list_scan_tc_n<128>(a, max_items, s);
+  else
+    launch_list_scan_tc_n<64>(a, max_items, s);
 }
 
 }  // namespace rbq

@@ -282,6 +282,10 @@ struct ScanArgs {
   // scan's candidate rows that overflowed); the other blocks return at once.
   const int32_t* over_cnt = nullptr;
   int over_cap = 0;
+  // Output rows: query q's slice s goes to out_keys + (q * out_slices + out_slice + s) * R
+  // (out_slices 0: slices), so that two scans can fill the halves of one [nq, 2, R] buffer.
+  int out_slices = 0;
+  int out_slice = 0;
 };
 // ---------------------------------------------------------------------------------------
 // List scan on the tensor cores (fixed per-query threshold).  For every (list, query) pair of
@@ -343,9 +347,17 @@ struct ExactArgs {
   int cap;
   int R;
   int64_t nq;
-  unsigned long long* out_keys;
+  unsigned long long* out_keys;  // query q's R keys at out_keys + (q * out_slices + out_slice) * R
+  int out_slices = 1;
+  int out_slice = 0;
 };
 void launch_exact_topr(const ExactArgs& a, cudaStream_t s);
+// tau[q] = min(tau[q], the R-th key's distance of keys[q * stride .. + R)) when that key is present.
+// The R smallest keys of `parts` ascending key rows per query ([nq, parts, R]) into row
+// out + (q * out_rows + out_row) * R; with over_cnt only the queries with over_cnt[q] > over_cap.
+void launch_merge_sorted_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,
+                              int out_rows, int out_row, const int32_t* over_cnt, int over_cap, cudaStream_t s);
+void launch_tighten_tau(const unsigned long long* keys, int64_t nq, int stride, int R, float* tau, cudaStream_t s);
 
 // qorder[0..nq) = the queries sorted by their nearest probe probes[q * pstride] (ascending list id;
 // queries without probes last), so that queries searching the same region of the index run at

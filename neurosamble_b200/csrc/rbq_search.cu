@@ -1357,7 +1357,8 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   for (int i = cnt + tid; i < r2; i += kScanThreads) keys[i] = kEmptyKey;
   __syncthreads();
   block_bitonic_sort(keys, r2);
-  unsigned long long* out = a.out_keys + ((size_t)q * a.slices + slice) * a.R;
+  unsigned long long* out =
+      a.out_keys + ((size_t)q * (a.out_slices ? a.out_slices : a.slices) + a.out_slice + slice) * a.R;
   for (int i = tid; i < a.R; i += kScanThreads) out[i] = i < cnt ? keys[i] : kEmptyKey;
   if (a.stats) {  // every vector of the slice is scanned once: the block adds `total`
     unsigned long long s1 = n_admit;
@@ -1406,8 +1407,8 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
   RBQ_CHECK(a.qbits == 4 || a.qbits == 8 || a.qbits == 16 || a.qbits == 32, RBQ_ERR_INVALID,
             "scan: query bits must be 4 (QUANT4), 8 (QUANT8), 16 (LUT16) or 32 (LUT32)");
   RBQ_CHECK(!(a.tau_out && a.qbits >= 16), RBQ_ERR_INVALID, "scan: the LUT modes have no bound seed");
-  RBQ_CHECK(!a.fixed_tau || (a.slices == 1 && !a.init_keys && !a.tau_out), RBQ_ERR_INVALID,
-            "scan: a fixed-threshold scan takes one slice and no initial candidates");
+  RBQ_CHECK(!a.fixed_tau || (!a.init_keys && !a.tau_out), RBQ_ERR_INVALID,
+            "scan: a fixed-threshold scan takes no initial candidates");
   RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
             "scan: more than 2^31 vectors on one shard");
   switch (a.W) {
@@ -1664,8 +1665,24 @@ __global__ void __launch_bounds__(kExactThreads) exact_topr_kernel(const ExactAr
   for (int i = cnt + tid; i < r2; i += kExactThreads) keys[i] = kEmptyKey;
   __syncthreads();
   block_bitonic_sort(keys, r2);
-  unsigned long long* out = a.out_keys + q * a.R;
+  unsigned long long* out = a.out_keys + ((size_t)q * a.out_slices + a.out_slice) * a.R;
   for (int i = tid; i < a.R; i += kExactThreads) out[i] = i < cnt ? keys[i] : kEmptyKey;
+}
+
+__global__ void tighten_tau_kernel(const unsigned long long* __restrict__ keys, int64_t nq, int stride, int R,
+                                   float* __restrict__ tau)
+{
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const unsigned long long k = keys[q * stride + R - 1];
+  if (k != kEmptyKey) tau[q] = fminf(tau[q], from_ordered_bits((uint32_t)(k >> 32)));
+}
+
+void launch_tighten_tau(const unsigned long long* keys, int64_t nq, int stride, int R, float* tau, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  tighten_tau_kernel<<<(unsigned)ceil_div(nq, 256), 256, 0, s>>>(keys, nq, stride, R, tau);
+  RBQ_LAUNCHED();
 }
 
 void launch_exact_topr(const ExactArgs& a, cudaStream_t s)
@@ -1714,6 +1731,61 @@ __global__ void __launch_bounds__(256) merge_keys_kernel(const unsigned long lon
   __syncthreads();
   block_bitonic_sort(res, r2);
   for (int i = threadIdx.x; i < R; i += blockDim.x) out[q * R + i] = res[i];
+}
+
+// The R smallest keys of `parts` ascending rows of R keys per query (in [nq, parts, R]), without a
+// sort: a key at rank r of row p lands at r plus, per other row, its count of keys below (rows
+// after p) or up to (rows before p) the key, found by binary search in shared memory.  The result
+// row of query q is out + (q * out_rows + out_row) * R.  With over_cnt, only queries whose
+// over_cnt[q] exceeds over_cap are merged (the others' rows are left as they are).
+__global__ void __launch_bounds__(256) merge_sorted_keys_kernel(const unsigned long long* __restrict__ in,
+                                                                int parts, int R, unsigned long long* __restrict__ out,
+                                                                int out_rows, int out_row,
+                                                                const int32_t* __restrict__ over_cnt, int over_cap)
+{
+  extern __shared__ unsigned long long ms[];  // [parts * R] rows, then [R] result
+  const int64_t q = blockIdx.x;
+  if (over_cnt && over_cnt[q] <= over_cap) return;
+  unsigned long long* res = ms + (size_t)parts * R;
+  const int tot = parts * R;
+  for (int i = threadIdx.x; i < tot; i += blockDim.x) ms[i] = in[q * tot + i];
+  for (int i = threadIdx.x; i < R; i += blockDim.x) res[i] = kEmptyKey;
+  __syncthreads();
+  for (int i = threadIdx.x; i < tot; i += blockDim.x) {
+    const unsigned long long e = ms[i];
+    if (e == kEmptyKey) continue;
+    const int p = i / R;
+    int pos = i - p * R;
+    for (int o = 0; o < parts && pos < R; ++o) {
+      if (o == p) continue;
+      const unsigned long long* row = ms + o * R;
+      int lo = 0, hi = R;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (row[mid] < e || (o < p && row[mid] == e))
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      pos += lo;
+    }
+    if (pos < R) res[pos] = e;
+  }
+  __syncthreads();
+  unsigned long long* dst = out + ((size_t)q * out_rows + out_row) * R;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) dst[i] = res[i];
+}
+
+void launch_merge_sorted_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,
+                              int out_rows, int out_row, const int32_t* over_cnt, int over_cap, cudaStream_t s)
+{
+  if (nq <= 0) return;
+  const size_t smem = ((size_t)parts + 1) * R * 8;
+  RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "merge: too many candidates per query");
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(merge_sorted_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  merge_sorted_keys_kernel<<<(unsigned)nq, 256, smem, s>>>(in, parts, R, out, out_rows, out_row, over_cnt, over_cap);
+  RBQ_LAUNCHED();
 }
 
 void launch_merge_keys(const unsigned long long* in, int64_t nq, int parts, int R, unsigned long long* out,

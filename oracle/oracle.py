@@ -463,15 +463,20 @@ def assign(X, C) -> np.ndarray:
     return labels
 
 
+# The list scan (rbq_search_params_t.scan_kind): batches whose probed lists are shared by at least
+# this many queries on average take it under scan_kind 0 (auto).
+LIST_SCAN_MIN_PAIRS_PER_LIST = 16
+
+
 def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K) -> bool:
-    """The library's choice between the tile scan and the list scan (fixed thresholds): the list
-    scan when scan_kind is 2, the tile scan under 0 (auto) and 1."""
+    """The library's choice between the tile scan and the list scan: 2 the list scan, 1 the tile
+    scan, 0 (auto) the list scan for popcount modes with the prune on when nq * P >= 16 K."""
     able = query_bits in (4, 8) and bool(prune) and dp % 32 == 0 and dp <= 768
     if scan_kind == 2:
         if not able:
             raise ValueError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
         return True
-    return False
+    return scan_kind == 0 and able and nq * nprobe >= LIST_SCAN_MIN_PAIRS_PER_LIST * K
 
 
 def list_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tau0, shard_rank=0, shard_count=1,
@@ -485,6 +490,26 @@ def list_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tau0, shard_
                 owner=owner)
 
 
+def list_search_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None, shard_rank=0,
+                     shard_count=1, owner=None):
+    """The scan of a search with scan_kind 2: (1) the bound seed over the leading probed lists
+    holding >= R vectors; (2) the tile scan of the nearest probe from that seed; (3) the threshold
+    for the other probes = min(seed, the nearest list's R-th distance when it found R); (4) the
+    list scan of probes 1..P-1 with that fixed threshold; (5) the R smallest keys of (2) and (4).
+    Returns (ids, dist, stats) like scan(..., with_stats=True)."""
+    probes, g = _c(probes, np.int32), _c(g, np.float32)
+    seed = bound_seed(ix, planes, delta, k1, probes, g, R, shard_rank, shard_count, owner)
+    ia, da, sa = scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, 1, 1, shard_rank,
+                      shard_count, with_stats=True, tau0=seed, owner=owner)
+    if probes.shape[1] == 1:
+        return ia, da, sa
+    tau1 = np.where(ia[:, R - 1] >= 0, np.minimum(seed, da[:, R - 1]), seed).astype(np.float32)
+    ib, db, sb = list_scan(ix, Qr, planes, delta, k1, probes[:, 1:], g[:, 1:], R, tau1, shard_rank, shard_count,
+                           with_stats=True, owner=owner)
+    mi, md = merge_candidates([(ia, da), (ib, db)], R)
+    return mi, md, sa + sb
+
+
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
            shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None, query_bits=4,
            scan_kind=0):
@@ -496,9 +521,8 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
     scan's top-k estimates (the reference behaviour).  query_bits 8 (QUANT8) quantises the
     queries to 8 bits with ix.t8 (set it to query_scale(dp, seed, 7) of the index); 16 / 32
     (LUT16 / LUT32) estimate with fp16 / fp32 tables of the float query (one pass, no seed).
-    scan_kind (rbq_search_params_t.scan_kind): 0 auto, 1 tile scan, 2 list scan (thresholds fixed
-    at the bound seed over the leading probed lists holding >= R vectors); the sharded search's
-    pipeline (exchange=True) scans by tiles."""
+    scan_kind (rbq_search_params_t.scan_kind): 0 auto, 1 tile scan, 2 list scan (list_search);
+    the sharded search's pipeline (exchange=True) scans by tiles."""
     Q = _c(Q, np.float32)
     Qr = rotate(Q, ix.P)
     probes, g = coarse(Qr, ix.c_rot, nprobe)
@@ -517,9 +541,7 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
         return (dist, ids, res[2]) if with_stats else (dist, ids)
     two = slices > 1 if seeded < 0 else seeded > 0
     if not exchange and uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k):
-        tau = bound_seed(ix, planes, delta, k1, probes, g, R, shard_rank, shard_count, owner)
-        res = list_scan(ix, Qr, planes, delta, k1, probes, g, R, tau, shard_rank, shard_count, with_stats=True,
-                        owner=owner)
+        res = list_search_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, shard_rank, shard_count, owner)
     elif exchange or two:
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
                           shard_count, with_stats=True, exchange=exchange, owner=owner)

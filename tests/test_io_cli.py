@@ -74,7 +74,8 @@ def test_neighbor_files_round_trip(tmp_path):
 @pytest.mark.parametrize("argv,msg", [
     ([], "need --emb"),
     (["--emb", "x.f16"], "need --emb"),
-    (["--emb", "x.f16", "--n", "10", "--bits", "2"], "only 1-bit"),
+    (["--emb", "x.f16", "--n", "10", "--bits", "10"], "must be in [1, 9]"),
+    (["--emb", "x.f16", "--n", "10", "--bits", "0"], "must be in [1, 9]"),
     (["--emb", "x.f16", "--n", "10", "--search_mode", "LUT64"], "one of QUANT4, QUANT8, LUT16, LUT32"),
     (["--emb", "x.f16", "--n", "10", "--topk", "0"], "--topk"),
 ])
@@ -91,6 +92,7 @@ def test_cli_defaults_follow_the_reference():
     assert (a.search_mode, a.strategy, a.out_nbr, a.out_dist, a.rerank) == ("QUANT4", "centroid_reorder",
                                                                              "neighbors.i64", "dists.f32", 0)
     assert cli.check_args(a) == ""
+    assert cli.check_args(cli.parse_args(["--emb", "e", "--n", "3", "--bits", "4"])) == ""
 
 
 @pytest.mark.gpu

@@ -45,7 +45,10 @@ def test_fixed_threshold_keeps_the_tile_scan_answer(oracle, small):
 
 def test_auto_rule():
     from oracle import oracle as O
-    assert not O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)  # auto: the tile scan
+    assert O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)      # 312 queries per list
+    assert not O.uses_list_scan(0, 4, 1, 256, 64, 32, 1024)     # 2 per list: the tile scan
+    assert not O.uses_list_scan(0, 16, 1, 256, 10000, 32, 1024)  # LUT modes scan by tiles
+    assert not O.uses_list_scan(0, 4, 0, 256, 10000, 32, 1024)   # no prune: nothing to fix
     assert not O.uses_list_scan(1, 4, 1, 256, 10000, 32, 1024)
     assert O.uses_list_scan(2, 8, 1, 768, 1, 1, 1024)
     with pytest.raises(ValueError):
@@ -125,7 +128,8 @@ def test_list_scan_search_bit_exact(oracle, gcase, bits, R):
 
 @pytest.mark.gpu
 def test_scan_kinds_match_the_oracle(oracle, gcase):
-    """scan_kind 0 (auto: the tile scan), 1 and 2 each equal the oracle's search of that kind."""
+    """scan_kind 0 (auto: here the list scan for 400 queries, the tile scan for 5), 1 and 2 each
+    equal the oracle's search of that kind."""
     idx, oix, X, Q, C, lab = gcase
     idx.nprobe, idx.k_rerank = 12, 40
     try:
