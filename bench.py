@@ -241,13 +241,13 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
 
 def list_scan_used(cfg, world=1):
     """Whether the library's search of the whole batch takes the list scan (its auto rule:
-    popcount modes, padded dim <= 768, nq * nprobe >= 16 * nlist; scan_kind 1 / 2 force the tile /
+    popcount modes, padded dim <= 768, nq * nprobe >= 64 * nlist; scan_kind 1 / 2 force the tile /
     list scan; the sharded search scans by tiles).  The CPU oracle is told the same, so that its
     sample answers like the full batch."""
     dp = (cfg["d"] + 31) // 32 * 32
     kind = cfg.get("scan_kind", 0)
     able = world == 1 and cfg["query_bits"] in (4, 8) and dp <= 768
-    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 16 * cfg["nlist"]))
+    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 64 * cfg["nlist"]))
 
 
 def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):

@@ -129,7 +129,7 @@ typedef struct {
                          /* per block, searcher_gpu_quantize_query.cu:172-300); the admitted    */
                          /* vectors' exact distances then rank per query.  Needs QUANT4 /       */
                          /* QUANT8, the prune on and a padded dim <= 768.  0 (default, auto):   */
-                         /* the list scan when nq * n_probes >= 16 * n_lists (the lists are     */
+                         /* the list scan when nq * n_probes >= 64 * n_lists (the lists are     */
                          /* shared by many queries), else the tile scan.                        */
 } rbq_search_params_t;
 

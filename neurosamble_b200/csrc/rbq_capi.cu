@@ -754,12 +754,13 @@ struct SearchPlan {
 };
 
 // The list scan serves batches whose probed lists are shared by at least this many queries on
-// average (at the benchmark shapes it beats the tile scan by 1.4x at D = 128 and 256 and 3.1x at
-// D = 768); smaller batches take the tile scan.
-constexpr int64_t kListScanMinPairsPerList = 16;
+// average (at the benchmark shapes, 98 to 390 per list, it beats the tile scan by 1.4x at D = 128
+// and 256 and 3.1x at D = 768; at 32 per list it loses, 1.5 against 0.8 ms); smaller batches
+// take the tile scan.
+constexpr int64_t kListScanMinPairsPerList = 64;
 
 // Whether a search takes the list scan: scan_kind 2 asks for it, 1 for the tile scan; 0 (auto)
-// takes the list scan for popcount modes with the prune on when nq * P >= 16 K.
+// takes the list scan for popcount modes with the prune on when nq * P >= 64 K.
 bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K)
 {
   RBQ_CHECK(scan_kind >= 0 && scan_kind <= 2, RBQ_ERR_INVALID,
@@ -1011,7 +1012,8 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
     a0.stats = nullptr;
     a0.tau_out = tau_a;
     launch_scan(a0, s);
-    // 2. the tile scan of the nearest probe from that seed -> keys_s[q][0]
+    // 2. the tile scan of the nearest probe from that seed -> keys_s[q][0] (a list scan of one
+    //    probe column shares each list among too few queries to pay)
     ScanArgs aa = sa;
     aa.nprobe = 1;
     aa.pstride = sp.P;

@@ -465,12 +465,12 @@ def assign(X, C) -> np.ndarray:
 
 # The list scan (rbq_search_params_t.scan_kind): batches whose probed lists are shared by at least
 # this many queries on average take it under scan_kind 0 (auto).
-LIST_SCAN_MIN_PAIRS_PER_LIST = 16
+LIST_SCAN_MIN_PAIRS_PER_LIST = 64
 
 
 def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K) -> bool:
     """The library's choice between the tile scan and the list scan: 2 the list scan, 1 the tile
-    scan, 0 (auto) the list scan for popcount modes with the prune on when nq * P >= 16 K."""
+    scan, 0 (auto) the list scan for popcount modes with the prune on when nq * P >= 64 K."""
     able = query_bits in (4, 8) and bool(prune) and dp % 32 == 0 and dp <= 768
     if scan_kind == 2:
         if not able:

@@ -697,7 +697,9 @@ def test_search_front_end_subchunks_equal_small_batches(oracle):
     torch.cuda.synchronize()
     p2, g2 = oracle.coarse(qr.cpu().numpy(), idx.centroids()[1], P)
     assert np.array_equal(probes.cpu().numpy(), p2) and np.array_equal(u32(g.cpu().numpy()), u32(g2))
-    idx.nprobe, idx.k_rerank = P, 20
+    # one scan kind for both batch sizes (auto would take the list scan for 40,000 queries and
+    # the tile scan for 5,000, whose thresholds differ)
+    idx.nprobe, idx.k_rerank, idx.scan_kind = P, 20, 1
     d, i = idx.search(Q, 10)
     parts = [idx.search(Q[a:a + 5000], 10) for a in range(0, 40000, 5000)]
     assert np.array_equal(i, np.concatenate([p[1] for p in parts]))
