@@ -242,11 +242,11 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
 def list_scan_used(cfg, world=1):
     """Whether the library's search of the whole batch takes the list scan (its auto rule:
     popcount modes, padded dim <= 768, nq * nprobe >= 64 * nlist; scan_kind 1 / 2 force the tile /
-    list scan; the sharded search scans by tiles).  The CPU oracle is told the same, so that its
-    sample answers like the full batch."""
+    list scan; the sharded search follows the same rule).  The CPU oracle is told the same, so
+    that its sample answers like the full batch."""
     dp = (cfg["d"] + 31) // 32 * 32
     kind = cfg.get("scan_kind", 0)
-    able = world == 1 and cfg["query_bits"] in (4, 8) and dp <= 768
+    able = cfg["query_bits"] in (4, 8) and dp <= 768
     return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 64 * cfg["nlist"]))
 
 
@@ -434,9 +434,9 @@ def run_ours(args, cfg):
     index.nprobe = cfg["nprobe"]
     index.prune = True
     index.query_bits = cfg["query_bits"]
+    index.scan_kind = args.scan_kind
     if world == 1:
         index.seeded = args.seeded
-        index.scan_kind = args.scan_kind
 
     # ---- recall at the config's rerank depth; raise R along the ladder until recall >= target
     # (exact neighbours of the first gt_sample queries: all of config 2's, 1,000 at configs 4 / 5)
@@ -706,15 +706,35 @@ def scan_roofline(ix, Qd, cfg, R_search, flush, steps, dev, seeded, lists=False)
 
     ids = torch.empty((nq, R), dtype=torch.int64, device=dev)
     dist = torch.empty((nq, R), dtype=torch.float32, device=dev)
-    if lists:  # bound seeds over the leading probed lists, then the list scan from them
+    if lists:  # the search's list scan, stage by stage: bound seeds over the leading probed lists,
+        # the tile scan of the nearest probe from them, the nearest list's R-th distance as the
+        # fixed threshold of the list scan of the other probes, the merge of both
         tau_l = torch.empty(nq, dtype=torch.float32, device=dev)
+        dd = torch.empty((2, nq, R), dtype=torch.float32, device=dev)
+        ii = torch.empty((2, nq, R), dtype=torch.int64, device=dev)
+        pa, ga = probes[:, :1], g[:, :1]  # strided column views, row stride P
+        pb, gb = probes[:, 1:], g[:, 1:]
 
         def run_lists(stats_t):
+            sp_ = _ptr(stats_t) if stats_t is not None else None
             _lib.call("rbq_bound_seed", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g),
                       P, P, R, 0, _ptr(tau_l), qb, st)
-            _lib.call("rbq_scan_lists", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g),
-                      P, P, _ptr(tau_l), R, _ptr(ids), _ptr(dist), _ptr(stats_t) if stats_t is not None else None,
-                      qb, st)
+            if info.shard_count > 1:
+                import torch.distributed as tdist
+                tdist.all_reduce(tau_l, op=tdist.ReduceOp.MIN)
+            _lib.call("rbq_scan", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pa), _ptr(ga), 1, P,
+                      _ptr(tau_l), None, None, R, 1, 1, 0, _ptr(ii[0]), _ptr(dd[0]), sp_, qb, st)
+            if P == 1:
+                ids.copy_(ii[0])
+                dist.copy_(dd[0])
+                return
+            tau1 = torch.where(ii[0][:, R - 1] >= 0, torch.minimum(tau_l, dd[0][:, R - 1]), tau_l).contiguous()
+            if info.shard_count > 1:
+                import torch.distributed as tdist
+                tdist.all_reduce(tau1, op=tdist.ReduceOp.MIN)
+            _lib.call("rbq_scan_lists", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(pb), _ptr(gb),
+                      P - 1, P, _ptr(tau1), R, _ptr(ii[1]), _ptr(dd[1]), sp_, qb, st)
+            _lib.call("rbq_merge_results", _ptr(dd), _ptr(ii), 2, nq, R, _ptr(dist), _ptr(ids), st)
 
         run_lists(stats)
         scan_ms = timed(lambda: run_lists(None))
@@ -762,7 +782,8 @@ def scan_roofline(ix, Qd, cfg, R_search, flush, steps, dev, seeded, lists=False)
     ach = scan_bytes / (scan_ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
             "traffic": traffic, "traffic_source": traffic_src, "peak_kind": kind,
-            "kernel": ("rbq list scan: bound seeds, tcgen05 kind::i8 list GEMM + admission, exact pass per query"
+            "kernel": ("rbq list scan: bound seeds, tile scan of the nearest probe, tcgen05 kind::i8 list GEMM + "
+                       "admission, exact pass per query, merge"
                        if lists else "rbq scan_kernel (+ key->id epilogue)"
                        + (", 2 launches: seed list + rest" if seeded else "")),
             "accounting": ("algorithmic bytes per query summed over the batch; the list scan reads each list once "

@@ -758,8 +758,12 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
         expand_word(cw[j], o);
         const int byte = w << 5, u0 = (byte & 127) >> 4;
         unsigned char* rowp = Bs + (byte >> 7) * (N * 128) + v * 128;
-        *reinterpret_cast<uint4*>(rowp + ((u0 ^ (v & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ (v & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        // words of odd 128-byte chunks store their second unit first: the 8 threads of a
+        // quarter warp then cover 8 different 16-byte units (all 32 banks) in each store
+        const int sw = (w >> 2) & 1;
+        const uint4 lo = make_uint4(o[0], o[1], o[2], o[3]), hi = make_uint4(o[4], o[5], o[6], o[7]);
+        *reinterpret_cast<uint4*>(rowp + (((u0 + sw) ^ (v & 7)) << 4)) = sw ? hi : lo;
+        *reinterpret_cast<uint4*>(rowp + (((u0 + 1 - sw) ^ (v & 7)) << 4)) = sw ? lo : hi;
       }
     }
     for (int v = tid; v < N; v += kLsThreads)

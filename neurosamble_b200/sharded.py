@@ -13,7 +13,11 @@ A search of a batch replicated on every rank runs in four steps:
    every rank that threshold, so a shard prunes its lists as tightly as one GPU prunes all of
    them (without it a shard far from the query admits most of its vectors);
 3. scan the shard's probed lists from that threshold and rerank the shard's candidates (only
-   those under the threshold survive, ~R / world per shard);
+   those under the threshold survive, ~R / world per shard).  Large batches take the list scan
+   instead (the library's rule, scan_kind): each rank's bound seed over its leading owned lists,
+   all-reduced (min); the tile scan of the nearest probe on its owner from that seed; the
+   nearest list's R-th distance, all-reduced (min), as the fixed threshold of the list scan of
+   every rank's other probes;
 4. the per-rank [nq, k] results cross NVLink in one all-gather (one packed buffer per rank)
    and are merged on the device by (distance, id).
 
@@ -39,6 +43,17 @@ def _pow2(v: int) -> int:
     while p < v:
         p <<= 1
     return p
+
+
+def uses_list_scan(scan_kind: int, query_bits: int, prune: bool, dp: int, nq: int, nprobe: int, nlist: int) -> bool:
+    """The library's choice of scan (rbq_search_params_t.scan_kind): 2 the list scan, 1 the tile
+    scan, 0 the list scan for popcount modes with the prune on when nq * nprobe >= 64 nlist."""
+    able = query_bits in (4, 8) and prune and dp % 32 == 0 and dp <= 768
+    if scan_kind == 2:
+        if not able:
+            raise RuntimeError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
+        return True
+    return scan_kind == 0 and able and nlist > 0 and nq * nprobe >= 64 * nlist
 
 
 def plan(nq: int, nprobe: int, k: int, k_rerank: int, probe_split: int, cand_cap: int, world: int):
@@ -77,12 +92,14 @@ class ShardedIndexIVFRaBitQ:
         self.device = self.local.device
 
     def __getattr__(self, name):
-        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits"):
+        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits",
+                    "scan_kind"):
             return getattr(self.local, name)
         raise AttributeError(name)
 
     def __setattr__(self, name, value):
-        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits"):
+        if name in ("nprobe", "k_rerank", "prune", "probe_split", "cand_cap", "coarse_margin", "query_bits",
+                    "scan_kind"):
             setattr(self.local, name, value)
         else:
             object.__setattr__(self, name, value)
@@ -138,7 +155,8 @@ class ShardedIndexIVFRaBitQ:
             d, i = sharded_search(LibStages(loc), t, int(k), int(loc.nprobe), int(loc.k_rerank), bool(loc.prune),
                                   int(loc.probe_split), int(loc.cand_cap), int(loc.coarse_margin),
                                   loc.info().padded_dim, self.rank, self.world, self.group, stats,
-                                  query_bits=int(loc.query_bits), timings=timings)
+                                  query_bits=int(loc.query_bits), timings=timings, nlist=self.nlist,
+                                  scan_kind=int(loc.scan_kind))
             if loc.metric == "ip":
                 d = 1.0 - 0.5 * d
         if on_dev:
@@ -187,6 +205,14 @@ class LibStages:
                       prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None,
                       mode or planes.shape[1], self.st)
 
+    def scan_lists(self, qr, planes, delta, k1, probes, g, tau0, R, ids, d, stats):
+        """The list scan with fixed thresholds tau0 (rbq_scan_lists); probes / g as in scan."""
+        assert probes.stride(1) == 1 and g.stride() == probes.stride()
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_scan_lists", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0],
+                      _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), _ptr(tau0), R, _ptr(ids), _ptr(d),
+                      _ptr(stats) if stats is not None else None, planes.shape[1], self.st)
+
     def merge(self, d, ids, out_d, out_i):
         with torch.cuda.device(self.device):
             _lib.call("rbq_merge_results", _ptr(d), _ptr(ids), d.shape[0], d.shape[1], d.shape[2], _ptr(out_d),
@@ -233,7 +259,7 @@ class _StageClock:
 
 def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, prune: bool, probe_split: int,
                    cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None,
-                   query_bits: int = 4, timings=None):
+                   query_bits: int = 4, timings=None, nlist: int = 0, scan_kind: int = 0):
     """The four steps of a sharded search (module docstring) for the batch t [nq, D] that
     every rank passes; `stages` computes (LibStages: librbq.so), this function moves data.
     timings (optional dict) receives this rank's milliseconds per stage."""
@@ -270,6 +296,9 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)
     clk.mark("query planes")
+    if not lut and uses_list_scan(scan_kind, query_bits, prune, dp, nq, P, nlist):
+        mi, md = _sharded_list_scan(stages, qr, planes, delta, k1, probes, g, R, cap, stats, group, clk)
+        return _finish(stages, t, mi, md, k, k_rerank, group, clk)
     # 2. seed: the bound seed of the nearest probe, on the rank that owns it (+inf elsewhere);
     #    min over ranks.
     tau = None
@@ -285,6 +314,40 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     stages.scan(qr, planes, delta, k1, probes, g, tau, None, R, int(prune), slices, cap, mi, md, stats,
                 mode=query_bits if lut else 0)
     clk.mark("scan")
+    return _finish(stages, t, mi, md, k, k_rerank, group, clk)
+
+
+def _sharded_list_scan(stages, qr, planes, delta, k1, probes, g, R, cap, stats, group, clk):
+    """Step 3 of a large batch: this rank's R best candidates by the list scan (module
+    docstring), thresholds shared by two all-reduces (min)."""
+    nq, P = probes.shape
+    dev = qr.device
+    tau = torch.empty(nq, dtype=torch.float32, device=dev)
+    stages.bound_seed(qr, planes, delta, k1, probes, g, R, cap, tau)
+    clk.mark("bound seed")
+    dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
+    clk.mark("all_reduce (seed)")
+    d2 = torch.empty((2, nq, R), dtype=torch.float32, device=dev)
+    i2 = torch.empty((2, nq, R), dtype=torch.int64, device=dev)
+    stages.scan(qr, planes, delta, k1, probes[:, :1], g[:, :1], tau, None, R, 1, 1, cap, i2[0], d2[0], stats)
+    if P == 1:
+        clk.mark("scan")
+        return i2[0], d2[0]
+    tau1 = torch.where(i2[0][:, R - 1] >= 0, torch.minimum(tau, d2[0][:, R - 1]), tau).contiguous()
+    dist.all_reduce(tau1, op=dist.ReduceOp.MIN, group=group)
+    clk.mark("scan (nearest probe) + all_reduce (threshold)")
+    stages.scan_lists(qr, planes, delta, k1, probes[:, 1:], g[:, 1:], tau1, R, i2[1], d2[1], stats)
+    mi = torch.empty((nq, R), dtype=torch.int64, device=dev)
+    md = torch.empty((nq, R), dtype=torch.float32, device=dev)
+    stages.merge(d2, i2, md, mi)
+    clk.mark("scan")
+    return mi, md
+
+
+def _finish(stages, t, mi, md, k, k_rerank, group, clk):
+    """Steps 3 (rerank) and 4 of a sharded search from this rank's candidates (mi, md)."""
+    dev = t.device
+    nq = t.shape[0]
     if k_rerank > 0:
         d = torch.empty((nq, k), dtype=torch.float32, device=dev)
         i = torch.empty((nq, k), dtype=torch.int64, device=dev)

@@ -510,6 +510,31 @@ def list_search_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=
     return mi, md, sa + sb
 
 
+def sharded_list_search_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None,
+                             shard_rank=0, shard_count=1, owner=None):
+    """The list scan of the sharded search (neurosamble_b200.sharded) on shard `shard_rank`: the
+    seed is the minimum over the shards of each shard's bound seed over its leading owned probed
+    lists; the nearest probe's owner scans it by tiles from that seed; the threshold for the other
+    probes is the minimum over the shards of min(seed, the nearest list's R-th distance); every
+    shard list-scans its other owned probes with it; the shard's answer is the R smallest of
+    both."""
+    probes, g = _c(probes, np.int32), _c(g, np.float32)
+    ranks = range(shard_count)
+    seed = np.min([bound_seed(ix, planes, delta, k1, probes, g, R, r, shard_count, owner) for r in ranks],
+                  axis=0).astype(np.float32)
+    A = [scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, 1, 1, r, shard_count,
+              with_stats=True, tau0=seed, owner=owner) for r in ranks]
+    ia, da, sa = A[shard_rank]
+    if probes.shape[1] == 1:
+        return ia, da, sa
+    tau1 = np.min([np.where(a[0][:, R - 1] >= 0, np.minimum(seed, a[1][:, R - 1]), seed) for a in A],
+                  axis=0).astype(np.float32)
+    ib, db, sb = list_scan(ix, Qr, planes, delta, k1, probes[:, 1:], g[:, 1:], R, tau1, shard_rank, shard_count,
+                           with_stats=True, owner=owner)
+    mi, md = merge_candidates([(ia, da), (ib, db)], R)
+    return mi, md, sa + sb
+
+
 def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None, prune=1, slices=1,
            shard_rank=0, shard_count=1, with_stats=False, exchange=False, seeded=-1, owner=None, query_bits=4,
            scan_kind=0):
@@ -540,8 +565,12 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
             dist, ids = cd[:, :k].copy(), cand[:, :k].copy()
         return (dist, ids, res[2]) if with_stats else (dist, ids)
     two = slices > 1 if seeded < 0 else seeded > 0
-    if not exchange and uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k):
-        res = list_search_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, shard_rank, shard_count, owner)
+    if uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k):
+        if exchange:
+            res = sharded_list_search_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, shard_rank,
+                                           shard_count, owner)
+        else:
+            res = list_search_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, shard_rank, shard_count, owner)
     elif exchange or two:
         res = seeded_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, prune, slices, shard_rank,
                           shard_count, with_stats=True, exchange=exchange, owner=owner)

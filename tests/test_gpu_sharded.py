@@ -51,6 +51,13 @@ def _rank_main(rank, world, port, outdir):
     d, i = idx.search(Q, 10, stats=st)
     stats = [torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}") for _ in range(world)]
     dist.all_gather(stats, st)
+    # the list scan (scan_kind 2): seeds and the nearest list's threshold all-reduced
+    idx.scan_kind = 2
+    stl = torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}")
+    dl, il = idx.search(Q, 10, stats=stl)
+    idx.scan_kind = 0
+    stats_l = [torch.zeros(2, dtype=torch.int64, device=f"cuda:{rank}") for _ in range(world)]
+    dist.all_gather(stats_l, stl)
     # build(): with the given centroids and labels, and by training (rank 0 trains, the table is
     # broadcast), against train() + add() on the same rows; a second build is refused
     same = []
@@ -77,7 +84,7 @@ def _rank_main(rank, world, port, outdir):
     if rank == 0:
         with open(os.path.join(outdir, "res.pkl"), "wb") as f:
             pickle.dump((d, i, C, lab, idx.local.rotation(), idx.local.query_scale, X, Q, idx.local.list_owners(),
-                         [s.cpu().numpy() for s in stats], same), f)
+                         [s.cpu().numpy() for s in stats], same, dl, il, [s.cpu().numpy() for s in stats_l]), f)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -87,7 +94,8 @@ def test_two_gpu_sharded_search_matches_oracle(oracle):
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(_rank_main, args=(2, _port(), td), nprocs=2, join=True)
-        d, i, C, lab, P, t4, X, Q, owners, stats, same = pickle.load(open(os.path.join(td, "res.pkl"), "rb"))
+        d, i, C, lab, P, t4, X, Q, owners, stats, same, dl, il, stats_l = pickle.load(
+            open(os.path.join(td, "res.pkl"), "rb"))
     assert same == [True, True, True], same  # build() == train() / centroids + add(); rebuild refused
     oix = oracle.build(X, C, lab, P, t4)
     want = oracle.list_owners("balanced", np.bincount(lab, minlength=64), 2)
@@ -99,3 +107,10 @@ def test_two_gpu_sharded_search_matches_oracle(oracle):
     want_i, want_d = oracle.merge_candidates([(p[1], p[0]) for p in parts], 10)
     assert np.array_equal(i, want_i)
     assert np.array_equal(d.view(np.uint32), want_d.view(np.uint32))
+    parts = [oracle.search(oix, Q, 10, 12, 40, shard_rank=r, shard_count=2, slices=1, exchange=True, owner=want,
+                           with_stats=True, scan_kind=2) for r in range(2)]
+    for r in range(2):
+        assert np.array_equal(stats_l[r], parts[r][2]), (r, stats_l[r], parts[r][2])
+    want_i, want_d = oracle.merge_candidates([(p[1], p[0]) for p in parts], 10)
+    assert np.array_equal(il, want_i)
+    assert np.array_equal(dl.view(np.uint32), want_d.view(np.uint32))

@@ -175,6 +175,14 @@ class _OracleStages:
         ids.copy_(torch.from_numpy(oi))
         d.copy_(torch.from_numpy(od))
 
+    def scan_lists(self, qr, planes, delta, k1, probes, g, tau0, R, ids, d, stats):
+        import torch
+        oi, od = self.O.list_scan(self.ix, qr.numpy(), planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(),
+                                  probes.numpy(), g.numpy(), R, tau0.numpy(), shard_rank=self.rank,
+                                  shard_count=self.world, owner=self.owner)
+        ids.copy_(torch.from_numpy(oi))
+        d.copy_(torch.from_numpy(od))
+
     def merge(self, d, ids, out_d, out_i):
         import torch
         mi, md = self.O.merge_candidates([(ids[p].numpy(), d[p].numpy()) for p in range(d.shape[0])], d.shape[2])
@@ -201,7 +209,7 @@ class _OracleStages:
         out_i.copy_(torch.from_numpy(ii))
 
 
-def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits, bpd):
+def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits, bpd, kind):
     import torch
     import torch.distributed as dist
 
@@ -220,18 +228,19 @@ def _seeded_worker(rank, world, port, outdir, nq, prune, policy, bits, bpd):
     ix.t8 = O.query_scale(64, 3, 7)
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
     d, i = sharded_search(_OracleStages(O, ix, rank, world, owner), torch.from_numpy(Q), 10, 8, 60, prune, 0, 0, 0,
-                          64, rank, world, query_bits=bits)
+                          64, rank, world, query_bits=bits, nlist=24, scan_kind=kind)
     with open(os.path.join(outdir, f"rank{rank}.pkl"), "wb") as f:
         pickle.dump((d.numpy(), i.numpy()), f)
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,nq,prune,policy,bits,bpd", [
-    (2, 40, 1, "balanced", 4, 1), (3, 7, 1, "round_robin", 4, 1), (2, 40, 0, "balanced", 4, 1),
-    (2, 40, 1, "balanced", 8, 1), (2, 40, 1, "balanced", 16, 1), (3, 9, 1, "round_robin", 32, 1),
-    (2, 40, 1, "balanced", 4, 4), (3, 9, 1, "round_robin", 16, 3)])
-def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits, bpd):
+@pytest.mark.parametrize("world,nq,prune,policy,bits,bpd,kind", [
+    (2, 40, 1, "balanced", 4, 1, 0), (3, 7, 1, "round_robin", 4, 1, 0), (2, 40, 0, "balanced", 4, 1, 0),
+    (2, 40, 1, "balanced", 8, 1, 0), (2, 40, 1, "balanced", 16, 1, 0), (3, 9, 1, "round_robin", 32, 1, 0),
+    (2, 40, 1, "balanced", 4, 4, 0), (3, 9, 1, "round_robin", 16, 3, 0),
+    (2, 40, 1, "balanced", 4, 1, 2), (3, 9, 1, "round_robin", 8, 1, 2), (2, 40, 1, "balanced", 4, 3, 2)])
+def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits, bpd, kind):
     """The orchestration (queries split for the rotation and coarse quantiser and padded, rotated
     rows and probe rows all-gathered, seeds all-reduced, results all-gathered and merged) gives, on every rank, the
     merge of the oracle's per-shard searches with the shared seed.  With the prune off every
@@ -242,7 +251,7 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits, bpd):
     from neurosamble_b200.sharded import plan
 
     with tempfile.TemporaryDirectory() as td:
-        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy, bits, bpd), nprocs=world,
+        mp.spawn(_seeded_worker, args=(world, _free_port(), td, nq, prune, policy, bits, bpd, kind), nprocs=world,
                  join=True)
         res = [pickle.load(open(os.path.join(td, f"rank{r}.pkl"), "rb")) for r in range(world)]
     X, Q = mixture(6000, 64, 12, 0.3, 40, seed=9)
@@ -254,7 +263,7 @@ def test_seeded_sharded_search_over_gloo(world, nq, prune, policy, bits, bpd):
     slices = plan(nq, 8, 10, 60, 0, 0, world)[1]
     owner = O.list_owners(policy, np.bincount(lab, minlength=24), world)
     parts = [O.search(ix, Q, 10, 8, 60, prune=prune, slices=slices, shard_rank=r, shard_count=world, exchange=True,
-                      owner=owner, query_bits=bits) for r in range(world)]
+                      owner=owner, query_bits=bits, scan_kind=kind) for r in range(world)]
     want_i, want_d = O.merge_candidates([(p[1], p[0]) for p in parts], 10)
     for d, i in res:
         assert np.array_equal(i, want_i)
