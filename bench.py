@@ -239,20 +239,23 @@ def kmeans_numpy(X, k, iters, per_list, seed, kind="balanced"):
     return C
 
 
-def list_scan_used(cfg, world=1):
+def list_scan_used(cfg, world=1, R=0):
     """Whether the library's search of the whole batch takes the list scan (its auto rule:
-    popcount modes, padded dim <= 768, nq * nprobe >= 64 * nlist; scan_kind 1 / 2 force the tile /
+    popcount modes, padded dim <= 768, nq * nprobe >= 64 * nlist, n >= max(R, k) * nlist; scan_kind
+    1 / 2 force the tile /
     list scan; the sharded search follows the same rule).  The CPU oracle is told the same, so
     that its sample answers like the full batch."""
     dp = (cfg["d"] + 31) // 32 * 32
     kind = cfg.get("scan_kind", 0)
     able = cfg["query_bits"] in (4, 8) and dp <= 768
-    return able and (kind == 2 or (kind == 0 and cfg["nq"] * cfg["nprobe"] >= 64 * cfg["nlist"]))
+    auto = (cfg["nq"] * cfg["nprobe"] >= 64 * cfg["nlist"]
+            and cfg["n"] >= max(R, cfg["k"]) * cfg["nlist"])
+    return able and (kind == 2 or (kind == 0 and auto))
 
 
 def cpu_search_timed(O, oix, Q, cfg, R, budget_s=20.0):
     """Time the oracle search on a bounded query sample sized to ~budget_s of CPU work."""
-    sk = 2 if list_scan_used(cfg) else 1
+    sk = 2 if list_scan_used(cfg, 1, R) else 1
     probe = min(len(Q), 200)
     t0 = time.perf_counter()
     O.search(oix, Q[:probe], cfg["k"], cfg["nprobe"], R, query_bits=cfg["query_bits"], scan_kind=sk)
@@ -302,7 +305,7 @@ def run_reference(args, cfg):
         R = rerank_ladder(cfg)[-1]
         for cand in rerank_ladder(cfg):
             _, ids = O.search(oix, Q[:ns], cfg["k"], cfg["nprobe"], cand, query_bits=cfg["query_bits"],
-                              scan_kind=2 if list_scan_used(cfg) else 1)
+                              scan_kind=2 if list_scan_used(cfg, 1, cand) else 1)
             recalls[cand] = O.recall(ids, gt)
             if recalls[cand] >= RECALL_TARGET:
                 R = cand
@@ -582,7 +585,7 @@ def run_ours(args, cfg):
 
     # ---- roofline of the dominant kernel (the list scan), live CUDA events on its stream
     seeded = (world > 1 or args.seeded == 1) and cfg["query_bits"] < 16  # LUT modes: one pass, no seed
-    lists = list_scan_used(cfg, world)
+    lists = list_scan_used(cfg, world, R)
     roof, roof_rr = scan_roofline(local_ix, Qd, cfg, R, flush, args.steps, dev, seeded, lists)
     scan_share = round(roof["launch_ms"] / ms, 3)
 

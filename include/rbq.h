@@ -130,7 +130,8 @@ typedef struct {
                          /* vectors' exact distances then rank per query.  Needs QUANT4 /       */
                          /* QUANT8, the prune on and a padded dim <= 768.  0 (default, auto):   */
                          /* the list scan when nq * n_probes >= 64 * n_lists (the lists are     */
-                         /* shared by many queries), else the tile scan.                        */
+                         /* shared by many queries) and the index holds >= R vectors per list   */
+                         /* on average (R = max(rerank, k)), else the tile scan.                */
 } rbq_search_params_t;
 
 typedef struct {

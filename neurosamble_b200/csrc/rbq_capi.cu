@@ -302,6 +302,11 @@ void relayout(Index& ix, cudaStream_t s)
   std::vector<int64_t> off, order;
   counting_sort(lab, ix.K, off, order);
   ix.off_host = off;
+  ix.min_list = -1;
+  for (int l = 0; l < ix.K; ++l)
+    if (ix.owner_host[l] == ix.shard_rank && (ix.min_list < 0 || off[l + 1] - off[l] < ix.min_list))
+      ix.min_list = off[l + 1] - off[l];
+  if (ix.min_list < 0) ix.min_list = 0;
   dev_free(ix.list_off);
   dev_free(ix.ids);
   dev_free(ix.codes);
@@ -754,14 +759,17 @@ struct SearchPlan {
 };
 
 // The list scan serves batches whose probed lists are shared by at least this many queries on
-// average (at the benchmark shapes, 98 to 390 per list, it beats the tile scan by 1.4x at D = 128
-// and 256 and 3.1x at D = 768; at 32 per list it loses, 1.5 against 0.8 ms); smaller batches
-// take the tile scan.
+// average (at the benchmark shapes, 98 to 390 per list, it beats the tile scan by 1.3x at D = 128
+// and 256 and 3x at D = 768; at 32 per list it loses, 1.5 against 0.8 ms), on indexes whose lists
+// hold R vectors on average (the nearest list then gives a tight fixed threshold; with lists of
+// 98 vectors and R = 800 the threshold admits 93 % of the probed vectors); others take the tile
+// scan.
 constexpr int64_t kListScanMinPairsPerList = 64;
 
 // Whether a search takes the list scan: scan_kind 2 asks for it, 1 for the tile scan; 0 (auto)
-// takes the list scan for popcount modes with the prune on when nq * P >= 64 K.
-bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K)
+// takes the list scan for popcount modes with the prune on when nq * P >= 64 K and the index
+// holds n_total >= R K vectors.
+bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int P, int K, int64_t n_total, int R)
 {
   RBQ_CHECK(scan_kind >= 0 && scan_kind <= 2, RBQ_ERR_INVALID,
             "scan_kind must be 0 (auto), 1 (tile scan) or 2 (list scan)");
@@ -769,7 +777,7 @@ bool use_list_scan(int scan_kind, int qbits, int prune, int dp, int64_t nq, int 
   RBQ_CHECK(scan_kind != 2 || able, RBQ_ERR_INVALID,
             "list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768");
   if (scan_kind == 2) return true;
-  return scan_kind == 0 && able && nq * (int64_t)P >= kListScanMinPairsPerList * K;
+  return scan_kind == 0 && able && nq * (int64_t)P >= kListScanMinPairsPerList * K && n_total >= (int64_t)R * K;
 }
 
 int list_scan_cap(int R)
@@ -839,7 +847,7 @@ SearchPlan plan_search(const Index& ix, const rbq_search_params_t& p, int64_t nq
   sp.prune = p.prune ? 1 : 0;
   sp.qbits = query_bits_of(p.query_bits);
   sp.seeded = sp.qbits < 16 && (p.seeded < 0 ? sp.slices > 1 : p.seeded > 0);  // no bound seed in LUT modes
-  sp.lists = use_list_scan(p.scan_kind, sp.qbits, sp.prune, ix.Dp, nq, sp.P, ix.K);
+  sp.lists = use_list_scan(p.scan_kind, sp.qbits, sp.prune, ix.Dp, nq, sp.P, ix.K, ix.n_total, sp.R);
   sp.lcap = list_scan_cap(sp.R);
   if (sp.lists) {  // two key rows per query: the nearest probe's tile scan and the list scan
     sp.slices = 2;
@@ -1006,21 +1014,26 @@ void search_scan(const Index& ix, const SearchPlan& sp, const float* Qr, const u
   ScanArgs sa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, sp.P, sp.R, sp.cap, sp.prune, sp.slices,
                                 keys_s, stats, sp.qbits);
   if (sp.lists) {
-    // 1. the bound seed over the leading probed lists holding >= R vectors
-    ScanArgs a0 = sa;
-    a0.slices = 1;
-    a0.stats = nullptr;
-    a0.tau_out = tau_a;
-    launch_scan(a0, s);
-    // 2. the tile scan of the nearest probe from that seed -> keys_s[q][0] (a list scan of one
-    //    probe column shares each list among too few queries to pay)
+    // 1. the bound seed over the leading probed lists holding >= R vectors; 2. the tile scan of
+    //    the nearest probe from that seed -> keys_s[q][0] (a list scan of one probe column shares
+    //    each list among too few queries to pay).  On one GPU whose every list holds R vectors
+    //    the seed is the nearest list's, which the tile scan computes itself (and reports).
     ScanArgs aa = sa;
     aa.nprobe = 1;
     aa.pstride = sp.P;
     aa.slices = 1;
-    aa.tau0 = tau_a;
     aa.out_keys = keys_s;
     aa.out_slices = sp.P > 1 ? 2 : 1;
+    if (ix.shard_count == 1 && ix.min_list >= sp.R) {
+      aa.seed_out = tau_a;
+    } else {
+      ScanArgs a0 = sa;
+      a0.slices = 1;
+      a0.stats = nullptr;
+      a0.tau_out = tau_a;
+      launch_scan(a0, s);
+      aa.tau0 = tau_a;
+    }
     launch_scan(aa, s);
     if (sp.P == 1) {
       RBQ_CUDA(cudaMemcpyAsync(keys, keys_s, (size_t)nq * sp.R * 8, cudaMemcpyDeviceToDevice, s));

@@ -95,6 +95,7 @@ struct Index {
   int shard_policy = RBQ_SHARD_ROUND_ROBIN;
   bool has_raw = true;              // X_r holds the raw rows (false for an index imported without them)
   bool raw_on_host = false;         // X_r is pinned, mapped host memory (RBQ_RAW_HOST), else HBM
+  int64_t min_list = 0;             // vectors in this shard's smallest list (set by relayout)
   float t8 = 0.0f / 0.0f;           // 8-bit query constant of an imported reference file (NaN: derive)
   bool owners_fixed = false;
   std::vector<int32_t> owner_host;  // [K] rank holding list l
@@ -269,6 +270,9 @@ struct ScanArgs {
   // Seed-only launch (slices 1, prune on): write the slice's starting threshold to tau_out[q]
   // (the bound seed, or +inf when its lists hold fewer than R vectors) and scan nothing.
   float* tau_out = nullptr;
+  // Optional [nq]: slice 0 writes the threshold it starts its scan from (tau0, the bound seed it
+  // computed, or +inf) and then scans as usual.
+  float* seed_out = nullptr;
   unsigned long long* out_keys;  // [nq, slices, R]
   unsigned long long* stats;     // optional [2]: scanned, admitted
   // Optional [nq] visiting order: block i scans query qorder[i / slices] (a permutation of

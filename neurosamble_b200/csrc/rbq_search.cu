@@ -1232,6 +1232,7 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
     if (tid == 0) a.tau_out[q] = s_tau;
     return;
   }
+  if (a.seed_out && slice == 0 && tid == 0) a.seed_out[q] = s_tau;  // the threshold the scan starts from
   unsigned n_admit = 0;
   // list cursor (monotone per thread): current list, end of it in the flat sequence, slot shift
   int cur = 0;

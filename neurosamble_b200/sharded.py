@@ -45,15 +45,17 @@ def _pow2(v: int) -> int:
     return p
 
 
-def uses_list_scan(scan_kind: int, query_bits: int, prune: bool, dp: int, nq: int, nprobe: int, nlist: int) -> bool:
+def uses_list_scan(scan_kind: int, query_bits: int, prune: bool, dp: int, nq: int, nprobe: int, nlist: int,
+                   n_total: int = 0, R: int = 0) -> bool:
     """The library's choice of scan (rbq_search_params_t.scan_kind): 2 the list scan, 1 the tile
-    scan, 0 the list scan for popcount modes with the prune on when nq * nprobe >= 64 nlist."""
+    scan, 0 the list scan for popcount modes with the prune on when nq * nprobe >= 64 nlist and
+    the index holds n_total >= R nlist vectors."""
     able = query_bits in (4, 8) and prune and dp % 32 == 0 and dp <= 768
     if scan_kind == 2:
         if not able:
             raise RuntimeError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
         return True
-    return scan_kind == 0 and able and nlist > 0 and nq * nprobe >= 64 * nlist
+    return scan_kind == 0 and able and nlist > 0 and nq * nprobe >= 64 * nlist and n_total >= R * nlist
 
 
 def plan(nq: int, nprobe: int, k: int, k_rerank: int, probe_split: int, cand_cap: int, world: int):
@@ -156,7 +158,7 @@ class ShardedIndexIVFRaBitQ:
                                   int(loc.probe_split), int(loc.cand_cap), int(loc.coarse_margin),
                                   loc.info().padded_dim, self.rank, self.world, self.group, stats,
                                   query_bits=int(loc.query_bits), timings=timings, nlist=self.nlist,
-                                  scan_kind=int(loc.scan_kind))
+                                  scan_kind=int(loc.scan_kind), n_total=self.ntotal)
             if loc.metric == "ip":
                 d = 1.0 - 0.5 * d
         if on_dev:
@@ -259,7 +261,7 @@ class _StageClock:
 
 def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, prune: bool, probe_split: int,
                    cand_cap: int, margin: int, dp: int, rank: int, world: int, group=None, stats=None,
-                   query_bits: int = 4, timings=None, nlist: int = 0, scan_kind: int = 0):
+                   query_bits: int = 4, timings=None, nlist: int = 0, scan_kind: int = 0, n_total: int = 0):
     """The four steps of a sharded search (module docstring) for the batch t [nq, D] that
     every rank passes; `stages` computes (LibStages: librbq.so), this function moves data.
     timings (optional dict) receives this rank's milliseconds per stage."""
@@ -296,7 +298,7 @@ def sharded_search(stages, t: torch.Tensor, k: int, nprobe: int, k_rerank: int, 
     k1 = torch.empty(nq, dtype=torch.float32, device=dev)
     stages.prep(qr, planes, delta, k1)
     clk.mark("query planes")
-    if not lut and uses_list_scan(scan_kind, query_bits, prune, dp, nq, P, nlist):
+    if not lut and uses_list_scan(scan_kind, query_bits, prune, dp, nq, P, nlist, n_total, R):
         mi, md = _sharded_list_scan(stages, qr, planes, delta, k1, probes, g, R, cap, stats, group, clk)
         return _finish(stages, t, mi, md, k, k_rerank, group, clk)
     # 2. seed: the bound seed of the nearest probe, on the rank that owns it (+inf elsewhere);

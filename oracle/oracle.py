@@ -468,15 +468,17 @@ def assign(X, C) -> np.ndarray:
 LIST_SCAN_MIN_PAIRS_PER_LIST = 64
 
 
-def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K) -> bool:
+def uses_list_scan(scan_kind, query_bits, prune, dp, nq, nprobe, K, n_total=None, R=0) -> bool:
     """The library's choice between the tile scan and the list scan: 2 the list scan, 1 the tile
-    scan, 0 (auto) the list scan for popcount modes with the prune on when nq * P >= 64 K."""
+    scan, 0 (auto) the list scan for popcount modes with the prune on when nq * P >= 64 K and
+    the index holds n_total >= R K vectors (R = max(rerank, k))."""
     able = query_bits in (4, 8) and bool(prune) and dp % 32 == 0 and dp <= 768
     if scan_kind == 2:
         if not able:
             raise ValueError("list scan: needs QUANT4 / QUANT8, the prune on and a padded dim <= 768")
         return True
-    return scan_kind == 0 and able and nq * nprobe >= LIST_SCAN_MIN_PAIRS_PER_LIST * K
+    return (scan_kind == 0 and able and nq * nprobe >= LIST_SCAN_MIN_PAIRS_PER_LIST * K
+            and (n_total is None or n_total >= R * K))
 
 
 def list_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tau0, shard_rank=0, shard_count=1,
@@ -565,7 +567,7 @@ def search(ix: OracleIndex, Q, k, nprobe, rerank_depth, tile=SCAN_TILE, cap=None
             dist, ids = cd[:, :k].copy(), cand[:, :k].copy()
         return (dist, ids, res[2]) if with_stats else (dist, ids)
     two = slices > 1 if seeded < 0 else seeded > 0
-    if uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k):
+    if uses_list_scan(scan_kind, query_bits, prune, ix.dp, Q.shape[0], nprobe, ix.k, int(ix.list_off[-1]), R):
         if exchange:
             res = sharded_list_search_scan(ix, Qr, planes, delta, k1, probes, g, R, tile, cap, shard_rank,
                                            shard_count, owner)

@@ -46,6 +46,8 @@ def test_fixed_threshold_keeps_the_tile_scan_answer(oracle, small):
 def test_auto_rule():
     from oracle import oracle as O
     assert O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024)      # 312 queries per list
+    assert O.uses_list_scan(0, 4, 1, 256, 10000, 32, 1024, 1_000_000, 200)  # lists of 976 >= R
+    assert not O.uses_list_scan(0, 4, 1, 256, 200000, 48, 2048, 200_000, 800)  # lists of 98 < R
     assert not O.uses_list_scan(0, 4, 1, 256, 64, 32, 1024)     # 2 per list: the tile scan
     assert not O.uses_list_scan(0, 16, 1, 256, 10000, 32, 1024)  # LUT modes scan by tiles
     assert not O.uses_list_scan(0, 4, 0, 256, 10000, 32, 1024)   # no prune: nothing to fix
@@ -207,3 +209,21 @@ def test_overflowed_rows_take_the_fixed_threshold_tile_scan(oracle):
     oi, od, ost = oracle.list_scan(oix, Qr, pl, de, k1, probes, g, 10, tau, with_stats=True)
     assert np.array_equal(ids.cpu().numpy(), oi) and np.array_equal(u32(dist.cpu().numpy()), u32(od))
     assert stats.cpu().tolist() == ost.tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("K,R", [(64, 200), (16, 40)])
+def test_list_scan_seed_from_leading_lists_or_the_nearest(oracle, K, R):
+    """Lists smaller than R (6,000 vectors in 64 lists, R 200) need the separate bound-seed launch
+    over the leading lists; lists of R or more (16 lists, R 40) let the nearest probe's tile scan
+    seed itself.  Both equal the oracle's list search."""
+    X, Q = mixture(6000, 64, 30, 0.3, 150, seed=K)
+    C, _ = oracle.kmeans(X[::3], K, iters=3)
+    lab = oracle.assign(X, C)
+    idx, oix = _index(oracle, X, C, lab)
+    idx.nprobe, idx.k_rerank, idx.scan_kind = 8, R, 2
+    d1, i1 = idx.search(Q, 10)
+    d2, i2 = oracle.search(oix, Q, 10, 8, R, scan_kind=2)
+    assert np.array_equal(i1, i2) and np.array_equal(u32(d1), u32(d2))
+    sizes = np.diff(oix.list_off)
+    assert (sizes.min() < R) == (K == 64)
