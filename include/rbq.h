@@ -308,6 +308,13 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
                    const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
                    int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, int32_t query_bits,
                    void* stream);
+/* rbq_bound_seed for the queries whose nearest probe (column 0 of probes_dev) this shard owns;
+ * +inf for the others.  A sharded search all-reduces (min) it: each query's seed is then its
+ * nearest list's owner's, over that shard's leading owned lists, at 1/N of the work per shard. */
+int rbq_bound_seed_owned(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                         const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                         int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, int32_t query_bits,
+                         void* stream);
 /* rbq_scan without any device allocation, for callers that cannot allocate GPU memory at
  * search time: a host program whose device memory is handed out up front by its own pool
  * (so a library cudaMalloc would fail or break its budget), or a latency-critical search

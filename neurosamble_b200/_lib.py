@@ -74,6 +74,7 @@ SIGNATURES = {
     "rbq_get_centroids": [_P, _P, _P],
     "rbq_export_lists": [_P, _P, _P, _P, _P, _P, _P],
     "rbq_export_ex_lists": [_P, _P, _P, _P],
+    "rbq_bound_seed_owned": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _I32, _P],
     "rbq_scan_lists": [_P, _P, _P, _P, _P, _I64, _P, _P, _I32, _I32, _P, _I32, _P, _P, _P, _I32, _P],
     "rbq_get_list_owners": [_P, _P],
     "rbq_rotate": [_P, _P, _I64, _P, _P],

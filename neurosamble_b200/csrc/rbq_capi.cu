@@ -2378,6 +2378,31 @@ int rbq_bound_seed(rbq_index_t* index, const float* Qr_dev, const uint32_t* plan
   });
 }
 
+int rbq_bound_seed_owned(rbq_index_t* index, const float* Qr_dev, const uint32_t* planes_dev, const float* delta_dev,
+                         const float* k1_dev, int64_t nq, const int32_t* probes_dev, const float* g_dev, int32_t nprobe,
+                         int32_t probe_stride, int32_t R, int32_t cand_cap, float* tau_dev, int32_t query_bits,
+                         void* stream)
+{
+  return guarded([&] {
+    Range nvtx_range("rbq_bound_seed_owned");
+    RBQ_CHECK(index, RBQ_ERR_INVALID, "null argument");
+    RBQ_CHECK(nq == 0 || (Qr_dev && planes_dev && delta_dev && k1_dev && probes_dev && g_dev && tau_dev),
+              RBQ_ERR_INVALID, "null buffer");
+    RBQ_CHECK(R >= 1 && R <= 4096 && nprobe >= 1 && (probe_stride == 0 || probe_stride >= nprobe), RBQ_ERR_INVALID,
+              "bad seed parameters");
+    if (nq == 0) return;
+    Index& ix = index->ix;
+    DeviceGuard dg(ix.device);
+    const int cap = std::max(next_pow2(cand_cap > 0 ? cand_cap : 1024), next_pow2(R + kScanTile));
+    ScanArgs sa = batch_scan_args(ix, Qr_dev, planes_dev, delta_dev, k1_dev, nq, probes_dev, g_dev, nprobe, R, cap,
+                                  1, 1, nullptr, nullptr, query_bits_of(query_bits));
+    sa.pstride = probe_stride;
+    sa.tau_out = tau_dev;
+    sa.seed_nearest_owned = 1;
+    launch_scan(sa, as_stream(stream));
+  });
+}
+
 int rbq_list_estimates(rbq_index_t* index, const uint32_t* planes_dev, float delta, float k1, float g, int32_t list,
                        int32_t* acc_dev, float* est_dev, float* low_dev, int32_t query_bits, void* stream)
 {

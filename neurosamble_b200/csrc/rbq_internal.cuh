@@ -270,6 +270,9 @@ struct ScanArgs {
   // Seed-only launch (slices 1, prune on): write the slice's starting threshold to tau_out[q]
   // (the bound seed, or +inf when its lists hold fewer than R vectors) and scan nothing.
   float* tau_out = nullptr;
+  // With tau_out: only queries whose nearest probe (column 0) this shard owns compute the seed;
+  // the others get +inf (a sharded search takes the minimum over the shards).
+  int seed_nearest_owned = 0;
   // Optional [nq]: slice 0 writes the threshold it starts its scan from (tau0, the bound seed it
   // computed, or +inf) and then scans as usual.
   float* seed_out = nullptr;

@@ -1084,6 +1084,13 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   const int64_t q = a.qorder ? (int64_t)a.qorder[qi] : qi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (a.over_cnt && a.over_cnt[q] <= a.over_cap) return;  // only the list scan's overflowed rows
+  if (a.tau_out && a.seed_nearest_owned) {
+    const int l0 = a.probes[q * a.pstride];
+    if (l0 < 0 || __ldg(a.owner + l0) != a.shard_rank) {
+      if (tid == 0) a.tau_out[q] = __int_as_float(0x7f800000);
+      return;
+    }
+  }
   // fixed-threshold scan: admission against tau0[q] throughout
   const float tau_fix = a.tau0 ? a.tau0[q] : __int_as_float(0x7f800000);
 

@@ -14,8 +14,9 @@ A search of a batch replicated on every rank runs in four steps:
    them (without it a shard far from the query admits most of its vectors);
 3. scan the shard's probed lists from that threshold and rerank the shard's candidates (only
    those under the threshold survive, ~R / world per shard).  Large batches take the list scan
-   instead (the library's rule, scan_kind): each rank's bound seed over its leading owned lists,
-   all-reduced (min); the tile scan of the nearest probe on its owner from that seed; the
+   instead (the library's rule, scan_kind): the bound seed over the leading owned lists of the
+   nearest probe's owner, all-reduced (min); the tile scan of the nearest probe on its owner from
+   that seed; the
    nearest list's R-th distance, all-reduced (min), as the fixed threshold of the list scan of
    every rank's other probes;
 4. the per-rank [nq, k] results cross NVLink in one all-gather (one packed buffer per rank)
@@ -207,6 +208,14 @@ class LibStages:
                       prune, slices, cap, _ptr(ids), _ptr(d), _ptr(stats) if stats is not None else None,
                       mode or planes.shape[1], self.st)
 
+    def bound_seed_owned(self, qr, planes, delta, k1, probes, g, R, cap, tau):
+        """bound_seed for the queries whose nearest probe this rank owns (+inf elsewhere)."""
+        assert probes.stride(1) == 1 and g.stride() == probes.stride()
+        with torch.cuda.device(self.device):
+            _lib.call("rbq_bound_seed_owned", self.h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), qr.shape[0],
+                      _ptr(probes), _ptr(g), probes.shape[1], probes.stride(0), R, cap, _ptr(tau), planes.shape[1],
+                      self.st)
+
     def scan_lists(self, qr, planes, delta, k1, probes, g, tau0, R, ids, d, stats):
         """The list scan with fixed thresholds tau0 (rbq_scan_lists); probes / g as in scan."""
         assert probes.stride(1) == 1 and g.stride() == probes.stride()
@@ -325,7 +334,7 @@ def _sharded_list_scan(stages, qr, planes, delta, k1, probes, g, R, cap, stats, 
     nq, P = probes.shape
     dev = qr.device
     tau = torch.empty(nq, dtype=torch.float32, device=dev)
-    stages.bound_seed(qr, planes, delta, k1, probes, g, R, cap, tau)
+    stages.bound_seed_owned(qr, planes, delta, k1, probes, g, R, cap, tau)
     clk.mark("bound seed")
     dist.all_reduce(tau, op=dist.ReduceOp.MIN, group=group)
     clk.mark("all_reduce (seed)")

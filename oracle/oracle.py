@@ -515,15 +515,16 @@ def list_search_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=
 def sharded_list_search_scan(ix: OracleIndex, Qr, planes, delta, k1, probes, g, R, tile=SCAN_TILE, cap=None,
                              shard_rank=0, shard_count=1, owner=None):
     """The list scan of the sharded search (neurosamble_b200.sharded) on shard `shard_rank`: the
-    seed is the minimum over the shards of each shard's bound seed over its leading owned probed
-    lists; the nearest probe's owner scans it by tiles from that seed; the threshold for the other
+    seed is the bound seed over the leading owned probed lists of the shard that owns the nearest
+    probe; that shard scans the nearest probe by tiles from it; the threshold for the other
     probes is the minimum over the shards of min(seed, the nearest list's R-th distance); every
     shard list-scans its other owned probes with it; the shard's answer is the R smallest of
     both."""
     probes, g = _c(probes, np.int32), _c(g, np.float32)
     ranks = range(shard_count)
-    seed = np.min([bound_seed(ix, planes, delta, k1, probes, g, R, r, shard_count, owner) for r in ranks],
-                  axis=0).astype(np.float32)
+    own0 = (np.asarray(owner)[probes[:, 0]] if owner is not None else probes[:, 0] % shard_count)
+    seed = np.min([np.where(own0 == r, bound_seed(ix, planes, delta, k1, probes, g, R, r, shard_count, owner),
+                            np.float32(np.inf)) for r in ranks], axis=0).astype(np.float32)
     A = [scan(ix, Qr, planes, delta, k1, probes[:, :1], g[:, :1], R, tile, cap, 1, 1, r, shard_count,
               with_stats=True, tau0=seed, owner=owner) for r in ranks]
     ia, da, sa = A[shard_rank]

@@ -175,6 +175,14 @@ class _OracleStages:
         ids.copy_(torch.from_numpy(oi))
         d.copy_(torch.from_numpy(od))
 
+    def bound_seed_owned(self, qr, planes, delta, k1, probes, g, R, cap, tau):
+        import torch
+        t = self.O.bound_seed(self.ix, planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(), probes.numpy(),
+                              g.numpy(), R, shard_rank=self.rank, shard_count=self.world, owner=self.owner)
+        p0 = probes.numpy()[:, 0]
+        own0 = self.owner[p0] if self.owner is not None else p0 % self.world
+        tau.copy_(torch.from_numpy(np.where(own0 == self.rank, t, np.float32(np.inf)).astype(np.float32)))
+
     def scan_lists(self, qr, planes, delta, k1, probes, g, tau0, R, ids, d, stats):
         import torch
         oi, od = self.O.list_scan(self.ix, qr.numpy(), planes.numpy().view(np.uint32), delta.numpy(), k1.numpy(),
