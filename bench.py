@@ -720,8 +720,9 @@ def scan_roofline(ix, Qd, cfg, R_search, flush, steps, dev, seeded, lists=False)
 
         def run_lists(stats_t):
             sp_ = _ptr(stats_t) if stats_t is not None else None
-            _lib.call("rbq_bound_seed", h, _ptr(qr), _ptr(planes), _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g),
-                      P, P, R, 0, _ptr(tau_l), qb, st)
+            # sharded: the seed on the nearest probe's owner only, then the minimum over the ranks
+            _lib.call("rbq_bound_seed_owned" if info.shard_count > 1 else "rbq_bound_seed", h, _ptr(qr), _ptr(planes),
+                      _ptr(delta), _ptr(k1), nq, _ptr(probes), _ptr(g), P, P, R, 0, _ptr(tau_l), qb, st)
             if info.shard_count > 1:
                 import torch.distributed as tdist
                 tdist.all_reduce(tau_l, op=tdist.ReduceOp.MIN)
