@@ -647,12 +647,13 @@ __device__ __forceinline__ void expand_word(uint32_t c, uint32_t (&o)[8])
 }
 
 template <int N>
-__global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScanArgs a)
+__global__ void __launch_bounds__(kLsThreads, N == 128 ? 2 : 1) list_scan_tc_kernel(const ListScanArgs a)
 {
   constexpr int kWpt = N * 24 / kLsThreads;  // code words per thread per tile (W <= 24)
-  extern __shared__ unsigned char ls_smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(ls_smem_raw) + 1023) & ~(uintptr_t)1023);
+  extern __shared__ __align__(16) unsigned char ls_smem_raw[];
+  // 1024-byte aligned by an offset from the shared array itself, so that every access through
+  // these pointers stays a shared-memory access
+  unsigned char* base = ls_smem_raw + ((1024u - (smem_u32(ls_smem_raw) & 1023u)) & 1023u);
   const int Kc = (a.Dp + 127) >> 7;
   unsigned char* As = base;                           // [Kc][kLsM rows][128 B]
   unsigned char* Bs0 = base + Kc * kLsM * 128;        // [2][Kc][N rows][128 B]
@@ -736,14 +737,23 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
             make_uint4(0u, 0u, 0u, 0u);
     }
   const int ntiles = (nl + N - 1) / N;
+  // i / W for i < N * 24 as a multiply-high by ceil(2^32 / W) (exact in that range)
+  const unsigned long long w_magic = (0xFFFFFFFFull + (unsigned)W) / (unsigned)W;
+  auto div_w = [&](int i) { return (int)(((unsigned long long)(unsigned)i * w_magic) >> 32); };
   uint32_t cw[kWpt];
-  auto load_codes = [&](int t) {  // code words of tile t into registers (0 past the list)
+  float cf0 = 0.0f, cf1 = 0.0f, cf2 = 0.0f;  // column data of the tile being loaded (threads < N)
+  auto load_codes = [&](int t) {  // code words and column data of tile t into registers
     const int t0 = t * N;
 #pragma unroll
     for (int j = 0; j < kWpt; ++j) {
       const int i = tid + j * kLsThreads;
-      const int v = i / W;
-      cw[j] = (i < N * W && t0 + v < nl) ? __ldg(a.codes + (lb + t0) * W + i) : 0u;
+      cw[j] = (i < N * W && t0 + div_w(i) < nl) ? __ldg(a.codes + (lb + t0) * W + i) : 0u;
+    }
+    if (tid < N && t0 + tid < nl) {
+      const int64_t slot = lb + t0 + tid;
+      cf0 = __ldg(a.fadd + slot);
+      cf1 = __ldg(a.frescale + slot);
+      cf2 = __ldg(a.ferr + slot);
     }
   };
   auto store_tile = [&](int t) {  // expand tile t into B[t % 2], its column data into s_col[t % 3]
@@ -753,7 +763,7 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
     for (int j = 0; j < kWpt; ++j) {
       const int i = tid + j * kLsThreads;
       if (i < N * W) {
-        const int v = i / W, w = i - v * W;
+        const int v = div_w(i), w = i - v * W;
         uint32_t o[8];
         expand_word(cw[j], o);
         const int byte = w << 5, u0 = (byte & 127) >> 4;
@@ -766,12 +776,8 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
         *reinterpret_cast<uint4*>(rowp + (((u0 + 1 - sw) ^ (v & 7)) << 4)) = sw ? lo : hi;
       }
     }
-    for (int v = tid; v < N; v += kLsThreads)
-      if (t0 + v < nl) {
-        const int64_t slot = lb + t0 + v;
-        s_col[t % 3][v] = make_float4(__ldg(a.fadd + slot), __ldg(a.frescale + slot), __ldg(a.ferr + slot),
-                                      __uint_as_float((uint32_t)slot));
-      }
+    if (tid < N && t0 + tid < nl)
+      s_col[t % 3][tid] = make_float4(cf0, cf1, cf2, __uint_as_float((uint32_t)(lb + t0 + tid)));
   };
   auto issue = [&](int t) {  // thread 0: tile t's MMAs into accumulator t % 2, committed to s_bar[t % 2]
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -784,6 +790,7 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
                   ls_idesc<N>(), (c > 0 || ks > 0) ? 1u : 0u);
     tc_commit(smem_u32(&s_bar[t & 1]));
   };
+  static_assert(N <= kLsThreads, "one column per thread");
   if (ntiles > 0) {
     load_codes(0);
     store_tile(0);
@@ -830,6 +837,9 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
       uint32_t acc[32];
       tc_ld32_u(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((t & 1) * N + col0), acc);
       if (row_ok && col0 < tn) {
+        // admission of the 32 columns as a bit mask (no branch per pair); the few admitted
+        // vectors are appended afterwards
+        uint32_t adm = 0u;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float4 c = col[col0 + i];
@@ -837,11 +847,15 @@ __global__ void __launch_bounds__(kLsThreads) list_scan_tc_kernel(const ListScan
           const float base_d = __fadd_rn(c.x, g);
           const float est = __fadd_rn(base_d, __fmul_rn(c.y, __fadd_rn(ip, kk)));
           const float low = __fsub_rn(est, __fmul_rn(c.z, sg));
-          if (low < tau && col0 + i < tn) {
-            ++n_admit;
-            const int pos = atomicAdd(a.cand_cnt + q, 1);
-            if (pos < a.cap) a.cand[(size_t)q * a.cap + pos] = gbits | __float_as_uint(c.w);
-          }
+          adm |= (low < tau ? 1u : 0u) << i;
+        }
+        if (tn - col0 < 32) adm &= (1u << (tn - col0)) - 1u;  // columns past the list
+        while (adm) {
+          const int i = __ffs((int)adm) - 1;
+          adm &= adm - 1u;
+          ++n_admit;
+          const int pos = atomicAdd(a.cand_cnt + q, 1);
+          if (pos < a.cap) a.cand[(size_t)q * a.cap + pos] = gbits | __float_as_uint(col[col0 + i].w);
         }
       }
     }
