@@ -633,6 +633,45 @@ __device__ __forceinline__ float warp_exact_ip(const uint32_t* __restrict__ code
   return v;
 }
 
+// warp_exact_ip for four vectors at once, one per 8-lane group (lanes 8g..8g+7 take the vector
+// at their own `slot`): lane k of a group forms the values that lanes k, k + 8, k + 16 and k + 24
+// hold in warp_exact_ip, then adds them in that function's tree order (xor 16, then xor 8) and
+// finishes with the xor 4, 2, 1 steps inside the group.  Every addition has the same operands,
+// so the result equals warp_exact_ip's bit for bit; every lane of a group returns it.
+template <int W>
+__device__ __forceinline__ float group8_exact_ip(const uint32_t* __restrict__ codes, int64_t slot,
+                                                 const float* __restrict__ qsT, int lane)
+{
+  constexpr int NB = 4 * W;
+  constexpr int M = (NB + 31) / 32;
+  const unsigned char* cb = reinterpret_cast<const unsigned char*>(codes + slot * W);
+  const int k = lane & 7;
+  float v[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int j = k + 8 * h + 32 * m;
+      if (j < NB) {
+        const uint32_t u8 = __ldg(cb + (j ^ 3));
+        float b = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float q = qsT[jj * NB + j];
+          b = ((u8 >> (7 - jj)) & 1u) ? __fadd_rn(b, q) : b;
+        }
+        acc = __fadd_rn(acc, b);
+      }
+    }
+    v[h] = acc;
+  }
+  float t = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
+#pragma unroll
+  for (int off = 4; off; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
+  return t;
+}
+
 // <x, q> of the extra-bit code x at `slot` (planes [ex, W], plane p = bit p of every dim's
 // code), computed by the whole warp: lane l takes code bytes j = l, l + 32, ...; per byte, planes
 // p = ex-1 down to 0 add 2^p * bsum_p(j) (the sum of q over the set bits of byte j of plane p, bit
@@ -1307,30 +1346,46 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
       if constexpr (kLut) {
         if (a.ex_bits == 0) continue;  // no exact pass: the table estimate is the distance
       }
-      // phase 2: the warp's admitted vectors of this round, one at a time, all lanes.
+      // phase 2: the warp's admitted vectors of this round.
       unsigned mask = __ballot_sync(0xffffffffu, surv);
-      while (mask) {
+      if (!kLut && a.ex_bits == 0) {
+        // four at a time, one per 8-lane group (group g takes the g-th lowest admitted lane)
+        while (mask) {
+          int src = -1;
+#pragma unroll
+          for (int gi = 0; gi < 4; ++gi) {
+            const int sb = __ffs((int)mask) - 1;
+            if ((lane >> 3) == gi) src = sb;
+            mask &= mask - 1u;
+          }
+          const int from = src < 0 ? 0 : src;
+          const int slot = __shfl_sync(0xffffffffu, sslot, from);
+          const float base_d = __shfl_sync(0xffffffffu, sbase, from);
+          const float fr = __shfl_sync(0xffffffffu, sfr, from);
+          const float eip = group8_exact_ip<W>(a.codes, slot, qsT, lane);
+          const float dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
+          if ((lane & 7) == 0 && src >= 0 && dist <= tau) {
+            const int at = atomicAdd(&s_count, 1);
+            keys[at] = make_key(dist, __ldg(a.ids + slot));
+          }
+        }
+      }
+      while (mask) {  // one at a time, all lanes (extra-bit codes)
         const int src = __ffs(mask) - 1;
         mask &= mask - 1;
         const int slot = __shfl_sync(0xffffffffu, sslot, src);
         const float base_d = __shfl_sync(0xffffffffu, sbase, src);
         const float fr = __shfl_sync(0xffffffffu, sfr, src);
-        float dist;
-        if (a.ex_bits == 0) {
-          const float eip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
-          dist = __fadd_rn(base_d, __fmul_rn(fr, __fadd_rn(eip, k1)));
-        } else {
-          // the extra-bit distance (f_ex_add + g) + f_ex_rescale * ((2^ex ip + ip_x) + kb), ip the
-          // 1-bit inner product: exact, or the table one (carried in fr) in the LUT modes
-          float ip;
-          if constexpr (kLut)
-            ip = fr;
-          else
-            ip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
-          const float ipx = warp_ex_ip<W>(a.ex_codes, slot, a.ex_bits, qsT, lane);
-          const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, ip), ipx), kb);
-          dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), base_d), __fmul_rn(__ldg(a.fexr + slot), T));
-        }
+        // the extra-bit distance (f_ex_add + g) + f_ex_rescale * ((2^ex ip + ip_x) + kb), ip the
+        // 1-bit inner product: exact, or the table one (carried in fr) in the LUT modes
+        float ip;
+        if constexpr (kLut)
+          ip = fr;
+        else
+          ip = warp_exact_ip<W>(a.codes, slot, qsT, lane);
+        const float ipx = warp_ex_ip<W>(a.ex_codes, slot, a.ex_bits, qsT, lane);
+        const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, ip), ipx), kb);
+        const float dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), base_d), __fmul_rn(__ldg(a.fexr + slot), T));
         if (lane == 0 && dist <= tau) {
           const int at = atomicAdd(&s_count, 1);
           keys[at] = make_key(dist, __ldg(a.ids + slot));
@@ -1600,9 +1655,9 @@ void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int np
   RBQ_LAUNCHED();
 }
 
-// Exact pass of the list scan, one block per query: the candidates of its row, taken one at a
-// time by a warp (the exact 1-bit inner product of the tile scan, or the extra-bit distance),
-// kept while dist <= tau0[q]; the R smallest keys, ascending, go to out_keys.  The admitted set
+// Exact pass of the list scan, one block per query: the candidates of its row, taken four at a
+// time by a warp, one per 8-lane group (the exact 1-bit inner product of the tile scan), or one
+// at a time with extra bits (the extra-bit distance), kept while dist <= tau0[q]; the R smallest keys, ascending, go to out_keys.  The admitted set
 // does not depend on the order the list scan found it in, so neither does the result.
 constexpr int kExactThreads = 256;
 
@@ -1631,7 +1686,32 @@ __global__ void __launch_bounds__(kExactThreads) exact_topr_kernel(const ExactAr
   const float ex_scale = (float)(1 << a.ex_bits);
   const float kb = __fmul_rn(k1, (float)((2 << a.ex_bits) - 1));
   const unsigned long long* row = a.cand + q * a.cap;
-  for (int c = warp; c < n; c += kExactThreads / 32) {
+  if (a.ex_bits == 0) {
+    // four candidates per warp at a time, one per 8-lane group
+    const int grp = lane >> 3;
+    for (int c0 = 4 * warp; c0 < n; c0 += 4 * (kExactThreads / 32)) {
+      const int c = c0 + grp;
+      const bool has = c < n;
+      const unsigned long long e = row[has ? c : c0];
+      const int slot = (int)(uint32_t)e;
+      const float g = __uint_as_float((uint32_t)(e >> 32));
+      float eip;
+      switch (W) {
+#define RBQ_EXACT_W(w) \
+  case w: eip = group8_exact_ip<w>(a.codes, slot, qsT, lane); break;
+        RBQ_EXACT_W(1) RBQ_EXACT_W(2) RBQ_EXACT_W(3) RBQ_EXACT_W(4) RBQ_EXACT_W(6) RBQ_EXACT_W(8) RBQ_EXACT_W(12)
+        RBQ_EXACT_W(16) RBQ_EXACT_W(24)
+#undef RBQ_EXACT_W
+        default: eip = 0.0f;
+      }
+      if ((lane & 7) == 0 && has) {
+        const float dist =
+            __fadd_rn(__fadd_rn(__ldg(a.fadd + slot), g), __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(eip, k1)));
+        if (dist <= tau) keys[atomicAdd(&s_count, 1)] = make_key(dist, __ldg(a.ids + slot));
+      }
+    }
+  }
+  for (int c = warp; a.ex_bits > 0 && c < n; c += kExactThreads / 32) {
     const unsigned long long e = row[c];
     const int slot = (int)(uint32_t)e;
     const float g = __uint_as_float((uint32_t)(e >> 32));
@@ -1644,21 +1724,16 @@ __global__ void __launch_bounds__(kExactThreads) exact_topr_kernel(const ExactAr
 #undef RBQ_EXACT_W
       default: eip = 0.0f;
     }
-    float dist;
-    if (a.ex_bits == 0) {
-      dist = __fadd_rn(__fadd_rn(__ldg(a.fadd + slot), g), __fmul_rn(__ldg(a.frescale + slot), __fadd_rn(eip, k1)));
-    } else {
-      float ipx;
-      switch (W) {
+    float ipx;
+    switch (W) {
 #define RBQ_EX_W(w) \
   case w: ipx = warp_ex_ip<w>(a.ex_codes, slot, a.ex_bits, qsT, lane); break;
-        RBQ_EX_W(1) RBQ_EX_W(2) RBQ_EX_W(3) RBQ_EX_W(4) RBQ_EX_W(6) RBQ_EX_W(8) RBQ_EX_W(12) RBQ_EX_W(16) RBQ_EX_W(24)
+      RBQ_EX_W(1) RBQ_EX_W(2) RBQ_EX_W(3) RBQ_EX_W(4) RBQ_EX_W(6) RBQ_EX_W(8) RBQ_EX_W(12) RBQ_EX_W(16) RBQ_EX_W(24)
 #undef RBQ_EX_W
-        default: ipx = 0.0f;
-      }
-      const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, eip), ipx), kb);
-      dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), g), __fmul_rn(__ldg(a.fexr + slot), T));
+      default: ipx = 0.0f;
     }
+    const float T = __fadd_rn(__fadd_rn(__fmul_rn(ex_scale, eip), ipx), kb);
+    const float dist = __fadd_rn(__fadd_rn(__ldg(a.fexadd + slot), g), __fmul_rn(__ldg(a.fexr + slot), T));
     if (lane == 0 && dist <= tau) keys[atomicAdd(&s_count, 1)] = make_key(dist, __ldg(a.ids + slot));
   }
   __syncthreads();
