@@ -897,26 +897,39 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
   return sa;
 }
 
-// The list scan of a search: one pass over all probes in sp.slices slices.  With sp.seeded
-// every slice starts from the bound seed of the query's nearest probe (computed first, by a
-// seed-only launch over that list) instead of finding its own: split slices then prune from
-// their first vector.
-// Scratch of a list scan over nq queries with P probe columns.
-// Slices of the tile scan that answers the queries whose candidate row overflowed (their
-// lists split four ways, so that a far query's many admitted vectors spread over four blocks).
-constexpr int kListFallbackSlices = 4;
+// The queries whose candidate row overflowed are few (at config 2, 50 of 10,000) but far: they
+// admit up to every probed vector.  The tile scan answers them, each split into up to 16 slices
+// of its probes, the slices of the listed queries spread over a fixed grid.  The slices' keys
+// [nq, slices, R] are held to 256 MiB (no fewer than 4 slices), and the merge of a query's
+// slices must fit in shared memory.
+constexpr int kListFallbackMaxSlices = 16;
+constexpr int64_t kListFallbackBytes = 256ll << 20;
+constexpr int kListFallbackBlocks = 148 * 8;
 
+int list_fallback_slices(int64_t nq, int nprobe, int R)
+{
+  int fs = std::max(1, std::min(nprobe, kListFallbackMaxSlices));
+  while (fs > 4 && (nq * fs * R * 8 > kListFallbackBytes || (int64_t)(fs + 1) * R * 8 > 200 * 1024)) fs /= 2;
+  return std::max(1, std::min(fs, nprobe));
+}
+
+// Scratch of a list scan over nq queries with P probe columns.
 struct ListScanScratch {
   int8_t* qcodes;
   int32_t *list_start, *item_start, *cursor, *pair_q, *cand_cnt;
   float* pair_g;
   unsigned long long* cand;
-  unsigned long long* fall;  // [nq, kListFallbackSlices, R] keys of the overflowed queries' slices
+  int fs;                    // slices of the overflowed queries' tile scan
+  int32_t *over_list, *over_n;  // the overflowed queries, their count
+  unsigned long long* fall;  // [nq, fs, R] keys of the overflowed queries' slices
 };
 
 ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int P, int cap, int R)
 {
   ListScanScratch w;
+  w.fs = list_fallback_slices(nq, P, R);
+  w.over_list = sc.get<int32_t>((size_t)nq);
+  w.over_n = sc.get<int32_t>(1);
   w.qcodes = sc.get<int8_t>((size_t)nq * ix.Dp);
   w.list_start = sc.get<int32_t>((size_t)ix.K + 1);
   w.item_start = sc.get<int32_t>((size_t)ix.K + 1);
@@ -925,7 +938,7 @@ ListScanScratch list_scan_scratch(Scratch& sc, const Index& ix, int64_t nq, int 
   w.pair_g = sc.get<float>((size_t)nq * P);
   w.cand_cnt = sc.get<int32_t>((size_t)nq);
   w.cand = sc.get<unsigned long long>((size_t)nq * cap);
-  w.fall = sc.get<unsigned long long>((size_t)nq * kListFallbackSlices * R);
+  w.fall = sc.get<unsigned long long>((size_t)nq * w.fs * R);
   return w;
 }
 
@@ -991,10 +1004,11 @@ void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbi
   ea.out_slices = out_slices;
   ea.out_slice = out_slice;
   launch_exact_topr(ea, s);
-  // rows that overflowed: the tile scan with the same fixed thresholds, in slices merged into the
-  // query's row (its blocks for the other queries return at once; the list scan already counted
-  // every admitted vector).  Slices keep the answer: each holds the R best of its part of a set.
-  const int fs = std::min(nprobe, kListFallbackSlices);
+  // rows that overflowed: listed on the device, then the tile scan with the same fixed
+  // thresholds over the listed queries only, in slices merged into the query's row.  Slices
+  // keep the answer: each holds the R best of its part of a set.
+  const int fs = std::min(nprobe, w.fs);
+  launch_over_list(w.cand_cnt, nq, cap, w.over_list, w.over_n, s);
   ScanArgs fa = batch_scan_args(ix, Qr, planes, delta, k1, nq, probes, g, nprobe, R,
                                 std::max(next_pow2(1024), next_pow2(R + kScanTile)), 1, fs, w.fall, nullptr, qbits);
   fa.pstride = pstride;
@@ -1002,6 +1016,9 @@ void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbi
   fa.fixed_tau = 1;
   fa.over_cnt = w.cand_cnt;
   fa.over_cap = cap;
+  fa.qorder = w.over_list;
+  fa.unit_count = w.over_n;
+  fa.grid_blocks = kListFallbackBlocks;
   launch_scan(fa, s);
   launch_merge_sorted_keys(w.fall, nq, fs, R, out_keys, out_slices, out_slice, w.cand_cnt, cap, s);
 }

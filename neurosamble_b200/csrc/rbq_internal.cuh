@@ -281,6 +281,10 @@ struct ScanArgs {
   // Optional [nq] visiting order: block i scans query qorder[i / slices] (a permutation of
   // 0..nq-1).  Only the order in which queries run changes; every query's result is its own.
   const int32_t* qorder = nullptr;
+  // Optional (device): scan only the first *unit_count queries of qorder, their units spread by
+  // a grid-stride loop over grid_blocks blocks (a list whose length only the device knows).
+  const int32_t* unit_count = nullptr;
+  int grid_blocks = 0;
   // Fixed-threshold scan (the list scan's semantics): the prune admits a vector while
   // low < tau0[q] (+inf when tau0 is null), however far the kept candidates have tightened the
   // threshold; only the keep test and the buffer cuts use the running threshold.
@@ -329,6 +333,8 @@ constexpr int kListScanRows = 128;  // (list, query) pairs per work item
 void launch_list_scan_tc(const ListScanArgs& a, int64_t max_items, cudaStream_t s);
 // The work plan of a list scan: codes of the queries ([nq, Dp] int8, from planes [nq, QB, W]),
 // the (list, query) pairs of this shard's probed lists bucketed by list, and the work items.
+// The queries q < nq with cnt[q] > cap into list[0..*n) (n zeroed first), in no fixed order.
+void launch_over_list(const int32_t* cnt, int64_t nq, int cap, int32_t* list, int32_t* n, cudaStream_t s);
 void launch_planes_to_codes(const uint32_t* planes, int64_t nq, int W, int QB, int8_t* codes, cudaStream_t s);
 void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int nprobe, int pstride,
                        const int32_t* owner, int rank, int K, int32_t* list_start, int32_t* item_start,

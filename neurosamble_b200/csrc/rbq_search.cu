@@ -1097,8 +1097,10 @@ __device__ __forceinline__ float lut_ip(const unsigned char* __restrict__ tab, c
   return ip;
 }
 
+// One unit of the tile scan: slice u % slices of query qorder[u / slices] (u / slices without
+// an order).  Every early return is taken by the whole block.
 template <int W, int QB>
-__global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kernel(const ScanArgs a)
+__device__ __forceinline__ void scan_unit(const ScanArgs& a, const unsigned u)
 {
   constexpr int NB = 4 * W;
   constexpr bool kLut = QB >= 16;    // LUT16 / LUT32: the table estimate is the distance
@@ -1118,8 +1120,8 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   __shared__ unsigned s_hist[256];
   __shared__ unsigned long long s_kmax;
 
-  const int64_t qi = blockIdx.x / a.slices;
-  const int slice = blockIdx.x - (int)(qi * a.slices);
+  const int64_t qi = u / (unsigned)a.slices;
+  const int slice = (int)(u - (unsigned)qi * (unsigned)a.slices);
   const int64_t q = a.qorder ? (int64_t)a.qorder[qi] : qi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (a.over_cnt && a.over_cnt[q] <= a.over_cap) return;  // only the list scan's overflowed rows
@@ -1431,16 +1433,47 @@ __global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kerne
   }
 }
 
+// One unit per block.
+template <int W, int QB>
+__global__ void __launch_bounds__(kScanThreads, scan_min_blocks<W>()) scan_kernel(const ScanArgs a)
+{
+  scan_unit<W, QB>(a, blockIdx.x);
+}
+
+// A grid-stride loop over the units of the first *unit_count queries of qorder (a list whose
+// length only the device knows: the list scan's overflowed rows).  A kernel of its own, compiled
+// for fewer resident blocks, so that the loop costs the one-unit scan no registers.
+template <int W, int QB>
+__global__ void __launch_bounds__(kScanThreads, 4) scan_listed_kernel(const ScanArgs a)
+{
+  const unsigned units = (unsigned)*a.unit_count * (unsigned)a.slices;
+  for (unsigned u = blockIdx.x; u < units; u += gridDim.x) {
+    scan_unit<W, QB>(a, u);
+    __syncthreads();  // the unit's shared memory is free again
+  }
+}
+
 template <int W, int QB>
 static void launch_scan_wq(const ScanArgs& a, cudaStream_t s)
 {
   const size_t smem = (size_t)a.cap * 8 * 2 + (size_t)(2 * a.nprobe + 1) * 4 + (size_t)2 * a.nprobe * 4 +
                       (size_t)scan_head_bytes<W, QB>();
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "scan: shared memory budget exceeded (cap/nprobe too large)");
-  if (smem > 48 * 1024)
-    RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t blocks = a.nq * a.slices;
   RBQ_CHECK(blocks <= 0x7fffffff, RBQ_ERR_INVALID, "scan: grid too large");
+  if constexpr (QB <= 8 && W <= 24) {  // the list scan's modes and dimensions
+    if (a.unit_count) {
+      if (smem > 48 * 1024)
+        RBQ_CUDA(cudaFuncSetAttribute(scan_listed_kernel<W, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+      scan_listed_kernel<W, QB><<<(unsigned)std::min<int64_t>(blocks, a.grid_blocks), kScanThreads, smem, s>>>(a);
+      RBQ_LAUNCHED();
+      return;
+    }
+  }
+  RBQ_CHECK(!a.unit_count, RBQ_ERR_INVALID, "scan: a listed-query scan takes 4- or 8-bit queries, dim <= 768");
+  if (smem > 48 * 1024)
+    RBQ_CUDA(cudaFuncSetAttribute(scan_kernel<W, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   scan_kernel<W, QB><<<(unsigned)blocks, kScanThreads, smem, s>>>(a);
   RBQ_LAUNCHED();
 }
@@ -1474,6 +1507,8 @@ void launch_scan(const ScanArgs& args, cudaStream_t s)
             "scan: a fixed-threshold scan takes no initial candidates");
   RBQ_CHECK(a.n_slots >= 0 && a.n_slots < (int64_t)0x7fffffff - 2 * kScanTile, RBQ_ERR_INVALID,
             "scan: more than 2^31 vectors on one shard");
+  RBQ_CHECK(!a.unit_count || (a.qorder && a.grid_blocks >= 1), RBQ_ERR_INVALID,
+            "scan: a listed-query scan needs the list (qorder) and a grid size");
   switch (a.W) {
     case 1: launch_scan_w<1>(a, s); break;
     case 2: launch_scan_w<2>(a, s); break;
@@ -1652,6 +1687,29 @@ void launch_list_pairs(const int32_t* probes, const float* g, int64_t nq, int np
   RBQ_CUDA(cudaMemcpyAsync(cursor, list_start, (size_t)(K + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
   list_pairs_scatter_kernel<<<grid, 256, 0, s>>>(probes, g, nq, nprobe, pstride, owner, rank, K, cursor, pair_q,
                                                   pair_g);
+  RBQ_LAUNCHED();
+}
+
+// The queries whose candidate row overflowed (cnt[q] > cap), in no particular order: list[0..*n).
+__global__ void over_list_kernel(const int32_t* __restrict__ cnt, int64_t nq, int cap, int32_t* __restrict__ list,
+                                 int32_t* __restrict__ n)
+{
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool over = q < nq && cnt[q] > cap;
+  const unsigned m = __ballot_sync(0xffffffffu, over);
+  if (!m) return;
+  const int lane = threadIdx.x & 31;
+  int base = 0;
+  if (lane == 0) base = atomicAdd(n, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (over) list[base + __popc(m & ((1u << lane) - 1u))] = (int32_t)q;
+}
+
+void launch_over_list(const int32_t* cnt, int64_t nq, int cap, int32_t* list, int32_t* n, cudaStream_t s)
+{
+  RBQ_CUDA(cudaMemsetAsync(n, 0, sizeof(int32_t), s));
+  if (nq <= 0) return;
+  over_list_kernel<<<(unsigned)ceil_div(nq, 256), 256, 0, s>>>(cnt, nq, cap, list, n);
   RBQ_LAUNCHED();
 }
 
