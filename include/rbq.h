@@ -120,9 +120,10 @@ typedef struct {
                          /* 0 (default): launch the kernels one by one.                         */
   int32_t scan_kind;     /* the list scan's schedule.  1: the tile scan (each query walks its   */
                          /* probed lists in tiles of rbq_scan_tile() vectors, the threshold     */
-                         /* tightening between tiles).  2: the list scan: every query's        */
-                         /* threshold is fixed at its bound seed over the leading probed lists  */
-                         /* holding >= R vectors, and each probed list is scored against all    */
+                         /* tightening between tiles).  2: the list scan: the nearest probe is  */
+                         /* tile-scanned from its bound seed; every query's threshold for its   */
+                         /* other probes is then fixed at min(seed, the nearest list's R-th     */
+                         /* distance), and each of those lists is scored against all         */
                          /* the batch's queries that probe it in one int8 GEMM on the tensor    */
                          /* cores (4- or 8-bit query codes x code bits, exactly the popcount    */
                          /* estimator's integers, as the reference scans one (list, query) pair */
