@@ -777,14 +777,15 @@ def scan_roofline(ix, Qd, cfg, R_search, flush, steps, dev, seeded, lists=False)
     # DRAM traffic cannot be read inside a plain run: it comes from a stored ncu capture of the
     # same kernel and workload (profiles/scan_traffic.json), and the line says so
     traffic, traffic_src = None, None
-    tf = os.path.join(HERE, "profiles", "scan_traffic.json")
+    tname = "list_scan_traffic.json" if lists else "scan_traffic.json"
+    tf = os.path.join(HERE, "profiles", tname)
     if os.path.exists(tf):
         try:
             with open(tf) as f:
                 tj = json.load(f)
             if tj.get("config", 2) == cfg.get("config", 2):
                 traffic = tj.get("bytes_per_launch_scaled_to_bench")
-                traffic_src = "stored ncu capture (profiles/scan_traffic.json), not measured in this run"
+                traffic_src = f"stored ncu capture (profiles/{tname}), not measured in this run"
         except Exception:
             traffic = None
     ach = scan_bytes / (scan_ms / 1000.0) / 1e9
