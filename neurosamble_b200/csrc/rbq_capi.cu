@@ -901,12 +901,12 @@ ScanArgs batch_scan_args(const Index& ix, const float* Qr, const uint32_t* plane
 
 // The queries whose candidate row overflowed are few (at config 2, 50 of 10,000) but far: they
 // admit up to every probed vector.  The tile scan answers them, each split into up to 16 slices
-// of its probes, the slices of the listed queries spread over a fixed grid.  The slices' keys
+// of its probes, the slices of the listed queries spread over 8 blocks per SM.  The slices' keys
 // [nq, slices, R] are held to 256 MiB (no fewer than 4 slices), and the merge of a query's
 // slices must fit in shared memory.
 constexpr int kListFallbackMaxSlices = 16;
 constexpr int64_t kListFallbackBytes = 256ll << 20;
-constexpr int kListFallbackBlocks = 148 * 8;
+constexpr int kListFallbackBlocksPerSm = 8;
 
 int list_fallback_slices(int64_t nq, int nprobe, int R)
 {
@@ -1020,7 +1020,7 @@ void list_scan(const Index& ix, const float* Qr, const uint32_t* planes, int qbi
   fa.over_cap = cap;
   fa.qorder = w.over_list;
   fa.unit_count = w.over_n;
-  fa.grid_blocks = kListFallbackBlocks;
+  fa.grid_blocks = kListFallbackBlocksPerSm * device_sm_count();
   launch_scan(fa, s);
   launch_merge_sorted_keys(w.fall, nq, fs, R, out_keys, out_slices, out_slice, w.cand_cnt, cap, s);
 }

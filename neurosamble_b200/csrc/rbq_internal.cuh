@@ -329,6 +329,8 @@ struct ListScanArgs {
   int* err;
 };
 bool list_scan_tc_supported(int dp);
+// SMs of the current device (grid sizes of the persistent and grid-stride kernels).
+int device_sm_count();
 constexpr int kListScanRows = 128;  // (list, query) pairs per work item
 void launch_list_scan_tc(const ListScanArgs& a, int64_t max_items, cudaStream_t s);
 // The work plan of a list scan: codes of the queries ([nq, Dp] int8, from planes [nq, QB, W]),

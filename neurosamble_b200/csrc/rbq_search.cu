@@ -424,6 +424,14 @@ __global__ void __launch_bounds__(256) refine_all_kernel(const float* __restrict
   }
 }
 
+int device_sm_count()
+{
+  int dev = 0, n = 0;
+  RBQ_CUDA(cudaGetDevice(&dev));
+  RBQ_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  return n > 0 ? n : 1;
+}
+
 void launch_refine_all(const float* A, int64_t nq, const float* C, int d, int K, int p, const int* unsafe,
                        int32_t* probes, float* g, cudaStream_t s)
 {
@@ -433,7 +441,7 @@ void launch_refine_all(const float* A, int64_t nq, const float* C, int d, int K,
   RBQ_CHECK(smem <= 200 * 1024, RBQ_ERR_INVALID, "coarse: exact probe pass too large (nprobe / dim)");
   if (smem > 48 * 1024)
     RBQ_CUDA(cudaFuncSetAttribute(refine_all_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const unsigned grid = (unsigned)std::min<int64_t>(nq, 148 * 4);
+  const unsigned grid = (unsigned)std::min<int64_t>(nq, (int64_t)device_sm_count() * 4);
   refine_all_kernel<<<grid, 256, smem, s>>>(A, C, d, K, p, buf, unsafe, probes, g);
   RBQ_LAUNCHED();
 }
