@@ -57,6 +57,16 @@ def test_auto_rule():
         O.uses_list_scan(2, 4, 1, 1024, 1, 1, 8)
 
 
+def test_word_to_vector_mapping_by_multiply_high():
+    """The list scan maps its code-word index i (< N * 24, N = 128 vectors per tile) to the vector
+    i / W by a multiply-high with ceil(2^32 / W) instead of an integer division: exact for every
+    word count W = Dp / 32 up to 24 (Dp <= 768) over that whole range."""
+    i = np.arange(128 * 24 + 1, dtype=np.uint64)
+    for W in range(1, 25):
+        magic = np.uint64((2 ** 32 + W - 1) // W)
+        assert np.array_equal((i * magic) >> np.uint64(32), i // np.uint64(W)), W
+
+
 # ------------------------------------------------------------------------------------------
 # GPU
 # ------------------------------------------------------------------------------------------
