@@ -67,6 +67,22 @@ def test_word_to_vector_mapping_by_multiply_high():
         assert np.array_equal((i * magic) >> np.uint64(32), i // np.uint64(W)), W
 
 
+def test_code_word_expansion_to_bytes():
+    """The list scan's B operand: a code word (dim 32w + j -> bit 31 - j) becomes 32 bytes 0 / 1,
+    byte j = dim 32w + j, by a bit reversal and, per nibble, a multiply by 0x00204081 masked with
+    0x01010101 (the four shifted copies of the nibble do not overlap, so nothing carries)."""
+    rng = np.random.default_rng(5)
+    words = np.concatenate([rng.integers(0, 2 ** 32, 2000, dtype=np.uint64),
+                            np.array([0, 0xFFFFFFFF, 0x80000001, 0x0F0F0F0F], np.uint64)])
+    for c in words.tolist():
+        r = int("{:032b}".format(c)[::-1], 2)  # __brev
+        out = []
+        for i in range(8):
+            o = ((((r >> (4 * i)) & 0xF) * 0x00204081) & 0xFFFFFFFF) & 0x01010101
+            out += [(o >> (8 * b)) & 0xFF for b in range(4)]  # little-endian bytes of the word
+        assert out == [(c >> (31 - j)) & 1 for j in range(32)], hex(c)
+
+
 # ------------------------------------------------------------------------------------------
 # GPU
 # ------------------------------------------------------------------------------------------
