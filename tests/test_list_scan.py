@@ -67,6 +67,25 @@ def test_word_to_vector_mapping_by_multiply_high():
         assert np.array_equal((i * magic) >> np.uint64(32), i // np.uint64(W)), W
 
 
+@pytest.mark.parametrize("QB", [4, 8])
+@pytest.mark.parametrize("W", [1, 2, 4, 8, 24])
+def test_int8_gemm_form_equals_the_popcount_estimator(oracle, QB, W):
+    """The list scan's A operand: a query's planes read back as signed int8 codes (two's
+    complement over its QB planes, bit j of a plane word's reversal = dim j).  The int8 dot product
+    of those codes with a vector's code bits is the popcount estimator's integer, for any planes."""
+    rng = np.random.default_rng(QB * 100 + W)
+    for _ in range(30):
+        planes = rng.integers(0, 2 ** 32, (QB, W), dtype=np.uint64).astype(np.uint32)
+        code = rng.integers(0, 2 ** 32, W, dtype=np.uint64).astype(np.uint32)
+        dims = np.arange(32 * W)
+        w, j = dims // 32, dims % 32
+        pbits = (planes[:, w].astype(np.int64) >> (31 - j)) & 1  # [QB, dims]: plane b, dim 32w + j
+        q8 = sum(pbits[b] << b for b in range(QB - 1)) - (pbits[QB - 1] << (QB - 1))
+        assert q8.min() >= -(1 << (QB - 1)) and q8.max() < (1 << (QB - 1))  # fits int8
+        cbits = (code[w].astype(np.int64) >> (31 - j)) & 1
+        assert int((q8 * cbits).sum()) == oracle.popcount_ip(planes, code)
+
+
 def test_code_word_expansion_to_bytes():
     """The list scan's B operand: a code word (dim 32w + j -> bit 31 - j) becomes 32 bytes 0 / 1,
     byte j = dim 32w + j, by a bit reversal and, per nibble, a multiply by 0x00204081 masked with
