@@ -911,7 +911,8 @@ constexpr int kListFallbackBlocksPerSm = 8;
 int list_fallback_slices(int64_t nq, int nprobe, int R)
 {
   int fs = std::max(1, std::min(nprobe, kListFallbackMaxSlices));
-  while (fs > 4 && (nq * fs * R * 8 > kListFallbackBytes || (int64_t)(fs + 1) * R * 8 > 200 * 1024)) fs /= 2;
+  while (fs > 4 && (nq * fs * R * 8 > kListFallbackBytes || (int64_t)(fs + 1) * R * 8 > 200 * 1024))
+    fs = std::max(4, fs / 2);
   return std::max(1, std::min(fs, nprobe));
 }
 
